@@ -1,0 +1,62 @@
+// Python bindings of the sm_100a kernels (module axrl_b200._C).
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace ax {
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps);
+std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd);
+std::vector<at::Tensor> qknorm_rope_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, int64_t, double);
+std::vector<at::Tensor> qknorm_rope_cache(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, int64_t, double,
+                                          at::Tensor, at::Tensor, at::Tensor);
+std::vector<at::Tensor> qknorm_rope_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
+                                        at::Tensor, at::Tensor, int64_t, int64_t);
+at::Tensor swiglu_fwd(at::Tensor gu);
+at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor gu);
+void logprob_fwd(at::Tensor, at::Tensor, double, at::Tensor, at::Tensor, at::Tensor);
+void logprob_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, double);
+void sample_tokens(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, c10::optional<at::Tensor>, c10::optional<at::Tensor>);
+at::Tensor linear_fwd(at::Tensor x, at::Tensor w);
+at::Tensor linear_dgrad(at::Tensor dy, at::Tensor w);
+at::Tensor linear_wgrad(at::Tensor dy, at::Tensor x);
+void linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc);
+at::Tensor gemm_bf16(at::Tensor a, at::Tensor b, bool trans_b);
+std::vector<at::Tensor> attn_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, double);
+std::vector<at::Tensor> attn_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
+                                 at::Tensor, double);
+void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
+                       double);
+void kv_store(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
+void sqnorm_accumulate(at::Tensor x, at::Tensor acc);
+void adamw_step(at::Tensor, at::Tensor, at::Tensor, at::Tensor, c10::optional<at::Tensor>, int64_t, double, double, double, double,
+                double, int64_t, c10::optional<at::Tensor>, double, double);
+at::Tensor embed_fwd(at::Tensor ids, at::Tensor table);
+void embed_bwd(at::Tensor ids, at::Tensor dout, at::Tensor grad);
+}  // namespace ax
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("rmsnorm_fwd", &ax::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &ax::rmsnorm_bwd);
+  m.def("qknorm_rope_fwd", &ax::qknorm_rope_fwd);
+  m.def("qknorm_rope_cache", &ax::qknorm_rope_cache);
+  m.def("qknorm_rope_bwd", &ax::qknorm_rope_bwd);
+  m.def("swiglu_fwd", &ax::swiglu_fwd);
+  m.def("swiglu_bwd", &ax::swiglu_bwd);
+  m.def("logprob_fwd", &ax::logprob_fwd);
+  m.def("logprob_bwd", &ax::logprob_bwd);
+  m.def("sample_tokens", &ax::sample_tokens, py::arg("logits"), py::arg("temperature"), py::arg("seed"), py::arg("out_tok"),
+        py::arg("out_lp"), py::arg("row_ids") = py::none(), py::arg("forced") = py::none());
+  m.def("linear_fwd", &ax::linear_fwd);
+  m.def("linear_dgrad", &ax::linear_dgrad);
+  m.def("linear_wgrad", &ax::linear_wgrad);
+  m.def("linear_wgrad_acc", &ax::linear_wgrad_acc);
+  m.def("gemm", &ax::gemm_bf16);
+  m.def("attn_fwd", &ax::attn_fwd);
+  m.def("attn_bwd", &ax::attn_bwd);
+  m.def("paged_decode_attn", &ax::paged_decode_attn);
+  m.def("kv_store", &ax::kv_store);
+  m.def("sqnorm_accumulate", &ax::sqnorm_accumulate);
+  m.def("adamw_step", &ax::adamw_step);
+  m.def("embed_fwd", &ax::embed_fwd);
+  m.def("embed_bwd", &ax::embed_bwd);
+}

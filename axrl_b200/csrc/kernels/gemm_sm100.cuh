@@ -1,0 +1,110 @@
+// bf16 GEMMs on 5th-gen tensor cores (tcgen05.mma, TMEM accumulators, TMA operand loads),
+// composed from CUTLASS sm100 collectives.  Cluster shapes are chosen so that no operand
+// load uses cluster multicast: 1-SM kernels run with cluster (1,1,1); 2-SM kernels
+// (cta_group::2, one MMA tile spanning an SM pair) run with cluster (2,1,1), where each
+// CTA of the pair loads its own half of A and of B.
+//
+// Convention: D[M,N] = alpha * A[M,K] @ B[K,N] + beta * C[M,N], row-major D/C.
+//   LayoutA RowMajor    -> A stored M x K (K contiguous)
+//   LayoutA ColumnMajor -> A stored K x M (M contiguous)
+//   LayoutB ColumnMajor -> B stored N x K (K contiguous)   (x @ W^T with W [N,K])
+//   LayoutB RowMajor    -> B stored K x N (N contiguous)
+#pragma once
+#include "../common.cuh"
+
+#include "cute/tensor.hpp"
+#include "cutlass/cutlass.h"
+#include "cutlass/epilogue/collective/collective_builder.hpp"
+#include "cutlass/gemm/collective/collective_builder.hpp"
+#include "cutlass/gemm/device/gemm_universal_adapter.h"
+#include "cutlass/gemm/dispatch_policy.hpp"
+#include "cutlass/gemm/kernel/gemm_universal.hpp"
+#include "cutlass/util/packed_stride.hpp"
+
+namespace ax {
+namespace gemm {
+
+using namespace cute;
+
+struct Sm1 {
+  using Tile = Shape<_128, _128, _64>;
+  using Cluster = Shape<_1, _1, _1>;
+  using Kernel = cutlass::gemm::KernelTmaWarpSpecialized1SmSm100;
+  using Epi = cutlass::epilogue::TmaWarpSpecialized1Sm;
+};
+struct Sm1Narrow {
+  using Tile = Shape<_128, _64, _64>;
+  using Cluster = Shape<_1, _1, _1>;
+  using Kernel = cutlass::gemm::KernelTmaWarpSpecialized1SmSm100;
+  using Epi = cutlass::epilogue::TmaWarpSpecialized1Sm;
+};
+struct Sm2 {
+  using Tile = Shape<_256, _256, _64>;
+  using Cluster = Shape<_2, _1, _1>;
+  using Kernel = cutlass::gemm::KernelTmaWarpSpecialized2SmSm100;
+  using Epi = cutlass::epilogue::TmaWarpSpecialized2Sm;
+};
+
+template <class LayoutA, class LayoutB, class ElemD, class Cfg>
+struct Gemm {
+  using ElemA = cutlass::bfloat16_t;
+  using ElemB = cutlass::bfloat16_t;
+  using ElemAcc = float;
+  using LayoutC = cutlass::layout::RowMajor;
+  static constexpr int kAlignD = 128 / cutlass::sizeof_bits<ElemD>::value;
+
+  using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
+      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, typename Cfg::Tile, typename Cfg::Cluster,
+      cutlass::epilogue::collective::EpilogueTileAuto, ElemAcc, ElemAcc, ElemD, LayoutC, kAlignD, ElemD, LayoutC, kAlignD,
+      typename Cfg::Epi>::CollectiveOp;
+
+  using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
+      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, ElemA, LayoutA, 8, ElemB, LayoutB, 8, ElemAcc,
+      typename Cfg::Tile, typename Cfg::Cluster,
+      cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
+      typename Cfg::Kernel>::CollectiveOp;
+
+  using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue, void>;
+  using Op = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
+
+  static void run(const void* A, const void* B, const void* C, void* D, int M, int N, int K, float alpha, float beta,
+                  cudaStream_t st) {
+    using SA = typename Kernel::StrideA;
+    using SB = typename Kernel::StrideB;
+    using SC = typename Kernel::StrideC;
+    using SD = typename Kernel::StrideD;
+    SA sa = cutlass::make_cute_packed_stride(SA{}, cute::make_shape(M, K, 1));
+    SB sb = cutlass::make_cute_packed_stride(SB{}, cute::make_shape(N, K, 1));
+    SC sc = cutlass::make_cute_packed_stride(SC{}, cute::make_shape(M, N, 1));
+    SD sd = cutlass::make_cute_packed_stride(SD{}, cute::make_shape(M, N, 1));
+    typename Op::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
+                                {M, N, K, 1},
+                                {static_cast<const ElemA*>(A), sa, static_cast<const ElemB*>(B), sb},
+                                {{alpha, beta}, static_cast<const ElemD*>(C), sc, static_cast<ElemD*>(D), sd}};
+    args.hw_info.device_id = 0;
+    args.hw_info.sm_count = num_sms();
+    Op op;
+    auto st_impl = op.can_implement(args);
+    TORCH_CHECK(st_impl == cutlass::Status::kSuccess, "GEMM cannot implement M=", M, " N=", N, " K=", K);
+    size_t ws = Op::get_workspace_size(args);
+    at::Tensor wst;
+    void* wsp = nullptr;
+    if (ws) {
+      wst = at::empty({(int64_t)ws}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA));
+      wsp = wst.data_ptr();
+    }
+    auto s1 = op.initialize(args, wsp, st);
+    TORCH_CHECK(s1 == cutlass::Status::kSuccess, "GEMM init failed");
+    auto s2 = op.run(st);
+    TORCH_CHECK(s2 == cutlass::Status::kSuccess, "GEMM run failed");
+  }
+};
+
+// Entry points (one translation unit per layout family, for parallel builds).
+void run_tn(const void* A, const void* B, void* D, int M, int N, int K, bool d_fp32, cudaStream_t st);   // A MxK, B NxK
+void run_nn(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);                // A MxK, B KxN
+void run_wgrad(const void* A, const void* B, void* D, int M, int N, int K, bool accumulate, bool d_fp32,
+               cudaStream_t st);  // A stored KxM (M contiguous), B KxN
+
+}  // namespace gemm
+}  // namespace ax

@@ -1,0 +1,102 @@
+"""Sparse MoE block (Qwen3-MoE): fp32 router, top-k softmax routing, SwiGLU experts.
+
+Routing replay (R3, reference ``axrl/utils/megatron/router_replay.py:67-108``):
+when ``ctx.replay[layer]`` holds top-k expert ids recorded by the rollout
+engine, the forward uses those ids (recomputing only the gate weights from the
+current router logits); with ``ctx.loss_tokens_only`` the replayed ids apply
+on loss tokens and the live top-k elsewhere.  ``ctx.capture`` collects the ids
+actually used, per layer, which is how the rollout engine records routing.
+
+On a single GPU the expert FFNs run as one grouped GEMM over tokens sorted by
+expert; under expert parallelism :mod:`axrl_b200.parallel.expert` replaces the
+local dispatch with the fused all-to-all path.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+
+from axrl_b200.ops import core as ops
+
+
+@dataclass
+class MoEContext:
+    replay: dict[int, torch.Tensor] | None = None  # layer -> (T, K) int
+    replay_mask: torch.Tensor | None = None  # (T,) bool, replay only where True
+    capture: dict[int, torch.Tensor] | None = None  # filled with (T, K) int16
+    aux_loss: list[torch.Tensor] = field(default_factory=list)
+    ep_group: object | None = None
+
+
+def route(logits: torch.Tensor, k: int, renorm: bool, replay: torch.Tensor | None = None, replay_mask: torch.Tensor | None = None):  # noqa: ANN201
+    """Top-k routing in fp32.  Returns (weights (T,k) fp32, ids (T,k) int64)."""
+    probs = torch.softmax(logits.float(), -1)
+    top_w, top_i = probs.topk(k, -1)
+    if replay is not None:
+        rep = replay.long()
+        if replay_mask is not None:
+            rep = torch.where(replay_mask[:, None], rep, top_i)
+        top_i = rep
+        top_w = probs.gather(1, top_i)
+    if renorm:
+        top_w = top_w / top_w.sum(-1, keepdim=True).clamp_min(1e-20)
+    return top_w, top_i
+
+
+def grouped_ffn_ref(x_sorted: torch.Tensor, counts: list[int], w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    outs, s = [], 0
+    for e, c in enumerate(counts):
+        if c:
+            xe = x_sorted[s:s + c]
+            outs.append(ops.linear(ops.swiglu(ops.linear(xe, w_gate_up[e])), w_down[e]))
+        s += c
+    return torch.cat(outs, 0) if outs else x_sorted[:0]
+
+
+class MoEBlock(nn.Module):
+    def __init__(self, cfg) -> None:  # noqa: ANN001
+        super().__init__()
+        E, H, F = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
+        self.E, self.k, self.renorm = E, cfg.num_experts_per_tok, cfg.norm_topk_prob
+        self.router = nn.Parameter(torch.empty(E, H))
+        self.experts_gate_up = nn.Parameter(torch.empty(E, 2 * F, H))
+        self.experts_down = nn.Parameter(torch.empty(E, H, F))
+
+    def hf_tensors(self, prefix: str) -> dict[str, torch.Tensor]:
+        out = {prefix + "mlp.gate.weight": self.router}
+        F = self.experts_down.shape[2]
+        for e in range(self.E):
+            q = f"{prefix}mlp.experts.{e}."
+            out[q + "gate_proj.weight"] = self.experts_gate_up[e, :F]
+            out[q + "up_proj.weight"] = self.experts_gate_up[e, F:]
+            out[q + "down_proj.weight"] = self.experts_down[e]
+        return out
+
+    def forward(self, x: torch.Tensor, ctx: MoEContext | None = None, layer_idx: int = 0) -> torch.Tensor:
+        T, H = x.shape
+        logits = torch.nn.functional.linear(x.float(), self.router.float())
+        replay = ctx.replay.get(layer_idx) if ctx is not None and ctx.replay else None
+        w, ids = route(logits, self.k, self.renorm, replay, ctx.replay_mask if ctx is not None else None)
+        if ctx is not None and ctx.capture is not None:
+            ctx.capture[layer_idx] = ids.to(torch.int16)
+        if ctx is not None and ctx.ep_group is not None:
+            from axrl_b200.parallel.expert import ep_moe_forward
+
+            return ep_moe_forward(x, w, ids, self, ctx.ep_group)
+        flat = ids.reshape(-1)
+        order = torch.argsort(flat, stable=True)
+        tok = order // self.k
+        counts = torch.bincount(flat, minlength=self.E).tolist()
+        xs = x.index_select(0, tok)
+        if x.is_cuda:
+            from axrl_b200.ops.grouped import grouped_swiglu_ffn
+
+            ys = grouped_swiglu_ffn(xs, counts, self.experts_gate_up, self.experts_down)
+        else:
+            ys = grouped_ffn_ref(xs, counts, self.experts_gate_up, self.experts_down)
+        ys = ys.float() * w.reshape(-1)[order][:, None]
+        out = torch.zeros(T, H, dtype=torch.float32, device=x.device).index_add_(0, tok, ys)
+        return out.to(x.dtype)

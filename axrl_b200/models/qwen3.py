@@ -1,0 +1,274 @@
+"""Qwen3 dense and MoE decoder (trainer side), written over ``axrl_b200.ops``.
+
+The reference builds these models through Megatron-Bridge/TransformerEngine
+(``axrl/worker/megatron_worker.py:817-915``).  Here the model is a plain
+PyTorch module over this package's kernels, operating on *packed* tokens
+(``(T,)`` ids, ``(T,)`` positions, an :class:`AttnSpec`) so the same code runs
+flat varlen batches, prefix trees and CP shards.
+
+Layout choices (B200-first):
+* Q/K/V share one fused weight ``qkv_proj`` ((nq + 2 nkv) * D, H) and gate/up
+  share ``gate_up_proj`` (2F, H): one GEMM each, activations written once;
+* q/k RMSNorm + RoPE run in one kernel on the QKV GEMM output;
+* the LM head is never materialised for a whole micro-batch: the logprob op
+  chunks tokens and fuses log-softmax/label gather/entropy;
+* parameters are bf16; the optimizer owns fp32 master copies and attaches
+  ``main_grad`` fp32 buffers that weight-gradient GEMMs accumulate into.
+
+HF names are produced by :func:`hf_state_dict` / consumed by
+:func:`load_hf_state_dict` (split/concat of the fused weights).
+"""
+
+from __future__ import annotations
+
+import math
+import zlib
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+from torch.utils.checkpoint import checkpoint
+
+from axrl_b200.ops import core as ops
+from axrl_b200.ops.attention_spec import AttnSpec
+
+
+@dataclass
+class Qwen3Config:
+    vocab_size: int = 151936
+    hidden_size: int = 4096
+    intermediate_size: int = 12288
+    num_hidden_layers: int = 36
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1_000_000.0
+    tie_word_embeddings: bool = False
+    max_position_embeddings: int = 40960
+    # MoE (num_experts == 0 -> dense)
+    num_experts: int = 0
+    num_experts_per_tok: int = 8
+    moe_intermediate_size: int = 768
+    norm_topk_prob: bool = True
+    decoder_sparse_step: int = 1
+    mlp_only_layers: list[int] = field(default_factory=list)
+    initializer_range: float = 0.02
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    def layer_is_moe(self, i: int) -> bool:
+        return self.is_moe and i not in self.mlp_only_layers and (i + 1) % self.decoder_sparse_step == 0
+
+    def num_params(self) -> int:
+        H, D = self.hidden_size, self.head_dim
+        attn = H * (self.num_attention_heads + 2 * self.num_key_value_heads) * D + self.num_attention_heads * D * H + 2 * D
+        per = attn + 2 * H
+        total = 0
+        for i in range(self.num_hidden_layers):
+            if self.layer_is_moe(i):
+                total += per + H * self.num_experts + self.num_experts * 3 * H * self.moe_intermediate_size
+            else:
+                total += per + 3 * H * self.intermediate_size
+        total += self.vocab_size * H * (1 if self.tie_word_embeddings else 2) + H
+        return total
+
+    @staticmethod
+    def from_hf_dict(d: dict) -> "Qwen3Config":
+        keys = Qwen3Config.__dataclass_fields__.keys()
+        kw = {k: d[k] for k in keys if k in d}
+        if "head_dim" not in d and "hidden_size" in d:
+            kw["head_dim"] = d["hidden_size"] // d["num_attention_heads"]
+        return Qwen3Config(**kw)
+
+
+PRESETS: dict[str, Qwen3Config] = {
+    # Qwen3-8B shape: 36 layers, hidden 4096, 32q/8kv, head 128, FFN 12288, vocab 151936.
+    "qwen3-8b": Qwen3Config(),
+    # Qwen3-30B-A3B shape: 48 layers, hidden 2048, 32q/4kv, 128 experts top-8, expert FFN 768.
+    "qwen3-30b-a3b": Qwen3Config(hidden_size=2048, intermediate_size=6144, num_hidden_layers=48, num_attention_heads=32,
+                                 num_key_value_heads=4, head_dim=128, num_experts=128, num_experts_per_tok=8,
+                                 moe_intermediate_size=768),
+    "qwen3-0.6b": Qwen3Config(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28, num_attention_heads=16,
+                              num_key_value_heads=8, head_dim=128, tie_word_embeddings=True),
+    # Plumbing-check model: 2 layers, hidden 256, 4 heads, FFN 768, vocab 1024.
+    "tiny": Qwen3Config(vocab_size=1024, hidden_size=256, intermediate_size=768, num_hidden_layers=2, num_attention_heads=4,
+                        num_key_value_heads=4, head_dim=64, rope_theta=10000.0, tie_word_embeddings=False),
+    "tiny-moe": Qwen3Config(vocab_size=1024, hidden_size=256, intermediate_size=768, num_hidden_layers=2, num_attention_heads=4,
+                            num_key_value_heads=2, head_dim=64, rope_theta=10000.0, num_experts=8, num_experts_per_tok=2,
+                            moe_intermediate_size=128),
+}
+
+
+def resolve_preset(name: str) -> Qwen3Config:
+    key = name.split(":", 1)[1] if name.startswith("synthetic:") else name
+    if key not in PRESETS:
+        raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}")
+    return PRESETS[key]
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.rms_norm(x, self.weight, self.eps)
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: Qwen3Config, tp_size: int = 1) -> None:
+        super().__init__()
+        assert cfg.num_attention_heads % tp_size == 0 and cfg.num_key_value_heads % tp_size == 0
+        self.nq = cfg.num_attention_heads // tp_size
+        self.nkv = cfg.num_key_value_heads // tp_size
+        self.d = cfg.head_dim
+        self.eps = cfg.rms_norm_eps
+        H = cfg.hidden_size
+        self.qkv_proj = nn.Parameter(torch.empty((self.nq + 2 * self.nkv) * self.d, H))
+        self.o_proj = nn.Parameter(torch.empty(H, self.nq * self.d))
+        self.q_norm = nn.Parameter(torch.ones(self.d))
+        self.k_norm = nn.Parameter(torch.ones(self.d))
+
+    def forward(self, x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec) -> torch.Tensor:
+        qkv = ops.linear(x, self.qkv_proj)
+        q, k, v = ops.qk_norm_rope(qkv, self.q_norm, self.k_norm, pos, inv_freq, self.nq, self.nkv, self.eps)
+        o = ops.attention(q, k, v, spec)
+        return ops.linear(o.reshape(o.shape[0], -1), self.o_proj)
+
+
+class MLP(nn.Module):
+    def __init__(self, hidden: int, ffn: int) -> None:
+        super().__init__()
+        self.gate_up_proj = nn.Parameter(torch.empty(2 * ffn, hidden))
+        self.down_proj = nn.Parameter(torch.empty(hidden, ffn))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.linear(ops.swiglu(ops.linear(x, self.gate_up_proj)), self.down_proj)
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: Qwen3Config, layer_idx: int, tp_size: int = 1) -> None:
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        self.self_attn = Attention(cfg, tp_size)
+        self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        if cfg.layer_is_moe(layer_idx):
+            from axrl_b200.models.moe import MoEBlock
+
+            self.mlp: nn.Module = MoEBlock(cfg)
+        else:
+            self.mlp = MLP(cfg.hidden_size, cfg.intermediate_size // tp_size)
+
+    def forward(self, h: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, moe_ctx=None) -> torch.Tensor:  # noqa: ANN001
+        h = h + self.self_attn(self.input_layernorm(h), pos, inv_freq, spec)
+        x = self.post_attention_layernorm(h)
+        if moe_ctx is not None and hasattr(self.mlp, "router"):
+            return h + self.mlp(x, moe_ctx, self.layer_idx)
+        return h + self.mlp(x)
+
+
+class Qwen3Model(nn.Module):
+    """Decoder stack.  ``forward`` returns final hidden states (T, H); the LM head
+    is applied by :meth:`logprobs` (fused, chunked) or :meth:`logits`."""
+
+    def __init__(self, cfg: Qwen3Config, tp_size: int = 1) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.embed_tokens = nn.Parameter(torch.empty(cfg.vocab_size, cfg.hidden_size))
+        self.layers = nn.ModuleList(DecoderLayer(cfg, i, tp_size) for i in range(cfg.num_hidden_layers))
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        self.lm_head = None if cfg.tie_word_embeddings else nn.Parameter(torch.empty(cfg.vocab_size, cfg.hidden_size))
+        self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.head_dim, cfg.rope_theta), persistent=False)
+        self.recompute = False
+
+    @property
+    def lm_weight(self) -> torch.Tensor:
+        return self.embed_tokens if self.lm_head is None else self.lm_head
+
+    @torch.no_grad()
+    def init_weights(self, seed: int = 0) -> None:
+        """Random init from ``seed`` (normal(0, 0.02), out-projections scaled by 1/sqrt(2L))."""
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        std = self.cfg.initializer_range
+        out_std = std / math.sqrt(2 * self.cfg.num_hidden_layers)
+        for name, p in self.named_parameters():
+            if p.dim() == 1:
+                p.fill_(1.0)
+                continue
+            s = out_std if name.endswith(("o_proj", "down_proj")) else std
+            if p.is_cuda:
+                # Per-tensor CUDA generator seeded deterministically from (seed, name).
+                cg = torch.Generator(device=p.device).manual_seed(seed * 1000003 + zlib.crc32(name.encode()))
+                p.normal_(0.0, s, generator=cg)
+            else:
+                p.copy_(torch.randn(p.shape, generator=g) * s)
+
+    def embed(self, ids: torch.Tensor) -> torch.Tensor:
+        return ops.embedding(ids, self.embed_tokens)
+
+    def forward(self, ids: torch.Tensor, pos: torch.Tensor, spec: AttnSpec, moe_ctx=None) -> torch.Tensor:  # noqa: ANN001
+        h = self.embed(ids)
+        inv = self.inv_freq
+        for layer in self.layers:
+            if self.recompute and torch.is_grad_enabled():
+                h = checkpoint(layer, h, pos, inv, spec, moe_ctx, use_reentrant=False)
+            else:
+                h = layer(h, pos, inv, spec, moe_ctx)
+        return self.norm(h)
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        return torch.nn.functional.linear(hidden.float(), self.lm_weight.float())
+
+    def logprobs(self, hidden: torch.Tensor, labels: torch.Tensor, temperature: float = 1.0, entropy: bool = False):  # noqa: ANN201
+        from axrl_b200.ops.logprob import fused_logprob
+
+        return fused_logprob(hidden, self.lm_weight, labels, temperature=temperature, compute_entropy=entropy)
+
+
+# ----------------------------------------------------------------------------- HF naming
+
+
+def hf_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
+    """Unfused HF-named tensors (views where possible)."""
+    cfg = model.cfg
+    out: dict[str, torch.Tensor] = {"model.embed_tokens.weight": model.embed_tokens, "model.norm.weight": model.norm.weight}
+    if model.lm_head is not None:
+        out["lm_head.weight"] = model.lm_head
+    for i, layer in enumerate(model.layers):
+        p = f"model.layers.{i}."
+        a = layer.self_attn
+        q, k, v = a.qkv_proj.split([a.nq * a.d, a.nkv * a.d, a.nkv * a.d], 0)
+        out |= {p + "self_attn.q_proj.weight": q, p + "self_attn.k_proj.weight": k, p + "self_attn.v_proj.weight": v,
+                p + "self_attn.o_proj.weight": a.o_proj, p + "self_attn.q_norm.weight": a.q_norm,
+                p + "self_attn.k_norm.weight": a.k_norm, p + "input_layernorm.weight": layer.input_layernorm.weight,
+                p + "post_attention_layernorm.weight": layer.post_attention_layernorm.weight}
+        if cfg.layer_is_moe(i):
+            out |= layer.mlp.hf_tensors(p)
+        else:
+            g, u = layer.mlp.gate_up_proj.chunk(2, 0)
+            out |= {p + "mlp.gate_proj.weight": g, p + "mlp.up_proj.weight": u, p + "mlp.down_proj.weight": layer.mlp.down_proj}
+    return out
+
+
+@torch.no_grad()
+def load_hf_state_dict(model: Qwen3Model, sd: dict[str, torch.Tensor], strict: bool = True) -> list[str]:
+    """Copy HF tensors into the fused parameters; returns missing names."""
+    targets = hf_state_dict(model)
+    missing = []
+    for name, dst in targets.items():
+        src = sd.get(name)
+        if src is None:
+            if name == "lm_head.weight" and "model.embed_tokens.weight" in sd:
+                src = sd["model.embed_tokens.weight"]
+            else:
+                missing.append(name)
+                continue
+        dst.copy_(src.to(dst.dtype))
+    if strict and missing:
+        raise KeyError(f"missing HF tensors: {missing[:8]}{'...' if len(missing) > 8 else ''}")
+    return missing

@@ -1,0 +1,238 @@
+"""Autograd-aware hot ops.
+
+CUDA tensors run the sm_100a kernels in ``axrl_b200/csrc`` (loaded through
+:mod:`axrl_b200.ops._ext`, which raises when the extension is missing).  CPU
+tensors run the PyTorch definitions below, which double as the numerical
+oracle for the GPU tests.
+
+Op                 | reference call site it replaces
+-------------------|-----------------------------------------------------------
+rms_norm           | TE fused RMSNorm inside Megatron layers
+qk_norm_rope       | TE fused RoPE (``axrl/utils/megatron/magi_forward.py:405-430``) + Qwen3 q/k norm
+swiglu             | Megatron/TE gated activation
+attention          | TE FA3 THD varlen / MagiAttention FFA (``magi_forward.py:445-466``)
+linear             | TE / cuBLAS dense GEMMs
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from axrl_b200.ops import _ext
+from axrl_b200.ops.attention_spec import AttnSpec, dense_mask
+
+# ----------------------------------------------------------------------------- RMSNorm
+
+
+def _rms_ref(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):  # noqa: ANN001, ANN205
+        y, rstd = _ext.ext().rmsnorm_fwd(x, w, eps)
+        ctx.save_for_backward(x, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        x, w, rstd = ctx.saved_tensors
+        dx, dw = _ext.ext().rmsnorm_bwd(dy.contiguous(), x, w, rstd)
+        return dx, dw.to(w.dtype), None
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    if not x.is_cuda:
+        return _rms_ref(x, w, eps)
+    shp = x.shape
+    return _RMSNorm.apply(x.reshape(-1, shp[-1]).contiguous(), w, eps).view(shp)
+
+
+# ----------------------------------------------------------------------------- q/k norm + RoPE
+
+
+def rope_inv_freq(head_dim: int, theta: float, device=None) -> torch.Tensor:  # noqa: ANN001
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32, device=device) / head_dim))
+
+
+def _rope_ref(x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
+    # x: (T, H, D); neox-style rotate-half, angles in fp32.
+    ang = pos.float()[:, None] * inv_freq[None, :].to(pos.device)
+    cos = torch.cat([ang.cos(), ang.cos()], -1)[:, None, :]
+    sin = torch.cat([ang.sin(), ang.sin()], -1)[:, None, :]
+    xf = x.float()
+    h = xf.shape[-1] // 2
+    rot = torch.cat([-xf[..., h:], xf[..., :h]], -1)
+    return (xf * cos + rot * sin).to(x.dtype)
+
+
+def _qk_norm_rope_ref(qkv, qw, kw, pos, inv_freq, nq, nkv, eps):  # noqa: ANN001, ANN202
+    T = qkv.shape[0]
+    D = inv_freq.numel() * 2
+    q, k, v = qkv.view(T, nq + 2 * nkv, D).split([nq, nkv, nkv], dim=1)
+    q = _rope_ref(_rms_ref(q, qw, eps), pos, inv_freq)
+    k = _rope_ref(_rms_ref(k, kw, eps), pos, inv_freq)
+    return q.contiguous(), k.contiguous(), v.contiguous()
+
+
+class _QKNormRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, qw, kw, pos, inv_freq, nq, nkv, eps):  # noqa: ANN001, ANN205
+        q, k, v, rstd = _ext.ext().qknorm_rope_fwd(qkv, qw, kw, pos, inv_freq, nq, nkv, eps)
+        ctx.save_for_backward(qkv, qw, kw, pos, inv_freq, rstd)
+        ctx.shape = (nq, nkv)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):  # noqa: ANN001, ANN205
+        qkv, qw, kw, pos, inv_freq, rstd = ctx.saved_tensors
+        nq, nkv = ctx.shape
+        dqkv, dqw, dkw = _ext.ext().qknorm_rope_bwd(dq.contiguous(), dk.contiguous(), dv.contiguous(), qkv, qw, kw, pos, inv_freq, rstd, nq, nkv)
+        return dqkv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None, None, None
+
+
+def qk_norm_rope(qkv, q_norm_w, k_norm_w, pos, inv_freq, nq: int, nkv: int, eps: float = 1e-6):  # noqa: ANN001, ANN201
+    """Split fused QKV rows, RMS-normalise q/k per head, apply RoPE at ``pos``.
+    Returns contiguous ``q (T,nq,D)``, ``k (T,nkv,D)``, ``v (T,nkv,D)``."""
+    if not qkv.is_cuda:
+        return _qk_norm_rope_ref(qkv, q_norm_w, k_norm_w, pos, inv_freq, nq, nkv, eps)
+    return _QKNormRope.apply(qkv.contiguous(), q_norm_w, k_norm_w, pos.to(torch.int32).contiguous(), inv_freq, nq, nkv, eps)
+
+
+# ----------------------------------------------------------------------------- SwiGLU
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):  # noqa: ANN001, ANN205
+        ctx.save_for_backward(gu)
+        return _ext.ext().swiglu_fwd(gu)
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        (gu,) = ctx.saved_tensors
+        return _ext.ext().swiglu_bwd(dy.contiguous(), gu)
+
+
+def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` where each row is ``[gate | up]``."""
+    if not gate_up.is_cuda:
+        g, u = gate_up.float().chunk(2, -1)
+        return (torch.nn.functional.silu(g) * u).to(gate_up.dtype)
+    return _SwiGLU.apply(gate_up.contiguous())
+
+
+# ----------------------------------------------------------------------------- attention
+
+
+def _attn_ref(q, k, v, spec: AttnSpec, scale: float):  # noqa: ANN001, ANN202
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    rep = Hq // Hkv
+    mask = dense_mask(spec).to(q.device)
+    kk = k.float().repeat_interleave(rep, 1)
+    vv = v.float().repeat_interleave(rep, 1)
+    s = torch.einsum("thd,shd->hts", q.float(), kk) * scale
+    s = s.masked_fill(~mask[None], float("-inf"))
+    p = torch.softmax(s, -1).nan_to_num(0.0)
+    return torch.einsum("hts,shd->thd", p, vv).to(q.dtype)
+
+
+class _Attn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, spec, scale):  # noqa: ANN001, ANN205
+        o, lse = _ext.ext().attn_fwd(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.spec, ctx.scale = spec, scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):  # noqa: ANN001, ANN205
+        q, k, v, o, lse = ctx.saved_tensors
+        s = ctx.spec
+        dq, dk, dv = _ext.ext().attn_bwd(do.contiguous(), q, k, v, o, lse, s.kseg, s.qr, s.bwd_tiles, ctx.scale)
+        return dq, dk, dv, None, None
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: AttnSpec, scale: float | None = None) -> torch.Tensor:
+    """Range-list attention over packed tokens.  q: (T,Hq,D); k,v: (T,Hkv,D) with GQA."""
+    scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
+    if not q.is_cuda:
+        return _attn_ref(q, k, v, spec, scale)
+    if not spec.qseg.is_cuda:
+        spec = spec.to(q.device)
+    return _Attn.apply(q.contiguous(), k.contiguous(), v.contiguous(), spec, scale)
+
+
+# ----------------------------------------------------------------------------- linear
+
+
+def _gemm(a: torch.Tensor, b: torch.Tensor, trans_b: bool) -> torch.Tensor:
+    return _ext.ext().gemm(a, b, trans_b)
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w):  # noqa: ANN001, ANN205
+        ctx.save_for_backward(x, w)
+        return _ext.ext().linear_fwd(x, w)
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        x, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        e = _ext.ext()
+        dx = e.linear_dgrad(dy, w) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            main = getattr(w, "main_grad", None)
+            if main is not None:
+                e.linear_wgrad_acc(dy, x, main)  # fp32 accumulate in place
+                dw = None
+            else:
+                dw = e.linear_wgrad(dy, x)
+        return dx, dw
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w.T`` for x (..., K), w (N, K).  On GPU the weight grad accumulates
+    straight into ``w.main_grad`` (fp32) when present."""
+    if not x.is_cuda:
+        return torch.nn.functional.linear(x, w)
+    shp = x.shape
+    y = _Linear.apply(x.reshape(-1, shp[-1]).contiguous(), w)
+    return y.view(*shp[:-1], w.shape[0])
+
+
+# ----------------------------------------------------------------------------- embedding
+
+
+class _Embed(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, table):  # noqa: ANN001, ANN205
+        ctx.save_for_backward(ids)
+        ctx.table = table
+        return _ext.ext().embed_fwd(ids, table)
+
+    @staticmethod
+    def backward(ctx, dout):  # noqa: ANN001, ANN205
+        (ids,) = ctx.saved_tensors
+        table = ctx.table
+        main = getattr(table, "main_grad", None)
+        if main is not None:
+            _ext.ext().embed_bwd(ids, dout.contiguous(), main)
+            return None, None
+        g = torch.zeros(table.shape, dtype=torch.float32, device=table.device)
+        _ext.ext().embed_bwd(ids, dout.contiguous(), g)
+        return None, g.to(table.dtype)
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    """Row gather; on GPU the backward scatter-adds into ``table.main_grad`` (fp32)."""
+    if not table.is_cuda:
+        return torch.nn.functional.embedding(ids.long(), table)
+    return _Embed.apply(ids.long().contiguous(), table)

@@ -1,0 +1,101 @@
+"""Inference-side ops over the paged KV cache (rollout engine).
+
+Cache layout per layer: ``k_cache, v_cache: [num_pages, Hkv, page_size, D]``;
+a token's slot is ``page * page_size + offset``.  CUDA tensors use the kernels
+in ``csrc/kernels/decode_attn.cu`` / ``norm_act.cu`` / ``vocab.cu``; CPU
+tensors use the PyTorch definitions here (oracle + CPU plumbing runs).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from axrl_b200.ops import _ext
+from axrl_b200.ops.core import _qk_norm_rope_ref
+
+SPLIT_TOKENS = 256  # tokens per decode CTA (must match dec::SPLIT)
+
+
+def _scatter_ref(cache: torch.Tensor, x: torch.Tensor, slots: torch.Tensor) -> None:
+    P = cache.shape[2]
+    page, off = slots // P, slots % P
+    cache[page, :, off, :] = x.to(cache.dtype)
+
+
+def qk_norm_rope_cache(qkv, qw, kw, pos, inv_freq, nq, nkv, eps, k_cache, v_cache, slots):  # noqa: ANN001, ANN201
+    """q/k norm + RoPE and write k/v into the paged caches at ``slots``.  Returns q, k, v."""
+    if not qkv.is_cuda:
+        q, k, v = _qk_norm_rope_ref(qkv, qw, kw, pos, inv_freq, nq, nkv, eps)
+        _scatter_ref(k_cache, k, slots.long())
+        _scatter_ref(v_cache, v, slots.long())
+        return q, k, v
+    return _ext.ext().qknorm_rope_cache(qkv, qw, kw, pos, inv_freq, nq, nkv, eps, k_cache, v_cache, slots)
+
+
+def decode_attention_ref(q, k_cache, v_cache, block_table, seq_lens, scale):  # noqa: ANN001, ANN201
+    B, Hq, D = q.shape
+    Hkv, P = k_cache.shape[1], k_cache.shape[2]
+    out = torch.zeros_like(q)
+    for b in range(B):
+        n = int(seq_lens[b])
+        if n == 0:
+            continue
+        pages = block_table[b, : (n + P - 1) // P].long()
+        k = k_cache[pages].permute(0, 2, 1, 3).reshape(-1, Hkv, D)[:n].float()
+        v = v_cache[pages].permute(0, 2, 1, 3).reshape(-1, Hkv, D)[:n].float()
+        rep = Hq // Hkv
+        k = k.repeat_interleave(rep, 1)
+        v = v.repeat_interleave(rep, 1)
+        s = torch.einsum("hd,thd->ht", q[b].float(), k) * scale
+        p = torch.softmax(s, -1)
+        out[b] = torch.einsum("ht,thd->hd", p, v).to(q.dtype)
+    return out
+
+
+class DecodeWorkspace:
+    """Split-KV partial buffers sized for (max_batch, Hq, max_context)."""
+
+    def __init__(self, max_batch: int, hq: int, max_context: int, device) -> None:  # noqa: ANN001
+        self.splits = max(1, math.ceil(max_context / SPLIT_TOKENS))
+        self.part_o = torch.empty(max_batch * hq * self.splits * 128, dtype=torch.float32, device=device)
+        self.part_ml = torch.empty(max_batch * hq * self.splits * 2, dtype=torch.float32, device=device)
+
+
+def paged_decode_attention(q, k_cache, v_cache, block_table, seq_lens, ws: DecodeWorkspace | None, scale: float | None = None):  # noqa: ANN001, ANN201
+    scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
+    if not q.is_cuda:
+        return decode_attention_ref(q, k_cache, v_cache, block_table, seq_lens, scale)
+    out = torch.empty_like(q)
+    _ext.ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, out, ws.part_o, ws.part_ml, ws.splits, scale)
+    return out
+
+
+def sample_ref(logits: torch.Tensor, temperature: torch.Tensor, generator: torch.Generator | None = None,
+               forced: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    lf = logits.float()
+    t = temperature.float().to(lf.device)
+    greedy = t <= 0
+    scaled = lf / torch.where(greedy, torch.ones_like(t), t)[:, None]
+    logp = torch.log_softmax(scaled, -1)
+    probs = logp.exp()
+    tok = torch.multinomial(probs, 1, generator=generator).squeeze(-1)
+    tok = torch.where(greedy, scaled.argmax(-1), tok)
+    if forced is not None:
+        tok = torch.where(forced >= 0, forced.to(tok.device), tok)
+    return tok, logp.gather(-1, tok[:, None]).squeeze(-1)
+
+
+def sample(logits: torch.Tensor, temperature: torch.Tensor, seed: torch.Tensor, generator: torch.Generator | None = None,
+           forced: torch.Tensor | None = None, row_ids: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Categorical sample per row at its temperature (<=0: greedy) with the token's log-prob.
+    ``forced[row] >= 0`` overrides the token (its log-prob is still reported).
+    ``row_ids`` names each row's random stream (stable across batch re-ordering)."""
+    if not logits.is_cuda:
+        return sample_ref(logits, temperature, generator, forced)
+    B = logits.shape[0]
+    tok = torch.empty(B, dtype=torch.int64, device=logits.device)
+    lp = torch.empty(B, dtype=torch.float32, device=logits.device)
+    _ext.ext().sample_tokens(logits, temperature, seed, tok, lp, row_ids, forced)
+    return tok, lp

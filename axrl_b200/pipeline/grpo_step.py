@@ -1,0 +1,186 @@
+"""One synthetic GRPO step end to end: rollout -> rewards -> advantages -> packing ->
+ref/old logprobs -> train -> weight sync.
+
+This is the driver used by the plumbing run (tiny model on CPU, fp32) and by
+the B200 benchmark (Qwen3-8B shape, bf16).  It follows the reference online
+loop (``axrl/pipeline/controller.py:1617-1653``, rollout/train/sync of
+§3.1-3.4 in the reference docs): prompts are random token ids, the reward is
+1 when the response contains ``reward_token``, response lengths are either
+sampled freely (stop on EOS / max_new_tokens) or forced through EOS to a
+log-normal draw.
+
+Colocated single-process mode: the rollout engine reads the trainer's bf16
+parameters directly (zero-copy weight sync — the "sync" is the version bump
+plus a prefix-cache flush).  ``separate_rollout_copy=True`` keeps an engine-
+owned copy and syncs by copying every tensor (what the tiny plumbing config
+asks for).
+"""
+
+from __future__ import annotations
+
+import copy
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from axrl_b200.configs import GrpoTrainerConfig, MegatronWorkerConfig
+from axrl_b200.data.prefix_tree import merge_trajectory_samples
+from axrl_b200.data.sample import Sample, SampleBatch
+from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+from axrl_b200.pipeline.rewards import group_advantages
+from axrl_b200.rollout.engine import GenRequest, RolloutEngine
+from axrl_b200.train.engine import TrainEngine
+from axrl_b200.trainer.grpo_trainer import GrpoTrainer
+from axrl_b200.utils import iostats
+
+
+@dataclass
+class SyntheticGRPOConfig:
+    num_prompts: int = 8
+    prompt_len: int = 32
+    group_size: int = 4
+    max_new_tokens: int = 64
+    temperature: float = 1.0
+    reward_token: int = 7
+    # forced response lengths: log-normal(median, sigma) clipped to [min, max]; None = free sampling
+    forced_len_median: float | None = None
+    forced_len_sigma: float = 1.0
+    forced_len_min: int = 16
+    forced_len_max: int = 8192
+    eos_token_id: int = 0
+    merge_group_prompts: bool = True  # prefix-tree pack each group's shared prompt
+    compute_ref_logprobs: bool = True
+    compute_old_logprobs: bool = True
+    separate_rollout_copy: bool = False
+    seed: int = 0
+    kv_tokens: int | None = None
+    max_batch: int | None = None
+    use_cuda_graph: bool = True
+    extra: dict = field(default_factory=dict)
+
+
+class SyntheticGRPO:
+    def __init__(self, model_cfg: Qwen3Config, worker_cfg: MegatronWorkerConfig, grpo_cfg: GrpoTrainerConfig,
+                 sc: SyntheticGRPOConfig, device: str | torch.device = "cpu", train_engine: TrainEngine | None = None) -> None:
+        self.sc = sc
+        self.mcfg = model_cfg
+        self.device = torch.device(device)
+        self.train = train_engine or TrainEngine(worker_cfg, model_cfg, self.device)
+        self.trainer = GrpoTrainer(grpo_cfg)
+        self.rng = np.random.default_rng(sc.seed)
+        self.ref_weights = self.train.snapshot_weights() if sc.compute_ref_logprobs else None
+        if self.ref_weights is not None and self.device.type == "cuda":
+            self.ref_weights = self.ref_weights.pin_memory()
+        rollout_model = self.train.model
+        if sc.separate_rollout_copy:
+            rollout_model = copy.deepcopy(self.train.model)
+            for p in rollout_model.parameters():
+                p.requires_grad_(False)
+        n_seq = sc.num_prompts * sc.group_size
+        max_ctx = sc.prompt_len + (sc.forced_len_max if sc.forced_len_median else sc.max_new_tokens) + 8
+        kv_tokens = sc.kv_tokens or n_seq * (-(-max_ctx // 64) * 64)
+        self.rollout = RolloutEngine(rollout_model, max_batch=sc.max_batch or n_seq, kv_tokens=kv_tokens, page_size=64,
+                                     max_context=max_ctx, max_prefill_tokens=max(16384, sc.prompt_len), seed=sc.seed,
+                                     use_cuda_graph=sc.use_cuda_graph, eos_token_id=sc.eos_token_id)
+        self.weight_version = 0
+        self.step_idx = 0
+        self.last: dict = {}
+
+    # ------------------------------------------------------------------ pieces
+    def make_requests(self) -> list[GenRequest]:
+        sc, V = self.sc, self.mcfg.vocab_size
+        reqs = []
+        for p in range(sc.num_prompts):
+            prompt = self.rng.integers(1, V, size=sc.prompt_len).tolist()
+            for g in range(sc.group_size):
+                forced = None
+                if sc.forced_len_median:
+                    forced = int(np.clip(np.exp(np.log(sc.forced_len_median) + sc.forced_len_sigma * self.rng.standard_normal()),
+                                         sc.forced_len_min, sc.forced_len_max))
+                rid = f"s{self.step_idx}-p{p}-g{g}"
+                reqs.append(GenRequest(rid=rid, prompt=prompt, max_new_tokens=forced or sc.max_new_tokens, temperature=sc.temperature,
+                                       stop_token_ids=() if forced else (sc.eos_token_id,), forced_len=forced,
+                                       forced_token=sc.eos_token_id, seed_stream=self.step_idx * 1_000_000 + p * 1000 + g))
+        return reqs
+
+    def build_samples(self, reqs, results) -> tuple[list[Sample], dict]:  # noqa: ANN001
+        sc = self.sc
+        samples, scores = [], []
+        for r, res in zip(reqs, results):
+            scores.append(1.0 if sc.reward_token in res.output_ids else 0.0)
+        out: list[Sample] = []
+        for p in range(sc.num_prompts):
+            grp = slice(p * sc.group_size, (p + 1) * sc.group_size)
+            adv, mean, std = group_advantages(scores[grp])
+            group_samples = []
+            for i, (r, res) in enumerate(zip(reqs[grp], results[grp])):
+                s = Sample.from_tokens(r.prompt, res.output_ids, reward=scores[grp][i], advantage=float(adv[i]),
+                                       rollout_logprobs=res.output_logprobs, trajectory_id=p)
+                s.reward_baseline = mean
+                group_samples.append(s)
+            if sc.merge_group_prompts and sc.group_size > 1:
+                m = merge_trajectory_samples(group_samples, align_size=1 if self.device.type == "cpu" else 8)
+                m.trajectory_id = p
+                out.append(m)
+            else:
+                out.extend(group_samples)
+        resp_tokens = sum(len(res.output_ids) for res in results)
+        return out, {"reward_mean": float(np.mean(scores)), "response_tokens": resp_tokens,
+                     "mean_response_len": resp_tokens / max(1, len(results))}
+
+    # ------------------------------------------------------------------ the step
+    def run_step(self) -> dict:
+        sc = self.sc
+        t = {}
+        io0 = iostats.snapshot()
+        t0 = time.perf_counter()
+        reqs = self.make_requests()
+        results = self.rollout.generate(reqs)
+        t["rollout_s"] = time.perf_counter() - t0
+
+        t1 = time.perf_counter()
+        samples, info = self.build_samples(reqs, results)
+        batch = SampleBatch.from_samples(samples)
+        t["pack_s"] = time.perf_counter() - t1
+
+        t2 = time.perf_counter()
+        if sc.compute_ref_logprobs:
+            cur = self.train.snapshot_weights() if self.device.type == "cpu" else None
+            if cur is None:
+                cur = self.train.optim.bf16.clone() if self.train.optim else None
+            self.train.load_weights(self.ref_weights)
+            batch["ref_logprobs"] = self.train.compute_logprobs(batch, sc.temperature)
+            self.train.load_weights(cur)
+            del cur
+        if sc.compute_old_logprobs:
+            batch["old_logprobs"] = self.train.compute_logprobs(batch, sc.temperature)
+        else:
+            batch["old_logprobs"] = batch["rollout_logprobs"].clone()
+        if "ref_logprobs" not in batch.tensors:
+            batch["ref_logprobs"] = batch["old_logprobs"]
+        t["logprob_s"] = time.perf_counter() - t2
+
+        t3 = time.perf_counter()
+        metrics = self.train.train_step(batch, self.trainer, temperature=sc.temperature)
+        t["train_s"] = time.perf_counter() - t3
+
+        t4 = time.perf_counter()
+        self.sync_weights()
+        t["sync_s"] = time.perf_counter() - t4
+        self.step_idx += 1
+        io1 = iostats.snapshot()
+        t["h2d_bytes"], t["d2h_bytes"] = io1[0] - io0[0], io1[1] - io0[1]
+        trained_tokens = int(batch["seq_len"].sum())
+        out = {**metrics, **info, **t, "trained_tokens": trained_tokens, "num_samples": len(samples),
+               "sequences": len(results), "total_tokens": sum(len(r.prompt) + len(x.output_ids) for r, x in zip(reqs, results))}
+        self.last = out
+        return out
+
+    def sync_weights(self) -> None:
+        """Trainer -> rollout weight sync (in-process)."""
+        if self.sc.separate_rollout_copy:
+            self.rollout.update_weights_from_model(self.train.model)
+        self.rollout.reset_prefix_cache()
+        self.weight_version += 1

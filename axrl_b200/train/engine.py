@@ -1,0 +1,170 @@
+"""Trainer engine: logprob recompute and the GRPO/PPO/SFT train step on packed micro-batches.
+
+Reference counterpart: ``MegatronWorker`` (``axrl/worker/megatron_worker.py:173-1480``):
+``forward_backward_batch`` (:986-1031), the per-token loss rescale (:1041-1057),
+``train_step`` (:1059-1123: grad norm, clip, optimizer step) and
+``_compute_logprobs_from_local_batches`` (:1195-1303).
+
+Loss scaling follows Megatron's ``calculate_per_token_loss`` contract: each
+micro-batch contributes ``loss_mb * denom_mb`` and the accumulated gradient is
+divided once by the global ``sum(denom)`` (all micro-batches, all DP ranks).
+Here that division is folded into the fused Adam kernel (``grad_scale``).
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from axrl_b200.configs import MegatronWorkerConfig
+from axrl_b200.data.sample import SampleBatch
+from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+from axrl_b200.train.optimizer import FlatAdamW
+from axrl_b200.train.packing import PackedMicroBatch, pack_rows, split_balanced
+from axrl_b200.utils import iostats
+
+
+@dataclass
+class ParallelCtx:
+    """Process groups of one trainer rank (None = not parallel along that axis)."""
+
+    dp_group: object | None = None
+    tp_group: object | None = None
+    dp_size: int = 1
+    dp_rank: int = 0
+    tp_size: int = 1
+    tp_rank: int = 0
+
+
+class TrainEngine:
+    def __init__(self, cfg: MegatronWorkerConfig, model_cfg: Qwen3Config, device: torch.device | str = "cpu",
+                 dtype: torch.dtype | None = None, par: ParallelCtx | None = None, model: Qwen3Model | None = None):
+        self.cfg = cfg
+        self.mcfg = model_cfg
+        self.device = torch.device(device)
+        self.par = par or ParallelCtx()
+        dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
+        if model is None:
+            model = Qwen3Model(model_cfg, tp_size=self.par.tp_size)
+            model.init_weights(cfg.seed)
+            model = model.to(device=self.device, dtype=dtype)
+            model.inv_freq = model.inv_freq.float()
+        self.model = model
+        self.model.recompute = cfg.recompute_granularity == "full"
+        self.optim = None if cfg.inference_only else FlatAdamW(self.model, cfg.optimizer, cfg.lr_scheduler)
+        self.max_tokens = cfg.max_tokens_per_micro_batch
+        self.last_timing: dict[str, float] = {}
+
+    # ------------------------------------------------------------------ micro-batches
+    def micro_batches(self, batch: SampleBatch) -> list[PackedMicroBatch]:
+        lengths = []
+        infos = batch.objects.get("merge_info") or [None] * len(batch)
+        for r in range(len(batch)):
+            lengths.append(infos[r].total_padded if infos[r] is not None else int(batch["seq_len"][r]))
+        min_count = 1
+        if self.par.dp_group is not None and self.par.dp_size > 1:
+            # every DP rank must run the same number of micro-batches
+            n = torch.tensor([len(split_balanced(lengths, self.max_tokens))], dtype=torch.int64)
+            dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.par.dp_group)
+            min_count = int(n)
+        parts = split_balanced(lengths, self.max_tokens, min_count=min_count)
+        return [pack_rows(batch, p) for p in parts if p]
+
+    # ------------------------------------------------------------------ forward
+    def _hidden(self, mb: PackedMicroBatch, moe_ctx=None) -> torch.Tensor:  # noqa: ANN001
+        return self.model(mb.ids, mb.pos, mb.spec, moe_ctx)
+
+    @torch.no_grad()
+    def compute_logprobs(self, batch: SampleBatch, temperature: float = 1.0) -> torch.Tensor:
+        """Per-token log p(label) in the batch's (B, S) layout (0 where label is ignored)."""
+        self.model.eval()
+        B, S = batch["input_ids"].shape
+        out = torch.zeros((B, S), dtype=torch.float32)
+        for mb in self.micro_batches(batch):
+            dmb = mb.to(self.device)
+            h = self._hidden(dmb)
+            lp, _ = self.model.logprobs(h, dmb.labels.clamp(min=-1), temperature)
+            lp = torch.where(dmb.labels >= 0, lp, torch.zeros_like(lp))
+            dense = dmb.unpack(lp.float(), S).cpu()
+            if self.device.type == "cuda":
+                iostats.add_d2h(dense)
+            for li, r in enumerate(mb.rows):
+                out[r] = dense[li]
+        return out
+
+    # ------------------------------------------------------------------ train
+    def _global_denominator(self, batch: SampleBatch, trainer) -> float:  # noqa: ANN001
+        lm = batch["loss_mask"].bool()
+        turn_index = batch.get("turn_index", None)
+        from axrl_b200.trainer.grpo_trainer import get_num_turns
+
+        nt = get_num_turns(turn_index, lm) if (turn_index is not None and getattr(trainer.config, "micro_batch_denominator_type", "") == "seq_turn") else 0
+        d = torch.tensor([float(trainer.compute_micro_batch_denominator(lm, nt))], dtype=torch.float64)
+        if self.par.dp_group is not None and self.par.dp_size > 1:
+            dist.all_reduce(d, group=self.par.dp_group)
+        return float(d)
+
+    def train_step(self, batch: SampleBatch, trainer, temperature: float = 1.0, metrics_every_micro_batch: bool = True) -> dict:  # noqa: ANN001
+        """One optimizer step over ``batch`` (this rank's DP slice of one global batch)."""
+        assert self.optim is not None, "inference_only engine cannot train"
+        t0 = time.perf_counter()
+        self.model.train()
+        self.optim.zero_grad()
+        total_denom = max(self._global_denominator(batch, trainer), 1.0)
+        need_entropy = bool(getattr(trainer.config, "entropy_control", None) and
+                            (trainer.config.entropy_control.alpha > 0 or trainer.config.entropy_control.compute_entropy))
+        S = batch["input_ids"].shape[1]
+        mbs = self.micro_batches(batch)
+        metrics_acc: list[dict] = []
+        for i, mb in enumerate(mbs):
+            dmb = mb.to(self.device)
+            h = self._hidden(dmb)
+            lp, ent = self.model.logprobs(h, dmb.labels.clamp(min=-1), temperature, entropy=need_entropy)
+            lp = torch.where(dmb.labels >= 0, lp, torch.zeros_like(lp))
+            sub = batch.select_rows(mb.rows).to(self.device)
+            if self.device.type == "cuda":
+                iostats.add_h2d(*sub.tensors.values())
+            outputs = {"log_prob": dmb.unpack(lp, S),
+                       "entropy": dmb.unpack(ent, S) if ent is not None else torch.zeros((len(mb.rows), S), device=self.device)}
+            want = metrics_every_micro_batch or i == len(mbs) - 1
+            loss, denom, m = trainer.loss_func(outputs, sub, with_metrics=want)
+            (loss * denom.to(loss.dtype)).backward()
+            if want:
+                metrics_acc.append(m)
+        self.optim.fold_param_grads()
+        sq = self.optim.grad_sqnorm()
+        if self.par.dp_group is not None and self.par.dp_size > 1:
+            dist.all_reduce(self.optim.grad, group=self.par.dp_group)  # replicated-optimizer baseline path
+            sq = self.optim.grad_sqnorm()
+        norm = self.optim.step(grad_scale=1.0 / total_denom, sqnorm=sq)
+        out = {k: sum(d[k] for d in metrics_acc if k in d) / max(1, sum(1 for d in metrics_acc if k in d))
+               for k in {k for d in metrics_acc for k in d}}
+        out["grad_norm"] = float(norm)
+        out["num_micro_batches"] = len(mbs)
+        out["step_time_sec"] = time.perf_counter() - t0
+        out["lr"] = self.current_lr()
+        return out
+
+    def current_lr(self) -> float:
+        from axrl_b200.train.optimizer import lr_at
+
+        return lr_at(max(0, self.optim.step_count - 1), self.cfg.lr_scheduler) if self.optim else 0.0
+
+    # ------------------------------------------------------------------ weights
+    @torch.no_grad()
+    def snapshot_weights(self) -> torch.Tensor:
+        """CPU copy of all parameters (flat), e.g. the reference-policy snapshot."""
+        return self.optim.bf16.detach().to("cpu", copy=True) if self.optim else torch.cat([p.detach().reshape(-1).cpu() for p in self.model.parameters()])
+
+    @torch.no_grad()
+    def load_weights(self, flat: torch.Tensor) -> None:
+        if self.optim is not None:
+            self.optim.bf16.copy_(flat.to(self.optim.bf16.device, non_blocking=True))
+        else:
+            off = 0
+            for p in self.model.parameters():
+                p.copy_(flat[off:off + p.numel()].view(p.shape))
+                off += p.numel()
