@@ -32,6 +32,13 @@ void adamw_step(at::Tensor, at::Tensor, at::Tensor, at::Tensor, c10::optional<at
                 double, int64_t, c10::optional<at::Tensor>, double, double);
 at::Tensor embed_fwd(at::Tensor ids, at::Tensor table);
 void embed_bwd(at::Tensor ids, at::Tensor dout, at::Tensor grad);
+void p2p_reduce_shard(at::Tensor, at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
+void p2p_broadcast_shard(at::Tensor, at::Tensor, int64_t, int64_t, int64_t);
+void mc_reduce_shard(int64_t, at::Tensor, int64_t, int64_t, at::Tensor);
+void mc_broadcast_shard(int64_t, at::Tensor, int64_t, int64_t);
+void flag_signal(int64_t, int64_t, int64_t);
+void flag_wait_bounded(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
+void sync_push(at::Tensor, at::Tensor, at::Tensor, int64_t);
 }  // namespace ax
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -59,4 +66,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &ax::adamw_step);
   m.def("embed_fwd", &ax::embed_fwd);
   m.def("embed_bwd", &ax::embed_bwd);
+  m.def("p2p_reduce_shard", &ax::p2p_reduce_shard);
+  m.def("p2p_broadcast_shard", &ax::p2p_broadcast_shard);
+  m.def("mc_reduce_shard", &ax::mc_reduce_shard);
+  m.def("mc_broadcast_shard", &ax::mc_broadcast_shard);
+  m.def("flag_signal", &ax::flag_signal);
+  m.def("flag_wait_bounded", &ax::flag_wait_bounded);
+  m.def("sync_push", &ax::sync_push);
 }
