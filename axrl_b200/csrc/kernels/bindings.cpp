@@ -39,6 +39,9 @@ void mc_broadcast_shard(int64_t, at::Tensor, int64_t, int64_t);
 void flag_signal(int64_t, int64_t, int64_t);
 void flag_wait_bounded(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
 void sync_push(at::Tensor, at::Tensor, at::Tensor, int64_t);
+at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual);
+void decode_advance(int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor,
+                    at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor);
 }  // namespace ax
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -73,4 +76,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flag_signal", &ax::flag_signal);
   m.def("flag_wait_bounded", &ax::flag_wait_bounded);
   m.def("sync_push", &ax::sync_push);
+  m.def("linear_residual", &ax::linear_residual);
+  m.def("decode_advance", &ax::decode_advance);
 }

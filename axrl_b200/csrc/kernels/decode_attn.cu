@@ -7,7 +7,7 @@
 // (page, head) block is a contiguous page_size x 256-byte run.
 //
 // Kernel: one CTA per (sequence, kv head, split of SPLIT tokens); 4 warps, each warp owns one
-// 64-token slice.  The GQA group's q heads (<= 16) form the M=16 rows of mma.m16n8k16, so K/V
+// 32-token slice.  The GQA group's q heads (<= 16) form the M=16 rows of mma.m16n8k16, so K/V
 // are read exactly once per kv head.  The grid's split count is fixed by the cache capacity
 // (graph-capture friendly); CTAs past a sequence's end exit.  A combine kernel merges splits.
 #include "common.cuh"
@@ -17,7 +17,8 @@ namespace dec {
 
 constexpr int D = 128;
 constexpr int WARPS = 4;
-constexpr int SLICE = 64;                // tokens per warp
+constexpr int SLICE = 32;                // tokens per warp (68 KB smem per CTA: 3 CTAs per SM)
+constexpr int NSUB = SLICE / 8;          // n8 key tiles per warp
 constexpr int SPLIT = WARPS * SLICE;     // tokens per CTA
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -101,15 +102,15 @@ __global__ void __launch_bounds__(128) decode_k(Params p) {
   for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
   if (ws < we) {
-    float s[8][4];
+    float s[NSUB][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    for (int n = 0; n < NSUB; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
       uint32_t a0, a1, a2, a3;
       ldsm_x4(smem_u32(sQ + swz(lane & 15, kk * 16 + (lane >> 4) * 8)), a0, a1, a2, a3);
 #pragma unroll
-      for (int n2 = 0; n2 < 4; ++n2) {
+      for (int n2 = 0; n2 < NSUB / 2; ++n2) {
         uint32_t b0, b1, b2, b3;
         int key = n2 * 16 + (lane & 7) + (lane >> 4) * 8, col = kk * 16 + ((lane >> 3) & 1) * 8;
         ldsm_x4(smem_u32(sK + swz(key, col)), b0, b1, b2, b3);
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(128) decode_k(Params p) {
     for (int hh = 0; hh < 2; ++hh) {
       float mx = -INFINITY;
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int n = 0; n < NSUB; ++n)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           int tok = ws + n * 8 + (lane & 3) * 2 + e;
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(128) decode_k(Params p) {
       m[hh] = mx;
       float rs = 0.f;
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int n = 0; n < NSUB; ++n)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           float v = exp2f(s[n][2 * hh + e] - mx);
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(128) decode_k(Params p) {
       l[hh] = rs;
     }
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+    for (int kk = 0; kk < NSUB / 2; ++kk) {
       uint32_t a0 = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
       uint32_t a1 = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
       uint32_t a2 = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
@@ -248,7 +249,68 @@ __global__ void kv_store_k(const bf16* __restrict__ k, const bf16* __restrict__ 
   *reinterpret_cast<V8*>(vc + dst) = *reinterpret_cast<const V8*>(v + src);
 }
 
+// Device-side decode bookkeeping between two graph-replayed decode steps (one CTA, B <= 1024).
+// For every live row (len > 0): append the sampled token to the ring, then either freeze the row
+// (it reached end_total, or sampled EOS with stop_on_eos) or advance it: next input token, position,
+// length, KV slot from the block table, and the token to force on the next sample (EOS when the
+// next token is the row's last and force_eos is set).  Frozen rows get len 0 so decode skips them.
+__global__ void decode_advance_k(int B, const int64_t* __restrict__ out_tok, const float* __restrict__ out_lp,
+                                 int64_t* __restrict__ tok, int* __restrict__ pos, int* __restrict__ len,
+                                 int64_t* __restrict__ slot, const int* __restrict__ bt, int max_pages, int P,
+                                 const int* __restrict__ end_total, const int* __restrict__ force_eos,
+                                 const int* __restrict__ stop_on_eos, int64_t eos, int64_t* __restrict__ forced,
+                                 int64_t* __restrict__ ring_tok, float* __restrict__ ring_lp, int* __restrict__ ring_step,
+                                 int ring_cap, int ring_ld, int64_t scratch_slot, int64_t* __restrict__ seed) {
+  __shared__ int step;
+  if (threadIdx.x == 0) step = ring_step[0];
+  __syncthreads();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    int l = len[b];
+    long ri = (long)(step % ring_cap) * ring_ld + b;  // ring rows are max_batch wide, not bucket wide
+    if (l <= 0) {
+      ring_tok[ri] = -1;
+      ring_lp[ri] = 0.f;
+      continue;
+    }
+    int64_t t = out_tok[b];
+    ring_tok[ri] = t;
+    ring_lp[ri] = out_lp[b];
+    int n = l + 1;
+    bool done = n >= end_total[b] || (stop_on_eos[b] && t == eos);
+    if (done) {
+      len[b] = 0;
+      slot[b] = scratch_slot;
+      forced[b] = -1;
+      continue;
+    }
+    tok[b] = t;
+    pos[b] = n - 1;
+    len[b] = n;
+    slot[b] = (int64_t)bt[(long)b * max_pages + (n - 1) / P] * P + (n - 1) % P;
+    forced[b] = (force_eos[b] && n + 1 == end_total[b]) ? eos : -1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ring_step[0] = step + 1;
+    seed[0] += 1;
+  }
+}
+
 }  // namespace dec
+
+void decode_advance(int64_t B, at::Tensor out_tok, at::Tensor out_lp, at::Tensor tok, at::Tensor pos, at::Tensor len, at::Tensor slot,
+                    at::Tensor bt, int64_t P, at::Tensor end_total, at::Tensor force_eos, at::Tensor stop_on_eos, int64_t eos,
+                    at::Tensor forced, at::Tensor ring_tok, at::Tensor ring_lp, at::Tensor ring_step, int64_t scratch_slot,
+                    at::Tensor seed) {
+  AX_CHECK(B <= 1024, "decode batch must be <= 1024");
+  if (B == 0) return;
+  dec::decode_advance_k<<<1, 256, 0, stream()>>>(
+      (int)B, out_tok.data_ptr<int64_t>(), out_lp.data_ptr<float>(), tok.data_ptr<int64_t>(), pos.data_ptr<int>(), len.data_ptr<int>(),
+      slot.data_ptr<int64_t>(), bt.data_ptr<int>(), (int)bt.size(1), (int)P, end_total.data_ptr<int>(), force_eos.data_ptr<int>(),
+      stop_on_eos.data_ptr<int>(), eos, forced.data_ptr<int64_t>(), ring_tok.data_ptr<int64_t>(), ring_lp.data_ptr<float>(),
+      ring_step.data_ptr<int>(), (int)ring_tok.size(0), (int)ring_tok.size(1), scratch_slot, seed.data_ptr<int64_t>());
+  AX_LAUNCH_OK();
+}
 
 // q (B,Hq,128); caches (pages,Hkv,P,128); block_table (B,max_pages) int32; seq_lens (B,) int32.
 // `splits` is fixed by the caller (ceil(max_context / 256)) so the launch shape is static.

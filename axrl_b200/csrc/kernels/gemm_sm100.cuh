@@ -45,7 +45,7 @@ struct Sm2 {
   using Epi = cutlass::epilogue::TmaWarpSpecialized2Sm;
 };
 
-template <class LayoutA, class LayoutB, class ElemD, class Cfg>
+template <class LayoutA, class LayoutB, class ElemD, class Cfg, class Sched = void>
 struct Gemm {
   using ElemA = cutlass::bfloat16_t;
   using ElemB = cutlass::bfloat16_t;
@@ -64,7 +64,7 @@ struct Gemm {
       cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
       typename Cfg::Kernel>::CollectiveOp;
 
-  using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue, void>;
+  using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue, Sched>;
   using Op = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
 
   static void run(const void* A, const void* B, const void* C, void* D, int M, int N, int K, float alpha, float beta,
@@ -83,6 +83,11 @@ struct Gemm {
                                 {{alpha, beta}, static_cast<const ElemD*>(C), sc, static_cast<ElemD*>(D), sd}};
     args.hw_info.device_id = 0;
     args.hw_info.sm_count = num_sms();
+    if constexpr (std::is_same_v<Sched, cutlass::gemm::StreamKScheduler>) {
+      // Skinny problems (decode) have too few output tiles to fill 148 SMs: let the scheduler
+      // split K (stream-K) so every SM streams weights.
+      args.scheduler.decomposition_mode = cutlass::gemm::kernel::detail::DecompositionMode::Heuristic;
+    }
     Op op;
     auto st_impl = op.can_implement(args);
     TORCH_CHECK(st_impl == cutlass::Status::kSuccess, "GEMM cannot implement M=", M, " N=", N, " K=", K);
@@ -100,11 +105,21 @@ struct Gemm {
   }
 };
 
-// Entry points (one translation unit per layout family, for parallel builds).
-void run_tn(const void* A, const void* B, void* D, int M, int N, int K, bool d_fp32, cudaStream_t st);   // A MxK, B NxK
-void run_nn(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);                // A MxK, B KxN
-void run_wgrad(const void* A, const void* B, void* D, int M, int N, int K, bool accumulate, bool d_fp32,
-               cudaStream_t st);  // A stored KxM (M contiguous), B KxN
+using RM = cutlass::layout::RowMajor;
+using CM = cutlass::layout::ColumnMajor;
+using SK = cutlass::gemm::StreamKScheduler;
+
+// One translation unit per instantiation (parallel builds).  C (optional, beta = 1) is a
+// residual added in the epilogue.
+//   tn: D = A[M,K] @ B[N,K]^T (+ C)      nn: D = A[M,K] @ B[K,N]      wgrad: D (+)= A^T @ B, A stored [K,M]
+void tn_sm2(const void* A, const void* B, const void* C, void* D, int M, int N, int K, cudaStream_t st);
+void tn_sm1_sk(const void* A, const void* B, const void* C, void* D, int M, int N, int K, cudaStream_t st);
+void tn_narrow_sk(const void* A, const void* B, const void* C, void* D, int M, int N, int K, cudaStream_t st);
+void nn_sm2(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);
+void nn_sm1_sk(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);
+void wgrad_f32_sm2(const void* A, const void* B, void* D, int M, int N, int K, bool acc, cudaStream_t st);
+void wgrad_f32_sm1(const void* A, const void* B, void* D, int M, int N, int K, bool acc, cudaStream_t st);
+void wgrad_bf16_sm1(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);
 
 }  // namespace gemm
 }  // namespace ax

@@ -1,0 +1,10 @@
+// Forward GEMM, large M: 2-SM 256x256 tiles.
+#include "gemm_sm100.cuh"
+
+namespace ax {
+namespace gemm {
+void tn_sm2(const void* A, const void* B, const void* C, void* D, int M, int N, int K, cudaStream_t st) {
+  Gemm<RM, CM, cutlass::bfloat16_t, Sm2>::run(A, B, C, D, M, N, K, 1.f, C ? 1.f : 0.f, st);
+}
+}  // namespace gemm
+}  // namespace ax

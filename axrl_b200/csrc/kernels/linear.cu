@@ -1,4 +1,6 @@
-// torch-facing GEMM wrappers used by ops.linear / ops.logprob.
+// torch-facing GEMM wrappers used by ops.linear / ops.logprob / the rollout engine.
+// Tile-config choice by M (tokens): >= 512 -> 2-SM 256x256 data-parallel tiles;
+// 65..511 -> 1-SM 128x128 stream-K; <= 64 -> 1-SM 128x64 stream-K (decode: weight streaming).
 #include "common.cuh"
 #include "gemm_sm100.cuh"
 
@@ -11,16 +13,39 @@ static void check_bf16_2d(const at::Tensor& t, const char* n) {
   AX_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, n, ": 16-byte aligned base required");
 }
 
+at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
+
+static void tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K) {
+  if (M >= 512) gemm::tn_sm2(A, B, C, D, M, N, K, stream());
+  else if (M > 64) gemm::tn_sm1_sk(A, B, C, D, M, N, K, stream());
+  else gemm::tn_narrow_sk(A, B, C, D, M, N, K, stream());
+}
+
 // y[M,N] = x[M,K] @ w[N,K]^T
 at::Tensor linear_fwd(at::Tensor x, at::Tensor w) {
   check_bf16_2d(x, "x");
   check_bf16_2d(w, "w");
   AX_CHECK(x.size(1) == w.size(1), "K mismatch");
   int M = x.size(0), N = w.size(0), K = x.size(1);
+  if (M > 0 && M <= 64 && K % 64 == 0) return skinny_linear(x, w, c10::nullopt);  // decode: weight streaming
   auto y = at::empty({M, N}, x.options());
   if (M == 0 || N == 0) return y;
   if (K == 0) return y.zero_();
-  gemm::run_tn(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, N, K, false, stream());
+  tn(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K);
+  return y;
+}
+
+// y[M,N] = x[M,K] @ w[N,K]^T + residual[M,N]   (residual add fused into the epilogue)
+at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(residual, "residual");
+  int M = x.size(0), N = w.size(0), K = x.size(1);
+  AX_CHECK(residual.size(0) == M && residual.size(1) == N, "residual shape");
+  if (M > 0 && M <= 64 && K % 64 == 0) return skinny_linear(x, w, residual);
+  auto y = at::empty({M, N}, x.options());
+  if (M == 0 || N == 0) return y;
+  tn(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K);
   return y;
 }
 
@@ -33,7 +58,8 @@ at::Tensor linear_dgrad(at::Tensor dy, at::Tensor w) {
   auto dx = at::empty({M, K}, dy.options());
   if (M == 0 || K == 0) return dx;
   if (N == 0) return dx.zero_();
-  gemm::run_nn(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), M, K, N, stream());
+  if (M >= 512) gemm::nn_sm2(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), M, K, N, stream());
+  else gemm::nn_sm1_sk(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), M, K, N, stream());
   return dx;
 }
 
@@ -44,7 +70,7 @@ at::Tensor linear_wgrad(at::Tensor dy, at::Tensor x) {
   int M = dy.size(0), N = dy.size(1), K = x.size(1);
   auto dw = at::empty({N, K}, dy.options());
   if (M == 0) return dw.zero_();
-  gemm::run_wgrad(dy.data_ptr(), x.data_ptr(), dw.data_ptr(), N, K, M, false, false, stream());
+  gemm::wgrad_bf16_sm1(dy.data_ptr(), x.data_ptr(), dw.data_ptr(), N, K, M, stream());
   return dw;
 }
 
@@ -55,12 +81,11 @@ void linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc) {
   int M = dy.size(0), N = dy.size(1), K = x.size(1);
   AX_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.size(0) == N && acc.size(1) == K, "acc fp32 [N,K]");
   if (M == 0) return;
-  gemm::run_wgrad(dy.data_ptr(), x.data_ptr(), acc.data_ptr(), N, K, M, true, true, stream());
+  if (N >= 512 && K >= 512) gemm::wgrad_f32_sm2(dy.data_ptr(), x.data_ptr(), acc.data_ptr(), N, K, M, true, stream());
+  else gemm::wgrad_f32_sm1(dy.data_ptr(), x.data_ptr(), acc.data_ptr(), N, K, M, true, stream());
 }
 
 // Generic: trans_b ? a @ b^T : a @ b   (bf16 out)
-at::Tensor gemm_bf16(at::Tensor a, at::Tensor b, bool trans_b) {
-  return trans_b ? linear_fwd(a, b) : linear_dgrad(a, b);
-}
+at::Tensor gemm_bf16(at::Tensor a, at::Tensor b, bool trans_b) { return trans_b ? linear_fwd(a, b) : linear_dgrad(a, b); }
 
 }  // namespace ax

@@ -142,16 +142,21 @@ struct ArgMax {
   int i;
 };
 
-// Exact categorical sampling at temperature t by Gumbel-max:  argmax_j s_j + G_j,
-// G_j = -log(-log U_j).  temperature <= 0 means greedy.  Also returns log p(token) at
-// temperature t (greedy rows report the t=1 log-prob).  seed is read from device memory
-// so the kernel can live inside a captured CUDA graph.
+__device__ __forceinline__ void argmax_merge(ArgMax& a, float v, int i) {
+  if (v > a.v || (v == a.v && i < a.i)) a = {v, i};
+}
+
+// Stage 1 of exact categorical sampling at temperature t by Gumbel-max (argmax_j s_j + G_j,
+// G_j = -log(-log U_j)); temperature <= 0 means greedy.  The vocabulary row is split over
+// gridDim.y CTAs so small decode batches still use every SM; each CTA writes its partial
+// (max, sum-exp, best key, best index).  The seed is read from device memory so the kernel can
+// live inside a captured CUDA graph.
 template <typename T>
-__global__ void sample_k(const T* __restrict__ logits, int V, const float* __restrict__ temp, const int64_t* __restrict__ seed,
-                         int64_t* __restrict__ out_tok, float* __restrict__ out_lp, const int* __restrict__ row_ids,
-                         const int64_t* __restrict__ forced) {
+__global__ void sample_part_k(const T* __restrict__ logits, int V, const float* __restrict__ temp, const int64_t* __restrict__ seed,
+                              const int* __restrict__ row_ids, float4* __restrict__ part) {
   __shared__ ArgMax shm[32];
-  int row = blockIdx.x;
+  int row = blockIdx.x, S = gridDim.y, sp = blockIdx.y;
+  int chunk = (V + S - 1) / S, j0 = sp * chunk, j1 = min(V, j0 + chunk);
   int rid = row_ids ? row_ids[row] : row;
   const T* lr = logits + (size_t)row * V;
   float t = temp[row];
@@ -159,43 +164,53 @@ __global__ void sample_k(const T* __restrict__ logits, int V, const float* __res
   float inv_t = greedy ? 1.f : 1.f / t;
   uint64_t sd = (uint64_t)seed[0];
   LseAcc a{-INFINITY, 0.f, 0.f};
-  ArgMax best{-INFINITY, 0};
-  for (int j = threadIdx.x; j < V; j += blockDim.x) {
-    float s = (float)lr[j] * inv_t;
-    lse_push(a, s);
-    float key = s;
-    if (!greedy) {
-      float u = hash_uniform(sd, (uint64_t)rid, (uint64_t)j);
-      key = s - __logf(-__logf(u));
-    }
-    if (key > best.v) best = {key, j};
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+    float sv = (float)lr[j] * inv_t;
+    lse_push(a, sv);
+    float key = greedy ? sv : sv - __logf(-__logf(hash_uniform(sd, (uint64_t)rid, (uint64_t)j)));
+    argmax_merge(best, key, j);
   }
   a = block_lse(a);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    float v = __shfl_xor_sync(0xffffffffu, best.v, o);
-    int i = __shfl_xor_sync(0xffffffffu, best.i, o);
-    if (v > best.v || (v == best.v && i < best.i)) best = {v, i};
-  }
+  for (int o = 16; o > 0; o >>= 1) argmax_merge(best, __shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o));
   int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   __syncthreads();
   if (lane == 0) shm[wid] = best;
   __syncthreads();
   if (wid == 0) {
-    best = lane < nw ? shm[lane] : ArgMax{-INFINITY, 0};
+    best = lane < nw ? shm[lane] : ArgMax{-INFINITY, 0x7fffffff};
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      float v = __shfl_xor_sync(0xffffffffu, best.v, o);
-      int i = __shfl_xor_sync(0xffffffffu, best.i, o);
-      if (v > best.v || (v == best.v && i < best.i)) best = {v, i};
-    }
-    if (lane == 0) {
-      // A forced token (e.g. an EOS that ends a response at a prescribed length) replaces the
-      // sample; its log-prob is still taken under the same distribution.
-      int tok = (forced != nullptr && forced[row] >= 0) ? (int)forced[row] : best.i;
-      out_tok[row] = tok;
-      out_lp[row] = (float)lr[tok] * inv_t - (a.m + __logf(a.s));
-    }
+    for (int o = 16; o > 0; o >>= 1) argmax_merge(best, __shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o));
+    if (lane == 0) part[(size_t)row * S + sp] = make_float4(a.m, a.s, best.v, __int_as_float(best.i));
+  }
+}
+
+// Stage 2: one warp per row merges the partials; a forced token (e.g. an EOS ending a response
+// at a prescribed length) replaces the sample, its log-prob still taken under the same distribution.
+template <typename T>
+__global__ void sample_merge_k(const T* __restrict__ logits, int V, int S, const float* __restrict__ temp, const float4* __restrict__ part,
+                               const int64_t* __restrict__ forced, int64_t* __restrict__ out_tok, float* __restrict__ out_lp, int B) {
+  int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= B) return;
+  LseAcc a{-INFINITY, 0.f, 0.f};
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int s = lane; s < S; s += 32) {
+    float4 q = part[(size_t)row * S + s];
+    a = lse_merge(a, LseAcc{q.x, q.y, 0.f});
+    argmax_merge(best, q.z, __float_as_int(q.w));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a = lse_merge(a, LseAcc{__shfl_xor_sync(0xffffffffu, a.m, o), __shfl_xor_sync(0xffffffffu, a.s, o), 0.f});
+    argmax_merge(best, __shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o));
+  }
+  if (lane == 0) {
+    float t = temp[row];
+    float inv_t = t <= 0.f ? 1.f : 1.f / t;
+    int tok = (forced != nullptr && forced[row] >= 0) ? (int)forced[row] : best.i;
+    out_tok[row] = tok;
+    out_lp[row] = (float)logits[(size_t)row * V + tok] * inv_t - (a.m + __logf(a.s));
   }
 }
 
@@ -206,14 +221,24 @@ void sample_tokens(at::Tensor logits, at::Tensor temperature, at::Tensor seed, a
   if (B == 0) return;
   const int* rid = row_ids.has_value() ? row_ids->data_ptr<int>() : nullptr;
   const int64_t* fz = forced.has_value() ? forced->data_ptr<int64_t>() : nullptr;
-  if (logits.scalar_type() == at::kFloat)
-    sample_k<float><<<B, 1024, 0, stream()>>>(logits.data_ptr<float>(), V, temperature.data_ptr<float>(), seed.data_ptr<int64_t>(),
-                                              out_tok.data_ptr<int64_t>(), out_lp.data_ptr<float>(), rid, fz);
-  else {
+  int S = std::max(1, std::min(64, (num_sms() * 4 + B - 1) / B));
+  S = std::min(S, std::max(1, V / 1024));
+  auto part = at::empty({(long)B * S * 4}, logits.options().dtype(at::kFloat));
+  dim3 g1(B, S);
+  int wb = (B * 32 + 255) / 256;
+  if (logits.scalar_type() == at::kFloat) {
+    sample_part_k<float><<<g1, 256, 0, stream()>>>(logits.data_ptr<float>(), V, temperature.data_ptr<float>(), seed.data_ptr<int64_t>(), rid,
+                                                  reinterpret_cast<float4*>(part.data_ptr<float>()));
+    sample_merge_k<float><<<wb, 256, 0, stream()>>>(logits.data_ptr<float>(), V, S, temperature.data_ptr<float>(),
+                                                   reinterpret_cast<float4*>(part.data_ptr<float>()), fz, out_tok.data_ptr<int64_t>(),
+                                                   out_lp.data_ptr<float>(), B);
+  } else {
     AX_CHECK(logits.scalar_type() == at::kBFloat16, "logits bf16/fp32");
-    sample_k<__nv_bfloat16><<<B, 1024, 0, stream()>>>((const bf16*)logits.data_ptr(), V, temperature.data_ptr<float>(),
-                                                       seed.data_ptr<int64_t>(), out_tok.data_ptr<int64_t>(),
-                                                       out_lp.data_ptr<float>(), rid, fz);
+    sample_part_k<bf16><<<g1, 256, 0, stream()>>>((const bf16*)logits.data_ptr(), V, temperature.data_ptr<float>(), seed.data_ptr<int64_t>(),
+                                                 rid, reinterpret_cast<float4*>(part.data_ptr<float>()));
+    sample_merge_k<bf16><<<wb, 256, 0, stream()>>>((const bf16*)logits.data_ptr(), V, S, temperature.data_ptr<float>(),
+                                                  reinterpret_cast<float4*>(part.data_ptr<float>()), fz, out_tok.data_ptr<int64_t>(),
+                                                  out_lp.data_ptr<float>(), B);
   }
   AX_LAUNCH_OK();
 }

@@ -44,7 +44,7 @@ def load(name: str = "_C") -> ModuleType:
 
 
 # Kernel launches per extension entry point (entry points not listed launch one kernel).
-_KERNELS_PER_CALL = {"attn_bwd": 3, "paged_decode_attn": 2, "rmsnorm_bwd": 2, "logprob_fwd": 1, "gemm": 1}
+_KERNELS_PER_CALL = {"attn_bwd": 3, "paged_decode_attn": 2, "rmsnorm_bwd": 2, "logprob_fwd": 1, "gemm": 1, "sample_tokens": 2}
 _COUNT = {"launches": 0, "enabled": False}
 
 

@@ -15,7 +15,7 @@ import torch
 from axrl_b200.ops import _ext
 from axrl_b200.ops.core import _qk_norm_rope_ref
 
-SPLIT_TOKENS = 256  # tokens per decode CTA (must match dec::SPLIT)
+SPLIT_TOKENS = 128  # tokens per decode CTA (must match dec::SPLIT)
 
 
 def _scatter_ref(cache: torch.Tensor, x: torch.Tensor, slots: torch.Tensor) -> None:

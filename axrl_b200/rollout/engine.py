@@ -1,4 +1,4 @@
-"""From-scratch rollout engine: paged KV cache, continuous batching, CUDA-graph decode.
+"""From-scratch rollout engine: paged KV cache, continuous batching, CUDA-graph decode bursts.
 
 Reference counterpart: the SGLang engine driven by ``SGLangWorker``
 (``axrl/worker/sglang_worker.py:49-851``): token-in/token-out generation with
@@ -8,23 +8,24 @@ sampled-token logprobs (:489-580), abort-and-continue for partial rollout
 
 Design (B200-first):
 * KV lives in one tensor ``[L, 2, pages, Hkv, page_size, 128]`` bf16; the C++
-  :class:`BlockManager` owns page allocation, refcounts and the prefix cache;
+  ``BlockManager`` owns page allocation, refcounts and the prefix cache;
 * requests that share a prompt (a GRPO group) are prefilled ONCE; members share
   the prompt's full pages by refcount and copy the partial last page;
 * prefill runs the packed range-list attention over new prompts while the fused
   q/k-norm+RoPE kernel scatters K/V into pages;
-* decode runs the split-KV paged attention kernel; the whole decode step
-  (36 layers + LM head + sampler) is captured once per batch-size bucket in a
-  CUDA graph and replayed with static input buffers;
-* sampling is Gumbel-max in one kernel that also returns the sampled token's
-  log-prob (and honours forced tokens, used to end responses at prescribed
-  lengths).
+* decode is device-resident: one CUDA graph = one decode step (36 layers with
+  residual adds fused into the GEMM epilogues, LM head, Gumbel-max sampler, and a
+  bookkeeping kernel that feeds the sampled token back, advances positions and KV
+  slots, forces EOS at prescribed lengths and appends to a token ring).  The host
+  replays ``burst`` steps back to back and synchronises once per burst to collect
+  tokens, retire finished rows and admit new requests.
 """
 
 from __future__ import annotations
 
 import math
 import time
+import zlib
 from dataclasses import dataclass, field
 from typing import Sequence
 
@@ -74,18 +75,19 @@ class _Seq:
     stream: int = 0
     cached: int = 0
     routing: list = field(default_factory=list)
+    end_total: int = 0  # total length at which the sequence ends
+    force_eos: bool = False
+    stop_on_eos: bool = False
 
 
 def _stream_id(rid: str) -> int:
-    import zlib
-
     return zlib.crc32(rid.encode()) & 0x7FFFFFFF
 
 
 class RolloutEngine:
     def __init__(self, model: Qwen3Model, *, max_batch: int = 256, kv_tokens: int = 1 << 16, page_size: int = 64,
                  max_context: int = 16384, max_prefill_tokens: int = 16384, use_cuda_graph: bool = True, seed: int = 0,
-                 eos_token_id: int | None = None) -> None:
+                 eos_token_id: int | None = None, burst: int = 16) -> None:
         self.model = model
         cfg = model.cfg
         self.cfg = cfg
@@ -96,61 +98,64 @@ class RolloutEngine:
         self.max_batch = max_batch
         self.max_context = max_context
         self.max_prefill_tokens = max_prefill_tokens
-        self.eos = eos_token_id
+        self.eos = 0 if eos_token_id is None else eos_token_id
+        self.burst = burst
         L, Hkv, D = cfg.num_hidden_layers, model.layers[0].self_attn.nkv, cfg.head_dim
-        self.num_pages = max(2, math.ceil(kv_tokens / page_size)) + 1  # last page: scratch for padded rows
+        self.num_pages = max(2, math.ceil(kv_tokens / page_size)) + 1  # last page: scratch for frozen/padded rows
         self.scratch_page = self.num_pages - 1
         self.kv = torch.zeros((L, 2, self.num_pages, Hkv, page_size, D), dtype=self.dtype, device=self.device)
         self.bm = make_block_manager(self.num_pages - 1, page_size)
-        self.max_pages = math.ceil(max_context / page_size)
-        self.ws = paged.DecodeWorkspace(max_batch, model.layers[0].self_attn.nq, max_context, self.device) if self.is_cuda else None
+        self.max_pages = math.ceil(max_context / page_size) + 1
+        self.ws = paged.DecodeWorkspace(max_batch, model.layers[0].self_attn.nq, max_context + page_size, self.device) if self.is_cuda else None
         self.use_graph = use_cuda_graph and self.is_cuda and not cfg.is_moe
         self.graphs: dict[int, tuple] = {}
         self.seed = seed
-        self.step_counter = 0
         self.gen = torch.Generator(device="cpu").manual_seed(seed)
         self.waiting: list[GenRequest] = []
         self.running: list[_Seq] = []
-        self.paused = False
-        self.stats = {"prefill_tokens": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_s": 0.0, "decode_s": 0.0}
+        self.stats = {"prefill_tokens": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_s": 0.0, "decode_s": 0.0, "bursts": 0}
         self._alloc_static()
 
     # ------------------------------------------------------------------ static buffers
     def _alloc_static(self) -> None:
         B, dev = self.max_batch, self.device
-        self.s_tok = torch.zeros(B, dtype=torch.int64, device=dev)
-        self.s_pos = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.s_bt = torch.zeros((B, self.max_pages), dtype=torch.int32, device=dev)
-        self.s_len = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.s_slot = torch.zeros(B, dtype=torch.int64, device=dev)
-        self.s_temp = torch.ones(B, dtype=torch.float32, device=dev)
-        self.s_rid = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.s_forced = torch.full((B,), -1, dtype=torch.int64, device=dev)
-        self.s_seed = torch.zeros(1, dtype=torch.int64, device=dev)
-        self.s_out_tok = torch.zeros(B, dtype=torch.int64, device=dev)
-        self.s_out_lp = torch.zeros(B, dtype=torch.float32, device=dev)
+        z = lambda dt, *shape: torch.zeros(*shape, dtype=dt, device=dev)  # noqa: E731
+        self.st = {
+            "tok": z(torch.int64, B), "pos": z(torch.int32, B), "len": z(torch.int32, B), "slot": z(torch.int64, B),
+            "bt": z(torch.int32, B, self.max_pages), "temp": z(torch.float32, B), "rid": z(torch.int32, B),
+            "forced": torch.full((B,), -1, dtype=torch.int64, device=dev), "end_total": z(torch.int32, B),
+            "force_eos": z(torch.int32, B), "stop_on_eos": z(torch.int32, B),
+        }
+        self.s_seed = z(torch.int64, 1)
+        self.s_out_tok = z(torch.int64, B)
+        self.s_out_lp = z(torch.float32, B)
+        self.ring_cap = max(self.burst, 1)
+        self.ring_tok = torch.full((self.ring_cap, B), -1, dtype=torch.int64, device=dev)
+        self.ring_lp = z(torch.float32, self.ring_cap, B)
+        self.ring_step = z(torch.int32, 1)
         pin = self.is_cuda
-        self.h_in = {k: torch.zeros_like(v, device="cpu").pin_memory() if pin else torch.zeros_like(v, device="cpu")
-                     for k, v in dict(tok=self.s_tok, pos=self.s_pos, bt=self.s_bt, len=self.s_len, slot=self.s_slot,
-                                      temp=self.s_temp, rid=self.s_rid, forced=self.s_forced).items()}
+        self.h = {k: (torch.zeros_like(v, device="cpu").pin_memory() if pin else torch.zeros_like(v, device="cpu")) for k, v in self.st.items()}
 
     # ------------------------------------------------------------------ model pieces (inference, no autograd)
-    def _lin(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        return _ext.ext().linear_fwd(x, w) if self.is_cuda else torch.nn.functional.linear(x, w)
+    def _lin(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        if self.is_cuda:
+            e = _ext.ext()
+            return e.linear_fwd(x, w) if residual is None else e.linear_residual(x, w, residual)
+        y = torch.nn.functional.linear(x, w)
+        return y if residual is None else y + residual
 
     def _rms(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         if self.is_cuda:
             return _ext.ext().rmsnorm_fwd(x, w, self.cfg.rms_norm_eps)[0]
         return ops._rms_ref(x, w, self.cfg.rms_norm_eps)
 
-    def _mlp(self, layer, x: torch.Tensor, capture: dict | None, li: int) -> torch.Tensor:  # noqa: ANN001
+    def _mlp(self, layer, x: torch.Tensor, h: torch.Tensor, capture: dict | None, li: int) -> torch.Tensor:  # noqa: ANN001
         mlp = layer.mlp
         if hasattr(mlp, "router"):
             from axrl_b200.models.moe import MoEContext
 
-            ctx = MoEContext(capture=capture)
-            return mlp(x, ctx, li)
-        return self._lin(ops.swiglu(self._lin(x, mlp.gate_up_proj)), mlp.down_proj)
+            return h + mlp(x, MoEContext(capture=capture), li)
+        return self._lin(ops.swiglu(self._lin(x, mlp.gate_up_proj)), mlp.down_proj, residual=h)
 
     def _embed(self, ids: torch.Tensor) -> torch.Tensor:
         if self.is_cuda:
@@ -166,9 +171,9 @@ class RolloutEngine:
             q, k, v = paged.qk_norm_rope_cache(qkv, a.q_norm, a.k_norm, pos, inv, a.nq, a.nkv, a.eps,
                                                self.kv[li, 0], self.kv[li, 1], slots)
             o = attend(li, q, k, v)
-            h = h + self._lin(o.reshape(o.shape[0], -1), a.o_proj)
+            h = self._lin(o.reshape(o.shape[0], -1), a.o_proj, residual=h)
             x = self._rms(h, layer.post_attention_layernorm.weight)
-            h = h + self._mlp(layer, x, capture, li)
+            h = self._mlp(layer, x, h, capture, li)
         return self._rms(h, self.model.norm.weight)
 
     def _logits(self, h: torch.Tensor) -> torch.Tensor:
@@ -197,7 +202,7 @@ class RolloutEngine:
     def step(self) -> list[GenResult]:
         finished = self._admit()
         if self.running:
-            finished += self._decode_step()
+            finished += self._decode_burst()
         return finished
 
     # ------------------------------------------------------------------ admission + prefill
@@ -207,13 +212,13 @@ class RolloutEngine:
     def _admit(self) -> list[GenResult]:
         if not self.waiting or len(self.running) >= self.max_batch:
             return []
-        # group waiting requests by identical prompt (GRPO groups share one prefill)
         budget_seqs = self.max_batch - len(self.running)
         groups: dict[tuple, list[GenRequest]] = {}
         order: list[tuple] = []
-        taken = 0
-        tokens = 0
-        for r in list(self.waiting):
+        taken = tokens = 0
+        for r in self.waiting:
+            if taken >= budget_seqs:
+                break
             key = tuple(r.prompt)
             if key not in groups:
                 if tokens + len(r.prompt) > self.max_prefill_tokens and order:
@@ -221,20 +226,18 @@ class RolloutEngine:
                 groups[key] = []
                 order.append(key)
                 tokens += len(r.prompt)
-            if taken >= budget_seqs:
-                break
             groups[key].append(r)
             taken += 1
-        # page budget: shared full pages once per group + per-member partial/decode headroom
-        need = 0
-        for key in order:
+        headroom = self._pages_needed(self.burst + 1)
+
+        def need(key: tuple) -> int:
             n = len(key)
-            need += n // self.P + len(groups[key]) * (1 + (1 if n % self.P else 0))
-        while need > self.bm.num_available() and order:
-            key = order.pop()
-            n = len(key)
-            need -= n // self.P + len(groups[key]) * (1 + (1 if n % self.P else 0))
-            del groups[key]
+            return n // self.P + len(groups[key]) * ((1 if n % self.P else 0) + headroom)
+
+        total = sum(need(k) for k in order)
+        while order and total > self.bm.num_available():
+            total -= need(order[-1])
+            del groups[order.pop()]
         if not order:
             if not self.running:
                 raise RuntimeError("KV cache too small for a single request")
@@ -252,17 +255,8 @@ class RolloutEngine:
             r0 = members[0]
             n = len(r0.prompt)
             assert 0 < n < self.max_context, f"prompt length {n} out of range"
-            matched, nmatch = self.bm.match_prefix([int(t) for t in r0.prompt]) if n > self.P else ([], 0)
-            if nmatch >= n:  # keep at least one token to compute logits from
-                self.bm.release(matched[-1:])
-                matched, nmatch = matched[:-1], nmatch - self.P
-            pages = list(matched) + self.bm.allocate(self._pages_needed(n) - len(matched))
-            seq = _Seq(r0, list(r0.prompt), pages, cached=nmatch)
-            protos.append(seq)
-            # tokens [nmatch, n) are computed; attention over the whole prompt needs the cached
-            # prefix too, so prefix hits are only used when the whole prefix is page-aligned and
-            # we recompute it into the same pages (values are identical); simplest exact path:
-            # compute the full prompt.
+            pages = self.bm.allocate(self._pages_needed(n))
+            protos.append(_Seq(r0, list(r0.prompt), pages))
             ids.extend(r0.prompt)
             pos.extend(range(n))
             pg = np.asarray(pages, dtype=np.int64)
@@ -279,13 +273,11 @@ class RolloutEngine:
         if self.is_cuda:
             spec = spec.to(dev)
             iostats.add_h2d(ids_t, pos_t, slots_t, spec.qseg, spec.kr, spec.kseg, spec.qr, spec.fwd_tiles, spec.bwd_tiles)
-        capture = {} if any(m.capture_routing for g in groups for m in g) and self.cfg.is_moe else None
+        capture = {} if self.cfg.is_moe and any(m.capture_routing for g in groups for m in g) else None
         with torch.no_grad():
             h = self._embed(ids_t)
             h = self._layers(h, pos_t, slots_t, lambda li, q, k, v: ops.attention(q, k, v, spec), capture)
-            last = h.index_select(0, torch.tensor(lasts, device=dev))
-            logits = self._logits(last)
-        # expand to group members
+            logits = self._logits(h.index_select(0, torch.tensor(lasts, device=dev)))
         rows, temps, rids, forced = [], [], [], []
         new_seqs: list[_Seq] = []
         for gi, members in enumerate(groups):
@@ -302,62 +294,51 @@ class RolloutEngine:
                     extra = self.bm.allocate(len(proto.pages) - full)
                     if extra:
                         self.kv[:, :, extra[0]].copy_(self.kv[:, :, proto.pages[full]])
-                    s = _Seq(r, list(r.prompt), shared + extra, cached=proto.cached)
+                    s = _Seq(r, list(r.prompt), shared + extra)
                 s.stream = r.seed_stream if r.seed_stream is not None else _stream_id(r.rid)
+                s.end_total = min(n + (r.forced_len if r.forced_len is not None else r.max_new_tokens), self.max_context)
+                s.force_eos = r.forced_len is not None
+                s.stop_on_eos = (self.eos in r.stop_token_ids) and r.forced_len is None
                 if capture is not None and r.capture_routing:
-                    # prompt routing rows for positions 1..n-1 of this prompt (row k predicts token k+1)
                     o0 = sum(len(g[0].prompt) for g in groups[:gi])
                     s.routing.append(np.stack([capture[li][o0:o0 + n - 1].cpu().numpy() for li in sorted(capture)], 1))
                 new_seqs.append(s)
                 rows.append(gi)
                 temps.append(r.temperature)
                 rids.append(s.stream)
-                forced.append(self._forced_token(s))
+                forced.append(self.eos if (s.force_eos and n + 1 == s.end_total) else -1)
         lg = logits.index_select(0, torch.tensor(rows, device=dev))
-        tok, lp = self._sample(lg, temps, rids, forced)
+        tok, lp = self._sample_rows(lg, temps, rids, forced)
         self.stats["prefill_tokens"] += off
         self.stats["prefill_s"] += time.perf_counter() - t0
         finished = []
         for s, t, l in zip(new_seqs, tok.tolist(), lp.tolist()):
-            self._append(s, t, l)
-            if self._is_done(s):
+            if self._accept(s, t, l):
                 finished.append(self._finish(s, self._reason(s)))
             else:
                 self.running.append(s)
         return finished
 
-    def _sample(self, logits, temps, rids, forced):  # noqa: ANN001, ANN202
+    def _sample_rows(self, logits, temps, rids, forced):  # noqa: ANN001, ANN202
         dev = self.device
         t = torch.tensor(temps, dtype=torch.float32).to(dev)
         f = torch.tensor(forced, dtype=torch.int64).to(dev)
         if self.is_cuda:
-            self.step_counter += 1
-            seed = torch.tensor([self.seed * 1_000_003 + self.step_counter], dtype=torch.int64).to(dev)
-            return paged.sample(logits, t, seed, row_ids=torch.tensor(rids, dtype=torch.int32).to(dev), forced=f)
+            self.s_seed.add_(1)
+            return paged.sample(logits, t, self.s_seed, row_ids=torch.tensor(rids, dtype=torch.int32).to(dev), forced=f)
         return paged.sample(logits, t, torch.zeros(1, dtype=torch.int64), generator=self.gen, forced=f)
 
-    def _forced_token(self, s: _Seq) -> int:
-        r = s.req
-        if r.forced_len is not None and len(s.out_ids) + 1 >= r.forced_len:
-            return int(r.forced_token if r.forced_token is not None else (self.eos if self.eos is not None else 0))
-        return -1
-
-    def _append(self, s: _Seq, tok: int, lp: float) -> None:
+    def _accept(self, s: _Seq, tok: int, lp: float) -> bool:
+        """Append one sampled token; return True when the sequence is finished."""
         s.tokens.append(tok)
         s.out_ids.append(tok)
         s.out_lps.append(lp)
-
-    def _is_done(self, s: _Seq) -> bool:
-        r = s.req
-        if r.forced_len is not None and len(s.out_ids) >= r.forced_len:
-            return True
-        if s.out_ids and s.out_ids[-1] in r.stop_token_ids:
-            return True
-        return len(s.out_ids) >= r.max_new_tokens or len(s.tokens) >= self.max_context
+        return len(s.tokens) >= s.end_total or (s.stop_on_eos and tok == self.eos) or (tok in s.req.stop_token_ids and not s.force_eos)
 
     def _reason(self, s: _Seq) -> str:
-        r = s.req
-        if (r.forced_len is not None and len(s.out_ids) >= r.forced_len) or (s.out_ids and s.out_ids[-1] in r.stop_token_ids):
+        if s.force_eos and len(s.out_ids) >= (s.req.forced_len or 0):
+            return "stop"
+        if s.out_ids and s.out_ids[-1] in s.req.stop_token_ids and not s.force_eos:
             return "stop"
         return "length"
 
@@ -366,107 +347,156 @@ class RolloutEngine:
         routing = np.concatenate(s.routing, 0) if s.routing else None
         return GenResult(s.req.rid, s.out_ids, s.out_lps, reason, len(s.req.prompt), s.cached, routing)
 
-    # ------------------------------------------------------------------ decode
-    def _decode_step(self) -> list[GenResult]:
+    # ------------------------------------------------------------------ decode bursts
+    def _upload_state(self, B: int, bucket: int) -> None:
+        h, P = self.h, self.P
+        h["bt"][:bucket].zero_()
+        for i, s in enumerate(self.running):
+            n = len(s.tokens)
+            h["tok"][i] = s.tokens[-1]
+            h["pos"][i] = n - 1
+            h["len"][i] = n
+            h["slot"][i] = s.pages[(n - 1) // P] * P + (n - 1) % P
+            h["bt"][i, : len(s.pages)] = torch.as_tensor(s.pages, dtype=torch.int32)
+            h["temp"][i] = s.req.temperature
+            h["rid"][i] = s.stream
+            h["end_total"][i] = s.end_total
+            h["force_eos"][i] = int(s.force_eos)
+            h["stop_on_eos"][i] = int(s.stop_on_eos)
+            h["forced"][i] = self.eos if (s.force_eos and n + 1 == s.end_total) else -1
+        if bucket > B:
+            h["len"][B:bucket] = 0
+            h["slot"][B:bucket] = self.scratch_page * P
+            h["tok"][B:bucket] = 0
+            h["pos"][B:bucket] = 0
+            h["forced"][B:bucket] = -1
+            h["end_total"][B:bucket] = 0
+        for k, dst in self.st.items():
+            dst[:bucket].copy_(h[k][:bucket], non_blocking=True)
+            if self.is_cuda:
+                iostats.add_h2d(h[k][:bucket])
+        self.ring_step.zero_()
+
+    def _decode_burst(self) -> list[GenResult]:
         t0 = time.perf_counter()
         B = len(self.running)
-        # make sure each sequence has a page for position len-1 (its newest token's KV)
-        for s in self.running:
-            need = self._pages_needed(len(s.tokens))
+        # steps this burst: no row needs more than its remaining tokens
+        remaining = max(s.end_total - len(s.tokens) for s in self.running)
+        k = max(1, min(self.burst, remaining))
+        for s in self.running:  # pages for every position this burst may write
+            need = self._pages_needed(min(len(s.tokens) + k, s.end_total))
             if need > len(s.pages):
                 if self.bm.num_available() < need - len(s.pages):
                     raise RuntimeError("KV cache exhausted during decode (raise kv_tokens or lower max_batch)")
                 s.pages.extend(self.bm.allocate(need - len(s.pages)))
-        hi = self.h_in
-        hi["bt"][:B].zero_()
-        for i, s in enumerate(self.running):
-            n = len(s.tokens)
-            hi["tok"][i] = s.tokens[-1]
-            hi["pos"][i] = n - 1
-            hi["len"][i] = n
-            hi["slot"][i] = s.pages[(n - 1) // self.P] * self.P + (n - 1) % self.P
-            hi["bt"][i, : len(s.pages)] = torch.as_tensor(s.pages, dtype=torch.int32)
-            hi["temp"][i] = s.req.temperature
-            hi["rid"][i] = s.stream
-            hi["forced"][i] = self._forced_token(s)
         bucket = self._bucket(B)
-        if bucket > B:  # padded rows: zero-length, write into the scratch page
-            hi["len"][B:bucket] = 0
-            hi["slot"][B:bucket] = self.scratch_page * self.P
-            hi["tok"][B:bucket] = 0
-            hi["pos"][B:bucket] = 0
-            hi["forced"][B:bucket] = -1
-            hi["bt"][B:bucket] = 0
+        self._upload_state(B, bucket)
         capture = {} if self.cfg.is_moe and any(s.req.capture_routing for s in self.running) else None
-        for k, dst in dict(tok=self.s_tok, pos=self.s_pos, bt=self.s_bt, len=self.s_len, slot=self.s_slot, temp=self.s_temp,
-                           rid=self.s_rid, forced=self.s_forced).items():
-            dst[:bucket].copy_(hi[k][:bucket], non_blocking=True)
-            if self.is_cuda:
-                iostats.add_h2d(hi[k][:bucket])
-        self.step_counter += 1
-        self.s_seed.fill_(self.seed * 1_000_003 + self.step_counter)
+        captured_rows = []
         with torch.no_grad():
-            if self.use_graph:
-                self._replay(bucket)
-            else:
-                self._decode_eager(bucket, capture)
-        tok = self.s_out_tok[:B].cpu().tolist()
-        lp = self.s_out_lp[:B].cpu().tolist()
+            for _ in range(k):
+                if self.use_graph:
+                    self._replay(bucket)
+                else:
+                    self._decode_body(bucket, capture)
+                    if capture is not None:
+                        captured_rows.append(np.stack([capture[li][:B].cpu().numpy() for li in sorted(capture)], 1))
+        toks = self.ring_tok[:k, :B].cpu()
+        lps = self.ring_lp[:k, :B].cpu()
         if self.is_cuda:
-            iostats.add_d2h(self.s_out_tok[:B], self.s_out_lp[:B])
-        if capture is not None:
-            rows = np.stack([capture[li][:B].cpu().numpy() for li in sorted(capture)], 1)  # (B, L, K)
+            iostats.add_d2h(self.ring_tok[:k, :B], self.ring_lp[:k, :B])
+        toks_l, lps_l = toks.T.tolist(), lps.T.tolist()
         finished, keep = [], []
         for i, s in enumerate(self.running):
-            if capture is not None and s.req.capture_routing:
-                s.routing.append(rows[i:i + 1])
-            self._append(s, tok[i], lp[i])
-            if self._is_done(s):
+            done = False
+            for j in range(k):
+                t = toks_l[i][j]
+                if t < 0:
+                    break
+                if capture is not None and s.req.capture_routing:
+                    s.routing.append(captured_rows[j][i:i + 1])
+                if self._accept(s, t, lps_l[i][j]):
+                    done = True
+                    break
+            if done:
                 finished.append(self._finish(s, self._reason(s)))
             else:
                 keep.append(s)
         self.running = keep
-        self.stats["decode_steps"] += 1
-        self.stats["decode_tokens"] += B
+        self.stats["decode_steps"] += k
+        self.stats["decode_tokens"] += B * k
+        self.stats["bursts"] += 1
         self.stats["decode_s"] += time.perf_counter() - t0
         return finished
 
     def _bucket(self, B: int) -> int:
         if not self.use_graph:
             return B
-        b = 1
+        b = 8
         while b < B:
             b *= 2
         return min(b, self.max_batch)
 
+    def _advance(self, bucket: int) -> None:
+        st = self.st
+        if self.is_cuda:
+            _ext.ext().decode_advance(bucket, self.s_out_tok, self.s_out_lp, st["tok"], st["pos"], st["len"], st["slot"], st["bt"], self.P,
+                                      st["end_total"], st["force_eos"], st["stop_on_eos"], self.eos, st["forced"], self.ring_tok,
+                                      self.ring_lp, self.ring_step, self.scratch_page * self.P, self.s_seed)
+            return
+        # CPU reference of decode_advance
+        step = int(self.ring_step[0]) % self.ring_cap
+        for b in range(bucket):
+            l = int(st["len"][b])
+            if l <= 0:
+                self.ring_tok[step, b] = -1
+                continue
+            t = int(self.s_out_tok[b])
+            self.ring_tok[step, b] = t
+            self.ring_lp[step, b] = self.s_out_lp[b]
+            n = l + 1
+            if n >= int(st["end_total"][b]) or (int(st["stop_on_eos"][b]) and t == self.eos):
+                st["len"][b] = 0
+                st["slot"][b] = self.scratch_page * self.P
+                st["forced"][b] = -1
+                continue
+            st["tok"][b] = t
+            st["pos"][b] = n - 1
+            st["len"][b] = n
+            st["slot"][b] = int(st["bt"][b, (n - 1) // self.P]) * self.P + (n - 1) % self.P
+            st["forced"][b] = self.eos if (int(st["force_eos"][b]) and n + 1 == int(st["end_total"][b])) else -1
+        self.ring_step += 1
+        self.s_seed += 1
+
     def _decode_body(self, bucket: int, capture=None) -> None:  # noqa: ANN001
-        tok = self.s_tok[:bucket]
-        pos = self.s_pos[:bucket]
-        bt = self.s_bt[:bucket]
-        lens = self.s_len[:bucket]
-        slots = self.s_slot[:bucket]
+        st = self.st
+        tok, pos, bt, lens, slots = st["tok"][:bucket], st["pos"][:bucket], st["bt"][:bucket], st["len"][:bucket], st["slot"][:bucket]
         h = self._embed(tok)
         h = self._layers(h, pos, slots, lambda li, q, k, v: paged.paged_decode_attention(q, self.kv[li, 0], self.kv[li, 1], bt, lens, self.ws), capture)
         logits = self._logits(h)
         if self.is_cuda:
-            t, l = paged.sample(logits, self.s_temp[:bucket], self.s_seed, row_ids=self.s_rid[:bucket], forced=self.s_forced[:bucket])
+            t, l = paged.sample(logits, st["temp"][:bucket], self.s_seed, row_ids=st["rid"][:bucket], forced=st["forced"][:bucket])
         else:
-            t, l = paged.sample(logits, self.s_temp[:bucket], self.s_seed, generator=self.gen, forced=self.s_forced[:bucket])
+            t, l = paged.sample(logits, st["temp"][:bucket], self.s_seed, generator=self.gen, forced=st["forced"][:bucket])
         self.s_out_tok[:bucket].copy_(t)
         self.s_out_lp[:bucket].copy_(l)
-
-    def _decode_eager(self, bucket: int, capture=None) -> None:  # noqa: ANN001
-        self._decode_body(bucket, capture)
+        self._advance(bucket)
 
     def _replay(self, bucket: int) -> None:
         g = self.graphs.get(bucket)
         if g is None:
-            # warm up on a side stream, then capture
+            saved = {k: v.clone() for k, v in self.st.items()}
+            saved_ring = (self.ring_tok.clone(), self.ring_lp.clone(), self.ring_step.clone(), self.s_seed.clone())
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(s):
                 self._decode_body(bucket)
             torch.cuda.current_stream().wait_stream(s)
+            # warm-up advanced the state: restore before capturing
+            for k, v in saved.items():
+                self.st[k].copy_(v)
+            self.ring_tok.copy_(saved_ring[0]), self.ring_lp.copy_(saved_ring[1]), self.ring_step.copy_(saved_ring[2])
+            self.s_seed.copy_(saved_ring[3])
             graph = torch.cuda.CUDAGraph()
             was = _ext._COUNT["enabled"]
             before = _ext.count_launches(True)
@@ -476,6 +506,7 @@ class RolloutEngine:
             _ext._COUNT["launches"] = before
             self.graphs[bucket] = (graph, captured)
             g = self.graphs[bucket]
+            # capture does not execute: state is still the restored one; run the first step for real
         g[0].replay()
         _ext.add_launches(g[1])
 
@@ -491,5 +522,5 @@ class RolloutEngine:
             p1.copy_(p2, non_blocking=True)
 
     def reset_prefix_cache(self) -> None:
-        """Weights changed: cached pages no longer match (reference flushes the radix cache)."""
+        """Weights changed: cached pages no longer match (the reference flushes its radix cache)."""
         self.bm.clear_cache()

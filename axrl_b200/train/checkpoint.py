@@ -1,0 +1,229 @@
+"""Checkpoint I/O: HF safetensors and a Megatron-compatible distributed checkpoint.
+
+Reference: ``MegatronWorker`` save/load through Megatron-Bridge (``axrl/worker/megatron_worker.py:321-374,
+443-466,782-796``), ``BaseController.save_checkpoint`` / ``save_hf_checkpoint`` (rotation, retries;
+``axrl/controller/base_controller.py:153-244``).
+
+* HF format: ``model.safetensors.index.json`` + shards with HF parameter names
+  (``model.layers.{i}.self_attn.q_proj.weight`` ...), ``config.json``.
+* Distributed format (``torch_dist`` backend, the format Megatron-Core writes): an
+  ``iter_XXXXXXX/`` directory written with ``torch.distributed.checkpoint`` (``.metadata`` +
+  ``*.distcp``), ``metadata.json`` naming the backend, ``common.pt`` for non-tensor state,
+  ``latest_checkpointed_iteration.txt`` in the parent.  Tensor keys follow Megatron-Core naming
+  with transformer layers stacked along a leading layer axis
+  (``decoder.layers.self_attention.linear_qkv.weight`` of shape ``[L, ...]``), and the fused QKV
+  weight is stored in Megatron's per-query-group interleaved order ``[q_g, k_g, v_g]`` for each
+  KV group g.  Optimizer state (fp32 master weights and Adam moments) is stored under
+  ``optimizer.*`` keys in the same stacked layout.  Under data parallelism each rank writes only
+  its own shard of the optimizer state (DCP handles the global layout).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import shutil
+import time
+from pathlib import Path
+from typing import Any
+
+import torch
+
+from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model, hf_state_dict, load_hf_state_dict
+
+# ----------------------------------------------------------------------------- HF safetensors
+
+
+def save_hf_checkpoint(model: Qwen3Model, path: str | os.PathLike, max_shard_bytes: int = 5 << 30, dtype: torch.dtype = torch.bfloat16) -> None:
+    from safetensors.torch import save_file
+
+    path = Path(path)
+    path.mkdir(parents=True, exist_ok=True)
+    sd = {k: v.detach().to("cpu", dtype).contiguous() for k, v in hf_state_dict(model).items()}
+    shards, cur, size = [], {}, 0
+    for k, v in sd.items():
+        n = v.numel() * v.element_size()
+        if cur and size + n > max_shard_bytes:
+            shards.append(cur)
+            cur, size = {}, 0
+        cur[k] = v
+        size += n
+    if cur:
+        shards.append(cur)
+    index = {"metadata": {"total_size": sum(v.numel() * v.element_size() for v in sd.values())}, "weight_map": {}}
+    for i, sh in enumerate(shards):
+        name = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+        save_file(sh, str(path / name), metadata={"format": "pt"})
+        for k in sh:
+            index["weight_map"][k] = name
+    (path / "model.safetensors.index.json").write_text(json.dumps(index, indent=2))
+    cfg = model.cfg
+    hf_cfg = {"architectures": ["Qwen3MoeForCausalLM" if cfg.is_moe else "Qwen3ForCausalLM"], "model_type": "qwen3_moe" if cfg.is_moe else "qwen3",
+              "torch_dtype": str(dtype).replace("torch.", ""), **{k: getattr(cfg, k) for k in cfg.__dataclass_fields__}}
+    (path / "config.json").write_text(json.dumps(hf_cfg, indent=2))
+
+
+def read_hf_state_dict(path: str | os.PathLike) -> dict[str, torch.Tensor]:
+    from safetensors.torch import load_file
+
+    path = Path(path)
+    idx = path / "model.safetensors.index.json"
+    files = sorted(set(json.loads(idx.read_text())["weight_map"].values())) if idx.exists() else [p.name for p in path.glob("*.safetensors")]
+    sd: dict[str, torch.Tensor] = {}
+    for f in files:
+        sd.update(load_file(str(path / f)))
+    return sd
+
+
+def load_hf_checkpoint(model: Qwen3Model, path: str | os.PathLike, strict: bool = True) -> list[str]:
+    return load_hf_state_dict(model, read_hf_state_dict(path), strict=strict)
+
+
+def hf_config(path: str | os.PathLike) -> Qwen3Config:
+    return Qwen3Config.from_hf_dict(json.loads((Path(path) / "config.json").read_text()))
+
+
+# ----------------------------------------------------------------------------- Megatron-style dist checkpoint
+
+
+def _qkv_to_mcore(w: torch.Tensor, nq: int, nkv: int, d: int) -> torch.Tensor:
+    q, k, v = w.split([nq * d, nkv * d, nkv * d], 0)
+    g = nq // nkv
+    q = q.view(nkv, g * d, -1)
+    return torch.cat([q, k.view(nkv, d, -1), v.view(nkv, d, -1)], 1).reshape(w.shape)
+
+
+def _qkv_from_mcore(w: torch.Tensor, nq: int, nkv: int, d: int) -> torch.Tensor:
+    g = nq // nkv
+    x = w.view(nkv, (g + 2) * d, -1)
+    q, k, v = x.split([g * d, d, d], 1)
+    return torch.cat([q.reshape(nq * d, -1), k.reshape(nkv * d, -1), v.reshape(nkv * d, -1)], 0)
+
+
+def mcore_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
+    """Megatron-Core names, transformer layers stacked on axis 0."""
+    cfg = model.cfg
+    L = cfg.num_hidden_layers
+    out = {"embedding.word_embeddings.weight": model.embed_tokens.detach(), "decoder.final_layernorm.weight": model.norm.weight.detach()}
+    if model.lm_head is not None:
+        out["output_layer.weight"] = model.lm_head.detach()
+    per: dict[str, list[torch.Tensor]] = {}
+
+    def add(k: str, v: torch.Tensor) -> None:
+        per.setdefault(k, []).append(v.detach())
+
+    for layer in model.layers:
+        a = layer.self_attn
+        add("decoder.layers.self_attention.linear_qkv.layer_norm_weight", layer.input_layernorm.weight)
+        add("decoder.layers.self_attention.linear_qkv.weight", _qkv_to_mcore(a.qkv_proj.detach(), a.nq, a.nkv, a.d))
+        add("decoder.layers.self_attention.linear_proj.weight", a.o_proj)
+        add("decoder.layers.self_attention.q_layernorm.weight", a.q_norm)
+        add("decoder.layers.self_attention.k_layernorm.weight", a.k_norm)
+        mlp = layer.mlp
+        if hasattr(mlp, "router"):
+            add("decoder.layers.pre_mlp_layernorm.weight", layer.post_attention_layernorm.weight)
+            add("decoder.layers.mlp.router.weight", mlp.router)
+            add("decoder.layers.mlp.experts.linear_fc1.weight", mlp.experts_gate_up)
+            add("decoder.layers.mlp.experts.linear_fc2.weight", mlp.experts_down)
+        else:
+            add("decoder.layers.mlp.linear_fc1.layer_norm_weight", layer.post_attention_layernorm.weight)
+            add("decoder.layers.mlp.linear_fc1.weight", mlp.gate_up_proj)
+            add("decoder.layers.mlp.linear_fc2.weight", mlp.down_proj)
+    for k, vs in per.items():
+        assert len(vs) == L, f"{k}: heterogeneous layers are not stacked"
+        out[k] = torch.stack(vs, 0)
+    return out
+
+
+@torch.no_grad()
+def load_mcore_state_dict(model: Qwen3Model, sd: dict[str, torch.Tensor]) -> None:
+    model.embed_tokens.copy_(sd["embedding.word_embeddings.weight"])
+    model.norm.weight.copy_(sd["decoder.final_layernorm.weight"])
+    if model.lm_head is not None:
+        model.lm_head.copy_(sd["output_layer.weight"])
+    for i, layer in enumerate(model.layers):
+        a = layer.self_attn
+        g = lambda k: sd[k][i]  # noqa: E731
+        layer.input_layernorm.weight.copy_(g("decoder.layers.self_attention.linear_qkv.layer_norm_weight"))
+        a.qkv_proj.copy_(_qkv_from_mcore(g("decoder.layers.self_attention.linear_qkv.weight"), a.nq, a.nkv, a.d))
+        a.o_proj.copy_(g("decoder.layers.self_attention.linear_proj.weight"))
+        a.q_norm.copy_(g("decoder.layers.self_attention.q_layernorm.weight"))
+        a.k_norm.copy_(g("decoder.layers.self_attention.k_layernorm.weight"))
+        mlp = layer.mlp
+        if hasattr(mlp, "router"):
+            layer.post_attention_layernorm.weight.copy_(g("decoder.layers.pre_mlp_layernorm.weight"))
+            mlp.router.copy_(g("decoder.layers.mlp.router.weight"))
+            mlp.experts_gate_up.copy_(g("decoder.layers.mlp.experts.linear_fc1.weight"))
+            mlp.experts_down.copy_(g("decoder.layers.mlp.experts.linear_fc2.weight"))
+        else:
+            layer.post_attention_layernorm.weight.copy_(g("decoder.layers.mlp.linear_fc1.layer_norm_weight"))
+            mlp.gate_up_proj.copy_(g("decoder.layers.mlp.linear_fc1.weight"))
+            mlp.down_proj.copy_(g("decoder.layers.mlp.linear_fc2.weight"))
+
+
+def _iter_dir(root: Path, step: int) -> Path:
+    return root / f"iter_{step:07d}"
+
+
+def save_dist_checkpoint(root: str | os.PathLike, step: int, model: Qwen3Model, optim: Any = None, extra: dict | None = None,
+                         most_recent_k: int | None = 2, retries: int = 5) -> Path:
+    """Write ``root/iter_{step:07d}`` (torch_dist backend) and update the latest-iteration marker."""
+    import torch.distributed.checkpoint as dcp
+
+    root = Path(root)
+    d = _iter_dir(root, step)
+    state: dict[str, Any] = {f"model.{k}": v.to("cpu") for k, v in mcore_state_dict(model).items()}
+    if optim is not None:
+        osd = optim.state_dict()
+        for k in ("master", "exp_avg", "exp_avg_sq", "master_shard"):
+            if k in osd:
+                state[f"optimizer.{k}"] = osd[k].detach().to("cpu")
+    rank = torch.distributed.get_rank() if torch.distributed.is_initialized() else 0
+    for attempt in range(retries):
+        try:
+            d.mkdir(parents=True, exist_ok=True)
+            dcp.save(state, checkpoint_id=str(d))
+            if rank == 0:
+                (d / "metadata.json").write_text(json.dumps({"sharded_backend": "torch_dist", "sharded_backend_version": 1,
+                                                             "common_backend": "torch", "common_backend_version": 1}))
+                torch.save({"iteration": step, "optimizer_step": getattr(optim, "step_count", 0), "extra": extra or {}}, d / "common.pt")
+                (root / "latest_checkpointed_iteration.txt").write_text(str(step))
+            break
+        except OSError:
+            if attempt == retries - 1:
+                raise
+            time.sleep(2 ** attempt)
+    if rank == 0 and most_recent_k:
+        iters = sorted(p for p in root.glob("iter_*") if p.is_dir())
+        for old in iters[:-most_recent_k]:
+            shutil.rmtree(old, ignore_errors=True)
+    return d
+
+
+def latest_iteration(root: str | os.PathLike) -> int | None:
+    f = Path(root) / "latest_checkpointed_iteration.txt"
+    return int(f.read_text().strip()) if f.exists() else None
+
+
+def load_dist_checkpoint(root: str | os.PathLike, model: Qwen3Model, optim: Any = None, step: int | None = None) -> dict:
+    import torch.distributed.checkpoint as dcp
+
+    root = Path(root)
+    step = latest_iteration(root) if step is None else step
+    assert step is not None, f"no checkpoint under {root}"
+    d = _iter_dir(root, step)
+    state: dict[str, Any] = {f"model.{k}": torch.empty_like(v, device="cpu") for k, v in mcore_state_dict(model).items()}
+    if optim is not None:
+        for k, v in optim.state_dict().items():
+            if isinstance(v, torch.Tensor):
+                state[f"optimizer.{k}"] = torch.empty_like(v, device="cpu")
+    dcp.load(state, checkpoint_id=str(d))
+    load_mcore_state_dict(model, {k[len("model."):]: v for k, v in state.items() if k.startswith("model.")})
+    common = torch.load(d / "common.pt", weights_only=False)
+    if optim is not None:
+        osd = {k[len("optimizer."):]: v for k, v in state.items() if k.startswith("optimizer.")}
+        osd["step"] = common.get("optimizer_step", 0)
+        if "master_shard" in osd:
+            osd["exp_avg"], osd["exp_avg_sq"] = osd["exp_avg"], osd["exp_avg_sq"]
+        optim.load_state_dict(osd)
+    return common

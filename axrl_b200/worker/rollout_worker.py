@@ -1,0 +1,138 @@
+"""Async rollout worker around :class:`RolloutEngine` (the engine-adapter layer).
+
+Reference counterpart: ``SGLangWorker`` (``axrl/worker/sglang_worker.py:49-851``):
+
+* ``generate(GenerationInput) -> GenerationOutput`` token-in/token-out with sampled logprobs;
+* **partial rollout**: ``pause_generation`` aborts everything in flight; each aborted call
+  keeps its partial tokens and, after ``resume_generation``, re-submits
+  ``input_ids + output_ids`` with the remaining budget, concatenating outputs (reference
+  :338-405, :710-726);
+* routed-expert capture rows per call (R3) go to the tensor store as a handle;
+* memory release / resume and weight updates.
+
+The engine runs on a dedicated thread that owns the GPU work; coroutines submit requests
+through a thread-safe inbox and await futures.  One thread stepping the engine keeps
+continuous batching intact across every concurrent caller.
+"""
+
+from __future__ import annotations
+
+import asyncio
+import itertools
+import queue
+import threading
+import time
+from typing import Any
+
+import numpy as np
+
+from axrl_b200.configs import SamplingConfig
+from axrl_b200.data.conversation import GenerationInput, GenerationOutput
+from axrl_b200.rollout.engine import GenRequest, GenResult, RolloutEngine
+
+
+class RolloutWorker:
+    def __init__(self, engine: RolloutEngine, sampling: SamplingConfig | None = None, continue_after_abort: bool = True,
+                 tensor_store: Any = None, eos_token_id: int | None = None, decode_fn: Any = None) -> None:
+        self.engine = engine
+        self.sampling = sampling or SamplingConfig()
+        self.continue_after_abort = continue_after_abort
+        self.store = tensor_store
+        self.eos = eos_token_id
+        self.decode_fn = decode_fn
+        self._inbox: queue.Queue = queue.Queue()
+        self._pending: dict[str, tuple[asyncio.AbstractEventLoop, asyncio.Future]] = {}
+        self._ready = threading.Event()
+        self._ready.set()
+        self._pause_req = threading.Event()
+        self._stop = threading.Event()
+        self._ids = itertools.count()
+        self._thread = threading.Thread(target=self._loop, name="rollout-engine", daemon=True)
+        self._thread.start()
+
+    # ------------------------------------------------------------------ engine thread
+    def _loop(self) -> None:
+        while not self._stop.is_set():
+            try:
+                while True:
+                    req = self._inbox.get_nowait()
+                    self.engine.add_requests([req])
+            except queue.Empty:
+                pass
+            if self._pause_req.is_set():
+                for r in self.engine.abort_all():
+                    self._resolve(r)
+                self._pause_req.clear()
+                continue
+            if not (self.engine.waiting or self.engine.running):
+                time.sleep(0.0005)
+                continue
+            for r in self.engine.step():
+                self._resolve(r)
+
+    def _resolve(self, res: GenResult) -> None:
+        loop, fut = self._pending.pop(res.rid, (None, None))
+        if fut is not None:
+            loop.call_soon_threadsafe(lambda: fut.done() or fut.set_result(res))
+
+    async def _submit(self, req: GenRequest) -> GenResult:
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self._pending[req.rid] = (loop, fut)
+        self._inbox.put(req)
+        return await fut
+
+    # ------------------------------------------------------------------ public API
+    async def generate(self, inp: GenerationInput) -> GenerationOutput:
+        sc = inp.sampling_config or self.sampling
+        ids = [int(x) for x in np.asarray(inp.input_ids)]
+        budget = sc.max_new_tokens if sc.max_new_tokens is not None else max(1, sc.max_total_tokens - len(ids))
+        stop = (self.eos,) if self.eos is not None else ()
+        out_ids: list[int] = []
+        out_lps: list[float] = []
+        retry = 0
+        t0 = time.time()
+        inp.event_timing.stamp("worker_received")
+        routing = []
+        while True:
+            await asyncio.get_running_loop().run_in_executor(None, self._ready.wait)
+            rid = f"{inp.session_id}#{next(self._ids)}"
+            req = GenRequest(rid=rid, prompt=ids + out_ids, max_new_tokens=budget - len(out_ids), temperature=sc.temperature,
+                             stop_token_ids=stop, capture_routing=inp.capture_routing)
+            res = await self._submit(req)
+            out_ids += res.output_ids
+            out_lps += res.output_logprobs
+            if res.routed_experts is not None:
+                routing.append(res.routed_experts)
+            if res.finish_reason != "abort" or not self.continue_after_abort or len(out_ids) >= budget:
+                break
+            retry += 1
+        handle = None
+        if routing and self.store is not None:
+            rows = np.concatenate(routing, 0)[inp.routed_expert_start_index:]
+            handle = self.store.put(rows)
+        inp.event_timing.stamp("worker_returned")
+        text = self.decode_fn(out_ids) if self.decode_fn else ""
+        return GenerationOutput(session_id=inp.session_id, output_ids=np.asarray(out_ids), output_logprobs=np.asarray(out_lps),
+                                output_text=text, output_text_with_special_tokens=text, cached_tokens=res.cached_tokens,
+                                finish_reason=res.finish_reason, e2e_elapsed_seconds=time.time() - t0, stop_reason=None, retry=retry,
+                                routing_handle=handle, event_timing=inp.event_timing)
+
+    def pause_generation(self) -> None:
+        """Abort everything in flight; calls resume later from their partial outputs."""
+        self._ready.clear()
+        self._pause_req.set()
+        while self._pause_req.is_set() and self._thread.is_alive():
+            time.sleep(0.001)
+
+    def resume_generation(self) -> None:
+        self._ready.set()
+
+    def release_memory(self) -> None:
+        self.pause_generation()
+        self.engine.reset_prefix_cache()
+
+    def shutdown(self) -> None:
+        self._stop.set()
+        self._ready.set()
+        self._thread.join(timeout=5)

@@ -103,6 +103,21 @@ def test_gemm_family(M, N, K):
     close(acc, ref + 1, 1e-3, 1e-3, msg="wgrad acc")
 
 
+@pytest.mark.parametrize("M", [1, 7, 16, 33, 64, 100])
+@pytest.mark.parametrize("N,K", [(6144, 4096), (4096, 12288), (24576, 4096), (1024, 256)])
+def test_linear_residual_and_skinny(M, N, K):
+    """Decode-shaped GEMMs: skinny weight-streaming kernel (M <= 64, split-K with self-cleaning
+    workspace) and the residual-fused epilogue; called twice to check the workspace is left clean."""
+    e = _ext()
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) / math.sqrt(K)).bfloat16()
+    r = torch.randn(M, N, device=DEV).bfloat16()
+    ref = x.float() @ w.float().T
+    for _ in range(2):
+        close(e.linear_fwd(x, w), ref, 2e-2, 1e-2, msg="fwd")
+        close(e.linear_residual(x, w, r), ref + r.float(), 3e-2, 1e-2, msg="fwd+residual")
+
+
 def _spec_cases():
     from axrl_b200.data import prefix_tree as pt
     from axrl_b200.ops.attention_spec import causal_spec_from_cu_seqlens, tree_spec
