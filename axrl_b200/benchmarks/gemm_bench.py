@@ -1,0 +1,58 @@
+"""GEMM microbenchmark over decode/prefill/training shapes of the Qwen3-8B model.
+
+python -m axrl_b200.benchmarks.gemm_bench [--variants auto,skinny,swapab,cutlass]
+Times each variant with CUDA events after warm-up, flushing L2 (a 512 MB write) between
+iterations, and reports TB/s of operand traffic and TFLOP/s.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--variants", default="auto,skinny,swapab,cutlass")
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    from axrl_b200.ops import _ext
+
+    e = _ext.ext()
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288), "lm_head": (151936, 4096)}
+    for M in (1, 8, 32, 64, 128, 256, 4096):
+        for name, (N, K) in shapes.items():
+            x = torch.randn(M, K, device="cuda").bfloat16()
+            w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+            res = {"M": M, "shape": name, "N": N, "K": K}
+            for v in a.variants.split(","):
+                if v == "skinny" and M > 64:
+                    continue
+                if v == "swapab" and M > 64:
+                    continue
+                try:
+                    fn = (lambda: e.linear_fwd(x, w)) if v == "auto" else (lambda v=v: e.linear_variant(x, w, v))
+                    for _ in range(3):
+                        fn()
+                    ts = []
+                    for _ in range(a.iters):
+                        flush.zero_()
+                        s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        s.record()
+                        fn()
+                        t.record()
+                        t.synchronize()
+                        ts.append(s.elapsed_time(t))
+                    ms = sorted(ts)[len(ts) // 2]
+                    bytes_ = 2 * (M * K + N * K + M * N)
+                    res[v] = {"us": round(ms * 1000, 1), "TBps": round(bytes_ / ms / 1e9, 2), "TFLOPs": round(2 * M * N * K / ms / 1e9, 1)}
+                except Exception as ex:  # noqa: BLE001
+                    res[v] = str(ex)[:80]
+            print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -17,6 +17,7 @@ import argparse
 import glob
 import hashlib
 import os
+import re
 import subprocess
 import sys
 import sysconfig
@@ -62,12 +63,30 @@ def _torch_flags() -> tuple[list[str], list[str]]:
     return inc + defs, link
 
 
+_INCLUDE = re.compile(rb'^\s*#\s*include\s*"([^"]+)"', re.M)
+
+
+def _local_deps(path: str, seen: set[str]) -> None:
+    """Transitive closure of quoted includes that resolve inside this source tree."""
+    with open(path, "rb") as f:
+        text = f.read()
+    for inc in _INCLUDE.findall(text):
+        name = inc.decode()
+        for base in (os.path.dirname(path), HERE):
+            cand = os.path.normpath(os.path.join(base, name))
+            if os.path.isfile(cand) and cand.startswith(HERE):
+                if cand not in seen:
+                    seen.add(cand)
+                    _local_deps(cand, seen)
+                break
+
+
 def _digest(path: str, extra: list[str]) -> str:
     h = hashlib.sha1()
-    with open(path, "rb") as f:
-        h.update(f.read())
-    for hdr in sorted(glob.glob(os.path.join(HERE, "**", "*.cuh"), recursive=True) + glob.glob(os.path.join(HERE, "**", "*.h"), recursive=True)):
-        with open(hdr, "rb") as f:
+    deps: set[str] = set()
+    _local_deps(path, deps)
+    for p in [path, *sorted(deps)]:
+        with open(p, "rb") as f:
             h.update(f.read())
     h.update(" ".join(extra).encode())
     return h.hexdigest()[:16]

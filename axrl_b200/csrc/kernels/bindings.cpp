@@ -40,6 +40,8 @@ void flag_signal(int64_t, int64_t, int64_t);
 void flag_wait_bounded(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
 void sync_push(at::Tensor, at::Tensor, at::Tensor, int64_t);
 at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual);
+at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant);
+at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 void decode_advance(int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor,
                     at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor);
 }  // namespace ax
@@ -77,5 +79,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flag_wait_bounded", &ax::flag_wait_bounded);
   m.def("sync_push", &ax::sync_push);
   m.def("linear_residual", &ax::linear_residual);
+  m.def("linear_variant", &ax::linear_variant);
   m.def("decode_advance", &ax::decode_advance);
 }

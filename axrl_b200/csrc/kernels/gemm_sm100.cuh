@@ -45,12 +45,12 @@ struct Sm2 {
   using Epi = cutlass::epilogue::TmaWarpSpecialized2Sm;
 };
 
-template <class LayoutA, class LayoutB, class ElemD, class Cfg, class Sched = void>
+template <class LayoutA, class LayoutB, class ElemD, class Cfg, class Sched = void, class LayoutD = cutlass::layout::RowMajor>
 struct Gemm {
   using ElemA = cutlass::bfloat16_t;
   using ElemB = cutlass::bfloat16_t;
   using ElemAcc = float;
-  using LayoutC = cutlass::layout::RowMajor;
+  using LayoutC = LayoutD;
   static constexpr int kAlignD = 128 / cutlass::sizeof_bits<ElemD>::value;
 
   using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
@@ -120,6 +120,8 @@ void nn_sm1_sk(const void* A, const void* B, void* D, int M, int N, int K, cudaS
 void wgrad_f32_sm2(const void* A, const void* B, void* D, int M, int N, int K, bool acc, cudaStream_t st);
 void wgrad_f32_sm1(const void* A, const void* B, void* D, int M, int N, int K, bool acc, cudaStream_t st);
 void wgrad_bf16_sm1(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);
+// skinny (M <= 64): Y[M,N] = X[M,K] @ W[N,K]^T (+ C) computed as Y^T = W @ X^T (swap-AB)
+void tn_swapab(const void* X, const void* W, const void* C, void* D, int M, int N, int K, cudaStream_t st);
 
 }  // namespace gemm
 }  // namespace ax

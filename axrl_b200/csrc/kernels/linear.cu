@@ -27,11 +27,11 @@ at::Tensor linear_fwd(at::Tensor x, at::Tensor w) {
   check_bf16_2d(w, "w");
   AX_CHECK(x.size(1) == w.size(1), "K mismatch");
   int M = x.size(0), N = w.size(0), K = x.size(1);
-  if (M > 0 && M <= 64 && K % 64 == 0) return skinny_linear(x, w, c10::nullopt);  // decode: weight streaming
   auto y = at::empty({M, N}, x.options());
   if (M == 0 || N == 0) return y;
   if (K == 0) return y.zero_();
-  tn(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K);
+  if (M <= 64) gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K, stream());  // decode: weight streaming
+  else tn(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K);
   return y;
 }
 
@@ -42,10 +42,10 @@ at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual) {
   check_bf16_2d(residual, "residual");
   int M = x.size(0), N = w.size(0), K = x.size(1);
   AX_CHECK(residual.size(0) == M && residual.size(1) == N, "residual shape");
-  if (M > 0 && M <= 64 && K % 64 == 0) return skinny_linear(x, w, residual);
   auto y = at::empty({M, N}, x.options());
   if (M == 0 || N == 0) return y;
-  tn(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K);
+  if (M <= 64) gemm::tn_swapab(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K, stream());
+  else tn(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K);
   return y;
 }
 
@@ -83,6 +83,25 @@ void linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc) {
   if (M == 0) return;
   if (N >= 512 && K >= 512) gemm::wgrad_f32_sm2(dy.data_ptr(), x.data_ptr(), acc.data_ptr(), N, K, M, true, stream());
   else gemm::wgrad_f32_sm1(dy.data_ptr(), x.data_ptr(), acc.data_ptr(), N, K, M, true, stream());
+}
+
+// Benchmark / test entry: force one implementation ("skinny", "swapab", "cutlass").
+at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  int M = x.size(0), N = w.size(0), K = x.size(1);
+  if (variant == "skinny") return skinny_linear(x, w, c10::nullopt);
+  auto y = at::empty({M, N}, x.options());
+  if (M == 0) return y;
+  if (variant == "swapab") {
+    AX_CHECK(M <= 64, "swapab needs M <= 64");
+    gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K, stream());
+  } else if (variant == "cutlass") {
+    tn(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K);
+  } else {
+    AX_CHECK(false, "unknown GEMM variant ", variant);
+  }
+  return y;
 }
 
 // Generic: trans_b ? a @ b^T : a @ b   (bf16 out)

@@ -82,21 +82,29 @@ class Layout:
     nbytes: int
 
 
-def build_layout(specs: list[ParamSpec], tp: int, fp8: bool) -> Layout:
+def build_layout(specs: list[ParamSpec], tp: int, fp8: bool, base: int = 0) -> Layout:
+    """Offsets of each parameter in a flat buffer starting at byte ``base`` (256-byte aligned)."""
+    assert base % 256 == 0
     offs, soffs, shapes = {}, {}, {}
-    pos = 0
+    pos = base
     for s in specs:
         r, c = s.local_shape(tp)
         shapes[s.name] = (r, c)
-        if not fp8:
-            offs[s.name] = pos // 2
+        if not (fp8 and quantizable(s, r, c)):
+            offs[s.name] = pos // 2  # bf16 element offset
             pos += _align(r * c * 2, 256)
         else:
-            offs[s.name] = pos
+            offs[s.name] = pos  # e4m3 byte offset, then the fp32 block-scale grid
             pos += _align(r * c, 256)
             soffs[s.name] = pos
             pos += _align(-(-r // TILE) * -(-c // TILE) * 4, 256)
     return Layout(offs, soffs, shapes, pos)
+
+
+def quantizable(spec: ParamSpec, rows: int, cols: int) -> bool:
+    """Block-fp8 only for TP-split matrices whose local shape is a whole number of 128x128 blocks
+    (norms and other replicated vectors stay bf16)."""
+    return all(s.split != -1 for s in spec.subs) and rows % TILE == 0 and cols % TILE == 0
 
 
 def _slices(sub: Sub, tp: int) -> list[tuple[int, int, int, int]]:
@@ -126,7 +134,7 @@ def build_tiles(specs: list[ParamSpec], src_tp: int, dst_tp: int, src_layout: La
     for ps in specs:
         sr, sc = src_layout.shapes[ps.name]
         dr, dc = dst_layout.shapes[ps.name]
-        q8 = fp8 and all(s.split != -1 for s in ps.subs) and dr % TILE == 0 and dc % TILE == 0
+        q8 = fp8 and quantizable(ps, dr, dc)
         src_row_base = 0
         dst_row_base = [0] * dst_tp
         for sub in ps.subs:

@@ -1,0 +1,110 @@
+"""Worker program for the multi-GPU tests (launched by torch.distributed.run, one rank per GPU)."""
+
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def _tiny():
+    from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+
+    cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=128)
+    m = Qwen3Model(cfg)
+    m.init_weights(0)
+    return cfg, m.to("cuda", torch.bfloat16)
+
+
+def case_dist_optim() -> None:
+    from axrl_b200.configs import MegatronWorkerConfig
+    from axrl_b200.parallel.dist_optim import DistributedAdamW
+    from axrl_b200.train.optimizer import FlatAdamW
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    wc = MegatronWorkerConfig()
+    wc.lr_scheduler.lr_warmup_steps = 0
+    wc.lr_scheduler.max_lr = 1e-2
+    results = {}
+    for impl in ("replicated", "nccl", "p2p"):
+        _, m = _tiny()
+        opt = FlatAdamW(m, wc.optimizer, wc.lr_scheduler) if impl == "replicated" else DistributedAdamW(m, wc.optimizer, wc.lr_scheduler, backend=impl)
+        for step in range(3):
+            opt.zero_grad()
+            g = torch.Generator(device="cuda").manual_seed(100 * step + rank)
+            for p in opt.params:
+                p.main_grad.copy_(torch.randn(p.shape, device="cuda", generator=g))
+            if impl == "replicated":
+                dist.all_reduce(opt.grad)
+                norm = opt.step(grad_scale=0.5)
+            else:
+                norm = opt.step(grad_scale=0.5)
+        torch.cuda.synchronize()
+        results[impl] = (torch.cat([p.detach().float().reshape(-1) for p in m.parameters()]), float(norm))
+    ref, rn = results["replicated"]
+    for impl in ("nccl", "p2p"):
+        got, gn = results[impl]
+        err = (got - ref).abs().max().item()
+        assert err < 2e-2, f"{impl}: max param diff {err}"
+        assert abs(gn - rn) / rn < 1e-3, f"{impl}: grad norm {gn} vs {rn}"
+    print(f"rank {rank}: dist_optim ok", flush=True)
+
+
+def case_weight_sync() -> None:
+    from axrl_b200.sync.plan import qwen3_param_specs
+    from axrl_b200.sync.weight_sync import WeightSyncer
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg, m = _tiny()
+    specs = qwen3_param_specs(cfg)
+    full = {}
+    for name, p in m.named_parameters():
+        full[name.replace(".weight", "") if name.endswith("layernorm.weight") is False and name.endswith("norm.weight") is False else name] = p.detach()
+    from axrl_b200.sync.plan import _slices
+
+    def local(spec, tp, r):
+        t = dict(m.named_parameters())[spec.name if spec.name in dict(m.named_parameters()) else spec.name + ".weight"].detach()
+        t = t.reshape(-1, t.shape[-1]) if t.dim() > 1 else t.reshape(1, -1)
+        parts, row = [], 0
+        for sub in spec.subs:
+            blk = t[row:row + sub.rows]
+            r0, r1, c0, c1 = _slices(sub, tp)[r]
+            parts.append(blk[r0:r1, c0:c1])
+            row += sub.rows
+        return torch.cat(parts, 0)
+
+    for fp8 in (False, True):
+        dst_groups = [[(r + 1) % world for r in range(world)]]  # destination TP rank j lives on rank j+1: cross-GPU writes
+        ws = WeightSyncer(specs, src_tp=world, src_ranks=list(range(world)), dst_tp=world, dst_groups=dst_groups, fp8=fp8)
+        for spec in specs:
+            ws.param_view(spec.name, "src").copy_(local(spec, world, rank))
+        secs = ws.push()
+        torch.cuda.synchronize()
+        j = (rank - 1) % world  # destination TP rank held here
+        for spec in specs:
+            exp = local(spec, world, j).float()
+            got = ws.param_view(spec.name, "dst")
+            if fp8 and all(s.split != -1 for s in spec.subs) and got.dtype == torch.float8_e4m3fn:
+                sc = ws.scale_view(spec.name)
+                deq = got.float() * sc.repeat_interleave(128, 0).repeat_interleave(128, 1)[: got.shape[0], : got.shape[1]]
+                err = ((deq - exp).abs() / (exp.abs().max() + 1e-6)).max().item()
+                assert err < 0.07, f"{spec.name}: fp8 rel err {err}"
+            else:
+                assert torch.equal(got.float(), exp), spec.name
+        print(f"rank {rank}: weight_sync fp8={fp8} ok ({ws.bytes_pushed / 1e6:.1f} MB pushed in {secs * 1e3:.3f} ms)", flush=True)
+
+
+if __name__ == "__main__":
+    from datetime import timedelta
+
+    local_rank = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    try:
+        globals()[f"case_{sys.argv[1]}"]()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()

@@ -116,6 +116,9 @@ def test_linear_residual_and_skinny(M, N, K):
     for _ in range(2):
         close(e.linear_fwd(x, w), ref, 2e-2, 1e-2, msg="fwd")
         close(e.linear_residual(x, w, r), ref + r.float(), 3e-2, 1e-2, msg="fwd+residual")
+        if M <= 64:
+            for v in ("skinny", "swapab"):
+                close(e.linear_variant(x, w, v), ref, 2e-2, 1e-2, msg=v)
 
 
 def _spec_cases():
