@@ -1,8 +1,9 @@
 """GEMM microbenchmark over decode/prefill/training shapes of the Qwen3-8B model.
 
 python -m axrl_b200.benchmarks.gemm_bench [--variants auto,skinny,swapab,cutlass]
-Times each variant with CUDA events after warm-up, flushing L2 (a 512 MB write) between
-iterations, and reports TB/s of operand traffic and TFLOP/s.
+Times each variant with CUDA events after warm-up, flushing L2 between iterations by READING a
+512 MB buffer (a write flush would leave ~126 MB of dirty lines whose write-back the timed kernel
+would pay for), and reports TB/s of operand traffic and TFLOP/s.
 """
 
 from __future__ import annotations
@@ -21,7 +22,7 @@ def main() -> None:
     from axrl_b200.ops import _ext
 
     e = _ext.ext()
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
     shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288), "lm_head": (151936, 4096)}
     for M in (1, 8, 32, 64, 128, 256, 4096):
         for name, (N, K) in shapes.items():
@@ -39,7 +40,7 @@ def main() -> None:
                         fn()
                     ts = []
                     for _ in range(a.iters):
-                        flush.zero_()
+                        flush.sum()
                         s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         s.record()
                         fn()

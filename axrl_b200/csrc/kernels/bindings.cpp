@@ -40,6 +40,12 @@ void flag_signal(int64_t, int64_t, int64_t);
 void flag_wait_bounded(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
 void sync_push(at::Tensor, at::Tensor, at::Tensor, int64_t);
 at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual);
+void linear_fwd_into(at::Tensor x, at::Tensor w, at::Tensor out);
+void linear_dgrad_into(at::Tensor dy, at::Tensor w, at::Tensor out);
+void tp_push(at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, at::Tensor, int64_t, int64_t, int64_t, int64_t, at::Tensor,
+             int64_t, at::Tensor, int64_t);
+void tp_wait(at::Tensor, int64_t, int64_t, int64_t, int64_t, at::Tensor);
+void tp_reduce_slots(at::Tensor, int64_t, int64_t, c10::optional<at::Tensor>, at::Tensor);
 at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant);
 at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 void decode_advance(int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor,
@@ -59,6 +65,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_tokens", &ax::sample_tokens, py::arg("logits"), py::arg("temperature"), py::arg("seed"), py::arg("out_tok"),
         py::arg("out_lp"), py::arg("row_ids") = py::none(), py::arg("forced") = py::none());
   m.def("linear_fwd", &ax::linear_fwd);
+  m.def("linear_fwd_into", &ax::linear_fwd_into);
+  m.def("linear_dgrad_into", &ax::linear_dgrad_into);
+  m.def("tp_push", &ax::tp_push);
+  m.def("tp_wait", &ax::tp_wait);
+  m.def("tp_reduce_slots", &ax::tp_reduce_slots);
   m.def("linear_dgrad", &ax::linear_dgrad);
   m.def("linear_wgrad", &ax::linear_wgrad);
   m.def("linear_wgrad_acc", &ax::linear_wgrad_acc);

@@ -49,6 +49,30 @@ at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual) {
   return y;
 }
 
+// out[M,N] = x[M,K] @ w[N,K]^T into a caller-provided contiguous block of rows (chunked TP GEMMs)
+void linear_fwd_into(at::Tensor x, at::Tensor w, at::Tensor out) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(out, "out");
+  int M = x.size(0), N = w.size(0), K = x.size(1);
+  AX_CHECK(out.size(0) == M && out.size(1) == N && w.size(1) == K, "shapes");
+  if (M == 0 || N == 0) return;
+  if (M <= 64) gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, out.data_ptr(), M, N, K, stream());
+  else tn(x.data_ptr(), w.data_ptr(), nullptr, out.data_ptr(), M, N, K);
+}
+
+// out[M,K] = dy[M,N] @ w[N,K] into caller-provided rows
+void linear_dgrad_into(at::Tensor dy, at::Tensor w, at::Tensor out) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(out, "out");
+  int M = dy.size(0), N = dy.size(1), K = w.size(1);
+  AX_CHECK(w.size(0) == N && out.size(0) == M && out.size(1) == K, "shapes");
+  if (M == 0 || K == 0) return;
+  if (M >= 512) gemm::nn_sm2(dy.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, stream());
+  else gemm::nn_sm1_sk(dy.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, stream());
+}
+
 // dx[M,K] = dy[M,N] @ w[N,K]
 at::Tensor linear_dgrad(at::Tensor dy, at::Tensor w) {
   check_bf16_2d(dy, "dy");

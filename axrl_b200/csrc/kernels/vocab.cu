@@ -69,7 +69,8 @@ __global__ void logprob_fwd_k(const bf16* __restrict__ logits, const int* __rest
     float lse = a.m + __logf(a.s);
     int lab = labels[blockIdx.x];
     lse_out[blockIdx.x] = lse;
-    lp[blockIdx.x] = lab >= 0 ? __bfloat162float(row[lab]) * inv_t - lse : 0.f;
+    // lab >= V: a trained row whose label lives in another vocabulary shard (TP)
+    lp[blockIdx.x] = (lab >= 0 && lab < V) ? __bfloat162float(row[lab]) * inv_t - lse : 0.f;
     if (ent) ent[blockIdx.x] = lse - a.w / a.s;
   }
 }

@@ -30,6 +30,12 @@ class MoEContext:
     aux_loss: list[torch.Tensor] = field(default_factory=list)
     ep_group: object | None = None
 
+    def rows(self, a: int, b: int) -> "MoEContext":
+        """The context for token rows [a, b) (the sequence-parallel slice of a TP rank)."""
+        return MoEContext(replay={k: v[a:b] for k, v in self.replay.items()} if self.replay else self.replay,
+                          replay_mask=self.replay_mask[a:b] if self.replay_mask is not None else None,
+                          capture=self.capture, aux_loss=self.aux_loss, ep_group=self.ep_group)
+
 
 def route(logits: torch.Tensor, k: int, renorm: bool, replay: torch.Tensor | None = None, replay_mask: torch.Tensor | None = None):  # noqa: ANN201
     """Top-k routing in fp32.  Returns (weights (T,k) fp32, ids (T,k) int64)."""

@@ -17,6 +17,11 @@ Layout choices (B200-first):
 
 HF names are produced by :func:`hf_state_dict` / consumed by
 :func:`load_hf_state_dict` (split/concat of the fused weights).
+
+Tensor parallelism (``tp``, a :class:`~axrl_b200.parallel.tensor_parallel.TPContext`) follows
+Megatron with sequence parallelism: the hidden stream between blocks holds this rank's T/tp
+token rows, QKV / gate-up are column-parallel (all-gather in), O / down row-parallel
+(reduce-scatter out), embedding and LM head are vocabulary-parallel.
 """
 
 from __future__ import annotations
@@ -31,6 +36,10 @@ from torch.utils.checkpoint import checkpoint
 
 from axrl_b200.ops import core as ops
 from axrl_b200.ops.attention_spec import AttnSpec
+from axrl_b200.parallel import tensor_parallel as tpl
+from axrl_b200.parallel.tensor_parallel import TPContext
+
+_NO_TP = TPContext()
 
 
 @dataclass
@@ -133,11 +142,11 @@ class Attention(nn.Module):
         self.q_norm = nn.Parameter(torch.ones(self.d))
         self.k_norm = nn.Parameter(torch.ones(self.d))
 
-    def forward(self, x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec) -> torch.Tensor:
-        qkv = ops.linear(x, self.qkv_proj)
+    def forward(self, x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, tp: TPContext = _NO_TP) -> torch.Tensor:
+        qkv = tpl.column_parallel_linear(x, self.qkv_proj, tp)
         q, k, v = ops.qk_norm_rope(qkv, self.q_norm, self.k_norm, pos, inv_freq, self.nq, self.nkv, self.eps)
         o = ops.attention(q, k, v, spec)
-        return ops.linear(o.reshape(o.shape[0], -1), self.o_proj)
+        return tpl.row_parallel_linear(o.reshape(o.shape[0], -1), self.o_proj, tp)
 
 
 class MLP(nn.Module):
@@ -146,8 +155,8 @@ class MLP(nn.Module):
         self.gate_up_proj = nn.Parameter(torch.empty(2 * ffn, hidden))
         self.down_proj = nn.Parameter(torch.empty(hidden, ffn))
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return ops.linear(ops.swiglu(ops.linear(x, self.gate_up_proj)), self.down_proj)
+    def forward(self, x: torch.Tensor, tp: TPContext = _NO_TP) -> torch.Tensor:
+        return tpl.row_parallel_linear(ops.swiglu(tpl.column_parallel_linear(x, self.gate_up_proj, tp)), self.down_proj, tp)
 
 
 class DecoderLayer(nn.Module):
@@ -164,27 +173,38 @@ class DecoderLayer(nn.Module):
         else:
             self.mlp = MLP(cfg.hidden_size, cfg.intermediate_size // tp_size)
 
-    def forward(self, h: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, moe_ctx=None) -> torch.Tensor:  # noqa: ANN001
-        h = h + self.self_attn(self.input_layernorm(h), pos, inv_freq, spec)
+    def forward(self, h: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, moe_ctx=None,  # noqa: ANN001
+                tp: TPContext = _NO_TP) -> torch.Tensor:
+        h = h + self.self_attn(self.input_layernorm(h), pos, inv_freq, spec, tp)
         x = self.post_attention_layernorm(h)
-        if moe_ctx is not None and hasattr(self.mlp, "router"):
-            return h + self.mlp(x, moe_ctx, self.layer_idx)
-        return h + self.mlp(x)
+        if hasattr(self.mlp, "router"):
+            if moe_ctx is not None and tp.enabled:
+                moe_ctx = moe_ctx.rows(tp.rank * x.shape[0], (tp.rank + 1) * x.shape[0])
+            return h + (self.mlp(x, moe_ctx, self.layer_idx) if moe_ctx is not None else self.mlp(x))
+        return h + self.mlp(x, tp)
 
 
 class Qwen3Model(nn.Module):
     """Decoder stack.  ``forward`` returns final hidden states (T, H); the LM head
     is applied by :meth:`logprobs` (fused, chunked) or :meth:`logits`."""
 
-    def __init__(self, cfg: Qwen3Config, tp_size: int = 1) -> None:
+    def __init__(self, cfg: Qwen3Config, tp_size: int = 1, tp: TPContext | None = None) -> None:
         super().__init__()
         self.cfg = cfg
-        self.embed_tokens = nn.Parameter(torch.empty(cfg.vocab_size, cfg.hidden_size))
+        self.tp = tp or _NO_TP
+        tp_size = self.tp.size if tp is not None else tp_size
+        assert cfg.vocab_size % tp_size == 0, "vocabulary must split evenly over TP ranks"
+        V = cfg.vocab_size // tp_size
+        self.embed_tokens = nn.Parameter(torch.empty(V, cfg.hidden_size))
         self.layers = nn.ModuleList(DecoderLayer(cfg, i, tp_size) for i in range(cfg.num_hidden_layers))
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
-        self.lm_head = None if cfg.tie_word_embeddings else nn.Parameter(torch.empty(cfg.vocab_size, cfg.hidden_size))
+        self.lm_head = None if cfg.tie_word_embeddings else nn.Parameter(torch.empty(V, cfg.hidden_size))
         self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.head_dim, cfg.rope_theta), persistent=False)
         self.recompute = False
+        if tp_size > 1:
+            for name, p in self.named_parameters():
+                if p.dim() < 2 or ".mlp.router" in name or ".mlp.experts" in name:
+                    tpl.mark_replicated(p)
 
     @property
     def lm_weight(self) -> torch.Tensor:
@@ -192,8 +212,11 @@ class Qwen3Model(nn.Module):
 
     @torch.no_grad()
     def init_weights(self, seed: int = 0) -> None:
-        """Random init from ``seed`` (normal(0, 0.02), out-projections scaled by 1/sqrt(2L))."""
-        g = torch.Generator(device="cpu").manual_seed(seed)
+        """Random init from ``seed`` (normal(0, 0.02), out-projections scaled by 1/sqrt(2L)).
+
+        Each tensor draws from its own generator seeded by (seed, parameter name), so a tensor's
+        values do not depend on which other tensors exist; TP-sharded tensors add the TP rank to
+        the seed, TP-replicated ones do not (they must agree across ranks)."""
         std = self.cfg.initializer_range
         out_std = std / math.sqrt(2 * self.cfg.num_hidden_layers)
         for name, p in self.named_parameters():
@@ -201,30 +224,44 @@ class Qwen3Model(nn.Module):
                 p.fill_(1.0)
                 continue
             s = out_std if name.endswith(("o_proj", "down_proj")) else std
+            ps = seed * 1000003 + zlib.crc32(name.encode())
+            if self.tp.enabled and not getattr(p, "tp_replicated", False):
+                ps += 7919 * self.tp.rank
             if p.is_cuda:
-                # Per-tensor CUDA generator seeded deterministically from (seed, name).
-                cg = torch.Generator(device=p.device).manual_seed(seed * 1000003 + zlib.crc32(name.encode()))
+                cg = torch.Generator(device=p.device).manual_seed(ps)
                 p.normal_(0.0, s, generator=cg)
             else:
+                g = torch.Generator(device="cpu").manual_seed(ps)
                 p.copy_(torch.randn(p.shape, generator=g) * s)
 
     def embed(self, ids: torch.Tensor) -> torch.Tensor:
+        """Token rows of ``ids`` (T,) -> hidden (T, H), or this TP rank's (T/tp, H) slice."""
+        if self.tp.enabled:
+            return tpl.vocab_parallel_embedding(ids, self.embed_tokens, self.tp)
         return ops.embedding(ids, self.embed_tokens)
 
     def forward(self, ids: torch.Tensor, pos: torch.Tensor, spec: AttnSpec, moe_ctx=None) -> torch.Tensor:  # noqa: ANN001
+        """Final hidden states: (T, H), or (T/tp, H) rows of this rank under TP (T % tp == 0)."""
         h = self.embed(ids)
         inv = self.inv_freq
+        tp = self.tp
         for layer in self.layers:
             if self.recompute and torch.is_grad_enabled():
-                h = checkpoint(layer, h, pos, inv, spec, moe_ctx, use_reentrant=False)
+                h = checkpoint(layer, h, pos, inv, spec, moe_ctx, tp, use_reentrant=False)
             else:
-                h = layer(h, pos, inv, spec, moe_ctx)
+                h = layer(h, pos, inv, spec, moe_ctx, tp)
         return self.norm(h)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        assert not self.tp.enabled, "full logits are a rollout-side (TP=1) operation"
         return torch.nn.functional.linear(hidden.float(), self.lm_weight.float())
 
     def logprobs(self, hidden: torch.Tensor, labels: torch.Tensor, temperature: float = 1.0, entropy: bool = False):  # noqa: ANN201
+        """Per-token log p(label) (and entropy) for all T tokens; under TP ``hidden`` is the SP slice
+        and ``labels`` the full (T,) labels, and every TP rank returns the full result."""
+        if self.tp.enabled:
+            return tpl.vocab_parallel_logprob(tpl.gather_from_sp(hidden, self.tp), self.lm_weight, labels, self.tp,
+                                              temperature=temperature, compute_entropy=entropy)
         from axrl_b200.ops.logprob import fused_logprob
 
         return fused_logprob(hidden, self.lm_weight, labels, temperature=temperature, compute_entropy=entropy)

@@ -58,6 +58,8 @@ class SyntheticGRPOConfig:
     kv_tokens: int | None = None
     max_batch: int | None = None
     use_cuda_graph: bool = True
+    kv_gb: float | None = None  # cap on the KV pool size
+    kv_memory_saver: bool = True  # release the KV pool while training (same address on resume)
     extra: dict = field(default_factory=dict)
 
 
@@ -81,9 +83,16 @@ class SyntheticGRPO:
         n_seq = sc.num_prompts * sc.group_size
         max_ctx = sc.prompt_len + (sc.forced_len_max if sc.forced_len_median else sc.max_new_tokens) + 8
         kv_tokens = sc.kv_tokens or n_seq * (-(-max_ctx // 64) * 64)
+        cuda = self.device.type == "cuda"
+        if sc.kv_gb is not None:
+            per_tok = 2 * model_cfg.num_hidden_layers * model_cfg.num_key_value_heads * model_cfg.head_dim * 2
+            kv_tokens = min(kv_tokens, int(sc.kv_gb * (1 << 30)) // per_tok)
         self.rollout = RolloutEngine(rollout_model, max_batch=sc.max_batch or n_seq, kv_tokens=kv_tokens, page_size=64,
                                      max_context=max_ctx, max_prefill_tokens=max(16384, sc.prompt_len), seed=sc.seed,
-                                     use_cuda_graph=sc.use_cuda_graph, eos_token_id=sc.eos_token_id)
+                                     use_cuda_graph=sc.use_cuda_graph, eos_token_id=sc.eos_token_id,
+                                     kv_memory_saver=cuda and sc.kv_memory_saver)
+        if cuda and self.train.optim is not None:
+            self.train.release_grads_after_step = True  # the grad buffer is not needed during rollout
         self.weight_version = 0
         self.step_idx = 0
         self.last: dict = {}
@@ -137,7 +146,9 @@ class SyntheticGRPO:
         io0 = iostats.snapshot()
         t0 = time.perf_counter()
         reqs = self.make_requests()
+        self.rollout.acquire_kv()
         results = self.rollout.generate(reqs)
+        self.rollout.release_kv()
         t["rollout_s"] = time.perf_counter() - t0
 
         t1 = time.perf_counter()

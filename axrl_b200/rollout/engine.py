@@ -87,7 +87,7 @@ def _stream_id(rid: str) -> int:
 class RolloutEngine:
     def __init__(self, model: Qwen3Model, *, max_batch: int = 256, kv_tokens: int = 1 << 16, page_size: int = 64,
                  max_context: int = 16384, max_prefill_tokens: int = 16384, use_cuda_graph: bool = True, seed: int = 0,
-                 eos_token_id: int | None = None, burst: int = 16) -> None:
+                 eos_token_id: int | None = None, burst: int = 16, kv_memory_saver: bool = False) -> None:
         self.model = model
         cfg = model.cfg
         self.cfg = cfg
@@ -103,7 +103,17 @@ class RolloutEngine:
         L, Hkv, D = cfg.num_hidden_layers, model.layers[0].self_attn.nkv, cfg.head_dim
         self.num_pages = max(2, math.ceil(kv_tokens / page_size)) + 1  # last page: scratch for frozen/padded rows
         self.scratch_page = self.num_pages - 1
-        self.kv = torch.zeros((L, 2, self.num_pages, Hkv, page_size, D), dtype=self.dtype, device=self.device)
+        self.kv_buf = None
+        if self.is_cuda and kv_memory_saver:
+            # KV pages live in a VMM-tagged region: released while the trainer runs, re-mapped at the
+            # same address before the next rollout (captured decode graphs stay valid).
+            from axrl_b200.runtime.vmm import VmmBuffer
+
+            self.kv_buf = VmmBuffer((L, 2, self.num_pages, Hkv, page_size, D), self.dtype, tag=f"kv_cache_{id(self)}")
+            self.kv = self.kv_buf.tensor
+        else:
+            self.kv = torch.zeros((L, 2, self.num_pages, Hkv, page_size, D), dtype=self.dtype, device=self.device)
+        self.preempted: dict[str, _Seq] = {}
         self.bm = make_block_manager(self.num_pages - 1, page_size)
         self.max_pages = math.ceil(max_context / page_size) + 1
         self.ws = paged.DecodeWorkspace(max_batch, model.layers[0].self_attn.nq, max_context + page_size, self.device) if self.is_cuda else None
@@ -195,7 +205,7 @@ class RolloutEngine:
     def abort_all(self) -> list[GenResult]:
         """Stop every request now (partial rollout): running ones return their partial output."""
         out = [self._finish(s, "abort") for s in self.running]
-        out += [GenResult(r.rid, [], [], "abort", len(r.prompt)) for r in self.waiting]
+        out += [self._unwrap(GenResult(r.rid, [], [], "abort", len(r.prompt))) for r in self.waiting]
         self.running, self.waiting = [], []
         return out
 
@@ -345,7 +355,50 @@ class RolloutEngine:
     def _finish(self, s: _Seq, reason: str) -> GenResult:
         self.bm.release(s.pages)
         routing = np.concatenate(s.routing, 0) if s.routing else None
-        return GenResult(s.req.rid, s.out_ids, s.out_lps, reason, len(s.req.prompt), s.cached, routing)
+        return self._unwrap(GenResult(s.req.rid, s.out_ids, s.out_lps, reason, len(s.req.prompt), s.cached, routing))
+
+    def _unwrap(self, res: GenResult) -> GenResult:
+        """Stitch a finished continuation of a preempted sequence onto what the sequence had produced
+        before preemption (following the chain when it was preempted more than once).
+
+        The continuation re-prefilled prompt + partial output, so its routing rows start at its
+        first non-cached position and already cover the preempted part: keep the original rows and
+        append the continuation's rows past them."""
+        orig = self.preempted.pop(res.rid, None)
+        if orig is None:
+            return res
+        routing = np.concatenate(orig.routing, 0) if orig.routing else None
+        if res.routed_experts is not None:
+            r0 = 0 if routing is None else routing.shape[0]
+            tail = res.routed_experts[max(0, r0 - res.cached_tokens):]
+            routing = tail if routing is None else np.concatenate([routing, tail], 0)
+        return self._unwrap(GenResult(orig.req.rid, orig.out_ids + res.output_ids, orig.out_lps + res.output_logprobs, res.finish_reason,
+                                      len(orig.req.prompt), orig.cached, routing))
+
+    def _preempt(self, s: _Seq) -> None:
+        """Free a running sequence's pages; it resumes later by re-prefilling prompt + partial output."""
+        self.bm.release(s.pages)
+        s.pages = []
+        r = s.req
+        done = len(s.out_ids)
+        cont = GenRequest(rid=f"{r.rid}~p{done}", prompt=list(s.tokens), max_new_tokens=max(1, r.max_new_tokens - done),
+                          temperature=r.temperature, stop_token_ids=r.stop_token_ids,
+                          forced_len=None if r.forced_len is None else r.forced_len - done, forced_token=r.forced_token,
+                          capture_routing=r.capture_routing, seed_stream=s.stream)
+        self.preempted[cont.rid] = s
+        self.waiting.insert(0, cont)
+        self.stats["preempted"] = self.stats.get("preempted", 0) + 1
+
+    def release_kv(self) -> None:
+        """Give the KV memory back (colocated training phase).  Nothing may be running."""
+        assert not self.running, "abort or finish generation before releasing the KV cache"
+        self.bm.clear_cache()
+        if self.kv_buf is not None:
+            self.kv_buf.pause(backup=False)
+
+    def acquire_kv(self) -> None:
+        if self.kv_buf is not None:
+            self.kv_buf.resume()
 
     # ------------------------------------------------------------------ decode bursts
     def _upload_state(self, B: int, bucket: int) -> None:
@@ -379,16 +432,22 @@ class RolloutEngine:
 
     def _decode_burst(self) -> list[GenResult]:
         t0 = time.perf_counter()
-        B = len(self.running)
         # steps this burst: no row needs more than its remaining tokens
         remaining = max(s.end_total - len(s.tokens) for s in self.running)
         k = max(1, min(self.burst, remaining))
-        for s in self.running:  # pages for every position this burst may write
+        # pages for every position this burst may write; preempt the newest sequences when short
+        while True:
+            short = sum(max(0, self._pages_needed(min(len(s.tokens) + k, s.end_total)) - len(s.pages)) for s in self.running)
+            if short <= self.bm.num_available() or len(self.running) <= 1:
+                break
+            self._preempt(self.running.pop())
+        for s in self.running:
             need = self._pages_needed(min(len(s.tokens) + k, s.end_total))
             if need > len(s.pages):
                 if self.bm.num_available() < need - len(s.pages):
-                    raise RuntimeError("KV cache exhausted during decode (raise kv_tokens or lower max_batch)")
+                    raise RuntimeError("KV cache too small for a single sequence (raise kv_tokens)")
                 s.pages.extend(self.bm.allocate(need - len(s.pages)))
+        B = len(self.running)
         bucket = self._bucket(B)
         self._upload_state(B, bucket)
         capture = {} if self.cfg.is_moe and any(s.req.capture_routing for s in self.running) else None

@@ -37,6 +37,7 @@ class ParallelCtx:
     dp_rank: int = 0
     tp_size: int = 1
     tp_rank: int = 0
+    tp_backend: str = "torch"  # "torch" (NCCL/gloo collectives) | "p2p" (NVLink kernels)
 
 
 class TrainEngine:
@@ -47,8 +48,11 @@ class TrainEngine:
         self.device = torch.device(device)
         self.par = par or ParallelCtx()
         dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
+        from axrl_b200.parallel.tensor_parallel import TPContext
+
+        self.tp = TPContext.from_group(self.par.tp_group, backend=self.par.tp_backend) if self.par.tp_size > 1 else TPContext()
         if model is None:
-            model = Qwen3Model(model_cfg, tp_size=self.par.tp_size)
+            model = Qwen3Model(model_cfg, tp=self.tp)
             model.init_weights(cfg.seed)
             model = model.to(device=self.device, dtype=dtype)
             model.inv_freq = model.inv_freq.float()
@@ -57,6 +61,7 @@ class TrainEngine:
         self.optim = None if cfg.inference_only else FlatAdamW(self.model, cfg.optimizer, cfg.lr_scheduler)
         self.max_tokens = cfg.max_tokens_per_micro_batch
         self.last_timing: dict[str, float] = {}
+        self.release_grads_after_step = False
 
     # ------------------------------------------------------------------ micro-batches
     def micro_batches(self, batch: SampleBatch) -> list[PackedMicroBatch]:
@@ -71,7 +76,8 @@ class TrainEngine:
             dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.par.dp_group)
             min_count = int(n)
         parts = split_balanced(lengths, self.max_tokens, min_count=min_count)
-        return [pack_rows(batch, p) for p in parts if p]
+        pad_to = self.tp.size * (16 if self.device.type == "cuda" else 1)
+        return [pack_rows(batch, p, pad_to=pad_to) for p in parts if p]
 
     # ------------------------------------------------------------------ forward
     def _hidden(self, mb: PackedMicroBatch, moe_ctx=None) -> torch.Tensor:  # noqa: ANN001
@@ -135,11 +141,25 @@ class TrainEngine:
             if want:
                 metrics_acc.append(m)
         self.optim.fold_param_grads()
-        sq = self.optim.grad_sqnorm()
         if self.par.dp_group is not None and self.par.dp_size > 1:
             dist.all_reduce(self.optim.grad, group=self.par.dp_group)  # replicated-optimizer baseline path
+        sq = self.optim.grad_sqnorm()
+        if self.tp.enabled:
+            from axrl_b200.parallel import tensor_parallel as tpl
+
+            tpl.allreduce_replicated_grads(self.model, self.tp)
             sq = self.optim.grad_sqnorm()
+            rep = tpl.replicated_sqnorm(self.model)
+            if rep is not None:  # replicated tensors are counted once over the TP group
+                sq = sq - rep * (1.0 - 1.0 / self.tp.size)
+            sq = sq.reshape(1).float().clone()
+            self.tp.comm.all_reduce(sq)
         norm = self.optim.step(grad_scale=1.0 / total_denom, sqnorm=sq)
+        norm = float(norm)
+        if self.tp.enabled and hasattr(self.tp.comm, "check"):
+            self.tp.comm.check()
+        if self.release_grads_after_step:
+            self.optim.release_grads()
         out = {k: sum(d[k] for d in metrics_acc if k in d) / max(1, sum(1 for d in metrics_acc if k in d))
                for k in {k for d in metrics_acc for k in d}}
         out["grad_norm"] = float(norm)

@@ -21,6 +21,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from axrl_b200.configs import IGNORE_INDEX
 from axrl_b200.data.sample import SampleBatch
 from axrl_b200.ops.attention_spec import AttnSpec, spec_from_triples
 
@@ -57,8 +58,10 @@ class PackedMicroBatch:
     def unpack(self, flat: torch.Tensor, width: int) -> torch.Tensor:
         """(T,) per-token values -> (rows, width) right-padded with zeros."""
         out = torch.zeros((len(self.rows), width), dtype=flat.dtype, device=flat.device)
-        col = torch.arange(flat.numel(), device=flat.device) - torch.as_tensor(self.row_off, device=flat.device)[self.token_row]
-        out[self.token_row, col] = flat
+        n = sum(self.row_len)  # trailing padding tokens (token_row -1) are dropped
+        trow = self.token_row[:n]
+        col = torch.arange(n, device=flat.device) - torch.as_tensor(self.row_off, device=flat.device)[trow]
+        out[trow, col] = flat[:n]
         return out
 
 
@@ -66,8 +69,11 @@ def _row_valid(batch: SampleBatch, r: int) -> int:
     return int(batch["seq_len"][r]) if "seq_len" in batch.tensors else int(batch["attention_mask"][r].sum())
 
 
-def pack_rows(batch: SampleBatch, rows: list[int]) -> PackedMicroBatch:
-    """Flatten ``rows`` of a right-padded batch into one packed stream (host tensors)."""
+def pack_rows(batch: SampleBatch, rows: list[int], pad_to: int = 1) -> PackedMicroBatch:
+    """Flatten ``rows`` of a right-padded batch into one packed stream (host tensors).
+
+    ``pad_to`` rounds the stream length up (e.g. to a multiple of the TP size for sequence
+    parallelism) with a trailing causal segment of untrained padding tokens."""
     ids, pos, lab, lm, trow = [], [], [], [], []
     fields = {k: [] for k in TOKEN_KEYS_F32 if k in batch.tensors}
     triples = []
@@ -93,6 +99,17 @@ def pack_rows(batch: SampleBatch, rows: list[int]) -> PackedMicroBatch:
         row_len.append(n)
         row_off.append(off)
         off += n
+    pad = (-off) % max(1, pad_to)
+    if pad:
+        triples.append((off, off + pad, off, off + pad, 1))
+        ids.append(torch.zeros(pad, dtype=torch.int64))
+        pos.append(torch.arange(pad, dtype=torch.int64))
+        lab.append(torch.full((pad,), IGNORE_INDEX, dtype=torch.int64))
+        lm.append(torch.zeros(pad, dtype=torch.bool))
+        for k in fields:
+            fields[k].append(torch.zeros(pad, dtype=batch[k].dtype))
+        trow.append(torch.full((pad,), -1, dtype=torch.int64))
+        off += pad
     spec = spec_from_triples(triples, off)
     return PackedMicroBatch(
         rows=list(rows), row_len=row_len, row_off=row_off,

@@ -63,6 +63,9 @@ def build_moe_context(store: Any, mb: Any, handles: list, infos: list, moe_layer
     L, K = ref.shape[1], ref.shape[2]
     allr = np.concatenate([c if c is not None else np.zeros((len(v), L, K), np.int64) for c, v in zip(chunks, valid)], 0)
     mask = np.concatenate(valid)
+    if allr.shape[0] < T:  # trailing padding tokens of the packed stream: live router
+        allr = np.concatenate([allr, np.zeros((T - allr.shape[0], L, K), np.int64)], 0)
+        mask = np.concatenate([mask, np.zeros(T - mask.shape[0], bool)])
     if loss_tokens_only:
         mask &= mb.loss_mask.cpu().numpy().astype(bool)
     assert allr.shape[0] == T

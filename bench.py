@@ -43,6 +43,8 @@ def _args():
     ap.add_argument("--max-len", type=int, default=8192)
     ap.add_argument("--mb-tokens", type=int, default=16384)
     ap.add_argument("--no-ref", action="store_true", help="skip the reference-policy logprob pass")
+    ap.add_argument("--kv-gb", type=float, default=None, help="KV pool size (default: free memory minus --headroom-gb)")
+    ap.add_argument("--headroom-gb", type=int, default=24)
     ap.add_argument("--verbose", action="store_true")
     return ap.parse_args()
 
@@ -138,10 +140,13 @@ def main() -> None:
     grpo = GrpoTrainerConfig(loss_type="grpo", mismatch_token_clip_max=2.0)
     par = ParallelCtx(dp_group=dist.group.WORLD if world > 1 else None, dp_size=world, dp_rank=rank)
     train = TrainEngine(wc, mcfg, dev, par=par)
+    train.optim.release_grads()  # gradients live only inside the train phase
+    free = torch.cuda.mem_get_info(dev)[0]
+    kv_gb = a.kv_gb if a.kv_gb else max(2.0, (free - (a.headroom_gb << 30)) / (1 << 30))
     sc = SyntheticGRPOConfig(num_prompts=a.prompts_per_gpu, prompt_len=a.prompt_len, group_size=a.group, temperature=1.0,
                              forced_len_median=a.median, forced_len_sigma=1.0, forced_len_min=16, forced_len_max=a.max_len,
                              eos_token_id=151645 % mcfg.vocab_size, merge_group_prompts=False, compute_ref_logprobs=not a.no_ref,
-                             seed=1000 + rank, use_cuda_graph=True)
+                             seed=1000 + rank, use_cuda_graph=True, kv_gb=kv_gb, kv_memory_saver=True)
     pipe = SyntheticGRPO(mcfg, wc, grpo, sc, dev, train_engine=train)
 
     def barrier() -> None:
@@ -211,13 +216,14 @@ def main() -> None:
                        "seq_len": a.prompt_len + a.max_len, "prompt_len": a.prompt_len,
                        "response_len": f"lognormal(median {a.median:g}, sigma 1) clipped [16,{a.max_len}]",
                        "micro_batch_tokens": a.mb_tokens, "parallelism": f"dp{world}", "colocated": True,
-                       "ref_logprobs": not a.no_ref, "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
+                       "ref_logprobs": not a.no_ref, "kv_pool_gb": round(kv_gb, 1), "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
             "sync_s": round(sum(m["sync_s"] for m in step_metrics) / len(step_metrics), 4),
             "step_breakdown_s": {k: round(last[k], 2) for k in ("rollout_s", "logprob_s", "train_s", "sync_s", "pack_s") if k in last},
             "e2e": {"value": round(e2e, 1), "unit": "trained tokens/s (wall clock through SyntheticGRPO.run_step)",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches_all),
             "clocks": clk,
+            "rollout_stats_per_step": {k: round(v / (a.warmup + a.steps), 3) for k, v in pipe.rollout.stats.items()},
         }
         print(json.dumps(out), flush=True)
     pipe.rollout.release_graphs()

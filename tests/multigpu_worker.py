@@ -97,6 +97,95 @@ def case_weight_sync() -> None:
         print(f"rank {rank}: weight_sync fp8={fp8} ok ({ws.bytes_pushed / 1e6:.1f} MB pushed in {secs * 1e3:.3f} ms)", flush=True)
 
 
+def case_tp() -> None:
+    """TP=world with sequence parallelism: NCCL collectives and the overlapped P2P kernels, each
+    against the TP=1 model (same weights) on this GPU."""
+    from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from axrl_b200.ops.attention_spec import spec_from_triples
+    from axrl_b200.parallel import tensor_parallel as tpl
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = Qwen3Config(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=8,
+                      num_key_value_heads=4, head_dim=128)
+    full = Qwen3Model(cfg)
+    full.init_weights(5)
+    full = full.to("cuda", torch.bfloat16)
+    full.inv_freq = full.inv_freq.float()
+    state = {k: v.detach().clone() for k, v in full.named_parameters()}
+    T = 512
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (T,), generator=g).cuda()
+    labels = torch.randint(0, cfg.vocab_size, (T,), generator=g).cuda()
+    labels[::7] = -100
+    spec = spec_from_triples([(0, 200, 0, 200, 1), (200, T, 200, T, 1)], T).to("cuda")
+    pos = torch.cat([torch.arange(200), torch.arange(T - 200)]).int().cuda()
+
+    def run(model):
+        for p in model.parameters():
+            p.main_grad = torch.zeros(p.shape, dtype=torch.float32, device="cuda")
+            p.grad = None
+        h = model(ids, pos, spec)
+        lp, ent = model.logprobs(h, labels, entropy=True)
+        keep = (labels >= 0).float()
+        ((lp * keep).sum() / keep.sum() + 0.05 * (ent * keep).sum() / keep.sum()).backward()
+        for p in model.parameters():
+            if p.grad is not None:
+                p.main_grad += p.grad.float()
+                p.grad = None
+        return lp.detach(), ent.detach()
+
+    lp_ref, ent_ref = run(full)
+    keep = labels >= 0
+    for backend in ("torch", "p2p"):
+        tp = tpl.TPContext.from_group(dist.group.WORLD, backend=backend)
+        m = Qwen3Model(cfg, tp=tp).to("cuda", torch.bfloat16)
+        m.inv_freq = m.inv_freq.float()
+        tpl.load_shards_from_full(m, state, tp)
+        lp, ent = run(m)
+        tpl.allreduce_replicated_grads(m, tp)
+        torch.cuda.synchronize()
+        if hasattr(tp.comm, "check"):
+            tp.comm.check()
+        d_lp = (lp - lp_ref)[keep].abs().max().item()
+        d_ent = (ent - ent_ref).abs().max().item()
+        assert d_lp < 5e-2 and d_ent < 5e-2, f"{backend}: lp diff {d_lp}, entropy diff {d_ent}"
+        worst = 0.0
+        for n, p in m.named_parameters():
+            gr = p.main_grad
+            if not getattr(p, "tp_replicated", False):
+                parts = [torch.empty_like(gr) for _ in range(world)]
+                dist.all_gather(parts, gr.contiguous())
+                gr = tpl.unshard_param(n, parts, cfg)
+            ref = dict(full.named_parameters())[n].main_grad
+            rel = ((gr - ref).norm() / (ref.norm() + 1e-12)).item()
+            worst = max(worst, rel)
+            assert rel < 3e-2, f"{backend}: grad {n} rel err {rel}"
+        print(f"rank {rank}: tp {backend} ok (lp diff {d_lp:.2e}, worst grad rel err {worst:.2e})", flush=True)
+
+
+def case_tp_timeout() -> None:
+    """A P2P TP wait whose peer never signals returns an error status after its bounded wait
+    instead of hanging: rank 1 skips the collective; rank 0 must see the timeout."""
+    import os as _os
+
+    _os.environ["AXRL_TP_TIMEOUT_S"] = "1"
+    from axrl_b200.parallel.tp_overlap import P2PTPComm
+
+    rank = dist.get_rank()
+    comm = P2PTPComm(dist.group.WORLD, cap_tokens=256, hidden=128)
+    if rank == 0:
+        x = torch.ones(64, 128, dtype=torch.bfloat16, device="cuda")
+        comm.all_gather_rows(x)
+        torch.cuda.synchronize()
+        try:
+            comm.check()
+            raise AssertionError("expected a timeout")
+        except RuntimeError as e:
+            assert "timed out" in str(e)
+    dist.barrier()
+    print(f"rank {rank}: tp timeout ok", flush=True)
+
+
 if __name__ == "__main__":
     from datetime import timedelta
 

@@ -99,3 +99,50 @@ def test_grpo_step_on_gpu_reduces_loss_direction():
     for m in (m1, m2):
         assert m["trained_tokens"] > 0 and torch.isfinite(torch.tensor(m["loss"]))
     pipe.rollout.release_graphs()
+
+
+def test_vmm_buffer_pause_resume_keeps_address():
+    from axrl_b200.runtime.vmm import VmmBuffer
+
+    buf = VmmBuffer((3, 1000, 64), torch.bfloat16, tag="test_vmm")
+    ptr = buf.tensor.data_ptr()
+    x = torch.randn(3, 1000, 64, device="cuda").bfloat16()
+    buf.tensor.copy_(x)
+    buf.pause(backup=True)
+    buf.resume()
+    assert buf.tensor.data_ptr() == ptr
+    torch.testing.assert_close(buf.tensor, x, atol=0, rtol=0)
+    buf.pause(backup=False)
+    buf.resume()
+    buf.tensor.fill_(1.0)
+    assert buf.tensor.float().sum().item() == 3 * 1000 * 64
+    buf.free()
+
+
+def test_kv_release_acquire_and_preemption():
+    """Graph decode across a KV release/acquire cycle, and a KV pool too small for the batch
+    (the newest sequences are preempted and resumed by re-prefill)."""
+    from axrl_b200.rollout.engine import RolloutEngine
+
+    m = _model(4)
+    forced = [120, 7, 200, 64, 150, 90]
+    eng = RolloutEngine(m, max_batch=8, kv_tokens=4096, max_context=512, seed=3, burst=8, kv_memory_saver=True)
+    r1 = eng.generate(_reqs(6, forced))
+    eng.release_kv()
+    eng.acquire_kv()
+    r2 = eng.generate(_reqs(6, forced))
+    for a, b, L in zip(r1, r2, forced):
+        assert len(a.output_ids) == len(b.output_ids) == L
+    eng.release_graphs()
+
+    # 10 pages of 64 tokens for six sequences that need up to 5 pages each
+    small = RolloutEngine(m, max_batch=8, kv_tokens=640, max_context=512, seed=3, burst=8, eos_token_id=3)
+    reqs = _reqs(6, forced)
+    for r in reqs:
+        r.max_new_tokens = 300
+    res = small.generate(reqs)
+    assert small.stats.get("preempted", 0) > 0
+    for r, L in zip(res, forced):
+        assert len(r.output_ids) == len(r.output_logprobs) == L and r.output_ids[-1] == 3 and r.finish_reason == "stop"
+    assert [r.rid for r in res] == [q.rid for q in reqs]
+    small.release_graphs()

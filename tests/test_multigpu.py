@@ -29,3 +29,12 @@ def test_dist_optim_two_gpus():
 
 def test_weight_sync_two_gpus():
     assert _run("weight_sync").count("ok") == 4
+
+
+def test_tensor_parallel_two_gpus():
+    out = _run("tp")
+    assert out.count("tp torch ok") == 2 and out.count("tp p2p ok") == 2, out[-2000:]
+
+
+def test_tp_p2p_wait_times_out_without_hanging():
+    assert _run("tp_timeout").count("tp timeout ok") == 2
