@@ -351,3 +351,71 @@ void kv_store(at::Tensor k, at::Tensor v, at::Tensor kc, at::Tensor vc, at::Tens
 }
 
 }  // namespace ax
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free entry point (declared and documented in decode_attn_noalloc.h; no counterpart in
+// the reference).  Same kernels as paged_decode_attn; the split-KV partials live in a file-scope
+// device array instead of caller-provided workspace tensors.
+#include <cstdio>
+#include <mutex>
+
+#include "decode_attn_noalloc.h"
+
+static __device__ __align__(256) float g_decode_noalloc_scratch[(long)AXRL_DECODE_NOALLOC_MAX_ROWS * (ax::dec::D + 2)];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {nullptr};
+bool g_noalloc_attr = false;
+}  // namespace
+
+extern "C" int axrl_paged_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
+                                                   const int* seq_lens, void* out, int B, int Hq, int Hkv, int page_size, int max_pages,
+                                                   int max_context, float scale, void* stream) {
+  using namespace ax::dec;
+  using ax::bf16;
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || Hq / Hkv > 16 || page_size <= 0 || max_pages <= 0 || max_context <= 0 ||
+      (long)max_pages * page_size < max_context || !q || !k_cache || !v_cache || !block_table || !seq_lens || !out) {
+    std::fprintf(stderr, "axrl_paged_decode_attention_noalloc: invalid arguments\n");
+    return 2;
+  }
+  if (B == 0) return 0;
+  const int splits = (max_context + SPLIT - 1) / SPLIT;
+  const long rows = (long)B * Hq * splits;
+  if (rows > AXRL_DECODE_NOALLOC_MAX_ROWS) {
+    std::fprintf(stderr,
+                 "axrl_paged_decode_attention_noalloc: B*Hq*ceil(max_context/%d) = %ld rows exceeds the %d-row scratch array; "
+                 "use paged_decode_attn with a workspace instead\n",
+                 SPLIT, rows, AXRL_DECODE_NOALLOC_MAX_ROWS);
+    return 1;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 3;
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+      if (e != cudaSuccess || p == nullptr) {
+        std::fprintf(stderr, "axrl_paged_decode_attention_noalloc: cudaGetSymbolAddress failed: %s\n", cudaGetErrorString(e));
+        return 3;
+      }
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    scratch = g_noalloc_ptr[dev];
+    if (!g_noalloc_attr) {
+      int smem = 16 * D * 2 + WARPS * 2 * SLICE * D * 2;
+      if (cudaFuncSetAttribute(decode_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return 4;
+      g_noalloc_attr = true;
+    }
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Params p{static_cast<const bf16*>(q), static_cast<const bf16*>(k_cache), static_cast<const bf16*>(v_cache), block_table, seq_lens,
+           scratch, scratch + rows * D, Hq, Hkv, page_size, max_pages, splits, scale * 1.4426950408889634f};
+  int smem = 16 * D * 2 + WARPS * 2 * SLICE * D * 2;
+  decode_k<<<dim3(B, Hkv, splits), 128, smem, st>>>(p);
+  long w = (long)B * Hq;
+  combine_k<<<(w * 32 + 255) / 256, 256, 0, st>>>(p.part_o, p.part_ml, seq_lens, static_cast<bf16*>(out), B, Hq, splits);
+  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+}
