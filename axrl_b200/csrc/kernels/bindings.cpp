@@ -45,6 +45,12 @@ void linear_dgrad_into(at::Tensor dy, at::Tensor w, at::Tensor out);
 void tp_push(at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, at::Tensor, int64_t, int64_t, int64_t, int64_t, at::Tensor,
              int64_t, at::Tensor, int64_t);
 void tp_wait(at::Tensor, int64_t, int64_t, int64_t, int64_t, at::Tensor);
+at::Tensor grouped_linear_fwd(at::Tensor x, at::Tensor w, at::Tensor offsets);
+at::Tensor grouped_linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor offsets);
+void grouped_linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor offsets, at::Tensor acc);
+void ep_plan(at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
+void ep_transfer(int64_t, at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
+                 at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, int64_t);
 void tp_reduce_slots(at::Tensor, int64_t, int64_t, c10::optional<at::Tensor>, at::Tensor);
 at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant);
 at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
@@ -69,6 +75,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_dgrad_into", &ax::linear_dgrad_into);
   m.def("tp_push", &ax::tp_push);
   m.def("tp_wait", &ax::tp_wait);
+  m.def("grouped_linear_fwd", &ax::grouped_linear_fwd);
+  m.def("grouped_linear_dgrad", &ax::grouped_linear_dgrad);
+  m.def("grouped_linear_wgrad_acc", &ax::grouped_linear_wgrad_acc);
+  m.def("ep_plan", &ax::ep_plan);
+  m.def("ep_transfer", &ax::ep_transfer);
   m.def("tp_reduce_slots", &ax::tp_reduce_slots);
   m.def("linear_dgrad", &ax::linear_dgrad);
   m.def("linear_wgrad", &ax::linear_wgrad);

@@ -81,7 +81,7 @@ struct Gemm {
                                 {M, N, K, 1},
                                 {static_cast<const ElemA*>(A), sa, static_cast<const ElemB*>(B), sb},
                                 {{alpha, beta}, static_cast<const ElemD*>(C), sc, static_cast<ElemD*>(D), sd}};
-    args.hw_info.device_id = 0;
+    cudaGetDevice(&args.hw_info.device_id);
     args.hw_info.sm_count = num_sms();
     if constexpr (std::is_same_v<Sched, cutlass::gemm::StreamKScheduler>) {
       // Skinny problems (decode) have too few output tiles to fill 148 SMs: let the scheduler

@@ -20,6 +20,7 @@ import torch
 from torch import nn
 
 from axrl_b200.ops import core as ops
+from axrl_b200.ops.grouped import expert_offsets, grouped_swiglu_ffn
 
 
 @dataclass
@@ -28,13 +29,12 @@ class MoEContext:
     replay_mask: torch.Tensor | None = None  # (T,) bool, replay only where True
     capture: dict[int, torch.Tensor] | None = None  # filled with (T, K) int16
     aux_loss: list[torch.Tensor] = field(default_factory=list)
-    ep_group: object | None = None
 
     def rows(self, a: int, b: int) -> "MoEContext":
         """The context for token rows [a, b) (the sequence-parallel slice of a TP rank)."""
         return MoEContext(replay={k: v[a:b] for k, v in self.replay.items()} if self.replay else self.replay,
                           replay_mask=self.replay_mask[a:b] if self.replay_mask is not None else None,
-                          capture=self.capture, aux_loss=self.aux_loss, ep_group=self.ep_group)
+                          capture=self.capture, aux_loss=self.aux_loss)
 
 
 def route(logits: torch.Tensor, k: int, renorm: bool, replay: torch.Tensor | None = None, replay_mask: torch.Tensor | None = None):  # noqa: ANN201
@@ -63,13 +63,20 @@ def grouped_ffn_ref(x_sorted: torch.Tensor, counts: list[int], w_gate_up: torch.
 
 
 class MoEBlock(nn.Module):
-    def __init__(self, cfg) -> None:  # noqa: ANN001
+    def __init__(self, cfg, ep=None) -> None:  # noqa: ANN001
         super().__init__()
         E, H, F = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
         self.E, self.k, self.renorm = E, cfg.num_experts_per_tok, cfg.norm_topk_prob
+        self.ep = ep
+        ep_size = ep.size if ep is not None else 1
+        assert E % ep_size == 0, "experts must split evenly over EP ranks"
+        E_l = E // ep_size  # experts held by this rank
         self.router = nn.Parameter(torch.empty(E, H))
-        self.experts_gate_up = nn.Parameter(torch.empty(E, 2 * F, H))
-        self.experts_down = nn.Parameter(torch.empty(E, H, F))
+        self.experts_gate_up = nn.Parameter(torch.empty(E_l, 2 * F, H))
+        self.experts_down = nn.Parameter(torch.empty(E_l, H, F))
+        if ep_size > 1:
+            self.experts_gate_up.expert_parallel = True
+            self.experts_down.expert_parallel = True
 
     def hf_tensors(self, prefix: str) -> dict[str, torch.Tensor]:
         out = {prefix + "mlp.gate.weight": self.router}
@@ -88,21 +95,16 @@ class MoEBlock(nn.Module):
         w, ids = route(logits, self.k, self.renorm, replay, ctx.replay_mask if ctx is not None else None)
         if ctx is not None and ctx.capture is not None:
             ctx.capture[layer_idx] = ids.to(torch.int16)
-        if ctx is not None and ctx.ep_group is not None:
+        if self.ep is not None and self.ep.enabled:
             from axrl_b200.parallel.expert import ep_moe_forward
 
-            return ep_moe_forward(x, w, ids, self, ctx.ep_group)
+            return ep_moe_forward(self, x, w, ids, self.ep)
         flat = ids.reshape(-1)
         order = torch.argsort(flat, stable=True)
         tok = order // self.k
-        counts = torch.bincount(flat, minlength=self.E).tolist()
+        offsets = expert_offsets(flat, self.E)
         xs = x.index_select(0, tok)
-        if x.is_cuda:
-            from axrl_b200.ops.grouped import grouped_swiglu_ffn
-
-            ys = grouped_swiglu_ffn(xs, counts, self.experts_gate_up, self.experts_down)
-        else:
-            ys = grouped_ffn_ref(xs, counts, self.experts_gate_up, self.experts_down)
+        ys = grouped_swiglu_ffn(xs, offsets, self.experts_gate_up, self.experts_down)
         ys = ys.float() * w.reshape(-1)[order][:, None]
         out = torch.zeros(T, H, dtype=torch.float32, device=x.device).index_add_(0, tok, ys)
         return out.to(x.dtype)

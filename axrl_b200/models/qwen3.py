@@ -160,7 +160,7 @@ class MLP(nn.Module):
 
 
 class DecoderLayer(nn.Module):
-    def __init__(self, cfg: Qwen3Config, layer_idx: int, tp_size: int = 1) -> None:
+    def __init__(self, cfg: Qwen3Config, layer_idx: int, tp_size: int = 1, ep=None) -> None:  # noqa: ANN001
         super().__init__()
         self.layer_idx = layer_idx
         self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
@@ -169,7 +169,7 @@ class DecoderLayer(nn.Module):
         if cfg.layer_is_moe(layer_idx):
             from axrl_b200.models.moe import MoEBlock
 
-            self.mlp: nn.Module = MoEBlock(cfg)
+            self.mlp: nn.Module = MoEBlock(cfg, ep)
         else:
             self.mlp = MLP(cfg.hidden_size, cfg.intermediate_size // tp_size)
 
@@ -188,15 +188,16 @@ class Qwen3Model(nn.Module):
     """Decoder stack.  ``forward`` returns final hidden states (T, H); the LM head
     is applied by :meth:`logprobs` (fused, chunked) or :meth:`logits`."""
 
-    def __init__(self, cfg: Qwen3Config, tp_size: int = 1, tp: TPContext | None = None) -> None:
+    def __init__(self, cfg: Qwen3Config, tp_size: int = 1, tp: TPContext | None = None, ep=None) -> None:  # noqa: ANN001
         super().__init__()
         self.cfg = cfg
         self.tp = tp or _NO_TP
+        self.ep = ep
         tp_size = self.tp.size if tp is not None else tp_size
         assert cfg.vocab_size % tp_size == 0, "vocabulary must split evenly over TP ranks"
         V = cfg.vocab_size // tp_size
         self.embed_tokens = nn.Parameter(torch.empty(V, cfg.hidden_size))
-        self.layers = nn.ModuleList(DecoderLayer(cfg, i, tp_size) for i in range(cfg.num_hidden_layers))
+        self.layers = nn.ModuleList(DecoderLayer(cfg, i, tp_size, ep) for i in range(cfg.num_hidden_layers))
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
         self.lm_head = None if cfg.tie_word_embeddings else nn.Parameter(torch.empty(V, cfg.hidden_size))
         self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.head_dim, cfg.rope_theta), persistent=False)
@@ -227,6 +228,8 @@ class Qwen3Model(nn.Module):
             ps = seed * 1000003 + zlib.crc32(name.encode())
             if self.tp.enabled and not getattr(p, "tp_replicated", False):
                 ps += 7919 * self.tp.rank
+            if getattr(p, "expert_parallel", False):
+                ps += 104729 * self.ep.rank
             if p.is_cuda:
                 cg = torch.Generator(device=p.device).manual_seed(ps)
                 p.normal_(0.0, s, generator=cg)

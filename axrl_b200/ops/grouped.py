@@ -1,25 +1,65 @@
 """Grouped expert FFN over tokens sorted by expert.
 
-Tokens arrive sorted by expert id with per-expert counts; each expert applies
-``down(swiglu(gate_up(x)))``.  This first version issues one tcgen05 GEMM pair per
-non-empty expert (the same kernels as the dense layers, so numerics and autograd are
-shared); the expert-parallel path (:mod:`axrl_b200.parallel.expert`) feeds it the tokens
-received from peers.
+Tokens arrive sorted by expert id with DEVICE row offsets (``offsets[e]:offsets[e+1]`` are expert
+``e``'s rows); each expert applies ``down(swiglu(gate_up(x)))``.  On the GPU each projection is
+ONE grouped tcgen05 GEMM over all experts (``csrc/kernels/grouped_gemm.cu``), so routing never
+forces a host sync; backward runs the grouped dgrad and accumulates the grouped weight gradient
+into the expert weights' fp32 ``main_grad``.  The CPU path loops over experts (the oracle).
+
+Reference counterpart: Megatron's grouped expert MLP (TE grouped GEMM) used by the Qwen3-MoE
+models (``axrl/worker/megatron_worker.py:833``).
 """
 
 from __future__ import annotations
 
 import torch
 
+from axrl_b200.ops import _ext
 from axrl_b200.ops import core as ops
 
 
-def grouped_swiglu_ffn(x_sorted: torch.Tensor, counts: list[int], w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
-    outs = []
-    s = 0
-    for e, c in enumerate(counts):
-        if c:
-            xe = x_sorted[s:s + c]
-            outs.append(ops.linear(ops.swiglu(ops.linear(xe, w_gate_up[e])), w_down[e]))
-        s += c
-    return torch.cat(outs, 0) if outs else x_sorted[:0]
+class _GroupedLinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, offsets):  # noqa: ANN001, ANN205
+        ctx.save_for_backward(x, w, offsets)
+        return _ext.ext().grouped_linear_fwd(x, w, offsets)
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        x, w, offsets = ctx.saved_tensors
+        dy = dy.contiguous()
+        e = _ext.ext()
+        dx = e.grouped_linear_dgrad(dy, w, offsets) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            main = getattr(w, "main_grad", None)
+            if main is not None:
+                e.grouped_linear_wgrad_acc(dy, x, offsets, main)
+            else:
+                acc = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+                e.grouped_linear_wgrad_acc(dy, x, offsets, acc)
+                dw = acc.to(w.dtype)
+        return dx, dw, None
+
+
+def grouped_linear_ref(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+    off = offsets.tolist()
+    outs = [x[off[e]:off[e + 1]] @ w[e].t() for e in range(w.shape[0])]
+    return torch.cat(outs, 0) if outs else x[:0, :0]
+
+
+def grouped_linear(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+    """Rows ``offsets[e]:offsets[e+1]`` of ``x`` times ``w[e].T`` for every expert ``e``."""
+    if not x.is_cuda:
+        return grouped_linear_ref(x, w, offsets)
+    return _GroupedLinear.apply(x.contiguous(), w, offsets.to(torch.int32).contiguous())
+
+
+def expert_offsets(expert_ids: torch.Tensor, num_experts: int) -> torch.Tensor:
+    """(E+1,) int32 row offsets of each expert in the expert-sorted order (device, no sync)."""
+    counts = torch.bincount(expert_ids, minlength=num_experts)
+    return torch.cat([counts.new_zeros(1), counts.cumsum(0)]).to(torch.int32)
+
+
+def grouped_swiglu_ffn(x_sorted: torch.Tensor, offsets: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    return grouped_linear(ops.swiglu(grouped_linear(x_sorted, w_gate_up, offsets)), w_down, offsets)

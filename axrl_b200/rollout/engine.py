@@ -245,7 +245,11 @@ class RolloutEngine:
             return n // self.P + len(groups[key]) * ((1 if n % self.P else 0) + headroom)
 
         total = sum(need(k) for k in order)
-        while order and total > self.bm.num_available():
+        # keep the pages that running sequences need for their next burst, plus a 1% watermark:
+        # admitting into that space would only force a preemption (and a re-prefill) next burst
+        reserve = sum(max(0, self._pages_needed(min(len(s.tokens) + self.burst, s.end_total)) - len(s.pages)) for s in self.running)
+        reserve += max(1, self.num_pages // 100) if self.running else 0
+        while order and total + reserve > self.bm.num_available():
             total -= need(order[-1])
             del groups[order.pop()]
         if not order:

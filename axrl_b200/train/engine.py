@@ -38,6 +38,9 @@ class ParallelCtx:
     tp_size: int = 1
     tp_rank: int = 0
     tp_backend: str = "torch"  # "torch" (NCCL/gloo collectives) | "p2p" (NVLink kernels)
+    ep_group: object | None = None
+    ep_size: int = 1
+    ep_backend: str = "torch"
 
 
 class TrainEngine:
@@ -51,8 +54,14 @@ class TrainEngine:
         from axrl_b200.parallel.tensor_parallel import TPContext
 
         self.tp = TPContext.from_group(self.par.tp_group, backend=self.par.tp_backend) if self.par.tp_size > 1 else TPContext()
+        from axrl_b200.parallel.expert import EPContext
+
+        self.ep = (EPContext.from_group(self.par.ep_group, backend=self.par.ep_backend, hidden=model_cfg.hidden_size,
+                                        num_experts=model_cfg.num_experts,
+                                        max_rows=(cfg.max_tokens_per_micro_batch + 1024) * max(1, model_cfg.num_experts_per_tok))
+                   if self.par.ep_size > 1 else EPContext())
         if model is None:
-            model = Qwen3Model(model_cfg, tp=self.tp)
+            model = Qwen3Model(model_cfg, tp=self.tp, ep=self.ep if self.ep.enabled else None)
             model.init_weights(cfg.seed)
             model = model.to(device=self.device, dtype=dtype)
             model.inv_freq = model.inv_freq.float()
@@ -142,8 +151,20 @@ class TrainEngine:
                 metrics_acc.append(m)
         self.optim.fold_param_grads()
         if self.par.dp_group is not None and self.par.dp_size > 1:
-            dist.all_reduce(self.optim.grad, group=self.par.dp_group)  # replicated-optimizer baseline path
+            if self.ep.enabled:  # expert weights differ per EP rank: reduce only the dense gradients
+                from axrl_b200.parallel.expert import dense_grad_allreduce
+
+                dense_grad_allreduce(self.model, self.par.dp_group)
+            else:
+                dist.all_reduce(self.optim.grad, group=self.par.dp_group)  # replicated-optimizer baseline path
         sq = self.optim.grad_sqnorm()
+        if self.ep.enabled:
+            from axrl_b200.parallel.expert import expert_params
+
+            sq_e = sum(p.main_grad.float().pow(2).sum() for p in expert_params(self.model)).reshape(1)
+            sq_all = sq_e.clone()
+            dist.all_reduce(sq_all, group=self.ep.group)
+            sq = (sq - sq_e + sq_all).float()
         if self.tp.enabled:
             from axrl_b200.parallel import tensor_parallel as tpl
 
@@ -156,8 +177,9 @@ class TrainEngine:
             self.tp.comm.all_reduce(sq)
         norm = self.optim.step(grad_scale=1.0 / total_denom, sqnorm=sq)
         norm = float(norm)
-        if self.tp.enabled and hasattr(self.tp.comm, "check"):
-            self.tp.comm.check()
+        for comm in (self.tp.comm, self.ep.comm):
+            if comm is not None and hasattr(comm, "check"):
+                comm.check()
         if self.release_grads_after_step:
             self.optim.release_grads()
         out = {k: sum(d[k] for d in metrics_acc if k in d) / max(1, sum(1 for d in metrics_acc if k in d))

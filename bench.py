@@ -155,10 +155,13 @@ def main() -> None:
         torch.cuda.synchronize()
 
     for i in range(a.warmup):
+        st0 = dict(pipe.rollout.stats)
         m = pipe.run_step()
         if a.verbose and rank == 0:
+            rs = {k: round(v - st0.get(k, 0), 3) for k, v in pipe.rollout.stats.items()}
             print(f"warmup {i}: " + json.dumps({k: round(v, 3) if isinstance(v, float) else v for k, v in m.items()
-                                                 if k.endswith("_s") or k in ("trained_tokens", "loss", "grad_norm", "reward_mean")}), flush=True)
+                                                 if k.endswith("_s") or k in ("trained_tokens", "loss", "grad_norm", "reward_mean")})
+                  + " rollout " + json.dumps(rs), flush=True)
 
     clocks = ClockSampler(local)
     barrier()

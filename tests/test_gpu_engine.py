@@ -135,7 +135,8 @@ def test_kv_release_acquire_and_preemption():
         assert len(a.output_ids) == len(b.output_ids) == L
     eng.release_graphs()
 
-    # 10 pages of 64 tokens for six sequences that need up to 5 pages each
+    # 10 pages of 64 tokens for six sequences that grow to up to 6 pages each
+    forced = [300, 7, 280, 64, 250, 90]
     small = RolloutEngine(m, max_batch=8, kv_tokens=640, max_context=512, seed=3, burst=8, eos_token_id=3)
     reqs = _reqs(6, forced)
     for r in reqs:

@@ -262,3 +262,31 @@ def test_embedding():
     out.backward(g.bfloat16())
     ref = torch.zeros(100, 256, device=DEV).index_add_(0, ids, g.bfloat16().float())
     close(table.grad, ref, 2e-2)
+
+
+def test_grouped_linear_fwd_bwd_matches_per_expert_fp32():
+    """One grouped tcgen05 GEMM over all experts (device offsets, some experts empty) against
+    per-expert fp32 matmuls; dgrad and the fp32 wgrad accumulation into main_grad."""
+    from axrl_b200.ops.grouped import expert_offsets, grouped_linear
+
+    torch.manual_seed(0)
+    E, N, K = 6, 384, 256
+    ids = torch.tensor([0] * 70 + [2] * 1 + [3] * 200 + [5] * 33, device="cuda")
+    off = expert_offsets(ids, E)
+    M = ids.numel()
+    x = (torch.randn(M, K, device="cuda") * 0.5).bfloat16().requires_grad_(True)
+    w = (torch.randn(E, N, K, device="cuda") * 0.05).bfloat16().requires_grad_(True)
+    w.main_grad = torch.ones(E, N, K, device="cuda")  # accumulates on top
+    y = grouped_linear(x, w, off)
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    y.backward(dy)
+    o = off.tolist()
+    xf, wf, dyf = x.detach().float(), w.detach().float(), dy.float()
+    for e in range(E):
+        r0, r1 = o[e], o[e + 1]
+        if r1 > r0:
+            torch.testing.assert_close(y[r0:r1].float(), xf[r0:r1] @ wf[e].t(), atol=3e-2, rtol=2e-2)
+            torch.testing.assert_close(x.grad[r0:r1].float(), dyf[r0:r1] @ wf[e], atol=3e-2, rtol=2e-2)
+        exp = 1.0 + dyf[r0:r1].t() @ xf[r0:r1]
+        torch.testing.assert_close(w.main_grad[e], exp, atol=5e-2, rtol=2e-2)
+    assert w.grad is None
