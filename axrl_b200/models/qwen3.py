@@ -188,18 +188,25 @@ class Qwen3Model(nn.Module):
     """Decoder stack.  ``forward`` returns final hidden states (T, H); the LM head
     is applied by :meth:`logprobs` (fused, chunked) or :meth:`logits`."""
 
-    def __init__(self, cfg: Qwen3Config, tp_size: int = 1, tp: TPContext | None = None, ep=None) -> None:  # noqa: ANN001
+    def __init__(self, cfg: Qwen3Config, tp_size: int = 1, tp: TPContext | None = None, ep=None, pp=None) -> None:  # noqa: ANN001
         super().__init__()
         self.cfg = cfg
         self.tp = tp or _NO_TP
         self.ep = ep
+        self.pp = pp
         tp_size = self.tp.size if tp is not None else tp_size
         assert cfg.vocab_size % tp_size == 0, "vocabulary must split evenly over TP ranks"
         V = cfg.vocab_size // tp_size
-        self.embed_tokens = nn.Parameter(torch.empty(V, cfg.hidden_size))
-        self.layers = nn.ModuleList(DecoderLayer(cfg, i, tp_size, ep) for i in range(cfg.num_hidden_layers))
-        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
-        self.lm_head = None if cfg.tie_word_embeddings else nn.Parameter(torch.empty(V, cfg.hidden_size))
+        # pipeline stage: a contiguous block of layers; embedding on the first stage, final norm and
+        # LM head on the last (a tied LM head is a copy of the embedding kept on the last stage)
+        lo, hi = (0, cfg.num_hidden_layers) if pp is None else pp.layer_range(cfg.num_hidden_layers)
+        self.layer_offset = lo
+        self.first = pp is None or pp.is_first
+        self.last = pp is None or pp.is_last
+        self.embed_tokens = nn.Parameter(torch.empty(V, cfg.hidden_size)) if (self.first or (self.last and cfg.tie_word_embeddings)) else None
+        self.layers = nn.ModuleList(DecoderLayer(cfg, i, tp_size, ep) for i in range(lo, hi))
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps) if self.last else None
+        self.lm_head = None if (cfg.tie_word_embeddings or not self.last) else nn.Parameter(torch.empty(V, cfg.hidden_size))
         self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.head_dim, cfg.rope_theta), persistent=False)
         self.recompute = False
         if tp_size > 1:
@@ -225,7 +232,7 @@ class Qwen3Model(nn.Module):
                 p.fill_(1.0)
                 continue
             s = out_std if name.endswith(("o_proj", "down_proj")) else std
-            ps = seed * 1000003 + zlib.crc32(name.encode())
+            ps = seed * 1000003 + zlib.crc32(self.global_name(name).encode())
             if self.tp.enabled and not getattr(p, "tp_replicated", False):
                 ps += 7919 * self.tp.rank
             if getattr(p, "expert_parallel", False):
@@ -237,15 +244,26 @@ class Qwen3Model(nn.Module):
                 g = torch.Generator(device="cpu").manual_seed(ps)
                 p.copy_(torch.randn(p.shape, generator=g) * s)
 
+    def global_name(self, name: str) -> str:
+        """Parameter name with the global layer index (pipeline stages hold a slice of the layers)."""
+        if self.layer_offset and name.startswith("layers."):
+            i, rest = name[len("layers."):].split(".", 1)
+            return f"layers.{int(i) + self.layer_offset}.{rest}"
+        return name
+
     def embed(self, ids: torch.Tensor) -> torch.Tensor:
         """Token rows of ``ids`` (T,) -> hidden (T, H), or this TP rank's (T/tp, H) slice."""
         if self.tp.enabled:
             return tpl.vocab_parallel_embedding(ids, self.embed_tokens, self.tp)
         return ops.embedding(ids, self.embed_tokens)
 
-    def forward(self, ids: torch.Tensor, pos: torch.Tensor, spec: AttnSpec, moe_ctx=None) -> torch.Tensor:  # noqa: ANN001
-        """Final hidden states: (T, H), or (T/tp, H) rows of this rank under TP (T % tp == 0)."""
-        h = self.embed(ids)
+    def forward(self, ids: torch.Tensor, pos: torch.Tensor, spec: AttnSpec, moe_ctx=None,  # noqa: ANN001
+                hidden: torch.Tensor | None = None) -> torch.Tensor:
+        """Final hidden states: (T, H), or (T/tp, H) rows of this rank under TP (T % tp == 0).
+
+        A pipeline stage other than the first takes the previous stage's output as ``hidden``; a
+        stage other than the last returns its raw output (no final norm)."""
+        h = self.embed(ids) if self.first else hidden
         inv = self.inv_freq
         tp = self.tp
         for layer in self.layers:
@@ -253,7 +271,7 @@ class Qwen3Model(nn.Module):
                 h = checkpoint(layer, h, pos, inv, spec, moe_ctx, tp, use_reentrant=False)
             else:
                 h = layer(h, pos, inv, spec, moe_ctx, tp)
-        return self.norm(h)
+        return self.norm(h) if self.last else h
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         assert not self.tp.enabled, "full logits are a rollout-side (TP=1) operation"

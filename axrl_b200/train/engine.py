@@ -41,6 +41,8 @@ class ParallelCtx:
     ep_group: object | None = None
     ep_size: int = 1
     ep_backend: str = "torch"
+    pp_group: object | None = None
+    pp_size: int = 1
 
 
 class TrainEngine:
@@ -60,8 +62,12 @@ class TrainEngine:
                                         num_experts=model_cfg.num_experts,
                                         max_rows=(cfg.max_tokens_per_micro_batch + 1024) * max(1, model_cfg.num_experts_per_tok))
                    if self.par.ep_size > 1 else EPContext())
+        from axrl_b200.parallel.pipeline import PPContext
+
+        self.pp = PPContext.from_group(self.par.pp_group) if self.par.pp_size > 1 else PPContext()
         if model is None:
-            model = Qwen3Model(model_cfg, tp=self.tp, ep=self.ep if self.ep.enabled else None)
+            model = Qwen3Model(model_cfg, tp=self.tp, ep=self.ep if self.ep.enabled else None,
+                               pp=self.pp if self.pp.enabled else None)
             model.init_weights(cfg.seed)
             model = model.to(device=self.device, dtype=dtype)
             model.inv_freq = model.inv_freq.float()
@@ -98,6 +104,8 @@ class TrainEngine:
         self.model.eval()
         B, S = batch["input_ids"].shape
         out = torch.zeros((B, S), dtype=torch.float32)
+        if self.pp.enabled:
+            return self._compute_logprobs_pp(batch, temperature, out)
         for mb in self.micro_batches(batch):
             dmb = mb.to(self.device)
             h = self._hidden(dmb)
@@ -109,6 +117,37 @@ class TrainEngine:
             for li, r in enumerate(mb.rows):
                 out[r] = dense[li]
         return out
+
+    def _act_shape(self, mb: PackedMicroBatch) -> tuple:
+        return (mb.num_tokens // self.tp.size, self.mcfg.hidden_size)
+
+    def _act_dtype(self) -> torch.dtype:
+        return next(self.model.parameters()).dtype
+
+    def _compute_logprobs_pp(self, batch: SampleBatch, temperature: float, out: torch.Tensor) -> torch.Tensor:
+        from axrl_b200.parallel.pipeline import run_forward_only
+
+        S = out.shape[1]
+        mbs = self.micro_batches(batch)
+        dmbs = [mb.to(self.device) for mb in mbs]
+
+        def fwd(i: int, inp):  # noqa: ANN001, ANN202
+            d = dmbs[i]
+            return self.model(d.ids, d.pos, d.spec, None, hidden=inp)
+
+        def consume(i: int, h: torch.Tensor) -> None:
+            d = dmbs[i]
+            lp, _ = self.model.logprobs(h, d.labels.clamp(min=-1), temperature)
+            lp = torch.where(d.labels >= 0, lp, torch.zeros_like(lp))
+            dense = d.unpack(lp.float(), S).cpu()
+            for li, r in enumerate(mbs[i].rows):
+                out[r] = dense[li]
+
+        run_forward_only(self.pp, len(mbs), lambda i: self._act_shape(mbs[i]), self._act_dtype(), self.device, fwd, consume)
+        # the last stage holds the result: broadcast it to every stage
+        t = out.to(self.device)
+        dist.broadcast(t, src=self.pp.ranks[-1], group=self.pp.group)
+        return t.cpu()
 
     # ------------------------------------------------------------------ train
     def _global_denominator(self, batch: SampleBatch, trainer) -> float:  # noqa: ANN001
@@ -134,7 +173,9 @@ class TrainEngine:
         S = batch["input_ids"].shape[1]
         mbs = self.micro_batches(batch)
         metrics_acc: list[dict] = []
-        for i, mb in enumerate(mbs):
+        if self.pp.enabled:
+            metrics_acc = self._forward_backward_pp(batch, mbs, trainer, temperature, need_entropy, metrics_every_micro_batch)
+        for i, mb in enumerate(mbs if not self.pp.enabled else []):
             dmb = mb.to(self.device)
             h = self._hidden(dmb)
             lp, ent = self.model.logprobs(h, dmb.labels.clamp(min=-1), temperature, entropy=need_entropy)
@@ -175,6 +216,9 @@ class TrainEngine:
                 sq = sq - rep * (1.0 - 1.0 / self.tp.size)
             sq = sq.reshape(1).float().clone()
             self.tp.comm.all_reduce(sq)
+        if self.pp.enabled:  # every stage holds different parameters
+            sq = sq.reshape(1).float().clone()
+            dist.all_reduce(sq, group=self.pp.group)
         norm = self.optim.step(grad_scale=1.0 / total_denom, sqnorm=sq)
         norm = float(norm)
         for comm in (self.tp.comm, self.ep.comm):
@@ -189,6 +233,37 @@ class TrainEngine:
         out["step_time_sec"] = time.perf_counter() - t0
         out["lr"] = self.current_lr()
         return out
+
+    def _forward_backward_pp(self, batch: SampleBatch, mbs: list[PackedMicroBatch], trainer, temperature: float,  # noqa: ANN001
+                             need_entropy: bool, every: bool) -> list[dict]:
+        from axrl_b200.parallel.pipeline import run_1f1b
+
+        S = batch["input_ids"].shape[1]
+        dmbs = [mb.to(self.device) for mb in mbs]
+        metrics_acc: list[dict] = []
+
+        def fwd(i: int, inp):  # noqa: ANN001, ANN202
+            d = dmbs[i]
+            return self.model(d.ids, d.pos, d.spec, None, hidden=inp)
+
+        def loss(i: int, h: torch.Tensor) -> torch.Tensor:
+            d = dmbs[i]
+            lp, ent = self.model.logprobs(h, d.labels.clamp(min=-1), temperature, entropy=need_entropy)
+            lp = torch.where(d.labels >= 0, lp, torch.zeros_like(lp))
+            sub = batch.select_rows(mbs[i].rows).to(self.device)
+            outputs = {"log_prob": d.unpack(lp, S),
+                       "entropy": d.unpack(ent, S) if ent is not None else torch.zeros((len(mbs[i].rows), S), device=self.device)}
+            want = every or i == len(mbs) - 1
+            l, denom, m = trainer.loss_func(outputs, sub, with_metrics=want)
+            if want:
+                metrics_acc.append(m)
+            return l * denom.to(l.dtype)
+
+        run_1f1b(self.pp, len(mbs), lambda i: self._act_shape(mbs[i]), self._act_dtype(), self.device, fwd, loss)
+        # metrics live on the last stage
+        obj = [metrics_acc if self.pp.is_last else None]
+        dist.broadcast_object_list(obj, src=self.pp.ranks[-1], group=self.pp.group)
+        return obj[0]
 
     def current_lr(self) -> float:
         from axrl_b200.train.optimizer import lr_at

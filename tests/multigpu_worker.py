@@ -186,6 +186,68 @@ def case_tp_timeout() -> None:
     print(f"rank {rank}: tp timeout ok", flush=True)
 
 
+def case_ep() -> None:
+    """EP=world MoE layer stack: NCCL all-to-all and the NVLink dispatch/combine kernels, each against
+    the EP=1 model (same weights) on this rank's own tokens; expert gradients summed over ranks."""
+    from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from axrl_b200.ops.attention_spec import spec_from_triples
+    from axrl_b200.parallel.expert import EPContext, load_ep_shards_from_full
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = Qwen3Config(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=8,
+                      num_key_value_heads=4, head_dim=128, num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256)
+    full = Qwen3Model(cfg)
+    full.init_weights(9)
+    full = full.to("cuda", torch.bfloat16)
+    full.inv_freq = full.inv_freq.float()
+    state = {k: v.detach().clone() for k, v in full.named_parameters()}
+    T = 300 + 64 * rank
+    g = torch.Generator().manual_seed(50 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (T,), generator=g).cuda()
+    labels = torch.randint(0, cfg.vocab_size, (T,), generator=g).cuda()
+    spec = spec_from_triples([(0, T, 0, T, 1)], T).to("cuda")
+    pos = torch.arange(T).int().cuda()
+
+    def run(model):
+        for p in model.parameters():
+            p.main_grad = torch.zeros(p.shape, dtype=torch.float32, device="cuda")
+            p.grad = None
+        lp, _ = model.logprobs(model(ids, pos, spec), labels)
+        lp.mean().backward()
+        for p in model.parameters():
+            if p.grad is not None:
+                p.main_grad += p.grad.float()
+                p.grad = None
+        return lp.detach()
+
+    lp_ref = run(full)
+    fulld = dict(full.named_parameters())
+    for backend in ("torch", "p2p"):
+        ep = EPContext.from_group(dist.group.WORLD, backend=backend, hidden=cfg.hidden_size, num_experts=cfg.num_experts,
+                                  max_rows=2048 * cfg.num_experts_per_tok)
+        m = Qwen3Model(cfg, ep=ep).to("cuda", torch.bfloat16)
+        m.inv_freq = m.inv_freq.float()
+        load_ep_shards_from_full(m, state, ep)
+        lp = run(m)
+        torch.cuda.synchronize()
+        if hasattr(ep.comm, "check"):
+            ep.comm.check()
+        d = (lp - lp_ref).abs().max().item()
+        assert d < 5e-2, f"{backend}: lp diff {d}"
+        worst = 0.0
+        for n, p in m.named_parameters():
+            ref = fulld[n].main_grad
+            if getattr(p, "expert_parallel", False):
+                ref = ref.clone()
+                dist.all_reduce(ref)
+                El = p.shape[0]
+                ref = ref[rank * El:(rank + 1) * El]
+            rel = ((p.main_grad - ref).norm() / (ref.norm() + 1e-12)).item()
+            worst = max(worst, rel)
+            assert rel < 3e-2, f"{backend}: grad {n} rel err {rel}"
+        print(f"rank {rank}: ep {backend} ok (lp diff {d:.2e}, worst grad rel err {worst:.2e})", flush=True)
+
+
 if __name__ == "__main__":
     from datetime import timedelta
 

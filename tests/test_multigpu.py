@@ -38,3 +38,8 @@ def test_tensor_parallel_two_gpus():
 
 def test_tp_p2p_wait_times_out_without_hanging():
     assert _run("tp_timeout").count("tp timeout ok") == 2
+
+
+def test_expert_parallel_two_gpus():
+    out = _run("ep")
+    assert out.count("ep torch ok") == 2 and out.count("ep p2p ok") == 2, out[-2000:]
