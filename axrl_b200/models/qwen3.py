@@ -141,10 +141,15 @@ class Attention(nn.Module):
         self.o_proj = nn.Parameter(torch.empty(H, self.nq * self.d))
         self.q_norm = nn.Parameter(torch.ones(self.d))
         self.k_norm = nn.Parameter(torch.ones(self.d))
+        self.cp = None  # context-parallel group (set by the model)
 
     def forward(self, x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, tp: TPContext = _NO_TP) -> torch.Tensor:
         qkv = tpl.column_parallel_linear(x, self.qkv_proj, tp)
         q, k, v = ops.qk_norm_rope(qkv, self.q_norm, self.k_norm, pos, inv_freq, self.nq, self.nkv, self.eps)
+        if self.cp is not None and self.cp.enabled:  # keys/values of every context-parallel rank
+            from axrl_b200.parallel.context_parallel import gather_kv
+
+            k, v = gather_kv(k, self.cp), gather_kv(v, self.cp)
         o = ops.attention(q, k, v, spec)
         return tpl.row_parallel_linear(o.reshape(o.shape[0], -1), self.o_proj, tp)
 
@@ -188,9 +193,10 @@ class Qwen3Model(nn.Module):
     """Decoder stack.  ``forward`` returns final hidden states (T, H); the LM head
     is applied by :meth:`logprobs` (fused, chunked) or :meth:`logits`."""
 
-    def __init__(self, cfg: Qwen3Config, tp_size: int = 1, tp: TPContext | None = None, ep=None, pp=None) -> None:  # noqa: ANN001
+    def __init__(self, cfg: Qwen3Config, tp_size: int = 1, tp: TPContext | None = None, ep=None, pp=None, cp=None) -> None:  # noqa: ANN001
         super().__init__()
         self.cfg = cfg
+        self.cp = cp
         self.tp = tp or _NO_TP
         self.ep = ep
         self.pp = pp
@@ -209,6 +215,8 @@ class Qwen3Model(nn.Module):
         self.lm_head = None if (cfg.tie_word_embeddings or not self.last) else nn.Parameter(torch.empty(V, cfg.hidden_size))
         self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.head_dim, cfg.rope_theta), persistent=False)
         self.recompute = False
+        for layer in self.layers:
+            layer.self_attn.cp = cp
         if tp_size > 1:
             for name, p in self.named_parameters():
                 if p.dim() < 2 or ".mlp.router" in name or ".mlp.experts" in name:

@@ -64,8 +64,9 @@ class AttnSpec:
         return out
 
 
-def spec_from_triples(triples: list[tuple[int, int, int, int, int]], total: int) -> AttnSpec:
-    """Build both groupings from ``(q0, q1, k0, k1, type)`` triples."""
+def spec_from_triples(triples: list[tuple[int, int, int, int, int]], total: int, total_k: int | None = None) -> AttnSpec:
+    """Build both groupings from ``(q0, q1, k0, k1, type)`` triples (``total_k`` defaults to
+    ``total``; it differs when the keys are gathered from other context-parallel ranks)."""
     by_q: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
     by_k: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
     for q0, q1, k0, k1, t in triples:
@@ -85,8 +86,8 @@ def spec_from_triples(triples: list[tuple[int, int, int, int, int]], total: int)
     kseg, qr = group(by_k)
     mq = int((qseg[:, 1] - qseg[:, 0]).max()) if len(qseg) else 0
     mk = int((kseg[:, 1] - kseg[:, 0]).max()) if len(kseg) else 0
-    return AttnSpec(torch.from_numpy(qseg), torch.from_numpy(kr), torch.from_numpy(kseg), torch.from_numpy(qr), total, total, mq, mk,
-                    _tiles(qseg, FWD_Q_TILE), _tiles(kseg, BWD_K_TILE))
+    return AttnSpec(torch.from_numpy(qseg), torch.from_numpy(kr), torch.from_numpy(kseg), torch.from_numpy(qr), total,
+                    total if total_k is None else total_k, mq, mk, _tiles(qseg, FWD_Q_TILE), _tiles(kseg, BWD_K_TILE))
 
 
 FWD_Q_TILE = 128

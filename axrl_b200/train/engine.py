@@ -43,6 +43,8 @@ class ParallelCtx:
     ep_backend: str = "torch"
     pp_group: object | None = None
     pp_size: int = 1
+    cp_group: object | None = None
+    cp_size: int = 1
 
 
 class TrainEngine:
@@ -62,12 +64,14 @@ class TrainEngine:
                                         num_experts=model_cfg.num_experts,
                                         max_rows=(cfg.max_tokens_per_micro_batch + 1024) * max(1, model_cfg.num_experts_per_tok))
                    if self.par.ep_size > 1 else EPContext())
+        from axrl_b200.parallel.context_parallel import CPContext
         from axrl_b200.parallel.pipeline import PPContext
 
         self.pp = PPContext.from_group(self.par.pp_group) if self.par.pp_size > 1 else PPContext()
+        self.cp = CPContext.from_group(self.par.cp_group) if self.par.cp_size > 1 else CPContext()
         if model is None:
             model = Qwen3Model(model_cfg, tp=self.tp, ep=self.ep if self.ep.enabled else None,
-                               pp=self.pp if self.pp.enabled else None)
+                               pp=self.pp if self.pp.enabled else None, cp=self.cp if self.cp.enabled else None)
             model.init_weights(cfg.seed)
             model = model.to(device=self.device, dtype=dtype)
             model.inv_freq = model.inv_freq.float()
@@ -90,7 +94,11 @@ class TrainEngine:
             n = torch.tensor([len(split_balanced(lengths, self.max_tokens))], dtype=torch.int64)
             dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.par.dp_group)
             min_count = int(n)
-        parts = split_balanced(lengths, self.max_tokens, min_count=min_count)
+        parts = split_balanced(lengths, self.max_tokens * self.cp.size, min_count=min_count)
+        if self.cp.enabled:
+            from axrl_b200.parallel.context_parallel import pack_rows_cp
+
+            return [pack_rows_cp(batch, p, self.cp) for p in parts if p]
         pad_to = self.tp.size * (16 if self.device.type == "cuda" else 1)
         return [pack_rows(batch, p, pad_to=pad_to) for p in parts if p]
 
@@ -115,7 +123,11 @@ class TrainEngine:
             if self.device.type == "cuda":
                 iostats.add_d2h(dense)
             for li, r in enumerate(mb.rows):
-                out[r] = dense[li]
+                out[r] += dense[li]
+        if self.cp.enabled:  # every position is held by exactly one CP rank
+            t = out.to(self.device)
+            dist.all_reduce(t, group=self.cp.group)
+            out = t.cpu()
         return out
 
     def _act_shape(self, mb: PackedMicroBatch) -> tuple:
@@ -183,6 +195,10 @@ class TrainEngine:
             sub = batch.select_rows(mb.rows).to(self.device)
             if self.device.type == "cuda":
                 iostats.add_h2d(*sub.tensors.values())
+            if self.cp.enabled:  # this rank trains on the tokens it holds
+                from axrl_b200.parallel.context_parallel import local_token_mask
+
+                sub["loss_mask"] = (sub["loss_mask"].bool() & local_token_mask(dmb, S)).to(sub["loss_mask"].dtype)
             outputs = {"log_prob": dmb.unpack(lp, S),
                        "entropy": dmb.unpack(ent, S) if ent is not None else torch.zeros((len(mb.rows), S), device=self.device)}
             want = metrics_every_micro_batch or i == len(mbs) - 1
@@ -191,6 +207,8 @@ class TrainEngine:
             if want:
                 metrics_acc.append(m)
         self.optim.fold_param_grads()
+        if self.cp.enabled:  # each CP rank back-propagated its own tokens: sum
+            dist.all_reduce(self.optim.grad, group=self.cp.group)
         if self.par.dp_group is not None and self.par.dp_size > 1:
             if self.ep.enabled:  # expert weights differ per EP rank: reduce only the dense gradients
                 from axrl_b200.parallel.expert import dense_grad_allreduce

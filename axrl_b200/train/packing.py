@@ -41,6 +41,7 @@ class PackedMicroBatch:
     spec: AttnSpec
     fields: dict[str, torch.Tensor]  # per-token float fields (advantage, logprobs, ...)
     merge_info: list | None = None
+    token_col: torch.Tensor | None = None  # (T,) column of each token in its row when rows are not contiguous (CP)
 
     @property
     def num_tokens(self) -> int:
@@ -53,11 +54,16 @@ class PackedMicroBatch:
             iostats.add_h2d(self.ids, self.pos, self.labels, self.loss_mask, self.token_row, *self.fields.values())
         mv = lambda t: t.to(device, non_blocking=non_blocking)  # noqa: E731
         return PackedMicroBatch(self.rows, self.row_len, self.row_off, mv(self.ids), mv(self.pos), mv(self.labels), mv(self.loss_mask),
-                                mv(self.token_row), self.spec.to(device), {k: mv(v) for k, v in self.fields.items()}, self.merge_info)
+                                mv(self.token_row), self.spec.to(device), {k: mv(v) for k, v in self.fields.items()}, self.merge_info,
+                                None if self.token_col is None else mv(self.token_col))
 
     def unpack(self, flat: torch.Tensor, width: int) -> torch.Tensor:
         """(T,) per-token values -> (rows, width) right-padded with zeros."""
         out = torch.zeros((len(self.rows), width), dtype=flat.dtype, device=flat.device)
+        if self.token_col is not None:
+            keep = self.token_row >= 0
+            out[self.token_row[keep], self.token_col[keep]] = flat[keep]
+            return out
         n = sum(self.row_len)  # trailing padding tokens (token_row -1) are dropped
         trow = self.token_row[:n]
         col = torch.arange(n, device=flat.device) - torch.as_tensor(self.row_off, device=flat.device)[trow]
