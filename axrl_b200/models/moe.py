@@ -37,6 +37,30 @@ class MoEContext:
                           capture=self.capture, aux_loss=self.aux_loss)
 
 
+class _RouterLinear(torch.autograd.Function):
+    """fp32 router logits; the weight gradient goes straight into ``main_grad`` when present."""
+
+    @staticmethod
+    def forward(ctx, x, w):  # noqa: ANN001, ANN205
+        ctx.save_for_backward(x, w)
+        return torch.nn.functional.linear(x.float(), w.float())
+
+    @staticmethod
+    def backward(ctx, g):  # noqa: ANN001, ANN205
+        x, w = ctx.saved_tensors
+        dx = (g @ w.float()).to(x.dtype)
+        dw = g.t() @ x.float()
+        main = getattr(w, "main_grad", None)
+        if main is not None:
+            main.add_(dw)
+            return dx, None
+        return dx, dw.to(w.dtype)
+
+
+def router_logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    return _RouterLinear.apply(x, w)
+
+
 def route(logits: torch.Tensor, k: int, renorm: bool, replay: torch.Tensor | None = None, replay_mask: torch.Tensor | None = None):  # noqa: ANN201
     """Top-k routing in fp32.  Returns (weights (T,k) fp32, ids (T,k) int64)."""
     probs = torch.softmax(logits.float(), -1)
@@ -90,7 +114,7 @@ class MoEBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, ctx: MoEContext | None = None, layer_idx: int = 0) -> torch.Tensor:
         T, H = x.shape
-        logits = torch.nn.functional.linear(x.float(), self.router.float())
+        logits = router_logits(x, self.router)
         replay = ctx.replay.get(layer_idx) if ctx is not None and ctx.replay else None
         w, ids = route(logits, self.k, self.renorm, replay, ctx.replay_mask if ctx is not None else None)
         if ctx is not None and ctx.capture is not None:

@@ -189,6 +189,14 @@ class DecoderLayer(nn.Module):
         return h + self.mlp(x, tp)
 
 
+class _LayerDone:
+    def __init__(self, fn, idx: int) -> None:  # noqa: ANN001
+        self.fn, self.idx = fn, idx
+
+    def __call__(self, g: torch.Tensor) -> None:
+        self.fn(self.idx)
+
+
 class Qwen3Model(nn.Module):
     """Decoder stack.  ``forward`` returns final hidden states (T, H); the LM head
     is applied by :meth:`logprobs` (fused, chunked) or :meth:`logits`."""
@@ -215,6 +223,7 @@ class Qwen3Model(nn.Module):
         self.lm_head = None if (cfg.tie_word_embeddings or not self.last) else nn.Parameter(torch.empty(V, cfg.hidden_size))
         self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.head_dim, cfg.rope_theta), persistent=False)
         self.recompute = False
+        self.grad_ready_hook = None  # set by an optimizer that reduces gradients during backward
         for layer in self.layers:
             layer.self_attn.cp = cp
         if tp_size > 1:
@@ -274,7 +283,12 @@ class Qwen3Model(nn.Module):
         h = self.embed(ids) if self.first else hidden
         inv = self.inv_freq
         tp = self.tp
+        hook = self.grad_ready_hook if torch.is_grad_enabled() else None
         for layer in self.layers:
+            if hook is not None and h.requires_grad:
+                # fires once the gradient of this layer's input exists, i.e. the layer's backward
+                # (weight gradients included) has been issued
+                h.register_hook(_LayerDone(hook, layer.layer_idx))
             if self.recompute and torch.is_grad_enabled():
                 h = checkpoint(layer, h, pos, inv, spec, moe_ctx, tp, use_reentrant=False)
             else:

@@ -26,6 +26,16 @@ from axrl_b200.ops.attention_spec import AttnSpec, dense_mask
 # ----------------------------------------------------------------------------- RMSNorm
 
 
+def _to_main_grad(w: torch.Tensor, dw: torch.Tensor):  # noqa: ANN202
+    """Weight gradient of a small parameter: added into its fp32 ``main_grad`` when the optimizer
+    attached one (so every gradient is final when the layer's backward ends), else returned."""
+    main = getattr(w, "main_grad", None)
+    if main is not None:
+        main.add_(dw.float())
+        return None
+    return dw.to(w.dtype)
+
+
 def _rms_ref(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     xf = x.float()
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
@@ -42,7 +52,7 @@ class _RMSNorm(torch.autograd.Function):
     def backward(ctx, dy):  # noqa: ANN001, ANN205
         x, w, rstd = ctx.saved_tensors
         dx, dw = _ext.ext().rmsnorm_bwd(dy.contiguous(), x, w, rstd)
-        return dx, dw.to(w.dtype), None
+        return dx, _to_main_grad(w, dw), None
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
@@ -92,7 +102,7 @@ class _QKNormRope(torch.autograd.Function):
         qkv, qw, kw, pos, inv_freq, rstd = ctx.saved_tensors
         nq, nkv = ctx.shape
         dqkv, dqw, dkw = _ext.ext().qknorm_rope_bwd(dq.contiguous(), dk.contiguous(), dv.contiguous(), qkv, qw, kw, pos, inv_freq, rstd, nq, nkv)
-        return dqkv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None, None, None
+        return dqkv, _to_main_grad(qw, dqw), _to_main_grad(kw, dkw), None, None, None, None, None
 
 
 def qk_norm_rope(qkv, q_norm_w, k_norm_w, pos, inv_freq, nq: int, nkv: int, eps: float = 1e-6):  # noqa: ANN001, ANN201

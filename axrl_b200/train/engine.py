@@ -45,6 +45,7 @@ class ParallelCtx:
     pp_size: int = 1
     cp_group: object | None = None
     cp_size: int = 1
+    zero_backend: str = "p2p"  # distributed optimizer over DP: "p2p" (NVLink) | "nccl" | "off" (replicated)
 
 
 class TrainEngine:
@@ -77,7 +78,17 @@ class TrainEngine:
             model.inv_freq = model.inv_freq.float()
         self.model = model
         self.model.recompute = cfg.recompute_granularity == "full"
-        self.optim = None if cfg.inference_only else FlatAdamW(self.model, cfg.optimizer, cfg.lr_scheduler)
+        self.optim = None
+        if not cfg.inference_only:
+            dp_dist = (cfg.optimizer.use_distributed_optimizer and self.par.dp_group is not None and self.par.dp_size > 1
+                       and not self.ep.enabled and not self.tp.enabled and not self.cp.enabled and self.par.zero_backend != "off")
+            if dp_dist:
+                from axrl_b200.parallel.zero import BucketedZeroAdamW
+
+                backend = self.par.zero_backend if self.device.type == "cuda" else "nccl"
+                self.optim = BucketedZeroAdamW(self.model, cfg.optimizer, cfg.lr_scheduler, group=self.par.dp_group, backend=backend)
+            else:
+                self.optim = FlatAdamW(self.model, cfg.optimizer, cfg.lr_scheduler)
         self.max_tokens = cfg.max_tokens_per_micro_batch
         self.last_timing: dict[str, float] = {}
         self.release_grads_after_step = False
@@ -203,13 +214,17 @@ class TrainEngine:
                        "entropy": dmb.unpack(ent, S) if ent is not None else torch.zeros((len(mb.rows), S), device=self.device)}
             want = metrics_every_micro_batch or i == len(mbs) - 1
             loss, denom, m = trainer.loss_func(outputs, sub, with_metrics=want)
+            if i == len(mbs) - 1 and hasattr(self.optim, "arm"):
+                self.optim.arm()  # gradients become final during this backward: reduce buckets as they complete
             (loss * denom.to(loss.dtype)).backward()
             if want:
                 metrics_acc.append(m)
         self.optim.fold_param_grads()
         if self.cp.enabled:  # each CP rank back-propagated its own tokens: sum
             dist.all_reduce(self.optim.grad, group=self.cp.group)
-        if self.par.dp_group is not None and self.par.dp_size > 1:
+        if hasattr(self.optim, "finish_grad_sync"):  # distributed optimizer: reduce-scatter already (mostly) done
+            self.optim.finish_grad_sync()
+        elif self.par.dp_group is not None and self.par.dp_size > 1:
             if self.ep.enabled:  # expert weights differ per EP rank: reduce only the dense gradients
                 from axrl_b200.parallel.expert import dense_grad_allreduce
 

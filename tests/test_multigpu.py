@@ -43,3 +43,8 @@ def test_tp_p2p_wait_times_out_without_hanging():
 def test_expert_parallel_two_gpus():
     out = _run("ep")
     assert out.count("ep torch ok") == 2 and out.count("ep p2p ok") == 2, out[-2000:]
+
+
+def test_bucketed_zero_two_gpus():
+    out = _run("zero")
+    assert out.count("zero nccl ok") == 2 and out.count("zero p2p ok") == 2, out[-2000:]
