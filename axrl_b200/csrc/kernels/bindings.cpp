@@ -49,6 +49,8 @@ at::Tensor grouped_linear_fwd(at::Tensor x, at::Tensor w, at::Tensor offsets);
 at::Tensor grouped_linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor offsets);
 void grouped_linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor offsets, at::Tensor acc);
 void ep_plan(at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
+std::vector<at::Tensor> grpo_pg_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, double, double, double);
+at::Tensor grpo_pg_bwd(at::Tensor, at::Tensor);
 void ep_transfer(int64_t, at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
                  at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, int64_t);
 void tp_reduce_slots(at::Tensor, int64_t, int64_t, c10::optional<at::Tensor>, at::Tensor);
@@ -79,6 +81,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_linear_dgrad", &ax::grouped_linear_dgrad);
   m.def("grouped_linear_wgrad_acc", &ax::grouped_linear_wgrad_acc);
   m.def("ep_plan", &ax::ep_plan);
+  m.def("grpo_pg_fwd", &ax::grpo_pg_fwd);
+  m.def("grpo_pg_bwd", &ax::grpo_pg_bwd);
   m.def("ep_transfer", &ax::ep_transfer);
   m.def("tp_reduce_slots", &ax::tp_reduce_slots);
   m.def("linear_dgrad", &ax::linear_dgrad);

@@ -91,6 +91,14 @@ class GrpoTrainer(BaseTrainer):
     # ------------------------------------------------------------------ policy losses
     def grpo_loss(self, *, loss_mask, advantages, logprobs, base_logprobs, token_mismatch_tir):  # noqa: ANN001
         c = self.config
+        if logprobs.is_cuda:  # fused kernel: ratio, clips, IS weight and gradient in one pass
+            from axrl_b200.ops.grpo_loss import grpo_policy_loss
+
+            if c.dual_clip_neg_adv_factor is not None:
+                assert c.dual_clip_neg_adv_factor > 1.0
+            pgw, ratio, eff = grpo_policy_loss(logprobs, base_logprobs, advantages, token_mismatch_tir, c.clip_ratio_low,
+                                               c.clip_ratio_high, c.dual_clip_neg_adv_factor)
+            return aggregate_with_mask(pgw, loss_mask, c.loss_agg_type), ratio, eff
         ratio = _ratio(logprobs, base_logprobs)
         clipped = torch.clamp(ratio, 1 - c.clip_ratio_low, 1 + c.clip_ratio_high)
         ppo = torch.maximum(-advantages * ratio, -advantages * clipped)

@@ -290,3 +290,32 @@ def test_grouped_linear_fwd_bwd_matches_per_expert_fp32():
         exp = 1.0 + dyf[r0:r1].t() @ xf[r0:r1]
         torch.testing.assert_close(w.main_grad[e], exp, atol=5e-2, rtol=2e-2)
     assert w.grad is None
+
+
+@pytest.mark.parametrize("dual", [None, 3.0])
+def test_fused_grpo_policy_loss_matches_torch(dual):
+    """Fused per-token GRPO/PPO objective (ratio, clip, dual clip, IS weight, gradient) against the
+    PyTorch oracle of GrpoTrainer.grpo_loss, values and d loss / d logprobs."""
+    from axrl_b200.configs import GrpoTrainerConfig
+    from axrl_b200.trainer.grpo_trainer import GrpoTrainer
+
+    torch.manual_seed(1)
+    B, S = 6, 300
+    lp = (-torch.rand(B, S) * 3).double()
+    base = lp + torch.randn(B, S) * 0.3
+    base[0, :5] = lp[0, :5] + 30  # log-ratio clamp region
+    adv = torch.randn(B, S)
+    adv[1] = 0.0
+    w = torch.rand(B, S) * 2
+    mask = torch.rand(B, S) > 0.2
+    t = GrpoTrainer(GrpoTrainerConfig(loss_type="grpo", clip_ratio_low=0.2, clip_ratio_high=0.28, dual_clip_neg_adv_factor=dual,
+                                      loss_agg_type="token-mean"))
+    outs = {}
+    for dev in ("cpu", "cuda"):
+        x = lp.float().to(dev).requires_grad_(True)
+        loss, ratio, eff = t.grpo_loss(loss_mask=mask.to(dev), advantages=adv.to(dev), logprobs=x, base_logprobs=base.float().to(dev),
+                                       token_mismatch_tir=w.to(dev))
+        loss.backward()
+        outs[dev] = (loss.detach().cpu(), x.grad.cpu(), ratio.detach().cpu(), eff.detach().cpu())
+    for a, b in zip(outs["cpu"], outs["cuda"]):
+        torch.testing.assert_close(b, a, atol=1e-5, rtol=1e-4)
