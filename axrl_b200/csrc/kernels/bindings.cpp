@@ -51,6 +51,8 @@ void grouped_linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor offsets, a
 void ep_plan(at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
 std::vector<at::Tensor> grpo_pg_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, double, double, double);
 at::Tensor grpo_pg_bwd(at::Tensor, at::Tensor);
+std::vector<at::Tensor> quant_fp8_rows(at::Tensor x);
+at::Tensor fp8_block_linear(at::Tensor xq, at::Tensor xs, at::Tensor wq, at::Tensor ws);
 void ep_transfer(int64_t, at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
                  at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, int64_t);
 void tp_reduce_slots(at::Tensor, int64_t, int64_t, c10::optional<at::Tensor>, at::Tensor);
@@ -83,6 +85,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_plan", &ax::ep_plan);
   m.def("grpo_pg_fwd", &ax::grpo_pg_fwd);
   m.def("grpo_pg_bwd", &ax::grpo_pg_bwd);
+  m.def("quant_fp8_rows", &ax::quant_fp8_rows);
+  m.def("fp8_block_linear", &ax::fp8_block_linear);
   m.def("ep_transfer", &ax::ep_transfer);
   m.def("tp_reduce_slots", &ax::tp_reduce_slots);
   m.def("linear_dgrad", &ax::linear_dgrad);

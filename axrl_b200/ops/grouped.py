@@ -57,7 +57,9 @@ def grouped_linear(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor) -> t
 
 def expert_offsets(expert_ids: torch.Tensor, num_experts: int) -> torch.Tensor:
     """(E+1,) int32 row offsets of each expert in the expert-sorted order (device, no sync)."""
-    counts = torch.bincount(expert_ids, minlength=num_experts)
+    # scatter_add instead of bincount: fixed output size, so no host sync (CUDA-graph capturable)
+    counts = torch.zeros(num_experts, dtype=torch.int64, device=expert_ids.device)
+    counts.scatter_add_(0, expert_ids.long(), torch.ones_like(expert_ids, dtype=torch.int64))
     return torch.cat([counts.new_zeros(1), counts.cumsum(0)]).to(torch.int32)
 
 

@@ -101,7 +101,8 @@ class P2PEPComm:
     # -------------------------------------------------------------- steps
     def plan(self, exp_sorted: torch.Tensor) -> _Plan:
         e = _ext.ext()
-        counts = torch.bincount(exp_sorted, minlength=self.E).to(torch.int32)
+        counts = torch.zeros(self.E, dtype=torch.int32, device=exp_sorted.device)  # no host sync (unlike bincount)
+        counts.scatter_add_(0, exp_sorted.long(), torch.ones_like(exp_sorted, dtype=torch.int32))
         ep = self._next()
         e.tp_push(counts, self.E * 4, 0, self.cnt_ptrs, self.rank * self.E * 4, self.flag_ptrs, self.flags, CH_CNT, ep, self.rank,
                   (1 << self.size) - 1, self.ticket, self.timeout_ns, self.status, 1)

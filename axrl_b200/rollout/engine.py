@@ -87,8 +87,11 @@ def _stream_id(rid: str) -> int:
 class RolloutEngine:
     def __init__(self, model: Qwen3Model, *, max_batch: int = 256, kv_tokens: int = 1 << 16, page_size: int = 64,
                  max_context: int = 16384, max_prefill_tokens: int = 16384, use_cuda_graph: bool = True, seed: int = 0,
-                 eos_token_id: int | None = None, burst: int = 16, kv_memory_saver: bool = False) -> None:
+                 eos_token_id: int | None = None, burst: int = 16, kv_memory_saver: bool = False, weight_format: str = "bf16") -> None:
         self.model = model
+        assert weight_format in ("bf16", "fp8_block")
+        self.weight_format = weight_format
+        self.fp8: dict[int, object] = {}
         cfg = model.cfg
         self.cfg = cfg
         p0 = next(model.parameters())
@@ -125,6 +128,32 @@ class RolloutEngine:
         self.running: list[_Seq] = []
         self.stats = {"prefill_tokens": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_s": 0.0, "decode_s": 0.0, "bursts": 0}
         self._alloc_static()
+        if weight_format == "fp8_block":
+            self.quantize_weights()
+
+    # ------------------------------------------------------------------ fp8 serving
+    def _dense_linear_weights(self) -> list[tuple[str, torch.Tensor]]:
+        out = []
+        for name, p in self.model.named_parameters():
+            if name.endswith(("qkv_proj", "o_proj", "gate_up_proj", "down_proj")) and p.dim() == 2:
+                out.append((name, p))
+        return out
+
+    @torch.no_grad()
+    def quantize_weights(self) -> None:
+        """Block-quantise every dense projection (128x128 e4m3 blocks + fp32 scales); embedding,
+        norms and the LM head stay bf16."""
+        from axrl_b200.ops.fp8 import Fp8Weight
+
+        self.fp8 = {id(p): Fp8Weight.from_dense(p.detach()) for _, p in self._dense_linear_weights()}
+
+    def set_fp8_weights(self, weights: dict[str, tuple[torch.Tensor, torch.Tensor]]) -> None:
+        """Use externally produced block-fp8 weights (e.g. buffers written by the weight-sync push)."""
+        from axrl_b200.ops.fp8 import Fp8Weight
+
+        params = dict(self.model.named_parameters())
+        for name, (q, s) in weights.items():
+            self.fp8[id(params[name])] = Fp8Weight(q, s)
 
     # ------------------------------------------------------------------ static buffers
     def _alloc_static(self) -> None:
@@ -148,6 +177,12 @@ class RolloutEngine:
 
     # ------------------------------------------------------------------ model pieces (inference, no autograd)
     def _lin(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        fw = self.fp8.get(id(w)) if self.fp8 else None
+        if fw is not None:
+            from axrl_b200.ops.fp8 import fp8_linear
+
+            y = fp8_linear(x, fw)
+            return y if residual is None else y + residual
         if self.is_cuda:
             e = _ext.ext()
             return e.linear_fwd(x, w) if residual is None else e.linear_residual(x, w, residual)
@@ -583,6 +618,8 @@ class RolloutEngine:
         for (n1, p1), (n2, p2) in zip(self.model.named_parameters(), src.named_parameters()):
             assert n1 == n2 and p1.shape == p2.shape, f"layout mismatch {n1} vs {n2}"
             p1.copy_(p2, non_blocking=True)
+        if self.weight_format == "fp8_block":
+            self.quantize_weights()
 
     def reset_prefix_cache(self) -> None:
         """Weights changed: cached pages no longer match (the reference flushes its radix cache)."""

@@ -319,3 +319,42 @@ def test_fused_grpo_policy_loss_matches_torch(dual):
         outs[dev] = (loss.detach().cpu(), x.grad.cpu(), ratio.detach().cpu(), eff.detach().cpu())
     for a, b in zip(outs["cpu"], outs["cuda"]):
         torch.testing.assert_close(b, a, atol=1e-5, rtol=1e-4)
+
+
+def test_fp8_block_linear_matches_dequantized_fp32():
+    """Block-scaled e4m3 GEMM (1x128 activation scales, 128x128 weight scales) against the fp32
+    product of the dequantised operands, and the activation quantiser against its torch oracle."""
+    from axrl_b200.ops import _ext
+    from axrl_b200.ops.fp8 import Fp8Weight, dequantize_weight_blocks, fp8_linear, quantize_rows_ref
+
+    torch.manual_seed(0)
+    for M, N, K in [(8, 256, 512), (200, 384, 1024), (1000, 1024, 256)]:
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+        fw = Fp8Weight.from_dense(w)
+        xq, xs = _ext.ext().quant_fp8_rows(x)
+        rq, rs = quantize_rows_ref(x)
+        torch.testing.assert_close(xs, rs, atol=0, rtol=1e-6)
+        assert (xq.float() - rq.float()).abs().max().item() <= 0.0 + 1e-6
+        y = fp8_linear(x, fw).float()
+        ref = (xq.float() * xs.repeat_interleave(128, 1)) @ dequantize_weight_blocks(fw.q, fw.s).t()
+        torch.testing.assert_close(y, ref, atol=2e-2, rtol=2e-2)
+        dense = x.float() @ w.float().t()  # quantisation error stays small
+        assert ((y - dense).norm() / dense.norm()).item() < 0.08
+
+
+def test_rollout_engine_fp8_weights_run():
+    from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from axrl_b200.rollout.engine import GenRequest, RolloutEngine
+
+    cfg = Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=128)
+    m = Qwen3Model(cfg)
+    m.init_weights(0)
+    m = m.to("cuda", torch.bfloat16)
+    m.inv_freq = m.inv_freq.float()
+    eng = RolloutEngine(m, max_batch=4, kv_tokens=2048, max_context=256, seed=0, weight_format="fp8_block")
+    assert len(eng.fp8) == 4 * cfg.num_hidden_layers // 2 * 2
+    res = eng.generate([GenRequest(rid=f"r{i}", prompt=list(range(5, 40)), max_new_tokens=20, seed_stream=i) for i in range(3)])
+    assert all(len(r.output_ids) == 20 and all(lp <= 0 for lp in r.output_logprobs) for r in res)
+    eng.release_graphs()
