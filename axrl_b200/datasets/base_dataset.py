@@ -93,6 +93,7 @@ class SyntheticTokenDataset(BaseDataset):
 
     def __init__(self, num: int = 256, prompt_len: int = 512, vocab_size: int = 151936, seed: int = 0, **kw) -> None:  # noqa: ANN003
         super().__init__(seed=seed, **kw)
+        self.prompt_len, self.vocab_size = prompt_len, vocab_size
         rng = np.random.default_rng(seed)
         for i in range(num):
             c = Conversation(messages=[Message("user", "")], conversation_id=f"syn-{i}")

@@ -22,6 +22,7 @@ import logging
 import time
 from collections import defaultdict
 from pathlib import Path
+from pathlib import Path as _Path
 from typing import Any
 
 import numpy as np
@@ -103,8 +104,14 @@ class PipelineController:
             if mode == "online_rl_train":
                 return await self.run_online_rl_train()
             if mode == "eval_only":
-                return await self.run_evals()
-            raise NotImplementedError(f"run mode {mode} is driven by axrl_b200.pipeline.modes")
+                return {"results": await self.run_eval_only()}
+            if mode == "sft_train":
+                return {"curve": await self.run_sft_train()}
+            if mode == "replay_rl_train":
+                return await self.run_replay_rl_train()
+            if mode == "mismatch_test":
+                return await self.run_mismatch_test()
+            raise ValueError(f"unknown run mode {mode}")
         finally:
             await self.shutdown()
 
@@ -245,5 +252,197 @@ class PipelineController:
             logger.info("step %d %s", self.global_step, json.dumps({k: round(v, 4) for k, v in m.items() if isinstance(v, float)}))
         return {"history": history}
 
-    async def run_evals(self) -> dict:
-        return {}
+    # ------------------------------------------------------------------ other run modes
+    def get_test_datasets(self) -> list[tuple[str, Any]]:
+        """(name, dataset) pairs: the controller's ``test_datasets`` or the recipe's."""
+        ds = getattr(self, "test_datasets", None)
+        if ds is None and hasattr(self.recipe, "get_test_datasets"):
+            ds = self.recipe.get_test_datasets()
+        return list(ds or [])
+
+    async def collect_results(self, n: int) -> list:
+        out = []
+        while len(out) < n:
+            r = await self.result_queue.get(timeout=RESULT_TIMEOUT_S)
+            if r is None:
+                for a in self.actors:
+                    a.check_health()
+                continue
+            await self.result_queue.complete()
+            out.append(r)
+        return out
+
+    async def run_eval_rollouts(self) -> list:
+        """Roll out every test conversation once (``smoke_eval_rollouts`` caps the total); metrics per
+        dataset under ``eval_<name>/``; rollouts saved when ``save_eval_rollouts``."""
+        from axrl_b200.utils.zst_utils import save_zst
+
+        all_results = []
+        budget = self.config.controller.smoke_eval_rollouts
+        for name, ds in self.get_test_datasets():
+            if budget is not None and budget <= 0:
+                break
+            convs = [c.deep_copy() for c in ds.conversations]
+            if budget is not None:
+                convs = convs[:budget]
+                budget -= len(convs)
+            for i, c in enumerate(convs):
+                c.extra["group_id"] = f"eval:{name}:{c.conversation_id}@{self.global_step}"
+                c.extra["group_index"] = i
+            t0 = time.time()
+            await self.rollout_queue.put_many(convs)
+            results = await self.collect_results(len(convs))
+            dt = time.time() - t0
+            m = aggregate_response_metrics([r.metric for r in results], f"eval_{name}", dt)
+            m[f"eval_{name}/eval_time_sec"] = dt
+            self.metrics_log.append(m)
+            if self.config.controller.save_eval_rollouts:
+                save_zst(results, self.output_dir / f"eval_rollouts-{name}-step{self.global_step}.zst")
+            all_results.extend(results)
+        return all_results
+
+    async def run_evals(self) -> list:
+        if not self.get_test_datasets():
+            logger.info("no test datasets configured; skipping evaluation")
+            return []
+        return await self.run_eval_rollouts()
+
+    async def run_eval_only(self) -> list:
+        results = await self.run_eval_rollouts()
+        assert results, "eval_only needs at least one test dataset with conversations"
+        return results
+
+    def build_sft_samples(self, dataset: Any) -> SampleBatch:
+        samples = self.recipe.build_sft_samples(dataset)
+        batch = SampleBatch.from_samples(samples)
+        batch["trajectory_id"] = torch.arange(len(batch), dtype=torch.long)
+        return batch
+
+    async def run_sft_train(self) -> list[dict]:
+        """Supervised fine-tuning over the recipe's SFT samples for ``megatron_worker.num_epochs``
+        epochs; the eval loss is the token-mean NLL of the test datasets."""
+        from axrl_b200.configs import SftTrainerConfig
+        from axrl_b200.data.global_batch_iterator import build_global_batches_for_dp_rank
+        from axrl_b200.trainer.sft_trainer import SftTrainer
+
+        c = self.config
+        train = self.build_sft_samples(self.train_dataset)
+        evals = [self.build_sft_samples(ds) for _, ds in self.get_test_datasets()]
+        trainer = SftTrainer(getattr(c, "sft", None) or SftTrainerConfig())
+        curve = []
+        for epoch in range(c.megatron_worker.num_epochs):
+            t0 = time.time()
+            g = torch.Generator().manual_seed(self.global_step)
+            order = torch.randperm(len(train), generator=g).tolist()
+            shuffled = train.select_rows(order)
+            last = {}
+            for b in build_global_batches_for_dp_rank(shuffled, global_batch_size=c.megatron_worker.global_batch_size, dp_size=1,
+                                                      dp_rank=0, padding_sample_length=c.megatron_worker.padding_sample_length):
+                last = self.train.train_step(b, trainer)
+                self.global_step += 1
+            row = {"global_step": float(self.global_step), "epoch": float(epoch), "train_loss": float(last.get("loss", float("nan"))),
+                   "train_grad_norm": float(last.get("grad_norm", float("nan"))), "timing/train_seconds": time.time() - t0}
+            if evals:
+                tot, cnt = 0.0, 0.0
+                for eb in evals:
+                    lp = self.train.compute_logprobs(eb)
+                    m = eb["loss_mask"].bool()
+                    tot += float(-lp[m].sum())
+                    cnt += float(m.sum())
+                row["eval_loss"] = tot / max(cnt, 1.0)
+            curve.append(row)
+            self.metrics_log.append(row)
+        return curve
+
+    def select_replay_groups(self, groups: list[list]) -> list[list]:
+        """Re-normalise each loaded group and drop zero-std groups (as the online loop does)."""
+        keep = []
+        for g in groups:
+            self.normalize_group_rewards(g)
+            if self.config.online_rl_train.filter_zero_std and np.std([r.metric.score for r in g]) < 1e-8:
+                continue
+            keep.append(g)
+        return keep
+
+    async def run_replay_rl_train(self) -> dict:
+        """Train on recorded data: a saved sample set, or saved rollout groups re-packed here."""
+        from pathlib import Path as _P
+
+        from axrl_b200.utils.zst_utils import load_zst
+
+        rc = self.config.replay_rl_train
+        assert (rc.sample_dict_path is None) != (rc.rollout_groups_path is None), \
+            "replay_rl_train requires exactly one of sample_dict_path or rollout_groups_path"
+        if rc.sample_dict_path is not None:
+            batch = load_zst(_P(rc.sample_dict_path))
+        else:
+            groups = self.select_replay_groups(load_zst(_P(rc.rollout_groups_path)))
+            batch = self.pack_groups(groups)
+        if not self.config.controller.allow_prefix_merging and "merge_info" in batch.objects:
+            batch.objects.pop("merge_info")
+        t0 = time.time()
+        metrics = self.train_on(batch)
+        out = {"train_metrics": metrics, "timing/train_seconds": time.time() - t0}
+        self.metrics_log.append({k: v for k, v in out.items() if isinstance(v, float)})
+        return out
+
+    async def run_mismatch_test(self) -> dict:
+        """Roll out one global batch (zero-std filter off, or load saved rollouts), recompute the
+        trainer's log-probs of every sampled token, save the samples and report the rollout-vs-trainer
+        mismatch (optionally against a baseline run)."""
+        from datetime import datetime, timezone
+
+        from axrl_b200.metrics.report_mismatch import MCoreRunMetrics, MismatchReportTask, MismatchRunResult, report_mismatch
+        from axrl_b200.utils.zst_utils import load_zst, save_zst
+
+        mc = self.config.mismatch_test
+        name = mc.name
+        for d in (mc.get_output_dir(), mc.get_result_dir(), mc.get_log_dir(), mc.get_fig_dir()):
+            d.mkdir(parents=True, exist_ok=True)
+        stem = mc._sanitize_name(name)
+        result_path = mc.get_result_dir() / f"result-{stem}.zst"
+        save_zst(MismatchRunResult(success=False, grpo_config=self.config.grpo.model_copy()), result_path)
+        rollout_path = mc.get_result_dir() / "data" / f"valid_rollouts-{stem}.zst"
+        samples_path = mc.get_result_dir() / "data" / f"samples-{stem}.zst"
+        t0 = time.time()
+        if rollout_path.exists() and not mc.override_rollouts_if_exists:
+            groups = load_zst(rollout_path)
+        else:
+            keep = self.config.online_rl_train.filter_zero_std
+            self.config.online_rl_train.filter_zero_std = False
+            try:
+                n = self.groups_per_sync()
+                await self.schedule_groups(self.train_dataset.sample(n, self.config.online_rl_train.sample_type))
+                groups, _ = await self.stream_groups(n)
+            finally:
+                self.config.online_rl_train.filter_zero_std = keep
+            save_zst(groups, rollout_path)
+        t_roll = time.time() - t0
+        metrics_r = [r.metric for g in groups for r in g]
+        resp = aggregate_response_metrics(metrics_r, "Mismatch-Rollout", None)
+        tokens = sum(m.response_length for m in metrics_r)
+        self.worker.pause_generation()
+        batch = self.pack_groups(groups)
+        t1 = time.time()
+        batch["old_logprobs"] = self.train.compute_logprobs(batch, self.config.train_sampling_config.temperature)
+        batch["ref_logprobs"] = batch["old_logprobs"].clone()  # no update happened: the reference policy is the current one
+        t_mcore = time.time() - t1
+        save_zst(batch, samples_path)
+        base = None
+        if mc.baseline_samples_path is not None:
+            base = mc.baseline_samples_path
+        elif mc.baseline_name is not None:
+            base = str(mc.get_result_dir() / "data" / f"samples-{mc._sanitize_name(mc.baseline_name)}.zst")
+        if base is not None and not _Path(base).exists():
+            raise FileNotFoundError(f"baseline sample set not found at {base}")
+        ts = datetime.now(tz=timezone.utc).strftime("%Y%m%d-%H%M%S")
+        mm = report_mismatch(MismatchReportTask(exp_name=name, exp_sample_data_path=str(samples_path), baseline_sample_data_path=base,
+                                                baseline_name=mc.baseline_name or "baseline",
+                                                output_fig_path=str(mc.get_fig_dir() / f"mismatch_report-{stem}-{ts}.svg"),
+                                                output_txt_path=str(mc.get_log_dir() / f"top_mismatch-{stem}-{ts}.log")))
+        result = MismatchRunResult(success=True, grpo_config=self.config.grpo.model_copy(),
+                                   metadata={"pipeline_config": self.config.model_dump(mode="json")}, response_metrics=resp,
+                                   rollout_throughput=tokens / t_roll if t_roll > 0 else None,
+                                   mcore=MCoreRunMetrics(end_to_end_time_sec=t_mcore), mismatch_metrics=mm)
+        save_zst(result, result_path)
+        return {"result_path": str(result_path), "mismatch": mm}

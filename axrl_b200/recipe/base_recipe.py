@@ -39,6 +39,14 @@ class BaseRecipe:
     def get_test_dataset_configs(self) -> Sequence[Any] | None:
         return None
 
+    def get_test_datasets(self) -> list[tuple[str, Any]]:
+        """(name, dataset) pairs evaluated by ``eval_only`` and the periodic evals."""
+        return []
+
+    def build_sft_samples(self, dataset: Any) -> list:
+        """SFT samples (prompt + target tokens, loss on the target) of ``dataset`` for ``sft_train``."""
+        raise NotImplementedError(f"{self.__class__.__name__} does not provide SFT samples")
+
     async def run_rollout(self, conversation: Any, runtime: Any) -> Any:
         raise NotImplementedError(f"{self.__class__.__name__}.run_rollout() must be implemented")
 

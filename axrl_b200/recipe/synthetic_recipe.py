@@ -34,3 +34,18 @@ class SyntheticTokenRecipe(BaseRecipe):
         metric = ResponseMetric(score=score, response_length=len(out.output_ids), prompt_length=len(ids), finish_reason=out.finish_reason,
                                 repetition_ratio=ResponseMetric.repetition(out.output_ids.tolist()))
         return RolloutResult(conversation=conversation, trace=trace, metric=metric)
+
+    def get_test_datasets(self) -> list[tuple[str, SyntheticTokenDataset]]:
+        if not hasattr(self, "_test"):
+            self._test = SyntheticTokenDataset(num=4, prompt_len=self.dataset.prompt_len, vocab_size=self.dataset.vocab_size, seed=99)
+        return [("synthetic_test", self._test)]
+
+    def build_sft_samples(self, dataset) -> list:  # noqa: ANN001
+        """Target: the reward token repeated, then the prompt's first tokens (a learnable mapping)."""
+        from axrl_b200.data.sample import Sample
+
+        out = []
+        for c in dataset.conversations:
+            p = [int(t) for t in c.gen_state.input_ids]
+            out.append(Sample.from_tokens(p, [self.reward_token] * 4 + p[:4]))
+        return out

@@ -60,3 +60,59 @@ def test_online_rl_loop_tiny_cpu():
     assert len(hist) == 2 and ctl.global_step == 2
     assert all(h["Valid-Rollouts/num"] == 8 for h in hist)
     assert all(torch.isfinite(torch.tensor(h["train/grad_norm"])) for h in hist)
+
+
+def _ctl(tmp_path, mode):
+    from axrl_b200.models.qwen3 import resolve_preset
+    from axrl_b200.pipeline.config import PipelineExperimentConfig
+    from axrl_b200.pipeline.controller import PipelineController
+    from axrl_b200.recipe.synthetic_recipe import SyntheticTokenRecipe
+
+    torch.manual_seed(0)
+    c = PipelineExperimentConfig()
+    c.controller.run_mode = mode
+    c.megatron_worker.global_batch_size = 8
+    c.megatron_worker.model.seq_length = 256
+    c.megatron_worker.num_epochs = 3
+    c.online_rl_train.num_rollouts_per_conversation = 4
+    c.online_rl_train.model_sync_every_n_global_updates = 1
+    c.online_rl_train.batch_rollout_for_n_global_updates = 1
+    c.train_sampling_config.max_new_tokens = 16
+    c.train_sampling_config.max_total_tokens = 64
+    c.rollout_worker.max_running_requests = 16
+    c.controller.max_running_requests = 16
+    c.mismatch_test.output_dir = str(tmp_path / "mm")
+    recipe = SyntheticTokenRecipe(c, num_prompts=8, prompt_len=16)
+    ctl = PipelineController(c, recipe, device="cpu", model_cfg=resolve_preset("tiny"))
+    ctl.output_dir = tmp_path / "out"
+    ctl.train_dataset = recipe.dataset
+    return ctl
+
+
+def test_eval_only_and_sft_modes(tmp_path):
+    ctl = _ctl(tmp_path, "eval_only")
+    out = asyncio.run(ctl.start())
+    assert len(out["results"]) == 4 and any("eval_synthetic_test/num" in m for m in ctl.metrics_log)
+    assert list((tmp_path / "out").glob("eval_rollouts-*.zst"))
+    ctl = _ctl(tmp_path, "sft_train")
+    curve = asyncio.run(ctl.start())["curve"]
+    assert len(curve) == 3 and curve[-1]["train_loss"] < curve[0]["train_loss"] and "eval_loss" in curve[0]
+
+
+def test_mismatch_then_replay(tmp_path):
+    from axrl_b200.utils.zst_utils import load_zst
+
+    ctl = _ctl(tmp_path, "mismatch_test")
+    out = asyncio.run(ctl.start())
+    mm = out["mismatch"]
+    # same fp32 weights, same math: the rollout engine and the trainer agree closely
+    assert mm["mismatch/cur-exp/num_tokens"] > 0 and mm["mismatch/cur-exp/abs_diff_mean"] < 1e-3
+    res = load_zst(out["result_path"])
+    assert res.success and res.mismatch_metrics == mm
+    rollouts = list((tmp_path / "mm" / "results" / "data").glob("valid_rollouts-*.zst"))
+    assert rollouts and list((tmp_path / "mm" / "results" / "figs").glob("*.svg"))
+    ctl = _ctl(tmp_path, "replay_rl_train")
+    ctl.config.replay_rl_train.rollout_groups_path = str(rollouts[0])
+    ctl.config.online_rl_train.filter_zero_std = False
+    out = asyncio.run(ctl.start())
+    assert out["train_metrics"] and all(torch.isfinite(torch.tensor(m["grad_norm"])) for m in out["train_metrics"])
