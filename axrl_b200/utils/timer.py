@@ -35,10 +35,29 @@ class Timer:
 
 
 class SessionTimer(Timer):
-    """Timer whose log lines embed ``{session_id, execution_kind, function_name}`` as JSON (for timelines)."""
+    """Timer whose log lines embed ``{session_id, execution_kind, function_name}`` as JSON (for timelines).
+
+    When ``AXRL_SESSION_TIMELINE`` names a file, every finished span is also appended to it as one
+    JSON line ``{session_id, execution_kind, function_name, start, end}`` (wall-clock seconds) —
+    the input of :mod:`axrl_b200.utils.visualize_session_timer`."""
 
     def __init__(self, session_id: str, execution_kind: str, function_name: str) -> None:
-        super().__init__(json.dumps({"session_id": session_id, "execution_kind": execution_kind, "function_name": function_name}))
+        self.tag = {"session_id": session_id, "execution_kind": execution_kind, "function_name": function_name}
+        super().__init__(json.dumps(self.tag))
+
+    def __enter__(self) -> "SessionTimer":
+        self.wall0 = time.time()
+        super().__enter__()
+        return self
+
+    def __exit__(self, *exc) -> None:  # noqa: ANN002
+        super().__exit__(*exc)
+        import os
+
+        path = os.environ.get("AXRL_SESSION_TIMELINE")
+        if path:
+            with open(path, "a") as f:
+                f.write(json.dumps({**self.tag, "start": self.wall0, "end": self.wall0 + self.elapsed_seconds}) + "\n")
 
 
 class CudaTimer:
