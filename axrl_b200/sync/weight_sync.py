@@ -55,6 +55,17 @@ class WeightSyncer:
             self.tiles_copy = torch.from_numpy(c).to(self.device)
             self.tiles_q8 = torch.from_numpy(q).to(self.device)
         self.bytes_pushed = 0 if self.src_rank is None else int(self._pushed_bytes())
+        # NCCL baseline: every trainer shard is broadcast to all ranks, then each destination rank
+        # reshards locally with the same tile kernel (its own tiles only)
+        self.src_ranks = list(src_ranks)
+        self._nccl_tiles: list[tuple[torch.Tensor, torch.Tensor]] = []
+        my_groups = [g for g in dst_groups if self.rank in g]
+        for i in range(len(src_ranks)):
+            tl = [build_tiles(specs, src_tp, dst_tp, self.src_layout, self.dst_layout, i, g, fp8) for g in my_groups]
+            allt = np.concatenate(tl, 0) if tl else np.zeros((0, 10), np.int64)
+            allt = allt[allt[:, 2] == self.rank]
+            c, q = split_modes(allt)
+            self._nccl_tiles.append((torch.from_numpy(c).to(self.device), torch.from_numpy(q).to(self.device)))
 
     def _pushed_bytes(self) -> int:
         n = 0
@@ -80,6 +91,30 @@ class WeightSyncer:
         r, c = lay.shapes[name]
         n = -(-r // TILE) * -(-c // TILE)
         return self.buf[lay.scale_offsets[name]: lay.scale_offsets[name] + 4 * n].view(torch.float32).view(-(-r // TILE), -(-c // TILE))
+
+    def push_nccl(self) -> float:
+        """Baseline: NCCL broadcast of every trainer shard + local reshard/quantise on each
+        destination; returns device seconds (this rank)."""
+        e = _ext.ext()
+        s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = -(-self.src_layout.nbytes // 16) * 16
+        recv = torch.empty(n, dtype=torch.uint8, device=self.device)
+        local = torch.full((len(self.handle.buffer_ptrs),), self.buf.data_ptr(), dtype=torch.int64, device=self.device)
+        dist.barrier(group=self.group)
+        s.record()
+        for i, r in enumerate(self.src_ranks):
+            shard = self.buf[:n] if self.rank == r else recv
+            dist.broadcast(shard, src=r, group=self.group)
+            copy_t, q_t = self._nccl_tiles[i]
+            src = shard.view(torch.bfloat16)
+            if copy_t.numel():
+                e.sync_push(copy_t, src, local, 0)
+            if q_t.numel():
+                e.sync_push(q_t, src, local, 1)
+        t.record()
+        t.synchronize()
+        dist.barrier(group=self.group)
+        return s.elapsed_time(t) / 1000.0
 
     def push(self) -> float:
         """One full reshard + (quantise) + push; returns device seconds (this rank)."""

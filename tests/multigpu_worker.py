@@ -95,6 +95,15 @@ def case_weight_sync() -> None:
             else:
                 assert torch.equal(got.float(), exp), spec.name
         print(f"rank {rank}: weight_sync fp8={fp8} ok ({ws.bytes_pushed / 1e6:.1f} MB pushed in {secs * 1e3:.3f} ms)", flush=True)
+        # the NCCL-broadcast baseline produces the same destination contents
+        snap = {spec.name: ws.param_view(spec.name, "dst").clone() for spec in specs}
+        for spec in specs:
+            ws.param_view(spec.name, "dst").zero_()
+        ws.push_nccl()
+        torch.cuda.synchronize()
+        for spec in specs:
+            assert torch.equal(ws.param_view(spec.name, "dst").view(torch.uint8), snap[spec.name].view(torch.uint8)), spec.name
+        print(f"rank {rank}: weight_sync nccl baseline fp8={fp8} ok", flush=True)
 
 
 def case_tp() -> None:

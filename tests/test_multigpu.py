@@ -28,7 +28,8 @@ def test_dist_optim_two_gpus():
 
 
 def test_weight_sync_two_gpus():
-    assert _run("weight_sync").count("ok") == 4
+    out = _run("weight_sync")
+    assert out.count("weight_sync fp8") == 4 and out.count("nccl baseline") == 4, out[-2000:]
 
 
 def test_tensor_parallel_two_gpus():
