@@ -273,6 +273,21 @@ class BucketedZeroAdamW:
                     full.copy_(torch.cat(parts))
         return sqnorm.sqrt() * grad_scale
 
+    # -------------------------------------------------------------- state (this rank's shards)
+    def state_dict(self) -> dict:
+        """Sharded state: keys carry the DP rank so every rank saves its own slices."""
+        r = self.rank
+        return {f"master.dp{r}": self.master, f"exp_avg.dp{r}": self.exp_avg, f"exp_avg_sq.dp{r}": self.exp_avg_sq,
+                "step": self.step_count}
+
+    @torch.no_grad()
+    def load_state_dict(self, sd: dict) -> None:
+        r = self.rank
+        self.master.copy_(sd[f"master.dp{r}"])
+        self.exp_avg.copy_(sd[f"exp_avg.dp{r}"])
+        self.exp_avg_sq.copy_(sd[f"exp_avg_sq.dp{r}"])
+        self.step_count = int(sd.get("step", self.step_count))
+
     def check(self) -> None:
         if self.backend == "p2p" and int(self.status.item()):
             raise RuntimeError("distributed optimizer: a peer did not reach a gradient/parameter barrier in time")

@@ -124,6 +124,50 @@ class PipelineController:
             await self.recipe.stop_services(self.services)
         await self.recipe.shutdown()
 
+    # ------------------------------------------------------------------ checkpoints
+    def checkpoint_root(self) -> Path:
+        return self.config.megatron_worker.get_checkpoint_dir()
+
+    def save_checkpoint(self) -> Path:
+        """torch_dist checkpoint of model + optimizer + controller/dataset state (retries inside),
+        plus an HF safetensors export with rotation when ``save_hf_checkpoint``.  Reference:
+        ``BaseController.save_checkpoint`` / ``save_hf_checkpoint`` (``axrl/controller/base_controller.py:153-203``)."""
+        import shutil
+
+        from axrl_b200.train.checkpoint import save_dist_checkpoint, save_hf_checkpoint
+
+        mw = self.config.megatron_worker
+        extra = {"global_step": self.global_step,
+                 "dataset_state": self.train_dataset.state_dict() if self.train_dataset is not None else None}
+        d = save_dist_checkpoint(self.checkpoint_root(), self.global_step, self.train.model, self.train.optim, extra=extra,
+                                 most_recent_k=mw.most_recent_checkpoint_k)
+        if mw.save_hf_checkpoint:
+            hf_root = self.checkpoint_root().parent / "hf"
+            save_hf_checkpoint(self.train.model, hf_root / f"step_{self.global_step:07d}")
+            olds = sorted(p for p in hf_root.glob("step_*") if p.is_dir())
+            for old in olds[:-mw.most_recent_checkpoint_k]:
+                shutil.rmtree(old, ignore_errors=True)
+        return d
+
+    def load_checkpoint_if_existed(self) -> bool:
+        from axrl_b200.train.checkpoint import latest_iteration, load_dist_checkpoint
+
+        root = self.checkpoint_root()
+        if latest_iteration(root) is None:
+            return False
+        common = load_dist_checkpoint(root, self.train.model, self.train.optim)
+        extra = common.get("extra", {})
+        self.global_step = int(extra.get("global_step", common.get("iteration", 0)))
+        if self.train_dataset is not None and extra.get("dataset_state"):
+            self.train_dataset.load_state_dict(extra["dataset_state"])
+        logger.info("resumed from %s at global_step=%d", root, self.global_step)
+        return True
+
+    def save_checkpoint_if_needed(self) -> None:
+        n = self.config.online_rl_train.checkpoint_every_n_global_updates
+        if n and self.global_step % n == 0:
+            self.save_checkpoint()
+
     # ------------------------------------------------------------------ scheduling
     def groups_per_sync(self) -> int:
         c = self.config
@@ -223,6 +267,7 @@ class PipelineController:
         c = self.config
         o = c.online_rl_train
         assert self.train_dataset is not None, "recipe must provide a train dataset (controller.train_dataset)"
+        self.load_checkpoint_if_existed()
         per_sync = self.groups_per_sync()
         scheduled = per_sync * o.batch_rollout_for_n_global_updates // o.model_sync_every_n_global_updates
         await self.schedule_groups(self.train_dataset.sample(scheduled, o.sample_type))
@@ -239,6 +284,7 @@ class PipelineController:
             step_metrics = self.train_on(batch)
             t_train = time.time() - t1
             t2 = time.time()
+            self.save_checkpoint_if_needed()
             self.engine.reset_prefix_cache()  # colocated: weights are shared, only the cache is stale
             self.worker.resume_generation()
             t_sync = time.time() - t2

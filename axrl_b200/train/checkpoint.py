@@ -174,10 +174,9 @@ def save_dist_checkpoint(root: str | os.PathLike, step: int, model: Qwen3Model, 
     d = _iter_dir(root, step)
     state: dict[str, Any] = {f"model.{k}": v.to("cpu") for k, v in mcore_state_dict(model).items()}
     if optim is not None:
-        osd = optim.state_dict()
-        for k in ("master", "exp_avg", "exp_avg_sq", "master_shard"):
-            if k in osd:
-                state[f"optimizer.{k}"] = osd[k].detach().to("cpu")
+        for k, v in optim.state_dict().items():
+            if isinstance(v, torch.Tensor):  # sharded optimizers name their slices per rank
+                state[f"optimizer.{k}"] = v.detach().to("cpu")
     rank = torch.distributed.get_rank() if torch.distributed.is_initialized() else 0
     for attempt in range(retries):
         try:

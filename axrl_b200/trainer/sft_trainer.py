@@ -21,7 +21,7 @@ class SftTrainer(BaseTrainer):
         denom = denominator_count(m, "token-mean")
         if with_metrics:
             metrics["denom"] = float(denom)
-            metrics["loss"] = float(loss)
+            metrics["loss"] = float(loss.detach())
         return loss, denom, metrics
 
     def compute_micro_batch_denominator(self, mask, num_turns: int = 0):  # noqa: ANN001, ANN201

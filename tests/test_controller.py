@@ -116,3 +116,24 @@ def test_mismatch_then_replay(tmp_path):
     ctl.config.online_rl_train.filter_zero_std = False
     out = asyncio.run(ctl.start())
     assert out["train_metrics"] and all(torch.isfinite(torch.tensor(m["grad_norm"])) for m in out["train_metrics"])
+
+
+def test_checkpoint_save_and_resume(tmp_path):
+    ctl = _ctl(tmp_path, "online_rl_train")
+    c = ctl.config
+    c.megatron_worker.checkpoint_dir = str(tmp_path / "ckpt")
+    c.megatron_worker.save_hf_checkpoint = True
+    c.megatron_worker.most_recent_checkpoint_k = 1
+    c.online_rl_train.max_global_updates = 2
+    c.online_rl_train.checkpoint_every_n_global_updates = 1
+    asyncio.run(ctl.start())
+    assert (tmp_path / "ckpt" / "latest_checkpointed_iteration.txt").read_text() == "2"
+    assert len(list((tmp_path / "ckpt").glob("iter_*"))) == 1 and len(list((tmp_path / "hf").glob("step_*"))) == 1
+    params = {n: p.detach().clone() for n, p in ctl.train.model.named_parameters()}
+    ctl2 = _ctl(tmp_path, "online_rl_train")
+    ctl2.config.megatron_worker.checkpoint_dir = str(tmp_path / "ckpt")
+    ctl2.config.online_rl_train.max_global_updates = 2  # already reached: resumes and stops
+    asyncio.run(ctl2.start())
+    assert ctl2.global_step == 2
+    for n, p in ctl2.train.model.named_parameters():
+        torch.testing.assert_close(p, params[n])
