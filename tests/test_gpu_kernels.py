@@ -358,3 +358,23 @@ def test_rollout_engine_fp8_weights_run():
     res = eng.generate([GenRequest(rid=f"r{i}", prompt=list(range(5, 40)), max_new_tokens=20, seed_stream=i) for i in range(3)])
     assert all(len(r.output_ids) == 20 and all(lp <= 0 for lp in r.output_logprobs) for r in res)
     eng.release_graphs()
+
+
+def test_bounded_flag_wait_times_out_and_context_stays_usable():
+    """A device-side wait on a flag that nothing sets gives up after its limit, reports status 1,
+    and the CUDA context keeps working (no trap, no hang)."""
+    import time
+
+    from axrl_b200.ops import _ext
+
+    flags = torch.zeros(8, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t0 = time.time()
+    _ext.ext().flag_wait_bounded(flags, 3, 7, 50_000_000, status)  # 50 ms limit
+    torch.cuda.synchronize()
+    assert status.item() == 1 and time.time() - t0 < 5
+    flags[3] = 7
+    _ext.ext().flag_wait_bounded(flags, 3, 7, 50_000_000, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0 and flags[3].item() == 0  # consumed
+    assert (torch.ones(4, device="cuda") * 2).sum().item() == 8
