@@ -34,6 +34,7 @@ from axrl_b200.rollout.engine import GenRequest, RolloutEngine
 from axrl_b200.train.engine import TrainEngine
 from axrl_b200.trainer.grpo_trainer import GrpoTrainer
 from axrl_b200.utils import iostats
+from axrl_b200.utils.nvtx import nvtx_range
 
 
 @dataclass
@@ -146,9 +147,10 @@ class SyntheticGRPO:
         io0 = iostats.snapshot()
         t0 = time.perf_counter()
         reqs = self.make_requests()
-        self.rollout.acquire_kv()
-        results = self.rollout.generate(reqs)
-        self.rollout.release_kv()
+        with nvtx_range("rollout"):
+            self.rollout.acquire_kv()
+            results = self.rollout.generate(reqs)
+            self.rollout.release_kv()
         t["rollout_s"] = time.perf_counter() - t0
 
         t1 = time.perf_counter()
@@ -174,7 +176,8 @@ class SyntheticGRPO:
         t["logprob_s"] = time.perf_counter() - t2
 
         t3 = time.perf_counter()
-        metrics = self.train.train_step(batch, self.trainer, temperature=sc.temperature)
+        with nvtx_range("train_step"):
+            metrics = self.train.train_step(batch, self.trainer, temperature=sc.temperature)
         t["train_s"] = time.perf_counter() - t3
 
         t4 = time.perf_counter()
