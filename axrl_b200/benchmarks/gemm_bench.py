@@ -18,7 +18,10 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--variants", default="auto,skinny,swapab,cutlass")
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--sweep-decomp", action="store_true", help="skinny shapes under every stream-K decomposition")
     a = ap.parse_args()
+    if a.sweep_decomp:
+        return sweep_decomp(a.iters)
     from axrl_b200.ops import _ext
 
     e = _ext.ext()
@@ -52,6 +55,48 @@ def main() -> None:
                     res[v] = {"us": round(ms * 1000, 1), "TBps": round(bytes_ / ms / 1e9, 2), "TFLOPs": round(2 * M * N * K / ms / 1e9, 1)}
                 except Exception as ex:  # noqa: BLE001
                     res[v] = str(ex)[:80]
+            print(json.dumps(res), flush=True)
+
+
+def _time(fn, flush: torch.Tensor, iters: int) -> float:
+    for _ in range(3):
+        fn()
+    ts = []
+    for _ in range(iters):
+        flush.sum()
+        s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        t.record()
+        t.synchronize()
+        ts.append(s.elapsed_time(t))
+    return sorted(ts)[len(ts) // 2]
+
+
+def sweep_decomp(iters: int) -> None:
+    """Decode-sized GEMMs (swap-AB path) under heuristic / data-parallel / split-K / stream-K."""
+    from axrl_b200.ops import _ext
+
+    e = _ext.ext()
+    flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
+    shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288)}
+    modes = [("heuristic", 0, 0), ("dp", 1, 0), ("split2", 2, 2), ("split4", 2, 4), ("split8", 2, 8), ("streamk", 3, 0)]
+    for M in (8, 32, 64):
+        for name, (N, K) in shapes.items():
+            x = torch.randn(M, K, device="cuda").bfloat16()
+            w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+            ref = e.linear_variant(x, w, "skinny").float()
+            res = {"M": M, "shape": name}
+            for tag, mode, splits in modes:
+                e.set_streamk_decomposition(mode, splits)
+                try:
+                    y = e.linear_variant(x, w, "swapab")
+                    err = (y.float() - ref).abs().max().item()
+                    ms = _time(lambda: e.linear_variant(x, w, "swapab"), flush, iters)
+                    res[tag] = {"us": round(ms * 1000, 1), "TBps": round(2 * N * K / ms / 1e9, 2), "err": round(err, 4)}
+                except Exception as ex:  # noqa: BLE001
+                    res[tag] = str(ex)[:60]
+            e.set_streamk_decomposition(0, 0)
             print(json.dumps(res), flush=True)
 
 

@@ -41,6 +41,7 @@ void flag_wait_bounded(at::Tensor, int64_t, int64_t, int64_t, at::Tensor);
 void sync_push(at::Tensor, at::Tensor, at::Tensor, int64_t);
 at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual);
 void linear_fwd_into(at::Tensor x, at::Tensor w, at::Tensor out);
+void set_streamk_decomposition(int64_t mode, int64_t splits);
 void linear_dgrad_into(at::Tensor dy, at::Tensor w, at::Tensor out);
 void tp_push(at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, at::Tensor, int64_t, int64_t, int64_t, int64_t, at::Tensor,
              int64_t, at::Tensor, int64_t);
@@ -76,6 +77,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_lp"), py::arg("row_ids") = py::none(), py::arg("forced") = py::none());
   m.def("linear_fwd", &ax::linear_fwd);
   m.def("linear_fwd_into", &ax::linear_fwd_into);
+  m.def("set_streamk_decomposition", &ax::set_streamk_decomposition);
   m.def("linear_dgrad_into", &ax::linear_dgrad_into);
   m.def("tp_push", &ax::tp_push);
   m.def("tp_wait", &ax::tp_wait);

@@ -45,6 +45,17 @@ struct Sm2 {
   using Epi = cutlass::epilogue::TmaWarpSpecialized2Sm;
 };
 
+// Stream-K decomposition override for tuning: mode 0 heuristic, 1 data-parallel, 2 split-K
+// (``splits`` ways), 3 stream-K.  Process-wide; read at each launch.
+struct DecompOverride {
+  int mode = 0;
+  int splits = 0;
+};
+inline DecompOverride& decomp_override() {
+  static DecompOverride o;
+  return o;
+}
+
 template <class LayoutA, class LayoutB, class ElemD, class Cfg, class Sched = void, class LayoutD = cutlass::layout::RowMajor>
 struct Gemm {
   using ElemA = cutlass::bfloat16_t;
@@ -85,8 +96,13 @@ struct Gemm {
     args.hw_info.sm_count = num_sms();
     if constexpr (std::is_same_v<Sched, cutlass::gemm::StreamKScheduler>) {
       // Skinny problems (decode) have too few output tiles to fill 148 SMs: let the scheduler
-      // split K (stream-K) so every SM streams weights.
-      args.scheduler.decomposition_mode = cutlass::gemm::kernel::detail::DecompositionMode::Heuristic;
+      // split K (stream-K) so every SM streams weights.  The decomposition can be overridden at
+      // run time (set_streamk_decomposition) for tuning sweeps.
+      using DM = cutlass::gemm::kernel::detail::DecompositionMode;
+      const DecompOverride& o = decomp_override();
+      args.scheduler.decomposition_mode = o.mode == 1 ? DM::DataParallel : o.mode == 2 ? DM::SplitK : o.mode == 3 ? DM::StreamK
+                                                                                                             : DM::Heuristic;
+      if (o.mode == 2 && o.splits > 0) args.scheduler.splits = o.splits;
     }
     Op op;
     auto st_impl = op.can_implement(args);

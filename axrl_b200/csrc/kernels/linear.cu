@@ -21,6 +21,12 @@ static void tn(const void* A, const void* B, const void* C, void* D, int M, int 
   else gemm::tn_narrow_sk(A, B, C, D, M, N, K, stream());
 }
 
+void set_streamk_decomposition(int64_t mode, int64_t splits) {
+  AX_CHECK(mode >= 0 && mode <= 3 && splits >= 0, "mode 0..3, splits >= 0");
+  gemm::decomp_override().mode = (int)mode;
+  gemm::decomp_override().splits = (int)splits;
+}
+
 // y[M,N] = x[M,K] @ w[N,K]^T
 at::Tensor linear_fwd(at::Tensor x, at::Tensor w) {
   check_bf16_2d(x, "x");

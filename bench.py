@@ -141,6 +141,7 @@ def main() -> None:
     par = ParallelCtx(dp_group=dist.group.WORLD if world > 1 else None, dp_size=world, dp_rank=rank)
     train = TrainEngine(wc, mcfg, dev, par=par)
     train.optim.release_grads()  # gradients live only inside the train phase
+    torch.cuda.empty_cache()  # the caching allocator still holds the released blocks
     free = torch.cuda.mem_get_info(dev)[0]
     kv_gb = a.kv_gb if a.kv_gb else max(2.0, (free - (a.headroom_gb << 30)) / (1 << 30))
     sc = SyntheticGRPOConfig(num_prompts=a.prompts_per_gpu, prompt_len=a.prompt_len, group_size=a.group, temperature=1.0,
