@@ -42,6 +42,9 @@ void sync_push(at::Tensor, at::Tensor, at::Tensor, int64_t);
 at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual);
 void linear_fwd_into(at::Tensor x, at::Tensor w, at::Tensor out);
 void set_streamk_decomposition(int64_t mode, int64_t splits);
+void tp_ar_rms(at::Tensor, int64_t, int64_t, int64_t, c10::optional<at::Tensor>, at::Tensor, double, c10::optional<at::Tensor>, at::Tensor,
+               at::Tensor, at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor);
+void tp_gather_cols(at::Tensor, int64_t, int64_t, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor);
 void linear_dgrad_into(at::Tensor dy, at::Tensor w, at::Tensor out);
 void tp_push(at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, at::Tensor, int64_t, int64_t, int64_t, int64_t, at::Tensor,
              int64_t, at::Tensor, int64_t);
@@ -78,6 +81,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_fwd", &ax::linear_fwd);
   m.def("linear_fwd_into", &ax::linear_fwd_into);
   m.def("set_streamk_decomposition", &ax::set_streamk_decomposition);
+  m.def("tp_ar_rms", &ax::tp_ar_rms);
+  m.def("tp_gather_cols", &ax::tp_gather_cols);
   m.def("linear_dgrad_into", &ax::linear_dgrad_into);
   m.def("tp_push", &ax::tp_push);
   m.def("tp_wait", &ax::tp_wait);

@@ -27,7 +27,7 @@ import math
 import time
 import zlib
 from dataclasses import dataclass, field
-from typing import Sequence
+from typing import Any, Sequence
 
 import numpy as np
 import torch
@@ -87,7 +87,8 @@ def _stream_id(rid: str) -> int:
 class RolloutEngine:
     def __init__(self, model: Qwen3Model, *, max_batch: int = 256, kv_tokens: int = 1 << 16, page_size: int = 64,
                  max_context: int = 16384, max_prefill_tokens: int = 16384, use_cuda_graph: bool = True, seed: int = 0,
-                 eos_token_id: int | None = None, burst: int = 16, kv_memory_saver: bool = False, weight_format: str = "bf16") -> None:
+                 eos_token_id: int | None = None, burst: int = 16, kv_memory_saver: bool = False, weight_format: str = "bf16",
+                 tp_group: Any = None, embed_full: torch.Tensor | None = None) -> None:
         self.model = model
         assert weight_format in ("bf16", "fp8_block")
         self.weight_format = weight_format
@@ -128,6 +129,16 @@ class RolloutEngine:
         self.running: list[_Seq] = []
         self.stats = {"prefill_tokens": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_s": 0.0, "decode_s": 0.0, "bursts": 0}
         self._alloc_static()
+        self.tp = None
+        if tp_group is not None and torch.distributed.get_world_size(tp_group) > 1:
+            # tensor-parallel serving: `model` holds this rank's shards (local heads / FFN columns /
+            # vocabulary rows); `embed_full` is the whole embedding table
+            from axrl_b200.rollout.tp import RolloutTP
+
+            assert self.is_cuda and not cfg.is_moe, "TP rollout serves dense models on GPUs"
+            assert embed_full is not None and embed_full.shape[0] == cfg.vocab_size, "TP rollout needs the full embedding table"
+            self.embed_full = embed_full
+            self.tp = RolloutTP(tp_group, cfg.hidden_size, model.lm_weight.shape[0], max(max_prefill_tokens, max_batch), max_batch, self.dtype)
         if weight_format == "fp8_block":
             self.quantize_weights()
 
@@ -203,11 +214,46 @@ class RolloutEngine:
         return self._lin(ops.swiglu(self._lin(x, mlp.gate_up_proj)), mlp.down_proj, residual=h)
 
     def _embed(self, ids: torch.Tensor) -> torch.Tensor:
+        if self.tp is not None:
+            return _ext.ext().embed_fwd(ids, self.embed_full)
         if self.is_cuda:
             return _ext.ext().embed_fwd(ids, self.model.embed_tokens)
         return torch.nn.functional.embedding(ids, self.model.embed_tokens)
 
+    def _layers_tp(self, h, pos, slots, attend):  # noqa: ANN001, ANN202
+        """TP forward: local-shard GEMMs, one fused all-reduce + residual + RMSNorm after each
+        row-parallel projection.  Returns the final normed hidden state."""
+        tp, e, eps = self.tp, _ext.ext(), self.cfg.rms_norm_eps
+        inv = self.model.inv_freq
+        rows = h.shape[0]
+        layers = self.model.layers
+        x = self._rms(h, layers[0].input_layernorm.weight)
+        for li, layer in enumerate(layers):
+            a = layer.self_attn
+            qkv = self._lin(x, a.qkv_proj)
+            q, k, v = paged.qk_norm_rope_cache(qkv, a.q_norm, a.k_norm, pos, inv, a.nq, a.nkv, a.eps, self.kv[li, 0], self.kv[li, 1], slots)
+            o = attend(li, q, k, v)
+            self._lin_into(o.reshape(rows, -1), a.o_proj, tp.partial_buffer(rows))
+            h, x = tp.allreduce_rms(rows, h, layer.post_attention_layernorm.weight, eps)
+            g = ops.swiglu(self._lin(x, layer.mlp.gate_up_proj))
+            self._lin_into(g, layer.mlp.down_proj, tp.partial_buffer(rows))
+            nxt = layers[li + 1].input_layernorm.weight if li + 1 < len(layers) else self.model.norm.weight
+            h, x = tp.allreduce_rms(rows, h, nxt, eps, want_h=li + 1 < len(layers))
+        _ = e
+        return x
+
+    def _lin_into(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
+        fw = self.fp8.get(id(w)) if self.fp8 else None
+        if fw is not None:
+            from axrl_b200.ops.fp8 import fp8_linear
+
+            out.copy_(fp8_linear(x, fw))
+            return
+        _ext.ext().linear_fwd_into(x.contiguous(), w, out)
+
     def _layers(self, h, pos, slots, attend, capture=None):  # noqa: ANN001, ANN202
+        if self.tp is not None:
+            return self._layers_tp(h, pos, slots, attend)
         inv = self.model.inv_freq
         for li, layer in enumerate(self.model.layers):
             a = layer.self_attn
@@ -222,6 +268,10 @@ class RolloutEngine:
         return self._rms(h, self.model.norm.weight)
 
     def _logits(self, h: torch.Tensor) -> torch.Tensor:
+        if self.tp is not None:  # vocabulary shard on this rank, rows all-gathered
+            rows = h.shape[0]
+            self._lin_into(h, self.model.lm_weight, self.tp.logits_buffer(rows))
+            return self.tp.gather_logits(rows)
         return self._lin(h, self.model.lm_weight)
 
     # ------------------------------------------------------------------ public API

@@ -304,6 +304,54 @@ def case_zero() -> None:
         print(f"rank {rank}: zero {zero} ok (max param diff {d:.2e})", flush=True)
 
 
+def case_rollout_tp() -> None:
+    """TP=world rollout engine (sharded weights, fused all-reduce + RMSNorm, gathered logits):
+    both ranks generate the same tokens, and the rollout log-probs match a TP=1 trainer recompute."""
+    from axrl_b200.configs import MegatronWorkerConfig
+    from axrl_b200.data.sample import Sample, SampleBatch
+    from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from axrl_b200.parallel import tensor_parallel as tpl
+    from axrl_b200.rollout.engine import GenRequest, RolloutEngine
+    from axrl_b200.train.engine import TrainEngine
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=3, num_attention_heads=8,
+                      num_key_value_heads=4, head_dim=128)
+    full = Qwen3Model(cfg)
+    full.init_weights(7)
+    full = full.to("cuda", torch.bfloat16)
+    full.inv_freq = full.inv_freq.float()
+    state = {k: v.detach().clone() for k, v in full.named_parameters()}
+    tp = tpl.TPContext.from_group(dist.group.WORLD)
+    shard = Qwen3Model(cfg, tp=tp).to("cuda", torch.bfloat16)
+    shard.inv_freq = shard.inv_freq.float()
+    tpl.load_shards_from_full(shard, state, tp)
+    for p in shard.parameters():
+        p.requires_grad_(False)
+    for use_graph in (False, True):
+        eng = RolloutEngine(shard, max_batch=8, kv_tokens=4096, max_context=256, seed=3, use_cuda_graph=use_graph, burst=8,
+                            tp_group=dist.group.WORLD, embed_full=state["embed_tokens"])
+        g = torch.Generator().manual_seed(0)
+        reqs = [GenRequest(rid=f"r{i}", prompt=torch.randint(1, 2048, (30 + 9 * i,), generator=g).tolist(), max_new_tokens=40,
+                           temperature=1.0, stop_token_ids=(), seed_stream=i) for i in range(5)]
+        res = eng.generate(reqs)
+        torch.cuda.synchronize()
+        eng.tp.check()
+        toks = torch.tensor([t for r in res for t in r.output_ids], device="cuda")
+        other = [torch.empty_like(toks) for _ in range(world)]
+        dist.all_gather(other, toks)
+        assert all(torch.equal(o, toks) for o in other), "TP ranks sampled different tokens"
+        samples = [Sample.from_tokens(q.prompt, r.output_ids, rollout_logprobs=r.output_logprobs) for q, r in zip(reqs, res)]
+        batch = SampleBatch.from_samples(samples)
+        tr = TrainEngine(MegatronWorkerConfig(inference_only=True), cfg, "cuda", model=full)
+        lp = tr.compute_logprobs(batch)
+        m = batch["loss_mask"]
+        diff = (lp - batch["rollout_logprobs"])[m].abs()
+        assert diff.mean().item() < 0.03 and diff.max().item() < 0.6, (diff.mean().item(), diff.max().item())
+        eng.release_graphs()
+        print(f"rank {rank}: rollout_tp graph={use_graph} ok (mean |dlp| {diff.mean().item():.4f})", flush=True)
+
+
 if __name__ == "__main__":
     from datetime import timedelta
 

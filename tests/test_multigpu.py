@@ -49,3 +49,8 @@ def test_expert_parallel_two_gpus():
 def test_bucketed_zero_two_gpus():
     out = _run("zero")
     assert out.count("zero nccl ok") == 2 and out.count("zero p2p ok") == 2, out[-2000:]
+
+
+def test_tensor_parallel_rollout_two_gpus():
+    out = _run("rollout_tp")
+    assert out.count("rollout_tp graph=False ok") == 2 and out.count("rollout_tp graph=True ok") == 2, out[-2000:]
