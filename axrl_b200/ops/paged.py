@@ -99,3 +99,55 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, seed: torch.Tensor, 
     lp = torch.empty(B, dtype=torch.float32, device=logits.device)
     _ext.ext().sample_tokens(logits, temperature, seed, tok, lp, row_ids, forced)
     return tok, lp
+
+
+def sample_filtered(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor, min_p: torch.Tensor,
+                    presence: torch.Tensor | None = None, frequency: torch.Tensor | None = None, repetition: torch.Tensor | None = None,
+                    history: torch.Tensor | None = None, bias: torch.Tensor | None = None, forced: torch.Tensor | None = None,
+                    generator: torch.Generator | None = None, kmax: int = 1024) -> tuple[torch.Tensor, torch.Tensor]:
+    """Sampling with the full SGLang-style controls (fixed shapes: CUDA-graph capturable).
+
+    Per row: repetition penalty (HF rule: divide positive / multiply negative logits of tokens seen),
+    frequency and presence penalties over ``history`` (generated tokens, -1 = empty), additive
+    ``bias`` (logit bias, or -inf outside an allowed set), temperature, then top-k, top-p (on the
+    ``kmax`` best candidates) and min-p filtering and a Gumbel-max draw.  Temperature <= 0 is greedy.
+    The reported log-prob is that of the sampled token under the temperature-scaled, unfiltered
+    distribution — the quantity the trainer recomputes."""
+    lf = logits.float()
+    B, V = lf.shape
+    greedy = temperature <= 0
+    t = torch.where(greedy, torch.ones_like(temperature), temperature).float()[:, None]
+    z = lf
+    if history is not None:
+        valid = (history >= 0).float()
+        counts = torch.zeros_like(lf).scatter_add_(1, history.clamp(min=0).long(), valid)
+        seen = counts > 0
+        if repetition is not None:
+            rp = repetition.float()[:, None]
+            z = torch.where(seen, torch.where(z > 0, z / rp, z * rp), z)
+        if frequency is not None:
+            z = z - frequency.float()[:, None] * counts
+        if presence is not None:
+            z = z - presence.float()[:, None] * seen.float()
+    if bias is not None:
+        z = z + bias.float()
+    z = z / t
+    k = min(kmax, V)
+    vals, idx = torch.topk(z, k, dim=-1)
+    ar = torch.arange(k, device=lf.device)[None, :]
+    k_eff = torch.where(top_k > 0, top_k, torch.full_like(top_k, k)).clamp(max=k)
+    drop = ar >= k_eff[:, None]
+    probs = torch.softmax(vals.masked_fill(drop, float("-inf")), -1)
+    before = probs.cumsum(-1) - probs
+    drop = drop | (before > top_p.float()[:, None])
+    drop = drop | (probs < min_p.float()[:, None] * probs[:, :1])
+    drop[:, 0] = False  # the best candidate always survives
+    vals = vals.masked_fill(drop, float("-inf"))
+    u = torch.rand(vals.shape, device=lf.device, generator=generator).clamp_(1e-20, 1.0)
+    pick = torch.argmax(vals - torch.log(-torch.log(u)), -1)
+    tok = torch.where(greedy, idx[:, 0], idx.gather(1, pick[:, None]).squeeze(1))
+    if forced is not None:
+        tok = torch.where(forced >= 0, forced.to(tok.dtype), tok)
+    scaled = lf / t
+    lp = scaled.gather(1, tok[:, None]).squeeze(1) - torch.logsumexp(scaled, -1)
+    return tok, lp

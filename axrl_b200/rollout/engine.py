@@ -52,6 +52,20 @@ class GenRequest:
     forced_token: int | None = None
     capture_routing: bool = False
     seed_stream: int | None = None  # random stream id (defaults to a hash of rid)
+    # sampling controls (defaults = plain temperature sampling on the fused kernel)
+    top_k: int = -1
+    top_p: float = 1.0
+    min_p: float = 0.0
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
+    repetition_penalty: float = 1.0
+    logit_bias: dict[int, float] | None = None
+    allowed_token_ids: Sequence[int] | None = None  # constrained decoding: only these tokens may be drawn
+
+    @property
+    def filtered(self) -> bool:
+        return (self.top_k > 0 or self.top_p < 1.0 or self.min_p > 0.0 or self.presence_penalty != 0.0 or self.frequency_penalty != 0.0
+                or self.repetition_penalty != 1.0 or bool(self.logit_bias) or self.allowed_token_ids is not None)
 
 
 @dataclass
@@ -177,6 +191,15 @@ class RolloutEngine:
             "force_eos": z(torch.int32, B), "stop_on_eos": z(torch.int32, B),
         }
         self.s_seed = z(torch.int64, 1)
+        # filtered sampling (top-k/p, min-p, penalties, bias / allowed set): per-row controls
+        self.st.update({"top_k": torch.full((B,), -1, dtype=torch.int64, device=dev), "top_p": torch.ones(B, device=dev),
+                        "min_p": z(torch.float32, B), "pres": z(torch.float32, B), "freq": z(torch.float32, B),
+                        "rep": torch.ones(B, device=dev), "ngen": z(torch.int64, B)})
+        self.hist_cap = 1024  # generated tokens remembered for the penalties (most recent)
+        self.hist = torch.full((B, self.hist_cap), -1, dtype=torch.int64, device=dev)
+        self.h_hist = torch.full((B, self.hist_cap), -1, dtype=torch.int64).pin_memory() if self.is_cuda else torch.full((B, self.hist_cap), -1, dtype=torch.int64)
+        self.bias: torch.Tensor | None = None  # (B, V) additive logit bias, allocated on first use
+        self.filtered_mode = False
         self.s_out_tok = z(torch.int64, B)
         self.s_out_lp = z(torch.float32, B)
         self.ring_cap = max(self.burst, 1)
@@ -407,7 +430,16 @@ class RolloutEngine:
                 rids.append(s.stream)
                 forced.append(self.eos if (s.force_eos and n + 1 == s.end_total) else -1)
         lg = logits.index_select(0, torch.tensor(rows, device=dev))
-        tok, lp = self._sample_rows(lg, temps, rids, forced)
+        if any(s.req.filtered for s in new_seqs):
+            rq = [s.req for s in new_seqs]
+            as_t = lambda vals, dt: torch.tensor(vals, dtype=dt).to(dev)  # noqa: E731
+            b = self._bias_rows(rq, len(rq))
+            tok, lp = paged.sample_filtered(lg, as_t(temps, torch.float32), as_t([r.top_k for r in rq], torch.int64),
+                                            as_t([r.top_p for r in rq], torch.float32), as_t([r.min_p for r in rq], torch.float32),
+                                            bias=None if b is None else b.to(dev), forced=as_t(forced, torch.int64),
+                                            generator=None if self.is_cuda else self.gen)
+        else:
+            tok, lp = self._sample_rows(lg, temps, rids, forced)
         self.stats["prefill_tokens"] += off
         self.stats["prefill_s"] += time.perf_counter() - t0
         finished = []
@@ -506,6 +538,13 @@ class RolloutEngine:
             h["force_eos"][i] = int(s.force_eos)
             h["stop_on_eos"][i] = int(s.stop_on_eos)
             h["forced"][i] = self.eos if (s.force_eos and n + 1 == s.end_total) else -1
+            r = s.req
+            h["top_k"][i], h["top_p"][i], h["min_p"][i] = r.top_k, r.top_p, r.min_p
+            h["pres"][i], h["freq"][i], h["rep"][i] = r.presence_penalty, r.frequency_penalty, r.repetition_penalty
+            h["ngen"][i] = min(len(s.out_ids), self.hist_cap - 1)
+        self.filtered_mode = any(s.req.filtered for s in self.running)
+        if self.filtered_mode:
+            self._upload_filters(self.running, bucket)
         if bucket > B:
             h["len"][B:bucket] = 0
             h["slot"][B:bucket] = self.scratch_page * P
@@ -518,6 +557,35 @@ class RolloutEngine:
             if self.is_cuda:
                 iostats.add_h2d(h[k][:bucket])
         self.ring_step.zero_()
+
+    def _bias_rows(self, reqs: list, n_rows: int) -> torch.Tensor | None:
+        """(n_rows, V) additive bias from logit_bias / allowed_token_ids (None when unused)."""
+        if not any(r.logit_bias or r.allowed_token_ids is not None for r in reqs):
+            return None
+        V = self.cfg.vocab_size
+        b = torch.zeros(n_rows, V, dtype=torch.float32)
+        for i, r in enumerate(reqs):
+            if r.allowed_token_ids is not None:
+                b[i].fill_(float("-inf"))
+                b[i, torch.as_tensor(list(r.allowed_token_ids), dtype=torch.long)] = 0.0
+            for t, v in (r.logit_bias or {}).items():
+                b[i, int(t)] += float(v)
+        return b
+
+    def _upload_filters(self, seqs: list, bucket: int) -> None:
+        self.h_hist.fill_(-1)
+        for i, s in enumerate(seqs):
+            tail = s.out_ids[-(self.hist_cap - 1):]
+            if tail:
+                self.h_hist[i, :len(tail)] = torch.as_tensor(tail, dtype=torch.int64)
+        self.hist[:bucket].copy_(self.h_hist[:bucket], non_blocking=True)
+        b = self._bias_rows([s.req for s in seqs], bucket)
+        if b is not None:
+            if self.bias is None:
+                self.bias = torch.zeros(self.max_batch, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+            self.bias[:bucket].copy_(b.to(self.device), non_blocking=True)
+        elif self.bias is not None:
+            self.bias[:bucket].zero_()
 
     def _decode_burst(self) -> list[GenResult]:
         t0 = time.perf_counter()
@@ -622,7 +690,15 @@ class RolloutEngine:
         h = self._embed(tok)
         h = self._layers(h, pos, slots, lambda li, q, k, v: paged.paged_decode_attention(q, self.kv[li, 0], self.kv[li, 1], bt, lens, self.ws), capture)
         logits = self._logits(h)
-        if self.is_cuda:
+        if self.filtered_mode:
+            t, l = paged.sample_filtered(logits, st["temp"][:bucket], st["top_k"][:bucket], st["top_p"][:bucket], st["min_p"][:bucket],
+                                         st["pres"][:bucket], st["freq"][:bucket], st["rep"][:bucket], self.hist[:bucket],
+                                         self.bias[:bucket] if self.bias is not None else None, forced=st["forced"][:bucket],
+                                         generator=None if self.is_cuda else self.gen)
+            ng = st["ngen"][:bucket]
+            self.hist[:bucket].scatter_(1, ng[:, None], t[:, None])
+            ng.add_(1).clamp_(max=self.hist_cap - 1)
+        elif self.is_cuda:
             t, l = paged.sample(logits, st["temp"][:bucket], self.s_seed, row_ids=st["rid"][:bucket], forced=st["forced"][:bucket])
         else:
             t, l = paged.sample(logits, st["temp"][:bucket], self.s_seed, generator=self.gen, forced=st["forced"][:bucket])
@@ -631,7 +707,8 @@ class RolloutEngine:
         self._advance(bucket)
 
     def _replay(self, bucket: int) -> None:
-        g = self.graphs.get(bucket)
+        key = (bucket, self.filtered_mode, self.bias is not None)
+        g = self.graphs.get(key)
         if g is None:
             saved = {k: v.clone() for k, v in self.st.items()}
             saved_ring = (self.ring_tok.clone(), self.ring_lp.clone(), self.ring_step.clone(), self.s_seed.clone())
@@ -652,8 +729,8 @@ class RolloutEngine:
                 self._decode_body(bucket)
             captured = _ext.count_launches(was) - before
             _ext._COUNT["launches"] = before
-            self.graphs[bucket] = (graph, captured)
-            g = self.graphs[bucket]
+            self.graphs[key] = (graph, captured)
+            g = self.graphs[key]
             # capture does not execute: state is still the restored one; run the first step for real
         g[0].replay()
         _ext.add_launches(g[1])

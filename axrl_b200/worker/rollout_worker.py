@@ -98,7 +98,9 @@ class RolloutWorker:
             await asyncio.get_running_loop().run_in_executor(None, self._ready.wait)
             rid = f"{inp.session_id}#{next(self._ids)}"
             req = GenRequest(rid=rid, prompt=ids + out_ids, max_new_tokens=budget - len(out_ids), temperature=sc.temperature,
-                             stop_token_ids=stop, capture_routing=inp.capture_routing)
+                             stop_token_ids=stop, capture_routing=inp.capture_routing, top_k=sc.top_k, top_p=sc.top_p, min_p=sc.min_p,
+                             presence_penalty=sc.presence_penalty, frequency_penalty=sc.frequency_penalty,
+                             repetition_penalty=sc.repetition_penalty)
             res = await self._submit(req)
             out_ids += res.output_ids
             out_lps += res.output_logprobs

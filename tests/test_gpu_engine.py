@@ -147,3 +147,20 @@ def test_kv_release_acquire_and_preemption():
         assert len(r.output_ids) == len(r.output_logprobs) == L and r.output_ids[-1] == 3 and r.finish_reason == "stop"
     assert [r.rid for r in res] == [q.rid for q in reqs]
     small.release_graphs()
+
+
+def test_filtered_sampling_in_graph_decode():
+    """top-k / penalties / allowed-token sets run inside the captured decode graph."""
+    from axrl_b200.rollout.engine import GenRequest, RolloutEngine
+
+    m = _model(6)
+    eng = RolloutEngine(m, max_batch=8, kv_tokens=4096, max_context=256, seed=4, burst=8)
+    reqs = [GenRequest(rid="allowed", prompt=list(range(3, 40)), max_new_tokens=24, allowed_token_ids=[100, 101, 102], seed_stream=1),
+            GenRequest(rid="norepeat", prompt=list(range(3, 40)), max_new_tokens=30, top_k=1, presence_penalty=1e4, seed_stream=2),
+            GenRequest(rid="topp", prompt=list(range(9, 30)), max_new_tokens=16, top_p=0.5, min_p=0.05, seed_stream=3)]
+    res = {r.rid: r for r in eng.generate(reqs)}
+    assert set(res["allowed"].output_ids) <= {100, 101, 102} and len(res["allowed"].output_ids) == 24
+    assert len(set(res["norepeat"].output_ids)) == 30
+    assert len(res["topp"].output_ids) == 16 and all(lp <= 0 for lp in res["topp"].output_logprobs)
+    assert any(k[1] for k in eng.graphs)  # a filtered-mode graph was captured
+    eng.release_graphs()

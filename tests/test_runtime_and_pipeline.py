@@ -100,3 +100,53 @@ def test_tiny_grpo_cpu_plumbing():
     after = list(pipe.rollout.model.parameters())
     assert any(not torch.equal(a, b) for a, b in zip(before, after))
     assert all(torch.equal(a, b) for a, b in zip(after, pipe.train.model.parameters()))
+
+
+def test_filtered_sampling_controls():
+    from axrl_b200.ops.paged import sample_filtered
+
+    torch.manual_seed(0)
+    B, V = 4, 64
+    logits = torch.randn(B, V)
+    logits[:, 5] = 10.0
+    ones = torch.ones(B)
+    g = torch.Generator().manual_seed(1)
+    # top_k = 1 behaves greedily
+    tok, lp = sample_filtered(logits, ones, torch.ones(B, dtype=torch.int64), ones, torch.zeros(B), generator=g)
+    assert (tok == 5).all()
+    assert torch.allclose(lp, torch.log_softmax(logits, -1)[:, 5], atol=1e-5)
+    # a huge presence penalty on token 5 (already generated) removes it from a top-1 draw
+    hist = torch.full((B, 3), -1, dtype=torch.int64)
+    hist[:, 0] = 5
+    tok2, _ = sample_filtered(logits, ones, torch.ones(B, dtype=torch.int64), ones, torch.zeros(B), presence=torch.full((B,), 100.0),
+                              history=hist, generator=g)
+    assert (tok2 != 5).all()
+    # allowed-token mask (constrained decoding): only tokens 10..12 may be drawn
+    bias = torch.full((B, V), float("-inf"))
+    bias[:, 10:13] = 0.0
+    for _ in range(5):
+        t3, _ = sample_filtered(logits, ones, torch.full((B,), -1), ones, torch.zeros(B), bias=bias, generator=g)
+        assert ((t3 >= 10) & (t3 < 13)).all()
+    # top-p 0: only the best token; min-p 1.0: only the best token
+    t4, _ = sample_filtered(logits, ones, torch.full((B,), -1), torch.zeros(B), torch.zeros(B), generator=g)
+    t5, _ = sample_filtered(logits, ones, torch.full((B,), -1), ones, torch.ones(B), generator=g)
+    assert (t4 == 5).all() and (t5 == 5).all()
+
+
+def test_engine_constrained_and_penalised_requests():
+    from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from axrl_b200.rollout.engine import GenRequest, RolloutEngine
+
+    cfg = Qwen3Config(vocab_size=256, hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=16)
+    m = Qwen3Model(cfg)
+    m.init_weights(0)
+    eng = RolloutEngine(m, max_batch=4, kv_tokens=1024, max_context=128, seed=0, use_cuda_graph=False, burst=4)
+    reqs = [GenRequest(rid="allowed", prompt=list(range(3, 15)), max_new_tokens=12, allowed_token_ids=[40, 41, 42]),
+            GenRequest(rid="norepeat", prompt=list(range(3, 15)), max_new_tokens=20, top_k=1, presence_penalty=1e4),
+            GenRequest(rid="plain", prompt=list(range(5, 9)), max_new_tokens=6)]
+    res = {r.rid: r for r in eng.generate(reqs)}
+    assert set(res["allowed"].output_ids) <= {40, 41, 42} and len(res["allowed"].output_ids) == 12
+    out = res["norepeat"].output_ids
+    assert len(out) == 20 and len(set(out)) == 20  # greedy with a huge presence penalty never repeats
+    assert len(res["plain"].output_ids) == 6
