@@ -299,7 +299,15 @@ class Qwen3Model(nn.Module):
         assert not self.tp.enabled, "full logits are a rollout-side (TP=1) operation"
         return torch.nn.functional.linear(hidden.float(), self.lm_weight.float())
 
-    def logprobs(self, hidden: torch.Tensor, labels: torch.Tensor, temperature: float = 1.0, entropy: bool = False):  # noqa: ANN201
+    def argmax_tokens(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Most likely token per row (TP=1; SFT accuracy)."""
+        from axrl_b200.ops.logprob import argmax_tokens
+
+        assert not self.tp.enabled, "argmax over a sharded vocabulary is not supported"
+        return argmax_tokens(hidden, self.lm_weight)
+
+    def logprobs(self, hidden: torch.Tensor, labels: torch.Tensor, temperature: float = 1.0, entropy: bool = False,  # noqa: ANN201
+                 entropy_top_k: int = 0):
         """Per-token log p(label) (and entropy) for all T tokens; under TP ``hidden`` is the SP slice
         and ``labels`` the full (T,) labels, and every TP rank returns the full result."""
         if self.tp.enabled:
@@ -307,7 +315,7 @@ class Qwen3Model(nn.Module):
                                               temperature=temperature, compute_entropy=entropy)
         from axrl_b200.ops.logprob import fused_logprob
 
-        return fused_logprob(hidden, self.lm_weight, labels, temperature=temperature, compute_entropy=entropy)
+        return fused_logprob(hidden, self.lm_weight, labels, temperature=temperature, compute_entropy=entropy, entropy_top_k=entropy_top_k)
 
 
 # ----------------------------------------------------------------------------- HF naming

@@ -201,7 +201,9 @@ class TrainEngine:
         for i, mb in enumerate(mbs if not self.pp.enabled else []):
             dmb = mb.to(self.device)
             h = self._hidden(dmb)
-            lp, ent = self.model.logprobs(h, dmb.labels.clamp(min=-1), temperature, entropy=need_entropy)
+            ec = getattr(trainer.config, "entropy_control", None)
+            lp, ent = self.model.logprobs(h, dmb.labels.clamp(min=-1), temperature, entropy=need_entropy,
+                                          entropy_top_k=max(0, ec.top_k) if ec is not None else 0)
             lp = torch.where(dmb.labels >= 0, lp, torch.zeros_like(lp))
             sub = batch.select_rows(mb.rows).to(self.device)
             if self.device.type == "cuda":
@@ -212,6 +214,8 @@ class TrainEngine:
                 sub["loss_mask"] = (sub["loss_mask"].bool() & local_token_mask(dmb, S)).to(sub["loss_mask"].dtype)
             outputs = {"log_prob": dmb.unpack(lp, S),
                        "entropy": dmb.unpack(ent, S) if ent is not None else torch.zeros((len(mb.rows), S), device=self.device)}
+            if getattr(trainer.config, "compute_accuracy", False) and not self.tp.enabled:
+                outputs["argmax"] = dmb.unpack(self.model.argmax_tokens(h.detach()).float(), S).long()
             want = metrics_every_micro_batch or i == len(mbs) - 1
             loss, denom, m = trainer.loss_func(outputs, sub, with_metrics=want)
             if i == len(mbs) - 1 and hasattr(self.optim, "arm"):

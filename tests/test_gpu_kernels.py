@@ -378,3 +378,26 @@ def test_bounded_flag_wait_times_out_and_context_stays_usable():
     torch.cuda.synchronize()
     assert status.item() == 0 and flags[3].item() == 0  # consumed
     assert (torch.ones(4, device="cuda") * 2).sum().item() == 8
+
+
+def test_fused_logprob_topk_entropy_and_argmax():
+    """Top-k masked entropy (values and gradients w.r.t. hidden and weight) against the fp32 oracle."""
+    from axrl_b200.ops.logprob import argmax_tokens, fused_logprob, logprob_ref
+
+    torch.manual_seed(3)
+    T, H, V = 300, 256, 4096
+    h = (torch.randn(T, H, device="cuda") * 0.5).bfloat16().requires_grad_(True)
+    w = (torch.randn(V, H, device="cuda") * 0.05).bfloat16().requires_grad_(True)
+    lab = torch.randint(0, V, (T,), device="cuda")
+    lp, ent = fused_logprob(h, w, lab, temperature=0.8, compute_entropy=True, entropy_top_k=20, chunk=128)
+    (lp.sum() + 3.0 * ent.sum()).backward()
+    hr, wr = h.detach().float().requires_grad_(True), w.detach().float().requires_grad_(True)
+    lpr, entr = logprob_ref(hr, wr, lab, temperature=0.8, compute_entropy=True, entropy_top_k=20)
+    (lpr.sum() + 3.0 * entr.sum()).backward()
+    torch.testing.assert_close(lp, lpr, atol=3e-2, rtol=0)
+    torch.testing.assert_close(ent, entr, atol=3e-2, rtol=0)
+    assert ((h.grad.float() - hr.grad).norm() / hr.grad.norm()).item() < 3e-2
+    assert ((w.grad.float() - wr.grad).norm() / wr.grad.norm()).item() < 3e-2
+    am = argmax_tokens(h.detach(), w.detach())
+    ref = (h.detach().float() @ w.detach().float().t()).argmax(-1)
+    assert (am == ref).float().mean().item() > 0.98

@@ -126,3 +126,19 @@ def test_denominators_and_opd():
     assert new[0, 0].item() == pytest.approx(0.5 * 1 - 0.5 * 0.5)
     assert new[0, 1].item() == pytest.approx(0.5 * 1 - 0.5 * 1.0)  # reverse KL 3 clipped to 1
     assert m["opd/reverse_kl_clip_rate"] == pytest.approx(0.5)
+
+
+def test_topk_entropy_ref_and_sft_accuracy():
+    from axrl_b200.ops.logprob import logprob_ref
+
+    torch.manual_seed(0)
+    h = torch.randn(5, 16)
+    w = torch.randn(40, 16)
+    lab = torch.randint(0, 40, (5,))
+    _, e_full = logprob_ref(h, w, lab, compute_entropy=True)
+    _, e_k = logprob_ref(h, w, lab, compute_entropy=True, entropy_top_k=4)
+    logits = h @ w.t()
+    top = torch.topk(logits, 4, -1).values
+    p = torch.softmax(top, -1)
+    torch.testing.assert_close(e_k, torch.logsumexp(top, -1) - (p * top).sum(-1))
+    assert (e_k <= e_full + 1e-6).all() and (e_k <= torch.log(torch.tensor(4.0)) + 1e-6).all()
