@@ -61,8 +61,38 @@ def router_logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return _RouterLinear.apply(x, w)
 
 
+class _FusedRoute(torch.autograd.Function):
+    """Softmax + top-k (or replayed ids) + renormalisation in one kernel; the backward goes
+    through the selected probabilities and the softmax."""
+
+    @staticmethod
+    def forward(ctx, logits, k, renorm, replay, replay_mask):  # noqa: ANN001, ANN205
+        from axrl_b200.ops import _ext
+
+        w, ids, probs = _ext.ext().router_topk(logits.contiguous(), k, renorm, replay, replay_mask)
+        ctx.save_for_backward(probs, ids, w)
+        ctx.renorm = renorm
+        ctx.mark_non_differentiable(ids)
+        return w, ids
+
+    @staticmethod
+    def backward(ctx, g_w, _g_ids):  # noqa: ANN001, ANN205
+        probs, ids, w = ctx.saved_tensors
+        g = g_w.float()
+        if ctx.renorm:  # w = p_sel / S:  dp_sel = (g - sum(g * w)) / S
+            p_sel = probs.gather(1, ids)
+            S = p_sel.sum(-1, keepdim=True).clamp_min(1e-20)
+            g = (g - (g * w).sum(-1, keepdim=True)) / S
+        dprobs = torch.zeros_like(probs).scatter_add_(1, ids, g)
+        dlogits = probs * (dprobs - (dprobs * probs).sum(-1, keepdim=True))
+        return dlogits, None, None, None, None
+
+
 def route(logits: torch.Tensor, k: int, renorm: bool, replay: torch.Tensor | None = None, replay_mask: torch.Tensor | None = None):  # noqa: ANN201
     """Top-k routing in fp32.  Returns (weights (T,k) fp32, ids (T,k) int64)."""
+    if logits.is_cuda and k <= 8 and logits.shape[-1] <= 256:
+        return _FusedRoute.apply(logits.float(), int(k), bool(renorm), None if replay is None else replay.long().contiguous(),
+                                 None if replay_mask is None or replay is None else replay_mask.bool().contiguous())
     probs = torch.softmax(logits.float(), -1)
     top_w, top_i = probs.topk(k, -1)
     if replay is not None:

@@ -401,3 +401,26 @@ def test_fused_logprob_topk_entropy_and_argmax():
     am = argmax_tokens(h.detach(), w.detach())
     ref = (h.detach().float() @ w.detach().float().t()).argmax(-1)
     assert (am == ref).float().mean().item() > 0.98
+
+
+@pytest.mark.parametrize("renorm", [True, False])
+def test_fused_router_matches_torch(renorm):
+    """Softmax + top-k + replay + renorm kernel and its backward against the PyTorch routing."""
+    from axrl_b200.models import moe
+
+    torch.manual_seed(0)
+    T, E, k = 500, 128, 8
+    x = torch.randn(T, E, device="cuda")
+    replay = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)])
+    mask = torch.rand(T, device="cuda") < 0.5
+    for rp, rm in ((None, None), (replay, mask)):
+        a = x.clone().requires_grad_(True)
+        b = x.clone().requires_grad_(True)
+        w1, i1 = moe.route(a, k, renorm, rp, rm)
+        w2, i2 = moe.route(b.cpu(), k, renorm, None if rp is None else rp.cpu(), None if rm is None else rm.cpu())
+        assert torch.equal(i1.cpu(), i2)
+        torch.testing.assert_close(w1.cpu(), w2, atol=1e-6, rtol=1e-5)
+        gw = torch.randn(T, k)
+        w1.backward(gw.cuda())
+        w2.backward(gw)
+        torch.testing.assert_close(a.grad.cpu(), b.grad.cpu(), atol=1e-6, rtol=1e-4)
