@@ -19,6 +19,8 @@ def main() -> None:
     ap.add_argument("--variants", default="auto,skinny,swapab,cutlass")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--sweep-decomp", action="store_true", help="skinny shapes under every stream-K decomposition")
+    ap.add_argument("--ms", default="1,8,32,64,128,256,4096", help="comma-separated M values")
+    ap.add_argument("--shapes", default="qkv,o,gate_up,down,lm_head")
     a = ap.parse_args()
     if a.sweep_decomp:
         return sweep_decomp(a.iters)
@@ -27,7 +29,8 @@ def main() -> None:
     e = _ext.ext()
     flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
     shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288), "lm_head": (151936, 4096)}
-    for M in (1, 8, 32, 64, 128, 256, 4096):
+    shapes = {k: v for k, v in shapes.items() if k in a.shapes.split(",")}
+    for M in [int(m) for m in a.ms.split(",")]:
         for name, (N, K) in shapes.items():
             x = torch.randn(M, K, device="cuda").bfloat16()
             w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
