@@ -16,7 +16,7 @@ import torch
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--variants", default="auto,skinny,swapab,cutlass")
+    ap.add_argument("--variants", default="auto,tma,skinny,swapab,cutlass")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--sweep-decomp", action="store_true", help="skinny shapes under every stream-K decomposition")
     ap.add_argument("--ms", default="1,8,32,64,128,256,4096", help="comma-separated M values")
@@ -38,7 +38,7 @@ def main() -> None:
             for v in a.variants.split(","):
                 if v == "skinny" and M > 64:
                     continue
-                if v == "swapab" and M > 64:
+                if v in ("swapab", "tma") and M > 64:
                     continue
                 try:
                     fn = (lambda: e.linear_fwd(x, w)) if v == "auto" else (lambda v=v: e.linear_variant(x, w, v))

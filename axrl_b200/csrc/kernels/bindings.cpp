@@ -42,6 +42,8 @@ void sync_push(at::Tensor, at::Tensor, at::Tensor, int64_t);
 at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual);
 void linear_fwd_into(at::Tensor x, at::Tensor w, at::Tensor out);
 void set_streamk_decomposition(int64_t mode, int64_t splits);
+at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
+int64_t skinny_tma_error();
 std::vector<at::Tensor> router_topk(at::Tensor, int64_t, bool, c10::optional<at::Tensor>, c10::optional<at::Tensor>);
 void tp_ar_rms(at::Tensor, int64_t, int64_t, int64_t, c10::optional<at::Tensor>, at::Tensor, double, c10::optional<at::Tensor>, at::Tensor,
                at::Tensor, at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor);
@@ -83,6 +85,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_fwd_into", &ax::linear_fwd_into);
   m.def("set_streamk_decomposition", &ax::set_streamk_decomposition);
   m.def("router_topk", &ax::router_topk);
+  m.def("skinny_tma_linear", &ax::skinny_tma_linear);
+  m.def("skinny_tma_error", &ax::skinny_tma_error);
   m.def("tp_ar_rms", &ax::tp_ar_rms);
   m.def("tp_gather_cols", &ax::tp_gather_cols);
   m.def("linear_dgrad_into", &ax::linear_dgrad_into);

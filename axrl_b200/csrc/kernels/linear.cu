@@ -14,6 +14,7 @@ static void check_bf16_2d(const at::Tensor& t, const char* n) {
 }
 
 at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
+at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 
 static void tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K) {
   if (M >= 512) gemm::tn_sm2(A, B, C, D, M, N, K, stream());
@@ -121,6 +122,7 @@ at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant) {
   check_bf16_2d(w, "w");
   int M = x.size(0), N = w.size(0), K = x.size(1);
   if (variant == "skinny") return skinny_linear(x, w, c10::nullopt);
+  if (variant == "tma") return skinny_tma_linear(x, w, c10::nullopt);
   auto y = at::empty({M, N}, x.options());
   if (M == 0) return y;
   if (variant == "swapab") {

@@ -1,0 +1,299 @@
+// Weight-streaming GEMM for decode-sized activations, fed by TMA:
+//   Y[M,N] = X[M,K] @ W[N,K]^T (+ R),  M <= 64.
+//
+// At decode batch sizes the projection is a read of W; what matters is keeping enough bytes in
+// flight on every SM.  Here:
+//   * a persistent grid of one CTA per SM walks a contiguous range of (128-row W tile, 64-wide K
+//     slab) work units, so every SM streams the same number of bytes whatever N and K are;
+//   * one producer thread issues 2-D TMA loads (cp.async.bulk.tensor, no multicast) of the W slab
+//     (16 KB, 128-byte swizzle) and the matching X slab into an 8-stage ring guarded by mbarriers;
+//   * four consumer warps (32 W rows each) multiply with mma.sync m16n8k16 (the activation rows
+//     are the MMA's M; tensor work is small next to the weight stream);
+//   * when a warp leaves a W tile (or finishes) it adds its fp32 partial into a workspace; the
+//     last warp to contribute to a tile (arrival counter) adds the residual, writes bf16 and zeroes
+//     the workspace tile and counter, so the workspace is clean for the next call without a memset
+//     (calls must be stream-ordered: they share the workspace).
+// Every mbarrier wait is bounded: on expiry the kernel records an error code and the CTA stops.
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace ax {
+namespace skt {
+
+constexpr int NT = 128;
+constexpr int KT = 64;
+constexpr int STAGES = 8;
+constexpr int CONSUMERS = 4;
+constexpr int THREADS = (CONSUMERS + 1) * 32;
+constexpr long WAIT_LIMIT = 1L << 22;  // try_wait rounds (each suspends up to a hardware time slice)
+
+struct Params {
+  int M, N, K;
+  const bf16* r;
+  bf16* y;
+  float* ws;
+  int* cnt;
+  int* err;
+  int kslabs, total, per;
+};
+
+__device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ int swz(int row, int col) { return row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2; }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(s32(b)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t phase, int* err, int code) {
+  for (long it = 0; !mbar_try_wait(b, phase); ++it) {
+    if (it > WAIT_LIMIT) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(s32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(s32(bar))
+      : "memory");
+}
+
+template <int MT>
+__global__ void __launch_bounds__(THREADS, 1) skinny_tma_k(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
+                                                            Params p) {
+  extern __shared__ char smem_raw[];
+  char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int WB = NT * KT * 2;
+  constexpr int XB = MT * KT * 2;
+  char* sW = smem;
+  char* sX = smem + STAGES * WB;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + STAGES * XB);
+  uint64_t* empty = full + STAGES;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int u0 = blockIdx.x * p.per, u1 = min(p.total, u0 + p.per);
+  if (u0 >= u1) return;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CONSUMERS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == CONSUMERS) {  // producer
+    if (lane == 0) {
+      for (int u = u0, i = 0; u < u1; ++u, ++i) {
+        const int s = i % STAGES;
+        if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, p.err, 1)) return;
+        mbar_expect_tx(&full[s], WB + XB);
+        const int t = u / p.kslabs, k = (u % p.kslabs) * KT;
+        tma_2d(sW + s * WB, &tw, k, t * NT, &full[s]);
+        tma_2d(sX + s * XB, &tx, k, 0, &full[s]);
+      }
+    }
+    return;
+  }
+
+  float acc[MT / 16][4][4];
+  auto zero = [&]() {
+#pragma unroll
+    for (int a = 0; a < MT / 16; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc[a][b][0] = acc[a][b][1] = acc[a][b][2] = acc[a][b][3] = 0.f;
+  };
+  zero();
+  for (int u = u0, i = 0; u < u1; ++u, ++i) {
+    const int s = i % STAGES;
+    if (!mbar_wait(&full[s], (i / STAGES) & 1, p.err, 2)) return;
+    const char* w = sW + s * WB;
+    const char* x = sX + s * XB;
+#pragma unroll
+    for (int k16 = 0; k16 < KT / 16; ++k16) {
+      uint32_t a[MT / 16][4];
+#pragma unroll
+      for (int mt = 0; mt < MT / 16; ++mt) {
+        const int row = mt * 16 + (lane & 15), col = k16 * 16 + (lane >> 4) * 8;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                     : "=r"(a[mt][0]), "=r"(a[mt][1]), "=r"(a[mt][2]), "=r"(a[mt][3])
+                     : "r"(s32(x + swz(row, col))));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t b0, b1;
+        const int row = warp * 32 + j * 8 + (lane & 7), col = k16 * 16 + ((lane >> 3) & 1) * 8;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(b0), "=r"(b1) : "r"(s32(w + swz(row, col))));
+#pragma unroll
+        for (int mt = 0; mt < MT / 16; ++mt)
+          asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                       : "+f"(acc[mt][j][0]), "+f"(acc[mt][j][1]), "+f"(acc[mt][j][2]), "+f"(acc[mt][j][3])
+                       : "r"(a[mt][0]), "r"(a[mt][1]), "r"(a[mt][2]), "r"(a[mt][3]), "r"(b0), "r"(b1));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    const bool tile_end = ((u + 1) % p.kslabs) == 0 || u + 1 == u1;
+    if (!tile_end) continue;
+    // ---- flush this CTA's partial of W tile t
+    const int t = u / p.kslabs, n0 = t * NT;
+#pragma unroll
+    for (int mt = 0; mt < MT / 16; ++mt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = mt * 16 + (lane >> 2) + h * 8;
+          const int col = n0 + warp * 32 + j * 8 + (lane & 3) * 2;
+          if (row < p.M && col < p.N) {
+            atomicAdd(p.ws + (long)row * p.N + col, acc[mt][j][2 * h]);
+            atomicAdd(p.ws + (long)row * p.N + col + 1, acc[mt][j][2 * h + 1]);
+          }
+        }
+    zero();
+    // the last WARP to contribute to tile t (all contributing CTAs x 4 warps) finalises it; no
+    // block-level barrier is needed, so a warp that gave up on a wait can never strand the others
+    __threadfence();
+    int is_last = 0;
+    if (lane == 0) {
+      const int first_cta = (t * p.kslabs) / p.per, last_cta = ((t + 1) * p.kslabs - 1) / p.per;
+      is_last = atomicAdd(p.cnt + t, 1) == (last_cta - first_cta + 1) * CONSUMERS - 1;
+    }
+    is_last = __shfl_sync(0xffffffffu, is_last, 0);
+    if (is_last) {
+      __threadfence();
+      const int cols = min(NT, p.N - n0);
+      for (int q = lane; q < p.M * (cols / 2); q += 32) {
+        const int row = q / (cols / 2), c = n0 + (q % (cols / 2)) * 2;
+        float* src = p.ws + (long)row * p.N + c;
+        float v0 = __ldcg(src), v1 = __ldcg(src + 1);
+        if (p.r) {
+          float2 rr = __bfloat1622float2(*reinterpret_cast<const bf162*>(p.r + (long)row * p.N + c));
+          v0 += rr.x;
+          v1 += rr.y;
+        }
+        *reinterpret_cast<bf162*>(p.y + (long)row * p.N + c) = __floats2bfloat162_rn(v0, v1);
+        __stcg(src, 0.f);
+        __stcg(src + 1, 0.f);
+      }
+      if (lane == 0) p.cnt[t] = 0;
+    }
+  }
+}
+
+constexpr long WS_FLOATS = 64L * 262144;  // M <= 64 rows x N <= 262144 columns
+constexpr int WS_TILES = 262144 / NT;
+
+struct Workspace {
+  at::Tensor ws, cnt, err;
+};
+
+static Workspace& workspace(int dev) {
+  static Workspace w[16];
+  if (!w[dev].ws.defined()) {
+    auto o = at::TensorOptions().device(at::kCUDA, dev);
+    w[dev].ws = at::zeros({WS_FLOATS}, o.dtype(at::kFloat));
+    w[dev].cnt = at::zeros({WS_TILES}, o.dtype(at::kInt));
+    w[dev].err = at::zeros({1}, o.dtype(at::kInt));
+  }
+  return w[dev];
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+
+static EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    AX_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && p, "cuTensorMapEncodeTiled");
+    fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 map over a row-major (rows x K) matrix, box (64 K) x box_rows, 128-byte swizzle.
+static CUtensorMap make_map(const void* ptr, long rows, long K, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)KT, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AX_CHECK(r == CUDA_SUCCESS, "tensor map encode failed (", (int)r, ")");
+  return m;
+}
+
+template <int MT>
+static void launch(const at::Tensor& x, const at::Tensor& w, const bf16* r, at::Tensor& y, Workspace& wsp) {
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  Params p;
+  p.M = M, p.N = N, p.K = K, p.r = r, p.y = (bf16*)y.data_ptr(), p.ws = wsp.ws.data_ptr<float>(), p.cnt = wsp.cnt.data_ptr<int>();
+  p.err = wsp.err.data_ptr<int>();
+  p.kslabs = K / KT;
+  const int tiles = (N + NT - 1) / NT;
+  p.total = tiles * p.kslabs;
+  const int grid = std::min(num_sms(), p.total);
+  p.per = (p.total + grid - 1) / grid;
+  const int used = (p.total + p.per - 1) / p.per;
+  CUtensorMap tw = make_map(w.data_ptr(), N, K, NT);
+  CUtensorMap tx = make_map(x.data_ptr(), M, K, MT);
+  const int smem = STAGES * (NT * KT * 2 + MT * KT * 2) + 2 * STAGES * 8 + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    AX_CHECK(cudaFuncSetAttribute(skinny_tma_k<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess, "smem attribute");
+    attr_set = true;
+  }
+  skinny_tma_k<MT><<<used, THREADS, smem, stream()>>>(tw, tx, p);
+  AX_LAUNCH_OK();
+}
+
+}  // namespace skt
+
+// Y = X @ W^T (+ R) for X with at most 64 rows (decode), TMA-fed weight streaming.
+at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual) {
+  using namespace skt;
+  AX_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() && w.is_contiguous(), "bf16 contiguous");
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  AX_CHECK(M >= 1 && M <= 64 && w.size(1) == K && K % KT == 0 && N % 8 == 0 && N <= 262144, "skinny_tma: M<=64, K%64==0, N%8==0");
+  AX_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "16-byte aligned");
+  auto y = at::empty({M, N}, x.options());
+  const bf16* r = nullptr;
+  if (residual.has_value()) {
+    AX_CHECK(residual->is_contiguous() && residual->size(0) == M && residual->size(1) == N, "residual shape");
+    r = (const bf16*)residual->data_ptr();
+  }
+  auto& wsp = workspace(x.get_device());
+  if (M <= 16) launch<16>(x, w, r, y, wsp);
+  else if (M <= 32) launch<32>(x, w, r, y, wsp);
+  else launch<64>(x, w, r, y, wsp);
+  return y;
+}
+
+// Error code of the last failed wait (0 = none); reading it synchronises the stream.
+int64_t skinny_tma_error() {
+  auto& wsp = skt::workspace(c10::cuda::current_device());
+  return wsp.err.item<int>();
+}
+
+}  // namespace ax
