@@ -25,7 +25,8 @@ std::vector<at::Tensor> attn_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor,
 std::vector<at::Tensor> attn_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
                                  at::Tensor, double);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
-                       double);
+                       double, c10::optional<at::Tensor>);
+void decode_plan(at::Tensor seq_lens, at::Tensor prefix);
 void kv_store(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
 void sqnorm_accumulate(at::Tensor x, at::Tensor acc);
 void adamw_step(at::Tensor, at::Tensor, at::Tensor, at::Tensor, c10::optional<at::Tensor>, int64_t, double, double, double, double,
@@ -85,6 +86,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_fwd_into", &ax::linear_fwd_into);
   m.def("set_streamk_decomposition", &ax::set_streamk_decomposition);
   m.def("router_topk", &ax::router_topk);
+  m.def("decode_plan", &ax::decode_plan);
   m.def("skinny_tma_linear", &ax::skinny_tma_linear);
   m.def("skinny_tma_error", &ax::skinny_tma_error);
   m.def("tp_ar_rms", &ax::tp_ar_rms);

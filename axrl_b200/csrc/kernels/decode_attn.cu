@@ -57,9 +57,8 @@ struct Params {
   float scale_log2;
 };
 
-__global__ void __launch_bounds__(128) decode_k(Params p) {
-  extern __shared__ __align__(128) char smem[];
-  const int b = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
+// One (sequence b, kv head hk, split sp) work item; all threads of the CTA call it together.
+__device__ __forceinline__ void decode_item(const Params& p, char* smem, int b, int hk, int sp) {
   const int len = p.seq_lens[b];
   const int t0 = sp * SPLIT;
   if (t0 >= len) return;
@@ -209,6 +208,43 @@ __global__ void __launch_bounds__(128) decode_k(Params p) {
   }
 }
 
+// Fixed grid: one CTA per (sequence, kv head, split of the cache capacity); CTAs past the end of
+// their sequence exit at once (used by the allocation-free entry point).
+__global__ void __launch_bounds__(128) decode_k(Params p) {
+  extern __shared__ __align__(128) char smem[];
+  decode_item(p, smem, blockIdx.x, blockIdx.y, blockIdx.z);
+}
+
+// Work list of the live (sequence, split) pairs: prefix[b] = sum over earlier sequences of
+// ceil(len / SPLIT).  Computed once per decode step and shared by every layer.
+__global__ void decode_plan_k(const int* __restrict__ seq_lens, int B, int* __restrict__ prefix) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int acc = 0;
+  for (int b = 0; b < B; ++b) {
+    prefix[b] = acc;
+    acc += (seq_lens[b] + SPLIT - 1) / SPLIT;
+  }
+  prefix[B] = acc;
+}
+
+// Persistent grid sized to the SMs: each CTA walks work items (kv head fastest), so the launch
+// costs the live work only, not B x Hkv x (capacity / SPLIT) mostly-empty CTAs.
+__global__ void __launch_bounds__(128) decode_persist_k(Params p, const int* __restrict__ prefix, int B) {
+  extern __shared__ __align__(128) char smem[];
+  const int total = prefix[B] * p.Hkv;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const int hk = w % p.Hkv, j = w / p.Hkv;
+    int lo = 0, hi = B - 1;  // last b with prefix[b] <= j
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= j) lo = mid;
+      else hi = mid - 1;
+    }
+    __syncthreads();  // the previous item's merge buffer aliases this item's K/V tiles
+    decode_item(p, smem, lo, hk, j - prefix[lo]);
+  }
+}
+
 // out[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s ; one warp per (b, h)
 __global__ void combine_k(const float* __restrict__ part_o, const float* __restrict__ part_ml, const int* __restrict__ seq_lens,
                           bf16* __restrict__ out, int B, int Hq, int splits) {
@@ -314,8 +350,15 @@ void decode_advance(int64_t B, at::Tensor out_tok, at::Tensor out_lp, at::Tensor
 
 // q (B,Hq,128); caches (pages,Hkv,P,128); block_table (B,max_pages) int32; seq_lens (B,) int32.
 // `splits` is fixed by the caller (ceil(max_context / 256)) so the launch shape is static.
+void decode_plan(at::Tensor seq_lens, at::Tensor prefix) {
+  int B = seq_lens.numel();
+  AX_CHECK(prefix.scalar_type() == at::kInt && prefix.numel() >= B + 1, "prefix: int32 (B + 1)");
+  dec::decode_plan_k<<<1, 32, 0, stream()>>>(seq_lens.data_ptr<int>(), B, prefix.data_ptr<int>());
+  AX_LAUNCH_OK();
+}
+
 void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table, at::Tensor seq_lens, at::Tensor out,
-                       at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale) {
+                       at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, c10::optional<at::Tensor> prefix) {
   using namespace dec;
   int B = q.size(0), Hq = q.size(1), Hkv = kc.size(1), P = kc.size(2);
   AX_CHECK(q.size(2) == D && kc.size(3) == D, "head_dim 128");
@@ -330,9 +373,15 @@ void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bl
   static bool attr = false;
   if (!attr) {
     AX_CUDA_OK(cudaFuncSetAttribute(decode_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    AX_CUDA_OK(cudaFuncSetAttribute(decode_persist_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  decode_k<<<dim3(B, Hkv, splits), 128, smem, stream()>>>(p);
+  if (prefix.has_value()) {  // planned: persistent grid over the live work items
+    AX_CHECK(prefix->scalar_type() == at::kInt && prefix->numel() >= B + 1, "prefix: int32 (B + 1)");
+    decode_persist_k<<<num_sms() * 3, 128, smem, stream()>>>(p, prefix->data_ptr<int>(), B);
+  } else {
+    decode_k<<<dim3(B, Hkv, splits), 128, smem, stream()>>>(p);
+  }
   AX_LAUNCH_OK();
   long w = (long)B * Hq;
   combine_k<<<(w * 32 + 255) / 256, 256, 0, stream()>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(), seq_lens.data_ptr<int>(),

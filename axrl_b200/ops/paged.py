@@ -61,14 +61,24 @@ class DecodeWorkspace:
         self.splits = max(1, math.ceil(max_context / SPLIT_TOKENS))
         self.part_o = torch.empty(max_batch * hq * self.splits * 128, dtype=torch.float32, device=device)
         self.part_ml = torch.empty(max_batch * hq * self.splits * 2, dtype=torch.float32, device=device)
+        self.prefix = torch.zeros(max_batch + 1, dtype=torch.int32, device=device)
+
+    def plan(self, seq_lens: torch.Tensor) -> None:
+        """Work list of live (sequence, split) pairs for ``seq_lens``; every layer of a step reuses it."""
+        if seq_lens.is_cuda:
+            _ext.ext().decode_plan(seq_lens, self.prefix)
 
 
-def paged_decode_attention(q, k_cache, v_cache, block_table, seq_lens, ws: DecodeWorkspace | None, scale: float | None = None):  # noqa: ANN001, ANN201
+def paged_decode_attention(q, k_cache, v_cache, block_table, seq_lens, ws: DecodeWorkspace | None, scale: float | None = None,  # noqa: ANN001, ANN201
+                           planned: bool = False):
+    """``planned=True``: ``ws.plan(seq_lens)`` already ran for these lengths (once per decode step)."""
     scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
     if not q.is_cuda:
         return decode_attention_ref(q, k_cache, v_cache, block_table, seq_lens, scale)
     out = torch.empty_like(q)
-    _ext.ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, out, ws.part_o, ws.part_ml, ws.splits, scale)
+    if not planned:
+        ws.plan(seq_lens)
+    _ext.ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, out, ws.part_o, ws.part_ml, ws.splits, scale, ws.prefix)
     return out
 
 

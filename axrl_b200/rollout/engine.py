@@ -687,8 +687,11 @@ class RolloutEngine:
     def _decode_body(self, bucket: int, capture=None) -> None:  # noqa: ANN001
         st = self.st
         tok, pos, bt, lens, slots = st["tok"][:bucket], st["pos"][:bucket], st["bt"][:bucket], st["len"][:bucket], st["slot"][:bucket]
+        if self.ws is not None:
+            self.ws.plan(lens)  # one work list for all layers of this step
         h = self._embed(tok)
-        h = self._layers(h, pos, slots, lambda li, q, k, v: paged.paged_decode_attention(q, self.kv[li, 0], self.kv[li, 1], bt, lens, self.ws), capture)
+        h = self._layers(h, pos, slots, lambda li, q, k, v: paged.paged_decode_attention(q, self.kv[li, 0], self.kv[li, 1], bt, lens, self.ws, planned=True),
+                         capture)
         logits = self._logits(h)
         if self.filtered_mode:
             t, l = paged.sample_filtered(logits, st["temp"][:bucket], st["top_k"][:bucket], st["top_p"][:bucket], st["min_p"][:bucket],

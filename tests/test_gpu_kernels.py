@@ -226,6 +226,16 @@ def test_paged_decode_attention():
     o = paged_decode_attention(q, kc, vc, bt, lens, ws)
     r = decode_attention_ref(q, kc, vc, bt, lens, 1 / math.sqrt(D))
     close(o, r, 2e-2)
+    # persistent work-list kernel after an in-place length change (plan once, reuse per layer)
+    lens.copy_(torch.tensor([129, 2, 2500, 0 + 1, 640], dtype=torch.int32, device=DEV))
+    for b in range(B):
+        n = (int(lens[b]) + P - 1) // P
+        bt[b, :n] = torch.randint(0, pages, (n,), device=DEV, dtype=torch.int32)
+    ws.plan(lens)
+    for _ in range(2):
+        o = paged_decode_attention(q, kc, vc, bt, lens, ws, planned=True)
+        close(o, decode_attention_ref(q, kc, vc, bt, lens, 1 / math.sqrt(D)), 2e-2)
+    assert ws.prefix[:B + 1].tolist() == [0, 2, 3, 23, 24, 29]
 
 
 def test_adamw_and_sqnorm():
