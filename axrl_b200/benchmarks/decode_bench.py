@@ -1,7 +1,7 @@
 """Rollout-engine microbenchmark: prefill + decode throughput of a Qwen3-shaped model.
 
-python -m axrl_b200.benchmarks.decode_bench --model qwen3-8b --batch 256 --prompt 512 --new 256
-Reports device-timed prefill seconds, decode ms/step and decode tokens/s (CUDA events).
+python -m axrl_b200.benchmarks.decode_bench --model qwen3-8b --batch 256 --prompt 512 --new 256 [--pdl 0]
+(AXRL_DECODE_GEMM=skinny|tma|tcgen05 forces the decode-size GEMM kernel.)  Reports device-timed prefill seconds, decode ms/step and decode tokens/s (CUDA events).
 """
 
 from __future__ import annotations
@@ -21,7 +21,13 @@ def main() -> None:
     ap.add_argument("--group", type=int, default=8)
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--burst", type=int, default=16)
+    ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch of the decode kernels (0 = off)")
     a = ap.parse_args()
+    import os
+
+    from axrl_b200.ops import _ext
+
+    _ext.ext().set_pdl(bool(a.pdl))
 
     from axrl_b200.models.qwen3 import Qwen3Model, resolve_preset
     from axrl_b200.rollout.engine import GenRequest, RolloutEngine
@@ -58,7 +64,7 @@ def main() -> None:
                       "prefill_s": round(st["prefill_s"], 3), "decode_s": round(st["decode_s"], 3),
                       "decode_ms_per_step": round(1000 * st["decode_s"] / max(1, st["decode_steps"]), 3),
                       "decode_tok_per_s": round(st["decode_tokens"] / max(1e-9, st["decode_s"]), 1), "bursts": st["bursts"],
-                      "graph": not a.eager}))
+                      "graph": not a.eager, "pdl": bool(a.pdl), "decode_gemm": os.environ.get("AXRL_DECODE_GEMM", "default")}))
     eng.release_graphs()
 
 

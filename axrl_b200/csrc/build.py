@@ -137,7 +137,7 @@ def build(jobs: int | None = None, force: bool = False, only: str | None = None)
     targets = {
         "_C": (sorted(glob.glob(os.path.join(HERE, "kernels", "*.cu"))) + sorted(glob.glob(os.path.join(HERE, "kernels", "*.cpp"))),
                [*tflags, f"-I{cut}", f"-I{os.path.join(os.path.dirname(cut), 'tools', 'util', 'include')}", f"-I{HERE}",
-                f"-I{cuda_home}/include"],
+                f"-I{cuda_home}/include", "-DCUTLASS_ENABLE_GDC_FOR_SM100"],
                [*tlink, f"-L{cuda_home}/lib64", f"-L{cuda_home}/lib64/stubs", "-lcudart", "-lcuda", f"-Wl,-rpath,{cuda_home}/lib64"]),
         "_runtime": (sorted(glob.glob(os.path.join(HERE, "runtime", "*.cpp"))) + sorted(glob.glob(os.path.join(HERE, "runtime", "*.cu"))),
                      [f"-I{sysconfig.get_paths()['include']}", f"-I{_pybind11_include()}", f"-I{HERE}", f"-I{cuda_home}/include"],

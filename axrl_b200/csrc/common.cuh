@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <utility>
+
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -80,6 +83,48 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
   __syncthreads();
   v = lane < nw ? sh[lane] : 0.f;
   return warp_sum(v);
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with launch_pdl() may be scheduled while its stream predecessor is still
+// running: as soon as every CTA of the predecessor has executed pdl_trigger() (or exited).  Every
+// thread of such a kernel executes pdl_wait() before it reads memory that earlier work writes and
+// before it writes memory that earlier work may still read; pdl_wait() returns once the
+// predecessor grid has completed and its writes are visible.  Only reads of data that no recent
+// kernel writes (weights during a rollout, see weights_static()) may be issued before it.  Every
+// kernel launched this way waits unconditionally, so a grid completes only after its predecessor,
+// and ordering stays transitive along the stream.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline bool& pdl_enabled() {
+  static bool on = [] {
+    const char* e = std::getenv("AXRL_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Set while the rollout engine decodes: the weight matrices are then read-only, so weight-streaming
+// GEMMs may start loading them before their predecessor finishes.
+inline bool& weights_static() {
+  static bool on = false;
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  AX_CUDA_OK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
 constexpr float kLog2e = 1.4426950408889634f;

@@ -43,6 +43,9 @@ void sync_push(at::Tensor, at::Tensor, at::Tensor, int64_t);
 at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual);
 void linear_fwd_into(at::Tensor x, at::Tensor w, at::Tensor out);
 void set_streamk_decomposition(int64_t mode, int64_t splits);
+void set_pdl(bool on);
+bool get_pdl();
+void set_weights_static(bool on);
 at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 int64_t skinny_tma_error();
 std::vector<at::Tensor> router_topk(at::Tensor, int64_t, bool, c10::optional<at::Tensor>, c10::optional<at::Tensor>);
@@ -85,6 +88,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_fwd", &ax::linear_fwd);
   m.def("linear_fwd_into", &ax::linear_fwd_into);
   m.def("set_streamk_decomposition", &ax::set_streamk_decomposition);
+  m.def("set_pdl", &ax::set_pdl);
+  m.def("get_pdl", &ax::get_pdl);
+  m.def("set_weights_static", &ax::set_weights_static);
   m.def("router_topk", &ax::router_topk);
   m.def("decode_plan", &ax::decode_plan);
   m.def("skinny_tma_linear", &ax::skinny_tma_linear);

@@ -218,6 +218,8 @@ __global__ void __launch_bounds__(128) decode_k(Params p) {
 // Work list of the live (sequence, split) pairs: prefix[b] = sum over earlier sequences of
 // ceil(len / SPLIT).  Computed once per decode step and shared by every layer.
 __global__ void decode_plan_k(const int* __restrict__ seq_lens, int B, int* __restrict__ prefix) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int acc = 0;
   for (int b = 0; b < B; ++b) {
@@ -230,6 +232,8 @@ __global__ void decode_plan_k(const int* __restrict__ seq_lens, int B, int* __re
 // Persistent grid sized to the SMs: each CTA walks work items (kv head fastest), so the launch
 // costs the live work only, not B x Hkv x (capacity / SPLIT) mostly-empty CTAs.
 __global__ void __launch_bounds__(128) decode_persist_k(Params p, const int* __restrict__ prefix, int B) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) char smem[];
   const int total = prefix[B] * p.Hkv;
   for (int w = blockIdx.x; w < total; w += gridDim.x) {
@@ -248,6 +252,8 @@ __global__ void __launch_bounds__(128) decode_persist_k(Params p, const int* __r
 // out[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s ; one warp per (b, h)
 __global__ void combine_k(const float* __restrict__ part_o, const float* __restrict__ part_ml, const int* __restrict__ seq_lens,
                           bf16* __restrict__ out, int B, int Hq, int splits) {
+  pdl_wait();
+  pdl_trigger();
   int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (w >= B * Hq) return;
   int b = w / Hq;
@@ -297,6 +303,8 @@ __global__ void decode_advance_k(int B, const int64_t* __restrict__ out_tok, con
                                  const int* __restrict__ stop_on_eos, int64_t eos, int64_t* __restrict__ forced,
                                  int64_t* __restrict__ ring_tok, float* __restrict__ ring_lp, int* __restrict__ ring_step,
                                  int ring_cap, int ring_ld, int64_t scratch_slot, int64_t* __restrict__ seed) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int step;
   if (threadIdx.x == 0) step = ring_step[0];
   __syncthreads();
@@ -340,7 +348,7 @@ void decode_advance(int64_t B, at::Tensor out_tok, at::Tensor out_lp, at::Tensor
                     at::Tensor seed) {
   AX_CHECK(B <= 1024, "decode batch must be <= 1024");
   if (B == 0) return;
-  dec::decode_advance_k<<<1, 256, 0, stream()>>>(
+  launch_pdl(dec::decode_advance_k, dim3(1), dim3(256), 0, stream(),
       (int)B, out_tok.data_ptr<int64_t>(), out_lp.data_ptr<float>(), tok.data_ptr<int64_t>(), pos.data_ptr<int>(), len.data_ptr<int>(),
       slot.data_ptr<int64_t>(), bt.data_ptr<int>(), (int)bt.size(1), (int)P, end_total.data_ptr<int>(), force_eos.data_ptr<int>(),
       stop_on_eos.data_ptr<int>(), eos, forced.data_ptr<int64_t>(), ring_tok.data_ptr<int64_t>(), ring_lp.data_ptr<float>(),
@@ -353,7 +361,7 @@ void decode_advance(int64_t B, at::Tensor out_tok, at::Tensor out_lp, at::Tensor
 void decode_plan(at::Tensor seq_lens, at::Tensor prefix) {
   int B = seq_lens.numel();
   AX_CHECK(prefix.scalar_type() == at::kInt && prefix.numel() >= B + 1, "prefix: int32 (B + 1)");
-  dec::decode_plan_k<<<1, 32, 0, stream()>>>(seq_lens.data_ptr<int>(), B, prefix.data_ptr<int>());
+  launch_pdl(dec::decode_plan_k, dim3(1), dim3(32), 0, stream(), seq_lens.data_ptr<int>(), B, prefix.data_ptr<int>());
   AX_LAUNCH_OK();
 }
 
@@ -378,14 +386,14 @@ void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bl
   }
   if (prefix.has_value()) {  // planned: persistent grid over the live work items
     AX_CHECK(prefix->scalar_type() == at::kInt && prefix->numel() >= B + 1, "prefix: int32 (B + 1)");
-    decode_persist_k<<<num_sms() * 3, 128, smem, stream()>>>(p, prefix->data_ptr<int>(), B);
+    launch_pdl(decode_persist_k, dim3(num_sms() * 3), dim3(128), smem, stream(), p, (const int*)prefix->data_ptr<int>(), B);
   } else {
     decode_k<<<dim3(B, Hkv, splits), 128, smem, stream()>>>(p);
   }
   AX_LAUNCH_OK();
   long w = (long)B * Hq;
-  combine_k<<<(w * 32 + 255) / 256, 256, 0, stream()>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(), seq_lens.data_ptr<int>(),
-                                                       (bf16*)out.data_ptr(), B, Hq, (int)splits);
+  launch_pdl(combine_k, dim3((w * 32 + 255) / 256), dim3(256), 0, stream(), (const float*)part_o.data_ptr<float>(),
+             (const float*)part_ml.data_ptr<float>(), (const int*)seq_lens.data_ptr<int>(), (bf16*)out.data_ptr(), B, Hq, (int)splits);
   AX_LAUNCH_OK();
 }
 

@@ -116,7 +116,9 @@ struct Gemm {
     }
     auto s1 = op.initialize(args, wsp, st);
     TORCH_CHECK(s1 == cutlass::Status::kSuccess, "GEMM init failed");
-    auto s2 = op.run(st);
+    // programmatic dependent launch: the kernel's load warps wait for the predecessor grid
+    // (CUTLASS_ENABLE_GDC_FOR_SM100), so its prologue overlaps the predecessor's tail
+    auto s2 = op.run(st, nullptr, pdl_enabled());
     TORCH_CHECK(s2 == cutlass::Status::kSuccess, "GEMM run failed");
   }
 };

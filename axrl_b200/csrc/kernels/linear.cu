@@ -1,6 +1,8 @@
 // torch-facing GEMM wrappers used by ops.linear / ops.logprob / the rollout engine.
 // Tile-config choice by M (tokens): >= 512 -> 2-SM 256x256 data-parallel tiles;
 // 65..511 -> 1-SM 128x128 stream-K; <= 64 -> 1-SM 128x64 stream-K (decode: weight streaming).
+#include <string>
+
 #include "common.cuh"
 #include "gemm_sm100.cuh"
 
@@ -15,12 +17,50 @@ static void check_bf16_2d(const at::Tensor& t, const char* n) {
 
 at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
+at::Tensor skinny_linear_out(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual, c10::optional<at::Tensor> out);
+at::Tensor skinny_tma_linear_out(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual, c10::optional<at::Tensor> out);
 
 static void tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K) {
   if (M >= 512) gemm::tn_sm2(A, B, C, D, M, N, K, stream());
   else if (M > 64) gemm::tn_sm1_sk(A, B, C, D, M, N, K, stream());
   else gemm::tn_narrow_sk(A, B, C, D, M, N, K, stream());
 }
+
+// Decode-size GEMMs are reads of the weight matrix.  Measured on B200 (bf16, L2 flushed between
+// calls): up to 16 activation rows and 64M weight elements the streaming kernels (skinny_gemm.cu,
+// cp.async ring; skinny_tma.cu, TMA ring) beat the tcgen05 swap-AB GEMM by 10-40%; from 32 rows on
+// and for the large gate/up and vocabulary matrices the tcgen05 GEMM streams at least as fast.
+// AXRL_DECODE_GEMM = skinny | tma | tcgen05 overrides the choice (benchmarking).
+enum DecodeGemm { kTcgen05 = 0, kSkinny = 1, kTma = 2 };
+
+static int decode_gemm_mode() {
+  static int mode = [] {
+    const char* e = std::getenv("AXRL_DECODE_GEMM");
+    if (!e) return -1;
+    std::string v(e);
+    return v == "skinny" ? (int)kSkinny : v == "tma" ? (int)kTma : v == "tcgen05" ? (int)kTcgen05 : -1;
+  }();
+  return mode;
+}
+
+static DecodeGemm decode_gemm(int M, int N, int K) {
+  if (M > 16 || K % 64 || N % 8 || (long)N * K > (64L << 20)) return kTcgen05;
+  const int forced = decode_gemm_mode();
+  return forced >= 0 ? (DecodeGemm)forced : kSkinny;
+}
+
+static bool streaming_into(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& r, at::Tensor& y) {
+  const int M = x.size(0), N = w.size(0), K = x.size(1);
+  const DecodeGemm g = decode_gemm(M, N, K);
+  if (g == kTcgen05) return false;
+  if (g == kSkinny) skinny_linear_out(x, w, r, y);
+  else skinny_tma_linear_out(x, w, r, y);
+  return true;
+}
+
+void set_pdl(bool on) { pdl_enabled() = on; }
+bool get_pdl() { return pdl_enabled(); }
+void set_weights_static(bool on) { weights_static() = on; }
 
 void set_streamk_decomposition(int64_t mode, int64_t splits) {
   AX_CHECK(mode >= 0 && mode <= 3 && splits >= 0, "mode 0..3, splits >= 0");
@@ -37,8 +77,13 @@ at::Tensor linear_fwd(at::Tensor x, at::Tensor w) {
   auto y = at::empty({M, N}, x.options());
   if (M == 0 || N == 0) return y;
   if (K == 0) return y.zero_();
-  if (M <= 64) gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K, stream());  // decode: weight streaming
-  else tn(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K);
+  if (M <= 64) {  // decode: weight streaming
+    if (decode_gemm(M, N, K) == kSkinny) return skinny_linear(x, w, c10::nullopt);
+    if (decode_gemm(M, N, K) == kTma) return skinny_tma_linear(x, w, c10::nullopt);
+    gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K, stream());
+  } else {
+    tn(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K);
+  }
   return y;
 }
 
@@ -51,8 +96,13 @@ at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual) {
   AX_CHECK(residual.size(0) == M && residual.size(1) == N, "residual shape");
   auto y = at::empty({M, N}, x.options());
   if (M == 0 || N == 0) return y;
-  if (M <= 64) gemm::tn_swapab(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K, stream());
-  else tn(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K);
+  if (M <= 64) {
+    if (decode_gemm(M, N, K) == kSkinny) return skinny_linear(x, w, residual);
+    if (decode_gemm(M, N, K) == kTma) return skinny_tma_linear(x, w, residual);
+    gemm::tn_swapab(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K, stream());
+  } else {
+    tn(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K);
+  }
   return y;
 }
 
@@ -64,8 +114,12 @@ void linear_fwd_into(at::Tensor x, at::Tensor w, at::Tensor out) {
   int M = x.size(0), N = w.size(0), K = x.size(1);
   AX_CHECK(out.size(0) == M && out.size(1) == N && w.size(1) == K, "shapes");
   if (M == 0 || N == 0) return;
-  if (M <= 64) gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, out.data_ptr(), M, N, K, stream());
-  else tn(x.data_ptr(), w.data_ptr(), nullptr, out.data_ptr(), M, N, K);
+  if (M <= 64) {
+    if (streaming_into(x, w, c10::nullopt, out)) return;
+    gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, out.data_ptr(), M, N, K, stream());
+  } else {
+    tn(x.data_ptr(), w.data_ptr(), nullptr, out.data_ptr(), M, N, K);
+  }
 }
 
 // out[M,K] = dy[M,N] @ w[N,K] into caller-provided rows

@@ -9,6 +9,8 @@ namespace ax {
 // One CTA per row; row re-read from L1/L2 on the second pass.
 __global__ void rmsnorm_fwd_k(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ y,
                               float* __restrict__ rstd, int H, float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sh[32];
   const bf16* xr = x + (size_t)blockIdx.x * H;
   bf16* yr = y + (size_t)blockIdx.x * H;
@@ -82,7 +84,7 @@ std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps) {
   auto rstd = at::empty({T}, x.options().dtype(at::kFloat));
   if (T == 0) return {y, rstd};
   int thr = H >= 2048 ? 256 : 128;
-  rmsnorm_fwd_k<<<T, thr, 0, stream()>>>((const bf16*)x.data_ptr(), (const bf16*)wb.data_ptr(), (bf16*)y.data_ptr(),
+  launch_pdl(rmsnorm_fwd_k, dim3(T), dim3(thr), 0, stream(), (const bf16*)x.data_ptr(), (const bf16*)wb.data_ptr(), (bf16*)y.data_ptr(),
                                         rstd.data_ptr<float>(), H, (float)eps);
   AX_LAUNCH_OK();
   return {y, rstd};
@@ -115,6 +117,8 @@ __global__ void qknorm_rope_fwd_k(const bf16* __restrict__ qkv, const bf16* __re
                                   bf16* __restrict__ q, bf16* __restrict__ k, bf16* __restrict__ v,
                                   float* __restrict__ rstd, int T, int nq, int nkv, float eps,
                                   bf16* __restrict__ kc, bf16* __restrict__ vc, const int64_t* __restrict__ slots, int P) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = 128;
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
@@ -250,7 +254,7 @@ std::vector<at::Tensor> qknorm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tenso
   auto qwb = as_bf16(qw), kwb = as_bf16(kw);
   auto p32 = pos.scalar_type() == at::kInt ? pos.contiguous() : pos.to(at::kInt).contiguous();
   auto inv = inv_freq.to(at::kFloat).contiguous();
-  qknorm_rope_fwd_k<false><<<(warps * 32 + 255) / 256, 256, 0, stream()>>>(
+  launch_pdl(qknorm_rope_fwd_k<false>, dim3((warps * 32 + 255) / 256), dim3(256), 0, stream(),
       (const bf16*)qkv.data_ptr(), (const bf16*)qwb.data_ptr(), (const bf16*)kwb.data_ptr(), p32.data_ptr<int>(),
       inv.data_ptr<float>(), (bf16*)q.data_ptr(), (bf16*)k.data_ptr(), (bf16*)v.data_ptr(), rstd.data_ptr<float>(), T, nq,
       nkv, (float)eps, nullptr, nullptr, nullptr, 1);
@@ -271,7 +275,7 @@ std::vector<at::Tensor> qknorm_rope_cache(at::Tensor qkv, at::Tensor qw, at::Ten
   auto q = at::empty({T, nq, D}, opt), k = at::empty({T, nkv, D}, opt), v = at::empty({T, nkv, D}, opt);
   long warps = (long)T * (nq + 2 * nkv);
   if (warps == 0) return {q, k, v};
-  qknorm_rope_fwd_k<true><<<(warps * 32 + 255) / 256, 256, 0, stream()>>>(
+  launch_pdl(qknorm_rope_fwd_k<true>, dim3((warps * 32 + 255) / 256), dim3(256), 0, stream(),
       (const bf16*)qkv.data_ptr(), (const bf16*)qw.data_ptr(), (const bf16*)kw.data_ptr(), pos.data_ptr<int>(),
       inv_freq.data_ptr<float>(), (bf16*)q.data_ptr(), (bf16*)k.data_ptr(), (bf16*)v.data_ptr(), nullptr, T, nq, nkv,
       (float)eps, (bf16*)k_cache.data_ptr(), (bf16*)v_cache.data_ptr(), slots.data_ptr<int64_t>(), (int)k_cache.size(2));
@@ -305,6 +309,8 @@ std::vector<at::Tensor> qknorm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor
 __device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
 
 __global__ void swiglu_fwd_k(const bf16* __restrict__ gu, bf16* __restrict__ y, long T, int F) {
+  pdl_wait();
+  pdl_trigger();
   long n8 = T * (F / 8);
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
     long t = i / (F / 8);
@@ -349,7 +355,7 @@ at::Tensor swiglu_fwd(at::Tensor gu) {
   long n8 = T * (F / 8);
   if (n8 == 0) return y;
   int ctas = (int)std::min<long>((n8 + 255) / 256, num_sms() * 16);
-  swiglu_fwd_k<<<ctas, 256, 0, stream()>>>((const bf16*)gu.data_ptr(), (bf16*)y.data_ptr(), T, F);
+  launch_pdl(swiglu_fwd_k, dim3(ctas), dim3(256), 0, stream(), (const bf16*)gu.data_ptr(), (bf16*)y.data_ptr(), T, F);
   AX_LAUNCH_OK();
   return y;
 }

@@ -74,6 +74,8 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
 
 // out[t, :] = table[ids[t], :]   (bf16 rows, H % 8 == 0)
 __global__ void embed_fwd_k(const int64_t* __restrict__ ids, const bf16* __restrict__ table, bf16* __restrict__ out, int T, int H) {
+  pdl_wait();
+  pdl_trigger();
   long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
   int per = H / 8;
   if (i >= (long)T * per) return;
@@ -101,7 +103,7 @@ at::Tensor embed_fwd(at::Tensor ids, at::Tensor table) {
   auto out = at::empty({T, H}, table.options());
   long n = (long)T * (H / 8);
   if (n == 0) return out;
-  embed_fwd_k<<<(n + 255) / 256, 256, 0, stream()>>>(ids.data_ptr<int64_t>(), (const bf16*)table.data_ptr(), (bf16*)out.data_ptr(), T, H);
+  launch_pdl(embed_fwd_k, dim3((n + 255) / 256), dim3(256), 0, stream(), (const int64_t*)ids.data_ptr<int64_t>(), (const bf16*)table.data_ptr(), (bf16*)out.data_ptr(), T, H);
   AX_LAUNCH_OK();
   return out;
 }

@@ -36,6 +36,7 @@ struct Params {
   float* ws;
   int* cnt;
   int M, N, K, kc, splits;
+  int prefetch_w;  // weights are read-only for this launch: stream them before the predecessor ends
 };
 
 template <int MT>
@@ -50,9 +51,8 @@ __global__ void __launch_bounds__(THREADS) skinny_k(Params p) {
   const int kb1 = min(p.K, kb0 + p.kc);
   const int nk = (kb1 - kb0) / KT;
 
-  auto load = [&](int kb, int slot) {
+  auto load_w = [&](int kb, int slot) {
     char* sw = smem + slot * SB;
-    char* sx = sw + WB;
     const int k = kb0 + kb * KT;
 #pragma unroll
     for (int i = tid; i < NT * 8; i += THREADS) {
@@ -61,6 +61,10 @@ __global__ void __launch_bounds__(THREADS) skinny_k(Params p) {
       bool ok = g < p.N;
       cp16(sw + swz(row, c), p.w + (long)(ok ? g : 0) * p.K + k + c, ok);
     }
+  };
+  auto load_x = [&](int kb, int slot) {
+    char* sx = smem + slot * SB + WB;
+    const int k = kb0 + kb * KT;
     for (int i = tid; i < MT * 8; i += THREADS) {
       int row = i >> 3, c = (i & 7) * 8;
       bool ok = row < p.M;
@@ -68,9 +72,22 @@ __global__ void __launch_bounds__(THREADS) skinny_k(Params p) {
     }
   };
 
+  // Weight slabs of the first stages may be in flight before the predecessor kernel finishes
+  // (programmatic dependent launch); activations, the residual and every write wait for it.  The
+  // early loads join the first commit group, so the pipeline accounting below is unchanged.
+  if (p.prefetch_w) {
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s)
+      if (s < nk) load_w(s, s);
+  }
+  pdl_wait();
+  pdl_trigger();
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
-    if (s < nk) load(s, s);
+    if (s < nk) {
+      if (!p.prefetch_w) load_w(s, s);
+      load_x(s, s);
+    }
     asm volatile("cp.async.commit_group;\n" ::);
   }
 
@@ -81,7 +98,10 @@ __global__ void __launch_bounds__(THREADS) skinny_k(Params p) {
   for (int kb = 0; kb < nk; ++kb) {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(STAGES - 2));
     __syncthreads();
-    if (kb + STAGES - 1 < nk) load(kb + STAGES - 1, (kb + STAGES - 1) % STAGES);
+    if (kb + STAGES - 1 < nk) {
+      load_w(kb + STAGES - 1, (kb + STAGES - 1) % STAGES);
+      load_x(kb + STAGES - 1, (kb + STAGES - 1) % STAGES);
+    }
     asm volatile("cp.async.commit_group;\n" ::);
     const char* sw = smem + (kb % STAGES) * SB;
     const char* sx = sw + WB;
@@ -185,12 +205,13 @@ static Workspace& workspace(int dev) {
 }  // namespace sk
 
 // Y = X @ W^T (+ R) for X with at most 64 rows.
-at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual) {
+at::Tensor skinny_linear_out(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual, c10::optional<at::Tensor> out) {
   using namespace sk;
   AX_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() && w.is_contiguous(), "bf16 contiguous");
   int M = x.size(0), K = x.size(1), N = w.size(0);
   AX_CHECK(M <= 64 && w.size(1) == K && K % KT == 0 && N % 8 == 0, "skinny_linear: M<=64, K%64==0, N%8==0");
-  auto y = at::empty({M, N}, x.options());
+  auto y = out.has_value() ? *out : at::empty({M, N}, x.options());
+  AX_CHECK(y.is_contiguous() && y.size(0) == M && y.size(1) == N, "output shape");
   if (M == 0) return y;
   const bf16* r = nullptr;
   if (residual.has_value()) {
@@ -215,7 +236,8 @@ at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> r
       kc = K;
     }
   }
-  Params p{(const bf16*)x.data_ptr(), (const bf16*)w.data_ptr(), r, (bf16*)y.data_ptr(), ws, cnt, M, N, K, kc, splits};
+  Params p{(const bf16*)x.data_ptr(), (const bf16*)w.data_ptr(), r, (bf16*)y.data_ptr(), ws, cnt, M, N, K, kc, splits,
+           (int)(weights_static() && pdl_enabled())};
   dim3 grid(n_tiles, splits);
   static bool attr_set[3] = {false, false, false};
   auto launch = [&](auto kern, int mt, int which) {
@@ -224,13 +246,17 @@ at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> r
       AX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, STAGES * (NT * KT * 2 + 64 * KT * 2)));
       attr_set[which] = true;
     }
-    kern<<<grid, THREADS, smem, stream()>>>(p);
+    launch_pdl(kern, grid, dim3(THREADS), smem, stream(), p);
   };
   if (M <= 16) launch(skinny_k<16>, 16, 0);
   else if (M <= 32) launch(skinny_k<32>, 32, 1);
   else launch(skinny_k<64>, 64, 2);
   AX_LAUNCH_OK();
   return y;
+}
+
+at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual) {
+  return skinny_linear_out(x, w, residual, c10::nullopt);
 }
 
 }  // namespace ax

@@ -36,6 +36,7 @@ struct Params {
   int* cnt;
   int* err;
   int kslabs, total, per;
+  int prefetch_w;  // weights are read-only for this launch: stream them before the predecessor ends
 };
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -88,8 +89,14 @@ __global__ void __launch_bounds__(THREADS, 1) skinny_tma_k(const __grid_constant
   uint64_t* empty = full + STAGES;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int u0 = blockIdx.x * p.per, u1 = min(p.total, u0 + p.per);
-  if (u0 >= u1) return;
+  if (u0 >= u1) {
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
   if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], CONSUMERS);
@@ -100,17 +107,35 @@ __global__ void __launch_bounds__(THREADS, 1) skinny_tma_k(const __grid_constant
 
   if (warp == CONSUMERS) {  // producer
     if (lane == 0) {
+      // Weight slabs of the first ring pass may be requested before the predecessor kernel ends
+      // (programmatic dependent launch); activation slabs only after it.
+      const int npre = p.prefetch_w ? min(STAGES, u1 - u0) : 0;
+      for (int i = 0; i < npre; ++i) {
+        const int u = u0 + i, t = u / p.kslabs, k = (u % p.kslabs) * KT;
+        mbar_expect_tx(&full[i], WB + XB);
+        tma_2d(sW + i * WB, &tw, k, t * NT, &full[i]);
+      }
+      pdl_wait();
+      pdl_trigger();
       for (int u = u0, i = 0; u < u1; ++u, ++i) {
         const int s = i % STAGES;
+        const int t = u / p.kslabs, k = (u % p.kslabs) * KT;
+        if (i < npre) {
+          tma_2d(sX + s * XB, &tx, k, 0, &full[s]);
+          continue;
+        }
         if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, p.err, 1)) return;
         mbar_expect_tx(&full[s], WB + XB);
-        const int t = u / p.kslabs, k = (u % p.kslabs) * KT;
         tma_2d(sW + s * WB, &tw, k, t * NT, &full[s]);
         tma_2d(sX + s * XB, &tx, k, 0, &full[s]);
       }
+    } else {
+      pdl_wait();
     }
     return;
   }
+  pdl_wait();
+  pdl_trigger();
 
   float acc[MT / 16][4][4];
   auto zero = [&]() {
@@ -250,6 +275,7 @@ static void launch(const at::Tensor& x, const at::Tensor& w, const bf16* r, at::
   Params p;
   p.M = M, p.N = N, p.K = K, p.r = r, p.y = (bf16*)y.data_ptr(), p.ws = wsp.ws.data_ptr<float>(), p.cnt = wsp.cnt.data_ptr<int>();
   p.err = wsp.err.data_ptr<int>();
+  p.prefetch_w = weights_static() && pdl_enabled();
   p.kslabs = K / KT;
   const int tiles = (N + NT - 1) / NT;
   p.total = tiles * p.kslabs;
@@ -264,20 +290,21 @@ static void launch(const at::Tensor& x, const at::Tensor& w, const bf16* r, at::
     AX_CHECK(cudaFuncSetAttribute(skinny_tma_k<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess, "smem attribute");
     attr_set = true;
   }
-  skinny_tma_k<MT><<<used, THREADS, smem, stream()>>>(tw, tx, p);
+  launch_pdl(skinny_tma_k<MT>, dim3(used), dim3(THREADS), smem, stream(), tw, tx, p);
   AX_LAUNCH_OK();
 }
 
 }  // namespace skt
 
 // Y = X @ W^T (+ R) for X with at most 64 rows (decode), TMA-fed weight streaming.
-at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual) {
+at::Tensor skinny_tma_linear_out(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual, c10::optional<at::Tensor> out) {
   using namespace skt;
   AX_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() && w.is_contiguous(), "bf16 contiguous");
   const int M = x.size(0), K = x.size(1), N = w.size(0);
   AX_CHECK(M >= 1 && M <= 64 && w.size(1) == K && K % KT == 0 && N % 8 == 0 && N <= 262144, "skinny_tma: M<=64, K%64==0, N%8==0");
   AX_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "16-byte aligned");
-  auto y = at::empty({M, N}, x.options());
+  auto y = out.has_value() ? *out : at::empty({M, N}, x.options());
+  AX_CHECK(y.is_contiguous() && y.size(0) == M && y.size(1) == N, "output shape");
   const bf16* r = nullptr;
   if (residual.has_value()) {
     AX_CHECK(residual->is_contiguous() && residual->size(0) == M && residual->size(1) == N, "residual shape");
@@ -288,6 +315,10 @@ at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tenso
   else if (M <= 32) launch<32>(x, w, r, y, wsp);
   else launch<64>(x, w, r, y, wsp);
   return y;
+}
+
+at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual) {
+  return skinny_tma_linear_out(x, w, residual, c10::nullopt);
 }
 
 // Error code of the last failed wait (0 = none); reading it synchronises the stream.

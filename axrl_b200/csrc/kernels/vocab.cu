@@ -155,6 +155,8 @@ __device__ __forceinline__ void argmax_merge(ArgMax& a, float v, int i) {
 template <typename T>
 __global__ void sample_part_k(const T* __restrict__ logits, int V, const float* __restrict__ temp, const int64_t* __restrict__ seed,
                               const int* __restrict__ row_ids, float4* __restrict__ part) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ ArgMax shm[32];
   int row = blockIdx.x, S = gridDim.y, sp = blockIdx.y;
   int chunk = (V + S - 1) / S, j0 = sp * chunk, j1 = min(V, j0 + chunk);
@@ -192,6 +194,8 @@ __global__ void sample_part_k(const T* __restrict__ logits, int V, const float* 
 template <typename T>
 __global__ void sample_merge_k(const T* __restrict__ logits, int V, int S, const float* __restrict__ temp, const float4* __restrict__ part,
                                const int64_t* __restrict__ forced, int64_t* __restrict__ out_tok, float* __restrict__ out_lp, int B) {
+  pdl_wait();
+  pdl_trigger();
   int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (row >= B) return;
   LseAcc a{-INFINITY, 0.f, 0.f};
@@ -228,16 +232,16 @@ void sample_tokens(at::Tensor logits, at::Tensor temperature, at::Tensor seed, a
   dim3 g1(B, S);
   int wb = (B * 32 + 255) / 256;
   if (logits.scalar_type() == at::kFloat) {
-    sample_part_k<float><<<g1, 256, 0, stream()>>>(logits.data_ptr<float>(), V, temperature.data_ptr<float>(), seed.data_ptr<int64_t>(), rid,
+    launch_pdl(sample_part_k<float>, g1, dim3(256), 0, stream(), (const float*)logits.data_ptr<float>(), V, temperature.data_ptr<float>(), seed.data_ptr<int64_t>(), rid,
                                                   reinterpret_cast<float4*>(part.data_ptr<float>()));
-    sample_merge_k<float><<<wb, 256, 0, stream()>>>(logits.data_ptr<float>(), V, S, temperature.data_ptr<float>(),
+    launch_pdl(sample_merge_k<float>, dim3(wb), dim3(256), 0, stream(), (const float*)logits.data_ptr<float>(), V, S, temperature.data_ptr<float>(),
                                                    reinterpret_cast<float4*>(part.data_ptr<float>()), fz, out_tok.data_ptr<int64_t>(),
                                                    out_lp.data_ptr<float>(), B);
   } else {
     AX_CHECK(logits.scalar_type() == at::kBFloat16, "logits bf16/fp32");
-    sample_part_k<bf16><<<g1, 256, 0, stream()>>>((const bf16*)logits.data_ptr(), V, temperature.data_ptr<float>(), seed.data_ptr<int64_t>(),
+    launch_pdl(sample_part_k<bf16>, g1, dim3(256), 0, stream(), (const bf16*)logits.data_ptr(), V, temperature.data_ptr<float>(), seed.data_ptr<int64_t>(),
                                                  rid, reinterpret_cast<float4*>(part.data_ptr<float>()));
-    sample_merge_k<bf16><<<wb, 256, 0, stream()>>>((const bf16*)logits.data_ptr(), V, S, temperature.data_ptr<float>(),
+    launch_pdl(sample_merge_k<bf16>, dim3(wb), dim3(256), 0, stream(), (const bf16*)logits.data_ptr(), V, S, temperature.data_ptr<float>(),
                                                   reinterpret_cast<float4*>(part.data_ptr<float>()), fz, out_tok.data_ptr<int64_t>(),
                                                   out_lp.data_ptr<float>(), B);
   }

@@ -318,9 +318,19 @@ class RolloutEngine:
         return out
 
     def step(self) -> list[GenResult]:
-        finished = self._admit()
-        if self.running:
-            finished += self._decode_burst()
+        if not self.is_cuda:
+            finished = self._admit()
+            return finished + (self._decode_burst() if self.running else [])
+        # weights are read-only while the engine steps: weight-streaming GEMMs may start loading
+        # them before the preceding kernel ends (programmatic dependent launch)
+        e = _ext.ext()
+        e.set_weights_static(True)
+        try:
+            finished = self._admit()
+            if self.running:
+                finished += self._decode_burst()
+        finally:
+            e.set_weights_static(False)
         return finished
 
     # ------------------------------------------------------------------ admission + prefill

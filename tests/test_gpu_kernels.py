@@ -453,3 +453,39 @@ def test_skinny_tma_gemm_matches_fp32(M):
             y = e.linear_variant(x, w, "tma")
             torch.testing.assert_close(y.float(), ref, atol=2e-2, rtol=2e-2)
     assert e.skinny_tma_error() == 0
+
+
+@pytest.mark.parametrize("variant", ["skinny", "tma"])
+def test_decode_gemm_chain_with_programmatic_launch(variant):
+    """Decode-size GEMMs launched with programmatic dependent launch and early weight loads: each
+    GEMM must read the activation its predecessor (RMSNorm) just wrote, add the residual that an
+    earlier GEMM wrote, and write into caller-provided rows; checked against fp32 over a chain of
+    dependent launches with changing data."""
+    e = _ext()
+    torch.manual_seed(3)
+    H, N = 1024, 1536
+    w1 = (torch.randn(N, H, device=DEV) * 0.03).bfloat16()
+    w2 = (torch.randn(H, N, device=DEV) * 0.03).bfloat16()
+    g = torch.ones(H, device=DEV).bfloat16()
+    e.set_pdl(True)
+    e.set_weights_static(True)
+    try:
+        for M in (1, 8, 13):
+            h = torch.randn(M, H, device=DEV).bfloat16()
+            for _ in range(4):
+                x = e.rmsnorm_fwd(h, g, 1e-6)[0]
+                y = e.linear_variant(x, w1, variant) if variant == "tma" else e.linear_fwd(x, w1)
+                out = torch.empty(M, H, device=DEV, dtype=torch.bfloat16)
+                e.linear_fwd_into(y, w2, out)
+                h2 = e.linear_residual(y, w2, h)
+                xr = h.float() * torch.rsqrt(h.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+                yr = xr.bfloat16().float() @ w1.float().t()
+                close(y, yr, 3e-2, 2e-2, msg=f"first GEMM M={M}")
+                o_ref = y.float() @ w2.float().t()
+                close(out, o_ref, 3e-2, 2e-2, msg=f"GEMM into rows M={M}")
+                close(h2, o_ref + h.float(), 3e-2, 2e-2, msg=f"residual GEMM M={M}")
+                h = h2
+    finally:
+        e.set_weights_static(False)
+    torch.cuda.synchronize()
+    assert e.skinny_tma_error() == 0
