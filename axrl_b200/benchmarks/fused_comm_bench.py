@@ -1,0 +1,161 @@
+"""Fused compute + collective paths against their NCCL baselines, as a fraction of the roofline.
+
+Run under torchrun, one rank per GPU (N = 2..8):
+
+* ``tp``: tensor-parallel GEMMs of the Qwen3-8B MLP with sequence parallelism, T tokens:
+  all-gather -> GEMM (``ag_linear``: (T/N, 4096) gathered, times the (2*12288/N, 4096) gate/up
+  shard) and GEMM -> reduce-scatter (``linear_rs``: (T, 12288/N) times the (4096, 12288/N) down
+  shard, rows reduce-scattered), NVLink P2P kernels (``parallel/tp_overlap.py``) vs NCCL
+  all-gather / reduce-scatter around the same GEMM.
+* ``ep``: one MoE layer of the Qwen3-30B-A3B shape (hidden 2048, 128 experts, top-8, expert FFN
+  768) with EP=N: routing, dispatch, grouped expert FFN, combine; NVLink device-side
+  dispatch/combine (``parallel/ep_p2p.py``) vs NCCL all-to-all (``parallel/expert.py``).
+
+Roofline of a fused path: the slower of its FLOPs at the measured bf16 GEMM peak and the bytes
+each GPU must receive over NVLink at the measured 770 GB/s per direction.  Every time is CUDA-event
+device time, max over ranks, median of ``--iters`` after ``--warmup`` iterations.
+
+torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m axrl_b200.benchmarks.fused_comm_bench [--paths tp,ep] [--tokens 16384]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction per GPU
+
+
+def _peaks() -> tuple[float, float]:
+    here = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    try:
+        with open(os.path.join(here, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk.get("bf16_tflops", 1590.0)), float(pk.get("hbm_gbs", 6650.0))
+    except (OSError, ValueError):
+        return 1590.0, 6650.0
+
+
+def _time(fn, warmup: int, iters: int) -> float:  # noqa: ANN001
+    for _ in range(warmup):
+        fn()
+    ts = []
+    for _ in range(iters):
+        dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ts.append(float(t))
+    return statistics.median(ts)
+
+
+def bench_tp(T: int, warmup: int, iters: int, tflops: float) -> list[dict]:
+    from axrl_b200.parallel.tensor_parallel import TPContext, column_parallel_linear, row_parallel_linear
+
+    N, r = dist.get_world_size(), dist.get_rank()
+    H, F = 4096, 12288
+    g = torch.Generator(device="cuda").manual_seed(11 + r)
+    x_sp = torch.randn(T // N, H, device="cuda", generator=g).bfloat16()
+    w_gu = (torch.randn(2 * F // N, H, device="cuda", generator=g) * 0.02).bfloat16()
+    y = torch.randn(T, F // N, device="cuda", generator=g).bfloat16()
+    w_dn = (torch.randn(H, F // N, device="cuda", generator=g) * 0.02).bfloat16()
+    out = []
+    ctxs = {b: TPContext.from_group(dist.group.WORLD, backend=b) for b in ("torch", "p2p")}
+    ref_ag = column_parallel_linear(x_sp, w_gu, ctxs["torch"])
+    ref_rs = row_parallel_linear(y, w_dn, ctxs["torch"])
+    for name, fn, flops, nbytes, ref in (
+        ("ag_gemm", column_parallel_linear, 2.0 * T * H * (2 * F // N), (N - 1) / N * T * H * 2, ref_ag),
+        ("gemm_rs", row_parallel_linear, 2.0 * T * (F // N) * H, (N - 1) / N * T * H * 2, ref_rs),
+    ):
+        row = {"path": f"tp_{name}", "tokens": T, "n_gpus": N}
+        for b, tp in ctxs.items():
+            args = (x_sp, w_gu) if name == "ag_gemm" else (y, w_dn)
+            res = fn(*args, tp)
+            err = ((res.float() - ref.float()).abs().max() / (ref.float().abs().max() + 1e-6)).item()
+            row[f"{b}_ms"] = round(_time(lambda: fn(*args, tp), warmup, iters), 4)  # noqa: B023
+            row[f"{b}_rel_err"] = float(f"{err:.2e}")
+        target_ms = max(flops / (tflops * 1e12), nbytes / (NVLINK_GBS * 1e9)) * 1e3
+        row.update({"gflop": round(flops / 1e9, 1), "nvlink_mb_per_gpu": round(nbytes / 1e6, 1), "roofline_ms": round(target_ms, 4),
+                    "p2p_frac_of_roofline": round(target_ms / row["p2p_ms"], 3),
+                    "nccl_frac_of_roofline": round(target_ms / row["torch_ms"], 3)})
+        ctxs["p2p"].comm.check()
+        out.append(row)
+    return out
+
+
+def bench_ep(T: int, warmup: int, iters: int, tflops: float) -> list[dict]:
+    from axrl_b200.models.moe import MoEBlock
+    from axrl_b200.models.qwen3 import resolve_preset
+    from axrl_b200.parallel.expert import EPContext
+
+    N, r = dist.get_world_size(), dist.get_rank()
+    cfg = resolve_preset("qwen3-30b-a3b")
+    H, E, k, F = cfg.hidden_size, cfg.num_experts, cfg.num_experts_per_tok, cfg.moe_intermediate_size
+    g = torch.Generator(device="cuda").manual_seed(5 + r)
+    x = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+    out = []
+    row = {"path": "ep_moe_layer", "tokens_per_gpu": T, "n_gpus": N, "experts": E, "top_k": k}
+    results = {}
+    for b in ("torch", "p2p"):
+        ep = EPContext.from_group(dist.group.WORLD, backend=b, hidden=H, num_experts=E, max_rows=T * k)
+        blk = MoEBlock(cfg, ep=ep).to("cuda", torch.bfloat16)
+        torch.manual_seed(123)  # the same expert weights for both backends
+        with torch.no_grad():
+            for p in blk.parameters():
+                p.normal_(0.0, 0.02)
+        fn = lambda: blk(x)  # noqa: E731
+        with torch.no_grad():
+            results[b] = fn().float()
+            row[f"{b}_ms"] = round(_time(fn, warmup, iters), 4)
+        if hasattr(ep.comm, "check"):
+            ep.comm.check()
+        del blk
+    ref = results["torch"]
+    row["p2p_rel_err"] = float(f"{((results['p2p'] - ref).abs().max() / (ref.abs().max() + 1e-6)).item():.2e}")
+    flops = 2.0 * T * k * 3 * H * F
+    nbytes = 2 * (N - 1) / N * T * k * H * 2  # dispatch + combine rows that leave the GPU
+    target_ms = max(flops / (tflops * 1e12), nbytes / (NVLINK_GBS * 1e9)) * 1e3
+    row.update({"gflop": round(flops / 1e9, 1), "nvlink_mb_per_gpu": round(nbytes / 1e6, 1), "roofline_ms": round(target_ms, 4),
+                "p2p_frac_of_roofline": round(target_ms / row["p2p_ms"], 3), "nccl_frac_of_roofline": round(target_ms / row["torch_ms"], 3)})
+    out.append(row)
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--paths", default="tp,ep")
+    ap.add_argument("--tokens", type=int, default=16384, help="TP: tokens of the sequence-parallel batch")
+    ap.add_argument("--ep-tokens", type=int, default=8192, help="EP: tokens per GPU")
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(minutes=5), device_id=torch.device("cuda", local))
+    tflops, _ = _peaks()
+    rows = []
+    paths = a.paths.split(",")
+    if "tp" in paths:
+        rows += bench_tp(a.tokens, a.warmup, a.iters, tflops)
+    if "ep" in paths:
+        rows += bench_ep(a.ep_tokens, a.warmup, a.iters, tflops)
+    if dist.get_rank() == 0:
+        for r in rows:
+            print(json.dumps(r), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

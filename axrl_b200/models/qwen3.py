@@ -360,3 +360,93 @@ def load_hf_state_dict(model: Qwen3Model, sd: dict[str, torch.Tensor], strict: b
     if strict and missing:
         raise KeyError(f"missing HF tensors: {missing[:8]}{'...' if len(missing) > 8 else ''}")
     return missing
+
+
+class VirtualPipelineModel(nn.Module):
+    """This rank's ``V`` chunks of an interleaved pipeline: chunk ``c`` is virtual stage
+    ``c * P + r`` of ``P * V`` (reference: Megatron virtual pipeline stages,
+    ``vpp_size`` in ``axrl/configs.py:380``).  Exposes the parts of :class:`Qwen3Model` the trainer
+    uses; ``forward(..., chunk=c)`` runs one chunk."""
+
+    def __init__(self, cfg: Qwen3Config, pp, tp: TPContext | None = None, ep=None, cp=None) -> None:  # noqa: ANN001
+        super().__init__()
+        self.cfg = cfg
+        self.pp = pp
+        self.vpp = pp.vpp
+        self.chunks = nn.ModuleList(Qwen3Model(cfg, tp=tp, ep=ep, pp=pp.virtual(c * pp.size + pp.rank), cp=cp) for c in range(pp.vpp))
+        self.tp = self.chunks[0].tp
+
+    # ---- the Qwen3Model surface
+    @property
+    def first(self) -> bool:
+        return self.chunks[0].first
+
+    @property
+    def last(self) -> bool:
+        return self.chunks[-1].last
+
+    @property
+    def layers(self) -> list:
+        return [layer for ch in self.chunks for layer in ch.layers]
+
+    @property
+    def embed_tokens(self):  # noqa: ANN201
+        return self.chunks[0].embed_tokens
+
+    @property
+    def norm(self):  # noqa: ANN201
+        return self.chunks[-1].norm
+
+    @property
+    def lm_head(self):  # noqa: ANN201
+        return self.chunks[-1].lm_head
+
+    @property
+    def lm_weight(self) -> torch.Tensor:
+        return self.chunks[-1].lm_weight
+
+    @property
+    def inv_freq(self) -> torch.Tensor:
+        return self.chunks[0].inv_freq
+
+    @inv_freq.setter
+    def inv_freq(self, t: torch.Tensor) -> None:
+        for ch in self.chunks:
+            ch.inv_freq = t
+
+    @property
+    def recompute(self) -> bool:
+        return self.chunks[0].recompute
+
+    @recompute.setter
+    def recompute(self, on: bool) -> None:
+        for ch in self.chunks:
+            ch.recompute = on
+
+    @property
+    def grad_ready_hook(self):  # noqa: ANN201
+        return self.chunks[0].grad_ready_hook
+
+    @grad_ready_hook.setter
+    def grad_ready_hook(self, fn) -> None:  # noqa: ANN001
+        for ch in self.chunks:
+            ch.grad_ready_hook = fn
+
+    def init_weights(self, seed: int = 0) -> None:
+        for ch in self.chunks:
+            ch.init_weights(seed)
+
+    def global_name(self, name: str) -> str:
+        c, rest = name[len("chunks."):].split(".", 1)
+        return self.chunks[int(c)].global_name(rest)
+
+    def forward(self, ids: torch.Tensor, pos: torch.Tensor, spec: AttnSpec, moe_ctx=None, hidden: torch.Tensor | None = None,  # noqa: ANN001
+                chunk: int = 0) -> torch.Tensor:
+        return self.chunks[chunk](ids, pos, spec, moe_ctx, hidden=hidden)
+
+    def logprobs(self, *a, **kw):  # noqa: ANN002, ANN003, ANN201
+        return self.chunks[-1].logprobs(*a, **kw)
+
+    def argmax_tokens(self, *a, **kw):  # noqa: ANN002, ANN003, ANN201
+        return self.chunks[-1].argmax_tokens(*a, **kw)
+

@@ -43,6 +43,7 @@ class ParallelCtx:
     ep_backend: str = "torch"
     pp_group: object | None = None
     pp_size: int = 1
+    vpp_size: int = 1  # virtual (interleaved) pipeline stages per rank
     cp_group: object | None = None
     cp_size: int = 1
     zero_backend: str = "p2p"  # distributed optimizer over DP: "p2p" (NVLink) | "nccl" | "off" (replicated)
@@ -68,8 +69,16 @@ class TrainEngine:
         from axrl_b200.parallel.context_parallel import CPContext
         from axrl_b200.parallel.pipeline import PPContext
 
-        self.pp = PPContext.from_group(self.par.pp_group) if self.par.pp_size > 1 else PPContext()
+        self.pp = PPContext.from_group(self.par.pp_group, vpp=self.par.vpp_size) if self.par.pp_size > 1 else PPContext()
         self.cp = CPContext.from_group(self.par.cp_group) if self.par.cp_size > 1 else CPContext()
+        if model is None and self.pp.enabled and self.pp.vpp > 1:
+            from axrl_b200.models.qwen3 import VirtualPipelineModel
+
+            model = VirtualPipelineModel(model_cfg, self.pp, tp=self.tp, ep=self.ep if self.ep.enabled else None,
+                                         cp=self.cp if self.cp.enabled else None)
+            model.init_weights(cfg.seed)
+            model = model.to(device=self.device, dtype=dtype)
+            model.inv_freq = model.chunks[0].inv_freq.float()
         if model is None:
             model = Qwen3Model(model_cfg, tp=self.tp, ep=self.ep if self.ep.enabled else None,
                                pp=self.pp if self.pp.enabled else None, cp=self.cp if self.cp.enabled else None)
@@ -166,7 +175,14 @@ class TrainEngine:
             for li, r in enumerate(mbs[i].rows):
                 out[r] = dense[li]
 
-        run_forward_only(self.pp, len(mbs), lambda i: self._act_shape(mbs[i]), self._act_dtype(), self.device, fwd, consume)
+        if self.pp.vpp > 1:
+            from axrl_b200.parallel.pipeline import run_interleaved_1f1b
+
+            run_interleaved_1f1b(self.pp, self.pp.vpp, len(mbs), lambda i: self._act_shape(mbs[i]), self._act_dtype(), self.device,
+                                 lambda i, c, inp: self.model(dmbs[i].ids, dmbs[i].pos, dmbs[i].spec, None, hidden=inp, chunk=c),
+                                 consume=consume)
+        else:
+            run_forward_only(self.pp, len(mbs), lambda i: self._act_shape(mbs[i]), self._act_dtype(), self.device, fwd, consume)
         # the last stage holds the result: broadcast it to every stage
         t = out.to(self.device)
         dist.broadcast(t, src=self.pp.ranks[-1], group=self.pp.group)
@@ -296,7 +312,14 @@ class TrainEngine:
                 metrics_acc.append(m)
             return l * denom.to(l.dtype)
 
-        run_1f1b(self.pp, len(mbs), lambda i: self._act_shape(mbs[i]), self._act_dtype(), self.device, fwd, loss)
+        if self.pp.vpp > 1:
+            from axrl_b200.parallel.pipeline import run_interleaved_1f1b
+
+            run_interleaved_1f1b(self.pp, self.pp.vpp, len(mbs), lambda i: self._act_shape(mbs[i]), self._act_dtype(), self.device,
+                                 lambda i, c, inp: self.model(dmbs[i].ids, dmbs[i].pos, dmbs[i].spec, None, hidden=inp, chunk=c),
+                                 loss=loss)
+        else:
+            run_1f1b(self.pp, len(mbs), lambda i: self._act_shape(mbs[i]), self._act_dtype(), self.device, fwd, loss)
         # metrics live on the last stage
         obj = [metrics_acc if self.pp.is_last else None]
         dist.broadcast_object_list(obj, src=self.pp.ranks[-1], group=self.pp.group)

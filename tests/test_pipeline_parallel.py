@@ -44,7 +44,7 @@ def _engine(par=None):
     return TrainEngine(wc, cfg, "cpu", par=par)
 
 
-def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+def _worker(rank: int, world: int, port: int, q, vpp: int = 1) -> None:  # noqa: ANN001
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -53,8 +53,12 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
         from axrl_b200.trainer.grpo_trainer import GrpoTrainer
 
         ref = _engine()
-        eng = _engine(ParallelCtx(pp_group=dist.group.WORLD, pp_size=world))
-        assert len(eng.model.layers) in (2, 3) and eng.model.layer_offset == (0 if rank == 0 else 3)
+        eng = _engine(ParallelCtx(pp_group=dist.group.WORLD, pp_size=world, vpp_size=vpp))
+        if vpp == 1:
+            assert len(eng.model.layers) in (2, 3) and eng.model.layer_offset == (0 if rank == 0 else 3)
+        else:  # 5 layers over 4 virtual stages: rank 0 holds layers 0-1 and 3, rank 1 layers 2 and 4
+            offs = [ch.layer_offset for ch in eng.model.chunks]
+            assert offs == ([0, 3] if rank == 0 else [2, 4]), offs
         b = _batch()
         assert len(eng.micro_batches(b)) >= 3  # warm-up, steady state and cool-down all run
         lp_ref = ref.compute_logprobs(b)
@@ -91,6 +95,43 @@ def test_pp2_1f1b_matches_pp1():
         p.join(timeout=60)
     for r, msg in res:
         assert msg == "ok", f"rank {r}:\n{msg}"
+
+
+def test_pp2_interleaved_vpp2_matches_pp1():
+    """Two virtual stages per rank (interleaved 1F1B, Megatron ``virtual_pipeline_model_parallel_size``):
+    the activation walks both ranks twice; results must equal the PP=1 engine."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, 2)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for r, msg in res:
+        assert msg == "ok", f"rank {r}:\n{msg}"
+
+
+def test_interleaved_plan_is_complete_and_deadlock_free():
+    from axrl_b200.parallel.pipeline import interleaved_order, plan_interleaved
+
+    for P in (2, 3, 4, 8):
+        for V in (1, 2, 3, 4):
+            for n in range(1, 20):
+                plan = plan_interleaved(P, V, n)
+                for r in range(P):
+                    acts = [a[r] for a in plan.actions if a[r] is not None]
+                    assert sorted(acts) == sorted(interleaved_order(P, V, r, n))
+                    # a backward never precedes its own forward on a rank
+                    seen = set()
+                    for kind, mb, c in acts:
+                        if kind == "F":
+                            seen.add((mb, c))
+                        else:
+                            assert (mb, c) in seen
+    # interleaving shortens the pipeline (ticks weighted by chunk size)
+    assert len(plan_interleaved(4, 2, 8).actions) / 2 < len(plan_interleaved(4, 1, 8).actions)
 
 
 def test_layer_ranges():
