@@ -196,6 +196,7 @@ __global__ void __launch_bounds__(THREADS, 1) skinny_tma_k(const __grid_constant
     // the last WARP to contribute to tile t (all contributing CTAs x 4 warps) finalises it; no
     // block-level barrier is needed, so a warp that gave up on a wait can never strand the others
     __threadfence();
+    __syncwarp();  // every lane's partial sums are visible before lane 0 counts the warp in
     int is_last = 0;
     if (lane == 0) {
       const int first_cta = (t * p.kslabs) / p.per, last_cta = ((t + 1) * p.kslabs - 1) / p.per;

@@ -142,6 +142,7 @@ class Attention(nn.Module):
         self.q_norm = nn.Parameter(torch.ones(self.d))
         self.k_norm = nn.Parameter(torch.ones(self.d))
         self.cp = None  # context-parallel group (set by the model)
+        self.stash = ops.AttnStash()  # attention outputs kept for the recompute in backward
 
     def forward(self, x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, tp: TPContext = _NO_TP) -> torch.Tensor:
         qkv = tpl.column_parallel_linear(x, self.qkv_proj, tp)
@@ -150,7 +151,7 @@ class Attention(nn.Module):
             from axrl_b200.parallel.context_parallel import gather_kv
 
             k, v = gather_kv(k, self.cp), gather_kv(v, self.cp)
-        o = ops.attention(q, k, v, spec)
+        o = ops.attention(q, k, v, spec, stash=self.stash if (self.training and torch.is_grad_enabled()) else None)
         return tpl.row_parallel_linear(o.reshape(o.shape[0], -1), self.o_proj, tp)
 
 
@@ -290,7 +291,11 @@ class Qwen3Model(nn.Module):
                 # (weight gradients included) has been issued
                 h.register_hook(_LayerDone(hook, layer.layer_idx))
             if self.recompute and torch.is_grad_enabled():
-                h = checkpoint(layer, h, pos, inv, spec, moe_ctx, tp, use_reentrant=False)
+                ops.AttnStash.pushing = True  # the replay in backward reuses this forward's attention
+                try:
+                    h = checkpoint(layer, h, pos, inv, spec, moe_ctx, tp, use_reentrant=False)
+                finally:
+                    ops.AttnStash.pushing = False
             else:
                 h = layer(h, pos, inv, spec, moe_ctx, tp)
         return self.norm(h) if self.last else h

@@ -87,16 +87,33 @@ def spec_from_triples(triples: list[tuple[int, int, int, int, int]], total: int,
     mq = int((qseg[:, 1] - qseg[:, 0]).max()) if len(qseg) else 0
     mk = int((kseg[:, 1] - kseg[:, 0]).max()) if len(kseg) else 0
     return AttnSpec(torch.from_numpy(qseg), torch.from_numpy(kr), torch.from_numpy(kseg), torch.from_numpy(qr), total,
-                    total if total_k is None else total_k, mq, mk, _tiles(qseg, FWD_Q_TILE), _tiles(kseg, BWD_K_TILE))
+                    total if total_k is None else total_k, mq, mk, _tiles(qseg, FWD_Q_TILE, kr, True),
+                    _tiles(kseg, BWD_K_TILE, qr, False))
 
 
 FWD_Q_TILE = 128
 BWD_K_TILE = 64
 
 
-def _tiles(seg: np.ndarray, bs: int) -> torch.Tensor:
-    rows = [(i, a) for i, (s0, s1, _, _) in enumerate(seg.tolist()) for a in range(s0, s1, bs)]
-    return torch.tensor(rows, dtype=torch.int32).reshape(-1, 2)
+def _tiles(seg: np.ndarray, bs: int, items: np.ndarray | None = None, fwd: bool = True) -> torch.Tensor:
+    """(segment, tile start) work list, heaviest tiles first: under causal masks the tiles at the
+    end of a long sequence see the most keys (forward) / the first key tiles are seen by the most
+    queries (backward), and starting them first keeps the last wave of CTAs short."""
+    rows, work = [], []
+    its = items.tolist() if items is not None else []
+    for i, (s0, s1, r0, r1) in enumerate(seg.tolist()):
+        for a in range(s0, s1, bs):
+            w = 0
+            for x0, x1, t in its[r0:r1]:
+                if fwd:  # keys seen by q rows [a, a + bs) of segment (s0, s1)
+                    e = min(a + bs, s1)
+                    w += max(0, min(x1, x0 + (e - s0)) - x0) if t == 1 else x1 - x0
+                else:  # q rows that see key tile [a, a + bs) of segment (s0, s1)
+                    w += max(0, x1 - (x0 + max(0, a - s0))) if t == 1 else x1 - x0
+            rows.append((i, a))
+            work.append(w)
+    order = sorted(range(len(rows)), key=lambda j: -work[j])
+    return torch.tensor([rows[j] for j in order], dtype=torch.int32).reshape(-1, 2)
 
 
 def causal_spec_from_cu_seqlens(cu_seqlens: list[int] | np.ndarray) -> AttnSpec:

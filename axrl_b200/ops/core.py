@@ -152,10 +152,39 @@ def _attn_ref(q, k, v, spec: AttnSpec, scale: float):  # noqa: ANN001, ANN202
     return torch.einsum("hts,shd->thd", p, vv).to(q.dtype)
 
 
+class AttnStash:
+    """Attention outputs (o, lse) of a checkpointed layer's first forward, reused by the forward
+    that backward replays, so activation recompute re-runs the projections and norms but not the
+    attention kernel (o and lse of one layer are (T, Hq, D) bf16 + (T, Hq) fp32).  The first
+    forward pushes, the replay pops the entry of the same spec and shape (FIFO per key, which is
+    the backward order of micro-batches under 1F1B and interleaved schedules)."""
+
+    pushing = False  # set (by the model) around the first forward of checkpointed layers
+
+    def __init__(self) -> None:
+        self.items: dict[tuple, list[tuple[torch.Tensor, torch.Tensor]]] = {}
+
+    def clear(self) -> None:
+        self.items.clear()
+
+
 class _Attn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, spec, scale):  # noqa: ANN001, ANN205
-        o, lse = _ext.ext().attn_fwd(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
+    def forward(ctx, q, k, v, spec, scale, stash=None):  # noqa: ANN001, ANN205
+        key = (id(spec), tuple(q.shape))
+        hit = None
+        if stash is not None and not AttnStash.pushing:
+            lst = stash.items.get(key)
+            if lst:
+                hit = lst.pop(0)
+                if not lst:
+                    del stash.items[key]
+        if hit is not None:
+            o, lse = hit
+        else:
+            o, lse = _ext.ext().attn_fwd(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
+            if stash is not None and AttnStash.pushing:
+                stash.items.setdefault(key, []).append((o, lse))
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.spec, ctx.scale = spec, scale
         return o
@@ -165,17 +194,18 @@ class _Attn(torch.autograd.Function):
         q, k, v, o, lse = ctx.saved_tensors
         s = ctx.spec
         dq, dk, dv = _ext.ext().attn_bwd(do.contiguous(), q, k, v, o, lse, s.kseg, s.qr, s.bwd_tiles, ctx.scale)
-        return dq, dk, dv, None, None
+        return dq, dk, dv, None, None, None
 
 
-def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: AttnSpec, scale: float | None = None) -> torch.Tensor:
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: AttnSpec, scale: float | None = None,
+              stash: AttnStash | None = None) -> torch.Tensor:
     """Range-list attention over packed tokens.  q: (T,Hq,D); k,v: (T,Hkv,D) with GQA."""
     scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
     if not q.is_cuda:
         return _attn_ref(q, k, v, spec, scale)
     if not spec.qseg.is_cuda:
         spec = spec.to(q.device)
-    return _Attn.apply(q.contiguous(), k.contiguous(), v.contiguous(), spec, scale)
+    return _Attn.apply(q.contiguous(), k.contiguous(), v.contiguous(), spec, scale, stash)
 
 
 # ----------------------------------------------------------------------------- linear

@@ -206,6 +206,9 @@ class TrainEngine:
         t0 = time.perf_counter()
         self.model.train()
         self.optim.zero_grad()
+        for m in self.model.modules():  # attention outputs kept for recompute: none may survive a step
+            if hasattr(m, "stash"):
+                m.stash.clear()
         total_denom = max(self._global_denominator(batch, trainer), 1.0)
         need_entropy = bool(getattr(trainer.config, "entropy_control", None) and
                             (trainer.config.entropy_control.alpha > 0 or trainer.config.entropy_control.compute_entropy))

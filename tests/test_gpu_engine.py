@@ -164,3 +164,31 @@ def test_filtered_sampling_in_graph_decode():
     assert len(res["topp"].output_ids) == 16 and all(lp <= 0 for lp in res["topp"].output_logprobs)
     assert any(k[1] for k in eng.graphs)  # a filtered-mode graph was captured
     eng.release_graphs()
+
+
+def test_recompute_reuses_attention_and_matches_plain_backward():
+    """Checkpointed layers keep (o, lse) of the first forward for the replay in backward: the
+    gradients equal those of the same model trained without recompute, and the attention kernel
+    runs once per layer instead of twice."""
+    from axrl_b200.ops import core
+    from axrl_b200.ops.attention_spec import causal_spec_from_cu_seqlens
+
+    torch.manual_seed(0)
+    T = 700
+    ids = torch.randint(0, 2048, (T,), device="cuda")
+    labels = torch.randint(0, 2048, (T,), device="cuda")
+    pos = torch.cat([torch.arange(300), torch.arange(400)]).int().cuda()
+    spec = causal_spec_from_cu_seqlens([0, 300, 700]).to("cuda")
+    grads = {}
+    for recompute in (False, True):
+        m = _model(5)
+        m.train()
+        m.recompute = recompute
+        lp, _ = m.logprobs(m(ids, pos, spec), labels)
+        lp.float().sum().backward()
+        grads[recompute] = {k: p.grad.float().clone() for k, p in m.named_parameters() if p.grad is not None}
+        assert all(not layer.self_attn.stash.items for layer in m.layers), "every stashed output consumed"
+    for k, g in grads[False].items():
+        rel = ((grads[True][k] - g).norm() / (g.norm() + 1e-12)).item()
+        assert rel < 1e-2, f"{k}: {rel}"
+    assert core.AttnStash.pushing is False
