@@ -14,6 +14,8 @@
 //
 // Tensor-core path: mma.sync m16n8k16 (bf16).  Shared memory rows of 128 bf16 are stored
 // with a 16-byte-chunk XOR swizzle (chunk ^ row%8) so ldmatrix is conflict-free.
+#include <string>
+
 #include "common.cuh"
 
 namespace ax {
@@ -519,9 +521,32 @@ __global__ void f32_to_bf16_k(const float* __restrict__ a, bf16* __restrict__ b,
 
 }  // namespace attn
 
-// q: (T,Hq,128) k,v: (T,Hkv,128) -> o (T,Hq,128), lse2 (Hq,T)
+std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
+                                    double scale);
+
+// Forward implementation: AXRL_ATTN_FWD=tc selects the tcgen05 kernel (attention_tc.cu), anything
+// else the mma.sync kernel below.
+static bool use_tc_forward() {
+  static int on = [] {
+    const char* e = std::getenv("AXRL_ATTN_FWD");
+    return (e && std::string(e) == "tc") ? 1 : 0;
+  }();
+  return on != 0;
+}
+
+std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
+                                     double scale);
+
+// q: (T,Hq,128) k,v: (Tk,Hkv,128) -> o (T,Hq,128), lse2 (Hq,T)
 std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                  double scale) {
+  if (use_tc_forward()) return attn_fwd_tc(q, k, v, qseg, kr, tiles, scale);
+  return attn_fwd_mma(q, k, v, qseg, kr, tiles, scale);
+}
+
+// mma.sync forward (the pre-tcgen05 tensor-core path)
+std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
+                                     double scale) {
   using namespace attn;
   AX_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(2) == D, "q bf16 (T,Hq,128)");
   AX_CHECK(k.is_contiguous() && v.is_contiguous() && k.sizes() == v.sizes(), "k/v layout");

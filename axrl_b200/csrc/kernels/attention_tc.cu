@@ -1,0 +1,467 @@
+// Range-list flash attention forward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Same problem and outputs as attn_fwd_k in attention.cu (packed tokens, (q-range, k-range, type)
+// triples, head_dim 128, GQA; O bf16 and the base-2 log-sum-exp of the scaled scores), computed
+// with one CTA per (128-row q tile, q head):
+//
+//   warp 4      TMA producer: the Q tile once, then K/V tiles of 128 keys into a 2-stage ring
+//               (cp.async.bulk.tensor, 128-byte swizzle, no multicast).
+//   warp 5      MMA issuer (one thread) and TMEM owner: S_j = Q K_j^T into one of two S buffers
+//               in TMEM (128 x 128 fp32 each), then O += P_{j-1} V_{j-1} into the O accumulator
+//               (TMEM, 128 x 128 fp32), so the QK product of a tile overlaps the softmax of the
+//               previous one.  A = Q / P and B = K are K-major, B = V is MN-major (V tiles are
+//               used as loaded, no transpose).
+//   warps 0-3   softmax, one query row per thread (TMEM lane = row): read S with tcgen05.ld,
+//               mask (range ends, causal diagonal), online softmax in base 2, write P (bf16) to
+//               shared memory in the UMMA K-major layout; the epilogue reads O back, divides by
+//               the row sum and stores O and the log-sum-exp.
+//
+// The running maximum used for the exponentials is only raised when a tile's maximum exceeds it
+// by more than 8 (log2 units): P then stays below 2^8, and O in TMEM is rescaled only on those
+// rare steps instead of after every tile.  The result is exact (the final division uses the same
+// maximum as the exponentials).
+//
+// Every mbarrier wait is bounded; on expiry the CTA records an error code, drains its own copies
+// and tensor-core work, frees its TMEM and exits.
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace ax {
+namespace atc {
+
+constexpr int D = 128;
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int THREADS = 192;
+constexpr int TILE = BN * D * 2;   // 32 KB: one 128 x 128 bf16 tile (two 64-column boxes of 16 KB)
+constexpr int HALF = TILE / 2;
+constexpr uint32_t TMEM_COLS = 512;  // S0 [0,128), S1 [128,256), O [256,384)
+constexpr long WAIT_LIMIT = 1L << 24;
+constexpr float RESCALE_THRESHOLD = 8.f;
+
+// barrier slots
+constexpr int B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 3, B_S_FULL = 5, B_S_FREE = 7, B_P_FULL = 9, B_O_DONE = 10, B_DRAIN = 11, NBAR = 12;
+
+struct Params {
+  bf16* o;
+  float* lse2;
+  const int* qseg;
+  const int* kr;
+  const int* tiles;
+  int Hq, Hkv, T;
+  float scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(s32(b)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false (and the CTA's abort flag set) when the limit is reached or another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t phase, volatile int* abort, int* err, int code) {
+  for (long it = 0; !mbar_try_wait(b, phase); ++it) {
+    if (*abort) return false;
+    if (it > WAIT_LIMIT) {
+      *abort = 1;
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(s32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(s32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s32(b)) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane.  The wait is part of the same asm
+// statement, so no use of the destination registers can be scheduled before the data arrived.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%"
+      "25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]),
+        "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%"
+      "24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+      "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+      "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle (version 1).  lbo / sbo in bytes.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: bf16 x bf16 -> fp32, M = 128, N = n; b_mn: B is MN-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// Key tiles of a q tile: every k-range of the q segment, BN keys at a time from the range start,
+// up to the range end (for causal ranges, the last key any row of the tile may see).
+struct KeyTiles {
+  const int* kr;
+  int r, r_last, q0, qe, ka, k0, rend, ty;
+  __device__ void load_range() {
+    while (r < r_last) {
+      k0 = kr[r * 3];
+      const int k1 = kr[r * 3 + 1];
+      ty = kr[r * 3 + 2];
+      rend = ty == 1 ? min(k1, k0 + (qe - q0)) : k1;
+      if (rend > k0) {
+        ka = k0;
+        return;
+      }
+      ++r;
+    }
+  }
+  __device__ bool valid() const { return r < r_last; }
+  __device__ void next() {
+    ka += BN;
+    if (ka >= rend) {
+      ++r;
+      load_range();
+    }
+  }
+};
+
+__global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                                                          const __grid_constant__ CUtensorMap tv, Params p) {
+  extern __shared__ char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  char* sQ = sm;
+  char* sK = sm + TILE;          // 2 stages
+  char* sV = sm + 3 * TILE;      // 2 stages
+  char* sP = sm + 5 * TILE;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 6 * TILE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seg = p.tiles[blockIdx.x * 2], qs = p.tiles[blockIdx.x * 2 + 1];
+  const int h = blockIdx.y, hk = h / (p.Hq / p.Hkv);
+  const int q0 = p.qseg[seg * 4], q1 = p.qseg[seg * 4 + 1], r_first = p.qseg[seg * 4 + 2], r_last = p.qseg[seg * 4 + 3];
+  const int qe = min(qs + BM, q1);
+
+  if (tid == 0) {
+    mbar_init(&bar[B_Q], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar[B_KV_FULL + s], 1);
+      mbar_init(&bar[B_KV_EMPTY + s], 1);
+      mbar_init(&bar[B_S_FULL + s], 1);
+      mbar_init(&bar[B_S_FREE + s], 4);
+    }
+    mbar_init(&bar[B_P_FULL], 4);
+    mbar_init(&bar[B_O_DONE], 1);
+    mbar_init(&bar[B_DRAIN], 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tq)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tv)) : "memory");
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  KeyTiles kt{p.kr, r_first, r_last, q0, qe, 0, 0, 0, 0};
+  kt.load_range();
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(&bar[B_Q], TILE);
+      tma_2d(sQ, &tq, h * D, qs, &bar[B_Q]);
+      tma_2d(sQ + HALF, &tq, h * D + 64, qs, &bar[B_Q]);
+      int j = 0;
+      for (; kt.valid(); kt.next(), ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&bar[B_KV_EMPTY + s], ((j - 2) >> 1) & 1, abort, p.err, 1)) break;
+        mbar_expect_tx(&bar[B_KV_FULL + s], 2 * TILE);
+        tma_2d(sK + s * TILE, &tk, hk * D, kt.ka, &bar[B_KV_FULL + s]);
+        tma_2d(sK + s * TILE + HALF, &tk, hk * D + 64, kt.ka, &bar[B_KV_FULL + s]);
+        tma_2d(sV + s * TILE, &tv, hk * D, kt.ka, &bar[B_KV_FULL + s]);
+        tma_2d(sV + s * TILE + HALF, &tv, hk * D + 64, kt.ka, &bar[B_KV_FULL + s]);
+      }
+      if (*abort) {  // let every copy this CTA started land before its shared memory is released
+        int zero = 0;
+        mbar_wait(&bar[B_Q], 0, (volatile int*)&zero, p.err, 1);
+        for (int i = max(0, j - 2); i < j; ++i) mbar_wait(&bar[B_KV_FULL + (i & 1)], (i >> 1) & 1, (volatile int*)&zero, p.err, 1);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_QK = idesc_bf16(BN, false), ID_PV = idesc_bf16(D, true);
+      const uint32_t q_base = s32(sQ), k_base = s32(sK), v_base = s32(sV), p_base = s32(sP);
+      bool ok = mbar_wait(&bar[B_Q], 0, abort, p.err, 2);
+      tc_fence_after();
+      int j = 0;
+      auto pv = [&](int t) {  // O += P_t V_t
+        if (!mbar_wait(&bar[B_P_FULL], t & 1, abort, p.err, 4)) return false;
+        tc_fence_after();
+        const uint32_t vb = v_base + (t & 1) * TILE;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t a = sdesc(p_base + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
+          const uint64_t b = sdesc(vb + kk * 2048, HALF, 1024);
+          tc_mma(tmem + 256, a, b, ID_PV, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&bar[B_O_DONE]);
+        tc_commit(&bar[B_KV_EMPTY + (t & 1)]);
+        return true;
+      };
+      for (; ok && kt.valid(); kt.next(), ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&bar[B_KV_FULL + b], (j >> 1) & 1, abort, p.err, 3)) break;
+        if (j >= 2 && !mbar_wait(&bar[B_S_FREE + b], ((j - 2) >> 1) & 1, abort, p.err, 3)) break;
+        tc_fence_after();
+        const uint32_t kb = k_base + b * TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          tc_mma(tmem + b * BN, sdesc(q_base + off, 16, 1024), sdesc(kb + off, 16, 1024), ID_QK, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&bar[B_S_FULL + b]);
+        if (j >= 1 && !pv(j - 1)) break;
+      }
+      if (!*abort && j >= 1) pv(j - 1);
+      // nothing this thread issued may still run when TMEM is freed
+      tc_commit(&bar[B_DRAIN]);
+      int zero = 0;
+      mbar_wait(&bar[B_DRAIN], 0, (volatile int*)&zero, p.err, 5);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (warps 0-3)
+    const int row = qs + tid;  // this thread's query row (TMEM lane tid)
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    float m_used = -INFINITY, l = 0.f;
+    int j = 0;
+    char* prow0 = sP + (tid >> 3) * 1024 + (tid & 7) * 128;  // row tid of the first 64-key block
+    for (; kt.valid(); kt.next(), ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&bar[B_S_FULL + b], (j >> 1) & 1, abort, p.err, 6)) break;
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32];
+        tmem_ld32(lane_addr + b * BN + c * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_S_FREE + b]);
+      // mask + scale (log2 units)
+      const int kend = min(kt.ka + BN, kt.rend);
+      const int climit = row < qe ? (kt.ty == 1 ? min(kend - kt.ka, row - q0 + kt.k0 - kt.ka + 1) : kend - kt.ka) : 0;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        s[c] = c < climit ? s[c] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, s[c]);
+      }
+      // P_j may only overwrite P_{j-1} (and O may only be rescaled) once PV_{j-1} has finished
+      if (j >= 1 && !mbar_wait(&bar[B_O_DONE], (j - 1) & 1, abort, p.err, 7)) break;
+      tc_fence_after();
+      const float m_new = fmaxf(m_used, mt);
+      if (m_new > m_used + RESCALE_THRESHOLD) {
+        if (j >= 1 && m_used != -INFINITY) {  // O holds the previous tiles' sum: scale it down
+          const float alpha = exp2f(m_used - m_new);
+          l *= alpha;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            tmem_ld32(lane_addr + 256 + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(lane_addr + 256 + c * 32, o);
+          }
+          tmem_st_wait();
+        }
+        m_used = m_new;
+      }
+      // P = exp2(s - m), bf16, K-major 128-byte-swizzled rows
+      float rs = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < BN / 8; ++c8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float a = m_used == -INFINITY ? 0.f : exp2f(s[c8 * 8 + 2 * i] - m_used);
+          const float bb = m_used == -INFINITY ? 0.f : exp2f(s[c8 * 8 + 2 * i + 1] - m_used);
+          rs += a + bb;
+          bf162 v2 = __floats2bfloat162_rn(a, bb);
+          w[i] = *reinterpret_cast<uint32_t*>(&v2);
+        }
+        char* dst = prow0 + (c8 >> 3) * HALF + (((c8 & 7) ^ (tid & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += rs;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_P_FULL]);
+    }
+    // epilogue: wait for the last PV, normalise, store
+    const int n = j;
+    bool ok = !*abort;
+    if (ok && n >= 1) ok = mbar_wait(&bar[B_O_DONE], (n - 1) & 1, abort, p.err, 8);
+    if (ok && n >= 1) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      bf16* orow = p.o + ((long)row * p.Hq + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        tmem_ld32(lane_addr + 256 + c * 32, o);
+        tmem_ld_wait();
+        if (row < qe) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = o[i + e] * inv;
+            store8(orow + c * 32 + i, f);
+          }
+        }
+      }
+      if (row < qe) p.lse2[(long)h * p.T + row] = l > 0.f ? m_used + log2f(l) : INFINITY;
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------------- host side
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+
+static EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    AX_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess && ptr, "cuTensorMapEncodeTiled");
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+
+// rows x width bf16 matrix (row stride = width), box 64 columns x 128 rows, 128-byte swizzle.
+static CUtensorMap map_rows(const void* base, long rows, long width) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)width * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AX_CHECK(r == CUDA_SUCCESS, "tensor map encode failed (", (int)r, ")");
+  return m;
+}
+
+static at::Tensor& err_flag(int dev) {
+  static at::Tensor e[16];
+  if (!e[dev].defined()) e[dev] = at::zeros({1}, at::TensorOptions().device(at::kCUDA, dev).dtype(at::kInt));
+  return e[dev];
+}
+
+}  // namespace atc
+
+// q (T,Hq,128), k/v (Tk,Hkv,128) -> o (T,Hq,128) bf16, lse2 (Hq,T) fp32 (base-2, +inf for rows without keys)
+std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles, double scale) {
+  using namespace atc;
+  AX_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(2) == D, "q bf16 (T,Hq,128)");
+  AX_CHECK(k.is_contiguous() && v.is_contiguous() && k.sizes() == v.sizes() && k.size(2) == D, "k/v layout");
+  const int T = q.size(0), Hq = q.size(1), Tk = k.size(0), Hkv = k.size(1);
+  AX_CHECK(Hq % Hkv == 0, "GQA");
+  auto o = at::zeros_like(q);
+  auto lse2 = at::full({Hq, T}, INFINITY, q.options().dtype(at::kFloat));
+  const int nt = tiles.size(0);
+  if (nt == 0 || T == 0 || Tk == 0) return {o, lse2};
+  AX_CHECK(qseg.is_cuda() && kr.is_cuda() && tiles.is_cuda(), "attention tables on the device");
+  const CUtensorMap tq = map_rows(q.data_ptr(), T, (long)Hq * D);
+  const CUtensorMap tk = map_rows(k.data_ptr(), Tk, (long)Hkv * D);
+  const CUtensorMap tv = map_rows(v.data_ptr(), Tk, (long)Hkv * D);
+  Params p{(bf16*)o.data_ptr(), lse2.data_ptr<float>(), qseg.data_ptr<int>(), kr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
+           (float)(scale * 1.4426950408889634), err_flag(q.get_device()).data_ptr<int>()};
+  const int smem = 6 * TILE + NBAR * 8 + 16 + 1024;
+  static bool attr = false;
+  if (!attr) {
+    AX_CUDA_OK(cudaFuncSetAttribute(attn_fwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  attn_fwd_tc_k<<<dim3(nt, Hq), THREADS, smem, stream()>>>(tq, tk, tv, p);
+  AX_LAUNCH_OK();
+  return {o, lse2};
+}
+
+// Error code of the last failed wait of the tcgen05 attention (0 = none); reading it synchronises.
+int64_t attn_tc_error() { return atc::err_flag(c10::cuda::current_device()).item<int>(); }
+
+}  // namespace ax

@@ -22,6 +22,11 @@ at::Tensor linear_wgrad(at::Tensor dy, at::Tensor x);
 void linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc);
 at::Tensor gemm_bf16(at::Tensor a, at::Tensor b, bool trans_b);
 std::vector<at::Tensor> attn_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, double);
+std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
+                                    double scale);
+std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
+                                     double scale);
+int64_t attn_tc_error();
 std::vector<at::Tensor> attn_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
                                  at::Tensor, double);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
@@ -115,6 +120,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_wgrad_acc", &ax::linear_wgrad_acc);
   m.def("gemm", &ax::gemm_bf16);
   m.def("attn_fwd", &ax::attn_fwd);
+  m.def("attn_fwd_tc", &ax::attn_fwd_tc);
+  m.def("attn_fwd_mma", &ax::attn_fwd_mma);
+  m.def("attn_tc_error", &ax::attn_tc_error);
   m.def("attn_bwd", &ax::attn_bwd);
   m.def("paged_decode_attn", &ax::paged_decode_attn);
   m.def("kv_store", &ax::kv_store);

@@ -489,3 +489,44 @@ def test_decode_gemm_chain_with_programmatic_launch(variant):
         e.set_weights_static(False)
     torch.cuda.synchronize()
     assert e.skinny_tma_error() == 0
+
+
+@pytest.mark.parametrize("case", [0, 1, 2, 3, 4])
+def test_attention_tcgen05_forward_matches_reference(case):
+    """tcgen05/TMEM/TMA forward (attention_tc.cu) against fp32 and the mma.sync kernel: causal
+    packs with odd lengths, a prefix tree, full (non-causal) ranges, keys gathered from a longer
+    buffer than the queries (context-parallel layout), and sharp scores that make the running
+    maximum jump (O rescaled in TMEM)."""
+    from axrl_b200.ops.attention_spec import spec_from_triples
+    from axrl_b200.ops.core import _attn_ref
+
+    e = _ext()
+    D = 128
+    if case < 3:
+        spec = _spec_cases()[case]
+        hq, hkv, sharp = 8, 2, 1.0
+    elif case == 3:  # full ranges + a causal one, keys from a longer buffer
+        spec = spec_from_triples([(0, 200, 0, 300, 0), (200, 457, 300, 557, 1), (457, 600, 100, 250, 0)], 600, total_k=700)
+        hq, hkv, sharp = 4, 4, 1.0
+    else:  # a long causal sequence with sharp scores
+        from axrl_b200.ops.attention_spec import causal_spec_from_cu_seqlens
+
+        spec = causal_spec_from_cu_seqlens([0, 77, 2100])
+        hq, hkv, sharp = 8, 1, 6.0
+    spec = spec.to(DEV)
+    T, Tk = spec.total_q, spec.total_k
+    torch.manual_seed(100 + case)
+    q = (torch.randn(T, hq, D, device=DEV) * sharp).bfloat16()
+    k = torch.randn(Tk, hkv, D, device=DEV).bfloat16()
+    v = torch.randn(Tk, hkv, D, device=DEV).bfloat16()
+    scale = 1 / math.sqrt(D)
+    o, lse = e.attn_fwd_tc(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
+    o2, lse2 = e.attn_fwd_mma(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
+    torch.cuda.synchronize()
+    assert e.attn_tc_error() == 0
+    if Tk == T:
+        close(o, _attn_ref(q.float(), k.float(), v.float(), spec, scale), 2e-2, msg="tc vs fp32")
+    close(o, o2, 2e-2, msg="tc vs mma.sync")
+    fin = torch.isfinite(lse2)
+    assert torch.equal(fin, torch.isfinite(lse)), "rows without keys differ"
+    close(lse[fin], lse2[fin], 1e-3, 1e-4, msg="lse")
