@@ -302,7 +302,9 @@ at::Tensor skinny_tma_linear_out(at::Tensor x, at::Tensor w, c10::optional<at::T
   using namespace skt;
   AX_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() && w.is_contiguous(), "bf16 contiguous");
   const int M = x.size(0), K = x.size(1), N = w.size(0);
-  AX_CHECK(M >= 1 && M <= 64 && w.size(1) == K && K % KT == 0 && N % 8 == 0 && N <= 262144, "skinny_tma: M<=64, K%64==0, N%8==0");
+  // The 64-row tile variant gave sporadic wrong partial sums under test (an unresolved race in its
+  // split-tile reduction), so it is not offered: up to 32 rows.
+  AX_CHECK(M >= 1 && M <= 32 && w.size(1) == K && K % KT == 0 && N % 8 == 0 && N <= 262144, "skinny_tma: M<=32, K%64==0, N%8==0");
   AX_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "16-byte aligned");
   auto y = out.has_value() ? *out : at::empty({M, N}, x.options());
   AX_CHECK(y.is_contiguous() && y.size(0) == M && y.size(1) == N, "output shape");
@@ -313,8 +315,7 @@ at::Tensor skinny_tma_linear_out(at::Tensor x, at::Tensor w, c10::optional<at::T
   }
   auto& wsp = workspace(x.get_device());
   if (M <= 16) launch<16>(x, w, r, y, wsp);
-  else if (M <= 32) launch<32>(x, w, r, y, wsp);
-  else launch<64>(x, w, r, y, wsp);
+  else launch<32>(x, w, r, y, wsp);
   return y;
 }
 

@@ -437,7 +437,7 @@ def test_fused_router_matches_torch(renorm):
         torch.testing.assert_close(a.grad.cpu(), b.grad.cpu(), atol=1e-6, rtol=1e-4)
 
 
-@pytest.mark.parametrize("M", [1, 5, 16, 23, 32, 48, 64])
+@pytest.mark.parametrize("M", [1, 5, 16, 23, 32])
 def test_skinny_tma_gemm_matches_fp32(M):
     """TMA-fed weight-streaming GEMM (persistent CTAs, mbarrier ring, split tiles with a
     self-cleaning workspace) against fp32, including N not a multiple of the 128-row tile."""
