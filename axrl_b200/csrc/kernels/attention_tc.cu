@@ -296,7 +296,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
     char* prow0 = sP + (tid >> 3) * 1024 + (tid & 7) * 128;  // row tid of the first 64-key block
     for (; kt.valid(); kt.next(), ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&bar[B_S_FULL + b], (j >> 1) & 1, abort, p.err, 6)) break;
+      // tcgen05.ld / st are warp-collective (.sync.aligned): every decision in front of one is
+      // made warp-uniform, so no lane can leave the loop or skip a TMEM access alone
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar[B_S_FULL + b], (j >> 1) & 1, abort, p.err, 6))) break;
       tc_fence_after();
       float s[BN];
 #pragma unroll
@@ -320,26 +322,25 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
         mt = fmaxf(mt, s[c]);
       }
       // P_j may only overwrite P_{j-1} (and O may only be rescaled) once PV_{j-1} has finished
-      if (j >= 1 && !mbar_wait(&bar[B_O_DONE], (j - 1) & 1, abort, p.err, 7)) break;
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&bar[B_O_DONE], (j - 1) & 1, abort, p.err, 7))) break;
       tc_fence_after();
       const float m_new = fmaxf(m_used, mt);
-      if (m_new > m_used + RESCALE_THRESHOLD) {
-        if (j >= 1 && m_used != -INFINITY) {  // O holds the previous tiles' sum: scale it down
-          const float alpha = exp2f(m_used - m_new);
-          l *= alpha;
+      const bool raise = m_new > m_used + RESCALE_THRESHOLD;
+      const bool rescale = raise && j >= 1 && m_used != -INFINITY;  // O holds earlier tiles' sum: scale it down
+      if (__any_sync(0xffffffffu, rescale)) {  // the whole warp touches its O rows; others scale by 1
+        const float alpha = rescale ? exp2f(m_used - m_new) : 1.f;
+        l *= alpha;
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            float o[32];
-            tmem_ld32(lane_addr + 256 + c * 32, o);
-            tmem_ld_wait();
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(lane_addr + 256 + c * 32, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(lane_addr + 256 + c * 32, o);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(lane_addr + 256 + c * 32, o);
         }
-        m_used = m_new;
+        tmem_st_wait();
       }
+      if (raise) m_used = m_new;
       // P = exp2(s - m), bf16, K-major 128-byte-swizzled rows
       float rs = 0.f;
 #pragma unroll
@@ -364,8 +365,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
     }
     // epilogue: wait for the last PV, normalise, store
     const int n = j;
-    bool ok = !*abort;
-    if (ok && n >= 1) ok = mbar_wait(&bar[B_O_DONE], (n - 1) & 1, abort, p.err, 8);
+    bool ok = __all_sync(0xffffffffu, !*abort);
+    if (ok && n >= 1) ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_O_DONE], (n - 1) & 1, abort, p.err, 8));
     if (ok && n >= 1) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
