@@ -23,6 +23,8 @@ Design (B200-first):
 
 from __future__ import annotations
 
+import dataclasses
+import json
 import math
 import time
 import zlib
@@ -61,11 +63,18 @@ class GenRequest:
     repetition_penalty: float = 1.0
     logit_bias: dict[int, float] | None = None
     allowed_token_ids: Sequence[int] | None = None  # constrained decoding: only these tokens may be drawn
+    regex: str | None = None  # constrained decoding: the response must match this expression
+    json_schema: Any = None  # ... or be JSON text of this schema (rollout/grammar.py subset)
+    gen_prefix: tuple[int, ...] = ()  # tokens generated before this request resumed (preemption)
+
+    @property
+    def constrained(self) -> bool:
+        return self.regex is not None or self.json_schema is not None
 
     @property
     def filtered(self) -> bool:
         return (self.top_k > 0 or self.top_p < 1.0 or self.min_p > 0.0 or self.presence_penalty != 0.0 or self.frequency_penalty != 0.0
-                or self.repetition_penalty != 1.0 or bool(self.logit_bias) or self.allowed_token_ids is not None)
+                or self.repetition_penalty != 1.0 or bool(self.logit_bias) or self.allowed_token_ids is not None or self.constrained)
 
 
 @dataclass
@@ -92,6 +101,8 @@ class _Seq:
     end_total: int = 0  # total length at which the sequence ends
     force_eos: bool = False
     stop_on_eos: bool = False
+    grammar: Any = None  # TokenGrammar of a constrained request
+    gstate: int = 0  # its automaton state after the tokens generated so far
 
 
 def _stream_id(rid: str) -> int:
@@ -102,8 +113,11 @@ class RolloutEngine:
     def __init__(self, model: Qwen3Model, *, max_batch: int = 256, kv_tokens: int = 1 << 16, page_size: int = 64,
                  max_context: int = 16384, max_prefill_tokens: int = 16384, use_cuda_graph: bool = True, seed: int = 0,
                  eos_token_id: int | None = None, burst: int = 16, kv_memory_saver: bool = False, weight_format: str = "bf16",
-                 tp_group: Any = None, embed_full: torch.Tensor | None = None) -> None:
+                 tp_group: Any = None, embed_full: torch.Tensor | None = None, tokenizer: Any = None) -> None:
         self.model = model
+        self.tokenizer = tokenizer  # token strings for grammar-constrained requests
+        self._grammars: dict[tuple, Any] = {}
+        self._token_strings: list[str] | None = None
         assert weight_format in ("bf16", "fp8_block")
         self.weight_format = weight_format
         self.fp8: dict[int, object] = {}
@@ -428,6 +442,11 @@ class RolloutEngine:
                         self.kv[:, :, extra[0]].copy_(self.kv[:, :, proto.pages[full]])
                     s = _Seq(r, list(r.prompt), shared + extra)
                 s.stream = r.seed_stream if r.seed_stream is not None else _stream_id(r.rid)
+                if r.constrained:
+                    s.grammar = self._grammar(r)
+                    s.gstate = s.grammar.start
+                    for t in r.gen_prefix:
+                        s.gstate = s.grammar.advance(s.gstate, t)
                 s.end_total = min(n + (r.forced_len if r.forced_len is not None else r.max_new_tokens), self.max_context)
                 s.force_eos = r.forced_len is not None
                 s.stop_on_eos = (self.eos in r.stop_token_ids) and r.forced_len is None
@@ -443,7 +462,7 @@ class RolloutEngine:
         if any(s.req.filtered for s in new_seqs):
             rq = [s.req for s in new_seqs]
             as_t = lambda vals, dt: torch.tensor(vals, dtype=dt).to(dev)  # noqa: E731
-            b = self._bias_rows(rq, len(rq))
+            b = self._bias_rows(new_seqs, len(rq))
             tok, lp = paged.sample_filtered(lg, as_t(temps, torch.float32), as_t([r.top_k for r in rq], torch.int64),
                                             as_t([r.top_p for r in rq], torch.float32), as_t([r.min_p for r in rq], torch.float32),
                                             bias=None if b is None else b.to(dev), forced=as_t(forced, torch.int64),
@@ -474,6 +493,8 @@ class RolloutEngine:
         s.tokens.append(tok)
         s.out_ids.append(tok)
         s.out_lps.append(lp)
+        if s.grammar is not None:
+            s.gstate = s.grammar.advance(s.gstate, tok)
         return len(s.tokens) >= s.end_total or (s.stop_on_eos and tok == self.eos) or (tok in s.req.stop_token_ids and not s.force_eos)
 
     def _reason(self, s: _Seq) -> str:
@@ -512,10 +533,10 @@ class RolloutEngine:
         s.pages = []
         r = s.req
         done = len(s.out_ids)
-        cont = GenRequest(rid=f"{r.rid}~p{done}", prompt=list(s.tokens), max_new_tokens=max(1, r.max_new_tokens - done),
-                          temperature=r.temperature, stop_token_ids=r.stop_token_ids,
-                          forced_len=None if r.forced_len is None else r.forced_len - done, forced_token=r.forced_token,
-                          capture_routing=r.capture_routing, seed_stream=s.stream)
+        # same sampling controls; the tokens generated so far stay visible to penalties and grammars
+        cont = dataclasses.replace(r, rid=f"{r.rid}~p{done}", prompt=list(s.tokens), max_new_tokens=max(1, r.max_new_tokens - done),
+                                   forced_len=None if r.forced_len is None else r.forced_len - done, seed_stream=s.stream,
+                                   gen_prefix=tuple(r.gen_prefix) + tuple(s.out_ids))
         self.preempted[cont.rid] = s
         self.waiting.insert(0, cont)
         self.stats["preempted"] = self.stats.get("preempted", 0) + 1
@@ -568,28 +589,53 @@ class RolloutEngine:
                 iostats.add_h2d(h[k][:bucket])
         self.ring_step.zero_()
 
-    def _bias_rows(self, reqs: list, n_rows: int) -> torch.Tensor | None:
-        """(n_rows, V) additive bias from logit_bias / allowed_token_ids (None when unused)."""
-        if not any(r.logit_bias or r.allowed_token_ids is not None for r in reqs):
+    def _bias_rows(self, seqs: list, n_rows: int) -> torch.Tensor | None:
+        """(n_rows, V) additive bias from logit_bias / allowed_token_ids / the row's grammar state
+        (None when unused)."""
+        if not any(s.req.logit_bias or s.req.allowed_token_ids is not None or s.grammar is not None for s in seqs):
             return None
         V = self.cfg.vocab_size
         b = torch.zeros(n_rows, V, dtype=torch.float32)
-        for i, r in enumerate(reqs):
+        for i, s in enumerate(seqs):
+            r = s.req
             if r.allowed_token_ids is not None:
                 b[i].fill_(float("-inf"))
                 b[i, torch.as_tensor(list(r.allowed_token_ids), dtype=torch.long)] = 0.0
+            if s.grammar is not None:
+                m = torch.from_numpy(s.grammar.allowed(s.gstate))
+                b[i, :m.numel()].masked_fill_(~m, float("-inf"))
+                b[i, m.numel():] = float("-inf")
             for t, v in (r.logit_bias or {}).items():
                 b[i, int(t)] += float(v)
         return b
 
+    def _grammar(self, r: GenRequest):  # noqa: ANN202
+        """Token-level automaton of a constrained request (cached per expression / schema)."""
+        from axrl_b200.rollout.grammar import make_token_grammar
+
+        key = (r.regex, json.dumps(r.json_schema, sort_keys=True) if r.json_schema is not None and not isinstance(r.json_schema, str)
+               else r.json_schema, tuple(r.stop_token_ids))
+        g = self._grammars.get(key)
+        if g is None:
+            if self._token_strings is None:
+                if self.tokenizer is None:
+                    raise ValueError("grammar-constrained requests need the engine's tokenizer")
+                n = min(self.cfg.vocab_size, len(self.tokenizer)) if hasattr(self.tokenizer, "__len__") else self.cfg.vocab_size
+                self._token_strings = [self.tokenizer.decode([i]) for i in range(n)]
+            eos = [self.eos] if self.eos is not None else []
+            g = make_token_grammar(regex=r.regex, json_schema=r.json_schema, token_strings=self._token_strings,
+                                   eos_ids=eos + [t for t in r.stop_token_ids if t not in eos])
+            self._grammars[key] = g
+        return g
+
     def _upload_filters(self, seqs: list, bucket: int) -> None:
         self.h_hist.fill_(-1)
         for i, s in enumerate(seqs):
-            tail = s.out_ids[-(self.hist_cap - 1):]
+            tail = (list(s.req.gen_prefix) + s.out_ids)[-(self.hist_cap - 1):]
             if tail:
                 self.h_hist[i, :len(tail)] = torch.as_tensor(tail, dtype=torch.int64)
         self.hist[:bucket].copy_(self.h_hist[:bucket], non_blocking=True)
-        b = self._bias_rows([s.req for s in seqs], bucket)
+        b = self._bias_rows(seqs, bucket)
         if b is not None:
             if self.bias is None:
                 self.bias = torch.zeros(self.max_batch, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
@@ -602,6 +648,8 @@ class RolloutEngine:
         # steps this burst: no row needs more than its remaining tokens
         remaining = max(s.end_total - len(s.tokens) for s in self.running)
         k = max(1, min(self.burst, remaining))
+        if any(s.grammar is not None for s in self.running):
+            k = 1  # a grammar's allowed set depends on the previous token: one step per burst
         # pages for every position this burst may write; preempt the newest sequences when short
         while True:
             short = sum(max(0, self._pages_needed(min(len(s.tokens) + k, s.end_total)) - len(s.pages)) for s in self.running)

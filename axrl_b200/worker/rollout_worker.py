@@ -31,6 +31,13 @@ from axrl_b200.data.conversation import GenerationInput, GenerationOutput
 from axrl_b200.rollout.engine import GenRequest, GenResult, RolloutEngine
 
 
+class _DecodeOnly:
+    """The tokenizer surface a grammar needs: ids -> text."""
+
+    def __init__(self, fn: Any) -> None:
+        self.decode = fn
+
+
 class RolloutWorker:
     def __init__(self, engine: RolloutEngine, sampling: SamplingConfig | None = None, continue_after_abort: bool = True,
                  tensor_store: Any = None, eos_token_id: int | None = None, decode_fn: Any = None) -> None:
@@ -40,6 +47,8 @@ class RolloutWorker:
         self.store = tensor_store
         self.eos = eos_token_id
         self.decode_fn = decode_fn
+        if decode_fn is not None and getattr(engine, "tokenizer", None) is None:
+            engine.tokenizer = _DecodeOnly(decode_fn)  # token strings for tool-call grammars
         self._inbox: queue.Queue = queue.Queue()
         self._pending: dict[str, tuple[asyncio.AbstractEventLoop, asyncio.Future]] = {}
         self._ready = threading.Event()
@@ -94,13 +103,16 @@ class RolloutWorker:
         t0 = time.time()
         inp.event_timing.stamp("worker_received")
         routing = []
+        from axrl_b200.rollout.grammar import tool_call_schema
+
+        schema = tool_call_schema(getattr(inp, "tools", None), getattr(inp, "tool_choice", None))
         while True:
             await asyncio.get_running_loop().run_in_executor(None, self._ready.wait)
             rid = f"{inp.session_id}#{next(self._ids)}"
             req = GenRequest(rid=rid, prompt=ids + out_ids, max_new_tokens=budget - len(out_ids), temperature=sc.temperature,
                              stop_token_ids=stop, capture_routing=inp.capture_routing, top_k=sc.top_k, top_p=sc.top_p, min_p=sc.min_p,
                              presence_penalty=sc.presence_penalty, frequency_penalty=sc.frequency_penalty,
-                             repetition_penalty=sc.repetition_penalty)
+                             repetition_penalty=sc.repetition_penalty, json_schema=schema, gen_prefix=tuple(out_ids))
             res = await self._submit(req)
             out_ids += res.output_ids
             out_lps += res.output_logprobs
