@@ -123,12 +123,14 @@ class MoEBlock(nn.Module):
         self.E, self.k, self.renorm = E, cfg.num_experts_per_tok, cfg.norm_topk_prob
         self.ep = ep
         ep_size = ep.size if ep is not None else 1
+        etp = ep.etp_size if ep is not None else 1
         assert E % ep_size == 0, "experts must split evenly over EP ranks"
-        E_l = E // ep_size  # experts held by this rank
+        assert F % etp == 0, "expert FFN width must split evenly over expert-TP ranks"
+        E_l, F_l = E // ep_size, F // etp  # experts held by this rank, and their FFN columns
         self.router = nn.Parameter(torch.empty(E, H))
-        self.experts_gate_up = nn.Parameter(torch.empty(E_l, 2 * F, H))
-        self.experts_down = nn.Parameter(torch.empty(E_l, H, F))
-        if ep_size > 1:
+        self.experts_gate_up = nn.Parameter(torch.empty(E_l, 2 * F_l, H))
+        self.experts_down = nn.Parameter(torch.empty(E_l, H, F_l))
+        if ep_size > 1 or etp > 1:
             self.experts_gate_up.expert_parallel = True
             self.experts_down.expert_parallel = True
 
@@ -149,7 +151,7 @@ class MoEBlock(nn.Module):
         w, ids = route(logits, self.k, self.renorm, replay, ctx.replay_mask if ctx is not None else None)
         if ctx is not None and ctx.capture is not None:
             ctx.capture[layer_idx] = ids.to(torch.int16)
-        if self.ep is not None and self.ep.enabled:
+        if self.ep is not None and (self.ep.enabled or self.ep.etp_size > 1):
             from axrl_b200.parallel.expert import ep_moe_forward
 
             return ep_moe_forward(self, x, w, ids, self.ep)

@@ -254,7 +254,7 @@ class Qwen3Model(nn.Module):
             if self.tp.enabled and not getattr(p, "tp_replicated", False):
                 ps += 7919 * self.tp.rank
             if getattr(p, "expert_parallel", False):
-                ps += 104729 * self.ep.rank
+                ps += 104729 * self.ep.rank + 15485863 * self.ep.etp_rank
             if p.is_cuda:
                 cg = torch.Generator(device=p.device).manual_seed(ps)
                 p.normal_(0.0, s, generator=cg)

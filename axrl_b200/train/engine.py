@@ -41,6 +41,8 @@ class ParallelCtx:
     ep_group: object | None = None
     ep_size: int = 1
     ep_backend: str = "torch"
+    etp_group: object | None = None  # expert tensor parallelism (ranks holding the same experts' column shards)
+    etp_size: int = 1
     pp_group: object | None = None
     pp_size: int = 1
     vpp_size: int = 1  # virtual (interleaved) pipeline stages per rank
@@ -64,8 +66,9 @@ class TrainEngine:
 
         self.ep = (EPContext.from_group(self.par.ep_group, backend=self.par.ep_backend, hidden=model_cfg.hidden_size,
                                         num_experts=model_cfg.num_experts,
-                                        max_rows=(cfg.max_tokens_per_micro_batch + 1024) * max(1, model_cfg.num_experts_per_tok))
-                   if self.par.ep_size > 1 else EPContext())
+                                        max_rows=(cfg.max_tokens_per_micro_batch + 1024) * max(1, model_cfg.num_experts_per_tok),
+                                        etp_group=self.par.etp_group)
+                   if self.par.ep_size > 1 or self.par.etp_size > 1 else EPContext())
         from axrl_b200.parallel.context_parallel import CPContext
         from axrl_b200.parallel.pipeline import PPContext
 
@@ -74,13 +77,13 @@ class TrainEngine:
         if model is None and self.pp.enabled and self.pp.vpp > 1:
             from axrl_b200.models.qwen3 import VirtualPipelineModel
 
-            model = VirtualPipelineModel(model_cfg, self.pp, tp=self.tp, ep=self.ep if self.ep.enabled else None,
+            model = VirtualPipelineModel(model_cfg, self.pp, tp=self.tp, ep=self.ep if self.ep.active else None,
                                          cp=self.cp if self.cp.enabled else None)
             model.init_weights(cfg.seed)
             model = model.to(device=self.device, dtype=dtype)
             model.inv_freq = model.chunks[0].inv_freq.float()
         if model is None:
-            model = Qwen3Model(model_cfg, tp=self.tp, ep=self.ep if self.ep.enabled else None,
+            model = Qwen3Model(model_cfg, tp=self.tp, ep=self.ep if self.ep.active else None,
                                pp=self.pp if self.pp.enabled else None, cp=self.cp if self.cp.enabled else None)
             model.init_weights(cfg.seed)
             model = model.to(device=self.device, dtype=dtype)
@@ -90,7 +93,7 @@ class TrainEngine:
         self.optim = None
         if not cfg.inference_only:
             dp_dist = (cfg.optimizer.use_distributed_optimizer and self.par.dp_group is not None and self.par.dp_size > 1
-                       and not self.ep.enabled and not self.tp.enabled and not self.cp.enabled and self.par.zero_backend != "off")
+                       and not self.ep.active and not self.tp.enabled and not self.cp.enabled and self.par.zero_backend != "off")
             if dp_dist:
                 from axrl_b200.parallel.zero import BucketedZeroAdamW
 
@@ -248,19 +251,22 @@ class TrainEngine:
         if hasattr(self.optim, "finish_grad_sync"):  # distributed optimizer: reduce-scatter already (mostly) done
             self.optim.finish_grad_sync()
         elif self.par.dp_group is not None and self.par.dp_size > 1:
-            if self.ep.enabled:  # expert weights differ per EP rank: reduce only the dense gradients
+            if self.ep.active:  # expert weights differ per EP / ETP rank: reduce only the dense gradients
                 from axrl_b200.parallel.expert import dense_grad_allreduce
 
                 dense_grad_allreduce(self.model, self.par.dp_group)
             else:
                 dist.all_reduce(self.optim.grad, group=self.par.dp_group)  # replicated-optimizer baseline path
         sq = self.optim.grad_sqnorm()
-        if self.ep.enabled:
+        if self.ep.active:
             from axrl_b200.parallel.expert import expert_params
 
             sq_e = sum(p.main_grad.float().pow(2).sum() for p in expert_params(self.model)).reshape(1)
             sq_all = sq_e.clone()
-            dist.all_reduce(sq_all, group=self.ep.group)
+            if self.ep.enabled:
+                dist.all_reduce(sq_all, group=self.ep.group)
+            if self.ep.etp_size > 1:  # and over the column shards
+                dist.all_reduce(sq_all, group=self.ep.etp_group)
             sq = (sq - sq_e + sq_all).float()
         if self.tp.enabled:
             from axrl_b200.parallel import tensor_parallel as tpl

@@ -16,7 +16,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+def _worker(rank: int, world: int, port: int, q, etp: int = 1) -> None:  # noqa: ANN001
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -30,10 +30,16 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
         full = Qwen3Model(cfg)
         full.init_weights(11)
         state = {k: v.detach().clone() for k, v in full.named_parameters()}
-        ep = EPContext.from_group(dist.group.WORLD)
+        if etp == 1:
+            ep = EPContext.from_group(dist.group.WORLD)
+        else:  # ETP groups {0,1},{2,3}; EP groups {0,2},{1,3} (every rank belongs to one of each)
+            ep_groups = [dist.new_group([r for r in range(world) if r % etp == i]) for i in range(etp)]
+            etp_groups = [dist.new_group(list(range(e * etp, (e + 1) * etp))) for e in range(world // etp)]
+            ep = EPContext.from_group(ep_groups[rank % etp], etp_group=etp_groups[rank // etp])
         model = Qwen3Model(cfg, ep=ep)
         load_ep_shards_from_full(model, state, ep)
-        assert model.layers[0].mlp.experts_gate_up.shape[0] == 4
+        ep_size = world // etp
+        assert model.layers[0].mlp.experts_gate_up.shape == (8 // ep_size, 2 * 32 // etp, 64)
 
         T = 20 + 6 * rank  # different token counts per rank
         g = torch.Generator().manual_seed(100 + rank)
@@ -71,7 +77,15 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
                 ref = ref.clone()
                 dist.all_reduce(ref)  # every rank's tokens reach the owner's experts
                 E_l = p.shape[0]
-                ref = ref[rank * E_l:(rank + 1) * E_l]
+                ref = ref[ep.rank * E_l:(ep.rank + 1) * E_l]
+                if etp > 1:  # this rank's FFN columns
+                    r = ep.etp_rank
+                    if n.endswith("experts_gate_up"):
+                        F, Fl = ref.shape[1] // 2, p.shape[1] // 2
+                        ref = torch.cat([ref[:, r * Fl:(r + 1) * Fl], ref[:, F + r * Fl:F + (r + 1) * Fl]], 1)
+                    else:
+                        Fl = p.shape[2]
+                        ref = ref[:, :, r * Fl:(r + 1) * Fl]
             torch.testing.assert_close(p.main_grad, ref, atol=1e-4, rtol=1e-3, msg=lambda m, n=n: f"{n}: {m}")
         assert len(expert_params(model)) == 2 * cfg.num_hidden_layers
         q.put((rank, "ok"))
@@ -88,6 +102,23 @@ def test_ep2_matches_ep1_with_replay():
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for r, msg in res:
+        assert msg == "ok", f"rank {r}:\n{msg}"
+
+
+def test_ep2_x_etp2_matches_ep1():
+    """Expert tensor parallelism (Megatron ``expert_tensor_parallel_size``, ``axrl/configs.py:384``):
+    4 ranks = EP 2 x ETP 2; each expert's FFN columns split over an ETP pair, rows all-gathered
+    before and partial sums reduce-scattered after the expert FFN."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 4, port, q, 2)) for r in range(4)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
