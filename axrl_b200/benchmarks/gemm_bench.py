@@ -38,7 +38,7 @@ def main() -> None:
             for v in a.variants.split(","):
                 if v == "skinny" and M > 64:
                     continue
-                if (v == "swapab" and M > 256) or (v == "tma" and M > 32):
+                if (v == "swapab" and M > 64) or (v == "tma" and M > 32):
                     continue
                 try:
                     fn = (lambda: e.linear_fwd(x, w)) if v == "auto" else (lambda v=v: e.linear_variant(x, w, v))

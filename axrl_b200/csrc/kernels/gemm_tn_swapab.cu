@@ -22,26 +22,12 @@ struct SwapN64 {
   using Epi = cutlass::epilogue::TmaWarpSpecialized1Sm;
 };
 
-struct SwapN128 {
-  using Tile = Shape<_128, _128, _64>;
-  using Cluster = Shape<_1, _1, _1>;
-  using Kernel = cutlass::gemm::KernelTmaWarpSpecialized1SmSm100;
-  using Epi = cutlass::epilogue::TmaWarpSpecialized1Sm;
-};
-struct SwapN256 {
-  using Tile = Shape<_128, _256, _64>;
-  using Cluster = Shape<_1, _1, _1>;
-  using Kernel = cutlass::gemm::KernelTmaWarpSpecialized1SmSm100;
-  using Epi = cutlass::epilogue::TmaWarpSpecialized1Sm;
-};
-
 // A = W (N x K, K contiguous), B = X (M x K, K contiguous), D = Y viewed as N x M column-major.
-// Up to 256 activation rows: each CTA streams 128 weight rows against all the activation rows.
+// (128/256-row swap-AB tiles were measured slower than the 1-SM 128x128 stream-K GEMM from 96
+// rows on, so swap-AB stops at 64 rows.)
 void tn_swapab(const void* X, const void* W, const void* C, void* D, int M, int N, int K, cudaStream_t st) {
   if (M <= 32) Gemm<RM, CM, cutlass::bfloat16_t, SwapN32, SK, CM>::run(W, X, C, D, N, M, K, 1.f, C ? 1.f : 0.f, st);
-  else if (M <= 64) Gemm<RM, CM, cutlass::bfloat16_t, SwapN64, SK, CM>::run(W, X, C, D, N, M, K, 1.f, C ? 1.f : 0.f, st);
-  else if (M <= 128) Gemm<RM, CM, cutlass::bfloat16_t, SwapN128, SK, CM>::run(W, X, C, D, N, M, K, 1.f, C ? 1.f : 0.f, st);
-  else Gemm<RM, CM, cutlass::bfloat16_t, SwapN256, SK, CM>::run(W, X, C, D, N, M, K, 1.f, C ? 1.f : 0.f, st);
+  else Gemm<RM, CM, cutlass::bfloat16_t, SwapN64, SK, CM>::run(W, X, C, D, N, M, K, 1.f, C ? 1.f : 0.f, st);
 }
 
 }  // namespace gemm

@@ -180,7 +180,7 @@ at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant) {
   auto y = at::empty({M, N}, x.options());
   if (M == 0) return y;
   if (variant == "swapab") {
-    AX_CHECK(M <= 256, "swapab needs M <= 256");
+    AX_CHECK(M <= 64, "swapab needs M <= 64");
     gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K, stream());
   } else if (variant == "cutlass") {
     tn(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K);

