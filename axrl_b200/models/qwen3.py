@@ -63,6 +63,21 @@ class Qwen3Config:
     decoder_sparse_step: int = 1
     mlp_only_layers: list[int] = field(default_factory=list)
     initializer_range: float = 0.02
+    # hybrid linear / full attention (Qwen3-Next / Qwen3.5 style): per-layer "linear_attention"
+    # (Gated DeltaNet, models/gdn.py) or "full_attention"; None = every layer full attention
+    layer_types: list[str] | None = None
+    linear_num_key_heads: int = 16
+    linear_num_value_heads: int = 32
+    linear_key_head_dim: int = 128
+    linear_value_head_dim: int = 128
+    linear_conv_kernel_dim: int = 4
+
+    def layer_is_linear(self, i: int) -> bool:
+        return self.layer_types is not None and self.layer_types[i] == "linear_attention"
+
+    @property
+    def is_hybrid(self) -> bool:
+        return self.layer_types is not None and "linear_attention" in self.layer_types
 
     @property
     def is_moe(self) -> bool:
@@ -108,6 +123,11 @@ PRESETS: dict[str, Qwen3Config] = {
     "tiny-moe": Qwen3Config(vocab_size=1024, hidden_size=256, intermediate_size=768, num_hidden_layers=2, num_attention_heads=4,
                             num_key_value_heads=2, head_dim=64, rope_theta=10000.0, num_experts=8, num_experts_per_tok=2,
                             moe_intermediate_size=128),
+    # Hybrid plumbing model: 4 layers, three Gated DeltaNet layers per full-attention layer.
+    "tiny-gdn": Qwen3Config(vocab_size=1024, hidden_size=256, intermediate_size=768, num_hidden_layers=4, num_attention_heads=4,
+                            num_key_value_heads=2, head_dim=64, rope_theta=10000.0,
+                            layer_types=["linear_attention", "linear_attention", "linear_attention", "full_attention"],
+                            linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32),
 }
 
 
@@ -170,7 +190,13 @@ class DecoderLayer(nn.Module):
         super().__init__()
         self.layer_idx = layer_idx
         self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
-        self.self_attn = Attention(cfg, tp_size)
+        if cfg.layer_is_linear(layer_idx):
+            from axrl_b200.models.gdn import GatedDeltaNet
+
+            assert tp_size == 1, "Gated DeltaNet layers run without tensor parallelism"
+            self.self_attn: nn.Module = GatedDeltaNet(cfg)
+        else:
+            self.self_attn = Attention(cfg, tp_size)
         self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
         if cfg.layer_is_moe(layer_idx):
             from axrl_b200.models.moe import MoEBlock
@@ -227,6 +253,8 @@ class Qwen3Model(nn.Module):
         self.grad_ready_hook = None  # set by an optimizer that reduces gradients during backward
         for layer in self.layers:
             layer.self_attn.cp = cp
+            if cp is not None and getattr(cp, "enabled", False) and cfg.layer_is_linear(layer.layer_idx):
+                raise NotImplementedError("Gated DeltaNet layers with context parallelism are not built")
         if tp_size > 1:
             for name, p in self.named_parameters():
                 if p.dim() < 2 or ".mlp.router" in name or ".mlp.experts" in name:
@@ -249,7 +277,7 @@ class Qwen3Model(nn.Module):
             if p.dim() == 1:
                 p.fill_(1.0)
                 continue
-            s = out_std if name.endswith(("o_proj", "down_proj")) else std
+            s = out_std if name.endswith(("o_proj", "down_proj", "out_proj")) else std
             ps = seed * 1000003 + zlib.crc32(self.global_name(name).encode())
             if self.tp.enabled and not getattr(p, "tp_replicated", False):
                 ps += 7919 * self.tp.rank
@@ -335,11 +363,18 @@ def hf_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
     for i, layer in enumerate(model.layers):
         p = f"model.layers.{i}."
         a = layer.self_attn
-        q, k, v = a.qkv_proj.split([a.nq * a.d, a.nkv * a.d, a.nkv * a.d], 0)
-        out |= {p + "self_attn.q_proj.weight": q, p + "self_attn.k_proj.weight": k, p + "self_attn.v_proj.weight": v,
-                p + "self_attn.o_proj.weight": a.o_proj, p + "self_attn.q_norm.weight": a.q_norm,
-                p + "self_attn.k_norm.weight": a.k_norm, p + "input_layernorm.weight": layer.input_layernorm.weight,
+        out |= {p + "input_layernorm.weight": layer.input_layernorm.weight,
                 p + "post_attention_layernorm.weight": layer.post_attention_layernorm.weight}
+        if cfg.layer_is_linear(i):  # HF Qwen3-Next / 3.5 "linear_attn" names
+            q = p + "linear_attn."
+            out |= {q + "in_proj_qkv.weight": a.in_proj_qkv, q + "in_proj_z.weight": a.in_proj_z, q + "in_proj_b.weight": a.in_proj_b,
+                    q + "in_proj_a.weight": a.in_proj_a, q + "conv1d.weight": a.conv_weight.unsqueeze(1), q + "dt_bias": a.dt_bias,
+                    q + "A_log": a.A_log, q + "norm.weight": a.norm_weight, q + "out_proj.weight": a.out_proj}
+        else:
+            q, k, v = a.qkv_proj.split([a.nq * a.d, a.nkv * a.d, a.nkv * a.d], 0)
+            out |= {p + "self_attn.q_proj.weight": q, p + "self_attn.k_proj.weight": k, p + "self_attn.v_proj.weight": v,
+                    p + "self_attn.o_proj.weight": a.o_proj, p + "self_attn.q_norm.weight": a.q_norm,
+                    p + "self_attn.k_norm.weight": a.k_norm}
         if cfg.layer_is_moe(i):
             out |= layer.mlp.hf_tensors(p)
         else:

@@ -103,6 +103,7 @@ class _Seq:
     stop_on_eos: bool = False
     grammar: Any = None  # TokenGrammar of a constrained request
     gstate: int = 0  # its automaton state after the tokens generated so far
+    lslot: int = -1  # slot of its linear-attention (Gated DeltaNet) states, hybrid models
 
 
 def _stream_id(rid: str) -> int:
@@ -132,7 +133,8 @@ class RolloutEngine:
         self.max_prefill_tokens = max_prefill_tokens
         self.eos = 0 if eos_token_id is None else eos_token_id
         self.burst = burst
-        L, Hkv, D = cfg.num_hidden_layers, model.layers[0].self_attn.nkv, cfg.head_dim
+        attn0 = next(layer.self_attn for layer in model.layers if hasattr(layer.self_attn, "nkv"))  # a full-attention layer
+        L, Hkv, D = cfg.num_hidden_layers, attn0.nkv, cfg.head_dim
         self.num_pages = max(2, math.ceil(kv_tokens / page_size)) + 1  # last page: scratch for frozen/padded rows
         self.scratch_page = self.num_pages - 1
         self.kv_buf = None
@@ -148,7 +150,7 @@ class RolloutEngine:
         self.preempted: dict[str, _Seq] = {}
         self.bm = make_block_manager(self.num_pages - 1, page_size)
         self.max_pages = math.ceil(max_context / page_size) + 1
-        self.ws = paged.DecodeWorkspace(max_batch, model.layers[0].self_attn.nq, max_context + page_size, self.device) if self.is_cuda else None
+        self.ws = paged.DecodeWorkspace(max_batch, attn0.nq, max_context + page_size, self.device) if self.is_cuda else None
         self.use_graph = use_cuda_graph and self.is_cuda and not cfg.is_moe
         self.graphs: dict[int, tuple] = {}
         self.seed = seed
@@ -156,6 +158,8 @@ class RolloutEngine:
         self.waiting: list[GenRequest] = []
         self.running: list[_Seq] = []
         self.stats = {"prefill_tokens": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_s": 0.0, "decode_s": 0.0, "bursts": 0}
+        if tp_group is not None and cfg.is_hybrid:
+            raise NotImplementedError("tensor-parallel engines for hybrid (Gated DeltaNet) models are not built")
         self._alloc_static()
         self.tp = None
         if tp_group is not None and torch.distributed.get_world_size(tp_group) > 1:
@@ -202,8 +206,17 @@ class RolloutEngine:
             "tok": z(torch.int64, B), "pos": z(torch.int32, B), "len": z(torch.int32, B), "slot": z(torch.int64, B),
             "bt": z(torch.int32, B, self.max_pages), "temp": z(torch.float32, B), "rid": z(torch.int32, B),
             "forced": torch.full((B,), -1, dtype=torch.int64, device=dev), "end_total": z(torch.int32, B),
-            "force_eos": z(torch.int32, B), "stop_on_eos": z(torch.int32, B),
+            "force_eos": z(torch.int32, B), "stop_on_eos": z(torch.int32, B), "lslot": torch.full((B,), B, dtype=torch.int64, device=dev),
         }
+        # hybrid models: per-sequence Gated DeltaNet states (conv window + recurrent state), one slot
+        # per running sequence; slot B is scratch for padded rows
+        self.gdn_index = {li: i for i, li in enumerate(li for li in range(self.cfg.num_hidden_layers) if self.cfg.layer_is_linear(li))}
+        self.gdn_free = list(range(B - 1, -1, -1))
+        if self.gdn_index:
+            a = self.model.layers[next(iter(self.gdn_index))].self_attn
+            n = len(self.gdn_index)
+            self.gdn_conv = z(torch.float32, n, B + 1, a.kernel - 1, a.conv_dim)
+            self.gdn_S = z(torch.float32, n, B + 1, a.nv, a.dk, a.dv)
         self.s_seed = z(torch.int64, 1)
         # filtered sampling (top-k/p, min-p, penalties, bias / allowed set): per-row controls
         self.st.update({"top_k": torch.full((B,), -1, dtype=torch.int64, device=dev), "top_p": torch.ones(B, device=dev),
@@ -288,13 +301,19 @@ class RolloutEngine:
             return
         _ext.ext().linear_fwd_into(x.contiguous(), w, out)
 
-    def _layers(self, h, pos, slots, attend, capture=None):  # noqa: ANN001, ANN202
+    def _layers(self, h, pos, slots, attend, capture=None, mix=None):  # noqa: ANN001, ANN202
+        """``mix(li, module, x)``: the token mixer of linear-attention layers (hybrid models)."""
         if self.tp is not None:
             return self._layers_tp(h, pos, slots, attend)
         inv = self.model.inv_freq
         for li, layer in enumerate(self.model.layers):
             a = layer.self_attn
             x = self._rms(h, layer.input_layernorm.weight)
+            if li in self.gdn_index:
+                h = h + mix(li, a, x)
+                x = self._rms(h, layer.post_attention_layernorm.weight)
+                h = self._mlp(layer, x, h, capture, li)
+                continue
             qkv = self._lin(x, a.qkv_proj)
             q, k, v = paged.qk_norm_rope_cache(qkv, a.q_norm, a.k_norm, pos, inv, a.nq, a.nkv, a.eps,
                                                self.kv[li, 0], self.kv[li, 1], slots)
@@ -420,9 +439,21 @@ class RolloutEngine:
             spec = spec.to(dev)
             iostats.add_h2d(ids_t, pos_t, slots_t, spec.qseg, spec.kr, spec.kseg, spec.qr, spec.fwd_tiles, spec.bwd_tiles)
         capture = {} if self.cfg.is_moe and any(m.capture_routing for g in groups for m in g) else None
+        lslots = [[self.gdn_free.pop() for _ in members] for members in groups] if self.gdn_index else None
+
+        def gdn_prefill(li: int, a, x: torch.Tensor) -> torch.Tensor:  # noqa: ANN001
+            states: list = []
+            out = a.forward(x, None, None, spec, states=states)
+            gi = self.gdn_index[li]
+            for (cs, S), sl in zip(states, lslots):  # every member of a group starts from the prompt's state
+                for slot in sl:
+                    self.gdn_conv[gi, slot].copy_(cs)
+                    self.gdn_S[gi, slot].copy_(S)
+            return out
+
         with torch.no_grad():
             h = self._embed(ids_t)
-            h = self._layers(h, pos_t, slots_t, lambda li, q, k, v: ops.attention(q, k, v, spec), capture)
+            h = self._layers(h, pos_t, slots_t, lambda li, q, k, v: ops.attention(q, k, v, spec), capture, mix=gdn_prefill)
             logits = self._logits(h.index_select(0, torch.tensor(lasts, device=dev)))
         rows, temps, rids, forced = [], [], [], []
         new_seqs: list[_Seq] = []
@@ -442,6 +473,8 @@ class RolloutEngine:
                         self.kv[:, :, extra[0]].copy_(self.kv[:, :, proto.pages[full]])
                     s = _Seq(r, list(r.prompt), shared + extra)
                 s.stream = r.seed_stream if r.seed_stream is not None else _stream_id(r.rid)
+                if lslots is not None:
+                    s.lslot = lslots[gi][mi]
                 if r.constrained:
                     s.grammar = self._grammar(r)
                     s.gstate = s.grammar.start
@@ -504,8 +537,14 @@ class RolloutEngine:
             return "stop"
         return "length"
 
+    def _free_lslot(self, s: _Seq) -> None:
+        if s.lslot >= 0:
+            self.gdn_free.append(s.lslot)
+            s.lslot = -1
+
     def _finish(self, s: _Seq, reason: str) -> GenResult:
         self.bm.release(s.pages)
+        self._free_lslot(s)
         routing = np.concatenate(s.routing, 0) if s.routing else None
         return self._unwrap(GenResult(s.req.rid, s.out_ids, s.out_lps, reason, len(s.req.prompt), s.cached, routing))
 
@@ -531,6 +570,7 @@ class RolloutEngine:
         """Free a running sequence's pages; it resumes later by re-prefilling prompt + partial output."""
         self.bm.release(s.pages)
         s.pages = []
+        self._free_lslot(s)
         r = s.req
         done = len(s.out_ids)
         # same sampling controls; the tokens generated so far stay visible to penalties and grammars
@@ -573,6 +613,7 @@ class RolloutEngine:
             h["top_k"][i], h["top_p"][i], h["min_p"][i] = r.top_k, r.top_p, r.min_p
             h["pres"][i], h["freq"][i], h["rep"][i] = r.presence_penalty, r.frequency_penalty, r.repetition_penalty
             h["ngen"][i] = min(len(s.out_ids), self.hist_cap - 1)
+            h["lslot"][i] = s.lslot if s.lslot >= 0 else self.max_batch
         self.filtered_mode = any(s.req.filtered for s in self.running)
         if self.filtered_mode:
             self._upload_filters(self.running, bucket)
@@ -583,6 +624,7 @@ class RolloutEngine:
             h["pos"][B:bucket] = 0
             h["forced"][B:bucket] = -1
             h["end_total"][B:bucket] = 0
+            h["lslot"][B:bucket] = self.max_batch
         for k, dst in self.st.items():
             dst[:bucket].copy_(h[k][:bucket], non_blocking=True)
             if self.is_cuda:
@@ -748,8 +790,18 @@ class RolloutEngine:
         if self.ws is not None:
             self.ws.plan(lens)  # one work list for all layers of this step
         h = self._embed(tok)
+        lsl = st["lslot"][:bucket]
+
+        def gdn_decode(li: int, a, x: torch.Tensor) -> torch.Tensor:  # noqa: ANN001
+            gi = self.gdn_index[li]
+            conv, S = self.gdn_conv[gi].index_select(0, lsl), self.gdn_S[gi].index_select(0, lsl)
+            out = a.step(x, conv, S)
+            self.gdn_conv[gi].index_copy_(0, lsl, conv)
+            self.gdn_S[gi].index_copy_(0, lsl, S)
+            return out
+
         h = self._layers(h, pos, slots, lambda li, q, k, v: paged.paged_decode_attention(q, self.kv[li, 0], self.kv[li, 1], bt, lens, self.ws, planned=True),
-                         capture)
+                         capture, mix=gdn_decode)
         logits = self._logits(h)
         if self.filtered_mode:
             t, l = paged.sample_filtered(logits, st["temp"][:bucket], st["top_k"][:bucket], st["top_p"][:bucket], st["min_p"][:bucket],

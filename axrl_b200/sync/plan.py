@@ -52,12 +52,24 @@ def qwen3_param_specs(cfg: Qwen3Config) -> list[ParamSpec]:
     specs = [ParamSpec("embed_tokens", (Sub(V, H, 0),))]
     for i in range(cfg.num_hidden_layers):
         p = f"layers.{i}."
+        specs.append(ParamSpec(p + "input_layernorm.weight", (Sub(1, H, -1),)))
+        if cfg.layer_is_linear(i):  # Gated DeltaNet mixer: replicated (no TP sharding)
+            kd, vd = cfg.linear_num_key_heads * cfg.linear_key_head_dim, cfg.linear_num_value_heads * cfg.linear_value_head_dim
+            nv, K = cfg.linear_num_value_heads, cfg.linear_conv_kernel_dim
+            a = p + "self_attn."
+            specs += [ParamSpec(a + "in_proj_qkv", (Sub(2 * kd + vd, H, -1),)), ParamSpec(a + "in_proj_z", (Sub(vd, H, -1),)),
+                      ParamSpec(a + "in_proj_b", (Sub(nv, H, -1),)), ParamSpec(a + "in_proj_a", (Sub(nv, H, -1),)),
+                      ParamSpec(a + "conv_weight", (Sub(2 * kd + vd, K, -1),)), ParamSpec(a + "dt_bias", (Sub(1, nv, -1),)),
+                      ParamSpec(a + "A_log", (Sub(1, nv, -1),)), ParamSpec(a + "norm_weight", (Sub(1, cfg.linear_value_head_dim, -1),)),
+                      ParamSpec(a + "out_proj", (Sub(H, vd, -1),))]
+        else:
+            specs += [
+                ParamSpec(p + "self_attn.qkv_proj", (Sub(nq * D, H, 0), Sub(nkv * D, H, 0), Sub(nkv * D, H, 0))),
+                ParamSpec(p + "self_attn.o_proj", (Sub(H, nq * D, 1),)),
+                ParamSpec(p + "self_attn.q_norm", (Sub(1, D, -1),)),
+                ParamSpec(p + "self_attn.k_norm", (Sub(1, D, -1),)),
+            ]
         specs += [
-            ParamSpec(p + "input_layernorm.weight", (Sub(1, H, -1),)),
-            ParamSpec(p + "self_attn.qkv_proj", (Sub(nq * D, H, 0), Sub(nkv * D, H, 0), Sub(nkv * D, H, 0))),
-            ParamSpec(p + "self_attn.o_proj", (Sub(H, nq * D, 1),)),
-            ParamSpec(p + "self_attn.q_norm", (Sub(1, D, -1),)),
-            ParamSpec(p + "self_attn.k_norm", (Sub(1, D, -1),)),
             ParamSpec(p + "post_attention_layernorm.weight", (Sub(1, H, -1),)),
             ParamSpec(p + "mlp.gate_up_proj", (Sub(F, H, 0), Sub(F, H, 0))),
             ParamSpec(p + "mlp.down_proj", (Sub(H, F, 1),)),

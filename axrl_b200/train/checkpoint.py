@@ -112,13 +112,17 @@ def mcore_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
     def add(k: str, v: torch.Tensor) -> None:
         per.setdefault(k, []).append(v.detach())
 
-    for layer in model.layers:
+    for i, layer in enumerate(model.layers):
         a = layer.self_attn
         add("decoder.layers.self_attention.linear_qkv.layer_norm_weight", layer.input_layernorm.weight)
-        add("decoder.layers.self_attention.linear_qkv.weight", _qkv_to_mcore(a.qkv_proj.detach(), a.nq, a.nkv, a.d))
-        add("decoder.layers.self_attention.linear_proj.weight", a.o_proj)
-        add("decoder.layers.self_attention.q_layernorm.weight", a.q_norm)
-        add("decoder.layers.self_attention.k_layernorm.weight", a.k_norm)
+        if cfg.is_hybrid:  # heterogeneous mixers: one entry per layer instead of a stacked one
+            for n, t in _mixer_tensors(cfg, i, a).items():
+                out[n] = t.detach()
+        else:
+            add("decoder.layers.self_attention.linear_qkv.weight", _qkv_to_mcore(a.qkv_proj.detach(), a.nq, a.nkv, a.d))
+            add("decoder.layers.self_attention.linear_proj.weight", a.o_proj)
+            add("decoder.layers.self_attention.q_layernorm.weight", a.q_norm)
+            add("decoder.layers.self_attention.k_layernorm.weight", a.k_norm)
         mlp = layer.mlp
         if hasattr(mlp, "router"):
             add("decoder.layers.pre_mlp_layernorm.weight", layer.post_attention_layernorm.weight)
@@ -135,6 +139,17 @@ def mcore_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
     return out
 
 
+def _mixer_tensors(cfg, i: int, a) -> dict[str, torch.Tensor]:  # noqa: ANN001
+    """Token-mixer tensors of layer ``i`` of a hybrid model, keyed per layer."""
+    p = f"decoder.layers.{i}."
+    if cfg.layer_is_linear(i):
+        return {p + f"linear_attention.{n}": getattr(a, n) for n in
+                ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "conv_weight", "dt_bias", "A_log", "norm_weight", "out_proj")}
+    return {p + "self_attention.linear_qkv.weight": _qkv_to_mcore(a.qkv_proj.detach(), a.nq, a.nkv, a.d),
+            p + "self_attention.linear_proj.weight": a.o_proj, p + "self_attention.q_layernorm.weight": a.q_norm,
+            p + "self_attention.k_layernorm.weight": a.k_norm}
+
+
 @torch.no_grad()
 def load_mcore_state_dict(model: Qwen3Model, sd: dict[str, torch.Tensor]) -> None:
     model.embed_tokens.copy_(sd["embedding.word_embeddings.weight"])
@@ -145,10 +160,21 @@ def load_mcore_state_dict(model: Qwen3Model, sd: dict[str, torch.Tensor]) -> Non
         a = layer.self_attn
         g = lambda k: sd[k][i]  # noqa: E731
         layer.input_layernorm.weight.copy_(g("decoder.layers.self_attention.linear_qkv.layer_norm_weight"))
-        a.qkv_proj.copy_(_qkv_from_mcore(g("decoder.layers.self_attention.linear_qkv.weight"), a.nq, a.nkv, a.d))
-        a.o_proj.copy_(g("decoder.layers.self_attention.linear_proj.weight"))
-        a.q_norm.copy_(g("decoder.layers.self_attention.q_layernorm.weight"))
-        a.k_norm.copy_(g("decoder.layers.self_attention.k_layernorm.weight"))
+        if model.cfg.is_hybrid:
+            p = f"decoder.layers.{i}."
+            if model.cfg.layer_is_linear(i):
+                for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "conv_weight", "dt_bias", "A_log", "norm_weight", "out_proj"):
+                    getattr(a, n).copy_(sd[p + f"linear_attention.{n}"])
+            else:
+                a.qkv_proj.copy_(_qkv_from_mcore(sd[p + "self_attention.linear_qkv.weight"], a.nq, a.nkv, a.d))
+                a.o_proj.copy_(sd[p + "self_attention.linear_proj.weight"])
+                a.q_norm.copy_(sd[p + "self_attention.q_layernorm.weight"])
+                a.k_norm.copy_(sd[p + "self_attention.k_layernorm.weight"])
+        else:
+            a.qkv_proj.copy_(_qkv_from_mcore(g("decoder.layers.self_attention.linear_qkv.weight"), a.nq, a.nkv, a.d))
+            a.o_proj.copy_(g("decoder.layers.self_attention.linear_proj.weight"))
+            a.q_norm.copy_(g("decoder.layers.self_attention.q_layernorm.weight"))
+            a.k_norm.copy_(g("decoder.layers.self_attention.k_layernorm.weight"))
         mlp = layer.mlp
         if hasattr(mlp, "router"):
             layer.post_attention_layernorm.weight.copy_(g("decoder.layers.pre_mlp_layernorm.weight"))
