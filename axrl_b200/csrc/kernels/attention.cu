@@ -524,12 +524,12 @@ __global__ void f32_to_bf16_k(const float* __restrict__ a, bf16* __restrict__ b,
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                     double scale);
 
-// Forward implementation: AXRL_ATTN_FWD=tc selects the tcgen05 kernel (attention_tc.cu), anything
-// else the mma.sync kernel below.
+// Forward implementation: the tcgen05 kernel (attention_tc.cu); AXRL_ATTN_FWD=mma selects the
+// mma.sync kernel below (benchmarking).
 static bool use_tc_forward() {
   static int on = [] {
     const char* e = std::getenv("AXRL_ATTN_FWD");
-    return (e && std::string(e) == "tc") ? 1 : 0;
+    return (e && std::string(e) == "mma") ? 0 : 1;
   }();
   return on != 0;
 }
