@@ -101,3 +101,13 @@ def available() -> bool:
         return True
     except Exception:  # noqa: BLE001
         return False
+
+
+def check_kernel_waits() -> None:
+    """Raise if the tcgen05 attention (bounded internal waits) gave up on a wait since the process
+    started: its outputs are then incomplete.  Synchronises the stream."""
+    e = ext()
+    codes = {"tcgen05 attention": int(e.attn_tc_error())}
+    bad = {k: v for k, v in codes.items() if v}
+    if bad:
+        raise RuntimeError(f"kernel wait timed out: {bad}")

@@ -294,6 +294,10 @@ class TrainEngine:
         out["num_micro_batches"] = len(mbs)
         out["step_time_sec"] = time.perf_counter() - t0
         out["lr"] = self.current_lr()
+        if self.device.type == "cuda":
+            from axrl_b200.ops import _ext
+
+            _ext.check_kernel_waits()
         return out
 
     def _forward_backward_pp(self, batch: SampleBatch, mbs: list[PackedMicroBatch], trainer, temperature: float,  # noqa: ANN001
