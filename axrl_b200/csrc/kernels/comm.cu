@@ -136,14 +136,14 @@ void p2p_broadcast_shard(at::Tensor ptrs, at::Tensor master, int64_t s0, int64_t
 }
 
 void mc_reduce_shard(int64_t mc_ptr, at::Tensor local, int64_t s0, int64_t n, at::Tensor sq) {
-  AX_CHECK(mc_ptr != 0 && n % 4 == 0 && s0 % 4 == 0, "multicast pointer and 16-byte aligned shard required");
+  AX_CHECK(mc_ptr != 0 && n % 4 == 0 && s0 % 4 == 0, "NVLS group address and 16-byte aligned shard required");
   if (n == 0) return;
   mc_reduce_shard_k<<<comm_ctas(n / 4), 256, 0, stream()>>>((uint64_t)mc_ptr, local.data_ptr<float>(), s0, n, sq.data_ptr<float>());
   AX_LAUNCH_OK();
 }
 
 void mc_broadcast_shard(int64_t mc_ptr, at::Tensor master, int64_t s0, int64_t n) {
-  AX_CHECK(mc_ptr != 0 && n % 8 == 0 && s0 % 8 == 0, "multicast pointer and 16-byte aligned shard required");
+  AX_CHECK(mc_ptr != 0 && n % 8 == 0 && s0 % 8 == 0, "NVLS group address and 16-byte aligned shard required");
   if (n == 0) return;
   mc_broadcast_shard_k<<<comm_ctas(n / 8), 256, 0, stream()>>>((uint64_t)mc_ptr, master.data_ptr<float>(), s0, n);
   AX_LAUNCH_OK();

@@ -1,8 +1,6 @@
 // bf16 GEMMs on 5th-gen tensor cores (tcgen05.mma, TMEM accumulators, TMA operand loads),
-// composed from CUTLASS sm100 collectives.  Cluster shapes are chosen so that no operand
-// load uses cluster multicast: 1-SM kernels run with cluster (1,1,1); 2-SM kernels
-// (cta_group::2, one MMA tile spanning an SM pair) run with cluster (2,1,1), where each
-// CTA of the pair loads its own half of A and of B.
+// composed from CUTLASS sm100 collectives.  Every configuration is a 1-SM kernel without a
+// thread-block cluster, so each CTA loads its own operand tiles.
 //
 // Convention: D[M,N] = alpha * A[M,K] @ B[K,N] + beta * C[M,N], row-major D/C.
 //   LayoutA RowMajor    -> A stored M x K (K contiguous)
@@ -38,11 +36,14 @@ struct Sm1Narrow {
   using Kernel = cutlass::gemm::KernelTmaWarpSpecialized1SmSm100;
   using Epi = cutlass::epilogue::TmaWarpSpecialized1Sm;
 };
+// Large problems: 1-SM 128x256 tiles.  Every configuration runs without a thread-block cluster
+// (cluster 1x1x1), so no operand tile is ever loaded with cluster multicast: each CTA loads its
+// own copy (this code also runs in multi-GPU processes).
 struct Sm2 {
-  using Tile = Shape<_256, _256, _64>;
-  using Cluster = Shape<_2, _1, _1>;
-  using Kernel = cutlass::gemm::KernelTmaWarpSpecialized2SmSm100;
-  using Epi = cutlass::epilogue::TmaWarpSpecialized2Sm;
+  using Tile = Shape<_128, _256, _64>;
+  using Cluster = Shape<_1, _1, _1>;
+  using Kernel = cutlass::gemm::KernelTmaWarpSpecialized1SmSm100;
+  using Epi = cutlass::epilogue::TmaWarpSpecialized1Sm;
 };
 
 // Stream-K decomposition override for tuning: mode 0 heuristic, 1 data-parallel, 2 split-K

@@ -1,4 +1,4 @@
-// Forward GEMM, large M: 2-SM 256x256 tiles.
+// Forward GEMM, large M: 1-SM 128x256 tiles (no cluster).
 #include "gemm_sm100.cuh"
 
 namespace ax {

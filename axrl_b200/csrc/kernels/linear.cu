@@ -1,5 +1,5 @@
 // torch-facing GEMM wrappers used by ops.linear / ops.logprob / the rollout engine.
-// Tile-config choice by M (tokens): >= 512 -> 2-SM 256x256 data-parallel tiles;
+// Tile-config choice by M (tokens): >= 512 -> 1-SM 128x256 data-parallel tiles;
 // 65..511 -> 1-SM 128x128 stream-K; <= 64 -> 1-SM 128x64 stream-K (decode: weight streaming).
 #include <string>
 
