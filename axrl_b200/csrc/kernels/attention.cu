@@ -522,17 +522,19 @@ __global__ void f32_to_bf16_k(const float* __restrict__ a, bf16* __restrict__ b,
 }  // namespace attn
 
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
-                                    double scale);
+                                    double scale, bool double_p);
 
 // Forward implementation: the tcgen05 kernel (attention_tc.cu); AXRL_ATTN_FWD=mma selects the
-// mma.sync kernel below (benchmarking).
-static bool use_tc_forward() {
-  static int on = [] {
+// mma.sync kernel below, AXRL_ATTN_FWD=tc2 the tcgen05 kernel with double-buffered P.
+static int tc_forward_mode() {
+  static int mode = [] {
     const char* e = std::getenv("AXRL_ATTN_FWD");
-    return (e && std::string(e) == "mma") ? 0 : 1;
+    const std::string v = e ? e : "";
+    return v == "mma" ? 0 : v == "tc2" ? 2 : 1;
   }();
-  return on != 0;
+  return mode;
 }
+static bool use_tc_forward() { return tc_forward_mode() != 0; }
 
 std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                      double scale);
@@ -540,7 +542,7 @@ std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, a
 // q: (T,Hq,128) k,v: (Tk,Hkv,128) -> o (T,Hq,128), lse2 (Hq,T)
 std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                  double scale) {
-  if (use_tc_forward()) return attn_fwd_tc(q, k, v, qseg, kr, tiles, scale);
+  if (use_tc_forward()) return attn_fwd_tc(q, k, v, qseg, kr, tiles, scale, tc_forward_mode() == 2);
   return attn_fwd_mma(q, k, v, qseg, kr, tiles, scale);
 }
 

@@ -41,7 +41,8 @@ constexpr long WAIT_LIMIT = 1L << 24;
 constexpr float RESCALE_THRESHOLD = 8.f;
 
 // barrier slots
-constexpr int B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 3, B_S_FULL = 5, B_S_FREE = 7, B_P_FULL = 9, B_O_DONE = 10, B_DRAIN = 11, NBAR = 12;
+constexpr int B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 3, B_S_FULL = 5, B_S_FREE = 7, B_P_FULL = 9, B_O_DONE = 10, B_DRAIN = 11,
+              B_P_FREE = 12, NBAR = 14;
 
 struct Params {
   bf16* o;
@@ -176,15 +177,19 @@ struct KeyTiles {
   }
 };
 
+// DOUBLE_P: two P buffers, so the softmax of tile j does not wait for PV_{j-1} (only for PV_{j-2},
+// whose buffer it reuses, and for PV_{j-1} on the rare O rescale).
+template <bool DOUBLE_P>
 __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                                                           const __grid_constant__ CUtensorMap tv, Params p) {
+  constexpr int NP = DOUBLE_P ? 2 : 1;
   extern __shared__ char smem_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   char* sQ = sm;
   char* sK = sm + TILE;          // 2 stages
   char* sV = sm + 3 * TILE;      // 2 stages
-  char* sP = sm + 5 * TILE;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 6 * TILE);
+  char* sP = sm + 5 * TILE;  // NP buffers
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + (5 + NP) * TILE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -204,6 +209,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
     }
     mbar_init(&bar[B_P_FULL], 4);
     mbar_init(&bar[B_O_DONE], 1);
+    mbar_init(&bar[B_P_FREE], 1);
+    mbar_init(&bar[B_P_FREE + 1], 1);
     mbar_init(&bar[B_DRAIN], 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -259,12 +266,13 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
         const uint32_t vb = v_base + (t & 1) * TILE;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = sdesc(p_base + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = sdesc(p_base + (DOUBLE_P ? (t & 1) * TILE : 0) + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
           const uint64_t b = sdesc(vb + kk * 2048, HALF, 1024);
           tc_mma(tmem + 256, a, b, ID_PV, (t > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(&bar[B_O_DONE]);
         tc_commit(&bar[B_KV_EMPTY + (t & 1)]);
+        if constexpr (DOUBLE_P) tc_commit(&bar[B_P_FREE + (t & 1)]);
         return true;
       };
       for (; ok && kt.valid(); kt.next(), ++j) {
@@ -321,13 +329,23 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
         s[c] = c < climit ? s[c] * p.scale_log2 : -INFINITY;
         mt = fmaxf(mt, s[c]);
       }
-      // P_j may only overwrite P_{j-1} (and O may only be rescaled) once PV_{j-1} has finished
-      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&bar[B_O_DONE], (j - 1) & 1, abort, p.err, 7))) break;
-      tc_fence_after();
+      if constexpr (DOUBLE_P) {
+        // P buffer j&1 is free once PV_{j-2} finished (which also bounds how far O_DONE can lag,
+        // so its parity below is unambiguous)
+        if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&bar[B_P_FREE + (j & 1)], ((j - 2) >> 1) & 1, abort, p.err, 7))) break;
+      } else {
+        // P_j may only overwrite P_{j-1} (and O may only be rescaled) once PV_{j-1} has finished
+        if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&bar[B_O_DONE], (j - 1) & 1, abort, p.err, 7))) break;
+        tc_fence_after();
+      }
       const float m_new = fmaxf(m_used, mt);
       const bool raise = m_new > m_used + RESCALE_THRESHOLD;
       const bool rescale = raise && j >= 1 && m_used != -INFINITY;  // O holds earlier tiles' sum: scale it down
       if (__any_sync(0xffffffffu, rescale)) {  // the whole warp touches its O rows; others scale by 1
+        if constexpr (DOUBLE_P) {  // O may only be rescaled once PV_{j-1} has finished (rare)
+          if (!__all_sync(0xffffffffu, mbar_wait(&bar[B_O_DONE], (j - 1) & 1, abort, p.err, 9))) break;
+          tc_fence_after();
+        }
         const float alpha = rescale ? exp2f(m_used - m_new) : 1.f;
         l *= alpha;
 #pragma unroll 1
@@ -354,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
           bf162 v2 = __floats2bfloat162_rn(a, bb);
           w[i] = *reinterpret_cast<uint32_t*>(&v2);
         }
-        char* dst = prow0 + (c8 >> 3) * HALF + (((c8 & 7) ^ (tid & 7)) << 4);
+        char* dst = prow0 + (DOUBLE_P ? (j & 1) * TILE : 0) + (c8 >> 3) * HALF + (((c8 & 7) ^ (tid & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l += rs;
@@ -366,7 +384,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
     // epilogue: wait for the last PV, normalise, store
     const int n = j;
     bool ok = __all_sync(0xffffffffu, !*abort);
-    if (ok && n >= 1) ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_O_DONE], (n - 1) & 1, abort, p.err, 8));
+    if (ok && n >= 1) {
+      if constexpr (DOUBLE_P)  // PV_{n-1} done (PV products complete in issue order), on its P buffer's barrier
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_P_FREE + ((n - 1) & 1)], ((n - 1) >> 1) & 1, abort, p.err, 8));
+      else
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_O_DONE], (n - 1) & 1, abort, p.err, 8));
+    }
     if (ok && n >= 1) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -435,7 +458,8 @@ static at::Tensor& err_flag(int dev) {
 }  // namespace atc
 
 // q (T,Hq,128), k/v (Tk,Hkv,128) -> o (T,Hq,128) bf16, lse2 (Hq,T) fp32 (base-2, +inf for rows without keys)
-std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles, double scale) {
+std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles, double scale,
+                                    bool double_p) {
   using namespace atc;
   AX_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(2) == D, "q bf16 (T,Hq,128)");
   AX_CHECK(k.is_contiguous() && v.is_contiguous() && k.sizes() == v.sizes() && k.size(2) == D, "k/v layout");
@@ -451,13 +475,15 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
   const CUtensorMap tv = map_rows(v.data_ptr(), Tk, (long)Hkv * D);
   Params p{(bf16*)o.data_ptr(), lse2.data_ptr<float>(), qseg.data_ptr<int>(), kr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
            (float)(scale * 1.4426950408889634), err_flag(q.get_device()).data_ptr<int>()};
-  const int smem = 6 * TILE + NBAR * 8 + 16 + 1024;
-  static bool attr = false;
-  if (!attr) {
-    AX_CUDA_OK(cudaFuncSetAttribute(attn_fwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
+  const bool dbl = double_p;
+  const int smem = (dbl ? 7 : 6) * TILE + NBAR * 8 + 16 + 1024;
+  static bool attr[2] = {false, false};
+  if (!attr[dbl]) {
+    AX_CUDA_OK(cudaFuncSetAttribute(dbl ? attn_fwd_tc_k<true> : attn_fwd_tc_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr[dbl] = true;
   }
-  attn_fwd_tc_k<<<dim3(nt, Hq), THREADS, smem, stream()>>>(tq, tk, tv, p);
+  if (dbl) attn_fwd_tc_k<true><<<dim3(nt, Hq), THREADS, smem, stream()>>>(tq, tk, tv, p);
+  else attn_fwd_tc_k<false><<<dim3(nt, Hq), THREADS, smem, stream()>>>(tq, tk, tv, p);
   AX_LAUNCH_OK();
   return {o, lse2};
 }
