@@ -114,7 +114,7 @@ class TrainEngine:
         min_count = 1
         if self.par.dp_group is not None and self.par.dp_size > 1:
             # every DP rank must run the same number of micro-batches
-            n = torch.tensor([len(split_balanced(lengths, self.max_tokens))], dtype=torch.int64)
+            n = torch.tensor([len(split_balanced(lengths, self.max_tokens))], dtype=torch.int64, device=self.device)  # NCCL: on the GPU
             dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.par.dp_group)
             min_count = int(n)
         parts = split_balanced(lengths, self.max_tokens * self.cp.size, min_count=min_count)
@@ -198,7 +198,7 @@ class TrainEngine:
         from axrl_b200.trainer.grpo_trainer import get_num_turns
 
         nt = get_num_turns(turn_index, lm) if (turn_index is not None and getattr(trainer.config, "micro_batch_denominator_type", "") == "seq_turn") else 0
-        d = torch.tensor([float(trainer.compute_micro_batch_denominator(lm, nt))], dtype=torch.float64)
+        d = torch.tensor([float(trainer.compute_micro_batch_denominator(lm, nt))], dtype=torch.float64, device=self.device)
         if self.par.dp_group is not None and self.par.dp_size > 1:
             dist.all_reduce(d, group=self.par.dp_group)
         return float(d)
