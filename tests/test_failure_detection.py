@@ -25,7 +25,8 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
     from axrl_b200.runtime.health import HeartbeatMonitor, RankFailure, bounded_collective
 
     store = dist.distributed_c10d._get_default_store()
-    hb = HeartbeatMonitor(store, rank, world, interval_s=0.1, timeout_s=1.0).start()
+    # a generous staleness limit: a loaded CI host can delay a heartbeat thread by a second or more
+    hb = HeartbeatMonitor(store, rank, world, interval_s=0.1, timeout_s=4.0).start()
     try:
         t = torch.ones(4)
         dist.all_reduce(t)  # everyone alive: one normal step
@@ -42,7 +43,7 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
             except RankFailure as e:
                 assert e.ranks == [1]
                 break
-            assert time.time() - t0 < 10, "failure not detected"
+            assert time.time() - t0 < 30, "failure not detected"
             time.sleep(0.05)
         # a collective posted anyway cannot complete: it either times out on the host or fails
         # when the transport notices the peer is gone -- both surface as an exception here
