@@ -1,6 +1,7 @@
 """sm_100a kernels vs plain PyTorch fp32 references of the same ops (small shapes)."""
 
 import math
+import os
 
 import pytest
 import torch
@@ -491,7 +492,8 @@ def test_decode_gemm_chain_with_programmatic_launch(variant):
     assert e.skinny_tma_error() == 0
 
 
-@pytest.mark.parametrize("double_p", [False, True])
+@pytest.mark.parametrize("double_p", [False, pytest.param(True, marks=pytest.mark.skipif(
+    os.environ.get("AXRL_TEST_ATTN_TC2") != "1", reason="double-buffered-P variant: opt-in until validated on a B200"))])
 @pytest.mark.parametrize("case", [0, 1, 2, 3, 4])
 def test_attention_tcgen05_forward_matches_reference(case, double_p):
     """tcgen05/TMEM/TMA forward (attention_tc.cu) against fp32 and the mma.sync kernel: causal
