@@ -22,7 +22,6 @@ master/m/v for 1/N of the parameters.
 
 from __future__ import annotations
 
-import math
 
 import torch
 import torch.distributed as dist

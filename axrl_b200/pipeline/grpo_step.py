@@ -28,7 +28,7 @@ import torch
 from axrl_b200.configs import GrpoTrainerConfig, MegatronWorkerConfig
 from axrl_b200.data.prefix_tree import merge_trajectory_samples
 from axrl_b200.data.sample import Sample, SampleBatch
-from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+from axrl_b200.models.qwen3 import Qwen3Config
 from axrl_b200.pipeline.rewards import group_advantages
 from axrl_b200.rollout.engine import GenRequest, RolloutEngine
 from axrl_b200.train.engine import TrainEngine

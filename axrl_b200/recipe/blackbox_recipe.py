@@ -22,7 +22,7 @@ from typing import Any, Callable
 
 import numpy as np
 
-from axrl_b200.data.conversation import GenerationInput, RolloutResult
+from axrl_b200.data.conversation import RolloutResult
 from axrl_b200.data.rollout_trace import RolloutTrace
 from axrl_b200.metrics.response_metric import ResponseMetric
 from axrl_b200.openai_proxy.chat_adapter import OpenAIChatAdapter

@@ -23,7 +23,7 @@ import torch
 import torch.distributed as dist
 
 from axrl_b200.ops import _ext
-from axrl_b200.sync.plan import TILE, Layout, ParamSpec, build_layout, build_tiles, split_modes
+from axrl_b200.sync.plan import TILE, ParamSpec, build_layout, build_tiles, split_modes
 
 
 class WeightSyncer:
