@@ -576,8 +576,23 @@ std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, a
   return {o, lse2};
 }
 
+void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor lse2, at::Tensor dsum, at::Tensor dq_acc,
+                       at::Tensor dk, at::Tensor dv, at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale);
+
+// Backward implementation: the mma.sync kernel below; AXRL_ATTN_BWD=tc selects the tcgen05 kernel
+// (attention_tc_bwd.cu, 128-key tiles from ``tiles_tc``).
+static int& tc_backward_flag() {
+  static int on = [] {
+    const char* e = std::getenv("AXRL_ATTN_BWD");
+    return (e && std::string(e) == "tc") ? 1 : 0;
+  }();
+  return on;
+}
+static bool use_tc_backward() { return tc_backward_flag() != 0; }
+void set_attn_bwd_tc(bool on) { tc_backward_flag() = on ? 1 : 0; }
+
 std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse2,
-                                 at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale) {
+                                 at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc) {
   using namespace attn;
   int T = q.size(0), Hq = q.size(1), Hkv = k.size(1);
   auto dq_acc = at::zeros({T, Hq, D}, q.options().dtype(at::kFloat));
@@ -590,6 +605,10 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
                                                             dsum.data_ptr<float>(), T, Hq);
   AX_LAUNCH_OK();
   int nt = tiles.size(0);
+  if (use_tc_backward() && tiles_tc.has_value()) {
+    attn_bwd_tc_tiles(dout, q, k, v, lse2, dsum, dq_acc, dk, dv, kseg, qr, *tiles_tc, scale);
+    nt = 0;
+  }
   if (nt > 0) {
     AX_CHECK(kseg.is_cuda() && qr.is_cuda() && tiles.is_cuda(), "attention tables must be on the device");
     auto& kseg_d = kseg;

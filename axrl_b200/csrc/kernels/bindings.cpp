@@ -27,8 +27,10 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
 std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                      double scale);
 int64_t attn_tc_error();
-std::vector<at::Tensor> attn_bwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
-                                 at::Tensor, double);
+std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse2,
+                                 at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc);
+int64_t attn_bwd_tc_error();
+void set_attn_bwd_tc(bool on);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
                        double, c10::optional<at::Tensor>);
 void decode_plan(at::Tensor seq_lens, at::Tensor prefix);
@@ -124,7 +126,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("double_p") = false);
   m.def("attn_fwd_mma", &ax::attn_fwd_mma);
   m.def("attn_tc_error", &ax::attn_tc_error);
-  m.def("attn_bwd", &ax::attn_bwd);
+  m.def("attn_bwd", &ax::attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse2"),
+        py::arg("kseg"), py::arg("qr"), py::arg("tiles"), py::arg("scale"), py::arg("tiles_tc") = py::none());
+  m.def("attn_bwd_tc_error", &ax::attn_bwd_tc_error);
+  m.def("set_attn_bwd_tc", &ax::set_attn_bwd_tc);
   m.def("paged_decode_attn", &ax::paged_decode_attn);
   m.def("kv_store", &ax::kv_store);
   m.def("sqnorm_accumulate", &ax::sqnorm_accumulate);

@@ -42,10 +42,11 @@ class AttnSpec:
     # backward (64-row k tiles) kernels.
     fwd_tiles: torch.Tensor | None = None
     bwd_tiles: torch.Tensor | None = None
+    bwd_tiles_tc: torch.Tensor | None = None  # 128-key tiles of the tcgen05 backward
 
     def to(self, device, non_blocking: bool = True) -> "AttnSpec":  # noqa: ANN001
         """Move every table to ``device`` in ONE host->device copy (pinned staging)."""
-        parts = [self.qseg, self.kr, self.kseg, self.qr, self.fwd_tiles, self.bwd_tiles]
+        parts = [self.qseg, self.kr, self.kseg, self.qr, self.fwd_tiles, self.bwd_tiles, self.bwd_tiles_tc]
         flat = torch.cat([p.reshape(-1) for p in parts])
         if torch.device(device).type == "cuda":
             flat = flat.pin_memory().to(device, non_blocking=non_blocking)
@@ -54,7 +55,7 @@ class AttnSpec:
             n = p.numel()
             out.append(flat[off:off + n].view(p.shape))
             off += n
-        return AttnSpec(*out[:4], self.total_q, self.total_k, self.max_q_len, self.max_k_len, out[4], out[5])
+        return AttnSpec(*out[:4], self.total_q, self.total_k, self.max_q_len, self.max_k_len, out[4], out[5], out[6])
 
     def triples(self) -> list[tuple[int, int, int, int, int]]:
         out = []
@@ -88,11 +89,12 @@ def spec_from_triples(triples: list[tuple[int, int, int, int, int]], total: int,
     mk = int((kseg[:, 1] - kseg[:, 0]).max()) if len(kseg) else 0
     return AttnSpec(torch.from_numpy(qseg), torch.from_numpy(kr), torch.from_numpy(kseg), torch.from_numpy(qr), total,
                     total if total_k is None else total_k, mq, mk, _tiles(qseg, FWD_Q_TILE, kr, True),
-                    _tiles(kseg, BWD_K_TILE, qr, False))
+                    _tiles(kseg, BWD_K_TILE, qr, False), _tiles(kseg, BWD_K_TILE_TC, qr, False))
 
 
 FWD_Q_TILE = 128
 BWD_K_TILE = 64
+BWD_K_TILE_TC = 128
 
 
 def _tiles(seg: np.ndarray, bs: int, items: np.ndarray | None = None, fwd: bool = True) -> torch.Tensor:

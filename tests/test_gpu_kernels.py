@@ -533,3 +533,37 @@ def test_attention_tcgen05_forward_matches_reference(case, double_p):
     fin = torch.isfinite(lse2)
     assert torch.equal(fin, torch.isfinite(lse)), "rows without keys differ"
     close(lse[fin], lse2[fin], 1e-3, 1e-4, msg="lse")
+
+
+@pytest.mark.skipif(os.environ.get("AXRL_TEST_ATTN_BWD_TC") != "1", reason="tcgen05 backward: opt-in until validated on a B200")
+@pytest.mark.parametrize("case", [0, 1, 2, 3])
+def test_attention_tcgen05_backward_matches_mma(case):
+    """tcgen05 backward (attention_tc_bwd.cu) against the mma.sync backward on the same inputs:
+    causal packs, a prefix tree, full ranges with a longer key buffer."""
+    from axrl_b200.ops.attention_spec import spec_from_triples
+
+    e = _ext()
+    D = 128
+    if case < 3:
+        spec, hq, hkv = _spec_cases()[case], 8, 2
+    else:
+        spec, hq, hkv = spec_from_triples([(0, 200, 0, 300, 0), (200, 457, 300, 557, 1)], 457, total_k=600), 4, 4
+    spec = spec.to(DEV)
+    T, Tk = spec.total_q, spec.total_k
+    torch.manual_seed(7 + case)
+    q = torch.randn(T, hq, D, device=DEV).bfloat16()
+    k = torch.randn(Tk, hkv, D, device=DEV).bfloat16()
+    v = torch.randn(Tk, hkv, D, device=DEV).bfloat16()
+    do = torch.randn(T, hq, D, device=DEV).bfloat16()
+    scale = 1 / math.sqrt(D)
+    o, lse = e.attn_fwd_mma(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
+    ref = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
+    e.set_attn_bwd_tc(True)
+    try:
+        got = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
+    finally:
+        e.set_attn_bwd_tc(False)
+    torch.cuda.synchronize()
+    assert e.attn_bwd_tc_error() == 0
+    for name, a, b in zip(("dq", "dk", "dv"), got, ref):
+        close(a, b, 3e-2, 2e-2, msg=name)
