@@ -1,0 +1,68 @@
+"""Expert-parallel rollout for MoE models on CPU: two gloo ranks, each holding half the experts and
+running the same requests (attention replicated, expert FFNs dispatched to their owners), produce
+the same tokens and log-probs as a single engine over the full model (reference counterpart: SGLang
+engines with ``ep_size``, ``axrl/configs.py:210-214``)."""
+
+import os
+import socket
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _reqs():
+    from axrl_b200.rollout.engine import GenRequest
+
+    g = torch.Generator().manual_seed(3)
+    return [GenRequest(rid=f"r{i}", prompt=torch.randint(1, 1024, (n,), generator=g).tolist(), max_new_tokens=10, temperature=1.0,
+                       seed_stream=i) for i, n in enumerate((7, 12, 9))]
+
+
+def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from axrl_b200.models.qwen3 import Qwen3Model, resolve_preset
+        from axrl_b200.parallel.expert import EPContext, load_ep_shards_from_full
+        from axrl_b200.rollout.engine import RolloutEngine
+
+        cfg = resolve_preset("tiny-moe")
+        full = Qwen3Model(cfg)
+        full.init_weights(2)
+        ref = RolloutEngine(full, max_batch=4, kv_tokens=2048, max_context=128, use_cuda_graph=False, seed=4).generate(_reqs())
+        ep = EPContext.from_group(dist.group.WORLD)
+        model = Qwen3Model(cfg, ep=ep)
+        load_ep_shards_from_full(model, {k: v.detach() for k, v in full.named_parameters()}, ep)
+        assert model.layers[0].mlp.experts_gate_up.shape[0] == cfg.num_experts // world
+        got = RolloutEngine(model, max_batch=4, kv_tokens=2048, max_context=128, use_cuda_graph=False, seed=4).generate(_reqs())
+        for a, b in zip(got, ref):
+            assert a.output_ids == b.output_ids, (a.output_ids, b.output_ids)
+            torch.testing.assert_close(torch.tensor(a.output_logprobs), torch.tensor(b.output_logprobs), atol=1e-4, rtol=1e-4)
+        q.put((rank, "ok"))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep2_rollout_matches_single_engine():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for r, msg in res:
+        assert msg == "ok", f"rank {r}:\n{msg}"
