@@ -65,11 +65,12 @@ class GenRequest:
     allowed_token_ids: Sequence[int] | None = None  # constrained decoding: only these tokens may be drawn
     regex: str | None = None  # constrained decoding: the response must match this expression
     json_schema: Any = None  # ... or be JSON text of this schema (rollout/grammar.py subset)
+    structural_tag: dict | None = None  # ... or free text whose tagged segments follow schemas
     gen_prefix: tuple[int, ...] = ()  # tokens generated before this request resumed (preemption)
 
     @property
     def constrained(self) -> bool:
-        return self.regex is not None or self.json_schema is not None
+        return self.regex is not None or self.json_schema is not None or self.structural_tag is not None
 
     @property
     def filtered(self) -> bool:
@@ -653,10 +654,10 @@ class RolloutEngine:
 
     def _grammar(self, r: GenRequest):  # noqa: ANN202
         """Token-level automaton of a constrained request (cached per expression / schema)."""
-        from axrl_b200.rollout.grammar import make_token_grammar
+        from axrl_b200.rollout.grammar import StructuralTagGrammar, make_token_grammar
 
-        key = (r.regex, json.dumps(r.json_schema, sort_keys=True) if r.json_schema is not None and not isinstance(r.json_schema, str)
-               else r.json_schema, tuple(r.stop_token_ids))
+        enc = lambda x: json.dumps(x, sort_keys=True) if x is not None and not isinstance(x, str) else x  # noqa: E731
+        key = (r.regex, enc(r.json_schema), enc(r.structural_tag), tuple(r.stop_token_ids))
         g = self._grammars.get(key)
         if g is None:
             if self._token_strings is None:
@@ -665,8 +666,12 @@ class RolloutEngine:
                 n = min(self.cfg.vocab_size, len(self.tokenizer)) if hasattr(self.tokenizer, "__len__") else self.cfg.vocab_size
                 self._token_strings = [self.tokenizer.decode([i]) for i in range(n)]
             eos = [self.eos] if self.eos is not None else []
-            g = make_token_grammar(regex=r.regex, json_schema=r.json_schema, token_strings=self._token_strings,
-                                   eos_ids=eos + [t for t in r.stop_token_ids if t not in eos])
+            eos_ids = eos + [t for t in r.stop_token_ids if t not in eos]
+            if r.structural_tag is not None:
+                tag = json.loads(r.structural_tag) if isinstance(r.structural_tag, str) else r.structural_tag
+                g = StructuralTagGrammar(tag["structures"], tag["triggers"], self._token_strings, eos_ids)
+            else:
+                g = make_token_grammar(regex=r.regex, json_schema=r.json_schema, token_strings=self._token_strings, eos_ids=eos_ids)
             self._grammars[key] = g
         return g
 

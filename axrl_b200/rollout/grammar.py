@@ -425,3 +425,105 @@ def tool_call_schema(tools: Sequence[dict] | None, tool_choice: Any) -> dict | N
                                                "parameters": f.get("parameters") or {"type": "object", "properties": {}}},
               "required": ["name", "parameters"]} for f in fns]
     return {"type": "array", "minItems": 1, "items": items[0] if len(items) == 1 else {"anyOf": items}}
+
+
+class StructuralTagGrammar:
+    """Free text in which every tagged segment is constrained (the reference's ``structural_tag``
+    constraint for ``tool_choice="auto"``, ``axrl/worker/sglang_worker.py:211-238``): once the text
+    ends with a trigger (e.g. ``<tool_call>``), the continuation must be one of the structures whose
+    ``begin`` starts with that trigger, i.e. ``begin`` + JSON of ``schema`` + ``end``; after ``end``
+    the text is free again.
+
+    States are ints: -1 - k encodes free text whose last ``k`` characters may still start a trigger
+    (a bounded suffix is kept in ``self.tails``); >= 0 are states of the tagged-segment automaton.
+    If a token completes a trigger and continues with text the structure does not allow, the
+    segment is left unconstrained (free) rather than rejected."""
+
+    def __init__(self, structures: Sequence[dict], triggers: Sequence[str], token_strings: Sequence[str], eos_ids: Sequence[int]) -> None:
+        self.triggers = list(triggers)
+        self.strings = list(token_strings)
+        self.V = len(token_strings)
+        self.eos = [int(e) for e in eos_ids if 0 <= int(e) < self.V]
+        alts: dict[str, list[str]] = {}
+        for s in structures:
+            trig = next((t for t in self.triggers if s["begin"].startswith(t)), None)
+            if trig is None:
+                raise ValueError(f"structure begin {s['begin']!r} does not start with a trigger")
+            alts.setdefault(trig, []).append(_lit(s["begin"][len(trig):]) + schema_to_regex(s.get("schema", True)) + _lit(s["end"]))
+        self.segment = {t: TokenGrammar(compile_regex("(" + "|".join(a) + ")"), token_strings, eos_ids) for t, a in alts.items()}
+        self.keep = max(len(t) for t in self.triggers)
+        self.tails: list[str] = [""]  # state -1 - i -> free text tail
+        self._tail_id = {"": 0}
+        self._seg_ids: dict[tuple[str, int], int] = {}
+        self._seg_rev: list[tuple[str, int]] = []
+        self.masks: dict[int, np.ndarray] = {}
+
+    @property
+    def start(self) -> int:
+        return -1
+
+    def _free(self, tail: str) -> int:
+        tail = tail[-self.keep:]
+        i = self._tail_id.get(tail)
+        if i is None:
+            i = len(self.tails)
+            self.tails.append(tail)
+            self._tail_id[tail] = i
+        return -1 - i
+
+    def _seg(self, trig: str, inner: int) -> int:
+        key = (trig, inner)
+        i = self._seg_ids.get(key)
+        if i is None:
+            i = len(self._seg_rev)
+            self._seg_rev.append(key)
+            self._seg_ids[key] = i
+        return i
+
+    def allowed(self, state: int) -> np.ndarray:
+        m = self.masks.get(state)
+        if m is None:
+            if state < 0:  # free text: anything
+                m = np.ones(self.V, dtype=bool)
+            else:
+                trig, inner = self._seg_rev[state]
+                g = self.segment[trig]
+                m = g.allowed(inner).copy()
+                if g.dfa.accepting(inner):  # segment complete: free text continues
+                    m[:] = True
+            self.masks[state] = m
+        return m
+
+    def advance(self, state: int, token: int) -> int:
+        if token in self.eos or not (0 <= token < self.V):
+            return state
+        text = self.strings[token]
+        if state >= 0:
+            trig, inner = self._seg_rev[state]
+            g = self.segment[trig]
+            if g.dfa.accepting(inner):
+                return self.advance(self._free(""), token)
+            nxt = g.dfa.walk(inner, text)
+            return self._seg(trig, nxt) if nxt >= 0 else self._free(text)
+        buf = self.tails[-1 - state] + text
+        for trig in self.triggers:
+            j = buf.find(trig)
+            if j >= 0 and trig in self.segment:
+                g = self.segment[trig]
+                inner = g.dfa.walk(g.dfa.start, buf[j + len(trig):])
+                return self._seg(trig, inner) if inner >= 0 else self._free(buf[j + len(trig):])
+        return self._free(buf)
+
+
+def tool_call_structural_tag(tools: Sequence[dict] | None, tool_call_parser: str | None) -> dict | None:
+    """Structural tag for ``tool_choice="auto"`` with the Qwen tool-call format (``<tool_call>`` JSON
+    ``</tool_call>``, parsers "qwen" / "qwen25" / "qwen3"): one structure per tool whose arguments
+    follow the tool's parameter schema."""
+    if not tools or tool_call_parser not in ("qwen", "qwen25", "qwen3", "hermes"):
+        return None
+    structures = []
+    for t in tools:
+        f = t.get("function", t)
+        structures.append({"begin": '<tool_call>\n{"name": ' + json.dumps(f["name"]) + ', "arguments": ',
+                           "schema": f.get("parameters") or {"type": "object", "properties": {}}, "end": "}\n</tool_call>"})
+    return {"type": "structural_tag", "structures": structures, "triggers": ["<tool_call>"]}

@@ -103,16 +103,18 @@ class RolloutWorker:
         t0 = time.time()
         inp.event_timing.stamp("worker_received")
         routing = []
-        from axrl_b200.rollout.grammar import tool_call_schema
+        from axrl_b200.rollout.grammar import tool_call_schema, tool_call_structural_tag
 
         schema = tool_call_schema(getattr(inp, "tools", None), getattr(inp, "tool_choice", None))
+        tag = (tool_call_structural_tag(inp.tools, inp.tool_call_parser)
+               if schema is None and inp.tools and inp.tool_choice in (None, "auto") else None)
         while True:
             await asyncio.get_running_loop().run_in_executor(None, self._ready.wait)
             rid = f"{inp.session_id}#{next(self._ids)}"
             req = GenRequest(rid=rid, prompt=ids + out_ids, max_new_tokens=budget - len(out_ids), temperature=sc.temperature,
                              stop_token_ids=stop, capture_routing=inp.capture_routing, top_k=sc.top_k, top_p=sc.top_p, min_p=sc.min_p,
                              presence_penalty=sc.presence_penalty, frequency_penalty=sc.frequency_penalty,
-                             repetition_penalty=sc.repetition_penalty, json_schema=schema, gen_prefix=tuple(out_ids))
+                             repetition_penalty=sc.repetition_penalty, json_schema=schema, structural_tag=tag, gen_prefix=tuple(out_ids))
             res = await self._submit(req)
             out_ids += res.output_ids
             out_lps += res.output_logprobs

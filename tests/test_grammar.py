@@ -95,3 +95,27 @@ def test_engine_generates_only_schema_conforming_json():
             assert d.walk(d.start, text) >= 0, text
     assert sum(res[f"r{i}"].finish_reason == "stop" for i in range(3)) >= 2  # complete JSON documents
     assert len(res["plain"].output_ids) == 10
+
+
+def test_structural_tag_constrains_only_tagged_segments():
+    from axrl_b200.rollout.grammar import StructuralTagGrammar, tool_call_structural_tag
+
+    tools = [{"type": "function", "function": {"name": "get_weather", "parameters": {
+        "type": "object", "properties": {"city": {"type": "string"}}, "required": ["city"]}}}]
+    tag = tool_call_structural_tag(tools, "qwen3")
+    assert tag["triggers"] == ["<tool_call>"] and tool_call_structural_tag(tools, None) is None
+    vocab = [chr(i) for i in range(32, 127)] + ["<tool_call>", "\n", "<eos>"]
+    eos = len(vocab) - 1
+    g = StructuralTagGrammar(tag["structures"], tag["triggers"], vocab, [eos])
+    s = g.start
+    for ch in "Sure.":
+        assert g.allowed(s).all()
+        s = g.advance(s, vocab.index(ch))
+    s = g.advance(s, vocab.index("<tool_call>"))
+    assert [vocab[i] for i in range(len(vocab)) if g.allowed(s)[i]] == ["\n"]
+    body = '\n{"name": "get_weather", "arguments": {"city": "Oslo"}}\n</tool_call>'
+    for ch in body:
+        tok = vocab.index(ch) if ch != "\n" else vocab.index("\n")
+        assert g.allowed(s)[tok], (ch, s)
+        s = g.advance(s, tok)
+    assert g.allowed(s).all()  # free text again after the end tag
