@@ -298,6 +298,12 @@ class TrainEngine:
             from axrl_b200.ops import _ext
 
             _ext.check_kernel_waits()
+        from axrl_b200.utils import consistency
+
+        if consistency.enabled() and self.par.dp_group is not None and self.par.dp_size > 1:
+            # data-parallel replicas must hold bit-identical parameters after the update
+            consistency.check_replicated(((n, p) for n, p in self.model.named_parameters() if not getattr(p, "expert_parallel", False)),
+                                         self.par.dp_group)
         return out
 
     def _forward_backward_pp(self, batch: SampleBatch, mbs: list[PackedMicroBatch], trainer, temperature: float,  # noqa: ANN001
