@@ -294,6 +294,7 @@ struct BwdParams {
   const int* tiles;  // (Ntiles, 2): kseg index, k tile start
   int Hq, Hkv, T;
   float scale_log2, scale;
+  int skip_dq;  // dQ computed by attn_bwd_dq_k instead (deterministic mode)
 };
 
 __global__ void __launch_bounds__(128, 2) attn_bwd_k(BwdParams p) {
@@ -455,7 +456,7 @@ __global__ void __launch_bounds__(128, 2) attn_bwd_k(BwdParams p) {
         }
         __syncthreads();
         // dQ[q, d] += sum_key dS[q, key] K[key, d]: warp w takes q rows [16w, 16w+16)
-        {
+        if (!p.skip_dq) {
           float dqa[16][4];
 #pragma unroll
           for (int i = 0; i < 16; ++i) dqa[i][0] = dqa[i][1] = dqa[i][2] = dqa[i][3] = 0.f;
@@ -576,6 +577,179 @@ std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, a
   return {o, lse2};
 }
 
+namespace attn {
+// Deterministic dQ: one CTA per (128-row q tile, q head) walks every key tile of its q segment
+// (the forward's iteration) and accumulates dQ = sum_j dS_j K_j in registers, so no two CTAs add
+// into the same dQ row.  Per 64-key tile: S = Q K^T and dP = dO V^T (mma.sync), P = exp2(S *
+// scale*log2e - lse2) (the forward's log-sum-exp; no running maximum needed), dS = P (dP - Dsum) *
+// scale, dQ += dS K.  Writes bf16 dQ directly.
+struct DqParams {
+  const bf16 *q, *k, *v, *dout;
+  const float *lse2, *dsum;
+  bf16* dq;
+  const int* qseg;
+  const int* kr;
+  const int* tiles;
+  int Hq, Hkv, T;
+  float scale_log2, scale;
+};
+
+__global__ void __launch_bounds__(256, 1) attn_bwd_dq_k(DqParams p) {
+  extern __shared__ __align__(128) char smem[];
+  char* sQ = smem;
+  char* sdO = sQ + FWD_BM * D * 2;
+  char* sK = sdO + FWD_BM * D * 2;
+  char* sV = sK + 2 * FWD_BN * D * 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seg = p.tiles[blockIdx.x * 2], qs = p.tiles[blockIdx.x * 2 + 1];
+  const int h = blockIdx.y, hk = h / (p.Hq / p.Hkv);
+  const int q0 = p.qseg[seg * 4], q1 = p.qseg[seg * 4 + 1], r_first = p.qseg[seg * 4 + 2], r_last = p.qseg[seg * 4 + 3];
+  const int qe = min(qs + FWD_BM, q1);
+  const long qstride = (long)p.Hq * D, kstride = (long)p.Hkv * D;
+
+  load_tile(sQ, p.q + (long)qs * qstride + (long)h * D, qstride, FWD_BM, qe - qs, tid, 256);
+  load_tile(sdO, p.dout + (long)qs * qstride + (long)h * D, qstride, FWD_BM, qe - qs, tid, 256);
+  cp_commit();
+
+  auto range_end = [&](int r) {
+    int k0 = p.kr[r * 3], k1 = p.kr[r * 3 + 1], ty = p.kr[r * 3 + 2];
+    return ty == 1 ? min(k1, k0 + (qe - q0)) : k1;
+  };
+  int lr = r_first, lks = lr < r_last ? p.kr[lr * 3] : 0;
+  auto advance = [&](int& r, int& ks) {
+    ks += FWD_BN;
+    while (r < r_last && ks >= range_end(r)) {
+      ++r;
+      if (r < r_last) ks = p.kr[r * 3];
+    }
+  };
+  while (lr < r_last && lks >= range_end(lr)) {
+    ++lr;
+    if (lr < r_last) lks = p.kr[lr * 3];
+  }
+  int stage = 0;
+  if (lr < r_last) {
+    int kend = range_end(lr);
+    load_tile(sK, p.k + (long)lks * kstride + (long)hk * D, kstride, FWD_BN, kend - lks, tid, 256);
+    load_tile(sV, p.v + (long)lks * kstride + (long)hk * D, kstride, FWD_BN, kend - lks, tid, 256);
+  }
+  cp_commit();
+  cp_wait<1>();
+  __syncthreads();
+  uint32_t qf[8][4], of[8][4];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    int row = warp * 16 + (lane & 15), col = kk * 16 + (lane >> 4) * 8;
+    ldsm_x4(smem_u32(sQ + swz(row, col)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+    ldsm_x4(smem_u32(sdO + swz(row, col)), of[kk][0], of[kk][1], of[kk][2], of[kk][3]);
+  }
+  const int row_a = qs + warp * 16 + (lane >> 2);  // rows of c0/c1; c2/c3 are +8
+  float lse[2], dsm[2];
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int qi = row_a + hh * 8;
+    lse[hh] = qi < qe ? p.lse2[(long)h * p.T + qi] : INFINITY;
+    dsm[hh] = qi < qe ? p.dsum[(long)h * p.T + qi] : 0.f;
+  }
+  float acc[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+  int cr = lr, cks = lks;
+  while (cr < r_last) {
+    int nr = cr, nks = cks;
+    advance(nr, nks);
+    if (nr < r_last) {
+      int kend = range_end(nr);
+      load_tile(sK + (stage ^ 1) * FWD_BN * D * 2, p.k + (long)nks * kstride + (long)hk * D, kstride, FWD_BN, kend - nks, tid, 256);
+      load_tile(sV + (stage ^ 1) * FWD_BN * D * 2, p.v + (long)nks * kstride + (long)hk * D, kstride, FWD_BN, kend - nks, tid, 256);
+    }
+    cp_commit();
+    cp_wait<1>();
+    __syncthreads();
+    const char* cK = sK + stage * FWD_BN * D * 2;
+    const char* cV = sV + stage * FWD_BN * D * 2;
+    const int k0 = p.kr[cr * 3], k1 = p.kr[cr * 3 + 1], ty = p.kr[cr * 3 + 2];
+    float sc[8][4], dp[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[n][e] = dp[n][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+      for (int n2 = 0; n2 < 4; ++n2) {
+        uint32_t b0, b1, b2, b3, c0, c1, c2, c3;
+        int key = n2 * 16 + (lane & 7) + (lane >> 4) * 8, col = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(smem_u32(cK + swz(key, col)), b0, b1, b2, b3);
+        ldsm_x4(smem_u32(cV + swz(key, col)), c0, c1, c2, c3);
+        mma16816(sc[2 * n2], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+        mma16816(sc[2 * n2 + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
+        mma16816(dp[2 * n2], of[kk][0], of[kk][1], of[kk][2], of[kk][3], c0, c1);
+        mma16816(dp[2 * n2 + 1], of[kk][0], of[kk][1], of[kk][2], of[kk][3], c2, c3);
+      }
+    }
+    // dS = P (dP - Dsum) * scale, masked like the forward
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int hh = e >> 1;
+        const int qi = row_a + hh * 8;
+        const int kj = cks + n * 8 + (lane & 3) * 2 + (e & 1);
+        const bool ok = kj < k1 && qi < qe && (ty == 0 || (kj - k0) <= (qi - q0));
+        const float pr = ok ? exp2f(sc[n][e] * p.scale_log2 - lse[hh]) : 0.f;
+        sc[n][e] = pr * (dp[n][e] - dsm[hh]) * p.scale;
+      }
+    }
+    // dQ += dS K   (A = dS from registers, B = K [key][d] via ldmatrix.trans)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t a0 = pack_bf16(sc[2 * kk][0], sc[2 * kk][1]);
+      uint32_t a1 = pack_bf16(sc[2 * kk][2], sc[2 * kk][3]);
+      uint32_t a2 = pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+      uint32_t a3 = pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+      for (int d2 = 0; d2 < 8; ++d2) {
+        uint32_t b0, b1, b2, b3;
+        int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, col = d2 * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(smem_u32(cK + swz(key, col)), b0, b1, b2, b3);
+        mma16816(acc[2 * d2], a0, a1, a2, a3, b0, b1);
+        mma16816(acc[2 * d2 + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncthreads();
+    stage ^= 1;
+    cr = nr;
+    cks = nks;
+  }
+  cp_wait<0>();
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int qi = row_a + hh * 8;
+    if (qi < qe) {
+      bf16* orow = p.dq + (long)qi * qstride + (long)h * D;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        int col = d * 8 + (lane & 3) * 2;
+        *reinterpret_cast<bf162*>(orow + col) = __floats2bfloat162_rn(acc[d][2 * hh], acc[d][2 * hh + 1]);
+      }
+    }
+  }
+}
+}  // namespace attn
+
+// Deterministic mode (AXRL_DETERMINISTIC_ATTN=1 or set_attn_deterministic): dK / dV from the
+// key-tile kernel without its dQ atomics, dQ from attn_bwd_dq_k.
+static int& deterministic_flag() {
+  static int on = [] {
+    const char* e = std::getenv("AXRL_DETERMINISTIC_ATTN");
+    return (e && e[0] == '1') ? 1 : 0;
+  }();
+  return on;
+}
+void set_attn_deterministic(bool on) { deterministic_flag() = on ? 1 : 0; }
+
 void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor lse2, at::Tensor dsum, at::Tensor dq_acc,
                        at::Tensor dk, at::Tensor dv, at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale);
 
@@ -592,7 +766,8 @@ static bool use_tc_backward() { return tc_backward_flag() != 0; }
 void set_attn_bwd_tc(bool on) { tc_backward_flag() = on ? 1 : 0; }
 
 std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse2,
-                                 at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc) {
+                                 at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc,
+                                 c10::optional<at::Tensor> qseg, c10::optional<at::Tensor> kr, c10::optional<at::Tensor> fwd_tiles) {
   using namespace attn;
   int T = q.size(0), Hq = q.size(1), Hkv = k.size(1);
   auto dq_acc = at::zeros({T, Hq, D}, q.options().dtype(at::kFloat));
@@ -605,7 +780,8 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
                                                             dsum.data_ptr<float>(), T, Hq);
   AX_LAUNCH_OK();
   int nt = tiles.size(0);
-  if (use_tc_backward() && tiles_tc.has_value()) {
+  const bool det = deterministic_flag() != 0 && fwd_tiles.has_value() && qseg.has_value() && kr.has_value();
+  if (use_tc_backward() && tiles_tc.has_value() && !det) {
     attn_bwd_tc_tiles(dout, q, k, v, lse2, dsum, dq_acc, dk, dv, kseg, qr, *tiles_tc, scale);
     nt = 0;
   }
@@ -616,7 +792,7 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
     BwdParams p{(const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), (const bf16*)dout.data_ptr(),
                 lse2.data_ptr<float>(), dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), (bf16*)dk.data_ptr(),
                 (bf16*)dv.data_ptr(), kseg_d.data_ptr<int>(), qr_d.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
-                (float)(scale * 1.4426950408889634), (float)scale};
+                (float)(scale * 1.4426950408889634), (float)scale, det ? 1 : 0};
     int smem = (2 * BWD_BN + 2 * BWD_BM) * D * 2 + BWD_BN * (BWD_BM + 8) * 2 + 2 * BWD_BM * 4;
     static bool attr = false;
     if (!attr) {
@@ -625,6 +801,24 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
     }
     attn_bwd_k<<<dim3(nt, Hkv), 128, smem, stream()>>>(p);
     AX_LAUNCH_OK();
+  }
+  if (det) {  // dQ owned by one CTA per q tile: no atomics, fixed summation order
+    DqParams dp{(const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), (const bf16*)dout.data_ptr(),
+                lse2.data_ptr<float>(), dsum.data_ptr<float>(), (bf16*)dq.data_ptr(), qseg->data_ptr<int>(), kr->data_ptr<int>(),
+                fwd_tiles->data_ptr<int>(), Hq, Hkv, T, (float)(scale * 1.4426950408889634), (float)scale};
+    const int ntq = fwd_tiles->size(0);
+    dq.zero_();
+    if (ntq > 0) {
+      const int smem = (2 * FWD_BM + 4 * FWD_BN) * D * 2;
+      static bool attr_dq = false;
+      if (!attr_dq) {
+        AX_CUDA_OK(cudaFuncSetAttribute(attn_bwd_dq_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr_dq = true;
+      }
+      attn_bwd_dq_k<<<dim3(ntq, Hq), 256, smem, stream()>>>(dp);
+      AX_LAUNCH_OK();
+    }
+    return {dq, dk, dv};
   }
   long n = (long)T * Hq * D;
   f32_to_bf16_k<<<std::min<long>((n / 4 + 255) / 256, num_sms() * 8), 256, 0, stream()>>>(dq_acc.data_ptr<float>(),

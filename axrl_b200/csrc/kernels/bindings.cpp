@@ -28,7 +28,9 @@ std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, a
                                      double scale);
 int64_t attn_tc_error();
 std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse2,
-                                 at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc);
+                                 at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc,
+                                 c10::optional<at::Tensor> qseg, c10::optional<at::Tensor> kr, c10::optional<at::Tensor> fwd_tiles);
+void set_attn_deterministic(bool on);
 int64_t attn_bwd_tc_error();
 void set_attn_bwd_tc(bool on);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
@@ -127,7 +129,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_mma", &ax::attn_fwd_mma);
   m.def("attn_tc_error", &ax::attn_tc_error);
   m.def("attn_bwd", &ax::attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse2"),
-        py::arg("kseg"), py::arg("qr"), py::arg("tiles"), py::arg("scale"), py::arg("tiles_tc") = py::none());
+        py::arg("kseg"), py::arg("qr"), py::arg("tiles"), py::arg("scale"), py::arg("tiles_tc") = py::none(), py::arg("qseg") = py::none(),
+        py::arg("kr") = py::none(), py::arg("fwd_tiles") = py::none());
+  m.def("set_attn_deterministic", &ax::set_attn_deterministic);
   m.def("attn_bwd_tc_error", &ax::attn_bwd_tc_error);
   m.def("set_attn_bwd_tc", &ax::set_attn_bwd_tc);
   m.def("paged_decode_attn", &ax::paged_decode_attn);

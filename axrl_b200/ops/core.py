@@ -193,7 +193,8 @@ class _Attn(torch.autograd.Function):
     def backward(ctx, do):  # noqa: ANN001, ANN205
         q, k, v, o, lse = ctx.saved_tensors
         s = ctx.spec
-        dq, dk, dv = _ext.ext().attn_bwd(do.contiguous(), q, k, v, o, lse, s.kseg, s.qr, s.bwd_tiles, ctx.scale, s.bwd_tiles_tc)
+        dq, dk, dv = _ext.ext().attn_bwd(do.contiguous(), q, k, v, o, lse, s.kseg, s.qr, s.bwd_tiles, ctx.scale, s.bwd_tiles_tc,
+                                         s.qseg, s.kr, s.fwd_tiles)
         return dq, dk, dv, None, None, None
 
 

@@ -567,3 +567,32 @@ def test_attention_tcgen05_backward_matches_mma(case):
     assert e.attn_bwd_tc_error() == 0
     for name, a, b in zip(("dq", "dk", "dv"), got, ref):
         close(a, b, 3e-2, 2e-2, msg=name)
+
+
+@pytest.mark.skipif(os.environ.get("AXRL_TEST_ATTN_DET") != "1", reason="deterministic dQ kernel: opt-in until validated on a B200")
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_attention_deterministic_dq(case):
+    """Deterministic mode: dQ from one CTA per q tile (no atomics) equals the atomic path and is
+    bitwise reproducible."""
+    e = _ext()
+    D = 128
+    spec = _spec_cases()[case].to(DEV)
+    T = spec.total_q
+    torch.manual_seed(11 + case)
+    q = torch.randn(T, 8, D, device=DEV).bfloat16()
+    k = torch.randn(T, 2, D, device=DEV).bfloat16()
+    v = torch.randn(T, 2, D, device=DEV).bfloat16()
+    do = torch.randn(T, 8, D, device=DEV).bfloat16()
+    scale = 1 / math.sqrt(D)
+    o, lse = e.attn_fwd_mma(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
+    args = (do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc, spec.qseg, spec.kr, spec.fwd_tiles)
+    ref = e.attn_bwd(*args)
+    e.set_attn_deterministic(True)
+    try:
+        a, b = e.attn_bwd(*args), e.attn_bwd(*args)
+    finally:
+        e.set_attn_deterministic(False)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y), "deterministic backward is not reproducible"
+    for name, x, y in zip(("dq", "dk", "dv"), a, ref):
+        close(x, y, 2e-2, 1e-2, msg=name)
