@@ -31,6 +31,7 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
                                  at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc,
                                  c10::optional<at::Tensor> qseg, c10::optional<at::Tensor> kr, c10::optional<at::Tensor> fwd_tiles);
 void set_attn_deterministic(bool on);
+at::Tensor gdn_step(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, at::Tensor pool, at::Tensor slots);
 int64_t attn_bwd_tc_error();
 void set_attn_bwd_tc(bool on);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
@@ -132,6 +133,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("kseg"), py::arg("qr"), py::arg("tiles"), py::arg("scale"), py::arg("tiles_tc") = py::none(), py::arg("qseg") = py::none(),
         py::arg("kr") = py::none(), py::arg("fwd_tiles") = py::none());
   m.def("set_attn_deterministic", &ax::set_attn_deterministic);
+  m.def("gdn_step", &ax::gdn_step);
   m.def("attn_bwd_tc_error", &ax::attn_bwd_tc_error);
   m.def("set_attn_bwd_tc", &ax::set_attn_bwd_tc);
   m.def("paged_decode_attn", &ax::paged_decode_attn);

@@ -201,3 +201,18 @@ class GatedDeltaNet(nn.Module):
         o, S_new = gated_delta_step(q, k, v, g, beta, S)
         S.copy_(S_new)
         return self._out(o, z, x.dtype)
+
+    def step_pool(self, x: torch.Tensor, conv_pool: torch.Tensor, S_pool: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:
+        """:meth:`step` on states kept in pools (rows ``slots``), the recurrent update done in place
+        by the ``gdn_step`` kernel (csrc/kernels/gdn.cu) without gathering the states."""
+        from axrl_b200.ops import _ext
+
+        mixed, z, b, a = self._project(x)
+        conv_state = conv_pool.index_select(0, slots)
+        window = torch.cat([conv_state, mixed.float()[:, None]], 1)
+        conv = F.silu((window * self.conv_weight.float().t()[None]).sum(1))
+        conv_pool.index_copy_(0, slots, window[:, 1:])
+        q, k, v, g, beta = self._heads(conv, b, a)
+        o = _ext.ext().gdn_step(q.contiguous(), k.contiguous(), v.contiguous(), g.contiguous(), beta.contiguous(), S_pool, slots)
+        return self._out(o, z, x.dtype)
+

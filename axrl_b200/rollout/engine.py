@@ -26,6 +26,7 @@ from __future__ import annotations
 import dataclasses
 import json
 import math
+import os
 import time
 import zlib
 from dataclasses import dataclass, field
@@ -213,6 +214,8 @@ class RolloutEngine:
         # per running sequence; slot B is scratch for padded rows
         self.gdn_index = {li: i for i, li in enumerate(li for li in range(self.cfg.num_hidden_layers) if self.cfg.layer_is_linear(li))}
         self.gdn_free = list(range(B - 1, -1, -1))
+        # the fused state-update kernel is opt-in until it has been validated on a B200
+        self.gdn_kernel = self.is_cuda and os.environ.get("AXRL_GDN_KERNEL", "0") == "1"
         if self.gdn_index:
             a = self.model.layers[next(iter(self.gdn_index))].self_attn
             n = len(self.gdn_index)
@@ -799,6 +802,8 @@ class RolloutEngine:
 
         def gdn_decode(li: int, a, x: torch.Tensor) -> torch.Tensor:  # noqa: ANN001
             gi = self.gdn_index[li]
+            if self.gdn_kernel:  # recurrent update in place in the pool (csrc/kernels/gdn.cu)
+                return a.step_pool(x, self.gdn_conv[gi], self.gdn_S[gi], lsl)
             conv, S = self.gdn_conv[gi].index_select(0, lsl), self.gdn_S[gi].index_select(0, lsl)
             out = a.step(x, conv, S)
             self.gdn_conv[gi].index_copy_(0, lsl, conv)

@@ -596,3 +596,22 @@ def test_attention_deterministic_dq(case):
         assert torch.equal(x, y), "deterministic backward is not reproducible"
     for name, x, y in zip(("dq", "dk", "dv"), a, ref):
         close(x, y, 2e-2, 1e-2, msg=name)
+
+
+@pytest.mark.skipif(os.environ.get("AXRL_TEST_GDN_KERNEL") != "1", reason="GDN state-update kernel: opt-in until validated on a B200")
+def test_gdn_step_kernel_matches_reference():
+    from axrl_b200.models.gdn import gated_delta_step
+
+    e = _ext()
+    torch.manual_seed(0)
+    B, H, dk, dv, slots_n = 5, 4, 128, 128, 9
+    q = torch.nn.functional.normalize(torch.randn(B, H, dk, device=DEV), dim=-1) / dk ** 0.5
+    k = torch.nn.functional.normalize(torch.randn(B, H, dk, device=DEV), dim=-1)
+    v, g, beta = torch.randn(B, H, dv, device=DEV), -torch.rand(B, H, device=DEV), torch.rand(B, H, device=DEV)
+    pool = torch.randn(slots_n, H, dk, dv, device=DEV) * 0.1
+    slots = torch.tensor([3, 0, 7, 1, 8], device=DEV)
+    S = pool[slots].clone()
+    o_ref, S_ref = gated_delta_step(q, k, v, g, beta, S)
+    o = e.gdn_step(q, k, v, g, beta, pool, slots)
+    close(o, o_ref, 1e-4, 1e-4, msg="o")
+    close(pool[slots], S_ref, 1e-4, 1e-4, msg="state")
