@@ -2,7 +2,8 @@
 
 Sequences of ``--lens`` tokens are packed into one buffer (Qwen3-8B heads: 32 q / 8 kv, head dim
 128, bf16) and attended causally per sequence through the range-list kernels
-(``csrc/kernels/attention.cu``).  Reports CUDA-event device time and TFLOP/s (causal FLOPs:
+(``csrc/kernels/attention.cu``).  Reference counterpart: the packed-attention cost inside ``benchmark/magi_forward`` (Magi
+``calc_attn``, ``axrl/utils/megatron/magi_forward.py:439-466``).  Reports CUDA-event device time and TFLOP/s (causal FLOPs:
 4 * D * Hq * sum(L * (L + 1) / 2) forward, 2.5x that backward).
 
 python -m axrl_b200.benchmarks.attention_bench [--lens 8192,2048,2048,1024,1024,512,512] [--iters 5]

@@ -11,6 +11,9 @@ Run under torchrun, one rank per GPU (N = 2..8):
   768) with EP=N: routing, dispatch, grouped expert FFN, combine; NVLink device-side
   dispatch/combine (``parallel/ep_p2p.py``) vs NCCL all-to-all (``parallel/expert.py``).
 
+Reference counterparts: Megatron's TP + sequence-parallel linears and the ``alltoall`` MoE token
+dispatcher (``axrl/worker/megatron_worker.py:833``), both on NCCL.
+
 Roofline of a fused path: the slower of its FLOPs at the measured bf16 GEMM peak and the bytes
 each GPU must receive over NVLink at the measured 770 GB/s per direction.  Every time is CUDA-event
 device time, max over ranks, median of ``--iters`` after ``--warmup`` iterations.

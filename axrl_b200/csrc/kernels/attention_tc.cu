@@ -1,4 +1,6 @@
 // Range-list flash attention forward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// Reference counterpart: MagiAttention's calc_attn called from the packed forward
+// (axrl/utils/megatron/magi_forward.py:439-466).
 //
 // Same problem and outputs as attn_fwd_k in attention.cu (packed tokens, (q-range, k-range, type)
 // triples, head_dim 128, GQA; O bf16 and the base-2 log-sum-exp of the scaled scores), computed

@@ -1,4 +1,6 @@
 // Range-list flash attention backward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// Reference counterpart: the backward of MagiAttention's calc_attn
+// (axrl/utils/megatron/magi_forward.py:439-466).
 //
 // Same problem, inputs and outputs as attn_bwd_k in attention.cu (dQ accumulated in fp32 through
 // atomics, dK / dV in bf16), computed with one CTA per (128-key tile, kv head).  For every q head of
