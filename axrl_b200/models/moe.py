@@ -133,9 +133,28 @@ class MoEBlock(nn.Module):
         if ep_size > 1 or etp > 1:
             self.experts_gate_up.expert_parallel = True
             self.experts_down.expert_parallel = True
+        # shared expert (Qwen3-Next / 3.5): a dense SwiGLU FFN every token passes through, scaled by
+        # sigmoid(x . shared_gate); replicated like the attention weights, not expert-parallel
+        Fs = getattr(cfg, "shared_expert_intermediate_size", 0)
+        self.shared_gate_up = nn.Parameter(torch.empty(2 * Fs, H)) if Fs else None
+        self.shared_down = nn.Parameter(torch.empty(H, Fs)) if Fs else None
+        self.shared_gate = nn.Parameter(torch.empty(1, H)) if Fs else None
+
+    def shared_expert(self, x: torch.Tensor, linear=None) -> torch.Tensor | None:  # noqa: ANN001
+        """Gated shared-expert output for ``x`` (T, H) (None without a shared expert)."""
+        if self.shared_gate_up is None:
+            return None
+        lin = linear or ops.linear
+        y = lin(ops.swiglu(lin(x, self.shared_gate_up)), self.shared_down)
+        return y * torch.sigmoid(lin(x, self.shared_gate).float()).to(y.dtype)
 
     def hf_tensors(self, prefix: str) -> dict[str, torch.Tensor]:
         out = {prefix + "mlp.gate.weight": self.router}
+        if self.shared_gate_up is not None:
+            g, u = self.shared_gate_up.chunk(2, 0)
+            out |= {prefix + "mlp.shared_expert.gate_proj.weight": g, prefix + "mlp.shared_expert.up_proj.weight": u,
+                    prefix + "mlp.shared_expert.down_proj.weight": self.shared_down,
+                    prefix + "mlp.shared_expert_gate.weight": self.shared_gate}
         F = self.experts_down.shape[2]
         for e in range(self.E):
             q = f"{prefix}mlp.experts.{e}."
@@ -145,6 +164,11 @@ class MoEBlock(nn.Module):
         return out
 
     def forward(self, x: torch.Tensor, ctx: MoEContext | None = None, layer_idx: int = 0) -> torch.Tensor:
+        y = self._routed(x, ctx, layer_idx)
+        sh = self.shared_expert(x)
+        return y if sh is None else y + sh
+
+    def _routed(self, x: torch.Tensor, ctx: MoEContext | None, layer_idx: int) -> torch.Tensor:
         T, H = x.shape
         logits = router_logits(x, self.router)
         replay = ctx.replay.get(layer_idx) if ctx is not None and ctx.replay else None

@@ -71,6 +71,15 @@ class Qwen3Config:
     linear_key_head_dim: int = 128
     linear_value_head_dim: int = 128
     linear_conv_kernel_dim: int = 4
+    # Qwen3-Next / Qwen3.5 full-attention and MoE specifics
+    attn_output_gate: bool = False  # o <- o * sigmoid(x W_gate) per head before o_proj
+    partial_rotary_factor: float = 1.0  # RoPE on the first rotary_dim of each head, the rest passed through
+    zero_centered_norm: bool = False  # checkpoints store RMSNorm weights as offsets from 1
+    shared_expert_intermediate_size: int = 0  # sigmoid-gated shared expert beside the routed ones
+
+    @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary_factor)
 
     def layer_is_linear(self, i: int) -> bool:
         return self.layer_types is not None and self.layer_types[i] == "linear_attention"
@@ -88,12 +97,18 @@ class Qwen3Config:
 
     def num_params(self) -> int:
         H, D = self.hidden_size, self.head_dim
-        attn = H * (self.num_attention_heads + 2 * self.num_key_value_heads) * D + self.num_attention_heads * D * H + 2 * D
-        per = attn + 2 * H
+        nq = self.num_attention_heads * (2 if self.attn_output_gate else 1)
+        attn = H * (nq + 2 * self.num_key_value_heads) * D + self.num_attention_heads * D * H + 2 * D
+        kd = self.linear_num_key_heads * self.linear_key_head_dim
+        vd = self.linear_num_value_heads * self.linear_value_head_dim
+        nv = self.linear_num_value_heads
+        gdn = H * (2 * kd + vd) + (2 * kd + vd) * self.linear_conv_kernel_dim + H * vd + 2 * H * nv + 2 * nv + self.linear_value_head_dim + vd * H
+        shared = (3 * H * self.shared_expert_intermediate_size + H) if self.shared_expert_intermediate_size else 0
         total = 0
         for i in range(self.num_hidden_layers):
+            per = (gdn if self.layer_is_linear(i) else attn) + 2 * H
             if self.layer_is_moe(i):
-                total += per + H * self.num_experts + self.num_experts * 3 * H * self.moe_intermediate_size
+                total += per + H * self.num_experts + self.num_experts * 3 * H * self.moe_intermediate_size + shared
             else:
                 total += per + 3 * H * self.intermediate_size
         total += self.vocab_size * H * (1 if self.tie_word_embeddings else 2) + H
@@ -101,10 +116,24 @@ class Qwen3Config:
 
     @staticmethod
     def from_hf_dict(d: dict) -> "Qwen3Config":
+        """From an HF ``config.json`` dict: Qwen3 / Qwen3-MoE, and Qwen3-Next / Qwen3.5 (dense or MoE,
+        text model; a multimodal config's ``text_config`` is used)."""
+        if "text_config" in d and "hidden_size" not in d:
+            d = {**d["text_config"], "model_type": d["text_config"].get("model_type", d.get("model_type", ""))}
         keys = Qwen3Config.__dataclass_fields__.keys()
         kw = {k: d[k] for k in keys if k in d}
         if "head_dim" not in d and "hidden_size" in d:
             kw["head_dim"] = d["hidden_size"] // d["num_attention_heads"]
+        rope = d.get("rope_parameters") or {}
+        for k in ("rope_theta", "partial_rotary_factor"):
+            if k in rope:
+                kw[k] = rope[k]
+        if str(d.get("model_type", "")).startswith(("qwen3_next", "qwen3_5")):
+            kw.setdefault("attn_output_gate", True)
+            kw.setdefault("zero_centered_norm", True)
+            if "layer_types" not in d and "full_attention_interval" in d:
+                n = d["full_attention_interval"]
+                kw["layer_types"] = ["linear_attention" if (i + 1) % n else "full_attention" for i in range(d["num_hidden_layers"])]
         return Qwen3Config(**kw)
 
 
@@ -128,6 +157,24 @@ PRESETS: dict[str, Qwen3Config] = {
                             num_key_value_heads=2, head_dim=64, rope_theta=10000.0,
                             layer_types=["linear_attention", "linear_attention", "linear_attention", "full_attention"],
                             linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32),
+    # Qwen3.5-35B-A3B shape: 40 layers (3 Gated DeltaNet : 1 gated full attention), hidden 2048, 16q/2kv,
+    # head 256 with RoPE on the first 64 dims, 256 experts top-8 (FFN 512) + a shared expert (FFN 512),
+    # vocab 248320.
+    "qwen3.5-35b-a3b": Qwen3Config(vocab_size=248320, hidden_size=2048, intermediate_size=512, num_hidden_layers=40,
+                                   num_attention_heads=16, num_key_value_heads=2, head_dim=256, rope_theta=10000.0,
+                                   max_position_embeddings=32768, num_experts=256, num_experts_per_tok=8,
+                                   moe_intermediate_size=512, shared_expert_intermediate_size=512,
+                                   layer_types=["linear_attention" if (i + 1) % 4 else "full_attention" for i in range(40)],
+                                   linear_num_key_heads=16, linear_num_value_heads=32, linear_key_head_dim=128,
+                                   linear_value_head_dim=128, attn_output_gate=True, partial_rotary_factor=0.25,
+                                   zero_centered_norm=True),
+    # Plumbing model of the same family: 4 layers (3 GDN : 1 gated attention), MoE 8 experts top-2 + shared expert.
+    "tiny-qwen3.5": Qwen3Config(vocab_size=1024, hidden_size=256, intermediate_size=128, num_hidden_layers=4, num_attention_heads=4,
+                                num_key_value_heads=2, head_dim=64, rope_theta=10000.0, num_experts=8, num_experts_per_tok=2,
+                                moe_intermediate_size=128, shared_expert_intermediate_size=128,
+                                layer_types=["linear_attention", "linear_attention", "linear_attention", "full_attention"],
+                                linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32,
+                                attn_output_gate=True, partial_rotary_factor=0.25, zero_centered_norm=True),
 }
 
 
@@ -161,8 +208,18 @@ class Attention(nn.Module):
         self.o_proj = nn.Parameter(torch.empty(H, self.nq * self.d))
         self.q_norm = nn.Parameter(torch.ones(self.d))
         self.k_norm = nn.Parameter(torch.ones(self.d))
+        # output gate (Qwen3-Next / 3.5): a per-head sigmoid gate on the attention output, projected
+        # from the same input as q; kept as its own weight so the fused q/k/v layout is unchanged
+        self.attn_gate = nn.Parameter(torch.empty(self.nq * self.d, H)) if cfg.attn_output_gate else None
         self.cp = None  # context-parallel group (set by the model)
         self.stash = ops.AttnStash()  # attention outputs kept for the recompute in backward
+
+    def gate_output(self, o: torch.Tensor, x: torch.Tensor, linear=None) -> torch.Tensor:  # noqa: ANN001
+        """``o`` (rows, nq*d) times sigmoid of the gate projection of ``x`` (identity without a gate)."""
+        if self.attn_gate is None:
+            return o
+        g = (linear or ops.linear)(x, self.attn_gate)
+        return o * torch.sigmoid(g.float()).to(o.dtype)
 
     def forward(self, x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, tp: TPContext = _NO_TP) -> torch.Tensor:
         qkv = tpl.column_parallel_linear(x, self.qkv_proj, tp)
@@ -172,7 +229,10 @@ class Attention(nn.Module):
 
             k, v = gather_kv(k, self.cp), gather_kv(v, self.cp)
         o = ops.attention(q, k, v, spec, stash=self.stash if (self.training and torch.is_grad_enabled()) else None)
-        return tpl.row_parallel_linear(o.reshape(o.shape[0], -1), self.o_proj, tp)
+        o = o.reshape(o.shape[0], -1)
+        if self.attn_gate is not None:
+            o = o * torch.sigmoid(tpl.column_parallel_linear(x, self.attn_gate, tp).float()).to(o.dtype)
+        return tpl.row_parallel_linear(o, self.o_proj, tp)
 
 
 class MLP(nn.Module):
@@ -248,7 +308,7 @@ class Qwen3Model(nn.Module):
         self.layers = nn.ModuleList(DecoderLayer(cfg, i, tp_size, ep) for i in range(lo, hi))
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps) if self.last else None
         self.lm_head = None if (cfg.tie_word_embeddings or not self.last) else nn.Parameter(torch.empty(V, cfg.hidden_size))
-        self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.head_dim, cfg.rope_theta), persistent=False)
+        self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.rotary_dim, cfg.rope_theta), persistent=False)
         self.recompute = False
         self.grad_ready_hook = None  # set by an optimizer that reduces gradients during backward
         for layer in self.layers:
@@ -257,7 +317,7 @@ class Qwen3Model(nn.Module):
                 raise NotImplementedError("Gated DeltaNet layers with context parallelism are not built")
         if tp_size > 1:
             for name, p in self.named_parameters():
-                if p.dim() < 2 or ".mlp.router" in name or ".mlp.experts" in name:
+                if p.dim() < 2 or ".mlp.router" in name or ".mlp.experts" in name or ".mlp.shared_" in name:
                     tpl.mark_replicated(p)
 
     @property
@@ -354,17 +414,30 @@ class Qwen3Model(nn.Module):
 # ----------------------------------------------------------------------------- HF naming
 
 
-def hf_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
-    """Unfused HF-named tensors (views where possible)."""
+def _hf_entries(model: Qwen3Model) -> tuple[dict[str, torch.Tensor], dict]:
+    """HF name -> tensor (a view of a parameter where the layouts agree), and, for names whose HF
+    tensor is computed (zero-centered norm offsets, the interleaved q / gate rows of a gated q_proj),
+    a writer that stores an HF tensor back into the parameters."""
     cfg = model.cfg
-    out: dict[str, torch.Tensor] = {"model.embed_tokens.weight": model.embed_tokens, "model.norm.weight": model.norm.weight}
+    out: dict[str, torch.Tensor] = {}
+    writers: dict = {}
+
+    def norm(name: str, w: torch.Tensor) -> None:
+        if cfg.zero_centered_norm:  # HF stores (weight - 1); the kernels use the weight itself
+            out[name] = w.detach() - 1.0
+            writers[name] = lambda src, w=w: w.copy_(src.to(w.dtype) + 1.0)
+        else:
+            out[name] = w
+
+    out["model.embed_tokens.weight"] = model.embed_tokens
+    norm("model.norm.weight", model.norm.weight)
     if model.lm_head is not None:
         out["lm_head.weight"] = model.lm_head
     for i, layer in enumerate(model.layers):
         p = f"model.layers.{i}."
         a = layer.self_attn
-        out |= {p + "input_layernorm.weight": layer.input_layernorm.weight,
-                p + "post_attention_layernorm.weight": layer.post_attention_layernorm.weight}
+        norm(p + "input_layernorm.weight", layer.input_layernorm.weight)
+        norm(p + "post_attention_layernorm.weight", layer.post_attention_layernorm.weight)
         if cfg.layer_is_linear(i):  # HF Qwen3-Next / 3.5 "linear_attn" names
             q = p + "linear_attn."
             out |= {q + "in_proj_qkv.weight": a.in_proj_qkv, q + "in_proj_z.weight": a.in_proj_z, q + "in_proj_b.weight": a.in_proj_b,
@@ -372,21 +445,62 @@ def hf_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
                     q + "A_log": a.A_log, q + "norm.weight": a.norm_weight, q + "out_proj.weight": a.out_proj}
         else:
             q, k, v = a.qkv_proj.split([a.nq * a.d, a.nkv * a.d, a.nkv * a.d], 0)
-            out |= {p + "self_attn.q_proj.weight": q, p + "self_attn.k_proj.weight": k, p + "self_attn.v_proj.weight": v,
-                    p + "self_attn.o_proj.weight": a.o_proj, p + "self_attn.q_norm.weight": a.q_norm,
-                    p + "self_attn.k_norm.weight": a.k_norm}
+            out |= {p + "self_attn.k_proj.weight": k, p + "self_attn.v_proj.weight": v, p + "self_attn.o_proj.weight": a.o_proj}
+            if a.attn_gate is not None:  # HF q_proj rows: [q_h; gate_h] per head
+                name = p + "self_attn.q_proj.weight"
+                out[name] = torch.stack([q.detach().view(a.nq, a.d, -1), a.attn_gate.detach().view(a.nq, a.d, -1)], 1).reshape(2 * a.nq * a.d, -1)
+
+                def write(src: torch.Tensor, q=q, g=a.attn_gate, nq=a.nq, d=a.d) -> None:
+                    s2 = src.view(nq, 2, d, -1)
+                    q.copy_(s2[:, 0].reshape(nq * d, -1).to(q.dtype))
+                    g.copy_(s2[:, 1].reshape(nq * d, -1).to(g.dtype))
+
+                writers[name] = write
+            else:
+                out[p + "self_attn.q_proj.weight"] = q
+            norm(p + "self_attn.q_norm.weight", a.q_norm)
+            norm(p + "self_attn.k_norm.weight", a.k_norm)
         if cfg.layer_is_moe(i):
             out |= layer.mlp.hf_tensors(p)
         else:
             g, u = layer.mlp.gate_up_proj.chunk(2, 0)
             out |= {p + "mlp.gate_proj.weight": g, p + "mlp.up_proj.weight": u, p + "mlp.down_proj.weight": layer.mlp.down_proj}
+    return out, writers
+
+
+def hf_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
+    """Unfused HF-named tensors (views where possible)."""
+    return _hf_entries(model)[0]
+
+
+def _normalise_hf_names(sd: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+    """Accept a multimodal checkpoint's text tower (``model.language_model.*``) and fused 3-D expert
+    tensors (``mlp.experts.gate_up_proj`` (E, 2F, H) / ``mlp.experts.down_proj`` (E, H, F))."""
+    out: dict[str, torch.Tensor] = {}
+    for k, v in sd.items():
+        if k.startswith("model.language_model."):
+            k = "model." + k[len("model.language_model."):]
+        elif k.startswith(("model.visual.", "visual.", "mtp.")):
+            continue
+        if k.endswith("mlp.experts.gate_up_proj") and v.dim() == 3:
+            base, F = k[: -len("gate_up_proj")], v.shape[1] // 2
+            for e in range(v.shape[0]):
+                out[f"{base}{e}.gate_proj.weight"], out[f"{base}{e}.up_proj.weight"] = v[e, :F], v[e, F:]
+            continue
+        if k.endswith("mlp.experts.down_proj") and v.dim() == 3:
+            base = k[: -len("down_proj")]
+            for e in range(v.shape[0]):
+                out[f"{base}{e}.down_proj.weight"] = v[e]
+            continue
+        out[k] = v
     return out
 
 
 @torch.no_grad()
 def load_hf_state_dict(model: Qwen3Model, sd: dict[str, torch.Tensor], strict: bool = True) -> list[str]:
     """Copy HF tensors into the fused parameters; returns missing names."""
-    targets = hf_state_dict(model)
+    targets, writers = _hf_entries(model)
+    sd = _normalise_hf_names(sd)
     missing = []
     for name, dst in targets.items():
         src = sd.get(name)
@@ -396,7 +510,10 @@ def load_hf_state_dict(model: Qwen3Model, sd: dict[str, torch.Tensor], strict: b
             else:
                 missing.append(name)
                 continue
-        dst.copy_(src.to(dst.dtype))
+        if name in writers:
+            writers[name](src)
+        else:
+            dst.copy_(src.to(dst.dtype))
     if strict and missing:
         raise KeyError(f"missing HF tensors: {missing[:8]}{'...' if len(missing) > 8 else ''}")
     return missing

@@ -70,23 +70,35 @@ def rope_inv_freq(head_dim: int, theta: float, device=None) -> torch.Tensor:  # 
 
 
 def _rope_ref(x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
-    # x: (T, H, D); neox-style rotate-half, angles in fp32.
+    # x: (T, H, D); neox-style rotate-half over the first 2 * len(inv_freq) dims (all of them unless the
+    # rotary embedding is partial), the remaining dims passed through; angles in fp32.
+    R = 2 * inv_freq.numel()
     ang = pos.float()[:, None] * inv_freq[None, :].to(pos.device)
     cos = torch.cat([ang.cos(), ang.cos()], -1)[:, None, :]
     sin = torch.cat([ang.sin(), ang.sin()], -1)[:, None, :]
     xf = x.float()
-    h = xf.shape[-1] // 2
-    rot = torch.cat([-xf[..., h:], xf[..., :h]], -1)
-    return (xf * cos + rot * sin).to(x.dtype)
+    xr = xf[..., :R]
+    h = R // 2
+    rot = torch.cat([-xr[..., h:], xr[..., :h]], -1)
+    out = xr * cos + rot * sin
+    if R < xf.shape[-1]:
+        out = torch.cat([out, xf[..., R:]], -1)
+    return out.to(x.dtype)
 
 
 def _qk_norm_rope_ref(qkv, qw, kw, pos, inv_freq, nq, nkv, eps):  # noqa: ANN001, ANN202
     T = qkv.shape[0]
-    D = inv_freq.numel() * 2
+    D = qw.numel()
     q, k, v = qkv.view(T, nq + 2 * nkv, D).split([nq, nkv, nkv], dim=1)
     q = _rope_ref(_rms_ref(q, qw, eps), pos, inv_freq)
     k = _rope_ref(_rms_ref(k, kw, eps), pos, inv_freq)
     return q.contiguous(), k.contiguous(), v.contiguous()
+
+
+def check_full_rotary(qw: torch.Tensor, inv_freq: torch.Tensor) -> None:
+    """The q/k-norm + RoPE kernels rotate the whole head (head_dim 128)."""
+    if 2 * inv_freq.numel() != qw.numel():
+        raise NotImplementedError(f"partial rotary embedding ({2 * inv_freq.numel()} of {qw.numel()} dims) has no CUDA kernel yet")
 
 
 class _QKNormRope(torch.autograd.Function):
@@ -110,6 +122,7 @@ def qk_norm_rope(qkv, q_norm_w, k_norm_w, pos, inv_freq, nq: int, nkv: int, eps:
     Returns contiguous ``q (T,nq,D)``, ``k (T,nkv,D)``, ``v (T,nkv,D)``."""
     if not qkv.is_cuda:
         return _qk_norm_rope_ref(qkv, q_norm_w, k_norm_w, pos, inv_freq, nq, nkv, eps)
+    check_full_rotary(q_norm_w, inv_freq)
     return _QKNormRope.apply(qkv.contiguous(), q_norm_w, k_norm_w, pos.to(torch.int32).contiguous(), inv_freq, nq, nkv, eps)
 
 

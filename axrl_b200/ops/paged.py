@@ -13,7 +13,7 @@ import math
 import torch
 
 from axrl_b200.ops import _ext
-from axrl_b200.ops.core import _qk_norm_rope_ref
+from axrl_b200.ops.core import _qk_norm_rope_ref, check_full_rotary
 
 SPLIT_TOKENS = 128  # tokens per decode CTA (must match dec::SPLIT)
 
@@ -31,6 +31,7 @@ def qk_norm_rope_cache(qkv, qw, kw, pos, inv_freq, nq, nkv, eps, k_cache, v_cach
         _scatter_ref(k_cache, k, slots.long())
         _scatter_ref(v_cache, v, slots.long())
         return q, k, v
+    check_full_rotary(qw, inv_freq)
     return _ext.ext().qknorm_rope_cache(qkv, qw, kw, pos, inv_freq, nq, nkv, eps, k_cache, v_cache, slots)
 
 

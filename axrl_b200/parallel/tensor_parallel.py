@@ -332,7 +332,7 @@ def shard_param(name: str, full: torch.Tensor, tp_rank: int, tp_size: int, cfg: 
         return torch.cat([full[:f].chunk(tp_size, 0)[tp_rank], full[f:].chunk(tp_size, 0)[tp_rank]], 0)
     if name.endswith(("o_proj", "down_proj")):
         return full.chunk(tp_size, 1)[tp_rank]
-    if name.endswith(("embed_tokens", "lm_head")):
+    if name.endswith(("embed_tokens", "lm_head", "attn_gate")):
         return full.chunk(tp_size, 0)[tp_rank]
     return full  # MoE experts / router: replicated over TP
 
@@ -354,7 +354,7 @@ def unshard_param(name: str, shards: list[torch.Tensor], cfg: Any) -> torch.Tens
         return torch.cat([torch.cat([s[:f] for s in shards], 0), torch.cat([s[f:] for s in shards], 0)], 0)
     if name.endswith(("o_proj", "down_proj")):
         return torch.cat(shards, 1)
-    if name.endswith(("embed_tokens", "lm_head")):
+    if name.endswith(("embed_tokens", "lm_head", "attn_gate")):
         return torch.cat(shards, 0)
     return shards[0]
 

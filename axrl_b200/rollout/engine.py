@@ -286,8 +286,8 @@ class RolloutEngine:
             a = layer.self_attn
             qkv = self._lin(x, a.qkv_proj)
             q, k, v = paged.qk_norm_rope_cache(qkv, a.q_norm, a.k_norm, pos, inv, a.nq, a.nkv, a.eps, self.kv[li, 0], self.kv[li, 1], slots)
-            o = attend(li, q, k, v)
-            self._lin_into(o.reshape(rows, -1), a.o_proj, tp.partial_buffer(rows))
+            o = a.gate_output(attend(li, q, k, v).reshape(rows, -1), x, self._lin)
+            self._lin_into(o, a.o_proj, tp.partial_buffer(rows))
             h, x = tp.allreduce_rms(rows, h, layer.post_attention_layernorm.weight, eps)
             g = ops.swiglu(self._lin(x, layer.mlp.gate_up_proj))
             self._lin_into(g, layer.mlp.down_proj, tp.partial_buffer(rows))
@@ -321,8 +321,8 @@ class RolloutEngine:
             qkv = self._lin(x, a.qkv_proj)
             q, k, v = paged.qk_norm_rope_cache(qkv, a.q_norm, a.k_norm, pos, inv, a.nq, a.nkv, a.eps,
                                                self.kv[li, 0], self.kv[li, 1], slots)
-            o = attend(li, q, k, v)
-            h = self._lin(o.reshape(o.shape[0], -1), a.o_proj, residual=h)
+            o = a.gate_output(attend(li, q, k, v).reshape(q.shape[0], -1), x, self._lin)
+            h = self._lin(o, a.o_proj, residual=h)
             x = self._rms(h, layer.post_attention_layernorm.weight)
             h = self._mlp(layer, x, h, capture, li)
         return self._rms(h, self.model.norm.weight)

@@ -69,6 +69,8 @@ def qwen3_param_specs(cfg: Qwen3Config) -> list[ParamSpec]:
                 ParamSpec(p + "self_attn.q_norm", (Sub(1, D, -1),)),
                 ParamSpec(p + "self_attn.k_norm", (Sub(1, D, -1),)),
             ]
+            if cfg.attn_output_gate:
+                specs.append(ParamSpec(p + "self_attn.attn_gate", (Sub(nq * D, H, 0),)))
         specs += [
             ParamSpec(p + "post_attention_layernorm.weight", (Sub(1, H, -1),)),
             ParamSpec(p + "mlp.gate_up_proj", (Sub(F, H, 0), Sub(F, H, 0))),

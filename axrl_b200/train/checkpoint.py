@@ -100,91 +100,81 @@ def _qkv_from_mcore(w: torch.Tensor, nq: int, nkv: int, d: int) -> torch.Tensor:
     return torch.cat([q.reshape(nq * d, -1), k.reshape(nkv * d, -1), v.reshape(nkv * d, -1)], 0)
 
 
-def mcore_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
-    """Megatron-Core names, transformer layers stacked on axis 0."""
+def _mcore_entries(model: Qwen3Model) -> list[tuple[str, int | None, torch.Tensor, Any]]:
+    """(Megatron-Core name, layer index or None, tensor in that layout, writer) for every tensor.
+
+    Entries of the same name over all layers are stacked on axis 0; a hybrid model keys its
+    token-mixer tensors per layer (``decoder.layers.{i}.*``) since the mixers differ.  Zero-centered
+    RMSNorms (Qwen3-Next / 3.5) are stored as offsets from 1, like Megatron's zero-centered gamma."""
     cfg = model.cfg
-    L = cfg.num_hidden_layers
-    out = {"embedding.word_embeddings.weight": model.embed_tokens.detach(), "decoder.final_layernorm.weight": model.norm.weight.detach()}
+    ents: list[tuple[str, int | None, torch.Tensor, Any]] = []
+
+    def plain(name: str, i: int | None, p: torch.Tensor) -> None:
+        ents.append((name, i, p.detach(), lambda src, p=p: p.copy_(src.to(p.dtype))))
+
+    def norm(name: str, i: int | None, p: torch.Tensor) -> None:
+        if cfg.zero_centered_norm:
+            ents.append((name, i, p.detach() - 1.0, lambda src, p=p: p.copy_(src.to(p.dtype) + 1.0)))
+        else:
+            plain(name, i, p)
+
+    plain("embedding.word_embeddings.weight", None, model.embed_tokens)
+    norm("decoder.final_layernorm.weight", None, model.norm.weight)
     if model.lm_head is not None:
-        out["output_layer.weight"] = model.lm_head.detach()
-    per: dict[str, list[torch.Tensor]] = {}
-
-    def add(k: str, v: torch.Tensor) -> None:
-        per.setdefault(k, []).append(v.detach())
-
+        plain("output_layer.weight", None, model.lm_head)
     for i, layer in enumerate(model.layers):
         a = layer.self_attn
-        add("decoder.layers.self_attention.linear_qkv.layer_norm_weight", layer.input_layernorm.weight)
-        if cfg.is_hybrid:  # heterogeneous mixers: one entry per layer instead of a stacked one
-            for n, t in _mixer_tensors(cfg, i, a).items():
-                out[n] = t.detach()
+        norm("decoder.layers.self_attention.linear_qkv.layer_norm_weight", i, layer.input_layernorm.weight)
+        m = f"decoder.layers.{i}." if cfg.is_hybrid else "decoder.layers."  # mixer tensors of a hybrid model: per layer
+        if cfg.layer_is_linear(i):
+            for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "conv_weight", "dt_bias", "A_log", "norm_weight", "out_proj"):
+                plain(m + f"linear_attention.{n}", None, getattr(a, n))
         else:
-            add("decoder.layers.self_attention.linear_qkv.weight", _qkv_to_mcore(a.qkv_proj.detach(), a.nq, a.nkv, a.d))
-            add("decoder.layers.self_attention.linear_proj.weight", a.o_proj)
-            add("decoder.layers.self_attention.q_layernorm.weight", a.q_norm)
-            add("decoder.layers.self_attention.k_layernorm.weight", a.k_norm)
+            li = None if cfg.is_hybrid else i
+            ents.append((m + "self_attention.linear_qkv.weight", li, _qkv_to_mcore(a.qkv_proj.detach(), a.nq, a.nkv, a.d),
+                         lambda src, a=a: a.qkv_proj.copy_(_qkv_from_mcore(src, a.nq, a.nkv, a.d).to(a.qkv_proj.dtype))))
+            plain(m + "self_attention.linear_proj.weight", li, a.o_proj)
+            norm(m + "self_attention.q_layernorm.weight", li, a.q_norm)
+            norm(m + "self_attention.k_layernorm.weight", li, a.k_norm)
+            if a.attn_gate is not None:
+                plain(m + "self_attention.linear_gate.weight", li, a.attn_gate)
         mlp = layer.mlp
         if hasattr(mlp, "router"):
-            add("decoder.layers.pre_mlp_layernorm.weight", layer.post_attention_layernorm.weight)
-            add("decoder.layers.mlp.router.weight", mlp.router)
-            add("decoder.layers.mlp.experts.linear_fc1.weight", mlp.experts_gate_up)
-            add("decoder.layers.mlp.experts.linear_fc2.weight", mlp.experts_down)
+            norm("decoder.layers.pre_mlp_layernorm.weight", i, layer.post_attention_layernorm.weight)
+            plain("decoder.layers.mlp.router.weight", i, mlp.router)
+            plain("decoder.layers.mlp.experts.linear_fc1.weight", i, mlp.experts_gate_up)
+            plain("decoder.layers.mlp.experts.linear_fc2.weight", i, mlp.experts_down)
+            if mlp.shared_gate_up is not None:
+                plain("decoder.layers.mlp.shared_experts.linear_fc1.weight", i, mlp.shared_gate_up)
+                plain("decoder.layers.mlp.shared_experts.linear_fc2.weight", i, mlp.shared_down)
+                plain("decoder.layers.mlp.shared_experts.gate_weight", i, mlp.shared_gate)
         else:
-            add("decoder.layers.mlp.linear_fc1.layer_norm_weight", layer.post_attention_layernorm.weight)
-            add("decoder.layers.mlp.linear_fc1.weight", mlp.gate_up_proj)
-            add("decoder.layers.mlp.linear_fc2.weight", mlp.down_proj)
+            norm("decoder.layers.mlp.linear_fc1.layer_norm_weight", i, layer.post_attention_layernorm.weight)
+            plain("decoder.layers.mlp.linear_fc1.weight", i, mlp.gate_up_proj)
+            plain("decoder.layers.mlp.linear_fc2.weight", i, mlp.down_proj)
+    return ents
+
+
+def mcore_state_dict(model: Qwen3Model) -> dict[str, torch.Tensor]:
+    """Megatron-Core names, transformer layers stacked on axis 0."""
+    L = model.cfg.num_hidden_layers
+    out: dict[str, torch.Tensor] = {}
+    per: dict[str, list[torch.Tensor]] = {}
+    for name, i, t, _ in _mcore_entries(model):
+        if i is None:
+            out[name] = t
+        else:
+            per.setdefault(name, []).append(t)
     for k, vs in per.items():
         assert len(vs) == L, f"{k}: heterogeneous layers are not stacked"
         out[k] = torch.stack(vs, 0)
     return out
 
 
-def _mixer_tensors(cfg, i: int, a) -> dict[str, torch.Tensor]:  # noqa: ANN001
-    """Token-mixer tensors of layer ``i`` of a hybrid model, keyed per layer."""
-    p = f"decoder.layers.{i}."
-    if cfg.layer_is_linear(i):
-        return {p + f"linear_attention.{n}": getattr(a, n) for n in
-                ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "conv_weight", "dt_bias", "A_log", "norm_weight", "out_proj")}
-    return {p + "self_attention.linear_qkv.weight": _qkv_to_mcore(a.qkv_proj.detach(), a.nq, a.nkv, a.d),
-            p + "self_attention.linear_proj.weight": a.o_proj, p + "self_attention.q_layernorm.weight": a.q_norm,
-            p + "self_attention.k_layernorm.weight": a.k_norm}
-
-
 @torch.no_grad()
 def load_mcore_state_dict(model: Qwen3Model, sd: dict[str, torch.Tensor]) -> None:
-    model.embed_tokens.copy_(sd["embedding.word_embeddings.weight"])
-    model.norm.weight.copy_(sd["decoder.final_layernorm.weight"])
-    if model.lm_head is not None:
-        model.lm_head.copy_(sd["output_layer.weight"])
-    for i, layer in enumerate(model.layers):
-        a = layer.self_attn
-        g = lambda k: sd[k][i]  # noqa: E731
-        layer.input_layernorm.weight.copy_(g("decoder.layers.self_attention.linear_qkv.layer_norm_weight"))
-        if model.cfg.is_hybrid:
-            p = f"decoder.layers.{i}."
-            if model.cfg.layer_is_linear(i):
-                for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "conv_weight", "dt_bias", "A_log", "norm_weight", "out_proj"):
-                    getattr(a, n).copy_(sd[p + f"linear_attention.{n}"])
-            else:
-                a.qkv_proj.copy_(_qkv_from_mcore(sd[p + "self_attention.linear_qkv.weight"], a.nq, a.nkv, a.d))
-                a.o_proj.copy_(sd[p + "self_attention.linear_proj.weight"])
-                a.q_norm.copy_(sd[p + "self_attention.q_layernorm.weight"])
-                a.k_norm.copy_(sd[p + "self_attention.k_layernorm.weight"])
-        else:
-            a.qkv_proj.copy_(_qkv_from_mcore(g("decoder.layers.self_attention.linear_qkv.weight"), a.nq, a.nkv, a.d))
-            a.o_proj.copy_(g("decoder.layers.self_attention.linear_proj.weight"))
-            a.q_norm.copy_(g("decoder.layers.self_attention.q_layernorm.weight"))
-            a.k_norm.copy_(g("decoder.layers.self_attention.k_layernorm.weight"))
-        mlp = layer.mlp
-        if hasattr(mlp, "router"):
-            layer.post_attention_layernorm.weight.copy_(g("decoder.layers.pre_mlp_layernorm.weight"))
-            mlp.router.copy_(g("decoder.layers.mlp.router.weight"))
-            mlp.experts_gate_up.copy_(g("decoder.layers.mlp.experts.linear_fc1.weight"))
-            mlp.experts_down.copy_(g("decoder.layers.mlp.experts.linear_fc2.weight"))
-        else:
-            layer.post_attention_layernorm.weight.copy_(g("decoder.layers.mlp.linear_fc1.layer_norm_weight"))
-            mlp.gate_up_proj.copy_(g("decoder.layers.mlp.linear_fc1.weight"))
-            mlp.down_proj.copy_(g("decoder.layers.mlp.linear_fc2.weight"))
+    for name, i, _, write in _mcore_entries(model):
+        write(sd[name] if i is None else sd[name][i])
 
 
 def _iter_dir(root: Path, step: int) -> Path:
