@@ -117,10 +117,19 @@ def gated_delta_recurrent(q, k, v, g, beta, state=None):  # noqa: ANN001, ANN201
 
 
 class GatedDeltaNet(nn.Module):
-    def __init__(self, cfg) -> None:  # noqa: ANN001
+    """Under tensor parallelism (``tp_size`` ranks) each rank holds 1/tp of the key and value heads
+    (value head j reads key head j // (nv / nk), so contiguous head blocks stay together): the q/k/v,
+    z, b, a projections, the convolution channels, ``dt_bias`` and ``A_log`` are split by heads, the
+    output projection by its input columns; the recurrence then runs on whole sequences of this
+    rank's heads (the sequence-parallel input is all-gathered once, the output reduce-scattered),
+    as Megatron shards its GDN layers."""
+
+    def __init__(self, cfg, tp_size: int = 1) -> None:  # noqa: ANN001
         super().__init__()
         H = cfg.hidden_size
-        self.nk, self.nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        if cfg.linear_num_key_heads % tp_size or cfg.linear_num_value_heads % tp_size:
+            raise ValueError("linear-attention key / value heads must split evenly over TP ranks")
+        self.nk, self.nv = cfg.linear_num_key_heads // tp_size, cfg.linear_num_value_heads // tp_size
         self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
         self.kernel = cfg.linear_conv_kernel_dim
         self.eps = cfg.rms_norm_eps
@@ -160,17 +169,25 @@ class GatedDeltaNet(nn.Module):
         g = -self.A_log.float().exp() * F.softplus(a + self.dt_bias.float())
         return q, k, v, g, b.sigmoid()
 
-    def _out(self, o: torch.Tensor, z: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    def _out(self, o: torch.Tensor, z: torch.Tensor, dtype: torch.dtype, tp=None) -> torch.Tensor:  # noqa: ANN001
         T = o.shape[0]
         o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + self.eps) * self.norm_weight.float()
         o = o * F.silu(z.float().reshape(T, self.nv, self.dv))
-        return F.linear(o.reshape(T, self.value_dim).to(dtype), self.out_proj)
+        o = o.reshape(T, self.value_dim).to(dtype)
+        if tp is not None:
+            from axrl_b200.parallel.tensor_parallel import row_parallel_linear
+
+            return row_parallel_linear(o, self.out_proj, tp)
+        return F.linear(o, self.out_proj)
 
     # ---- training / prefill over packed sequences
     def forward(self, x: torch.Tensor, pos, inv_freq, spec, tp=None, states: list | None = None) -> torch.Tensor:  # noqa: ANN001
         """``states`` (optional, prefill): receives one (conv_state, recurrent_state) per sequence."""
-        if tp is not None and getattr(tp, "enabled", False):
-            raise NotImplementedError("GDN layers run without tensor parallelism")
+        tp = tp if tp is not None and getattr(tp, "enabled", False) else None
+        if tp is not None:  # whole sequences of this rank's heads: gather the sequence-parallel rows
+            from axrl_b200.parallel.tensor_parallel import gather_from_sp
+
+            x = gather_from_sp(x, tp)
         T = x.shape[0]
         segs = _segments(spec, T)
         starts = torch.zeros(T, dtype=torch.long, device=x.device)
@@ -188,7 +205,7 @@ class GatedDeltaNet(nn.Module):
                 cs = torch.zeros(self.kernel - 1, self.conv_dim, dtype=torch.float32, device=x.device)
                 cs[cs.shape[0] - tailx.shape[0]:] = tailx
                 states.append((cs, S))
-        return self._out(o, z, x.dtype)
+        return self._out(o, z, x.dtype, tp)
 
     # ---- decode: one token per row with carried states
     def step(self, x: torch.Tensor, conv_state: torch.Tensor, S: torch.Tensor) -> torch.Tensor:

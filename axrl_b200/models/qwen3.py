@@ -253,8 +253,7 @@ class DecoderLayer(nn.Module):
         if cfg.layer_is_linear(layer_idx):
             from axrl_b200.models.gdn import GatedDeltaNet
 
-            assert tp_size == 1, "Gated DeltaNet layers run without tensor parallelism"
-            self.self_attn: nn.Module = GatedDeltaNet(cfg)
+            self.self_attn: nn.Module = GatedDeltaNet(cfg, tp_size)
         else:
             self.self_attn = Attention(cfg, tp_size)
         self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
@@ -317,7 +316,8 @@ class Qwen3Model(nn.Module):
                 raise NotImplementedError("Gated DeltaNet layers with context parallelism are not built")
         if tp_size > 1:
             for name, p in self.named_parameters():
-                if p.dim() < 2 or ".mlp.router" in name or ".mlp.experts" in name or ".mlp.shared_" in name:
+                if (p.dim() < 2 and not name.endswith(("dt_bias", "A_log"))) or ".mlp.router" in name or ".mlp.experts" in name \
+                        or ".mlp.shared_" in name:
                     tpl.mark_replicated(p)
 
     @property

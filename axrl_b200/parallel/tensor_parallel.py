@@ -317,9 +317,22 @@ def replicated_sqnorm(model: torch.nn.Module) -> torch.Tensor | None:
 # ----------------------------------------------------------------------------- sharding
 
 
+def _gdn_qkv_rows(cfg: Any) -> list[int]:
+    kd = cfg.linear_num_key_heads * cfg.linear_key_head_dim
+    return [kd, kd, cfg.linear_num_value_heads * cfg.linear_value_head_dim]
+
+
 def shard_param(name: str, full: torch.Tensor, tp_rank: int, tp_size: int, cfg: Any) -> torch.Tensor:
     """The TP shard of a full (TP=1) parameter of a Qwen3Model, by parameter name."""
-    if tp_size == 1 or full.dim() < 2:
+    if tp_size == 1:
+        return full
+    if name.endswith(("in_proj_qkv", "conv_weight")):  # Gated DeltaNet: [q; k; v] channels split by heads
+        return torch.cat([t.chunk(tp_size, 0)[tp_rank] for t in full.split(_gdn_qkv_rows(cfg), 0)], 0)
+    if name.endswith(("in_proj_z", "in_proj_b", "in_proj_a", "dt_bias", "A_log")):
+        return full.chunk(tp_size, 0)[tp_rank]
+    if name.endswith("out_proj"):
+        return full.chunk(tp_size, 1)[tp_rank]
+    if full.dim() < 2:
         return full
     d = cfg.head_dim
     if name.endswith("qkv_proj"):
@@ -340,7 +353,17 @@ def shard_param(name: str, full: torch.Tensor, tp_rank: int, tp_size: int, cfg: 
 def unshard_param(name: str, shards: list[torch.Tensor], cfg: Any) -> torch.Tensor:
     """Inverse of :func:`shard_param` given every rank's shard in rank order."""
     tp = len(shards)
-    if tp == 1 or shards[0].dim() < 2:
+    if tp == 1:
+        return shards[0]
+    if name.endswith(("in_proj_qkv", "conv_weight")):
+        rows = [r // tp for r in _gdn_qkv_rows(cfg)]
+        parts = [s.split(rows, 0) for s in shards]
+        return torch.cat([torch.cat([p[i] for p in parts], 0) for i in range(3)], 0)
+    if name.endswith(("in_proj_z", "in_proj_b", "in_proj_a", "dt_bias", "A_log")):
+        return torch.cat(shards, 0)
+    if name.endswith("out_proj"):
+        return torch.cat(shards, 1)
+    if shards[0].dim() < 2:
         return shards[0]
     d = cfg.head_dim
     if name.endswith("qkv_proj"):
@@ -371,7 +394,7 @@ def gather_full_state(model: torch.nn.Module, tp: TPContext) -> dict[str, torch.
     """Every parameter in its full (TP=1) shape, on every TP rank."""
     out = {}
     for name, p in model.named_parameters():
-        if not tp.enabled or p.dim() < 2 or getattr(p, "tp_replicated", False):
+        if not tp.enabled or getattr(p, "tp_replicated", False):
             out[name] = p.detach().clone()
             continue
         x = p.detach().contiguous()

@@ -53,15 +53,15 @@ def qwen3_param_specs(cfg: Qwen3Config) -> list[ParamSpec]:
     for i in range(cfg.num_hidden_layers):
         p = f"layers.{i}."
         specs.append(ParamSpec(p + "input_layernorm.weight", (Sub(1, H, -1),)))
-        if cfg.layer_is_linear(i):  # Gated DeltaNet mixer: replicated (no TP sharding)
+        if cfg.layer_is_linear(i):  # Gated DeltaNet mixer: split by heads over TP, like Megatron
             kd, vd = cfg.linear_num_key_heads * cfg.linear_key_head_dim, cfg.linear_num_value_heads * cfg.linear_value_head_dim
             nv, K = cfg.linear_num_value_heads, cfg.linear_conv_kernel_dim
             a = p + "self_attn."
-            specs += [ParamSpec(a + "in_proj_qkv", (Sub(2 * kd + vd, H, -1),)), ParamSpec(a + "in_proj_z", (Sub(vd, H, -1),)),
-                      ParamSpec(a + "in_proj_b", (Sub(nv, H, -1),)), ParamSpec(a + "in_proj_a", (Sub(nv, H, -1),)),
-                      ParamSpec(a + "conv_weight", (Sub(2 * kd + vd, K, -1),)), ParamSpec(a + "dt_bias", (Sub(1, nv, -1),)),
-                      ParamSpec(a + "A_log", (Sub(1, nv, -1),)), ParamSpec(a + "norm_weight", (Sub(1, cfg.linear_value_head_dim, -1),)),
-                      ParamSpec(a + "out_proj", (Sub(H, vd, -1),))]
+            specs += [ParamSpec(a + "in_proj_qkv", (Sub(kd, H, 0), Sub(kd, H, 0), Sub(vd, H, 0))), ParamSpec(a + "in_proj_z", (Sub(vd, H, 0),)),
+                      ParamSpec(a + "in_proj_b", (Sub(nv, H, 0),)), ParamSpec(a + "in_proj_a", (Sub(nv, H, 0),)),
+                      ParamSpec(a + "conv_weight", (Sub(kd, K, 0), Sub(kd, K, 0), Sub(vd, K, 0))), ParamSpec(a + "dt_bias", (Sub(1, nv, 1),)),
+                      ParamSpec(a + "A_log", (Sub(1, nv, 1),)), ParamSpec(a + "norm_weight", (Sub(1, cfg.linear_value_head_dim, -1),)),
+                      ParamSpec(a + "out_proj", (Sub(H, vd, 1),))]
         else:
             specs += [
                 ParamSpec(p + "self_attn.qkv_proj", (Sub(nq * D, H, 0), Sub(nkv * D, H, 0), Sub(nkv * D, H, 0))),
@@ -117,8 +117,10 @@ def build_layout(specs: list[ParamSpec], tp: int, fp8: bool, base: int = 0) -> L
 
 def quantizable(spec: ParamSpec, rows: int, cols: int) -> bool:
     """Block-fp8 only for TP-split matrices whose local shape is a whole number of 128x128 blocks
-    (norms and other replicated vectors stay bf16)."""
-    return all(s.split != -1 for s in spec.subs) and rows % TILE == 0 and cols % TILE == 0
+    (norms and other replicated vectors stay bf16) among the weights the rollout engine runs as fp8
+    GEMMs (the fused attention / MLP projections)."""
+    fp8_gemm = spec.name.endswith(("qkv_proj", "o_proj", "gate_up_proj", "down_proj", "lm_head", "embed_tokens"))
+    return fp8_gemm and all(s.split != -1 for s in spec.subs) and rows % TILE == 0 and cols % TILE == 0
 
 
 def _slices(sub: Sub, tp: int) -> list[tuple[int, int, int, int]]:

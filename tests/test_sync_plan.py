@@ -45,3 +45,32 @@ def test_reshard_plan(src_tp, dst_tp, fp8):
             else:
                 u = bufs[rk].view(np.uint16)[dl.offsets[s.name]: dl.offsets[s.name] + rr * cc].astype(np.int32) << 16
                 assert torch.equal(torch.from_numpy(u).view(torch.float32).view(rr, cc), exp), s.name
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_specs_match_trainer_shards(tp):
+    """The plan's per-rank layout of every parameter (Gated DeltaNet and gated attention included) is
+    the trainer's own TP shard of it."""
+    from axrl_b200.models.qwen3 import Qwen3Model
+    from axrl_b200.parallel.tensor_parallel import shard_param
+
+    cfg = Qwen3Config(vocab_size=256, hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=4, head_dim=16, layer_types=["linear_attention", "full_attention"],
+                      linear_num_key_heads=4, linear_num_value_heads=8, linear_key_head_dim=8, linear_value_head_dim=8,
+                      attn_output_gate=True)
+    m = Qwen3Model(cfg)
+    m.init_weights(2)
+    params = dict(m.named_parameters())
+    specs = qwen3_param_specs(cfg)
+    assert {s.name for s in specs} == set(params)
+    for s in specs:
+        full = params[s.name].detach()
+        full2 = full.reshape(1, -1) if full.dim() == 1 else full
+        blocks, r0 = [], 0
+        for sub in s.subs:
+            blocks.append(full2[r0:r0 + sub.rows])
+            r0 += sub.rows
+        for r in range(tp):
+            want = torch.cat([blk[a:b, c:d] for sub, blk in zip(s.subs, blocks) for a, b, c, d in [_slices(sub, tp)[r]]], 0)
+            got = shard_param(s.name, full, r, tp, cfg)
+            torch.testing.assert_close(got.reshape(want.shape), want, msg=s.name)

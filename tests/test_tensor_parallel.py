@@ -19,13 +19,19 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _cfg(moe: bool = False):
+def _cfg(moe: bool | str = False):
+    """``moe``: False (dense), True (MoE) or "hybrid" (Qwen3.5 style: Gated DeltaNet + gated attention
+    with partial RoPE, MoE with a shared expert)."""
     from axrl_b200.models.qwen3 import Qwen3Config
 
     kw = dict(vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
               num_key_value_heads=2, head_dim=16)
     if moe:
         kw.update(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=32)
+    if moe == "hybrid":
+        kw.update(layer_types=["linear_attention", "full_attention"], linear_num_key_heads=2, linear_num_value_heads=4,
+                  linear_key_head_dim=16, linear_value_head_dim=8, attn_output_gate=True, partial_rotary_factor=0.5,
+                  zero_centered_norm=True, shared_expert_intermediate_size=24)
     return Qwen3Config(**kw)
 
 
@@ -122,7 +128,7 @@ def _worker(rank: int, world: int, port: int, moe: bool, q) -> None:  # noqa: AN
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("moe", [False, True])
+@pytest.mark.parametrize("moe", [False, True, "hybrid"])
 def test_tp2_matches_tp1(moe):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -137,16 +143,19 @@ def test_tp2_matches_tp1(moe):
         assert msg == "ok", f"rank {r}:\n{msg}"
 
 
-def test_shard_unshard_roundtrip():
+@pytest.mark.parametrize("kind", [False, "hybrid"])
+def test_shard_unshard_roundtrip(kind):
     from axrl_b200.models.qwen3 import Qwen3Model
     from axrl_b200.parallel import tensor_parallel as tpl
 
-    cfg = _cfg()
+    cfg = _cfg(kind)
     m = Qwen3Model(cfg)
     m.init_weights(1)
     for n, p in m.named_parameters():
         for tp in (2, 4):
             if p.dim() >= 2 and n.endswith("qkv_proj") and cfg.num_key_value_heads % tp:
+                continue
+            if cfg.linear_num_key_heads % tp and n.startswith("layers.0.self_attn."):  # GDN layer 0: 2 key heads
                 continue
             shards = [tpl.shard_param(n, p.detach(), r, tp, cfg) for r in range(tp)]
             torch.testing.assert_close(tpl.unshard_param(n, shards, cfg), p.detach())
