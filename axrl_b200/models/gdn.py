@@ -154,20 +154,56 @@ class GatedDeltaNet(nn.Module):
         a = F.linear(x, self.in_proj_a).float()
         return mixed, z, b, a
 
-    def _heads(self, mixed: torch.Tensor, b: torch.Tensor, a: torch.Tensor):  # noqa: ANN202
+    def _heads(self, mixed: torch.Tensor, b: torch.Tensor, a: torch.Tensor, heads: tuple | None = None):  # noqa: ANN202
+        """``heads`` = (nk, nv, A_log, dt_bias) of a head subset (context parallelism); default all."""
+        nk, nv, A_log, dt_bias = heads or (self.nk, self.nv, self.A_log, self.dt_bias)
         T = mixed.shape[0]
-        q, k, v = torch.split(mixed.float(), [self.key_dim, self.key_dim, self.value_dim], -1)
-        q = q.reshape(T, self.nk, self.dk)
-        k = k.reshape(T, self.nk, self.dk)
-        v = v.reshape(T, self.nv, self.dv)
+        q, k, v = torch.split(mixed.float(), [nk * self.dk, nk * self.dk, nv * self.dv], -1)
+        q = q.reshape(T, nk, self.dk)
+        k = k.reshape(T, nk, self.dk)
+        v = v.reshape(T, nv, self.dv)
         q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6)
         k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
-        rep = self.nv // self.nk
+        rep = nv // nk
         if rep > 1:
             q, k = q.repeat_interleave(rep, 1), k.repeat_interleave(rep, 1)
         q = q / math.sqrt(self.dk)
-        g = -self.A_log.float().exp() * F.softplus(a + self.dt_bias.float())
+        g = -A_log.float().exp() * F.softplus(a + dt_bias.float())
         return q, k, v, g, b.sigmoid()
+
+    def _forward_cp(self, mixed: torch.Tensor, b: torch.Tensor, a: torch.Tensor, layout) -> torch.Tensor:  # noqa: ANN001
+        """Context parallelism: every rank holds a zigzag slice of each sequence.  An all-to-all swaps
+        the sequence split for a head split (rank j gets every token of head group j), the recurrence
+        runs on whole sequences, and a second all-to-all returns the outputs to the token owners."""
+        from axrl_b200.parallel.context_parallel import heads_to_seq, seq_to_heads
+
+        cp = self.cp
+        P, j, L = cp.size, cp.rank, mixed.shape[0]
+        if self.nk % P:
+            raise ValueError("linear-attention key heads must split evenly over context-parallel ranks")
+        nkg, nvg = self.nk // P, self.nv // P
+        q, k, v = torch.split(mixed.float(), [self.key_dim, self.key_dim, self.value_dim], -1)
+        groups = torch.cat([q.reshape(L, P, -1), k.reshape(L, P, -1), v.reshape(L, P, -1), b.reshape(L, P, nvg),
+                            a.reshape(L, P, nvg)], -1)  # (L, P, channels of one head group)
+        xg = seq_to_heads(groups.float(), cp)  # (P*L, .) rank-major stream, head group j
+        perm = layout.perm.to(xg.device)
+        xs = xg.index_select(0, perm)  # sequence order
+        kd, vd = nkg * self.dk, nvg * self.dv
+        m_g, b_g, a_g = torch.split(xs, [2 * kd + vd, nvg, nvg], -1)
+        wq, wk, wv = torch.split(self.conv_weight, [self.key_dim, self.key_dim, self.value_dim], 0)
+        w_g = torch.cat([wq.reshape(P, kd, -1)[j], wk.reshape(P, kd, -1)[j], wv.reshape(P, vd, -1)[j]], 0)
+        T = xs.shape[0]
+        starts = torch.zeros(T, dtype=torch.long, device=xs.device)
+        for s0, s1 in layout.segs:
+            starts[s0:s1] = torch.arange(s1 - s0, device=xs.device)
+        conv = causal_conv(m_g, w_g.float(), starts)
+        sl = slice(j * nvg, (j + 1) * nvg)
+        qh, kh, vh, g, beta = self._heads(conv, b_g, a_g, (nkg, nvg, self.A_log[sl], self.dt_bias[sl]))
+        o = torch.zeros(T, nvg, self.dv, dtype=torch.float32, device=xs.device)
+        for s0, s1 in layout.segs:
+            o[s0:s1] = gated_delta_chunked(qh[s0:s1], kh[s0:s1], vh[s0:s1], g[s0:s1], beta[s0:s1])[0]
+        o_stream = torch.empty_like(o).index_copy(0, perm, o)  # back to the rank-major stream
+        return heads_to_seq(o_stream.reshape(T, vd), cp).reshape(L, self.nv, self.dv)
 
     def _out(self, o: torch.Tensor, z: torch.Tensor, dtype: torch.dtype, tp=None) -> torch.Tensor:  # noqa: ANN001
         T = o.shape[0]
@@ -189,6 +225,12 @@ class GatedDeltaNet(nn.Module):
 
             x = gather_from_sp(x, tp)
         T = x.shape[0]
+        layout = getattr(spec, "seq_layout", None)
+        if self.cp is not None and getattr(self.cp, "enabled", False):
+            if layout is None or states is not None:
+                raise ValueError("Gated DeltaNet under context parallelism needs the CP packing's sequence layout")
+            mixed, z, b, a = self._project(x)
+            return self._out(self._forward_cp(mixed, b, a, layout), z, x.dtype, tp)
         segs = _segments(spec, T)
         starts = torch.zeros(T, dtype=torch.long, device=x.device)
         for s0, s1 in segs:

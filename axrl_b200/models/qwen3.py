@@ -312,8 +312,6 @@ class Qwen3Model(nn.Module):
         self.grad_ready_hook = None  # set by an optimizer that reduces gradients during backward
         for layer in self.layers:
             layer.self_attn.cp = cp
-            if cp is not None and getattr(cp, "enabled", False) and cfg.layer_is_linear(layer.layer_idx):
-                raise NotImplementedError("Gated DeltaNet layers with context parallelism are not built")
         if tp_size > 1:
             for name, p in self.named_parameters():
                 if (p.dim() < 2 and not name.endswith(("dt_bias", "A_log"))) or ".mlp.router" in name or ".mlp.experts" in name \

@@ -21,6 +21,7 @@ the device with one H2D each.
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import Any
 
 import numpy as np
 import torch
@@ -43,6 +44,9 @@ class AttnSpec:
     fwd_tiles: torch.Tensor | None = None
     bwd_tiles: torch.Tensor | None = None
     bwd_tiles_tc: torch.Tensor | None = None  # 128-key tiles of the tcgen05 backward
+    # host-side token layout for sequence mixers that need whole sequences (Gated DeltaNet under
+    # context parallelism: see ``parallel.context_parallel.CPSeqLayout``); None = flat packing
+    seq_layout: Any = None
 
     def to(self, device, non_blocking: bool = True) -> "AttnSpec":  # noqa: ANN001
         """Move every table to ``device`` in ONE host->device copy (pinned staging)."""
@@ -55,7 +59,7 @@ class AttnSpec:
             n = p.numel()
             out.append(flat[off:off + n].view(p.shape))
             off += n
-        return AttnSpec(*out[:4], self.total_q, self.total_k, self.max_q_len, self.max_k_len, out[4], out[5], out[6])
+        return AttnSpec(*out[:4], self.total_q, self.total_k, self.max_q_len, self.max_k_len, out[4], out[5], out[6], self.seq_layout)
 
     def triples(self) -> list[tuple[int, int, int, int, int]]:
         out = []

@@ -73,6 +73,66 @@ def gather_kv(x: torch.Tensor, cp: CPContext) -> torch.Tensor:
     return _GatherKV.apply(x.contiguous(), cp.comm) if cp.enabled else x
 
 
+@dataclass
+class CPSeqLayout:
+    """Where every token of the rank-major ``cp*L`` stream sits in its sequence.
+
+    ``perm[i]`` is the stream index of the i-th token in sequence order (rows one after the other,
+    each row's 2*cp chunks in order, padding at the row's end); ``segs`` are the rows' (start, end)
+    in that order.  Sequence mixers that need whole sequences (Gated DeltaNet) use it."""
+
+    perm: torch.Tensor  # (cp*L,) int64
+    segs: list[tuple[int, int]]
+
+
+def _a2a(x: torch.Tensor, group: Any) -> torch.Tensor:
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    dist.all_to_all_single(out, x, group=group)
+    return out
+
+
+class _SeqToHeads(torch.autograd.Function):
+    """(L, P, C) local rows x head groups -> (P*L, C): head group ``rank`` of every rank's rows,
+    rank-major (an all-to-all; Ulysses-style exchange of sequence shards for head shards)."""
+
+    @staticmethod
+    def forward(ctx, x, group):  # noqa: ANN001, ANN205
+        ctx.group = group
+        L, P, C = x.shape
+        return _a2a(x.transpose(0, 1), group).reshape(P * L, C)
+
+    @staticmethod
+    def backward(ctx, g):  # noqa: ANN001, ANN205
+        PL, C = g.shape
+        P = dist.get_world_size(ctx.group)
+        return _a2a(g.reshape(P, PL // P, C), ctx.group).transpose(0, 1), None
+
+
+class _HeadsToSeq(torch.autograd.Function):
+    """Inverse of :class:`_SeqToHeads`: (P*L, C) rows of this rank's head group -> (L, P, C)."""
+
+    @staticmethod
+    def forward(ctx, x, group):  # noqa: ANN001, ANN205
+        ctx.group = group
+        PL, C = x.shape
+        P = dist.get_world_size(group)
+        return _a2a(x.reshape(P, PL // P, C), group).transpose(0, 1)
+
+    @staticmethod
+    def backward(ctx, g):  # noqa: ANN001, ANN205
+        L, P, C = g.shape
+        return _a2a(g.transpose(0, 1), ctx.group).reshape(P * L, C), None
+
+
+def seq_to_heads(x: torch.Tensor, cp: CPContext) -> torch.Tensor:
+    return _SeqToHeads.apply(x, cp.group)
+
+
+def heads_to_seq(x: torch.Tensor, cp: CPContext) -> torch.Tensor:
+    return _HeadsToSeq.apply(x, cp.group)
+
+
 def _row_triples(info, n: int) -> list[tuple[int, int, int, int, int]]:  # noqa: ANN001
     if info is None:
         return [(0, n, 0, n, 1)]
@@ -129,6 +189,15 @@ def pack_rows_cp(batch, rows: list[int], cp: CPContext):  # noqa: ANN001, ANN201
     def owner(k: int) -> tuple[int, int]:  # chunk -> (rank, 0 first / 1 second chunk of that rank)
         return (k, 0) if k < P else (nch - 1 - k, 1)
 
+    perm = []
+    for (_, c, rb) in plan:
+        for k in range(nch):
+            rk, half = owner(k)
+            perm.append(torch.arange(rk * L + rb + half * c, rk * L + rb + (half + 1) * c))
+    segs, s0 = [], 0
+    for (_, c, _) in plan:
+        segs.append((s0, s0 + nch * c))
+        s0 += nch * c
     triples = []
     for tri, c, rb in plan:
         def local_q(k: int) -> int | None:  # local stream offset of chunk k (None: not held here)
@@ -161,6 +230,7 @@ def pack_rows_cp(batch, rows: list[int], cp: CPContext):  # noqa: ANN001, ANN201
                         continue
                     triples.append((lq + qa - kq * c, lq + qb - kq * c, glob_k(kk) + ka - kk * c, glob_k(kk) + kb - kk * c, typ))
     spec = spec_from_triples(triples, L, L * P)
+    spec.seq_layout = CPSeqLayout(torch.cat(perm) if perm else torch.zeros(0, dtype=torch.int64), segs)
     return PackedMicroBatch(rows=list(rows), row_len=row_len, row_off=[0] * len(rows), ids=torch.cat(ids), pos=torch.cat(pos).int(),
                             labels=torch.cat(lab), loss_mask=torch.cat(lm), token_row=torch.cat(trow), spec=spec,
                             fields={k: torch.cat(v) for k, v in fields.items()},

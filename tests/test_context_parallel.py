@@ -5,6 +5,7 @@ against the CP=1 engine on the same batch, flat sequences plus a prefix-tree mer
 import os
 import socket
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -16,7 +17,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _batch():
+def _batch(tree: bool = True):
     from axrl_b200.data.prefix_tree import merge_trajectory_samples
     from axrl_b200.data.sample import Sample, SampleBatch
 
@@ -27,6 +28,8 @@ def _batch():
         r = torch.randint(1, 200, (9 + 5 * i,), generator=g).tolist()
         samples.append(Sample.from_tokens(p, r, advantage=float(i % 3) - 1.0, rollout_logprobs=(-torch.rand(len(r), generator=g)).tolist(),
                                           trajectory_id=i))
+    if not tree:
+        return SampleBatch.from_samples(samples)
     prompt = torch.randint(1, 200, (11,), generator=g).tolist()
     group = []
     for j in range(3):
@@ -37,20 +40,24 @@ def _batch():
     return SampleBatch.from_samples(samples)
 
 
-def _engine(par=None):
+def _engine(par=None, hybrid: bool = False):
     from axrl_b200.configs import MegatronWorkerConfig
     from axrl_b200.models.qwen3 import Qwen3Config
     from axrl_b200.train.engine import TrainEngine
 
+    kw = {}
+    if hybrid:  # a Gated DeltaNet layer (heads exchanged for tokens by all-to-all) + gated attention
+        kw = dict(layer_types=["linear_attention", "full_attention"], linear_num_key_heads=2, linear_num_value_heads=4,
+                  linear_key_head_dim=16, linear_value_head_dim=8, attn_output_gate=True, partial_rotary_factor=0.5)
     cfg = Qwen3Config(vocab_size=256, hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
-                      num_key_value_heads=2, head_dim=16)
+                      num_key_value_heads=2, head_dim=16, **kw)
     wc = MegatronWorkerConfig(max_tokens_per_micro_batch=48, seed=3)
     wc.lr_scheduler.lr_warmup_steps = 0
     wc.lr_scheduler.max_lr = 1e-3
     return TrainEngine(wc, cfg, "cpu", par=par)
 
 
-def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+def _worker(rank: int, world: int, port: int, q, hybrid: bool = False) -> None:  # noqa: ANN001
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -58,9 +65,9 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
         from axrl_b200.train.engine import ParallelCtx
         from axrl_b200.trainer.grpo_trainer import GrpoTrainer
 
-        ref = _engine()
-        eng = _engine(ParallelCtx(cp_group=dist.group.WORLD, cp_size=world))
-        b = _batch()
+        ref = _engine(hybrid=hybrid)
+        eng = _engine(ParallelCtx(cp_group=dist.group.WORLD, cp_size=world), hybrid=hybrid)
+        b = _batch(tree=not hybrid)
         lp_ref = ref.compute_logprobs(b)
         lp = eng.compute_logprobs(b)
         torch.testing.assert_close(lp, lp_ref, atol=1e-5, rtol=1e-5)
@@ -70,8 +77,11 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
         m_ref = ref.train_step(b, trainer)
         m = eng.train_step(b, trainer)
         assert abs(m["grad_norm"] - m_ref["grad_norm"]) < 1e-4 * max(1.0, m_ref["grad_norm"]), (m["grad_norm"], m_ref["grad_norm"])
+        # Adam normalises each element's gradient, so near-zero gradients summed in another order
+        # (the GDN all-to-all path) can move an element by a fraction of one lr-sized step
+        atol = 2e-5 if hybrid else 1e-6
         for (n, p), pr in zip(eng.model.named_parameters(), ref.model.parameters()):
-            torch.testing.assert_close(p, pr, atol=1e-6, rtol=1e-5, msg=lambda msg, n=n: f"{n}: {msg}")
+            torch.testing.assert_close(p, pr, atol=atol, rtol=1e-5, msg=lambda msg, n=n: f"{n}: {msg}")
         q.put((rank, "ok"))
     except Exception:  # noqa: BLE001
         import traceback
@@ -81,11 +91,12 @@ def _worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
         dist.destroy_process_group()
 
 
-def test_cp2_matches_cp1():
+@pytest.mark.parametrize("hybrid", [False, True])
+def test_cp2_matches_cp1(hybrid):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, hybrid)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
