@@ -73,7 +73,8 @@ class PipelineController:
         max_ctx = c.train_sampling_config.max_total_tokens
         kv_tokens = int(rw.max_running_requests * (max_ctx + 128))
         self.engine = RolloutEngine(self.train.model, max_batch=rw.max_running_requests, kv_tokens=kv_tokens, page_size=rw.kv_page_size,
-                                    max_context=max_ctx, use_cuda_graph=rw.use_cuda_graph, seed=c.megatron_worker.seed)
+                                    max_context=max_ctx, use_cuda_graph=rw.use_cuda_graph, seed=c.megatron_worker.seed,
+                                    dp_attention=_ep_active(self.train.model))
         self.worker = RolloutWorker(self.engine, c.train_sampling_config, continue_after_abort=rw.continue_generation_after_abort)
         self.router = InferenceRouter([self.worker], max_imbalance=rw.max_imbalance)
         self.rollout_queue: AsyncTaskQueue = AsyncTaskQueue(max_running=c.controller.max_running_requests, name="rollout")
@@ -492,3 +493,10 @@ class PipelineController:
                                    mcore=MCoreRunMetrics(end_to_end_time_sec=t_mcore), mismatch_metrics=mm)
         save_zst(result, result_path)
         return {"result_path": str(result_path), "mismatch": mm}
+
+
+def _ep_active(model) -> bool:  # noqa: ANN001
+    """An expert-parallel model: every rank runs its own requests and the engines step in lockstep
+    (data-parallel attention), since each MoE layer's dispatch is collective over the EP group."""
+    ep = getattr(model, "ep", None)
+    return bool(ep is not None and getattr(ep, "active", False))

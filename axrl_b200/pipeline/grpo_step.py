@@ -91,7 +91,8 @@ class SyntheticGRPO:
         self.rollout = RolloutEngine(rollout_model, max_batch=sc.max_batch or n_seq, kv_tokens=kv_tokens, page_size=64,
                                      max_context=max_ctx, max_prefill_tokens=max(16384, sc.prompt_len), seed=sc.seed,
                                      use_cuda_graph=sc.use_cuda_graph, eos_token_id=sc.eos_token_id,
-                                     kv_memory_saver=cuda and sc.kv_memory_saver)
+                                     kv_memory_saver=cuda and sc.kv_memory_saver,
+                                     dp_attention=_ep_active(rollout_model))
         if cuda and self.train.optim is not None:
             self.train.release_grads_after_step = True  # the grad buffer is not needed during rollout
         self.weight_version = 0
@@ -198,3 +199,10 @@ class SyntheticGRPO:
             self.rollout.update_weights_from_model(self.train.model)
         self.rollout.reset_prefix_cache()
         self.weight_version += 1
+
+
+def _ep_active(model) -> bool:  # noqa: ANN001
+    """An expert-parallel model: every rank runs its own requests and the engines step in lockstep
+    (data-parallel attention), since each MoE layer's dispatch is collective over the EP group."""
+    ep = getattr(model, "ep", None)
+    return bool(ep is not None and getattr(ep, "active", False))

@@ -116,8 +116,18 @@ class RolloutEngine:
     def __init__(self, model: Qwen3Model, *, max_batch: int = 256, kv_tokens: int = 1 << 16, page_size: int = 64,
                  max_context: int = 16384, max_prefill_tokens: int = 16384, use_cuda_graph: bool = True, seed: int = 0,
                  eos_token_id: int | None = None, burst: int = 16, kv_memory_saver: bool = False, weight_format: str = "bf16",
-                 tp_group: Any = None, embed_full: torch.Tensor | None = None, tokenizer: Any = None) -> None:
+                 tp_group: Any = None, embed_full: torch.Tensor | None = None, tokenizer: Any = None,
+                 dp_attention: bool = False) -> None:
         self.model = model
+        # data-parallel attention over an expert-parallel model: every EP rank serves its own requests
+        # (own KV cache, own batch) and the ranks step in lockstep so each MoE layer's dispatch /
+        # combine meets the same layer on every rank (a rank without work runs empty forwards)
+        self.dp_attention = dp_attention
+        if dp_attention:
+            ep = getattr(model, "ep", None)
+            if ep is None or not getattr(ep, "active", False):
+                raise ValueError("dp_attention needs an expert-parallel MoE model")
+            use_cuda_graph = False
         self.tokenizer = tokenizer  # token strings for grammar-constrained requests
         self._grammars: dict[tuple, Any] = {}
         self._token_strings: list[str] | None = None
@@ -339,13 +349,62 @@ class RolloutEngine:
         self.waiting.extend(reqs)
 
     def generate(self, reqs: Sequence[GenRequest]) -> list[GenResult]:
-        """Run ``reqs`` to completion (continuous batching); results in request order."""
+        """Run ``reqs`` to completion (continuous batching); results in request order.  With
+        ``dp_attention`` this is collective over the EP group: every rank calls it (with its own
+        requests, possibly none) and all return once no rank has work left."""
         self.add_requests(reqs)
         done: dict[str, GenResult] = {}
-        while self.waiting or self.running:
+        while self._any_work():
             for r in self.step():
                 done[r.rid] = r
         return [done[r.rid] for r in reqs]
+
+    # ------------------------------------------------------------------ data-parallel attention
+    def _ep_max(self, vals: list[int]) -> list[int]:
+        """Element-wise max of small integers over every rank the MoE layers exchange rows with
+        (the EP group, then the expert-TP group: together the whole EP x ETP grid)."""
+        ep = self.model.ep
+        t = None
+        for g, n in ((ep.group, ep.size), (ep.etp_group, ep.etp_size)):
+            if n <= 1:
+                continue
+            dev = self.device if torch.distributed.get_backend(g) == "nccl" else torch.device("cpu")
+            t = torch.tensor(vals, dtype=torch.int64, device=dev) if t is None else t.to(dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=g)
+        return vals if t is None else t.tolist()
+
+    def _any_work(self) -> bool:
+        local = bool(self.waiting or self.running)
+        return bool(self._ep_max([int(local)])[0]) if self.dp_attention else local
+
+    def _empty_forward(self) -> None:
+        """The expert-parallel collectives of one forward with no tokens (a rank without work keeps
+        the MoE layers of the other ranks' forward company)."""
+        H = self.cfg.hidden_size
+        x = torch.zeros(0, H, dtype=self.model.embed_tokens.dtype if self.model.embed_tokens is not None else torch.bfloat16,
+                        device=self.device)
+        with torch.no_grad():
+            for li, layer in enumerate(self.model.layers):
+                if hasattr(layer.mlp, "router"):
+                    from axrl_b200.models.moe import MoEContext
+
+                    layer.mlp(x, MoEContext(), li)
+
+    def _step_dp(self) -> list[GenResult]:
+        groups = self._plan_admission()
+        finished: list[GenResult] = []
+        if self._ep_max([int(bool(groups))])[0]:
+            if groups:
+                finished += self._prefill(groups)
+            else:
+                self._empty_forward()
+        k = self._burst_len() if self.running else 0
+        k_max = self._ep_max([k])[0]
+        if k:
+            finished += self._decode_burst(k)
+        for _ in range(k_max - k):
+            self._empty_forward()
+        return finished
 
     def abort_all(self) -> list[GenResult]:
         """Stop every request now (partial rollout): running ones return their partial output."""
@@ -355,6 +414,8 @@ class RolloutEngine:
         return out
 
     def step(self) -> list[GenResult]:
+        if self.dp_attention:
+            return self._step_dp()
         if not self.is_cuda:
             finished = self._admit()
             return finished + (self._decode_burst() if self.running else [])
@@ -375,6 +436,11 @@ class RolloutEngine:
         return -(-n_tokens // self.P)
 
     def _admit(self) -> list[GenResult]:
+        groups = self._plan_admission()
+        return self._prefill(groups) if groups else []
+
+    def _plan_admission(self) -> list[list[GenRequest]]:
+        """Requests admitted this step, grouped by identical prompt (removed from ``waiting``)."""
         if not self.waiting or len(self.running) >= self.max_batch:
             return []
         budget_seqs = self.max_batch - len(self.running)
@@ -413,7 +479,7 @@ class RolloutEngine:
             return []
         admitted = {id(r) for key in order for r in groups[key]}
         self.waiting = [r for r in self.waiting if id(r) not in admitted]
-        return self._prefill([groups[k] for k in order])
+        return [groups[k] for k in order]
 
     def _prefill(self, groups: list[list[GenRequest]]) -> list[GenResult]:
         t0 = time.perf_counter()
@@ -693,13 +759,17 @@ class RolloutEngine:
         elif self.bias is not None:
             self.bias[:bucket].zero_()
 
-    def _decode_burst(self) -> list[GenResult]:
-        t0 = time.perf_counter()
+    def _burst_len(self) -> int:
         # steps this burst: no row needs more than its remaining tokens
         remaining = max(s.end_total - len(s.tokens) for s in self.running)
         k = max(1, min(self.burst, remaining))
         if any(s.grammar is not None for s in self.running):
             k = 1  # a grammar's allowed set depends on the previous token: one step per burst
+        return k
+
+    def _decode_burst(self, k: int | None = None) -> list[GenResult]:
+        t0 = time.perf_counter()
+        k = self._burst_len() if k is None else k
         # pages for every position this burst may write; preempt the newest sequences when short
         while True:
             short = sum(max(0, self._pages_needed(min(len(s.tokens) + k, s.end_total)) - len(s.pages)) for s in self.running)

@@ -66,3 +66,61 @@ def test_ep2_rollout_matches_single_engine():
         p.join(timeout=60)
     for r, msg in res:
         assert msg == "ok", f"rank {r}:\n{msg}"
+
+
+def _dp_reqs(rank: int):
+    from axrl_b200.rollout.engine import GenRequest
+
+    g = torch.Generator().manual_seed(11 + rank)
+    lens, news = ((7, 12, 9), (10, 4, 14)) if rank == 0 else ((5, 16), (3, 9))  # ranks finish at different steps
+    return [GenRequest(rid=f"d{rank}_{i}", prompt=torch.randint(1, 1024, (n,), generator=g).tolist(), max_new_tokens=m,
+                       temperature=1.0, seed_stream=100 * rank + i) for i, (n, m) in enumerate(zip(lens, news))]
+
+
+def _dp_worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from axrl_b200.models.qwen3 import Qwen3Model, resolve_preset
+        from axrl_b200.parallel.expert import EPContext, load_ep_shards_from_full
+        from axrl_b200.rollout.engine import RolloutEngine
+
+        cfg = resolve_preset("tiny-moe")
+        full = Qwen3Model(cfg)
+        full.init_weights(2)
+        ref = RolloutEngine(full, max_batch=4, kv_tokens=2048, max_context=128, use_cuda_graph=False, seed=4, burst=4).generate(_dp_reqs(rank))
+        ep = EPContext.from_group(dist.group.WORLD)
+        model = Qwen3Model(cfg, ep=ep)
+        load_ep_shards_from_full(model, {k: v.detach() for k, v in full.named_parameters()}, ep)
+        eng = RolloutEngine(model, max_batch=4, kv_tokens=2048, max_context=128, seed=4, burst=4, dp_attention=True)
+        got = eng.generate(_dp_reqs(rank))
+        for a, b in zip(got, ref):
+            assert a.output_ids == b.output_ids, (a.output_ids, b.output_ids)
+            torch.testing.assert_close(torch.tensor(a.output_logprobs), torch.tensor(b.output_logprobs), atol=1e-4, rtol=1e-4)
+        # a rank with no requests still joins the other ranks' forwards
+        extra = _dp_reqs(0)[:1] if rank == 0 else []
+        got2 = eng.generate(extra)
+        assert len(got2) == len(extra) and all(len(r.output_ids) == 10 for r in got2)
+        q.put((rank, "ok"))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep2_dp_attention_rollout_matches_single_engines():
+    """Data-parallel attention: each EP rank serves different requests (attention and KV cache per
+    rank, experts shared through the EP dispatch); results equal one engine per request set."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for r, msg in res:
+        assert msg == "ok", f"rank {r}:\n{msg}"
