@@ -45,6 +45,9 @@ def _args():
     ap.add_argument("--no-ref", action="store_true", help="skip the reference-policy logprob pass")
     ap.add_argument("--kv-gb", type=float, default=None, help="KV pool size (default: free memory minus --headroom-gb)")
     ap.add_argument("--headroom-gb", type=int, default=24)
+    ap.add_argument("--ep", type=int, default=None,
+                    help="expert parallelism for MoE models (default: every GPU, dense parts data-parallel over the same ranks)")
+    ap.add_argument("--ep-backend", choices=["p2p", "torch"], default="p2p", help="EP dispatch / combine: NVLink kernels or NCCL all-to-all")
     ap.add_argument("--verbose", action="store_true")
     return ap.parse_args()
 
@@ -138,7 +141,11 @@ def main() -> None:
     mcfg = resolve_preset(a.model)
     wc = MegatronWorkerConfig(recompute_granularity="full", max_tokens_per_micro_batch=a.mb_tokens, seed=1234)
     grpo = GrpoTrainerConfig(loss_type="grpo", mismatch_token_clip_max=2.0)
-    par = ParallelCtx(dp_group=dist.group.WORLD if world > 1 else None, dp_size=world, dp_rank=rank)
+    ep = (a.ep or world) if mcfg.is_moe else 1
+    if ep not in (1, world):
+        raise SystemExit("--ep must be 1 or the number of GPUs")
+    par = ParallelCtx(dp_group=dist.group.WORLD if world > 1 else None, dp_size=world, dp_rank=rank,
+                      ep_group=dist.group.WORLD if ep > 1 else None, ep_size=ep, ep_backend=a.ep_backend)
     train = TrainEngine(wc, mcfg, dev, par=par)
     train.optim.release_grads()  # gradients live only inside the train phase
     torch.cuda.empty_cache()  # the caching allocator still holds the released blocks
@@ -219,7 +226,7 @@ def main() -> None:
                        "global_batch": a.prompts_per_gpu * a.group * world, "prompts": a.prompts_per_gpu * world, "group_size": a.group,
                        "seq_len": a.prompt_len + a.max_len, "prompt_len": a.prompt_len,
                        "response_len": f"lognormal(median {a.median:g}, sigma 1) clipped [16,{a.max_len}]",
-                       "micro_batch_tokens": a.mb_tokens, "parallelism": f"dp{world}", "colocated": True,
+                       "micro_batch_tokens": a.mb_tokens, "parallelism": f"dp{world}" + (f"ep{ep}" if ep > 1 else ""), "colocated": True,
                        "ref_logprobs": not a.no_ref, "kv_pool_gb": round(kv_gb, 1), "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
             "sync_s": round(sum(m["sync_s"] for m in step_metrics) / len(step_metrics), 4),
             "step_breakdown_s": {k: round(last[k], 2) for k in ("rollout_s", "logprob_s", "train_s", "sync_s", "pack_s") if k in last},
