@@ -96,6 +96,73 @@ def gated_delta_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: to
     return o, S
 
 
+def gated_delta_chunked_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                               segs: list[tuple[int, int]], chunk: int = 64) -> tuple[torch.Tensor, torch.Tensor]:
+    """:func:`gated_delta_chunked` over every packed sequence at once.
+
+    q, k (T, H, dk), v (T, H, dv), g, beta (T, H) fp32; ``segs`` the sequences' (start, end).  The
+    within-chunk algebra (decay masks, the triangular solve, W, U, Q K^T) runs batched over all
+    chunks of all sequences; the state recurrence then advances every sequence that still has a
+    chunk left, one chunk position per step (as many steps as the longest sequence has chunks).
+    A sequence's last chunk is padded with g = 0, beta = 0, k = v = 0, which leaves its state as it
+    was.  Returns o (T, H, dv) and the final states (len(segs), H, dk, dv)."""
+    T, H, dk = k.shape
+    dv = v.shape[-1]
+    dev = q.device
+    C = chunk
+    rows, steps = [], []  # token index of each chunk slot (-1 = padding); per sequence its chunk ids
+    for s0, s1 in segs:
+        ids = []
+        for c0 in range(s0, s1, C):
+            r = list(range(c0, min(c0 + C, s1)))
+            ids.append(len(rows))
+            rows.append(r + [-1] * (C - len(r)))
+        steps.append(ids)
+    B = len(segs)
+    if not rows:
+        return q.new_zeros(T, H, dv), q.new_zeros(B, H, dk, dv)
+    idx = torch.tensor(rows, dtype=torch.long, device=dev)  # (M, C)
+    valid = idx >= 0
+    src = idx.clamp(min=0)
+    vm = valid[..., None].float()
+
+    def take(x: torch.Tensor) -> torch.Tensor:  # (T, H, d) -> (M, H, C, d), zero on padding
+        return (x[src] * vm[..., None]).permute(0, 2, 1, 3)
+
+    Q, Kc, Vc = take(q), take(k), take(v)
+    Gs = (g[src] * vm).permute(0, 2, 1).cumsum(-1)  # (M, H, C)
+    Bt = (beta[src] * vm).permute(0, 2, 1)
+    diff = Gs[..., :, None] - Gs[..., None, :]
+    lower = torch.tril(torch.ones(C, C, dtype=torch.bool, device=dev))
+    strict = torch.tril(torch.ones(C, C, dtype=torch.bool, device=dev), -1)
+    decay = torch.where(lower, diff, torch.full_like(diff, -torch.inf)).exp()
+    kk = Kc @ Kc.transpose(-1, -2)
+    A = torch.where(strict, -(Bt[..., :, None] * decay * kk), torch.zeros_like(kk))
+    eye = torch.eye(C, dtype=torch.float32, device=dev)
+    Tm = torch.linalg.solve_triangular(eye - A, eye.expand_as(A).contiguous(), upper=False, unitriangular=True)
+    eG = Gs.exp()
+    W = Tm @ (Kc * (Bt * eG)[..., None])
+    U = Tm @ (Vc * Bt[..., None])
+    qk = (Q @ Kc.transpose(-1, -2)) * decay
+    Kt = (Kc * (Gs[..., -1:] - Gs).exp()[..., None]).transpose(-1, -2)  # (K o e^{G_C - G})^T
+    S = q.new_zeros(B, H, dk, dv)
+    outs, out_ids = [], []
+    for c in range(max(len(s) for s in steps)):
+        act = [i for i, s in enumerate(steps) if len(s) > c]
+        a = torch.tensor(act, dtype=torch.long, device=dev)
+        m = torch.tensor([steps[i][c] for i in act], dtype=torch.long, device=dev)
+        Sa = S.index_select(0, a)
+        D = U.index_select(0, m) - W.index_select(0, m) @ Sa
+        outs.append((Q.index_select(0, m) * eG.index_select(0, m)[..., None]) @ Sa + qk.index_select(0, m) @ D)
+        out_ids.append(m)
+        Sn = eG.index_select(0, m)[:, :, -1, None, None] * Sa + Kt.index_select(0, m) @ D
+        S = S.index_copy(0, a, Sn)
+    O = torch.cat(outs).new_zeros(idx.shape[0], H, C, dv).index_copy(0, torch.cat(out_ids), torch.cat(outs))
+    flat = O.permute(0, 2, 1, 3).reshape(-1, H, dv)[valid.reshape(-1)]
+    o = q.new_zeros(T, H, dv).index_copy(0, idx.reshape(-1)[valid.reshape(-1)], flat)
+    return o, S
+
+
 def gated_delta_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
                      S: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """One token for a batch: q, k (B, H, dk), v (B, H, dv), g, beta (B, H), S (B, H, dk, dv) fp32."""
@@ -199,9 +266,7 @@ class GatedDeltaNet(nn.Module):
         conv = causal_conv(m_g, w_g.float(), starts)
         sl = slice(j * nvg, (j + 1) * nvg)
         qh, kh, vh, g, beta = self._heads(conv, b_g, a_g, (nkg, nvg, self.A_log[sl], self.dt_bias[sl]))
-        o = torch.zeros(T, nvg, self.dv, dtype=torch.float32, device=xs.device)
-        for s0, s1 in layout.segs:
-            o[s0:s1] = gated_delta_chunked(qh[s0:s1], kh[s0:s1], vh[s0:s1], g[s0:s1], beta[s0:s1])[0]
+        o = gated_delta_chunked_varlen(qh, kh, vh, g, beta, layout.segs)[0]
         o_stream = torch.empty_like(o).index_copy(0, perm, o)  # back to the rank-major stream
         return heads_to_seq(o_stream.reshape(T, vd), cp).reshape(L, self.nv, self.dv)
 
@@ -238,15 +303,13 @@ class GatedDeltaNet(nn.Module):
         mixed, z, b, a = self._project(x)
         conv = causal_conv(mixed.float(), self.conv_weight.float(), starts)
         q, k, v, g, beta = self._heads(conv, b, a)
-        o = torch.zeros(T, self.nv, self.dv, dtype=torch.float32, device=x.device)
-        for s0, s1 in segs:
-            o_s, S = gated_delta_chunked(q[s0:s1], k[s0:s1], v[s0:s1], g[s0:s1], beta[s0:s1])
-            o[s0:s1] = o_s
-            if states is not None:
+        o, S_all = gated_delta_chunked_varlen(q, k, v, g, beta, segs)
+        if states is not None:
+            for i, (s0, s1) in enumerate(segs):
                 tailx = mixed[max(s0, s1 - (self.kernel - 1)):s1].float()
                 cs = torch.zeros(self.kernel - 1, self.conv_dim, dtype=torch.float32, device=x.device)
                 cs[cs.shape[0] - tailx.shape[0]:] = tailx
-                states.append((cs, S))
+                states.append((cs, S_all[i]))
         return self._out(o, z, x.dtype, tp)
 
     # ---- decode: one token per row with carried states

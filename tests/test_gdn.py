@@ -6,7 +6,7 @@ decode) against the trainer's packed forward."""
 
 import torch
 
-from axrl_b200.models.gdn import gated_delta_chunked, gated_delta_recurrent
+from axrl_b200.models.gdn import gated_delta_chunked, gated_delta_chunked_varlen, gated_delta_recurrent
 
 
 def _cfg():
@@ -27,6 +27,32 @@ def test_chunked_delta_rule_matches_recurrence():
         o2, s2 = gated_delta_recurrent(q, k, v, g, beta, S0)
         torch.testing.assert_close(o1, o2, atol=1e-5, rtol=1e-4)
         torch.testing.assert_close(s1, s2, atol=1e-5, rtol=1e-4)
+
+
+def test_varlen_chunked_matches_per_sequence():
+    """All packed sequences at once (chunks batched, padded tails) = one sequence at a time, values and
+    gradients."""
+    torch.manual_seed(1)
+    lens, H, dk, dv, C = [5, 16, 70, 33, 1], 2, 8, 4, 16
+    T = sum(lens)
+    segs, o = [], 0
+    for n in lens:
+        segs.append((o, o + n))
+        o += n
+    q = (torch.nn.functional.normalize(torch.randn(T, H, dk), dim=-1) / dk ** 0.5).requires_grad_(True)
+    k = torch.nn.functional.normalize(torch.randn(T, H, dk), dim=-1).requires_grad_(True)
+    v = torch.randn(T, H, dv, requires_grad=True)
+    g, beta = (-torch.rand(T, H)).requires_grad_(True), torch.rand(T, H, requires_grad=True)
+    o1, S1 = gated_delta_chunked_varlen(q, k, v, g, beta, segs, chunk=C)
+    ref = [gated_delta_chunked(q[a:b], k[a:b], v[a:b], g[a:b], beta[a:b], chunk=C) for a, b in segs]
+    o2, S2 = torch.cat([r[0] for r in ref]), torch.stack([r[1] for r in ref])
+    torch.testing.assert_close(o1, o2, atol=1e-5, rtol=1e-4)
+    torch.testing.assert_close(S1, S2, atol=1e-5, rtol=1e-4)
+    w = torch.randn_like(o1)
+    g1 = torch.autograd.grad((o1 * w).sum() + S1.sum(), (q, k, v, g, beta))
+    g2 = torch.autograd.grad((o2 * w).sum() + S2.sum(), (q, k, v, g, beta))
+    for a, b in zip(g1, g2):
+        torch.testing.assert_close(a, b, atol=1e-4, rtol=1e-4)
 
 
 def test_packed_sequences_stay_independent():
