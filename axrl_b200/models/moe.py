@@ -146,7 +146,9 @@ class MoEBlock(nn.Module):
             return None
         lin = linear or ops.linear
         y = lin(ops.swiglu(lin(x, self.shared_gate_up)), self.shared_down)
-        return y * torch.sigmoid(lin(x, self.shared_gate).float()).to(y.dtype)
+        # the (T, 1) gate logit is a matrix-vector product: fp32, outside the tiled GEMM kernels
+        gate = torch.nn.functional.linear(x.float(), self.shared_gate.float())
+        return y * torch.sigmoid(gate).to(y.dtype)
 
     def hf_tensors(self, prefix: str) -> dict[str, torch.Tensor]:
         out = {prefix + "mlp.gate.weight": self.router}

@@ -193,3 +193,51 @@ def test_recompute_reuses_attention_and_matches_plain_backward():
         rel = ((grads[True][k] - g).norm() / (g.norm() + 1e-12)).item()
         assert rel < 1e-2, f"{k}: {rel}"
     assert core.AttnStash.pushing is False
+
+
+def test_qwen35_style_hybrid_on_gpu_matches_fp32_and_rollout():
+    """Gated attention output, zero-centered norms, Gated DeltaNet layers and a shared expert on the GPU
+    path (head dim 128, full rotary: the shapes the GPU kernels cover): bf16 trainer log-probs track
+    the fp32 CPU model, and rollout log-probs track the trainer's recomputation."""
+    from axrl_b200.configs import MegatronWorkerConfig
+    from axrl_b200.data.sample import Sample, SampleBatch
+    from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from axrl_b200.ops.attention_spec import causal_spec_from_cu_seqlens
+    from axrl_b200.rollout.engine import RolloutEngine
+    from axrl_b200.train.engine import TrainEngine
+
+    cfg = Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=4, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=128, num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256,
+                      shared_expert_intermediate_size=256, layer_types=["linear_attention", "full_attention"] * 2,
+                      linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=64, linear_value_head_dim=64,
+                      attn_output_gate=True, zero_centered_norm=True)
+    cpu = Qwen3Model(cfg)
+    cpu.init_weights(4)
+    gpu = Qwen3Model(cfg)
+    gpu.load_state_dict(cpu.state_dict())
+    gpu = gpu.to("cuda", torch.bfloat16)
+    gpu.inv_freq = gpu.inv_freq.float()
+    g = torch.Generator().manual_seed(6)
+    ids = torch.randint(1, 2048, (96,), generator=g)
+    pos = torch.cat([torch.arange(40), torch.arange(56)]).int()
+    spec = causal_spec_from_cu_seqlens([0, 40, 96])
+    labels = torch.roll(ids, -1)
+    with torch.no_grad():
+        lp_ref = cpu.logprobs(cpu(ids, pos, spec), labels)[0]
+        lp = gpu.logprobs(gpu(ids.cuda(), pos.cuda(), spec.to("cuda")), labels.cuda())[0].float().cpu()
+    d = (lp - lp_ref).abs()
+    assert d.mean().item() < 0.03 and d.max().item() < 0.3, (d.mean().item(), d.max().item())
+
+    for p in gpu.parameters():
+        p.requires_grad_(False)
+    eng = RolloutEngine(gpu, max_batch=4, kv_tokens=2048, max_context=256, seed=3)
+    reqs = _reqs(3)
+    res = eng.generate(reqs)
+    samples = [Sample.from_tokens(r.prompt, x.output_ids, rollout_logprobs=x.output_logprobs) for r, x in zip(reqs, res)]
+    batch = SampleBatch.from_samples(samples)
+    tr = TrainEngine(MegatronWorkerConfig(inference_only=True), cfg, "cuda", model=gpu)
+    lp2 = tr.compute_logprobs(batch)
+    mask = batch["loss_mask"]
+    diff = (lp2 - batch["rollout_logprobs"])[mask].abs()
+    assert diff.mean().item() < 0.02 and diff.max().item() < 0.5, (diff.mean().item(), diff.max().item())
+    eng.release_graphs()
