@@ -3,7 +3,6 @@ normalisation, packing, training, partial-rollout pause/resume; plus queue and r
 
 import asyncio
 
-import pytest
 import torch
 
 from axrl_b200.runtime.task_queue import AsyncTaskQueue

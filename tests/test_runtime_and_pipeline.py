@@ -2,7 +2,6 @@
 tiny CPU GRPO plumbing run (2 layers, hidden 256, 4 heads, FFN 768, vocab 1024, fp32)."""
 
 import numpy as np
-import pytest
 import torch
 
 from axrl_b200.rollout.kv import PyBlockManager, make_block_manager
