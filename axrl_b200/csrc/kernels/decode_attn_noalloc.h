@@ -2,10 +2,9 @@
 // device memory.  This interface has no counterpart in the reference project.
 //
 // Who needs it: code that runs where a device allocation is not allowed or not affordable —
-// e.g. a host loop being captured into a CUDA graph in global capture mode (cudaMalloc is illegal
-// during such a capture), a latency-critical serving loop (cudaMalloc/cudaFree synchronise the
-// device), or a host framework / plugin that owns all device memory and hands kernels only the
-// tensors it allocated.  Such callers pass inputs and outputs; the split-KV partial results that the
+// e.g. a latency-critical serving loop (cudaMalloc/cudaFree synchronise the device and can stall
+// every stream), or a host framework / plugin that owns all device memory through its own pool and
+// hands kernels only the tensors it allocated.  Such callers pass inputs and outputs; the split-KV partial results that the
 // regular entry point keeps in a caller-allocated workspace live here in a fixed, file-scope device
 // array instead.
 //

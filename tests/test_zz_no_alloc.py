@@ -1,8 +1,9 @@
 """Allocation-free paged decode attention, called through its exported C symbol.
 
-The entry point serves callers that cannot allocate device memory (for example host code being
-captured into a CUDA graph in global capture mode, or a host framework that owns all device
-memory); it keeps its split-KV partials in a fixed device array inside the library.  This test
+The entry point serves callers that cannot allocate device memory (for example a host framework
+that owns all device memory through its own pool, or a serving loop that must not pay for the
+device-wide synchronisation of cudaMalloc / cudaFree); it keeps its split-KV partials in a fixed
+device array inside the library.  This test
 calls it twice in a row with different inputs and checks each result against the regular entry
 point (which uses a caller-allocated workspace) within the decode-attention test tolerance.
 """
