@@ -128,6 +128,10 @@ class RolloutEngine:
             if ep is None or not getattr(ep, "active", False):
                 raise ValueError("dp_attention needs an expert-parallel MoE model")
             use_cuda_graph = False
+        # lockstep decisions go over a group of their own (gloo, host tensors): an engine thread may
+        # reach them while this rank's main thread still runs training collectives on the model's groups
+        self._lock_group = (torch.distributed.new_group(backend="gloo")
+                            if dp_attention and torch.distributed.is_initialized() and torch.distributed.get_world_size() > 1 else None)
         self.tokenizer = tokenizer  # token strings for grammar-constrained requests
         self._grammars: dict[tuple, Any] = {}
         self._token_strings: list[str] | None = None
@@ -361,17 +365,14 @@ class RolloutEngine:
 
     # ------------------------------------------------------------------ data-parallel attention
     def _ep_max(self, vals: list[int]) -> list[int]:
-        """Element-wise max of small integers over every rank the MoE layers exchange rows with
-        (the EP group, then the expert-TP group: together the whole EP x ETP grid)."""
-        ep = self.model.ep
-        t = None
-        for g, n in ((ep.group, ep.size), (ep.etp_group, ep.etp_size)):
-            if n <= 1:
-                continue
-            dev = self.device if torch.distributed.get_backend(g) == "nccl" else torch.device("cpu")
-            t = torch.tensor(vals, dtype=torch.int64, device=dev) if t is None else t.to(dev)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=g)
-        return vals if t is None else t.tolist()
+        """Element-wise max of small integers over every rank the MoE layers exchange rows with.  The
+        max runs over the whole world (a superset of the EP x ETP grid: ranks of other EP groups only
+        run a few more empty forwards) on the engine's own gloo group."""
+        if self._lock_group is None:
+            return vals
+        t = torch.tensor(vals, dtype=torch.int64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=self._lock_group)
+        return t.tolist()
 
     def _any_work(self) -> bool:
         local = bool(self.waiting or self.running)

@@ -60,7 +60,42 @@ class RolloutWorker:
         self._thread.start()
 
     # ------------------------------------------------------------------ engine thread
+    def _drain_inbox(self) -> None:
+        try:
+            while True:
+                self.engine.add_requests([self._inbox.get_nowait()])
+        except queue.Empty:
+            pass
+
+    def _loop_lockstep(self) -> None:
+        """Engine thread of a data-parallel-attention engine: every rank's thread takes each decision
+        together (one small all-reduce per iteration), so every rank steps, pauses and stops at the
+        same iteration.  A pause happens once every rank asked for it; after it the thread waits for
+        this rank's resume, and its next all-reduce waits for every rank's, so the engine's expert
+        collectives never overlap a rank's training."""
+        eng = self.engine
+        while True:
+            self._drain_inbox()
+            work, not_paused, stop = eng._ep_max([int(bool(eng.waiting or eng.running)), int(not self._pause_req.is_set()),
+                                                  int(self._stop.is_set())])
+            if stop:
+                return
+            if not not_paused:  # every rank asked to pause
+                for r in eng.abort_all():
+                    self._resolve(r)
+                self._pause_req.clear()
+                while not self._ready.wait(0.05):
+                    pass
+                continue
+            if not work:
+                time.sleep(0.001)
+                continue
+            for r in eng.step():
+                self._resolve(r)
+
     def _loop(self) -> None:
+        if getattr(self.engine, "dp_attention", False):
+            return self._loop_lockstep()
         while not self._stop.is_set():
             try:
                 while True:

@@ -124,3 +124,62 @@ def test_ep2_dp_attention_rollout_matches_single_engines():
         p.join(timeout=60)
     for r, msg in res:
         assert msg == "ok", f"rank {r}:\n{msg}"
+
+
+def _worker_lockstep(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import asyncio
+
+        import numpy as np
+
+        from axrl_b200.configs import SamplingConfig
+        from axrl_b200.data.conversation import GenerationInput
+        from axrl_b200.models.qwen3 import Qwen3Model, resolve_preset
+        from axrl_b200.parallel.expert import EPContext
+        from axrl_b200.rollout.engine import RolloutEngine
+        from axrl_b200.worker.rollout_worker import RolloutWorker
+
+        cfg = resolve_preset("tiny-moe")
+        model = Qwen3Model(cfg, ep=EPContext.from_group(dist.group.WORLD))
+        model.init_weights(2)
+        eng = RolloutEngine(model, max_batch=4, kv_tokens=2048, max_context=128, seed=4, burst=4, dp_attention=True)
+        w = RolloutWorker(eng, SamplingConfig(max_new_tokens=6 + 5 * rank, temperature=1.0))
+        g = np.random.default_rng(rank)
+
+        async def batch(n: int) -> list:
+            return await asyncio.gather(*[w.generate(GenerationInput(session_id=f"s{rank}_{i}", input_ids=g.integers(1, 1024, 9 + i)))
+                                          for i in range(n)])
+
+        outs = asyncio.run(batch(2 + rank))
+        assert all(len(o.output_ids) == 6 + 5 * rank for o in outs)
+        w.pause_generation()  # both ranks: the engine threads pause together
+        dist.barrier()  # stands in for training collectives between pause and resume
+        w.resume_generation()
+        outs = asyncio.run(batch(1))
+        assert len(outs[0].output_ids) == 6 + 5 * rank
+        w.shutdown()
+        q.put((rank, "ok"))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_rollout_worker_lockstep_with_dp_attention():
+    """Rollout workers over data-parallel-attention engines: per-rank requests of different lengths,
+    a pause / resume between them, and shutdown, with the engine threads in lockstep."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_lockstep, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for r, msg in res:
+        assert msg == "ok", f"rank {r}:\n{msg}"
