@@ -58,8 +58,14 @@ def save_hf_checkpoint(model: Qwen3Model, path: str | os.PathLike, max_shard_byt
             index["weight_map"][k] = name
     (path / "model.safetensors.index.json").write_text(json.dumps(index, indent=2))
     cfg = model.cfg
-    hf_cfg = {"architectures": ["Qwen3MoeForCausalLM" if cfg.is_moe else "Qwen3ForCausalLM"], "model_type": "qwen3_moe" if cfg.is_moe else "qwen3",
-              "torch_dtype": str(dtype).replace("torch.", ""), **{k: getattr(cfg, k) for k in cfg.__dataclass_fields__}}
+    if cfg.is_hybrid:  # Qwen3.5 / 3.6 text model (HF keeps the RoPE fraction in rope_parameters)
+        arch, mtype = ("Qwen3_5MoeForCausalLM", "qwen3_5_moe_text") if cfg.is_moe else ("Qwen3_5ForCausalLM", "qwen3_5_text")
+    else:
+        arch, mtype = ("Qwen3MoeForCausalLM", "qwen3_moe") if cfg.is_moe else ("Qwen3ForCausalLM", "qwen3")
+    hf_cfg = {"architectures": [arch], "model_type": mtype, "torch_dtype": str(dtype).replace("torch.", ""),
+              **{k: getattr(cfg, k) for k in cfg.__dataclass_fields__}}
+    if cfg.is_hybrid:
+        hf_cfg["rope_parameters"] = {"rope_type": "default", "rope_theta": cfg.rope_theta, "partial_rotary_factor": cfg.partial_rotary_factor}
     (path / "config.json").write_text(json.dumps(hf_cfg, indent=2))
 
 

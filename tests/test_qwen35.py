@@ -122,3 +122,23 @@ def test_grpo_step_and_rollout_logprobs_on_cpu():
     after = dict(tr.model.named_parameters())
     for n in names:
         assert not torch.equal(after[n], before[n]), n
+
+
+def test_hf_checkpoint_directory_round_trip(tmp_path):
+    """save_hf_checkpoint writes a Qwen3.5 text config and safetensors that load back unchanged."""
+    import json
+
+    from axrl_b200.models.qwen3 import Qwen3Model, resolve_preset
+    from axrl_b200.train.checkpoint import hf_config, load_hf_checkpoint, save_hf_checkpoint
+
+    a = Qwen3Model(resolve_preset("tiny-qwen3.5"))
+    a.init_weights(7)
+    save_hf_checkpoint(a, tmp_path, dtype=torch.float32)
+    meta = json.loads((tmp_path / "config.json").read_text())
+    assert meta["model_type"] == "qwen3_5_moe_text" and meta["rope_parameters"]["partial_rotary_factor"] == 0.25
+    cfg = hf_config(tmp_path)
+    assert cfg == a.cfg
+    b = Qwen3Model(cfg)
+    load_hf_checkpoint(b, tmp_path)
+    for (n, p), (_, q) in zip(a.named_parameters(), b.named_parameters()):
+        assert torch.allclose(p, q, atol=1e-6, rtol=0), n
