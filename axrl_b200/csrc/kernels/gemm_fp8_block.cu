@@ -12,7 +12,6 @@
 // (axrl/configs.py:391).
 #include <cuda_fp8.h>
 
-#include "common.cuh"
 #include "cutlass/detail/blockwise_scale_layout.hpp"
 #include "gemm_sm100.cuh"
 
@@ -65,36 +64,15 @@ __global__ void quant_rows_k(const bf16* __restrict__ x, long M, int K, __nv_fp8
   if (lane == 0) s[row * groups + g] = scale;
 }
 
-}  // namespace fp8
-
-// x (M,K) bf16 -> (q (M,K) e4m3, s (M, K/128) fp32)
-std::vector<at::Tensor> quant_fp8_rows(at::Tensor x) {
-  AX_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x: contiguous bf16 (M, K)");
-  long M = x.size(0);
-  int K = x.size(1);
-  AX_CHECK(K % 128 == 0, "K must be a multiple of 128");
-  auto q = at::empty({M, K}, x.options().dtype(at::kFloat8_e4m3fn));
-  auto s = at::empty({M, K / 128}, x.options().dtype(at::kFloat));
+void quant_rows(const void* x, long M, int K, void* q, float* s, cudaStream_t st) {
   long warps = M * (K / 128);
-  if (warps) {
-    fp8::quant_rows_k<<<(int)((warps * 32 + 255) / 256), 256, 0, stream()>>>((const bf16*)x.data_ptr(), M, K,
-                                                                             (__nv_fp8_e4m3*)q.data_ptr(), s.data_ptr<float>());
-    AX_LAUNCH_OK();
-  }
-  return {q, s};
+  if (!warps) return;
+  quant_rows_k<<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>((const bf16*)x, M, K, (__nv_fp8_e4m3*)q, s);
+  AX_LAUNCH_OK();
 }
 
-// y (M,N) bf16 = blockwise-scaled xq @ wq^T
-at::Tensor fp8_block_linear(at::Tensor xq, at::Tensor xs, at::Tensor wq, at::Tensor ws) {
-  AX_CHECK(xq.is_cuda() && xq.scalar_type() == at::kFloat8_e4m3fn && xq.is_contiguous() && xq.dim() == 2, "xq: e4m3 (M,K)");
-  AX_CHECK(wq.is_cuda() && wq.scalar_type() == at::kFloat8_e4m3fn && wq.is_contiguous() && wq.dim() == 2, "wq: e4m3 (N,K)");
-  int M = xq.size(0), K = xq.size(1), N = wq.size(0);
-  AX_CHECK(wq.size(1) == K && K % 128 == 0 && N % 128 == 0, "shapes: K and N multiples of 128");
-  AX_CHECK(xs.scalar_type() == at::kFloat && xs.is_contiguous() && xs.size(0) == M && xs.size(1) == K / 128, "xs: (M, K/128) fp32");
-  AX_CHECK(ws.scalar_type() == at::kFloat && ws.is_contiguous() && ws.size(0) == N / 128 && ws.size(1) == K / 128, "ws: (N/128, K/128) fp32");
-  auto y = at::empty({M, N}, xq.options().dtype(at::kBFloat16));
-  if (M == 0) return y;
-  using namespace fp8;
+// y (M,N) bf16 = blockwise-scaled xq @ wq^T; xs (M, K/128), ws (N/128, K/128) fp32, K-major.
+void block_linear(const void* xq, const float* xs, const void* wq, const float* ws, void* y, int M, int N, int K, cudaStream_t st) {
   using SA = typename Kernel::StrideA;
   using SB = typename Kernel::StrideB;
   using SC = typename Kernel::StrideC;
@@ -102,22 +80,19 @@ at::Tensor fp8_block_linear(at::Tensor xq, at::Tensor xs, at::Tensor wq, at::Ten
   auto shape = make_shape(M, N, K, 1);
   typename Op::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
                               {M, N, K, 1},
-                              {(const ElemA*)xq.data_ptr(), cutlass::make_cute_packed_stride(SA{}, make_shape(M, K, 1)),
-                               (const ElemB*)wq.data_ptr(), cutlass::make_cute_packed_stride(SB{}, make_shape(N, K, 1)),
-                               xs.data_ptr<float>(), ScaleConfig::tile_atom_to_shape_SFA(shape), ws.data_ptr<float>(),
+                              {(const ElemA*)xq, cutlass::make_cute_packed_stride(SA{}, make_shape(M, K, 1)), (const ElemB*)wq,
+                               cutlass::make_cute_packed_stride(SB{}, make_shape(N, K, 1)), xs, ScaleConfig::tile_atom_to_shape_SFA(shape), ws,
                                ScaleConfig::tile_atom_to_shape_SFB(shape)},
-                              {{1.f, 0.f}, nullptr, cutlass::make_cute_packed_stride(SC{}, make_shape(M, N, 1)),
-                               (cutlass::bfloat16_t*)y.data_ptr(), cutlass::make_cute_packed_stride(SD{}, make_shape(M, N, 1))}};
+                              {{1.f, 0.f}, nullptr, cutlass::make_cute_packed_stride(SC{}, make_shape(M, N, 1)), (cutlass::bfloat16_t*)y,
+                               cutlass::make_cute_packed_stride(SD{}, make_shape(M, N, 1))}};
   cudaGetDevice(&args.hw_info.device_id);
   args.hw_info.sm_count = num_sms();
   Op op;
-  AX_CHECK(op.can_implement(args) == cutlass::Status::kSuccess, "fp8 block GEMM cannot implement M=", M, " N=", N, " K=", K);
-  size_t wsz = Op::get_workspace_size(args);
-  at::Tensor wst;
-  if (wsz) wst = at::empty({(int64_t)wsz}, xq.options().dtype(at::kByte));
-  AX_CHECK(op.initialize(args, wsz ? wst.data_ptr() : nullptr, stream()) == cutlass::Status::kSuccess, "fp8 GEMM init");
-  AX_CHECK(op.run(stream()) == cutlass::Status::kSuccess, "fp8 GEMM run");
-  return y;
+  AX_REQUIRE(op.can_implement(args) == cutlass::Status::kSuccess, "fp8 block GEMM cannot implement M=", M, " N=", N, " K=", K);
+  Scratch wsp(Op::get_workspace_size(args), st);
+  AX_REQUIRE(op.initialize(args, wsp.ptr, st) == cutlass::Status::kSuccess, "fp8 GEMM init");
+  AX_REQUIRE(op.run(st) == cutlass::Status::kSuccess, "fp8 GEMM run");
 }
 
+}  // namespace fp8
 }  // namespace ax

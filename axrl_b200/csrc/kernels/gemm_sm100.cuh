@@ -8,7 +8,8 @@
 //   LayoutB ColumnMajor -> B stored N x K (K contiguous)   (x @ W^T with W [N,K])
 //   LayoutB RowMajor    -> B stored K x N (N contiguous)
 #pragma once
-#include "../common.cuh"
+#include "../cuda_common.cuh"
+#include "gemm_api.h"
 
 #include "cute/tensor.hpp"
 #include "cutlass/cutlass.h"
@@ -45,17 +46,6 @@ struct Sm2 {
   using Kernel = cutlass::gemm::KernelTmaWarpSpecialized1SmSm100;
   using Epi = cutlass::epilogue::TmaWarpSpecialized1Sm;
 };
-
-// Stream-K decomposition override for tuning: mode 0 heuristic, 1 data-parallel, 2 split-K
-// (``splits`` ways), 3 stream-K.  Process-wide; read at each launch.
-struct DecompOverride {
-  int mode = 0;
-  int splits = 0;
-};
-inline DecompOverride& decomp_override() {
-  static DecompOverride o;
-  return o;
-}
 
 template <class LayoutA, class LayoutB, class ElemD, class Cfg, class Sched = void, class LayoutD = cutlass::layout::RowMajor>
 struct Gemm {
@@ -107,20 +97,14 @@ struct Gemm {
     }
     Op op;
     auto st_impl = op.can_implement(args);
-    TORCH_CHECK(st_impl == cutlass::Status::kSuccess, "GEMM cannot implement M=", M, " N=", N, " K=", K);
-    size_t ws = Op::get_workspace_size(args);
-    at::Tensor wst;
-    void* wsp = nullptr;
-    if (ws) {
-      wst = at::empty({(int64_t)ws}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA));
-      wsp = wst.data_ptr();
-    }
-    auto s1 = op.initialize(args, wsp, st);
-    TORCH_CHECK(s1 == cutlass::Status::kSuccess, "GEMM init failed");
+    AX_REQUIRE(st_impl == cutlass::Status::kSuccess, "GEMM cannot implement M=", M, " N=", N, " K=", K);
+    Scratch ws(Op::get_workspace_size(args), st);
+    auto s1 = op.initialize(args, ws.ptr, st);
+    AX_REQUIRE(s1 == cutlass::Status::kSuccess, "GEMM init failed");
     // programmatic dependent launch: the kernel's load warps wait for the predecessor grid
     // (CUTLASS_ENABLE_GDC_FOR_SM100), so its prologue overlaps the predecessor's tail
     auto s2 = op.run(st, nullptr, pdl_enabled());
-    TORCH_CHECK(s2 == cutlass::Status::kSuccess, "GEMM run failed");
+    AX_REQUIRE(s2 == cutlass::Status::kSuccess, "GEMM run failed");
   }
 };
 
@@ -128,19 +112,6 @@ using RM = cutlass::layout::RowMajor;
 using CM = cutlass::layout::ColumnMajor;
 using SK = cutlass::gemm::StreamKScheduler;
 
-// One translation unit per instantiation (parallel builds).  C (optional, beta = 1) is a
-// residual added in the epilogue.
-//   tn: D = A[M,K] @ B[N,K]^T (+ C)      nn: D = A[M,K] @ B[K,N]      wgrad: D (+)= A^T @ B, A stored [K,M]
-void tn_sm2(const void* A, const void* B, const void* C, void* D, int M, int N, int K, cudaStream_t st);
-void tn_sm1_sk(const void* A, const void* B, const void* C, void* D, int M, int N, int K, cudaStream_t st);
-void tn_narrow_sk(const void* A, const void* B, const void* C, void* D, int M, int N, int K, cudaStream_t st);
-void nn_sm2(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);
-void nn_sm1_sk(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);
-void wgrad_f32_sm2(const void* A, const void* B, void* D, int M, int N, int K, bool acc, cudaStream_t st);
-void wgrad_f32_sm1(const void* A, const void* B, void* D, int M, int N, int K, bool acc, cudaStream_t st);
-void wgrad_bf16_sm1(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t st);
-// skinny (M <= 64): Y[M,N] = X[M,K] @ W[N,K]^T (+ C) computed as Y^T = W @ X^T (swap-AB)
-void tn_swapab(const void* X, const void* W, const void* C, void* D, int M, int N, int K, cudaStream_t st);
-
 }  // namespace gemm
 }  // namespace ax
+

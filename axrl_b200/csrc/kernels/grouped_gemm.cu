@@ -14,7 +14,6 @@
 //
 // Reference counterpart: the grouped expert GEMM of Megatron's MoE layer (TE grouped GEMM /
 // sequential MLP) behind moe_token_dispatcher_type="alltoall" (axrl/worker/megatron_worker.py:833).
-#include "common.cuh"
 #include "gemm_sm100.cuh"
 
 namespace ax {
@@ -64,14 +63,21 @@ struct Arrays {
 };
 
 template <class G, class ElemD>
-static Arrays<G, ElemD> carve(at::Tensor& buf, int E) {
+static size_t carve_bytes(int E) {
   auto align = [](size_t x) { return (x + 255) & ~size_t(255); };
   size_t sizes[9] = {sizeof(UShape), sizeof(void*), sizeof(void*), sizeof(void*), sizeof(void*), sizeof(typename G::SA),
                      sizeof(typename G::SB), sizeof(typename G::SC), sizeof(typename G::SD)};
   size_t total = 0;
   for (size_t s : sizes) total += align(s * E);
-  buf = at::empty({(int64_t)total}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA));
-  char* p = static_cast<char*>(buf.data_ptr());
+  return total;
+}
+
+template <class G, class ElemD>
+static Arrays<G, ElemD> carve(void* base, int E) {
+  auto align = [](size_t x) { return (x + 255) & ~size_t(255); };
+  size_t sizes[9] = {sizeof(UShape), sizeof(void*), sizeof(void*), sizeof(void*), sizeof(void*), sizeof(typename G::SA),
+                     sizeof(typename G::SB), sizeof(typename G::SC), sizeof(typename G::SD)};
+  char* p = static_cast<char*>(base);
   Arrays<G, ElemD> r;
   size_t off = 0;
   auto take = [&](size_t s) { char* q = p + off; off += align(s * E); return q; };
@@ -142,7 +148,7 @@ __global__ void setup_wgrad_k(const int* __restrict__ off, int E, int N, int K, 
 }
 
 template <class G, class ElemD>
-static void run(const Arrays<G, ElemD>& r, int E, float beta) {
+static void run(const Arrays<G, ElemD>& r, int E, float beta, cudaStream_t st) {
   typename G::Op::Arguments args;
   args.mode = cutlass::gemm::GemmUniversalMode::kGrouped;
   args.problem_shape = Problem{E, r.shape, nullptr};
@@ -159,72 +165,40 @@ static void run(const Arrays<G, ElemD>& r, int E, float beta) {
   cudaGetDevice(&args.hw_info.device_id);
   args.hw_info.sm_count = num_sms();
   typename G::Op op;
-  AX_CHECK(op.can_implement(args) == cutlass::Status::kSuccess, "grouped GEMM cannot implement");
-  size_t ws = G::Op::get_workspace_size(args);
-  at::Tensor wst;
-  if (ws) wst = at::empty({(int64_t)ws}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA));
-  AX_CHECK(op.initialize(args, ws ? wst.data_ptr() : nullptr, stream()) == cutlass::Status::kSuccess, "grouped GEMM init");
-  AX_CHECK(op.run(stream()) == cutlass::Status::kSuccess, "grouped GEMM run");
+  AX_REQUIRE(op.can_implement(args) == cutlass::Status::kSuccess, "grouped GEMM cannot implement");
+  Scratch ws(G::Op::get_workspace_size(args), st);
+  AX_REQUIRE(op.initialize(args, ws.ptr, st) == cutlass::Status::kSuccess, "grouped GEMM init");
+  AX_REQUIRE(op.run(st) == cutlass::Status::kSuccess, "grouped GEMM run");
 }
 
-static void check_rows(const at::Tensor& t, const char* n) {
-  AX_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.dim() == 2, n, ": contiguous bf16 (rows, C)");
-  AX_CHECK(t.size(1) % 8 == 0, n, ": row length must be a multiple of 8");
-}
+using B16 = cutlass::bfloat16_t;
 
-}  // namespace grouped
-
-// Y (rows, N) = per-expert X rows @ W[e]^T; offsets (E+1) int32 on the device.
-at::Tensor grouped_linear_fwd(at::Tensor x, at::Tensor w, at::Tensor offsets) {
-  grouped::check_rows(x, "x");
-  AX_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: (E, N, K) bf16");
-  AX_CHECK(offsets.scalar_type() == at::kInt && offsets.numel() == w.size(0) + 1, "offsets: E+1 int32");
-  int E = w.size(0), N = w.size(1), K = w.size(2);
-  AX_CHECK(x.size(1) == K, "K mismatch");
-  auto y = at::empty({x.size(0), N}, x.options());
-  if (x.size(0) == 0) return y;
-  at::Tensor buf;
-  auto r = grouped::carve<grouped::Fwd, cutlass::bfloat16_t>(buf, E);
-  grouped::setup_fwd_k<<<(E + 127) / 128, 128, 0, stream()>>>(offsets.data_ptr<int>(), E, N, K,
-                                                             (const cutlass::bfloat16_t*)x.data_ptr(), (const cutlass::bfloat16_t*)w.data_ptr(),
-                                                             (cutlass::bfloat16_t*)y.data_ptr(), r);
+// Y (rows, N) = per-expert X rows @ W[e]^T; off (E+1) int32 on the device.
+void fwd(const int* off, int E, int N, int K, const void* X, const void* W, void* Y, cudaStream_t st) {
+  Scratch buf(carve_bytes<Fwd, B16>(E), st);
+  auto r = carve<Fwd, B16>(buf.ptr, E);
+  setup_fwd_k<<<(E + 127) / 128, 128, 0, st>>>(off, E, N, K, (const B16*)X, (const B16*)W, (B16*)Y, r);
   AX_LAUNCH_OK();
-  grouped::run<grouped::Fwd, cutlass::bfloat16_t>(r, E, 0.f);
-  return y;
+  run<Fwd, B16>(r, E, 0.f, st);
 }
 
 // dX (rows, K) = per-expert dY rows @ W[e]
-at::Tensor grouped_linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor offsets) {
-  grouped::check_rows(dy, "dy");
-  int E = w.size(0), N = w.size(1), K = w.size(2);
-  AX_CHECK(dy.size(1) == N, "N mismatch");
-  auto dx = at::empty({dy.size(0), K}, dy.options());
-  if (dy.size(0) == 0) return dx;
-  at::Tensor buf;
-  auto r = grouped::carve<grouped::Dgrad, cutlass::bfloat16_t>(buf, E);
-  grouped::setup_dgrad_k<<<(E + 127) / 128, 128, 0, stream()>>>(offsets.data_ptr<int>(), E, N, K,
-                                                               (const cutlass::bfloat16_t*)dy.data_ptr(), (const cutlass::bfloat16_t*)w.data_ptr(),
-                                                               (cutlass::bfloat16_t*)dx.data_ptr(), r);
+void dgrad(const int* off, int E, int N, int K, const void* dY, const void* W, void* dX, cudaStream_t st) {
+  Scratch buf(carve_bytes<Dgrad, B16>(E), st);
+  auto r = carve<Dgrad, B16>(buf.ptr, E);
+  setup_dgrad_k<<<(E + 127) / 128, 128, 0, st>>>(off, E, N, K, (const B16*)dY, (const B16*)W, (B16*)dX, r);
   AX_LAUNCH_OK();
-  grouped::run<grouped::Dgrad, cutlass::bfloat16_t>(r, E, 0.f);
-  return dx;
+  run<Dgrad, B16>(r, E, 0.f, st);
 }
 
-// acc (E, N, K) fp32 += per-expert dY rows^T @ X rows
-void grouped_linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor offsets, at::Tensor acc) {
-  grouped::check_rows(dy, "dy");
-  grouped::check_rows(x, "x");
-  AX_CHECK(acc.is_cuda() && acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.dim() == 3, "acc: (E, N, K) fp32");
-  int E = acc.size(0), N = acc.size(1), K = acc.size(2);
-  AX_CHECK(dy.size(1) == N && x.size(1) == K && dy.size(0) == x.size(0), "shapes");
-  auto zeros = at::zeros({8, std::max(N, K)}, dy.options());
-  at::Tensor buf;
-  auto r = grouped::carve<grouped::Wgrad, float>(buf, E);
-  grouped::setup_wgrad_k<<<(E + 127) / 128, 128, 0, stream()>>>(offsets.data_ptr<int>(), E, N, K,
-                                                               (const cutlass::bfloat16_t*)dy.data_ptr(), (const cutlass::bfloat16_t*)x.data_ptr(),
-                                                               acc.data_ptr<float>(), (const cutlass::bfloat16_t*)zeros.data_ptr(), r);
+// acc (E, N, K) fp32 += per-expert dY rows^T @ X rows; zeros: 8 x max(N, K) bf16 zeros.
+void wgrad_acc(const int* off, int E, int N, int K, const void* dY, const void* X, float* acc, const void* zeros, cudaStream_t st) {
+  Scratch buf(carve_bytes<Wgrad, float>(E), st);
+  auto r = carve<Wgrad, float>(buf.ptr, E);
+  setup_wgrad_k<<<(E + 127) / 128, 128, 0, st>>>(off, E, N, K, (const B16*)dY, (const B16*)X, acc, (const B16*)zeros, r);
   AX_LAUNCH_OK();
-  grouped::run<grouped::Wgrad, float>(r, E, 1.f);
+  run<Wgrad, float>(r, E, 1.f, st);
 }
 
+}  // namespace grouped
 }  // namespace ax

@@ -2,11 +2,17 @@
 // Tile-config choice by M (tokens): >= 512 -> 1-SM 128x256 data-parallel tiles;
 // 65..511 -> 1-SM 128x128 stream-K; <= 64 -> 1-SM 128x64 stream-K (decode: weight streaming).
 #include <string>
+#include <vector>
+
+#include <c10/cuda/CUDACachingAllocator.h>
 
 #include "common.cuh"
-#include "gemm_sm100.cuh"
+#include "gemm_api.h"
 
 namespace ax {
+
+void* scratch_alloc(size_t bytes, cudaStream_t st) { return c10::cuda::CUDACachingAllocator::raw_alloc_with_stream(bytes, st); }
+void scratch_free(void* p) { c10::cuda::CUDACachingAllocator::raw_delete(p); }
 
 static void check_bf16_2d(const at::Tensor& t, const char* n) {
   AX_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1 && t.stride(0) == t.size(1),
@@ -192,5 +198,76 @@ at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant) {
 
 // Generic: trans_b ? a @ b^T : a @ b   (bf16 out)
 at::Tensor gemm_bf16(at::Tensor a, at::Tensor b, bool trans_b) { return trans_b ? linear_fwd(a, b) : linear_dgrad(a, b); }
+
+// ---------------------------------------------------------------- grouped (per-expert) GEMMs
+static void check_rows(const at::Tensor& t, const char* n) {
+  AX_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.dim() == 2, n, ": contiguous bf16 (rows, C)");
+  AX_CHECK(t.size(1) % 8 == 0, n, ": row length must be a multiple of 8");
+}
+
+// Y (rows, N) = per-expert X rows @ W[e]^T; offsets (E+1) int32 on the device.
+at::Tensor grouped_linear_fwd(at::Tensor x, at::Tensor w, at::Tensor offsets) {
+  check_rows(x, "x");
+  AX_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: (E, N, K) bf16");
+  AX_CHECK(offsets.scalar_type() == at::kInt && offsets.numel() == w.size(0) + 1, "offsets: E+1 int32");
+  int E = w.size(0), N = w.size(1), K = w.size(2);
+  AX_CHECK(x.size(1) == K, "K mismatch");
+  auto y = at::empty({x.size(0), N}, x.options());
+  if (x.size(0) == 0) return y;
+  grouped::fwd(offsets.data_ptr<int>(), E, N, K, x.data_ptr(), w.data_ptr(), y.data_ptr(), stream());
+  return y;
+}
+
+// dX (rows, K) = per-expert dY rows @ W[e]
+at::Tensor grouped_linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor offsets) {
+  check_rows(dy, "dy");
+  AX_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: (E, N, K) bf16");
+  AX_CHECK(offsets.scalar_type() == at::kInt && offsets.numel() == w.size(0) + 1, "offsets: E+1 int32");
+  int E = w.size(0), N = w.size(1), K = w.size(2);
+  AX_CHECK(dy.size(1) == N, "N mismatch");
+  auto dx = at::empty({dy.size(0), K}, dy.options());
+  if (dy.size(0) == 0) return dx;
+  grouped::dgrad(offsets.data_ptr<int>(), E, N, K, dy.data_ptr(), w.data_ptr(), dx.data_ptr(), stream());
+  return dx;
+}
+
+// acc (E, N, K) fp32 += per-expert dY rows^T @ X rows
+void grouped_linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor offsets, at::Tensor acc) {
+  check_rows(dy, "dy");
+  check_rows(x, "x");
+  AX_CHECK(acc.is_cuda() && acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.dim() == 3, "acc: (E, N, K) fp32");
+  int E = acc.size(0), N = acc.size(1), K = acc.size(2);
+  AX_CHECK(offsets.scalar_type() == at::kInt && offsets.numel() == E + 1, "offsets: E+1 int32");
+  AX_CHECK(dy.size(1) == N && x.size(1) == K && dy.size(0) == x.size(0), "shapes");
+  auto zeros = at::zeros({8, std::max(N, K)}, dy.options());
+  grouped::wgrad_acc(offsets.data_ptr<int>(), E, N, K, dy.data_ptr(), x.data_ptr(), acc.data_ptr<float>(), zeros.data_ptr(), stream());
+}
+
+// ---------------------------------------------------------------- block-scaled fp8
+// x (M,K) bf16 -> (q (M,K) e4m3, s (M, K/128) fp32)
+std::vector<at::Tensor> quant_fp8_rows(at::Tensor x) {
+  AX_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x: contiguous bf16 (M, K)");
+  long M = x.size(0);
+  int K = x.size(1);
+  AX_CHECK(K % 128 == 0, "K must be a multiple of 128");
+  auto q = at::empty({M, K}, x.options().dtype(at::kFloat8_e4m3fn));
+  auto s = at::empty({M, K / 128}, x.options().dtype(at::kFloat));
+  fp8::quant_rows(x.data_ptr(), M, K, q.data_ptr(), s.data_ptr<float>(), stream());
+  return {q, s};
+}
+
+// y (M,N) bf16 = blockwise-scaled xq @ wq^T
+at::Tensor fp8_block_linear(at::Tensor xq, at::Tensor xs, at::Tensor wq, at::Tensor ws) {
+  AX_CHECK(xq.is_cuda() && xq.scalar_type() == at::kFloat8_e4m3fn && xq.is_contiguous() && xq.dim() == 2, "xq: e4m3 (M,K)");
+  AX_CHECK(wq.is_cuda() && wq.scalar_type() == at::kFloat8_e4m3fn && wq.is_contiguous() && wq.dim() == 2, "wq: e4m3 (N,K)");
+  int M = xq.size(0), K = xq.size(1), N = wq.size(0);
+  AX_CHECK(wq.size(1) == K && K % 128 == 0 && N % 128 == 0, "shapes: K and N multiples of 128");
+  AX_CHECK(xs.scalar_type() == at::kFloat && xs.is_contiguous() && xs.size(0) == M && xs.size(1) == K / 128, "xs: (M, K/128) fp32");
+  AX_CHECK(ws.scalar_type() == at::kFloat && ws.is_contiguous() && ws.size(0) == N / 128 && ws.size(1) == K / 128, "ws: (N/128, K/128) fp32");
+  auto y = at::empty({M, N}, xq.options().dtype(at::kBFloat16));
+  if (M == 0) return y;
+  fp8::block_linear(xq.data_ptr(), xs.data_ptr<float>(), wq.data_ptr(), ws.data_ptr<float>(), y.data_ptr(), M, N, K, stream());
+  return y;
+}
 
 }  // namespace ax

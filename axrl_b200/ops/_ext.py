@@ -2,8 +2,10 @@
 
 The extension is compiled ahead of time by ``axrl_b200/csrc/build.py`` (called
 from ``__graft_entry__.build``).  On a machine with a GPU every op dispatches
-CUDA tensors to it; if it is missing, the op raises instead of silently
-falling back to PyTorch.  CPU tensors use the PyTorch reference code in each
+CUDA tensors to it.  If the shared object is missing there, the loader builds it
+in-tree once (under a file lock, so concurrent ranks build it one time; set
+``AXRL_AUTOBUILD=0`` to disable) and raises if that fails: no op silently falls
+back to PyTorch.  CPU tensors use the PyTorch reference code in each
 op module (the numerical oracle and the path CPU tests exercise).
 """
 
@@ -24,6 +26,25 @@ def _so_path(name: str) -> str | None:
     return hits[0] if hits else None
 
 
+def _build_locked(name: str) -> str | None:
+    """Build the missing extension in-tree; one process builds while the others wait on the lock."""
+    import fcntl
+    import sys
+
+    from axrl_b200.csrc import build as _b
+
+    os.makedirs(_b.BUILD, exist_ok=True)
+    with open(os.path.join(_b.BUILD, ".lock"), "w") as lk:
+        fcntl.flock(lk, fcntl.LOCK_EX)
+        try:
+            if _so_path(name) is None:
+                sys.stderr.write(f"axrl_b200: extension {name} missing, building it in-tree\n")
+                _b.build(only=name)
+        finally:
+            fcntl.flock(lk, fcntl.LOCK_UN)
+    return _so_path(name)
+
+
 def load(name: str = "_C") -> ModuleType:
     global _MOD, _ERR
     if _MOD is not None and name == "_C":
@@ -31,6 +52,8 @@ def load(name: str = "_C") -> ModuleType:
     import torch  # noqa: F401  (libtorch symbols must be loaded first)
 
     path = _so_path(name)
+    if path is None and torch.cuda.is_available() and os.environ.get("AXRL_AUTOBUILD", "1") != "0":
+        path = _build_locked(name)
     if path is None:
         _ERR = f"extension {name} not built: run `python -m axrl_b200.csrc.build`"
         raise RuntimeError(_ERR)
