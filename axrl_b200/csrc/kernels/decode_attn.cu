@@ -55,11 +55,12 @@ struct Params {
   float* part_ml;         // (B, Hq, splits, 2): (max, sum) in log2 domain
   int Hq, Hkv, P, max_pages, splits;
   float scale_log2;
+  int max_len;            // lengths are clamped to this (<= max_pages * P and <= splits * SPLIT)
 };
 
 // One (sequence b, kv head hk, split sp) work item; all threads of the CTA call it together.
 __device__ __forceinline__ void decode_item(const Params& p, char* smem, int b, int hk, int sp) {
-  const int len = p.seq_lens[b];
+  const int len = min(p.seq_lens[b], p.max_len);  // never read block_table past max_pages
   const int t0 = sp * SPLIT;
   if (t0 >= len) return;
   const int G = p.Hq / p.Hkv;
@@ -251,13 +252,13 @@ __global__ void __launch_bounds__(128) decode_persist_k(Params p, const int* __r
 
 // out[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s ; one warp per (b, h)
 __global__ void combine_k(const float* __restrict__ part_o, const float* __restrict__ part_ml, const int* __restrict__ seq_lens,
-                          bf16* __restrict__ out, int B, int Hq, int splits) {
+                          bf16* __restrict__ out, int B, int Hq, int splits, int max_len) {
   pdl_wait();
   pdl_trigger();
   int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (w >= B * Hq) return;
   int b = w / Hq;
-  int ns = min(splits, (seq_lens[b] + SPLIT - 1) / SPLIT);
+  int ns = min(splits, (min(seq_lens[b], max_len) + SPLIT - 1) / SPLIT);
   const float* ml = part_ml + (long)w * splits * 2;
   float M = -INFINITY;
   for (int s = 0; s < ns; ++s) M = fmaxf(M, ml[2 * s]);
@@ -357,7 +358,8 @@ void decode_advance(int64_t B, at::Tensor out_tok, at::Tensor out_lp, at::Tensor
 }
 
 // q (B,Hq,128); caches (pages,Hkv,P,128); block_table (B,max_pages) int32; seq_lens (B,) int32.
-// `splits` is fixed by the caller (ceil(max_context / 256)) so the launch shape is static.
+// `splits` is fixed by the caller (ceil(max_context / SPLIT), SPLIT = 128 tokens) so the launch
+// shape is static.
 void decode_plan(at::Tensor seq_lens, at::Tensor prefix) {
   int B = seq_lens.numel();
   AX_CHECK(prefix.scalar_type() == at::kInt && prefix.numel() >= B + 1, "prefix: int32 (B + 1)");
@@ -373,16 +375,20 @@ void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bl
   AX_CHECK(Hq % Hkv == 0 && Hq / Hkv <= 16, "GQA group must be <= 16");
   AX_CHECK(part_o.numel() >= (long)B * Hq * splits * D && part_ml.numel() >= (long)B * Hq * splits * 2, "partial buffers too small");
   if (B == 0) return;
+  const int max_len = (int)std::min<long>((long)block_table.size(1) * P, (long)splits * SPLIT);
   Params p{(const bf16*)q.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(), block_table.data_ptr<int>(),
            seq_lens.data_ptr<int>(), part_o.data_ptr<float>(), part_ml.data_ptr<float>(), Hq, Hkv, P, (int)block_table.size(1),
-           (int)splits, (float)(scale * 1.4426950408889634)};
+           (int)splits, (float)(scale * 1.4426950408889634), max_len};
   int smem = 16 * D * 2 + WARPS * 2 * SLICE * D * 2;
   static_assert(WARPS * 16 * (D + 2) * 4 <= WARPS * 2 * SLICE * D * 2, "merge buffer must fit in the K/V area");
-  static bool attr = false;
-  if (!attr) {
+  // the shared-memory opt-in is a per-device function attribute
+  static bool attr[64] = {false};
+  const int dev = c10::cuda::current_device();
+  AX_CHECK(dev >= 0 && dev < 64, "device index");
+  if (!attr[dev]) {
     AX_CUDA_OK(cudaFuncSetAttribute(decode_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     AX_CUDA_OK(cudaFuncSetAttribute(decode_persist_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
+    attr[dev] = true;
   }
   if (prefix.has_value()) {  // planned: persistent grid over the live work items
     AX_CHECK(prefix->scalar_type() == at::kInt && prefix->numel() >= B + 1, "prefix: int32 (B + 1)");
@@ -393,7 +399,8 @@ void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bl
   AX_LAUNCH_OK();
   long w = (long)B * Hq;
   launch_pdl(combine_k, dim3((w * 32 + 255) / 256), dim3(256), 0, stream(), (const float*)part_o.data_ptr<float>(),
-             (const float*)part_ml.data_ptr<float>(), (const int*)seq_lens.data_ptr<int>(), (bf16*)out.data_ptr(), B, Hq, (int)splits);
+             (const float*)part_ml.data_ptr<float>(), (const int*)seq_lens.data_ptr<int>(), (bf16*)out.data_ptr(), B, Hq, (int)splits,
+             max_len);
   AX_LAUNCH_OK();
 }
 
@@ -422,8 +429,8 @@ static __device__ __align__(256) float g_decode_noalloc_scratch[(long)AXRL_DECOD
 
 namespace {
 std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[64] = {nullptr};
-bool g_noalloc_attr = false;
+float* g_noalloc_ptr[64] = {nullptr};  // device address of the array, per device
+bool g_noalloc_attr[64] = {false};     // shared-memory opt-in of decode_k done, per device
 }  // namespace
 
 extern "C" int axrl_paged_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
@@ -446,6 +453,12 @@ extern "C" int axrl_paged_decode_attention_noalloc(const void* q, const void* k_
                  SPLIT, rows, AXRL_DECODE_NOALLOC_MAX_ROWS);
     return 1;
   }
+  // An error left pending by earlier work on this thread (or a context already in an error state)
+  // belongs to its owner: report it without launching and without clearing it.
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    std::fprintf(stderr, "axrl_paged_decode_attention_noalloc: a CUDA error is already pending; nothing launched\n");
+    return 5;
+  }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 3;
   float* scratch = nullptr;
@@ -461,18 +474,20 @@ extern "C" int axrl_paged_decode_attention_noalloc(const void* q, const void* k_
       g_noalloc_ptr[dev] = static_cast<float*>(p);
     }
     scratch = g_noalloc_ptr[dev];
-    if (!g_noalloc_attr) {
+    if (!g_noalloc_attr[dev]) {
       int smem = 16 * D * 2 + WARPS * 2 * SLICE * D * 2;
       if (cudaFuncSetAttribute(decode_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return 4;
-      g_noalloc_attr = true;
+      g_noalloc_attr[dev] = true;
     }
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Params p{static_cast<const bf16*>(q), static_cast<const bf16*>(k_cache), static_cast<const bf16*>(v_cache), block_table, seq_lens,
-           scratch, scratch + rows * D, Hq, Hkv, page_size, max_pages, splits, scale * 1.4426950408889634f};
+           scratch, scratch + rows * D, Hq, Hkv, page_size, max_pages, splits, scale * 1.4426950408889634f, max_context};
   int smem = 16 * D * 2 + WARPS * 2 * SLICE * D * 2;
   decode_k<<<dim3(B, Hkv, splits), 128, smem, st>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return 4;
   long w = (long)B * Hq;
-  combine_k<<<(w * 32 + 255) / 256, 256, 0, st>>>(p.part_o, p.part_ml, seq_lens, static_cast<bf16*>(out), B, Hq, splits);
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  combine_k<<<(w * 32 + 255) / 256, 256, 0, st>>>(p.part_o, p.part_ml, seq_lens, static_cast<bf16*>(out), B, Hq, splits, max_context);
+  if (cudaGetLastError() != cudaSuccess) return 4;
+  return 0;
 }

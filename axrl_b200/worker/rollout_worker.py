@@ -13,12 +13,18 @@ Reference counterpart: ``SGLangWorker`` (``axrl/worker/sglang_worker.py:49-851``
 The engine runs on a dedicated thread that owns the GPU work; coroutines submit requests
 through a thread-safe inbox and await futures.  One thread stepping the engine keeps
 continuous batching intact across every concurrent caller.
+
+When the engine thread ends (``shutdown`` on any rank of a lockstep group, or an exception in
+the engine), every request it still holds is aborted and returned with its partial output, and
+every call that was not yet admitted resolves as an empty ``abort``; after an exception the
+callers' futures carry the exception instead.  No ``generate`` call is left waiting.
 """
 
 from __future__ import annotations
 
 import asyncio
 import itertools
+import logging
 import queue
 import threading
 import time
@@ -29,6 +35,8 @@ import numpy as np
 from axrl_b200.configs import SamplingConfig
 from axrl_b200.data.conversation import GenerationInput, GenerationOutput
 from axrl_b200.rollout.engine import GenRequest, GenResult, RolloutEngine
+
+log = logging.getLogger(__name__)
 
 
 class _DecodeOnly:
@@ -50,13 +58,16 @@ class RolloutWorker:
         if decode_fn is not None and getattr(engine, "tokenizer", None) is None:
             engine.tokenizer = _DecodeOnly(decode_fn)  # token strings for tool-call grammars
         self._inbox: queue.Queue = queue.Queue()
-        self._pending: dict[str, tuple[asyncio.AbstractEventLoop, asyncio.Future]] = {}
+        self._pending: dict[str, tuple[asyncio.AbstractEventLoop, asyncio.Future, int]] = {}
+        self._lock = threading.Lock()  # guards _pending and _closed
+        self._closed = False
+        self._error: BaseException | None = None
         self._ready = threading.Event()
         self._ready.set()
         self._pause_req = threading.Event()
         self._stop = threading.Event()
         self._ids = itertools.count()
-        self._thread = threading.Thread(target=self._loop, name="rollout-engine", daemon=True)
+        self._thread = threading.Thread(target=self._run, name="rollout-engine", daemon=True)
         self._thread.start()
 
     # ------------------------------------------------------------------ engine thread
@@ -93,9 +104,54 @@ class RolloutWorker:
             for r in eng.step():
                 self._resolve(r)
 
+    def _run(self) -> None:
+        lockstep = getattr(self.engine, "dp_attention", False)
+        try:
+            self._loop_lockstep() if lockstep else self._loop()
+        except BaseException as e:  # noqa: BLE001
+            log.exception("rollout engine thread failed")
+            self._error = e
+            self._finish(e)
+            if lockstep:
+                # Best effort: tell the peers to stop at their next decision.  Peers that are inside
+                # a forward waiting for this rank end through their own collective timeouts.
+                try:
+                    self.engine._ep_max([0, 1, 1])
+                except Exception:  # noqa: BLE001
+                    pass
+            return
+        self._finish(None)
+
+    def _finish(self, exc: BaseException | None) -> None:
+        """Resolve every call this worker still holds; later submissions are refused."""
+        with self._lock:
+            self._closed = True
+        done: list[GenResult] = []
+        try:
+            done = self.engine.abort_all()
+        except Exception:  # noqa: BLE001
+            log.exception("abort_all failed while stopping the rollout engine")
+        try:
+            while True:  # admitted to the inbox but never to the engine
+                r = self._inbox.get_nowait()
+                done.append(GenResult(r.rid, [], [], "abort", len(r.prompt)))
+        except queue.Empty:
+            pass
+        if exc is None:
+            for r in done:
+                self._resolve(r)
+        with self._lock:
+            rest, self._pending = self._pending, {}
+        err = exc if exc is not None else None
+        for rid, (loop, fut, plen) in rest.items():
+            if err is not None:
+                loop.call_soon_threadsafe(lambda f=fut, e=err: f.done() or f.set_exception(RuntimeError(f"rollout engine failed: {e!r}")))
+            else:
+                res = GenResult(rid, [], [], "abort", plen)
+                loop.call_soon_threadsafe(lambda f=fut, r=res: f.done() or f.set_result(r))
+        self._ready.set()  # wake callers waiting to resubmit
+
     def _loop(self) -> None:
-        if getattr(self.engine, "dp_attention", False):
-            return self._loop_lockstep()
         while not self._stop.is_set():
             try:
                 while True:
@@ -115,15 +171,23 @@ class RolloutWorker:
                 self._resolve(r)
 
     def _resolve(self, res: GenResult) -> None:
-        loop, fut = self._pending.pop(res.rid, (None, None))
+        with self._lock:
+            loop, fut, _ = self._pending.pop(res.rid, (None, None, 0))
         if fut is not None:
             loop.call_soon_threadsafe(lambda: fut.done() or fut.set_result(res))
 
     async def _submit(self, req: GenRequest) -> GenResult:
         loop = asyncio.get_running_loop()
         fut = loop.create_future()
-        self._pending[req.rid] = (loop, fut)
-        self._inbox.put(req)
+        with self._lock:
+            closed = self._closed
+            if not closed:
+                self._pending[req.rid] = (loop, fut, len(req.prompt))
+                self._inbox.put(req)
+        if closed:
+            if self._error is not None:
+                raise RuntimeError(f"rollout engine failed: {self._error!r}")
+            return GenResult(req.rid, [], [], "abort", len(req.prompt))
         return await fut
 
     # ------------------------------------------------------------------ public API
@@ -155,7 +219,7 @@ class RolloutWorker:
             out_lps += res.output_logprobs
             if res.routed_experts is not None:
                 routing.append(res.routed_experts)
-            if res.finish_reason != "abort" or not self.continue_after_abort or len(out_ids) >= budget:
+            if res.finish_reason != "abort" or not self.continue_after_abort or len(out_ids) >= budget or self._closed:
                 break
             retry += 1
         handle = None

@@ -183,3 +183,69 @@ def test_rollout_worker_lockstep_with_dp_attention():
         p.join(timeout=60)
     for r, msg in res:
         assert msg == "ok", f"rank {r}:\n{msg}"
+
+
+def _worker_one_rank_stops(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import asyncio
+
+        import numpy as np
+
+        from axrl_b200.configs import SamplingConfig
+        from axrl_b200.data.conversation import GenerationInput
+        from axrl_b200.models.qwen3 import Qwen3Model, resolve_preset
+        from axrl_b200.parallel.expert import EPContext
+        from axrl_b200.rollout.engine import RolloutEngine
+        from axrl_b200.worker.rollout_worker import RolloutWorker
+
+        cfg = resolve_preset("tiny-moe")
+        model = Qwen3Model(cfg, ep=EPContext.from_group(dist.group.WORLD))
+        model.init_weights(2)
+        eng = RolloutEngine(model, max_batch=4, kv_tokens=4096, max_context=512, seed=4, burst=4, dp_attention=True)
+        budget = 400 if rank == 0 else 4
+        w = RolloutWorker(eng, SamplingConfig(max_new_tokens=budget, temperature=1.0))
+        g = np.random.default_rng(rank)
+
+        async def run() -> list:
+            calls = [w.generate(GenerationInput(session_id=f"s{rank}_{i}", input_ids=g.integers(1, 1024, 9 + i))) for i in range(3)]
+            if rank == 0:
+                return await asyncio.gather(*calls)
+            outs = await asyncio.gather(*calls)
+            w.shutdown()  # only this rank asks; rank 0 still has requests in flight
+            return outs
+
+        outs = asyncio.run(asyncio.wait_for(run(), timeout=120))
+        w._thread.join(timeout=30)
+        assert not w._thread.is_alive(), "engine thread still running"
+        if rank == 0:
+            assert all(o.finish_reason == "abort" or len(o.output_ids) == budget for o in outs), [o.finish_reason for o in outs]
+            assert any(o.finish_reason == "abort" for o in outs)
+            # a call after the stop resolves at once instead of waiting for an engine that is gone
+            late = asyncio.run(asyncio.wait_for(w.generate(GenerationInput(session_id="late", input_ids=np.arange(1, 9))), timeout=10))
+            assert late.finish_reason == "abort" and len(late.output_ids) == 0
+        q.put((rank, "ok"))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_rollout_worker_lockstep_stop_on_one_rank_resolves_all_calls():
+    """One rank shuts its worker down while the other still generates: both engine threads stop at
+    the same decision, the busy rank's calls return their partial output as aborted, and a call made
+    after the stop resolves immediately."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_one_rank_stops, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for r, msg in res:
+        assert msg == "ok", f"rank {r}:\n{msg}"
