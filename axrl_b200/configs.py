@@ -17,7 +17,7 @@ from dataclasses import dataclass
 from pathlib import Path
 from typing import Literal
 
-from pydantic import BaseModel, ConfigDict
+from pydantic import BaseModel, ConfigDict, field_validator
 
 
 @dataclass
@@ -195,6 +195,15 @@ class RolloutWorkerConfig(InferWorkerConfig):
     use_cuda_graph: bool = True
     weight_dtype: Literal["bf16", "fp8_block"] = "bf16"
 
+    @field_validator("kv_cache_dtype")
+    @classmethod
+    def _kv_dtype_supported(cls, v: str) -> str:
+        # The paged KV cache and its decode kernel are bf16; an fp8 cache would be accepted and
+        # silently stored in bf16, so it is rejected instead.
+        if v != "auto":
+            raise ValueError(f"kv_cache_dtype={v!r} is not supported by the rollout engine (bf16 KV cache only); use 'auto'")
+        return v
+
     def gpus_per_worker(self) -> int:
         return self.tp_size * self.pp_size
 
@@ -359,6 +368,15 @@ class MegatronWorkerConfig(StrictBaseModel):
     use_magi_flat_forward: bool = False
     # Max tokens per packed micro-batch when use_dynamic_batch_size is on.
     max_tokens_per_micro_batch: int = 16384
+
+    @field_validator("fp8")
+    @classmethod
+    def _fp8_training_supported(cls, v: str | None) -> str | None:
+        # fp8 serves the rollout (RolloutWorkerConfig.weight_dtype="fp8_block"); the trainer's GEMMs
+        # are bf16, so an fp8 training recipe is rejected rather than ignored.
+        if v is not None:
+            raise ValueError(f"fp8={v!r} training is not supported (bf16 training; fp8 is available for rollout weights)")
+        return v
 
     def world_size(self) -> int:
         return self.dp_size * self.tp_size * self.pp_size * self.cp_size

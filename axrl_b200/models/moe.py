@@ -165,9 +165,16 @@ class MoEBlock(nn.Module):
             out[q + "down_proj.weight"] = self.experts_down[e]
         return out
 
+    shared_selective = False  # selective recompute of the shared expert (recompute_modules)
+
     def forward(self, x: torch.Tensor, ctx: MoEContext | None = None, layer_idx: int = 0) -> torch.Tensor:
         y = self._routed(x, ctx, layer_idx)
-        sh = self.shared_expert(x)
+        if self.shared_selective and torch.is_grad_enabled():  # recompute the shared expert in backward
+            from torch.utils.checkpoint import checkpoint
+
+            sh = checkpoint(self.shared_expert, x, use_reentrant=False)
+        else:
+            sh = self.shared_expert(x)
         return y if sh is None else y + sh
 
     def _routed(self, x: torch.Tensor, ctx: MoEContext | None, layer_idx: int) -> torch.Tensor:

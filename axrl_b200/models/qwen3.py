@@ -264,15 +264,79 @@ class DecoderLayer(nn.Module):
         else:
             self.mlp = MLP(cfg.hidden_size, cfg.intermediate_size // tp_size)
 
+    # selective recompute: submodules whose activations are recomputed in backward instead of
+    # stored (Megatron's recompute_modules); set by the model from its RecomputePolicy
+    selective: frozenset = frozenset()
+
+    def _sel(self, name: str, fn, *args):  # noqa: ANN001, ANN002, ANN202
+        if name in self.selective and torch.is_grad_enabled():
+            return checkpoint(fn, *args, use_reentrant=False)
+        return fn(*args)
+
     def forward(self, h: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, moe_ctx=None,  # noqa: ANN001
                 tp: TPContext = _NO_TP) -> torch.Tensor:
-        h = h + self.self_attn(self.input_layernorm(h), pos, inv_freq, spec, tp)
-        x = self.post_attention_layernorm(h)
+        h = h + self.self_attn(self._sel("layernorm", self.input_layernorm, h), pos, inv_freq, spec, tp)
+        x = self._sel("layernorm", self.post_attention_layernorm, h)
         if hasattr(self.mlp, "router"):
             if moe_ctx is not None and tp.enabled:
                 moe_ctx = moe_ctx.rows(tp.rank * x.shape[0], (tp.rank + 1) * x.shape[0])
-            return h + (self.mlp(x, moe_ctx, self.layer_idx) if moe_ctx is not None else self.mlp(x))
-        return h + self.mlp(x, tp)
+            if moe_ctx is not None:
+                return h + self._sel("moe", self.mlp, x, moe_ctx, self.layer_idx)
+            return h + self._sel("moe", self.mlp, x)
+        return h + self._sel("mlp", self.mlp, x, tp)
+
+
+SELECTIVE_MODULES = ("core_attn", "layernorm", "mlp", "moe", "shared_experts")
+
+
+@dataclass
+class RecomputePolicy:
+    """Activation recompute and host offload of the decoder stack (Megatron's recompute_* and
+    cpu_offloading* settings; reference ``axrl/configs.py:409-415``).
+
+    * ``granularity="full"``: a layer's activations are recomputed from its input in backward.
+      ``method="uniform"`` checkpoints groups of ``num_layers`` consecutive layers (default 1);
+      ``method="block"`` checkpoints the first ``num_layers`` layers of this stage and stores the
+      rest.
+    * ``granularity="selective"``: only the listed ``modules`` are recomputed.  ``core_attn`` needs
+      no extra work here: the attention kernels keep only the output and the log-sum-exp and always
+      recompute the scores in backward.  ``layernorm``, ``mlp``, ``moe`` and ``shared_experts``
+      recompute the norms, the dense MLP, the MoE block and the shared expert.
+    * ``offload_layers``: the activations saved by the first ``offload_layers`` layers (those not
+      recomputed) go to pinned host memory, on a side stream with ``offload_double_buffer``.
+    """
+
+    granularity: str | None = None
+    method: str | None = None
+    num_layers: int | None = None
+    modules: tuple[str, ...] = ("core_attn",)
+    offload_layers: int = 0
+    offload_double_buffer: bool = False
+
+    @classmethod
+    def from_worker_config(cls, cfg) -> "RecomputePolicy":  # noqa: ANN001
+        mods = tuple(cfg.recompute_modules) if cfg.recompute_modules else ("core_attn",)
+        bad = [m for m in mods if m not in SELECTIVE_MODULES]
+        if bad:
+            raise ValueError(f"recompute_modules {bad} are not supported (supported: {list(SELECTIVE_MODULES)})")
+        if cfg.recompute_granularity == "full" and cfg.recompute_method is None and cfg.recompute_num_layers not in (None, 1):
+            raise ValueError("recompute_num_layers needs recompute_method ('uniform' or 'block')")
+        if cfg.recompute_num_layers is not None and cfg.recompute_num_layers < (0 if cfg.recompute_method == "block" else 1):
+            raise ValueError(f"recompute_num_layers must be positive, got {cfg.recompute_num_layers}")
+        if cfg.cpu_offloading and cfg.cpu_offloading_num_layers < 1:
+            raise ValueError("cpu_offloading needs cpu_offloading_num_layers >= 1")
+        return cls(cfg.recompute_granularity, cfg.recompute_method, cfg.recompute_num_layers, mods,
+                   cfg.cpu_offloading_num_layers if cfg.cpu_offloading else 0, bool(cfg.cpu_offloading_double_buffering))
+
+    def groups(self, n_layers: int) -> list[tuple[int, int, bool]]:
+        """(start, end, checkpointed) ranges covering the stage's layers in order."""
+        if self.granularity != "full":
+            return [(i, i + 1, False) for i in range(n_layers)]
+        if self.method == "block":
+            k = n_layers if self.num_layers is None else min(self.num_layers, n_layers)
+            return [(i, i + 1, i < k) for i in range(n_layers)]
+        g = max(1, self.num_layers or 1)
+        return [(i, min(i + g, n_layers), True) for i in range(0, n_layers, g)]
 
 
 class _LayerDone:
@@ -281,6 +345,12 @@ class _LayerDone:
 
     def __call__(self, g: torch.Tensor) -> None:
         self.fn(self.idx)
+
+
+def _run_layers(layers, h, pos, inv, spec, moe_ctx, tp):  # noqa: ANN001, ANN201
+    for layer in layers:
+        h = layer(h, pos, inv, spec, moe_ctx, tp)
+    return h
 
 
 class Qwen3Model(nn.Module):
@@ -308,7 +378,7 @@ class Qwen3Model(nn.Module):
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps) if self.last else None
         self.lm_head = None if (cfg.tie_word_embeddings or not self.last) else nn.Parameter(torch.empty(V, cfg.hidden_size))
         self.register_buffer("inv_freq", ops.rope_inv_freq(cfg.rotary_dim, cfg.rope_theta), persistent=False)
-        self.recompute = False
+        self.policy = RecomputePolicy()
         self.grad_ready_hook = None  # set by an optimizer that reduces gradients during backward
         for layer in self.layers:
             layer.self_attn.cp = cp
@@ -371,20 +441,44 @@ class Qwen3Model(nn.Module):
         inv = self.inv_freq
         tp = self.tp
         hook = self.grad_ready_hook if torch.is_grad_enabled() else None
-        for layer in self.layers:
+        pol = self.policy
+        grad = torch.is_grad_enabled()
+        from axrl_b200.train.offload import offload_activations
+
+        for a, b, ckpt in pol.groups(len(self.layers)):
+            group = self.layers[a:b]
             if hook is not None and h.requires_grad:
-                # fires once the gradient of this layer's input exists, i.e. the layer's backward
-                # (weight gradients included) has been issued
-                h.register_hook(_LayerDone(hook, layer.layer_idx))
-            if self.recompute and torch.is_grad_enabled():
+                # fires once the gradient of the group's input exists, i.e. the backward of its
+                # layers (weight gradients included) has been issued
+                for layer in group:
+                    h.register_hook(_LayerDone(hook, layer.layer_idx))
+            if ckpt and grad:
                 ops.AttnStash.pushing = True  # the replay in backward reuses this forward's attention
                 try:
-                    h = checkpoint(layer, h, pos, inv, spec, moe_ctx, tp, use_reentrant=False)
+                    h = checkpoint(_run_layers, group, h, pos, inv, spec, moe_ctx, tp, use_reentrant=False)
                 finally:
                     ops.AttnStash.pushing = False
             else:
-                h = layer(h, pos, inv, spec, moe_ctx, tp)
+                with offload_activations(grad and a < pol.offload_layers, pol.offload_double_buffer):
+                    h = _run_layers(group, h, pos, inv, spec, moe_ctx, tp)
         return self.norm(h) if self.last else h
+
+    @property
+    def recompute(self) -> bool:
+        """Full per-layer recompute (the common setting); see :attr:`policy` for the others."""
+        return self.policy.granularity == "full"
+
+    @recompute.setter
+    def recompute(self, on: bool) -> None:
+        self.set_policy(RecomputePolicy("full") if on else RecomputePolicy())
+
+    def set_policy(self, policy: RecomputePolicy) -> None:
+        self.policy = policy
+        sel = frozenset(policy.modules) if policy.granularity == "selective" else frozenset()
+        for layer in self.layers:
+            layer.selective = sel
+            if hasattr(layer.mlp, "shared_selective"):
+                layer.mlp.shared_selective = "shared_experts" in sel
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         assert not self.tp.enabled, "full logits are a rollout-side (TP=1) operation"
@@ -577,6 +671,10 @@ class VirtualPipelineModel(nn.Module):
     def recompute(self, on: bool) -> None:
         for ch in self.chunks:
             ch.recompute = on
+
+    def set_policy(self, policy: RecomputePolicy) -> None:
+        for ch in self.chunks:
+            ch.set_policy(policy)
 
     @property
     def grad_ready_hook(self):  # noqa: ANN201

@@ -29,7 +29,6 @@ all-gathers them (NCCL).
 
 from __future__ import annotations
 
-import math
 from typing import Any
 
 import torch
@@ -136,9 +135,10 @@ class BucketedZeroAdamW:
         for b in buckets:
             self.shard_off.append(tot)
             tot += b["shard"]
-        self.master = torch.cat([self.bf16[b["s0"]:b["s0"] + b["shard"]].float() for b in buckets])
-        self.exp_avg = torch.zeros_like(self.master)
-        self.exp_avg_sq = torch.zeros_like(self.master)
+        from axrl_b200.train.offload import AdamState, offload_fraction
+
+        # fp32 master + moments of my shards; with optimizer_cpu_offload the tail fraction is on the host
+        self.state = AdamState(torch.cat([self.bf16[b["s0"]:b["s0"] + b["shard"]].float() for b in buckets]), offload_fraction(opt))
         self._sq = torch.zeros(1, dtype=torch.float32, device=dev)
         self.step_count = 0
         self.comm_stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
@@ -243,23 +243,18 @@ class BucketedZeroAdamW:
         o = self.opt
         lr = lr_at(self.step_count - 1, self.sched)
         e = _ext.ext() if self.device.type == "cuda" else None
+        p2p = self.backend == "p2p"
+        if p2p:
+            self._barrier(CH_PARAM)  # nobody reads parameters while they are rewritten
         for bi, b in enumerate(self.buckets):
             so, n = self.shard_off[bi], b["shard"]
-            m, g = self.master[so:so + n], self.grad[b["s0"]:b["s0"] + n]
-            ma, va = self.exp_avg[so:so + n], self.exp_avg_sq[so:so + n]
+            g = self.grad[b["s0"]:b["s0"] + n]
             dec = max(0, min(n, b["start"] + b["decay_n"] - b["s0"]))
-            if e is not None:
-                out = None if self.backend == "p2p" else self.bf16[b["s0"]:b["s0"] + n]
-                e.adamw_step(m, g, ma, va, out, dec, lr, o.adam_beta1, o.adam_beta2, o.adam_eps, o.weight_decay, self.step_count, sqnorm,
-                             float(o.clip_grad), float(grad_scale))
-            else:
-                _cpu_adamw(m, g, ma, va, dec, lr, o, self.step_count, sqnorm, grad_scale)
-                self.bf16[b["s0"]:b["s0"] + n].copy_(m)
-        if self.backend == "p2p":
-            self._barrier(CH_PARAM)  # nobody reads parameters while they are rewritten
-            for bi, b in enumerate(self.buckets):
-                so, n = self.shard_off[bi], b["shard"]
-                e.p2p_broadcast_shard(self.param_ptrs, self.master[so:so + n], b["s0"], n, self.world)
+            out = None if p2p else self.bf16[b["s0"]:b["s0"] + n]
+            m = self.state.step_range(so, n, g, out, dec, lr, o, self.step_count, sqnorm, grad_scale, need_master=p2p)
+            if p2p:  # the updated shard goes straight into every rank's parameters over NVLink
+                e.p2p_broadcast_shard(self.param_ptrs, m, b["s0"], n, self.world)
+        if p2p:
             self._barrier(CH_PARAM)
         else:
             for b in self.buckets:
@@ -277,15 +272,14 @@ class BucketedZeroAdamW:
     def state_dict(self) -> dict:
         """Sharded state: keys carry the DP rank so every rank saves its own slices."""
         r = self.rank
-        return {f"master.dp{r}": self.master, f"exp_avg.dp{r}": self.exp_avg, f"exp_avg_sq.dp{r}": self.exp_avg_sq,
+        st = self.state
+        return {f"master.dp{r}": st.master_full(), f"exp_avg.dp{r}": st.m_full(), f"exp_avg_sq.dp{r}": st.v_full(),
                 "step": self.step_count}
 
     @torch.no_grad()
     def load_state_dict(self, sd: dict) -> None:
         r = self.rank
-        self.master.copy_(sd[f"master.dp{r}"])
-        self.exp_avg.copy_(sd[f"exp_avg.dp{r}"])
-        self.exp_avg_sq.copy_(sd[f"exp_avg_sq.dp{r}"])
+        self.state.load(sd[f"master.dp{r}"], sd[f"exp_avg.dp{r}"], sd[f"exp_avg_sq.dp{r}"])
         self.step_count = int(sd.get("step", self.step_count))
 
     def check(self) -> None:
@@ -300,16 +294,3 @@ class _Null:
     def __exit__(self, *a: Any) -> None:
         return None
 
-
-def _cpu_adamw(m, g, ma, va, dec, lr, o, step, sqnorm, grad_scale) -> None:  # noqa: ANN001
-    norm = float(sqnorm.sqrt()) * grad_scale
-    gs = g * grad_scale
-    if o.clip_grad > 0:
-        gs = gs * min(1.0, o.clip_grad / (norm + 1e-6))
-    b1, b2 = o.adam_beta1, o.adam_beta2
-    ma.mul_(b1).add_(gs, alpha=1 - b1)
-    va.mul_(b2).addcmul_(gs, gs, value=1 - b2)
-    upd = (ma / (1 - b1 ** step)) / ((va / (1 - b2 ** step)).sqrt() + o.adam_eps)
-    upd[:dec] += o.weight_decay * m[:dec]
-    m.add_(upd, alpha=-lr)
-    _ = math

@@ -9,6 +9,13 @@ loop (``axrl/pipeline/controller.py:1617-1653``, rollout/train/sync of
 sampled freely (stop on EOS / max_new_tokens) or forced through EOS to a
 log-normal draw.
 
+Partial rollout (``partial_rollout=True``, the reference's streaming mode with carried-over
+trajectories, ``axrl/pipeline/controller.py`` partial rollout): a pool of ``inflight_prompts``
+groups stays in generation; a step ends its rollout phase as soon as ``num_prompts`` groups are
+complete, aborts the rest (they keep their partial responses) and trains on the completed groups.
+The aborted trajectories resume in the next step by re-prefilling prompt + partial response under
+the new weights, so the long tail of the response-length distribution never stalls a step.
+
 Colocated single-process mode: the rollout engine reads the trainer's bf16
 parameters directly (zero-copy weight sync — the "sync" is the version bump
 plus a prefix-cache flush).  ``separate_rollout_copy=True`` keeps an engine-
@@ -19,6 +26,7 @@ asks for).
 from __future__ import annotations
 
 import copy
+import dataclasses
 import time
 from dataclasses import dataclass, field
 
@@ -30,7 +38,7 @@ from axrl_b200.data.prefix_tree import merge_trajectory_samples
 from axrl_b200.data.sample import Sample, SampleBatch
 from axrl_b200.models.qwen3 import Qwen3Config
 from axrl_b200.pipeline.rewards import group_advantages
-from axrl_b200.rollout.engine import GenRequest, RolloutEngine
+from axrl_b200.rollout.engine import GenRequest, GenResult, RolloutEngine
 from axrl_b200.train.engine import TrainEngine
 from axrl_b200.trainer.grpo_trainer import GrpoTrainer
 from axrl_b200.utils import iostats
@@ -61,7 +69,27 @@ class SyntheticGRPOConfig:
     use_cuda_graph: bool = True
     kv_gb: float | None = None  # cap on the KV pool size
     kv_memory_saver: bool = True  # release the KV pool while training (same address on resume)
+    partial_rollout: bool = False  # keep unfinished groups in flight across steps
+    inflight_prompts: int | None = None  # groups in flight with partial rollout (default 2 x num_prompts)
     extra: dict = field(default_factory=dict)
+
+
+@dataclass
+class _Traj:
+    req: GenRequest  # the original request of this trajectory
+    out_ids: list[int] = field(default_factory=list)
+    out_lps: list[float] = field(default_factory=list)
+    done: bool = False
+    segments: int = 0  # rollout phases this trajectory took part in
+
+
+@dataclass
+class _Group:
+    members: list[_Traj]
+
+    @property
+    def done(self) -> bool:
+        return all(m.done for m in self.members)
 
 
 class SyntheticGRPO:
@@ -81,7 +109,10 @@ class SyntheticGRPO:
             rollout_model = copy.deepcopy(self.train.model)
             for p in rollout_model.parameters():
                 p.requires_grad_(False)
-        n_seq = sc.num_prompts * sc.group_size
+        self.pool: list[_Group] = []  # partial rollout: groups in flight
+        self._next_prompt = 0
+        inflight = (sc.inflight_prompts or 2 * sc.num_prompts) if sc.partial_rollout else sc.num_prompts
+        n_seq = inflight * sc.group_size
         max_ctx = sc.prompt_len + (sc.forced_len_max if sc.forced_len_median else sc.max_new_tokens) + 8
         kv_tokens = sc.kv_tokens or n_seq * (-(-max_ctx // 64) * 64)
         cuda = self.device.type == "cuda"
@@ -100,21 +131,22 @@ class SyntheticGRPO:
         self.last: dict = {}
 
     # ------------------------------------------------------------------ pieces
-    def make_requests(self) -> list[GenRequest]:
+    def _group_requests(self, p: int, tag: str) -> list[GenRequest]:
         sc, V = self.sc, self.mcfg.vocab_size
+        prompt = self.rng.integers(1, V, size=sc.prompt_len).tolist()
         reqs = []
-        for p in range(sc.num_prompts):
-            prompt = self.rng.integers(1, V, size=sc.prompt_len).tolist()
-            for g in range(sc.group_size):
-                forced = None
-                if sc.forced_len_median:
-                    forced = int(np.clip(np.exp(np.log(sc.forced_len_median) + sc.forced_len_sigma * self.rng.standard_normal()),
-                                         sc.forced_len_min, sc.forced_len_max))
-                rid = f"s{self.step_idx}-p{p}-g{g}"
-                reqs.append(GenRequest(rid=rid, prompt=prompt, max_new_tokens=forced or sc.max_new_tokens, temperature=sc.temperature,
-                                       stop_token_ids=() if forced else (sc.eos_token_id,), forced_len=forced,
-                                       forced_token=sc.eos_token_id, seed_stream=self.step_idx * 1_000_000 + p * 1000 + g))
+        for g in range(sc.group_size):
+            forced = None
+            if sc.forced_len_median:
+                forced = int(np.clip(np.exp(np.log(sc.forced_len_median) + sc.forced_len_sigma * self.rng.standard_normal()),
+                                     sc.forced_len_min, sc.forced_len_max))
+            reqs.append(GenRequest(rid=f"{tag}-p{p}-g{g}", prompt=prompt, max_new_tokens=forced or sc.max_new_tokens,
+                                   temperature=sc.temperature, stop_token_ids=() if forced else (sc.eos_token_id,), forced_len=forced,
+                                   forced_token=sc.eos_token_id, seed_stream=self.step_idx * 1_000_000 + p * 1000 + g))
         return reqs
+
+    def make_requests(self) -> list[GenRequest]:
+        return [r for p in range(self.sc.num_prompts) for r in self._group_requests(p, f"s{self.step_idx}")]
 
     def build_samples(self, reqs, results) -> tuple[list[Sample], dict]:  # noqa: ANN001
         sc = self.sc
@@ -122,7 +154,7 @@ class SyntheticGRPO:
         for r, res in zip(reqs, results):
             scores.append(1.0 if sc.reward_token in res.output_ids else 0.0)
         out: list[Sample] = []
-        for p in range(sc.num_prompts):
+        for p in range(len(reqs) // sc.group_size):
             grp = slice(p * sc.group_size, (p + 1) * sc.group_size)
             adv, mean, std = group_advantages(scores[grp])
             group_samples = []
@@ -147,11 +179,15 @@ class SyntheticGRPO:
         t = {}
         io0 = iostats.snapshot()
         t0 = time.perf_counter()
-        reqs = self.make_requests()
         with nvtx_range("rollout"):
-            self.rollout.acquire_kv()
-            results = self.rollout.generate(reqs)
-            self.rollout.release_kv()
+            if sc.partial_rollout:
+                reqs, results, pinfo = self._rollout_partial()
+            else:
+                reqs = self.make_requests()
+                self.rollout.acquire_kv()
+                results = self.rollout.generate(reqs)
+                self.rollout.release_kv()
+                pinfo = {}
         t["rollout_s"] = time.perf_counter() - t0
 
         t1 = time.perf_counter()
@@ -188,10 +224,61 @@ class SyntheticGRPO:
         io1 = iostats.snapshot()
         t["h2d_bytes"], t["d2h_bytes"] = io1[0] - io0[0], io1[1] - io0[1]
         trained_tokens = int(batch["seq_len"].sum())
-        out = {**metrics, **info, **t, "trained_tokens": trained_tokens, "num_samples": len(samples),
+        out = {**metrics, **info, **pinfo, **t, "trained_tokens": trained_tokens, "num_samples": len(samples),
                "sequences": len(results), "total_tokens": sum(len(r.prompt) + len(x.output_ids) for r, x in zip(reqs, results))}
         self.last = out
         return out
+
+    def _rollout_partial(self) -> tuple[list[GenRequest], list[GenResult], dict]:
+        """Streaming rollout phase: top the pool up, generate until ``num_prompts`` groups are
+        complete, abort the rest (partial responses kept) and return the completed groups."""
+        sc = self.sc
+        inflight = sc.inflight_prompts or 2 * sc.num_prompts
+        while len(self.pool) < inflight:
+            self.pool.append(_Group([_Traj(r) for r in self._group_requests(self._next_prompt, "q")]))
+            self._next_prompt += 1
+        live: dict[str, _Traj] = {}
+        reqs = []
+        resumed = 0
+        for g in self.pool:
+            for m in g.members:
+                if m.done:
+                    continue
+                r, n = m.req, len(m.out_ids)
+                rid = f"{r.rid}@{self.step_idx}"
+                resumed += n > 0
+                reqs.append(dataclasses.replace(r, rid=rid, prompt=list(r.prompt) + m.out_ids, max_new_tokens=max(1, r.max_new_tokens - n),
+                                                forced_len=None if r.forced_len is None else r.forced_len - n, gen_prefix=tuple(m.out_ids)))
+                live[rid] = m
+
+        def absorb(res: GenResult) -> None:
+            m = live.pop(res.rid)
+            m.out_ids += res.output_ids
+            m.out_lps += res.output_logprobs
+            m.segments += 1
+            if res.finish_reason != "abort":
+                m.done = True
+
+        self.rollout.acquire_kv()
+        self.rollout.add_requests(reqs)
+        while sum(g.done for g in self.pool) < sc.num_prompts and (self.rollout.waiting or self.rollout.running):
+            for res in self.rollout.step():
+                absorb(res)
+        aborted = 0
+        for res in self.rollout.abort_all():
+            aborted += 1
+            absorb(res)
+        self.rollout.release_kv()
+        take = [g for g in self.pool if g.done][:sc.num_prompts]
+        self.pool = [g for g in self.pool if not any(g is t for t in take)]
+        out_reqs, out_res = [], []
+        for g in take:
+            for m in g.members:
+                out_reqs.append(m.req)
+                out_res.append(GenResult(m.req.rid, m.out_ids, m.out_lps, "stop", len(m.req.prompt)))
+        info = {"groups_done": len(take), "resumed_trajectories": resumed, "aborted_trajectories": aborted,
+                "carried_groups": len(self.pool), "multi_segment_trajectories": sum(m.segments > 1 for g in take for m in g.members)}
+        return out_reqs, out_res, info
 
     def sync_weights(self) -> None:
         """Trainer -> rollout weight sync (in-process)."""

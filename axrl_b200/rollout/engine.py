@@ -229,7 +229,7 @@ class RolloutEngine:
         self.gdn_index = {li: i for i, li in enumerate(li for li in range(self.cfg.num_hidden_layers) if self.cfg.layer_is_linear(li))}
         self.gdn_free = list(range(B - 1, -1, -1))
         # the fused state-update kernel is opt-in until it has been validated on a B200
-        self.gdn_kernel = self.is_cuda and os.environ.get("AXRL_GDN_KERNEL", "0") == "1"
+        self.gdn_kernel = self.is_cuda and os.environ.get("AXRL_GDN_KERNEL", "1") == "1"
         if self.gdn_index:
             a = self.model.layers[next(iter(self.gdn_index))].self_attn
             n = len(self.gdn_index)

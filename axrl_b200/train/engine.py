@@ -22,6 +22,7 @@ import torch.distributed as dist
 from axrl_b200.configs import MegatronWorkerConfig
 from axrl_b200.data.sample import SampleBatch
 from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
+from axrl_b200.ops import _ext
 from axrl_b200.train.optimizer import FlatAdamW
 from axrl_b200.train.packing import PackedMicroBatch, pack_rows, split_balanced
 from axrl_b200.utils import iostats
@@ -89,7 +90,12 @@ class TrainEngine:
             model = model.to(device=self.device, dtype=dtype)
             model.inv_freq = model.inv_freq.float()
         self.model = model
-        self.model.recompute = cfg.recompute_granularity == "full"
+        from axrl_b200.models.qwen3 import RecomputePolicy
+
+        self.model.set_policy(RecomputePolicy.from_worker_config(cfg))
+        if self.device.type == "cuda":
+            # deterministic attention backward: dQ without atomics, fixed summation order
+            _ext.ext().set_attn_deterministic(bool(cfg.deterministic_mode))
         self.optim = None
         if not cfg.inference_only:
             dp_dist = (cfg.optimizer.use_distributed_optimizer and self.par.dp_group is not None and self.par.dp_size > 1

@@ -14,7 +14,10 @@ squared norm, one fused kernel clips + updates + writes the bf16 params back:
 no per-parameter launches and no host synchronisation.
 
 The grad buffer can be dropped between steps (:meth:`release_grads`) to make
-room for the rollout engine's KV cache when both share a GPU.
+room for the rollout engine's KV cache when both share a GPU.  With
+``optimizer_cpu_offload`` the tail ``optimizer_offload_fraction`` of the fp32
+state lives in pinned host memory and is updated on the CPU
+(:class:`axrl_b200.train.offload.AdamState`).
 """
 
 from __future__ import annotations
@@ -26,6 +29,7 @@ from torch import nn
 
 from axrl_b200.configs import MCoreLrSchedulerConfig, MCoreOptimizerConfig
 from axrl_b200.ops import _ext
+from axrl_b200.train.offload import AdamState, offload_fraction
 
 
 def lr_at(step: int, c: MCoreLrSchedulerConfig) -> float:
@@ -52,22 +56,35 @@ class FlatAdamW:
         dev = self.params[0].device
         self.device = dev
         self.bf16 = torch.empty(self.numel, dtype=self.params[0].dtype, device=dev)  # parameter storage (bf16 on GPU)
-        self.master = torch.empty(self.numel, dtype=torch.float32, device=dev)
+        master = torch.empty(self.numel, dtype=torch.float32, device=dev)
         off = 0
         self.offsets = []
         for p in self.params:
             n = p.numel()
-            self.master[off:off + n].copy_(p.detach().reshape(-1).float())
+            master[off:off + n].copy_(p.detach().reshape(-1).float())
             self.bf16[off:off + n].copy_(p.detach().reshape(-1))
             p.data = self.bf16[off:off + n].view(p.shape)
             self.offsets.append(off)
             off += n
-        self.exp_avg = torch.zeros_like(self.master)
-        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.state = AdamState(master, offload_fraction(opt))
+        del master
         self.grad: torch.Tensor | None = None
         self.step_count = 0
         self.alloc_grads()
         self._sq = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    # device-resident state (the whole state unless part of it is offloaded to the host)
+    @property
+    def master(self) -> torch.Tensor:
+        return self.state.dev_master
+
+    @property
+    def exp_avg(self) -> torch.Tensor:
+        return self.state.dev_m
+
+    @property
+    def exp_avg_sq(self) -> torch.Tensor:
+        return self.state.dev_v
 
     # -------------------------------------------------------------- grads
     def alloc_grads(self) -> None:
@@ -116,42 +133,21 @@ class FlatAdamW:
         if sqnorm is None:
             sqnorm = self.grad_sqnorm()
         norm = sqnorm.sqrt() * grad_scale
-        if self.grad.is_cuda:
-            _ext.ext().adamw_step(self.master, self.grad, self.exp_avg, self.exp_avg_sq, self.bf16, self.decay_end, lr,
-                                  o.adam_beta1, o.adam_beta2, o.adam_eps, wd, self.step_count, sqnorm, float(o.clip_grad),
-                                  float(grad_scale))
-        else:
-            self._cpu_step(lr, grad_scale, norm)
+        self.state.step_range(0, self.numel, self.grad, self.bf16, self.decay_end, lr, o, self.step_count, sqnorm, grad_scale)
         return norm
-
-    def _cpu_step(self, lr: float, grad_scale: float, norm: torch.Tensor) -> None:
-        o = self.opt
-        g = self.grad * grad_scale
-        if o.clip_grad > 0:
-            g = g * torch.clamp(o.clip_grad / (norm + 1e-6), max=1.0)
-        b1, b2 = o.adam_beta1, o.adam_beta2
-        self.exp_avg.mul_(b1).add_(g, alpha=1 - b1)
-        self.exp_avg_sq.mul_(b2).addcmul_(g, g, value=1 - b2)
-        bc1 = 1 - b1 ** self.step_count
-        bc2 = 1 - b2 ** self.step_count
-        upd = (self.exp_avg / bc1) / ((self.exp_avg_sq / bc2).sqrt() + o.adam_eps)
-        upd[: self.decay_end] += o.weight_decay * self.master[: self.decay_end]
-        self.master.add_(upd, alpha=-lr)
-        self.bf16.copy_(self.master)
 
     # -------------------------------------------------------------- state
     def state_dict(self) -> dict:
-        return {"master": self.master, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq, "step": self.step_count}
+        st = self.state
+        return {"master": st.master_full(), "exp_avg": st.m_full(), "exp_avg_sq": st.v_full(), "step": self.step_count}
 
     @torch.no_grad()
     def load_state_dict(self, sd: dict) -> None:
-        self.master.copy_(sd["master"])
-        self.exp_avg.copy_(sd["exp_avg"])
-        self.exp_avg_sq.copy_(sd["exp_avg_sq"])
+        self.state.load(sd["master"], sd["exp_avg"], sd["exp_avg_sq"])
         self.step_count = int(sd["step"])
-        self.bf16.copy_(self.master)
+        self.bf16.copy_(sd["master"].reshape(-1).to(self.bf16.device))
 
     @torch.no_grad()
     def sync_master_from_params(self) -> None:
         """After loading weights into the bf16 params, refresh the fp32 masters."""
-        self.master.copy_(self.bf16.float())
+        self.state.load(self.bf16.float())

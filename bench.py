@@ -1,10 +1,14 @@
 """GRPO step benchmark: Qwen3-8B-shaped dense model, colocated rollout + trainer, bf16, random init.
 
-Workload per GPU (weak scaling: 8 GPUs = the full 256-prompt batch):
-  32 prompts x 512 uniform-random token ids, group size 8 (256 sequences);
-  response lengths forced through EOS to a log-normal draw (median 1024,
-  sigma 1.0, clipped to [16, 8192]); reward = 1 if token 7 appears;
-  ref + old logprob recompute, one optimizer step (AdamW, fp32 master), weight sync.
+Workload per GPU (weak scaling):
+  prompts of 512 uniform-random token ids, group size 8; response lengths forced
+  through EOS to a log-normal draw (median 1024, sigma 1.0, clipped to [16, 8192]);
+  reward = 1 if token 7 appears; ref + old logprob recompute, one optimizer step
+  (AdamW, fp32 master, ZeRO over the data-parallel ranks), colocated weight sync.
+  Streaming partial rollout: `--inflight-per-gpu` groups stay in generation and a
+  step trains the first `--prompts-per-gpu` groups to complete; unfinished groups
+  keep their partial responses and resume after the weight update, so a step's
+  rollout is bounded by throughput rather than by the longest response.
 Metric: trained tokens per second for the whole job (prompt + response tokens of
 every sequence trained in the step, summed over ranks) and seconds per GRPO step.
 
@@ -36,7 +40,9 @@ def _args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", default="qwen3-8b")
-    ap.add_argument("--prompts-per-gpu", type=int, default=32)
+    ap.add_argument("--prompts-per-gpu", type=int, default=4, help="groups trained per step per GPU")
+    ap.add_argument("--inflight-per-gpu", type=int, default=8, help="groups kept in generation per GPU (partial rollout)")
+    ap.add_argument("--no-partial", action="store_true", help="every step generates its own groups to completion")
     ap.add_argument("--group", type=int, default=8)
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--median", type=float, default=1024.0)
@@ -154,7 +160,8 @@ def main() -> None:
     sc = SyntheticGRPOConfig(num_prompts=a.prompts_per_gpu, prompt_len=a.prompt_len, group_size=a.group, temperature=1.0,
                              forced_len_median=a.median, forced_len_sigma=1.0, forced_len_min=16, forced_len_max=a.max_len,
                              eos_token_id=151645 % mcfg.vocab_size, merge_group_prompts=False, compute_ref_logprobs=not a.no_ref,
-                             seed=1000 + rank, use_cuda_graph=True, kv_gb=kv_gb, kv_memory_saver=True)
+                             seed=1000 + rank, use_cuda_graph=True, kv_gb=kv_gb, kv_memory_saver=True,
+                             partial_rollout=not a.no_partial, inflight_prompts=a.inflight_per_gpu)
     pipe = SyntheticGRPO(mcfg, wc, grpo, sc, dev, train_engine=train)
 
     def barrier() -> None:
@@ -191,7 +198,9 @@ def main() -> None:
     clk = clocks.stop()
     dev_ms = start.elapsed_time(end)
 
-    t = torch.tensor([dev_ms, wall, float(tokens), float(launches)], dtype=torch.float64, device=dev)
+    phases = ("rollout_s", "logprob_s", "train_s", "sync_s", "pack_s")
+    ph = [sum(m.get(k, 0.0) for m in step_metrics) / len(step_metrics) for k in phases]
+    t = torch.tensor([dev_ms, wall, float(tokens), float(launches), *ph], dtype=torch.float64, device=dev)
     if world > 1:
         mx = t.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
@@ -199,6 +208,7 @@ def main() -> None:
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
         dev_ms, wall = float(mx[0]), float(mx[1])
         tokens_all, launches_all = float(tot[2]), float(tot[3])
+        ph = [float(x) for x in mx[4:]]
     else:
         tokens_all, launches_all = float(tokens), float(launches)
     ms_step = dev_ms / a.steps
@@ -223,13 +233,16 @@ def main() -> None:
             "dtype": "bf16",
             "data": "synthetic (uniform-random prompt ids, random-init weights, forced log-normal response lengths)",
             "config": {"model": f"{a.model} shape (36L, h4096, 32q/8kv, d128, ffn12288, vocab151936)" if a.model == "qwen3-8b" else a.model,
-                       "global_batch": a.prompts_per_gpu * a.group * world, "prompts": a.prompts_per_gpu * world, "group_size": a.group,
+                       "global_batch": a.prompts_per_gpu * a.group * world, "prompts_per_step": a.prompts_per_gpu * world,
+                       "group_size": a.group, "partial_rollout": not a.no_partial,
+                       "inflight_groups": (a.inflight_per_gpu if not a.no_partial else a.prompts_per_gpu) * world,
                        "seq_len": a.prompt_len + a.max_len, "prompt_len": a.prompt_len,
                        "response_len": f"lognormal(median {a.median:g}, sigma 1) clipped [16,{a.max_len}]",
                        "micro_batch_tokens": a.mb_tokens, "parallelism": f"dp{world}" + (f"ep{ep}" if ep > 1 else ""), "colocated": True,
                        "ref_logprobs": not a.no_ref, "kv_pool_gb": round(kv_gb, 1), "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
             "sync_s": round(sum(m["sync_s"] for m in step_metrics) / len(step_metrics), 4),
-            "step_breakdown_s": {k: round(last[k], 2) for k in ("rollout_s", "logprob_s", "train_s", "sync_s", "pack_s") if k in last},
+            "step_breakdown_s": {k: round(v, 3) for k, v in zip(phases, ph)},
+            "step_breakdown_note": "wall seconds per step, mean over the timed steps, max over ranks",
             "e2e": {"value": round(e2e, 1), "unit": "trained tokens/s (wall clock through SyntheticGRPO.run_step)",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches_all),

@@ -195,6 +195,59 @@ def test_recompute_reuses_attention_and_matches_plain_backward():
     assert core.AttnStash.pushing is False
 
 
+def test_recompute_policies_and_activation_offload_on_gpu():
+    """Grouped / block / selective recompute and pinned-host activation offload (with and without
+    the side-stream double buffer) give the gradients of plain backward."""
+    from axrl_b200.models.qwen3 import RecomputePolicy
+    from axrl_b200.ops.attention_spec import causal_spec_from_cu_seqlens
+
+    torch.manual_seed(0)
+    T = 512
+    ids = torch.randint(0, 2048, (T,), device="cuda")
+    labels = torch.randint(0, 2048, (T,), device="cuda")
+    pos = torch.cat([torch.arange(200), torch.arange(312)]).int().cuda()
+    spec = causal_spec_from_cu_seqlens([0, 200, 512]).to("cuda")
+    policies = [RecomputePolicy(), RecomputePolicy("full", "uniform", 2), RecomputePolicy("full", "block", 1),
+                RecomputePolicy("selective", modules=("core_attn", "layernorm", "mlp")), RecomputePolicy(offload_layers=2),
+                RecomputePolicy(offload_layers=1, offload_double_buffer=True)]
+    grads = []
+    for pol in policies:
+        m = _model(5)
+        m.train()
+        m.set_policy(pol)
+        lp, _ = m.logprobs(m(ids, pos, spec), labels)
+        lp.float().sum().backward()
+        torch.cuda.synchronize()
+        grads.append({k: p.grad.float().clone() for k, p in m.named_parameters() if p.grad is not None})
+    for pol, gr in zip(policies[1:], grads[1:]):
+        for k, g in grads[0].items():
+            rel = ((gr[k] - g).norm() / (g.norm() + 1e-12)).item()
+            assert rel < 1e-2, f"{pol}: {k}: {rel}"
+
+
+def test_optimizer_state_offload_on_gpu_matches_device_state():
+    """The tail of the fp32 optimizer state in pinned host memory, updated on the CPU, tracks the
+    fused device update (same parameters after three steps, within bf16 rounding)."""
+    from axrl_b200.configs import MCoreLrSchedulerConfig, MCoreOptimizerConfig
+    from axrl_b200.train.optimizer import FlatAdamW
+
+    sched = MCoreLrSchedulerConfig(lr_warmup_steps=0, max_lr=1e-3)
+    outs = []
+    for frac in (0.0, 0.4):
+        m = _model(7)
+        opt = FlatAdamW(m, MCoreOptimizerConfig(lr=1e-3, optimizer_cpu_offload=frac > 0, optimizer_offload_fraction=frac), sched)
+        assert opt.state.offloaded == round(opt.numel * frac)
+        for step in range(3):
+            opt.zero_grad()
+            g = torch.Generator(device="cuda").manual_seed(step)
+            opt.grad.copy_(torch.randn(opt.numel, device="cuda", generator=g))
+            opt.step()
+        torch.cuda.synchronize()
+        outs.append((opt.bf16.float().clone(), opt.state.master_full().float().cpu()))
+    assert (outs[0][0] - outs[1][0]).abs().max().item() <= 2 ** -7 * outs[0][0].abs().max().item()
+    torch.testing.assert_close(outs[1][1], outs[0][1], rtol=1e-5, atol=1e-6)
+
+
 def test_qwen35_style_hybrid_on_gpu_matches_fp32_and_rollout():
     """Gated attention output, zero-centered norms, Gated DeltaNet layers and a shared expert on the GPU
     path (head dim 128, full rotary: the shapes the GPU kernels cover): bf16 trainer log-probs track

@@ -535,7 +535,6 @@ def test_attention_tcgen05_forward_matches_reference(case, double_p):
     close(lse[fin], lse2[fin], 1e-3, 1e-4, msg="lse")
 
 
-@pytest.mark.skipif(os.environ.get("AXRL_TEST_ATTN_BWD_TC") != "1", reason="tcgen05 backward: opt-in until validated on a B200")
 @pytest.mark.parametrize("case", [0, 1, 2, 3])
 def test_attention_tcgen05_backward_matches_mma(case):
     """tcgen05 backward (attention_tc_bwd.cu) against the mma.sync backward on the same inputs:
@@ -557,19 +556,18 @@ def test_attention_tcgen05_backward_matches_mma(case):
     do = torch.randn(T, hq, D, device=DEV).bfloat16()
     scale = 1 / math.sqrt(D)
     o, lse = e.attn_fwd_mma(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
-    ref = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
-    e.set_attn_bwd_tc(True)
+    e.set_attn_bwd_tc(False)
     try:
-        got = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
+        ref = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
     finally:
-        e.set_attn_bwd_tc(False)
+        e.set_attn_bwd_tc(True)
+    got = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
     torch.cuda.synchronize()
     assert e.attn_bwd_tc_error() == 0
     for name, a, b in zip(("dq", "dk", "dv"), got, ref):
         close(a, b, 3e-2, 2e-2, msg=name)
 
 
-@pytest.mark.skipif(os.environ.get("AXRL_TEST_ATTN_DET") != "1", reason="deterministic dQ kernel: opt-in until validated on a B200")
 @pytest.mark.parametrize("case", [0, 1, 2])
 def test_attention_deterministic_dq(case):
     """Deterministic mode: dQ from one CTA per q tile (no atomics) equals the atomic path and is
@@ -598,7 +596,6 @@ def test_attention_deterministic_dq(case):
         close(x, y, 2e-2, 1e-2, msg=name)
 
 
-@pytest.mark.skipif(os.environ.get("AXRL_TEST_GDN_KERNEL") != "1", reason="GDN state-update kernel: opt-in until validated on a B200")
 def test_gdn_step_kernel_matches_reference():
     from axrl_b200.models.gdn import gated_delta_step
 

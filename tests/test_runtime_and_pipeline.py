@@ -149,3 +149,34 @@ def test_engine_constrained_and_penalised_requests():
     out = res["norepeat"].output_ids
     assert len(out) == 20 and len(set(out)) == 20  # greedy with a huge presence penalty never repeats
     assert len(res["plain"].output_ids) == 6
+
+
+def test_partial_rollout_carries_unfinished_groups_across_steps():
+    """Streaming rollout: each step trains exactly the first `num_prompts` groups to complete; the
+    rest keep their partial responses, resume after the weight update, and finish with exactly the
+    forced length (so trajectories that spanned several rollout phases are stitched correctly)."""
+    from axrl_b200.configs import GrpoTrainerConfig, MegatronWorkerConfig
+    from axrl_b200.models.qwen3 import resolve_preset
+    from axrl_b200.pipeline.grpo_step import SyntheticGRPO, SyntheticGRPOConfig
+
+    torch.manual_seed(0)
+    wc = MegatronWorkerConfig()
+    wc.lr_scheduler.lr_warmup_steps = 0
+    g = GrpoTrainerConfig(loss_type="grpo", mismatch_token_clip_max=2.0)
+    sc = SyntheticGRPOConfig(num_prompts=2, prompt_len=16, group_size=4, forced_len_median=12, forced_len_sigma=1.2,
+                             forced_len_min=2, forced_len_max=80, partial_rollout=True, inflight_prompts=5, seed=3,
+                             separate_rollout_copy=True, use_cuda_graph=False)
+    pipe = SyntheticGRPO(resolve_preset("tiny"), wc, g, sc, "cpu")
+    seen_multi = 0
+    for _ in range(4):
+        m = pipe.run_step()
+        assert m["groups_done"] == 2 and m["sequences"] == 8
+        assert m["carried_groups"] == 3
+        seen_multi += m["multi_segment_trajectories"]
+        assert np.isfinite(m["loss"])
+    assert seen_multi > 0, "no trajectory spanned two rollout phases"
+    # every trajectory still in flight holds a consistent partial state
+    for grp in pipe.pool:
+        for t in grp.members:
+            assert len(t.out_ids) == len(t.out_lps) <= t.req.forced_len
+            assert t.done == (len(t.out_ids) == t.req.forced_len)
