@@ -69,6 +69,13 @@ class PipelineController:
         mcfg = self.model_cfg or resolve_preset(c.megatron_worker.model.name)
         self.train = TrainEngine(c.megatron_worker, mcfg, self.device)
         self.trainer = GrpoTrainer(c.grpo)
+        self.value = self.value_trainer = None
+        self.value_step = 0
+        if c.value_worker is not None and self.is_ppo_training():
+            from axrl_b200.trainer.value_trainer import ValueTrainer
+
+            self.value = TrainEngine(c.value_worker, mcfg, self.device)  # the critic starts from the same architecture
+            self.value_trainer = ValueTrainer(c.grpo.ppo_value)
         rw = c.rollout_worker
         max_ctx = c.train_sampling_config.max_total_tokens
         kv_tokens = int(rw.max_running_requests * (max_ctx + 128))
@@ -87,6 +94,7 @@ class PipelineController:
             a.start()
 
     def check_configs(self) -> None:
+        self.check_ppo_value_configs(self.config)
         o = self.config.online_rl_train
         if o.strict_on_policy:
             assert o.model_sync_every_n_global_updates == 1 and o.batch_rollout_for_n_global_updates == 1, \
@@ -96,6 +104,52 @@ class PipelineController:
         if o.checkpoint_every_n_global_updates:
             assert o.checkpoint_every_n_global_updates % o.model_sync_every_n_global_updates == 0, \
                 "checkpoint cadence must be a multiple of the model-sync cadence"
+
+    @staticmethod
+    def check_ppo_value_configs(c: PipelineExperimentConfig) -> None:
+        """PPO needs a critic whose layout matches the actor (reference
+        ``axrl/pipeline/controller.py:152-200``)."""
+        g, actor, value = c.grpo, c.megatron_worker, c.value_worker
+
+        def need(ok: bool, msg: str) -> None:
+            if not ok:
+                raise ValueError(msg)
+
+        if g.loss_type == "ppo" or g.ppo_value is not None:
+            need(c.controller.run_mode == "online_rl_train", "PPO with a value worker runs in controller.run_mode='online_rl_train' only")
+        if g.loss_type == "ppo":
+            need(g.ppo_value is not None, "grpo.loss_type='ppo' requires grpo.ppo_value")
+            need(value is not None, "grpo.loss_type='ppo' requires value_worker")
+            need(value.model_role == "value", "PPO value_worker.model_role must be 'value'")
+            need(actor.model_role == "actor", "PPO megatron_worker.model_role must be 'actor'")
+            need(value.world_size() == actor.world_size(),
+                 f"PPO value_worker world_size ({value.world_size()}) must match the actor's ({actor.world_size()})")
+            need(value.model.seq_length == actor.model.seq_length, "PPO value_worker seq_length must match the actor's")
+            need(value.checkpoint_dir != actor.checkpoint_dir, "PPO actor and value workers need different checkpoint_dir values")
+            need(g.is_base_logprobs == "old_logprobs", "the PPO actor loss uses old_logprobs as the policy-ratio base")
+        if g.ppo_value is not None:
+            need(g.loss_type == "ppo", "grpo.ppo_value is only supported with grpo.loss_type='ppo'")
+            need(value is not None, "grpo.ppo_value requires value_worker")
+            need(not g.ppo_value.use_stateless_value_model, "grpo.ppo_value.use_stateless_value_model is not implemented")
+
+    def is_ppo_training(self) -> bool:
+        return self.config.grpo.loss_type == "ppo"
+
+    def prepare_ppo_training_samples(self, b: SampleBatch) -> None:
+        """Critic predictions before its update (``old_values``), terminal-token rewards, token-level
+        GAE -> per-token advantages and returns (reference ``controller.py:1310-1339``)."""
+        from axrl_b200.trainer.ppo_utils import build_terminal_token_rewards, compute_gae, normalize_over_valid_tokens_in_batch
+
+        pv = self.config.grpo.ppo_value
+        old_values = self.value.compute_values(b).float()
+        lm = b["loss_mask"].bool()
+        rewards = build_terminal_token_rewards(b["reward"].float(), lm)
+        adv, ret = compute_gae(rewards, old_values, lm, gamma=pv.gamma, gae_lambda=pv.gae_lambda)
+        if self.config.grpo.normalize_advantages_over_valid_tokens_in_batch:
+            adv = normalize_over_valid_tokens_in_batch(adv, lm)
+        b["old_values"] = old_values
+        b["returns"] = ret
+        b["advantage"] = adv.to(b["advantage"].dtype)
 
     # ------------------------------------------------------------------ entry
     async def start(self) -> dict:
@@ -257,7 +311,19 @@ class PipelineController:
             b["old_logprobs"] = self.train.compute_logprobs(b, c.train_sampling_config.temperature)
             if "ref_logprobs" not in b.tensors:
                 b["ref_logprobs"] = b["old_logprobs"]
-            m = self.train.train_step(b, self.trainer, temperature=c.train_sampling_config.temperature)
+            m: dict = {}
+            if self.is_ppo_training():
+                t0 = time.time()
+                self.prepare_ppo_training_samples(b)
+                vm = self.value.train_step(b, self.value_trainer)
+                self.value_step += 1
+                m.update({f"value/{k}": v for k, v in vm.items() if isinstance(v, (int, float))})
+                m["timing/value_train_seconds"] = time.time() - t0
+                if self.value_step <= c.grpo.ppo_value.num_value_only_updates:
+                    m["actor_trained"] = 0.0  # value-only warmup: the critic learns before the actor moves
+                    out.append(m)
+                    continue
+            m.update(self.train.train_step(b, self.trainer, temperature=c.train_sampling_config.temperature))
             self.global_step += 1
             m["global_step"] = self.global_step
             out.append(m)

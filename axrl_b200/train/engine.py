@@ -90,6 +90,17 @@ class TrainEngine:
             model = model.to(device=self.device, dtype=dtype)
             model.inv_freq = model.inv_freq.float()
         self.model = model
+        self.role = cfg.model_role
+        if self.role == "value":
+            # PPO critic: the decoder stack with a scalar value head instead of the LM head
+            # (reference axrl/utils/megatron/value_head.py).  The LM head is not trained.
+            if self.tp.enabled or self.pp.enabled or self.cp.enabled:
+                raise ValueError("the value model runs with tp_size = pp_size = cp_size = 1")
+            from axrl_b200.trainer.value_trainer import ValueHead
+
+            self.model.value_head = ValueHead(model_cfg.hidden_size).to(device=self.device, dtype=dtype)
+            if getattr(self.model, "lm_head", None) is not None:
+                self.model.lm_head.requires_grad_(False)
         from axrl_b200.models.qwen3 import RecomputePolicy
 
         self.model.set_policy(RecomputePolicy.from_worker_config(cfg))
@@ -157,6 +168,23 @@ class TrainEngine:
             t = out.to(self.device)
             dist.all_reduce(t, group=self.cp.group)
             out = t.cpu()
+        return out
+
+    @torch.no_grad()
+    def compute_values(self, batch: SampleBatch) -> torch.Tensor:
+        """Value-role engine: V(state) at every label position in the batch's (B, S) layout (0 where
+        the label is ignored), the critic predictions PPO's GAE bootstraps from."""
+        assert self.role == "value", "compute_values needs model_role='value'"
+        self.model.eval()
+        B, S = batch["input_ids"].shape
+        out = torch.zeros((B, S), dtype=torch.float32)
+        for mb in self.micro_batches(batch):
+            dmb = mb.to(self.device)
+            v = self.model.value_head(self._hidden(dmb))
+            v = torch.where(dmb.labels >= 0, v, torch.zeros_like(v))
+            dense = dmb.unpack(v.float(), S).cpu()
+            for li, r in enumerate(mb.rows):
+                out[r] += dense[li]
         return out
 
     def _act_shape(self, mb: PackedMicroBatch) -> tuple:
@@ -229,6 +257,17 @@ class TrainEngine:
         for i, mb in enumerate(mbs if not self.pp.enabled else []):
             dmb = mb.to(self.device)
             h = self._hidden(dmb)
+            if self.role == "value":  # clipped value loss on the critic's predictions
+                v = self.model.value_head(h)
+                sub = batch.select_rows(mb.rows).to(self.device)
+                want = metrics_every_micro_batch or i == len(mbs) - 1
+                loss, denom, m = trainer.loss_func({"values": dmb.unpack(v, S)}, sub, with_metrics=want)
+                if i == len(mbs) - 1 and hasattr(self.optim, "arm"):
+                    self.optim.arm()
+                (loss * denom.to(loss.dtype)).backward()
+                if want:
+                    metrics_acc.append(m)
+                continue
             ec = getattr(trainer.config, "entropy_control", None)
             lp, ent = self.model.logprobs(h, dmb.labels.clamp(min=-1), temperature, entropy=need_entropy,
                                           entropy_top_k=max(0, ec.top_k) if ec is not None else 0)

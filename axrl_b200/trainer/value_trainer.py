@@ -25,6 +25,10 @@ class ValueTrainer(BaseTrainer):
     def __init__(self, config: PPOValueConfig) -> None:
         self.config = config
 
+    def compute_micro_batch_denominator(self, mask, num_turns: int = 0):  # noqa: ANN001, ANN201
+        """The value loss is a token mean over loss tokens."""
+        return denominator_count(mask, "token-mean")
+
     def loss_func(self, outputs: dict, batch, with_metrics: bool = True):  # noqa: ANN001, ANN201
         values = outputs["values"]
         m = batch["loss_mask"].bool()
@@ -36,7 +40,8 @@ class ValueTrainer(BaseTrainer):
             def agg(v, mode):  # noqa: ANN001, ANN202
                 return float(aggregate_with_mask(v.float(), m, mode)) if m.any() else 0.0
 
-            metrics = {"loss": float(loss), "value_loss": float(loss), "denom": float(denom), "num_samples": float(values.shape[0]),
+            lv = float(loss.detach())
+            metrics = {"loss": lv, "value_loss": lv, "denom": float(denom), "num_samples": float(values.shape[0]),
                        "value_mean": agg(values, "token-mean"), "value_std": agg(values, "token-std"),
                        "return_mean": agg(batch["returns"], "token-mean"), "return_std": agg(batch["returns"], "token-std")}
             if clipfrac is not None:

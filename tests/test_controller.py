@@ -136,3 +136,81 @@ def test_checkpoint_save_and_resume(tmp_path):
     assert ctl2.global_step == 2
     for n, p in ctl2.train.model.named_parameters():
         torch.testing.assert_close(p, params[n])
+
+
+def _ppo_config():
+    from axrl_b200.configs import MegatronWorkerConfig, PPOValueConfig
+    from axrl_b200.pipeline.config import PipelineExperimentConfig
+
+    c = PipelineExperimentConfig()
+    c.megatron_worker.global_batch_size = 8
+    c.megatron_worker.model.seq_length = 256
+    c.online_rl_train.num_rollouts_per_conversation = 4
+    c.online_rl_train.model_sync_every_n_global_updates = 1
+    c.online_rl_train.batch_rollout_for_n_global_updates = 2
+    c.online_rl_train.max_global_updates = 2
+    c.online_rl_train.checkpoint_every_n_global_updates = None
+    c.train_sampling_config.max_new_tokens = 24
+    c.train_sampling_config.max_total_tokens = 96
+    c.rollout_worker.max_running_requests = 16
+    c.controller.max_running_requests = 16
+    c.grpo.loss_type = "ppo"
+    c.grpo.ppo_value = PPOValueConfig(gamma=1.0, gae_lambda=0.95, num_value_only_updates=1)
+    c.value_worker = MegatronWorkerConfig(model_role="value", checkpoint_dir="checkpoints/value", seed=7)
+    c.value_worker.model.seq_length = 256
+    c.value_worker.lr_scheduler.lr_warmup_steps = 0
+    return c
+
+
+def test_ppo_with_value_worker_tiny_cpu():
+    """PPO through the controller: the critic predicts old values, terminal rewards -> GAE give
+    per-token advantages and returns, the critic trains with the clipped value loss, and the actor
+    waits for the value-only warmup update before it trains."""
+    from axrl_b200.models.qwen3 import resolve_preset
+    from axrl_b200.pipeline.controller import PipelineController
+    from axrl_b200.recipe.synthetic_recipe import SyntheticTokenRecipe
+
+    torch.manual_seed(0)
+    c = _ppo_config()
+    recipe = SyntheticTokenRecipe(c, num_prompts=8, prompt_len=16)
+    ctl = PipelineController(c, recipe, device="cpu", model_cfg=resolve_preset("tiny"))
+    ctl.train_dataset = recipe.dataset
+    seen = {}
+    orig = ctl.prepare_ppo_training_samples
+
+    def spy(b):
+        orig(b)
+        # the last batch: the critic has been updated, so its values are no longer the zero init
+        seen["adv"], seen["ret"], seen["mask"] = b["advantage"].clone(), b["returns"].clone(), b["loss_mask"].bool().clone()
+
+    ctl.prepare_ppo_training_samples = spy
+    asyncio.run(ctl.start())
+    assert ctl.global_step == 2 and ctl.value_step == 3  # one value-only warmup update, then both train
+    m = seen["mask"]
+    assert torch.isfinite(seen["adv"]).all() and (seen["adv"][~m] == 0).all()
+    # per-token advantages vary along a response (GAE over the critic's values), unlike GRPO's constant
+    rows = [r for r in range(m.shape[0]) if m[r].sum() > 2]
+    assert any(seen["adv"][r][m[r]].unique().numel() > 1 for r in rows)
+    vw = ctl.value.model.value_head.weight
+    assert vw.abs().sum() > 0  # the critic's head moved away from its zero init
+
+
+def test_ppo_config_checks():
+    import pytest
+
+    from axrl_b200.pipeline.controller import PipelineController
+
+    c = _ppo_config()
+    PipelineController.check_ppo_value_configs(c)
+    bad = _ppo_config()
+    bad.value_worker.model_role = "actor"
+    with pytest.raises(ValueError, match="model_role"):
+        PipelineController.check_ppo_value_configs(bad)
+    bad = _ppo_config()
+    bad.value_worker.checkpoint_dir = bad.megatron_worker.checkpoint_dir
+    with pytest.raises(ValueError, match="checkpoint_dir"):
+        PipelineController.check_ppo_value_configs(bad)
+    bad = _ppo_config()
+    bad.grpo.loss_type = "grpo"
+    with pytest.raises(ValueError, match="ppo_value"):
+        PipelineController.check_ppo_value_configs(bad)
