@@ -29,7 +29,7 @@ import numpy as np
 import torch
 
 from axrl_b200.data.sample import SampleBatch
-from axrl_b200.metrics.response_metric import aggregate_response_metrics
+from axrl_b200.metrics.response_metric import aggregate_response_metrics, aggregate_response_metrics_by_subset
 from axrl_b200.pipeline.config import PipelineExperimentConfig
 from axrl_b200.pipeline.rewards import group_advantages
 from axrl_b200.pipeline.rollout_actor import RolloutActor, RolloutRuntime
@@ -408,6 +408,9 @@ class PipelineController:
             dt = time.time() - t0
             m = aggregate_response_metrics([r.metric for r in results], f"eval_{name}", dt)
             m[f"eval_{name}/eval_time_sec"] = dt
+            subset_key = getattr(getattr(ds, "config", None), "subset_key", None) or getattr(ds, "subset_key", None)
+            if subset_key:  # per-subset breakdown, e.g. by source benchmark
+                m.update(aggregate_response_metrics_by_subset(results, subset_key, f"eval_{name}"))
             self.metrics_log.append(m)
             if self.config.controller.save_eval_rollouts:
                 save_zst(results, self.output_dir / f"eval_rollouts-{name}-step{self.global_step}.zst")

@@ -14,9 +14,8 @@ from typing import Any
 import numpy as np
 
 from axrl_b200.data.conversation import GenerationInput, RolloutResult
-from axrl_b200.data.rollout_trace import RolloutTrace
 from axrl_b200.datasets.base_dataset import BaseDataset, ParquetQADataset
-from axrl_b200.metrics.response_metric import ResponseMetric
+from axrl_b200.envs.math_env import MathEnv
 from axrl_b200.processor.tokenizer import ChatTokenizer
 from axrl_b200.recipe.base_recipe import BaseRecipe
 from axrl_b200.verifier.gsm8k import compute_score
@@ -49,17 +48,18 @@ class SingleTurnQARecipe(BaseRecipe):
     def get_test_datasets(self) -> list[tuple[str, BaseDataset]]:
         return [(type(self).__name__.replace("Recipe", "").lower() + "_test", self.test)] if self.test is not None else []
 
+    def verify(self, text: str, answer: str) -> float:
+        """Scorer interface of :class:`MathEnv`."""
+        return self.score(text, answer)
+
     async def run_rollout(self, conversation: Any, runtime: Any) -> RolloutResult:
         ids = np.asarray(conversation.gen_state.input_ids)
         sid = f"{conversation.extra.get('group_id', conversation.conversation_id)}#{conversation.extra.get('group_index', 0)}"
         out = await runtime.rollout_worker.generate(GenerationInput(session_id=sid, input_ids=ids, sampling_config=self.config.train_sampling_config))
-        text = self.tok.decode(out.output_ids.tolist())
-        score = self.score(text, str(conversation.extra.get("answer", "")))
-        trace = RolloutTrace(max_length=len(ids) + len(out.output_ids) + 1)
-        trace.initialize(ids)
-        trace.append_assistant(out.output_ids, out.output_logprobs)
-        metric = ResponseMetric(score=score, response_length=len(out.output_ids), prompt_length=len(ids), finish_reason=out.finish_reason,
-                                repetition_ratio=ResponseMetric.repetition(out.output_ids.tolist()))
+        if not out.output_text:
+            out.output_text = self.tok.decode(out.output_ids.tolist())
+        env = MathEnv(self, conversation, str(conversation.extra.get("answer", "")), max_length=len(ids) + len(out.output_ids) + 1)
+        _, _, _, trace, metric = await env.step(out)
         return RolloutResult(conversation=conversation, trace=trace, metric=metric)
 
     def build_sft_samples(self, dataset: Any) -> list:
