@@ -43,7 +43,11 @@ class BlackboxRecipe(BaseRecipe):
         self.episode_timeout_s, self.api_key = episode_timeout_s, api_key
         self.registry = OpenAIProxySessionRegistry(request_timeout_seconds=episode_timeout_s)
         self.server: OpenAIProxyServer | None = None
-        self.adapter = OpenAIChatAdapter(lambda msgs, tools: self.tok.render(msgs, tools), self.tok.decode)
+        inner = getattr(self.tok, "tok", None)
+        self.adapter = OpenAIChatAdapter(lambda msgs, tools, **kw: self.tok.render(msgs, tools), self.tok.decode,
+                                         chat_template=getattr(inner, "chat_template", None) if isinstance(getattr(inner, "chat_template", None), str) else None,
+                                         tool_call_parser=getattr(config, "tool_call_parser", None) or "auto",
+                                         reasoning_parser=getattr(config, "reasoning_parser", None))
 
     async def start_services(self) -> dict[str, Any]:
         self.server = OpenAIProxyServer(self.registry, api_key=self.api_key)
@@ -58,7 +62,11 @@ class BlackboxRecipe(BaseRecipe):
     async def _serve(self, sid: str, runtime: Any, trace: RolloutTrace, stats: dict) -> None:
         while True:
             req = await self.registry.wait_for_request(sid, timeout_seconds=None)
-            gi = self.adapter.convert_request(req.body, sid, self.config.train_sampling_config)
+            try:
+                gi = self.adapter.convert_request(req.body, sid, self.config.train_sampling_config)
+            except ValueError as e:  # a request the rollout cannot honour: the agent gets a 400
+                await self.registry.fail(req.request_id, str(e), status_code=400)
+                continue
             ids = np.asarray(gi.input_ids)
             cur = trace.token_ids if trace.running_len else np.zeros(0, dtype=np.int32)
             if len(cur) == 0:
@@ -74,7 +82,7 @@ class BlackboxRecipe(BaseRecipe):
             stats["turns"] += 1
             stats["response_tokens"] += len(out.output_ids)
             stats["finish"] = out.finish_reason
-            await self.registry.respond(req.request_id, self.adapter.build_response(out, len(ids)))
+            await self.registry.respond(req.request_id, self.adapter.build_response(out, len(ids), req.body))
 
     async def run_rollout(self, conversation: Any, runtime: Any) -> RolloutResult:
         sid = f"{conversation.extra.get('group_id', conversation.conversation_id)}-{conversation.extra.get('group_index', 0)}".replace("/", "_")
