@@ -180,3 +180,49 @@ def test_partial_rollout_carries_unfinished_groups_across_steps():
         for t in grp.members:
             assert len(t.out_ids) == len(t.out_lps) <= t.req.forced_len
             assert t.done == (len(t.out_ids) == t.req.forced_len)
+
+
+def test_agentic_multi_turn_step_cpu():
+    """Multi-turn tool trajectories in groups sharing a prefix: every step trains the first group to
+    finish, packed into prefix trees with the loss on model tokens only; unfinished groups keep
+    their turns for the next step."""
+    from axrl_b200.configs import GrpoTrainerConfig, MegatronWorkerConfig
+    from axrl_b200.models.qwen3 import resolve_preset
+    from axrl_b200.pipeline.agentic_step import AgenticConfig, SyntheticAgentic
+
+    torch.manual_seed(0)
+    wc = MegatronWorkerConfig()
+    wc.lr_scheduler.lr_warmup_steps = 0
+    ac = AgenticConfig(group_size=3, inflight_groups=2, prefix_len=16, min_turns=2, max_turns=4, action_min=2, action_max=6, obs_min=2,
+                       obs_max=5, max_context=120, pack_len=96, seed=1)
+    pipe = SyntheticAgentic(resolve_preset("tiny"), wc, GrpoTrainerConfig(loss_type="grpo"), ac, "cpu")
+    for _ in range(3):
+        m = pipe.run_step()
+        assert m["trajectories"] == 3 and m["carried_groups"] == 1
+        assert 2 * 3 <= m["turns"] <= 4 * 3
+        assert np.isfinite(m["loss"]) and m["trained_tokens"] > 0
+        # the shared prefix and earlier turns are packed once: fewer tokens than the per-turn paths
+        assert m["trained_tokens"] < m["turns"] * ac.prefix_len + m["trajectory_tokens"] * 4
+    grp = pipe.pool[0]
+    assert all(len(t.trace.turn_samples) >= 0 for t in grp)
+
+
+def test_agentic_group_packing_shares_prefix():
+    from axrl_b200.configs import GrpoTrainerConfig, MegatronWorkerConfig
+    from axrl_b200.models.qwen3 import resolve_preset
+    from axrl_b200.pipeline.agentic_step import AgenticConfig, SyntheticAgentic
+
+    ac = AgenticConfig(group_size=4, inflight_groups=1, prefix_len=20, min_turns=2, max_turns=2, action_min=3, action_max=3, obs_min=2,
+                       obs_max=2, max_context=200, pack_len=4096, seed=2)
+    pipe = SyntheticAgentic(resolve_preset("tiny"), MegatronWorkerConfig(), GrpoTrainerConfig(), ac, "cpu")
+    pipe.pool.append(pipe._new_group())
+    while not all(t.done for t in pipe.pool[0]):
+        pipe._round([t for t in pipe.pool[0] if not t.done])
+    samples = pipe.pack_group(pipe.pool[0])
+    assert len(samples) == 1  # one tree for the whole group
+    s = samples[0]
+    # every generated token trains exactly once; the 20-token prefix is packed once, not per path
+    assert int(s.loss_mask.sum()) == 4 * 2 * 3
+    real = s.merge_info.real_total
+    paths = sum(len(t.turn_samples[i].input_ids) for t in (x.trace for x in pipe.pool[0]) for i in range(2))
+    assert real < paths and real <= 20 + 4 * (3 + 2 + 3 + 2)  # prefix once; each trajectory's turns + fork tokens
