@@ -523,19 +523,20 @@ __global__ void f32_to_bf16_k(const float* __restrict__ a, bf16* __restrict__ b,
 }  // namespace attn
 
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
-                                    double scale, bool double_p);
+                                    double scale, int64_t variant);
 
-// Forward implementation: the tcgen05 kernel (attention_tc.cu); AXRL_ATTN_FWD=mma selects the
-// mma.sync kernel below, AXRL_ATTN_FWD=tc2 the tcgen05 kernel with double-buffered P.
-static int tc_forward_mode() {
+// Forward implementation: the tcgen05 kernel (attention_tc.cu) with 4 softmax warps;
+// AXRL_ATTN_FWD=mma selects the mma.sync kernel below, =tc8 the tcgen05 kernel with 8 softmax
+// warps (two per row) and packed bf16x2 exponentials, =tc2 the double-buffered-P variant.
+static int tc_forward_mode() {  // -1: mma.sync, else the attn_fwd_tc variant
   static int mode = [] {
     const char* e = std::getenv("AXRL_ATTN_FWD");
     const std::string v = e ? e : "";
-    return v == "mma" ? 0 : v == "tc2" ? 2 : 1;
+    return v == "mma" ? -1 : v == "tc2" ? 1 : v == "tc8" ? 2 : 0;
   }();
   return mode;
 }
-static bool use_tc_forward() { return tc_forward_mode() != 0; }
+static bool use_tc_forward() { return tc_forward_mode() >= 0; }
 
 std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                      double scale);
@@ -543,7 +544,7 @@ std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, a
 // q: (T,Hq,128) k,v: (Tk,Hkv,128) -> o (T,Hq,128), lse2 (Hq,T)
 std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                  double scale) {
-  if (use_tc_forward()) return attn_fwd_tc(q, k, v, qseg, kr, tiles, scale, tc_forward_mode() == 2);
+  if (use_tc_forward()) return attn_fwd_tc(q, k, v, qseg, kr, tiles, scale, tc_forward_mode());
   return attn_fwd_mma(q, k, v, qseg, kr, tiles, scale);
 }
 

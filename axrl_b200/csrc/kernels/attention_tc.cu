@@ -330,6 +330,266 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
   }
 }
 
+// ---------------------------------------------------------------------------------- 8-warp softmax
+// Same pipeline with the softmax of every query row split over two warps (warps w and w + 4 own
+// TMEM lanes 32 (w % 4) .. +31; warp w < 4 takes key columns 0-63 of each tile, warp w + 4 columns
+// 64-127).  The two threads of a row exchange their partial maxima through shared memory once per
+// tile (a per-pair mbarrier with bounded waits; the exchange buffer alternates with the tile
+// parity), so both raise the running maximum identically, and they add their partial row sums
+// once at the end.  P is computed in packed pairs: the two scaled scores are rounded to a
+// bf16x2 word and exponentiated with one ex2.approx.ftz.bf16x2 (the bf16 P the PV product
+// consumes), which halves the special-function work per tile; the row sum adds the same bf16
+// values in fp32.
+constexpr int THREADS8 = 320;  // warps 0-7 softmax, 8 TMA producer, 9 MMA issuer
+constexpr int B8_Q = 0, B8_KV_FULL = 1, B8_KV_EMPTY = 3, B8_S_FULL = 5, B8_S_FREE = 7, B8_P_FULL = 9, B8_O_DONE = 10, B8_DRAIN = 11,
+              B8_XCH = 12, NBAR8 = 16;
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                                                            const __grid_constant__ CUtensorMap tv, Params p) {
+  extern __shared__ char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  char* sQ = sm;
+  char* sK = sm + TILE;      // 2 stages
+  char* sV = sm + 3 * TILE;  // 2 stages
+  char* sP = sm + 5 * TILE;
+  float* xmax = reinterpret_cast<float*>(sm + 6 * TILE);  // [tile parity][half][row]
+  float* xsum = xmax + 2 * 2 * BM;                         // [half][row]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xsum + 2 * BM);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR8);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seg = p.tiles[blockIdx.x * 2], qs = p.tiles[blockIdx.x * 2 + 1];
+  const int h = blockIdx.y, hk = h / (p.Hq / p.Hkv);
+  const int q0 = p.qseg[seg * 4], q1 = p.qseg[seg * 4 + 1], r_first = p.qseg[seg * 4 + 2], r_last = p.qseg[seg * 4 + 3];
+  const int qe = min(qs + BM, q1);
+
+  if (tid == 0) {
+    mbar_init(&bar[B8_Q], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar[B8_KV_FULL + s], 1);
+      mbar_init(&bar[B8_KV_EMPTY + s], 1);
+      mbar_init(&bar[B8_S_FULL + s], 1);
+      mbar_init(&bar[B8_S_FREE + s], 8);
+    }
+    mbar_init(&bar[B8_P_FULL], 8);
+    mbar_init(&bar[B8_O_DONE], 1);
+    mbar_init(&bar[B8_DRAIN], 1);
+    for (int w = 0; w < 4; ++w) mbar_init(&bar[B8_XCH + w], 64);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tq)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tv)) : "memory");
+  }
+  if (warp == 9) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  KeyTiles kt{p.kr, r_first, r_last, q0, qe, 0, 0, 0, 0};
+  kt.load_range();
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(&bar[B8_Q], TILE);
+      tma_2d(sQ, &tq, h * D, qs, &bar[B8_Q]);
+      tma_2d(sQ + HALF, &tq, h * D + 64, qs, &bar[B8_Q]);
+      int j = 0;
+      for (; kt.valid(); kt.next(), ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&bar[B8_KV_EMPTY + s], ((j - 2) >> 1) & 1, abort, p.err, 1)) break;
+        mbar_expect_tx(&bar[B8_KV_FULL + s], 2 * TILE);
+        tma_2d(sK + s * TILE, &tk, hk * D, kt.ka, &bar[B8_KV_FULL + s]);
+        tma_2d(sK + s * TILE + HALF, &tk, hk * D + 64, kt.ka, &bar[B8_KV_FULL + s]);
+        tma_2d(sV + s * TILE, &tv, hk * D, kt.ka, &bar[B8_KV_FULL + s]);
+        tma_2d(sV + s * TILE + HALF, &tv, hk * D + 64, kt.ka, &bar[B8_KV_FULL + s]);
+      }
+      if (*abort) {  // let every copy this CTA started land before its shared memory is released
+        int zero = 0;
+        mbar_wait(&bar[B8_Q], 0, (volatile int*)&zero, p.err, 1);
+        for (int i = max(0, j - 2); i < j; ++i) mbar_wait(&bar[B8_KV_FULL + (i & 1)], (i >> 1) & 1, (volatile int*)&zero, p.err, 1);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_QK = idesc_bf16(BN, false), ID_PV = idesc_bf16(D, true);
+      const uint32_t q_base = s32(sQ), k_base = s32(sK), v_base = s32(sV), p_base = s32(sP);
+      bool ok = mbar_wait(&bar[B8_Q], 0, abort, p.err, 2);
+      tc_fence_after();
+      int j = 0;
+      auto pv = [&](int t) {  // O += P_t V_t
+        if (!mbar_wait(&bar[B8_P_FULL], t & 1, abort, p.err, 4)) return false;
+        tc_fence_after();
+        const uint32_t vb = v_base + (t & 1) * TILE;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t a = sdesc(p_base + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
+          const uint64_t b = sdesc(vb + kk * 2048, HALF, 1024);
+          tc_mma(tmem + 256, a, b, ID_PV, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&bar[B8_O_DONE]);
+        tc_commit(&bar[B8_KV_EMPTY + (t & 1)]);
+        return true;
+      };
+      for (; ok && kt.valid(); kt.next(), ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&bar[B8_KV_FULL + b], (j >> 1) & 1, abort, p.err, 3)) break;
+        if (j >= 2 && !mbar_wait(&bar[B8_S_FREE + b], ((j - 2) >> 1) & 1, abort, p.err, 3)) break;
+        tc_fence_after();
+        const uint32_t kb = k_base + b * TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          tc_mma(tmem + b * BN, sdesc(q_base + off, 16, 1024), sdesc(kb + off, 16, 1024), ID_QK, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&bar[B8_S_FULL + b]);
+        if (j >= 1 && !pv(j - 1)) break;
+      }
+      if (!*abort && j >= 1) pv(j - 1);
+      tc_commit(&bar[B8_DRAIN]);
+      int zero = 0;
+      mbar_wait(&bar[B8_DRAIN], 0, (volatile int*)&zero, p.err, 5);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (warps 0-7)
+    const int wq = warp & 3, half = warp >> 2;
+    const int r = wq * 32 + lane;  // row within the tile == TMEM lane
+    const int row = qs + r;
+    const int col0 = half * (BN / 2);
+    const uint32_t lane_addr = tmem + ((uint32_t)(wq * 32) << 16);
+    uint64_t* xbar = &bar[B8_XCH + wq];
+    float m_used = -INFINITY, l = 0.f;
+    int j = 0;
+    char* prow = sP + half * HALF + (r >> 3) * 1024 + (r & 7) * 128;  // this row in this half's 64-key box
+    for (; kt.valid(); kt.next(), ++j) {
+      const int b = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar[B8_S_FULL + b], (j >> 1) & 1, abort, p.err, 6))) break;
+      tc_fence_after();
+      float s[BN / 2];
+      {
+        float t[32];
+        tmem_ld32(lane_addr + b * BN + col0, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = t[i];
+        tmem_ld32(lane_addr + b * BN + col0 + 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[32 + i] = t[i];
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B8_S_FREE + b]);
+      const int kend = min(kt.ka + BN, kt.rend);
+      const int climit = row < qe ? (kt.ty == 1 ? min(kend - kt.ka, row - q0 + kt.k0 - kt.ka + 1) : kend - kt.ka) : 0;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN / 2; ++c) {
+        s[c] = col0 + c < climit ? s[c] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, s[c]);
+      }
+      // exchange the partial maximum with the row's other half
+      xmax[((j & 1) * 2 + half) * BM + r] = mt;
+      mbar_arrive(xbar);
+      if (!__all_sync(0xffffffffu, mbar_wait(xbar, j & 1, abort, p.err, 10))) break;
+      mt = fmaxf(mt, xmax[((j & 1) * 2 + (half ^ 1)) * BM + r]);
+      // P_j overwrites P_{j-1} (and O may be rescaled) only once PV_{j-1} has finished
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&bar[B8_O_DONE], (j - 1) & 1, abort, p.err, 7))) break;
+      tc_fence_after();
+      const float m_new = fmaxf(m_used, mt);
+      const bool raise = m_new > m_used + RESCALE_THRESHOLD;
+      const bool rescale = raise && j >= 1 && m_used != -INFINITY;
+      if (__any_sync(0xffffffffu, rescale)) {  // both halves of these rows decide alike
+        const float alpha = rescale ? exp2f(m_used - m_new) : 1.f;
+        l *= alpha;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          tmem_ld32(lane_addr + 256 + col0 + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(lane_addr + 256 + col0 + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      if (raise) m_used = m_new;
+      float rs = 0.f;
+      const bool live = m_used != -INFINITY;
+#pragma unroll
+      for (int c8 = 0; c8 < BN / 16; ++c8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float x0 = s[c8 * 8 + 2 * i] - m_used, x1 = s[c8 * 8 + 2 * i + 1] - m_used;
+          const uint32_t e = live ? ex2_bf16x2(pack_bf16x2(x0, x1)) : 0u;
+          rs += __uint_as_float(e << 16) + __uint_as_float(e & 0xffff0000u);
+          w[i] = e;
+        }
+        *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += rs;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B8_P_FULL]);
+    }
+    // epilogue: last PV done, add the two halves' row sums, normalise, store this half's columns
+    const int n = j;
+    bool ok = __all_sync(0xffffffffu, !*abort);
+    if (ok && n >= 1) ok = __all_sync(0xffffffffu, mbar_wait(&bar[B8_O_DONE], (n - 1) & 1, abort, p.err, 8));
+    if (ok && n >= 1) {
+      xsum[half * BM + r] = l;
+      mbar_arrive(xbar);
+      ok = __all_sync(0xffffffffu, mbar_wait(xbar, n & 1, abort, p.err, 11));
+    }
+    if (ok && n >= 1) {
+      tc_fence_after();
+      const float L = xsum[r] + xsum[BM + r];
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      bf16* orow = p.o + ((long)row * p.Hq + h) * D + col0;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        float o[32];
+        tmem_ld32(lane_addr + 256 + col0 + c * 32, o);
+        tmem_ld_wait();
+        if (row < qe) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = o[i + e] * inv;
+            store8(orow + c * 32 + i, f);
+          }
+        }
+      }
+      if (row < qe && half == 0) p.lse2[(long)h * p.T + row] = L > 0.f ? m_used + log2f(L) : INFINITY;
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
 // ---------------------------------------------------------------------------------- host side
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
@@ -368,8 +628,9 @@ static at::Tensor& err_flag(int dev) {
 }  // namespace atc
 
 // q (T,Hq,128), k/v (Tk,Hkv,128) -> o (T,Hq,128) bf16, lse2 (Hq,T) fp32 (base-2, +inf for rows without keys)
+// variant: 0 = 4 softmax warps, 1 = 4 softmax warps with double-buffered P, 2 = 8 softmax warps
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles, double scale,
-                                    bool double_p) {
+                                    int64_t variant) {
   using namespace atc;
   AX_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(2) == D, "q bf16 (T,Hq,128)");
   AX_CHECK(k.is_contiguous() && v.is_contiguous() && k.sizes() == v.sizes() && k.size(2) == D, "k/v layout");
@@ -385,7 +646,19 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
   const CUtensorMap tv = map_rows(v.data_ptr(), Tk, (long)Hkv * D);
   Params p{(bf16*)o.data_ptr(), lse2.data_ptr<float>(), qseg.data_ptr<int>(), kr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
            (float)(scale * 1.4426950408889634), err_flag(q.get_device()).data_ptr<int>()};
-  const bool dbl = double_p;
+  if (variant == 2) {
+    const int smem8 = 6 * TILE + 3 * 2 * BM * 4 + NBAR8 * 8 + 16 + 1024;
+    static bool attr8[16] = {false};
+    const int dev = q.get_device();
+    if (!attr8[dev]) {
+      AX_CUDA_OK(cudaFuncSetAttribute(attn_fwd_tc8_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem8));
+      attr8[dev] = true;
+    }
+    attn_fwd_tc8_k<<<dim3(nt, Hq), THREADS8, smem8, stream()>>>(tq, tk, tv, p);
+    AX_LAUNCH_OK();
+    return {o, lse2};
+  }
+  const bool dbl = variant == 1;
   const int smem = (dbl ? 7 : 6) * TILE + NBAR * 8 + 16 + 1024;
   static bool attr[2] = {false, false};
   if (!attr[dbl]) {

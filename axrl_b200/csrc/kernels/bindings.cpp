@@ -23,7 +23,7 @@ void linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc);
 at::Tensor gemm_bf16(at::Tensor a, at::Tensor b, bool trans_b);
 std::vector<at::Tensor> attn_fwd(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, double);
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
-                                    double scale, bool double_p);
+                                    double scale, int64_t variant);
 std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                      double scale);
 int64_t attn_tc_error();
@@ -126,7 +126,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &ax::gemm_bf16);
   m.def("attn_fwd", &ax::attn_fwd);
   m.def("attn_fwd_tc", &ax::attn_fwd_tc, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("qseg"), py::arg("kr"), py::arg("tiles"),
-        py::arg("scale"), py::arg("double_p") = false);
+        py::arg("scale"), py::arg("variant") = 0);
   m.def("attn_fwd_mma", &ax::attn_fwd_mma);
   m.def("attn_tc_error", &ax::attn_tc_error);
   m.def("attn_bwd", &ax::attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse2"),

@@ -492,10 +492,12 @@ def test_decode_gemm_chain_with_programmatic_launch(variant):
     assert e.skinny_tma_error() == 0
 
 
-@pytest.mark.parametrize("double_p", [False, pytest.param(True, marks=pytest.mark.skipif(
-    os.environ.get("AXRL_TEST_ATTN_TC2") != "1", reason="double-buffered-P variant: opt-in until validated on a B200"))])
+@pytest.mark.parametrize("variant", [0, pytest.param(2, marks=pytest.mark.skipif(
+    os.environ.get("AXRL_TEST_ATTN_TC8") != "1", reason="8-warp softmax variant: opt-in until validated on a B200")),
+    pytest.param(1, marks=pytest.mark.skipif(
+        os.environ.get("AXRL_TEST_ATTN_TC2") != "1", reason="double-buffered-P variant: gives NaN on some inputs, under investigation"))])
 @pytest.mark.parametrize("case", [0, 1, 2, 3, 4])
-def test_attention_tcgen05_forward_matches_reference(case, double_p):
+def test_attention_tcgen05_forward_matches_reference(case, variant):
     """tcgen05/TMEM/TMA forward (attention_tc.cu) against fp32 and the mma.sync kernel: causal
     packs with odd lengths, a prefix tree, full (non-causal) ranges, keys gathered from a longer
     buffer than the queries (context-parallel layout), and sharp scores that make the running
@@ -523,7 +525,7 @@ def test_attention_tcgen05_forward_matches_reference(case, double_p):
     k = torch.randn(Tk, hkv, D, device=DEV).bfloat16()
     v = torch.randn(Tk, hkv, D, device=DEV).bfloat16()
     scale = 1 / math.sqrt(D)
-    o, lse = e.attn_fwd_tc(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale, double_p)
+    o, lse = e.attn_fwd_tc(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale, variant)
     o2, lse2 = e.attn_fwd_mma(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
     torch.cuda.synchronize()
     assert e.attn_tc_error() == 0
