@@ -16,7 +16,7 @@ import torch
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--variants", default="auto,tma,skinny,swapab,cutlass")
+    ap.add_argument("--variants", default="auto,tma,skinny,swapab,cutlass,tcgemm")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--sweep-decomp", action="store_true", help="skinny shapes under every stream-K decomposition")
     ap.add_argument("--ms", default="1,8,32,64,128,256,4096", help="comma-separated M values")
@@ -41,7 +41,12 @@ def main() -> None:
                 if (v == "swapab" and M > 64) or (v == "tma" and M > 32):
                     continue
                 try:
-                    fn = (lambda: e.linear_fwd(x, w)) if v == "auto" else (lambda v=v: e.linear_variant(x, w, v))
+                    if v == "auto":
+                        fn = lambda: e.linear_fwd(x, w)  # noqa: E731
+                    elif v == "tcgemm":  # hand-written persistent tcgen05 kernel (tcgemm.cu)
+                        fn = lambda: e.tc_linear(x, w)  # noqa: E731
+                    else:
+                        fn = lambda v=v: e.linear_variant(x, w, v)  # noqa: E731
                     for _ in range(3):
                         fn()
                     ts = []

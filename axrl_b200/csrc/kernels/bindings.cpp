@@ -81,6 +81,9 @@ at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant);
 at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 void decode_advance(int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor,
                     at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor);
+at::Tensor tc_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
+void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_t rank, int64_t rows_per_rank);
+int64_t tc_linear_error();
 }  // namespace ax
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -152,4 +155,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_residual", &ax::linear_residual);
   m.def("linear_variant", &ax::linear_variant);
   m.def("decode_advance", &ax::decode_advance);
+  m.def("tc_linear", &ax::tc_linear, py::arg("x"), py::arg("w"), py::arg("residual") = py::none());
+  m.def("tc_linear_to_slots", &ax::tc_linear_to_slots);
+  m.def("tc_linear_error", &ax::tc_linear_error);
 }

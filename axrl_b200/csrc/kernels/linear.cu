@@ -270,4 +270,46 @@ at::Tensor fp8_block_linear(at::Tensor xq, at::Tensor xs, at::Tensor wq, at::Ten
   return y;
 }
 
+// ---------------------------------------------------------------- hand-written tcgen05 GEMM (tcgemm.cu)
+void tcgemm_tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K, int* err, cudaStream_t st);
+void tcgemm_tn_to_slots(const void* A, const void* B, const int64_t* peers, int rank, int rows_per_rank, int M, int N, int K, int* err,
+                        cudaStream_t st);
+
+static at::Tensor& tcgemm_err(int dev) {
+  static at::Tensor e[64];
+  if (!e[dev].defined()) e[dev] = at::zeros({1}, at::TensorOptions().device(at::kCUDA, dev).dtype(at::kInt));
+  return e[dev];
+}
+
+// y (M, N) = x (M, K) @ w (N, K)^T (+ residual), on the hand-written persistent tcgen05 kernel
+at::Tensor tc_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  AX_CHECK(x.size(1) == w.size(1), "K mismatch");
+  const int M = x.size(0), N = w.size(0), K = x.size(1);
+  auto y = at::empty({M, N}, x.options());
+  const void* c = nullptr;
+  if (residual.has_value()) {
+    check_bf16_2d(*residual, "residual");
+    AX_CHECK(residual->size(0) == M && residual->size(1) == N, "residual shape");
+    c = residual->data_ptr();
+  }
+  tcgemm_tn(x.data_ptr(), w.data_ptr(), c, y.data_ptr(), M, N, K, tcgemm_err(x.get_device()).data_ptr<int>(), stream());
+  return y;
+}
+
+// Fused GEMM -> reduce-scatter producer: rows of x @ w^T go straight into their owner's receive
+// buffer (peer_ptrs[owner], int64 device pointers of (world * rows_per_rank, N) bf16 buffers), slot `rank`.
+void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_t rank, int64_t rows_per_rank) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  AX_CHECK(peer_ptrs.is_cuda() && peer_ptrs.scalar_type() == at::kLong, "peer_ptrs: int64 device tensor");
+  const int M = x.size(0), N = w.size(0), K = x.size(1);
+  AX_CHECK(M % rows_per_rank == 0 && M / rows_per_rank == peer_ptrs.numel(), "rows must split evenly over the ranks");
+  tcgemm_tn_to_slots(x.data_ptr(), w.data_ptr(), peer_ptrs.data_ptr<int64_t>(), (int)rank, (int)rows_per_rank, M, N, K,
+                     tcgemm_err(x.get_device()).data_ptr<int>(), stream());
+}
+
+int64_t tc_linear_error() { return tcgemm_err(c10::cuda::current_device()).item<int>(); }
+
 }  // namespace ax

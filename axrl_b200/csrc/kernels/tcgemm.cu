@@ -1,0 +1,346 @@
+// Hand-written persistent bf16 GEMM on the 5th-generation tensor cores, with epilogues that can
+// write tiles straight into another GPU's memory (the fused GEMM -> reduce-scatter of tensor
+// parallelism).  Reference counterpart: the TP row-parallel linear + sequence-parallel
+// reduce-scatter of Megatron / TransformerEngine (axrl/worker/megatron_worker.py:833-870), which
+// runs a cuBLAS GEMM and then an NCCL reduce-scatter.
+//
+//   D[M, N] = A[M, K] @ B[N, K]^T (+ C[M, N])      A, B K-major (x @ W^T), bf16 in, fp32 accumulate
+//
+// One CTA per SM walks output tiles of 128 x 256 (grouped raster: GROUP_M row tiles share the
+// column tiles they visit, so weight tiles stay in L2):
+//
+//   warp 0      TMA producer: A (128 x 64) and B (256 x 64) K-slices into a 4-stage ring
+//               (cp.async.bulk.tensor, 128-byte swizzle, no multicast).
+//   warp 1      MMA issuer (one thread) and TMEM owner: four tcgen05.mma (M 128, N 256, K 16) per
+//               K-slice into one of two 256-column fp32 accumulators, so the epilogue of tile t
+//               overlaps the main loop of tile t + 1.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes 32 (w % 4)),
+//               optional residual, bf16 conversion, and the store:
+//                 mode LOCAL   D row-major in this GPU's memory;
+//                 mode SLOTS   row r of the output belongs to TP rank r / rows_per_rank; the tile
+//                              is stored into that rank's receive slot for this rank
+//                              (peer[owner] + (rank * rows_per_rank + r % rows_per_rank) * N),
+//                              with plain stores over NVLink, so the transfer of every tile
+//                              overlaps the MMAs of the next one.
+//
+// Every mbarrier wait is bounded: on expiry the CTA records an error code, drains what it issued,
+// frees its TMEM and exits.  TMA reads only this GPU's memory.
+#include <cuda.h>
+
+#include "../cuda_common.cuh"
+
+namespace ax {
+namespace tg {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, GROUP_M = 8;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr long WAIT_LIMIT = 1L << 26;
+enum { B_FULL = 0, B_EMPTY = STAGES, B_ACC_FULL = 2 * STAGES, B_ACC_EMPTY = 2 * STAGES + 2, B_DRAIN = 2 * STAGES + 4, NBAR = 2 * STAGES + 5 };
+enum Mode { LOCAL = 0, SLOTS = 1 };
+
+struct Params {
+  int M, N, K;
+  int tiles_m, tiles_n;
+  bf16* d;               // LOCAL: D (M x N)
+  const bf16* c;         // optional residual (M x N), LOCAL mode
+  const int64_t* peers;  // SLOTS: receive buffer of every TP rank (device pointers as int64)
+  int rank, rows_per_rank;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* b, int n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void arrive(uint64_t* b) { asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s32(b)) : "memory"); }
+__device__ __forceinline__ bool try_wait(uint64_t* b, uint32_t ph) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(s32(b)), "r"(ph) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool wait(uint64_t* b, uint32_t ph, volatile int* abort, int* err, int code) {
+  for (long it = 0; !try_wait(b, ph); ++it) {
+    if (*abort) return false;
+    if (it > WAIT_LIMIT) {
+      *abort = 1;
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* b) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(s32(dst)),
+               "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(s32(b))
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s32(b)) : "memory");
+}
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d), "l"(a),
+               "l"(b), "r"(idesc), "r"(acc)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%"
+      "25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]),
+        "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+// K-major, 128-byte swizzle shared-memory descriptor (rows of 128 bytes, 8-row groups 1024 bytes apart)
+__device__ __forceinline__ uint64_t desc_k128(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// kind::f16 instruction descriptor: bf16 x bf16 -> fp32, M = 128, N = BN, both operands K-major
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+// Tile t of the grouped raster -> (row tile, column tile).
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int per_group = GROUP_M * tiles_n;
+  const int g = t / per_group, first = g * GROUP_M;
+  const int rows = min(GROUP_M, tiles_m - first);
+  const int in = t - g * per_group;
+  tm = first + in % rows;
+  tn = in / rows;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
+  extern __shared__ char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + STAGES * STAGE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = p.tiles_m * p.tiles_n, kslices = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar[B_FULL + s], 1);
+      mbar_init(&bar[B_EMPTY + s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bar[B_ACC_FULL + a], 1);
+      mbar_init(&bar[B_ACC_EMPTY + a], 4);
+    }
+    mbar_init(&bar[B_DRAIN], 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&ta)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tb)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      int it = 0;  // global K-slice counter (ring position)
+      for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        for (int kb = 0; kb < kslices; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !wait(&bar[B_EMPTY + s], ((it / STAGES) - 1) & 1, abort, p.err, 1)) break;
+          expect_tx(&bar[B_FULL + s], STAGE_BYTES);
+          char* st = sm + s * STAGE_BYTES;
+          tma2d(st, &ta, kb * BK, tm * BM, &bar[B_FULL + s]);
+          tma2d(st + A_BYTES, &tb, kb * BK, tn * BN, &bar[B_FULL + s]);
+        }
+      }
+      if (*abort) {  // every copy this CTA started lands before shared memory is released
+        int zero = 0;
+        for (int i = max(0, it - STAGES); i < it; ++i) wait(&bar[B_FULL + i % STAGES], (i / STAGES) & 1, (volatile int*)&zero, p.err, 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int it = 0, ti = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++ti) {
+        const int a = ti & 1;
+        if (ti >= 2 && !wait(&bar[B_ACC_EMPTY + a], ((ti >> 1) - 1) & 1, abort, p.err, 2)) break;
+        fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < kslices; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait(&bar[B_FULL + s], (it / STAGES) & 1, abort, p.err, 3)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t sa = s32(sm + s * STAGE_BYTES), sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) mma(tmem + a * BN, desc_k128(sa + kk * 32), desc_k128(sb + kk * 32), IDESC, (kb | kk) ? 1u : 0u);
+          commit(&bar[B_EMPTY + s]);
+        }
+        if (!ok) break;
+        commit(&bar[B_ACC_FULL + a]);
+      }
+      commit(&bar[B_DRAIN]);  // nothing issued here may still run when TMEM is freed
+      int zero = 0;
+      wait(&bar[B_DRAIN], 0, (volatile int*)&zero, p.err, 4);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2-5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    int ti = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti) {
+      const int a = ti & 1;
+      if (!__all_sync(0xffffffffu, wait(&bar[B_ACC_FULL + a], (ti >> 1) & 1, abort, p.err, 5))) break;
+      fence_after();
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      const int row = tm * BM + q * 32 + lane;
+      bf16* dst = nullptr;
+      const bf16* res = nullptr;
+      if (row < p.M) {
+        if (MODE == LOCAL) {
+          dst = p.d + (long)row * p.N;
+          if (p.c) res = p.c + (long)row * p.N;
+        } else {
+          const int owner = row / p.rows_per_rank;
+          bf16* base = reinterpret_cast<bf16*>(p.peers[owner]);
+          dst = base + ((long)p.rank * p.rows_per_rank + row % p.rows_per_rank) * p.N;
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(lane_base + a * BN + c * 32, r);
+        const int col = tn * BN + c * 32;
+        if (dst != nullptr && col < p.N) {
+          uint4 out[4];
+          uint32_t* w = reinterpret_cast<uint32_t*>(out);
+          if (res != nullptr) {
+            const uint4* rs = reinterpret_cast<const uint4*>(res + col);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 x = rs[v];
+              const bf162* h = reinterpret_cast<const bf162*>(&x);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 f = __bfloat1622float2(h[e]);
+                bf162 o = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 2 * e]) + f.x, __uint_as_float(r[v * 8 + 2 * e + 1]) + f.y);
+                w[v * 4 + e] = *reinterpret_cast<uint32_t*>(&o);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              bf162 o = __floats2bfloat162_rn(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+              w[e] = *reinterpret_cast<uint32_t*>(&o);
+            }
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(dst + col);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) d4[v] = out[v];
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) arrive(&bar[B_ACC_EMPTY + a]);
+    }
+    if (MODE == SLOTS) __threadfence_system();  // peer stores visible before the kernel completes
+  }
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------------- host side
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+
+static EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    AX_REQUIRE(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess && ptr,
+               "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+
+// rows x cols bf16, K-major box {64, box_rows}, 128-byte swizzle; out-of-range rows read as zero
+static CUtensorMap kmajor_map(const void* base, long rows, long cols, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AX_REQUIRE(r == CUDA_SUCCESS, "tensor map encode failed (", (int)r, ")");
+  return m;
+}
+
+static int smem_bytes() { return STAGES * STAGE_BYTES + NBAR * 8 + 16 + 1024; }
+
+template <int MODE>
+static void launch(const void* A, const void* B, Params p, cudaStream_t st) {
+  AX_REQUIRE(p.K % BK == 0, "tcgemm: K must be a multiple of 64, got ", p.K);
+  AX_REQUIRE(p.N % 32 == 0, "tcgemm: N must be a multiple of 32, got ", p.N);
+  AX_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(B) % 16 == 0, "tcgemm: 16-byte aligned operands");
+  if (p.M == 0 || p.N == 0) return;
+  const CUtensorMap ta = kmajor_map(A, p.M, p.K, BM);
+  const CUtensorMap tb = kmajor_map(B, p.N, p.K, BN);
+  p.tiles_m = (p.M + BM - 1) / BM;
+  p.tiles_n = (p.N + BN - 1) / BN;
+  static bool attr[2][64] = {{false}};
+  int dev = 0;
+  AX_CUDA_OK(cudaGetDevice(&dev));
+  if (!attr[MODE][dev]) {
+    AX_CUDA_OK(cudaFuncSetAttribute(gemm_k<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes()));
+    attr[MODE][dev] = true;
+  }
+  const int grid = std::min(p.tiles_m * p.tiles_n, num_sms());
+  launch_pdl(gemm_k<MODE>, dim3(grid), dim3(THREADS), (size_t)smem_bytes(), st, ta, tb, p);
+}
+
+}  // namespace tg
+
+// D[M,N] (+)= A[M,K] @ B[N,K]^T (+ C), bf16; err: device int that records a wait timeout.
+void tcgemm_tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K, int* err, cudaStream_t st) {
+  tg::Params p{M, N, K, 0, 0, static_cast<bf16*>(D), static_cast<const bf16*>(C), nullptr, 0, 1, err};
+  tg::launch<tg::LOCAL>(A, B, p, st);
+}
+
+// Row-parallel GEMM whose output rows are reduce-scattered: row r of A @ B^T goes to rank
+// r / rows_per_rank's receive buffer (peers[owner], device pointers), slot `rank`.
+void tcgemm_tn_to_slots(const void* A, const void* B, const int64_t* peers, int rank, int rows_per_rank, int M, int N, int K, int* err,
+                        cudaStream_t st) {
+  tg::Params p{M, N, K, 0, 0, nullptr, nullptr, peers, rank, rows_per_rank, err};
+  tg::launch<tg::SLOTS>(A, B, p, st);
+}
+
+}  // namespace ax

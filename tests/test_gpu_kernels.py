@@ -614,3 +614,22 @@ def test_gdn_step_kernel_matches_reference():
     o = e.gdn_step(q, k, v, g, beta, pool, slots)
     close(o, o_ref, 1e-4, 1e-4, msg="o")
     close(pool[slots], S_ref, 1e-4, 1e-4, msg="state")
+
+
+@pytest.mark.skipif(os.environ.get("AXRL_TEST_TCGEMM") != "1", reason="hand-written tcgen05 GEMM: opt-in until validated on a B200")
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 256), (4096, 4096, 4096), (1000, 6144, 4096), (77, 1056, 128)])
+def test_tcgemm_matches_fp32(M, N, K):
+    """Persistent tcgen05 GEMM (tcgemm.cu) against fp32: ragged M, N a multiple of 32 but not of
+    the 256-column tile, several tiles per CTA, with and without a residual."""
+    e = _ext()
+    torch.manual_seed(M + N)
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    r = torch.randn(M, N, device=DEV).bfloat16()
+    ref = x.float() @ w.float().t()
+    y = e.tc_linear(x, w)
+    y2 = e.tc_linear(x, w, r)
+    torch.cuda.synchronize()
+    assert e.tc_linear_error() == 0
+    close(y, ref, 2e-2, 1e-2, msg="tcgemm")
+    close(y2, ref + r.float(), 3e-2, 1e-2, msg="tcgemm + residual")
