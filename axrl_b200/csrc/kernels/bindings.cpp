@@ -82,7 +82,8 @@ at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> r
 void decode_advance(int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor,
                     at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor);
 at::Tensor tc_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
-void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_t rank, int64_t rows_per_rank);
+void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_t rank, int64_t rows_per_rank, at::Tensor flag_ptrs,
+                        at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ticket, int64_t timeout_ns, at::Tensor status);
 int64_t tc_linear_error();
 }  // namespace ax
 

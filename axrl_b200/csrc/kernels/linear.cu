@@ -272,8 +272,9 @@ at::Tensor fp8_block_linear(at::Tensor xq, at::Tensor xs, at::Tensor wq, at::Ten
 
 // ---------------------------------------------------------------- hand-written tcgen05 GEMM (tcgemm.cu)
 void tcgemm_tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K, int* err, cudaStream_t st);
-void tcgemm_tn_to_slots(const void* A, const void* B, const int64_t* peers, int rank, int rows_per_rank, int M, int N, int K, int* err,
-                        cudaStream_t st);
+void tcgemm_tn_to_slots(const void* A, const void* B, const int64_t* peers, int rank, int world, int rows_per_rank, int M, int N, int K,
+                        const int64_t* flag_peers, const int* my_flags, int ch, int epoch, unsigned* ticket, uint64_t timeout_ns,
+                        int* status, int* err, cudaStream_t st);
 
 static at::Tensor& tcgemm_err(int dev) {
   static at::Tensor e[64];
@@ -299,14 +300,22 @@ at::Tensor tc_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> resid
 }
 
 // Fused GEMM -> reduce-scatter producer: rows of x @ w^T go straight into their owner's receive
-// buffer (peer_ptrs[owner], int64 device pointers of (world * rows_per_rank, N) bf16 buffers), slot `rank`.
-void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_t rank, int64_t rows_per_rank) {
+// buffer (peer_ptrs[owner], int64 device pointers of (world * rows_per_rank, N) bf16 buffers),
+// slot `rank`; flag_ptrs (int64 device pointers of every rank's TP flag array), my_flags, ticket
+// and status follow the TP channel protocol of tp_comm.cu.
+void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_t rank, int64_t rows_per_rank, at::Tensor flag_ptrs,
+                        at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ticket, int64_t timeout_ns, at::Tensor status) {
   check_bf16_2d(x, "x");
   check_bf16_2d(w, "w");
   AX_CHECK(peer_ptrs.is_cuda() && peer_ptrs.scalar_type() == at::kLong, "peer_ptrs: int64 device tensor");
+  AX_CHECK(flag_ptrs.is_cuda() && flag_ptrs.scalar_type() == at::kLong && flag_ptrs.numel() == peer_ptrs.numel(), "flag_ptrs");
+  AX_CHECK(my_flags.scalar_type() == at::kInt && ticket.scalar_type() == at::kInt && status.scalar_type() == at::kInt, "int32 flags");
   const int M = x.size(0), N = w.size(0), K = x.size(1);
-  AX_CHECK(M % rows_per_rank == 0 && M / rows_per_rank == peer_ptrs.numel(), "rows must split evenly over the ranks");
-  tcgemm_tn_to_slots(x.data_ptr(), w.data_ptr(), peer_ptrs.data_ptr<int64_t>(), (int)rank, (int)rows_per_rank, M, N, K,
+  const int world = peer_ptrs.numel();
+  AX_CHECK(M % rows_per_rank == 0 && M / rows_per_rank == world, "rows must split evenly over the ranks");
+  tcgemm_tn_to_slots(x.data_ptr(), w.data_ptr(), peer_ptrs.data_ptr<int64_t>(), (int)rank, world, (int)rows_per_rank, M, N, K,
+                     flag_ptrs.data_ptr<int64_t>(), my_flags.data_ptr<int>(), (int)ch, (int)epoch,
+                     reinterpret_cast<unsigned*>(ticket.data_ptr<int>()) + ch, (uint64_t)timeout_ns, status.data_ptr<int>(),
                      tcgemm_err(x.get_device()).data_ptr<int>(), stream());
 }
 

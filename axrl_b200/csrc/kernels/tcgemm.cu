@@ -21,7 +21,12 @@
 //                              is stored into that rank's receive slot for this rank
 //                              (peer[owner] + (rank * rows_per_rank + r % rows_per_rank) * N),
 //                              with plain stores over NVLink, so the transfer of every tile
-//                              overlaps the MMAs of the next one.
+//                              overlaps the MMAs of the next one.  Synchronisation follows the
+//                              TP channel protocol of tp_comm.cu: CTA 0 declares this rank's
+//                              receive buffer free for the epoch, every epilogue waits (bounded)
+//                              until each peer has declared the same before its first store, and
+//                              the last CTA to finish fences and raises the epoch's data flag on
+//                              every peer.
 //
 // Every mbarrier wait is bounded: on expiry the CTA records an error code, drains what it issued,
 // frees its TMEM and exits.  TMA reads only this GPU's memory.
@@ -48,7 +53,40 @@ struct Params {
   const int64_t* peers;  // SLOTS: receive buffer of every TP rank (device pointers as int64)
   int rank, rows_per_rank;
   int* err;
+  // SLOTS: channel flags (tp_comm.cu layout: flags[ch][src]) of every rank and of this rank
+  const int64_t* flag_peers;
+  const int* my_flags;
+  int ch, epoch, world;
+  unsigned* ticket;
+  unsigned long long timeout_ns;
+  int* status;
 };
+
+constexpr int kMaxTP = 8, kFreeBase = 16;
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ int ld_acquire(const int* f) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* f, int v) { asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f), "r"(v) : "memory"); }
+// Every peer has declared this channel's buffer free for `epoch` (bounded).
+__device__ bool peers_free(const Params& p) {
+  const uint64_t t0 = gtimer();
+  for (int s = 0; s < p.world; ++s) {
+    if (s == p.rank) continue;
+    const int* f = p.my_flags + (p.ch + kFreeBase) * kMaxTP + s;
+    while (ld_acquire(f) < p.epoch) {
+      if (gtimer() - t0 > p.timeout_ns) return false;
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t* b, int n) {
@@ -140,6 +178,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
     }
     mbar_init(&bar[B_DRAIN], 1);
     *abort = 0;
+    tmem_slot[2] = 0u;  // epilogue warps finished (SLOTS completion count)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&ta)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tb)) : "memory");
@@ -207,6 +246,20 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
     // ---------------------------------------------------------------- epilogue (warps 2-5)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    if (MODE == SLOTS) {
+      if (blockIdx.x == 0 && warp == 2 && lane == 0)  // this rank's receive buffer may be overwritten
+        for (int s = 0; s < p.world; ++s)
+          if (s != p.rank) st_release(reinterpret_cast<int*>(p.flag_peers[s]) + (p.ch + kFreeBase) * kMaxTP + p.rank, p.epoch);
+      int ok = 1;
+      if (lane == 0 && !peers_free(p)) {
+        ok = 0;
+        atomicCAS(p.status, 0, 1);
+        *abort = 1;
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) goto epilogue_done;
+    }
+    {
     int ti = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti) {
       const int a = ti & 1;
@@ -264,7 +317,25 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
       __syncwarp();
       if (lane == 0) arrive(&bar[B_ACC_EMPTY + a]);
     }
-    if (MODE == SLOTS) __threadfence_system();  // peer stores visible before the kernel completes
+    }
+    if (MODE == SLOTS) {
+      // the last epilogue warp of the last CTA publishes the epoch's data flag on every peer
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0) {
+        unsigned* done_warps = reinterpret_cast<unsigned*>(tmem_slot + 2);
+        if (atomicAdd(done_warps, 1u) == 3u && !*abort) {
+          const unsigned t = atomicAdd(p.ticket, 1u);
+          if (t == gridDim.x - 1) {
+            *p.ticket = 0u;  // every CTA of this launch arrived; the next launch is stream-ordered
+            __threadfence_system();
+            for (int s = 0; s < p.world; ++s)
+              if (s != p.rank) st_release(reinterpret_cast<int*>(p.flag_peers[s]) + p.ch * kMaxTP + p.rank, p.epoch);
+          }
+        }
+      }
+    }
+  epilogue_done:;
   }
   __syncthreads();
   if (warp == 1) {
@@ -304,7 +375,7 @@ static CUtensorMap kmajor_map(const void* base, long rows, long cols, int box_ro
   return m;
 }
 
-static int smem_bytes() { return STAGES * STAGE_BYTES + NBAR * 8 + 16 + 1024; }
+static int smem_bytes() { return STAGES * STAGE_BYTES + NBAR * 8 + 32 + 1024; }
 
 template <int MODE>
 static void launch(const void* A, const void* B, Params p, cudaStream_t st) {
@@ -331,15 +402,22 @@ static void launch(const void* A, const void* B, Params p, cudaStream_t st) {
 
 // D[M,N] (+)= A[M,K] @ B[N,K]^T (+ C), bf16; err: device int that records a wait timeout.
 void tcgemm_tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K, int* err, cudaStream_t st) {
-  tg::Params p{M, N, K, 0, 0, static_cast<bf16*>(D), static_cast<const bf16*>(C), nullptr, 0, 1, err};
+  tg::Params p{};
+  p.M = M, p.N = N, p.K = K, p.d = static_cast<bf16*>(D), p.c = static_cast<const bf16*>(C), p.rows_per_rank = 1, p.err = err;
   tg::launch<tg::LOCAL>(A, B, p, st);
 }
 
 // Row-parallel GEMM whose output rows are reduce-scattered: row r of A @ B^T goes to rank
-// r / rows_per_rank's receive buffer (peers[owner], device pointers), slot `rank`.
-void tcgemm_tn_to_slots(const void* A, const void* B, const int64_t* peers, int rank, int rows_per_rank, int M, int N, int K, int* err,
-                        cudaStream_t st) {
-  tg::Params p{M, N, K, 0, 0, nullptr, nullptr, peers, rank, rows_per_rank, err};
+// r / rows_per_rank's receive buffer (peers[owner], device pointers), slot `rank`; channel `ch`
+// of the TP flag arrays carries the free / data handshakes of epoch `epoch`.
+void tcgemm_tn_to_slots(const void* A, const void* B, const int64_t* peers, int rank, int world, int rows_per_rank, int M, int N, int K,
+                        const int64_t* flag_peers, const int* my_flags, int ch, int epoch, unsigned* ticket, uint64_t timeout_ns,
+                        int* status, int* err, cudaStream_t st) {
+  AX_REQUIRE(world >= 1 && world <= tg::kMaxTP && rank < world && ch >= 0 && ch < tg::kFreeBase, "tcgemm slots: TP layout");
+  tg::Params p{};
+  p.M = M, p.N = N, p.K = K, p.peers = peers, p.rank = rank, p.rows_per_rank = rows_per_rank, p.err = err;
+  p.flag_peers = flag_peers, p.my_flags = my_flags, p.ch = ch, p.epoch = epoch, p.world = world, p.ticket = ticket;
+  p.timeout_ns = timeout_ns, p.status = status;
   tg::launch<tg::SLOTS>(A, B, p, st);
 }
 

@@ -14,6 +14,11 @@ all-gather / reduce-scatter around cuBLAS GEMMs (``axrl/worker/megatron_worker.p
   its slots (plus the residual, fused) once every peer's slot has arrived.
 * backward passes use the same two patterns in the other direction (dgrad -> reduce-scatter with
   the input re-gathered for the weight gradient under the dgrad GEMMs; all-gather of dy -> dgrad).
+* fused GEMM -> reduce-scatter (``AXRL_TP_FUSED=1``): ONE kernel (``csrc/kernels/tcgemm.cu``, mode
+  SLOTS) computes every output tile on the tensor cores and stores it straight into its owner's
+  receive slot over NVLink, so the transfer of each tile overlaps the MMAs of the next; the kernel
+  itself performs the free / data handshakes of the channel, and the owner then sums its slots
+  (plus the residual).
 
 All waits are bounded; :meth:`P2PTPComm.check` raises if a peer timed out.
 """
@@ -60,6 +65,9 @@ class P2PTPComm(TPComm):
         self.ag_ptrs = torch.tensor(self.h_ag.buffer_ptrs, dtype=torch.int64)
         self.rs_ptrs = torch.tensor(self.h_rs.buffer_ptrs, dtype=torch.int64)
         self.flag_ptrs = torch.tensor(self.h_flags.buffer_ptrs, dtype=torch.int64)
+        self.rs_ptrs_dev = self.rs_ptrs.to(dev)
+        self.flag_ptrs_dev = self.flag_ptrs.to(dev)
+        self.fused = os.environ.get("AXRL_TP_FUSED", "0") == "1"
         self.stage = torch.empty(2, cap // self.size, dtype=torch.bfloat16, device=dev)
         self.ticket = torch.zeros(_K_CHANNELS, dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -167,6 +175,24 @@ class P2PTPComm(TPComm):
         cur.wait_stream(self.comm_stream)
         return out
 
+    def fused_rs_ok(self, x: torch.Tensor, w: torch.Tensor) -> bool:
+        """Shapes the fused tcgen05 GEMM -> reduce-scatter kernel accepts."""
+        T, K = x.shape
+        N = w.shape[0]
+        return self.fused and T % self.size == 0 and K % 64 == 0 and N % 32 == 0 and T * N <= self.rs.numel()
+
+    def gemm_rs_fused(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None) -> torch.Tensor:
+        """out (T/tp, N) = RS(x @ w^T) (+ residual), the GEMM tiles stored into the owners' slots."""
+        T, N = x.shape[0], w.shape[0]
+        n = T // self.size
+        e = self._next_epoch()
+        _ext.ext().tc_linear_to_slots(x, w, self.rs_ptrs_dev, self.rank, n, self.flag_ptrs_dev, self.flags, CH_RS, e, self.ticket,
+                                      self.timeout_ns, self.status)
+        self._wait(CH_RS, (1 << self.size) - 1, e)
+        out = torch.empty(n, N, dtype=torch.bfloat16, device=self.device)
+        _ext.ext().tp_reduce_slots(self.rs, self.size, n * N, residual, out)
+        return out
+
     def ag_linear(self, x_local: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         T = x_local.shape[0] * self.size
         if not self._fits(x_local.reshape(x_local.shape[0], -1), T) or not w.is_cuda:
@@ -230,7 +256,10 @@ class _LinearRS(torch.autograd.Function):
         T = x.shape[0]
         n = T // comm.size
         e = _ext.ext()
-        out = comm._scatter_chunks(n, w.shape[0], lambda o, buf: e.linear_fwd_into(x[o * n:(o + 1) * n], w, buf), residual)
+        if comm.fused_rs_ok(x, w):  # one kernel: tcgen05 tiles stored into the owners' slots over NVLink
+            out = comm.gemm_rs_fused(x, w, residual)
+        else:
+            out = comm._scatter_chunks(n, w.shape[0], lambda o, buf: e.linear_fwd_into(x[o * n:(o + 1) * n], w, buf), residual)
         ctx.save_for_backward(x, w)
         ctx.comm = comm
         ctx.has_res = residual is not None

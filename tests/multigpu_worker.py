@@ -106,9 +106,11 @@ def case_weight_sync() -> None:
         print(f"rank {rank}: weight_sync nccl baseline fp8={fp8} ok", flush=True)
 
 
-def case_tp() -> None:
+def case_tp(backends=("torch", "p2p")) -> None:
     """TP=world with sequence parallelism: NCCL collectives and the overlapped P2P kernels, each
-    against the TP=1 model (same weights) on this GPU."""
+    against the TP=1 model (same weights) on this GPU.  ``p2p_fused``: the P2P communicator with
+    the row-parallel forward GEMM fused with its reduce-scatter (one tcgen05 kernel storing tiles
+    into the owners' slots)."""
     from axrl_b200.models.qwen3 import Qwen3Config, Qwen3Model
     from axrl_b200.ops.attention_spec import spec_from_triples
     from axrl_b200.parallel import tensor_parallel as tpl
@@ -145,8 +147,11 @@ def case_tp() -> None:
 
     lp_ref, ent_ref = run(full)
     keep = labels >= 0
-    for backend in ("torch", "p2p"):
-        tp = tpl.TPContext.from_group(dist.group.WORLD, backend=backend)
+    for backend in backends:
+        os.environ["AXRL_TP_FUSED"] = "1" if backend == "p2p_fused" else "0"
+        tp = tpl.TPContext.from_group(dist.group.WORLD, backend="p2p" if backend == "p2p_fused" else backend)
+        if backend == "p2p_fused":
+            assert tp.comm.fused
         m = Qwen3Model(cfg, tp=tp).to("cuda", torch.bfloat16)
         m.inv_freq = m.inv_freq.float()
         tpl.load_shards_from_full(m, state, tp)
@@ -170,6 +175,10 @@ def case_tp() -> None:
             worst = max(worst, rel)
             assert rel < 3e-2, f"{backend}: grad {n} rel err {rel}"
         print(f"rank {rank}: tp {backend} ok (lp diff {d_lp:.2e}, worst grad rel err {worst:.2e})", flush=True)
+
+
+def case_tp_fused() -> None:
+    case_tp(("p2p_fused",))
 
 
 def case_tp_timeout() -> None:

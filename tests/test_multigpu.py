@@ -37,6 +37,12 @@ def test_tensor_parallel_two_gpus():
     assert out.count("tp torch ok") == 2 and out.count("tp p2p ok") == 2, out[-2000:]
 
 
+def test_tensor_parallel_fused_gemm_rs_two_gpus():
+    """Row-parallel forward GEMM fused with its reduce-scatter (tcgen05 tiles stored into peer slots)."""
+    out = _run("tp_fused")
+    assert out.count("tp p2p_fused ok") == 2, out[-2000:]
+
+
 def test_tp_p2p_wait_times_out_without_hanging():
     assert _run("tp_timeout").count("tp timeout ok") == 2
 
