@@ -19,9 +19,14 @@
 // first two products) and as MN-major ones (dO, Q, K on the last three).  P^T and dS^T are written
 // by the softmax warps in the same swizzled layout: K-major A for dV / dK, MN-major A for dQ.
 //
-// Warp roles: warp 4 TMA producer, warp 5 MMA issuer (one thread) and TMEM owner, warps 0-3 the
-// element-wise gradient and the dQ / dK / dV read-out.  Every mbarrier wait is bounded; on expiry
-// the CTA records an error code, drains its copies and tensor-core work, frees TMEM and exits.
+// Warp roles: warp 8 TMA producer, warp 9 MMA issuer (one thread) and TMEM owner, warps 0-7 the
+// element-wise gradient and the dQ / dK / dV read-out: warps w and w + 4 share TMEM lanes
+// 32 (w % 4) (one key row for the key-major products, one q row for dQ) and split the 128 columns
+// in halves, so there is no cross-thread reduction.  The q tile's lse and Dsum values are staged
+// once in shared memory (alternating buffers by tile parity, a bounded mbarrier among the 256
+// threads), and dQ is added to the fp32 accumulator with 16-byte vector reductions
+// (red.global.add.v4.f32).  Every mbarrier wait is bounded; on expiry the CTA records an error
+// code, drains its copies and tensor-core work, frees TMEM and exits.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -35,13 +40,17 @@ using namespace tc;
 constexpr int D = 128;
 constexpr int BK = 128;  // keys per CTA
 constexpr int BQ = 128;  // q rows per tile
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // warps 0-7 element-wise, 8 TMA producer, 9 MMA issuer
 constexpr int TILE = 128 * 128 * 2;
 constexpr int HALF = TILE / 2;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int C_S = 0, C_DP = 128, C_DV = 256, C_DK = 384;
 
-constexpr int B_KV = 0, B_QD = 1, B_S = 2, B_P = 3, B_MM = 4, B_DQF = 5, B_DRAIN = 6, NBAR = 7;
+constexpr int B_KV = 0, B_QD = 1, B_S = 2, B_P = 3, B_MM = 4, B_DQF = 5, B_DRAIN = 6, B_LD = 7, NBAR = 8;
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
 
 struct Params {
   const float* lse2;  // (Hq, T)
@@ -98,7 +107,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
   char* sdO = sm + 3 * TILE;
   char* sP = sm + 4 * TILE;   // P^T  [key][q]
   char* sdS = sm + 5 * TILE;  // dS^T [key][q]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 6 * TILE);
+  float* sL = reinterpret_cast<float*>(sm + 6 * TILE);  // [tile parity][q column]: lse2
+  float* sDs = sL + 2 * BQ;                              // [tile parity][q column]: Dsum
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sDs + 2 * BQ);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -112,14 +123,15 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
     mbar_init(&bar[B_KV], 1);
     mbar_init(&bar[B_QD], 1);
     mbar_init(&bar[B_S], 1);
-    mbar_init(&bar[B_P], 4);
+    mbar_init(&bar[B_P], 8);
     mbar_init(&bar[B_MM], 1);
-    mbar_init(&bar[B_DQF], 4);
+    mbar_init(&bar[B_DQF], 8);
     mbar_init(&bar[B_DRAIN], 1);
+    mbar_init(&bar[B_LD], 256);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)), "r"(TMEM_COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -131,7 +143,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
   QTiles qt{p.qr, it0, it1, G, ks, k0s, 0, it0, 0, 0, 0, 0};
   qt.seek();
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       mbar_expect_tx(&bar[B_KV], 2 * TILE);
@@ -155,7 +167,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
         if (i >= 1) mbar_wait(&bar[B_QD], (i - 1) & 1, (volatile int*)&zero, p.err, 11);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t ID_KMAJ = idesc_bf16(128, false), ID_BMN = idesc_bf16(128, true), ID_ABMN = idesc_bf16(128, true, true);
@@ -191,11 +203,14 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
       mbar_wait(&bar[B_DRAIN], 0, (volatile int*)&zero, p.err, 14);
     }
   } else {
-    // ------------------------------------------------------------ gradient element-wise + read-out (warps 0-3)
-    const int key = ks + tid;  // this thread's key (TMEM lane tid of the key-major products)
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-    char* prow = sP + (tid >> 3) * 1024 + (tid & 7) * 128;
-    char* dsrow = sdS + (tid >> 3) * 1024 + (tid & 7) * 128;
+    // ------------------------------------------------------------ gradient element-wise + read-out (warps 0-7)
+    const int wq = warp & 3, half = warp >> 2;
+    const int r = wq * 32 + lane;  // TMEM lane: key row of the key-major products, q row of dQ
+    const int col0 = half * (BQ / 2);
+    const int key = ks + r;
+    const uint32_t lane_addr = tmem + ((uint32_t)(wq * 32) << 16);
+    char* prow = sP + (r >> 3) * 1024 + (r & 7) * 128 + half * HALF;
+    char* dsrow = sdS + (r >> 3) * 1024 + (r & 7) * 128 + half * HALF;
     int i = 0;
     for (; qt.valid(); qt.next(), ++i) {
       const int h = hk * G + qt.g;
@@ -204,12 +219,22 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
       // rows with (q - q0) >= (key - k0s)
       const int climit = key < ke ? qe - qs : 0;
       const int cfirst = qt.ty == 1 ? max(0, (key - k0s) - (qs - qt.q0)) : 0;
+      // stage the tile's lse2 / Dsum once (thread (half, r) loads column r of its half's copy)
+      {
+        float* L = sL + (i & 1) * BQ;
+        float* Ds = sDs + (i & 1) * BQ;
+        if (half == 0) L[r] = qs + r < qe ? p.lse2[(long)h * p.T + qs + r] : 0.f;
+        else Ds[r] = qs + r < qe ? p.dsum[(long)h * p.T + qs + r] : 0.f;
+        mbar_arrive(&bar[B_LD]);
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar[B_LD], i & 1, abort, p.err, 17))) break;
       if (!__all_sync(0xffffffffu, mbar_wait(&bar[B_S], i & 1, abort, p.err, 15))) break;
       tc_fence_after();
-      const float* lse = p.lse2 + (long)h * p.T + qs;
-      const float* dsm = p.dsum + (long)h * p.T + qs;
+      const float* L = sL + (i & 1) * BQ;
+      const float* Ds = sDs + (i & 1) * BQ;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BQ; c0 += 32) {
+      for (int cc = 0; cc < BQ / 2; cc += 32) {
+        const int c0 = col0 + cc;
         float s[32], dp[32];
         tmem_ld32(lane_addr + C_S + c0, s);
         tmem_ld32(lane_addr + C_DP + c0, dp);
@@ -221,19 +246,18 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
           for (int u = 0; u < 2; ++u) {
             const int c = c0 + e + u;
             const bool vis = c >= cfirst && c < climit;
-            const float l2 = vis ? __ldg(lse + c) : 0.f;
-            const float pr = vis ? exp2f(s[e + u] * p.scale_log2 - l2) : 0.f;
+            const float pr = vis ? exp2f(s[e + u] * p.scale_log2 - L[c]) : 0.f;
             pv[u] = pr;
-            dv2[u] = vis ? pr * (dp[e + u] - __ldg(dsm + c)) * p.scale : 0.f;
+            dv2[u] = vis ? pr * (dp[e + u] - Ds[c]) * p.scale : 0.f;
           }
           bf162 a = __floats2bfloat162_rn(pv[0], pv[1]), b = __floats2bfloat162_rn(dv2[0], dv2[1]);
           pw[e / 2] = *reinterpret_cast<uint32_t*>(&a);
           dw[e / 2] = *reinterpret_cast<uint32_t*>(&b);
         }
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {  // 4 chunks of 8 q columns, 128-byte swizzled rows
-          const int cc = (c0 >> 3) + q8;   // 16-byte chunk index over 128 columns
-          const int off = (cc >> 3) * HALF + (((cc & 7) ^ (tid & 7)) << 4);
+        for (int q8 = 0; q8 < 4; ++q8) {  // 4 chunks of 8 q columns, 128-byte swizzled rows of this half's box
+          const int ch = (cc >> 3) + q8;  // 16-byte chunk index within the 64-column box
+          const int off = ((ch ^ (r & 7)) << 4);
           *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[q8 * 4], pw[q8 * 4 + 1], pw[q8 * 4 + 2], pw[q8 * 4 + 3]);
           *reinterpret_cast<uint4*>(dsrow + off) = make_uint4(dw[q8 * 4], dw[q8 * 4 + 1], dw[q8 * 4 + 2], dw[q8 * 4 + 3]);
         }
@@ -242,35 +266,35 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_P]);
-      // dQ of this tile: TMEM lane = q row
+      // dQ of this tile: TMEM lane = q row, this half's 64 head-dim columns
       if (!__all_sync(0xffffffffu, mbar_wait(&bar[B_MM], i & 1, abort, p.err, 16))) break;
       tc_fence_after();
-      const int qrow = qs + tid;
-      float* dq = p.dq_acc + ((long)qrow * p.Hq + h) * D;
+      const int qrow = qs + r;
+      float* dq = p.dq_acc + ((long)qrow * p.Hq + h) * D + col0;
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int cc = 0; cc < D / 2; cc += 32) {
         float v[32];
-        tmem_ld32(lane_addr + C_S + c0, v);
+        tmem_ld32(lane_addr + C_S + col0 + cc, v);
         if (qrow < qe) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) atomicAdd(dq + c0 + e, v[e]);
+          for (int e = 0; e < 32; e += 4) red_add_v4(dq + cc + e, v[e], v[e + 1], v[e + 2], v[e + 3]);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_DQF]);
     }
-    // dK / dV of this key tile (accumulated over every q tile and head)
+    // dK / dV of this key tile (accumulated over every q tile and head), this half's columns
     const bool ok = __all_sync(0xffffffffu, !*abort) && i > 0;
     if (ok) {
       tc_fence_after();
-      bf16* dkr = p.dk + ((long)key * p.Hkv + hk) * D;
-      bf16* dvr = p.dv + ((long)key * p.Hkv + hk) * D;
+      bf16* dkr = p.dk + ((long)key * p.Hkv + hk) * D + col0;
+      bf16* dvr = p.dv + ((long)key * p.Hkv + hk) * D + col0;
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int cc = 0; cc < D / 2; cc += 32) {
         float a[32], b[32];
-        tmem_ld32(lane_addr + C_DK + c0, a);
-        tmem_ld32(lane_addr + C_DV + c0, b);
+        tmem_ld32(lane_addr + C_DK + col0 + cc, a);
+        tmem_ld32(lane_addr + C_DV + col0 + cc, b);
         if (key < ke) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
@@ -280,8 +304,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
               fa[u] = a[e + u];
               fb[u] = b[e + u];
             }
-            store8(dkr + c0 + e, fa);
-            store8(dvr + c0 + e, fb);
+            store8(dkr + cc + e, fa);
+            store8(dvr + cc + e, fb);
           }
         }
       }
@@ -289,7 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
     tc_fence_before();
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
@@ -347,7 +371,7 @@ void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v
   Params p{lse2.data_ptr<float>(), dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), (bf16*)dk.data_ptr(), (bf16*)dv.data_ptr(),
            kseg.data_ptr<int>(), qr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T, (float)(scale * 1.4426950408889634), (float)scale,
            err_flag(q.get_device()).data_ptr<int>()};
-  const int smem = 6 * TILE + NBAR * 8 + 16 + 1024;
+  const int smem = 6 * TILE + 4 * BQ * 4 + NBAR * 8 + 16 + 1024;
   static bool attr = false;
   if (!attr) {
     AX_CUDA_OK(cudaFuncSetAttribute(attn_bwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
