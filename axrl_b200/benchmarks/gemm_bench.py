@@ -16,7 +16,7 @@ import torch
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--variants", default="auto,tma,skinny,swapab,cutlass,tcgemm")
+    ap.add_argument("--variants", default="auto,tma,skinny,swapab,cutlass,tcgemm,tcstream")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--sweep-decomp", action="store_true", help="skinny shapes under every stream-K decomposition")
     ap.add_argument("--ms", default="1,8,32,64,128,256,4096", help="comma-separated M values")
@@ -38,7 +38,7 @@ def main() -> None:
             for v in a.variants.split(","):
                 if v == "skinny" and M > 64:
                     continue
-                if (v == "swapab" and M > 64) or (v == "tma" and M > 32):
+                if (v in ("swapab", "tcstream") and M > 64) or (v == "tma" and M > 32):
                     continue
                 try:
                     if v == "auto":

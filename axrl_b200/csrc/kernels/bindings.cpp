@@ -85,6 +85,8 @@ at::Tensor tc_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> resid
 void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_t rank, int64_t rows_per_rank, at::Tensor flag_ptrs,
                         at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ticket, int64_t timeout_ns, at::Tensor status);
 int64_t tc_linear_error();
+at::Tensor tc_stream_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
+int64_t tc_stream_error();
 }  // namespace ax
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -159,4 +161,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_linear", &ax::tc_linear, py::arg("x"), py::arg("w"), py::arg("residual") = py::none());
   m.def("tc_linear_to_slots", &ax::tc_linear_to_slots);
   m.def("tc_linear_error", &ax::tc_linear_error);
+  m.def("tc_stream_linear", &ax::tc_stream_linear, py::arg("x"), py::arg("w"), py::arg("residual") = py::none());
+  m.def("tc_stream_error", &ax::tc_stream_error);
 }

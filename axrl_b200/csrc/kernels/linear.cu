@@ -36,30 +36,59 @@ static void tn(const void* A, const void* B, const void* C, void* D, int M, int 
 // calls): up to 16 activation rows and 64M weight elements the streaming kernels (skinny_gemm.cu,
 // cp.async ring; skinny_tma.cu, TMA ring) beat the tcgen05 swap-AB GEMM by 10-40%; from 32 rows on
 // and for the large gate/up and vocabulary matrices the tcgen05 GEMM streams at least as fast.
-// AXRL_DECODE_GEMM = skinny | tma | tcgen05 overrides the choice (benchmarking).
-enum DecodeGemm { kTcgen05 = 0, kSkinny = 1, kTma = 2 };
+// AXRL_DECODE_GEMM = skinny | tma | tcgen05 | tcstream overrides the choice (tcstream: the
+// hand-written tcgen05 weight-streaming kernel of tcgemm.cu, 1..64 rows).
+enum DecodeGemm { kTcgen05 = 0, kSkinny = 1, kTma = 2, kTcStream = 3 };
+
+void tcgemm_stream(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, float* ws, int* cnt, int* err, bool prefetch_w,
+                   cudaStream_t st);
+
+// Zero-initialised, self-cleaning workspace of the streaming kernel, one per device.
+struct StreamWorkspace {
+  at::Tensor ws, cnt, err;
+};
+static StreamWorkspace& stream_workspace(int dev) {
+  static StreamWorkspace w[64];
+  if (!w[dev].ws.defined()) {
+    auto o = at::TensorOptions().device(at::kCUDA, dev);
+    w[dev].ws = at::zeros({64L * 262144}, o.dtype(at::kFloat));
+    w[dev].cnt = at::zeros({4 * 2048}, o.dtype(at::kInt));
+    w[dev].err = at::zeros({1}, o.dtype(at::kInt));
+  }
+  return w[dev];
+}
+
+static void tc_stream_into(const at::Tensor& x, const at::Tensor& w, const bf16* r, at::Tensor& y) {
+  const int M = x.size(0), N = w.size(0), K = x.size(1);
+  AX_CHECK(N <= 262144, "tcstream: N <= 262144");
+  auto& ws = stream_workspace(x.get_device());
+  tcgemm_stream(x.data_ptr(), w.data_ptr(), r, y.data_ptr(), M, N, K, ws.ws.data_ptr<float>(), ws.cnt.data_ptr<int>(),
+                ws.err.data_ptr<int>(), weights_static(), stream());
+}
 
 static int decode_gemm_mode() {
   static int mode = [] {
     const char* e = std::getenv("AXRL_DECODE_GEMM");
     if (!e) return -1;
     std::string v(e);
-    return v == "skinny" ? (int)kSkinny : v == "tma" ? (int)kTma : v == "tcgen05" ? (int)kTcgen05 : -1;
+    return v == "skinny" ? (int)kSkinny : v == "tma" ? (int)kTma : v == "tcgen05" ? (int)kTcgen05 : v == "tcstream" ? (int)kTcStream : -1;
   }();
   return mode;
 }
 
 static DecodeGemm decode_gemm(int M, int N, int K) {
-  if (M > 16 || K % 64 || N % 8 || (long)N * K > (64L << 20)) return kTcgen05;
   const int forced = decode_gemm_mode();
-  return forced >= 0 ? (DecodeGemm)forced : kSkinny;
+  if (forced == kTcStream && M <= 64 && K % 64 == 0 && N % 8 == 0 && N <= 262144) return kTcStream;
+  if (M > 16 || K % 64 || N % 8 || (long)N * K > (64L << 20)) return kTcgen05;
+  return forced >= 0 && forced != kTcStream ? (DecodeGemm)forced : kSkinny;
 }
 
 static bool streaming_into(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& r, at::Tensor& y) {
   const int M = x.size(0), N = w.size(0), K = x.size(1);
   const DecodeGemm g = decode_gemm(M, N, K);
   if (g == kTcgen05) return false;
-  if (g == kSkinny) skinny_linear_out(x, w, r, y);
+  if (g == kTcStream) tc_stream_into(x, w, r ? (const bf16*)r->data_ptr() : nullptr, y);
+  else if (g == kSkinny) skinny_linear_out(x, w, r, y);
   else skinny_tma_linear_out(x, w, r, y);
   return true;
 }
@@ -84,6 +113,10 @@ at::Tensor linear_fwd(at::Tensor x, at::Tensor w) {
   if (M == 0 || N == 0) return y;
   if (K == 0) return y.zero_();
   if (M <= 64) {  // decode: weight streaming
+    if (decode_gemm(M, N, K) == kTcStream) {
+      tc_stream_into(x, w, nullptr, y);
+      return y;
+    }
     if (decode_gemm(M, N, K) == kSkinny) return skinny_linear(x, w, c10::nullopt);
     if (decode_gemm(M, N, K) == kTma) return skinny_tma_linear(x, w, c10::nullopt);
     gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K, stream());
@@ -103,6 +136,10 @@ at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual) {
   auto y = at::empty({M, N}, x.options());
   if (M == 0 || N == 0) return y;
   if (M <= 64) {
+    if (decode_gemm(M, N, K) == kTcStream) {
+      tc_stream_into(x, w, (const bf16*)residual.data_ptr(), y);
+      return y;
+    }
     if (decode_gemm(M, N, K) == kSkinny) return skinny_linear(x, w, residual);
     if (decode_gemm(M, N, K) == kTma) return skinny_tma_linear(x, w, residual);
     gemm::tn_swapab(x.data_ptr(), w.data_ptr(), residual.data_ptr(), y.data_ptr(), M, N, K, stream());
@@ -185,6 +222,11 @@ at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant) {
   if (variant == "tma") return skinny_tma_linear(x, w, c10::nullopt);
   auto y = at::empty({M, N}, x.options());
   if (M == 0) return y;
+  if (variant == "tcstream") {
+    AX_CHECK(M <= 64, "tcstream needs M <= 64");
+    tc_stream_into(x, w, nullptr, y);
+    return y;
+  }
   if (variant == "swapab") {
     AX_CHECK(M <= 64, "swapab needs M <= 64");
     gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K, stream());
@@ -318,6 +360,24 @@ void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_
                      reinterpret_cast<unsigned*>(ticket.data_ptr<int>()) + ch, (uint64_t)timeout_ns, status.data_ptr<int>(),
                      tcgemm_err(x.get_device()).data_ptr<int>(), stream());
 }
+
+// Decode-size GEMM on the tcgen05 weight-streaming kernel (1..64 rows), for tests and benchmarks.
+at::Tensor tc_stream_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  const int M = x.size(0), N = w.size(0);
+  AX_CHECK(M >= 1 && M <= 64 && x.size(1) == w.size(1), "1..64 rows, K match");
+  auto y = at::empty({M, N}, x.options());
+  const bf16* r = nullptr;
+  if (residual.has_value()) {
+    check_bf16_2d(*residual, "residual");
+    r = (const bf16*)residual->data_ptr();
+  }
+  tc_stream_into(x, w, r, y);
+  return y;
+}
+
+int64_t tc_stream_error() { return stream_workspace(c10::cuda::current_device()).err.item<int>(); }
 
 int64_t tc_linear_error() { return tcgemm_err(c10::cuda::current_device()).item<int>(); }
 

@@ -344,6 +344,214 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
   }
 }
 
+// ---------------------------------------------------------------------------------- weight streaming (decode)
+// Y[M, N] = X[M, K] @ W[N, K]^T (+ R) for M <= 64 token rows, computed transposed on the tensor
+// cores: Y^T tile (128 weight rows x NTOK tokens) = W tile (128 x K, the MMA's M) @ X^T.  At decode
+// sizes the GEMM is a read of W, so the grid is one CTA per SM and every CTA streams the same
+// number of (128-row W tile, 64-wide K slab) units, a contiguous range in tile-major order:
+//
+//   warp 0      TMA producer: W slab (16 KB) + X slab (NTOK x 64) into an 8-stage ring; with
+//               `prefetch_w` (weights read-only during the rollout) the first W slabs are issued
+//               before waiting for the preceding kernel (programmatic dependent launch).
+//   warp 1      MMA issuer: four tcgen05.mma (M 128, N NTOK, K 16) per slab into one of two TMEM
+//               accumulators; a run of slabs of one W tile is a segment.
+//   warps 2-5   epilogue per segment, warp w owning weight rows 32 (w % 4) .. +31 of the tile (its
+//               TMEM lanes): a segment that covers the whole K range stores bf16 (+ R) directly;
+//               otherwise the fp32 partial is added to a workspace (red.global.add) and the
+//               stripe's arrival counter is advanced by the slabs covered; the warp that completes
+//               the stripe adds R, stores bf16 and zeroes the workspace stripe and counter, so the
+//               workspace is clean for the next call without a memset.  Calls sharing a workspace
+//               must be stream-ordered.
+namespace sk {
+constexpr int BW = 128, BK = 64, STAGES = 8, THREADS = 192;
+constexpr uint32_t TMEM_COLS = 128;  // two accumulators of up to 64 columns
+enum { B_FULL = 0, B_EMPTY = STAGES, B_ACC_FULL = 2 * STAGES, B_ACC_EMPTY = 2 * STAGES + 2, B_DRAIN = 2 * STAGES + 4, NBAR = 2 * STAGES + 5 };
+
+struct Params {
+  int M, N, K;
+  int kslabs, units, per;
+  const bf16* r;
+  bf16* y;
+  float* ws;  // M x N fp32, zero between calls
+  int* cnt;   // 4 counters per W tile, zero between calls
+  int* err;
+  int prefetch_w;
+};
+
+__device__ __forceinline__ void red_add(float* p, float v) { asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory"); }
+
+template <int NTOK>
+__device__ __forceinline__ void flush_stripe(const Params& p, int tile, int slabs, const uint32_t (&v)[NTOK], int lane, int q) {
+  const int n = tile * BW + q * 32 + lane;
+  const bool full = slabs == p.kslabs;
+  if (full) {
+    if (n < p.N)
+#pragma unroll 4
+      for (int t = 0; t < NTOK; ++t) {
+        if (t >= p.M) break;
+        float f = __uint_as_float(v[t]);
+        if (p.r) f += __bfloat162float(p.r[(long)t * p.N + n]);
+        p.y[(long)t * p.N + n] = __float2bfloat16_rn(f);
+      }
+    return;
+  }
+  if (n < p.N)
+#pragma unroll 4
+    for (int t = 0; t < NTOK; ++t) {
+      if (t >= p.M) break;
+      red_add(p.ws + (long)t * p.N + n, __uint_as_float(v[t]));
+    }
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    int* c = p.cnt + tile * 4 + q;
+    last = atomicAdd(c, slabs) + slabs == p.kslabs;
+    if (last) *c = 0;  // every contributor has arrived: reset for the next call
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  if (n < p.N)
+    for (int t = 0; t < p.M; ++t) {
+      float* w = p.ws + (long)t * p.N + n;
+      float f = __ldcg(w);
+      *w = 0.f;
+      if (p.r) f += __bfloat162float(p.r[(long)t * p.N + n]);
+      p.y[(long)t * p.N + n] = __float2bfloat16_rn(f);
+    }
+}
+
+template <int NTOK>
+__global__ void __launch_bounds__(THREADS, 1) stream_k(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, Params p) {
+  constexpr int W_BYTES = BW * BK * 2, X_BYTES = NTOK * BK * 2, STAGE = W_BYTES + X_BYTES;
+  constexpr uint32_t IDS = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NTOK >> 3) << 17) | ((uint32_t)(BW >> 4) << 24);
+  extern __shared__ char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + STAGES * STAGE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u0 = blockIdx.x * p.per, u1 = min(p.units, u0 + p.per);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tg::mbar_init(&bar[B_FULL + s], 1);
+      tg::mbar_init(&bar[B_EMPTY + s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tg::mbar_init(&bar[B_ACC_FULL + a], 1);
+      tg::mbar_init(&bar[B_ACC_EMPTY + a], 4);
+    }
+    tg::mbar_init(&bar[B_DRAIN], 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tg::s32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tg::fence_before();
+  __syncthreads();
+  tg::fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int n_units = max(0, u1 - u0);
+      int pre = 0;
+      if (p.prefetch_w) {  // weight slabs do not depend on the preceding kernel
+        pre = min(n_units, STAGES);
+        for (int i = 0; i < pre; ++i) {
+          const int u = u0 + i;
+          tg::expect_tx(&bar[B_FULL + i], STAGE);
+          tg::tma2d(sm + i * STAGE, &tw, (u % p.kslabs) * BK, (u / p.kslabs) * BW, &bar[B_FULL + i]);
+        }
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int i = 0; i < pre; ++i) {
+        const int u = u0 + i;
+        tg::tma2d(sm + i * STAGE + W_BYTES, &tx, (u % p.kslabs) * BK, 0, &bar[B_FULL + i]);
+      }
+      int i = pre;
+      for (; i < n_units; ++i) {
+        const int s = i % STAGES, u = u0 + i;
+        if (i >= STAGES && !tg::wait(&bar[B_EMPTY + s], ((i / STAGES) - 1) & 1, abort, p.err, 21)) break;
+        tg::expect_tx(&bar[B_FULL + s], STAGE);
+        tg::tma2d(sm + s * STAGE, &tw, (u % p.kslabs) * BK, (u / p.kslabs) * BW, &bar[B_FULL + s]);
+        tg::tma2d(sm + s * STAGE + W_BYTES, &tx, (u % p.kslabs) * BK, 0, &bar[B_FULL + s]);
+      }
+      if (*abort) {
+        int zero = 0;
+        for (int k = max(0, i - STAGES); k < i; ++k) tg::wait(&bar[B_FULL + k % STAGES], (k / STAGES) & 1, (volatile int*)&zero, p.err, 21);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int i = 0, seg = 0;
+      bool ok = true;
+      while (ok && u0 + i < u1) {
+        const int tile = (u0 + i) / p.kslabs, a = seg & 1;
+        if (seg >= 2 && !tg::wait(&bar[B_ACC_EMPTY + a], ((seg >> 1) - 1) & 1, abort, p.err, 22)) break;
+        tg::fence_after();
+        int j = 0;
+        for (; u0 + i < u1 && (u0 + i) / p.kslabs == tile; ++i, ++j) {
+          const int s = i % STAGES;
+          if (!tg::wait(&bar[B_FULL + s], (i / STAGES) & 1, abort, p.err, 23)) {
+            ok = false;
+            break;
+          }
+          tg::fence_after();
+          const uint32_t sw = tg::s32(sm + s * STAGE), sx = sw + W_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) tg::mma(tmem + a * 64, tg::desc_k128(sw + kk * 32), tg::desc_k128(sx + kk * 32), IDS, (j | kk) ? 1u : 0u);
+          tg::commit(&bar[B_EMPTY + s]);
+        }
+        if (!ok) break;
+        tg::commit(&bar[B_ACC_FULL + a]);
+        ++seg;
+      }
+      tg::commit(&bar[B_DRAIN]);
+      int zero = 0;
+      tg::wait(&bar[B_DRAIN], 0, (volatile int*)&zero, p.err, 24);
+    }
+  } else {
+    const int q = warp & 3;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    int i = 0, seg = 0;
+    while (u0 + i < u1) {
+      const int tile = (u0 + i) / p.kslabs, a = seg & 1;
+      int slabs = 0;
+      while (u0 + i < u1 && (u0 + i) / p.kslabs == tile) ++i, ++slabs;
+      if (!__all_sync(0xffffffffu, tg::wait(&bar[B_ACC_FULL + a], (seg >> 1) & 1, abort, p.err, 25))) break;
+      tg::fence_after();
+      uint32_t v[NTOK];
+      {
+        uint32_t t32[32];
+        tg::tmem_ld32(lane_base + a * 64, t32);
+#pragma unroll
+        for (int e = 0; e < 32 && e < NTOK; ++e) v[e] = t32[e];
+        if constexpr (NTOK == 64) {
+          tg::tmem_ld32(lane_base + a * 64 + 32, t32);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[32 + e] = t32[e];
+        }
+      }
+      tg::fence_before();
+      __syncwarp();
+      if (lane == 0) tg::arrive(&bar[B_ACC_EMPTY + a]);  // the accumulator may be reused while this stripe is stored
+      flush_stripe<NTOK>(p, tile, slabs, v, lane, q);
+      ++seg;
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tg::fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+}  // namespace sk
+
 // ---------------------------------------------------------------------------------- host side
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
@@ -398,7 +606,40 @@ static void launch(const void* A, const void* B, Params p, cudaStream_t st) {
   launch_pdl(gemm_k<MODE>, dim3(grid), dim3(THREADS), (size_t)smem_bytes(), st, ta, tb, p);
 }
 
+template <int NTOK>
+static void launch_stream(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, float* ws, int* cnt, int* err,
+                          bool prefetch_w, cudaStream_t st) {
+  constexpr int STAGE = sk::BW * sk::BK * 2 + NTOK * sk::BK * 2;
+  const int smem = sk::STAGES * STAGE + sk::NBAR * 8 + 16 + 1024;
+  static bool attr[64] = {false};
+  int dev = 0;
+  AX_CUDA_OK(cudaGetDevice(&dev));
+  if (!attr[dev]) {
+    AX_CUDA_OK(cudaFuncSetAttribute(sk::stream_k<NTOK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr[dev] = true;
+  }
+  const CUtensorMap tw = kmajor_map(W, N, K, sk::BW);
+  const CUtensorMap tx = kmajor_map(X, M, K, NTOK);
+  sk::Params p{};
+  p.M = M, p.N = N, p.K = K, p.kslabs = K / sk::BK;
+  p.units = ((N + sk::BW - 1) / sk::BW) * p.kslabs;
+  const int grid = std::min(num_sms(), p.units);
+  p.per = (p.units + grid - 1) / grid;
+  p.r = static_cast<const bf16*>(R), p.y = static_cast<bf16*>(Y), p.ws = ws, p.cnt = cnt, p.err = err, p.prefetch_w = prefetch_w ? 1 : 0;
+  launch_pdl(sk::stream_k<NTOK>, dim3((p.units + p.per - 1) / p.per), dim3(sk::THREADS), (size_t)smem, st, tw, tx, p);
+}
+
 }  // namespace tg
+
+// Decode-size GEMM (M <= 64 rows) streaming the weights on the tensor cores.  ws: M x N fp32 and
+// cnt: 4 * ceil(N / 128) ints, both zero and left zero; calls sharing them must be stream-ordered.
+void tcgemm_stream(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, float* ws, int* cnt, int* err, bool prefetch_w,
+                   cudaStream_t st) {
+  AX_REQUIRE(M >= 1 && M <= 64, "tcgemm_stream: 1..64 rows, got ", M);
+  AX_REQUIRE(K % 64 == 0 && N % 8 == 0, "tcgemm_stream: K multiple of 64, N multiple of 8");
+  if (M <= 32) tg::launch_stream<32>(X, W, R, Y, M, N, K, ws, cnt, err, prefetch_w, st);
+  else tg::launch_stream<64>(X, W, R, Y, M, N, K, ws, cnt, err, prefetch_w, st);
+}
 
 // D[M,N] (+)= A[M,K] @ B[N,K]^T (+ C), bf16; err: device int that records a wait timeout.
 void tcgemm_tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K, int* err, cudaStream_t st) {

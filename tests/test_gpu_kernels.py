@@ -635,3 +635,23 @@ def test_tcgemm_matches_fp32(M, N, K):
     assert e.tc_linear_error() == 0
     close(y, ref, 2e-2, 1e-2, msg="tcgemm")
     close(y2, ref + r.float(), 3e-2, 1e-2, msg="tcgemm + residual")
+
+
+@pytest.mark.skipif(os.environ.get("AXRL_TEST_TCGEMM") != "1", reason="tcgen05 weight-streaming GEMM: opt-in until validated on a B200")
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (17, 6144, 4096), (32, 4096, 12288), (33, 1000, 512), (64, 24576, 4096), (64, 4096, 64)])
+def test_tcgemm_stream_matches_fp32(M, N, K):
+    """Decode-size GEMM streaming the weights on tcgen05: split-K partials through the self-cleaning
+    workspace (several calls in a row) and whole-tile direct stores, with a residual."""
+    e = _ext()
+    torch.manual_seed(M * 7 + N)
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    for it in range(3):
+        x = torch.randn(M, K, device=DEV).bfloat16()
+        r = torch.randn(M, N, device=DEV).bfloat16()
+        ref = x.float() @ w.float().t()
+        y = e.tc_stream_linear(x, w)
+        y2 = e.tc_stream_linear(x, w, r)
+        torch.cuda.synchronize()
+        assert e.tc_stream_error() == 0
+        close(y, ref, 2e-2, 1e-2, msg=f"tcstream call {it}")
+        close(y2, ref + r.float(), 3e-2, 1e-2, msg=f"tcstream + residual call {it}")
