@@ -81,3 +81,54 @@ def test_prefix_merging_layer_diff_is_tiny_in_fp32():
     rows = prefix_merging_layer_diff(m, [list(s.input_ids) for s in turns], merged)
     assert len(rows) == cfg.num_hidden_layers + 1
     assert all(r["max_abs"] < 1e-4 * max(1.0, r["ref_mean_abs"]) for r in rows), rows
+
+
+def test_tunnel_waits_for_url_and_stops(tmp_path):
+    import asyncio
+    import sys
+
+    import pytest
+
+    from axrl_b200.utils.tunnel import Tunnel, TunnelConfig
+
+    script = tmp_path / "fake_tunnel.py"
+    script.write_text("import sys, time\nprint('starting', flush=True)\nprint('ready at https://abc-def.trycloudflare.com/ port', sys.argv[1], flush=True)\n"
+                      "time.sleep(60)\n")
+
+    async def go():
+        cfg = TunnelConfig(command=[sys.executable, str(script), "{port}"], startup_timeout_seconds=20)
+        t = await Tunnel.start(cfg, template_vars={"port": 8123})
+        assert t.base_url == "https://abc-def.trycloudflare.com"
+        assert any("8123" in ln for ln in t.lines)
+        await t.stop()
+        assert t.process.returncode is not None
+        bad = TunnelConfig(command=[sys.executable, "-c", "print('no url here')"], startup_timeout_seconds=20)
+        with pytest.raises(RuntimeError, match="exited before"):
+            await Tunnel.start(bad, template_vars={})
+        with pytest.raises(FileNotFoundError):
+            await Tunnel.start(TunnelConfig(command=["definitely-not-a-binary-xyz"]), template_vars={})
+
+    asyncio.run(go())
+
+
+def test_hf_download_skips_existing_and_reports_offline(tmp_path, monkeypatch):
+    import pytest
+
+    from axrl_b200.configs import HfDataConfig
+    from axrl_b200.utils import hf_download
+
+    cfg = HfDataConfig(repo_id="org/ds", filename="x.parquet")
+    monkeypatch.setattr(HfDataConfig, "get_full_path", lambda self: tmp_path / "org" / "ds" / "x.parquet")
+    (tmp_path / "org" / "ds").mkdir(parents=True)
+    (tmp_path / "org" / "ds" / "x.parquet").write_bytes(b"1")
+    assert hf_download.download_data_file(cfg) == tmp_path / "org" / "ds" / "x.parquet"
+
+    class Offline:
+        def snapshot_download(self, **kw):
+            raise OSError("no network")
+
+    monkeypatch.setattr(hf_download, "_hub", lambda: Offline())
+    from axrl_b200.configs import ModelConfig
+
+    with pytest.raises(RuntimeError, match="could not download"):
+        hf_download.download_model(ModelConfig(name="org/model"))
