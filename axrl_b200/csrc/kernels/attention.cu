@@ -527,12 +527,13 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
 
 // Forward implementation: the tcgen05 kernel (attention_tc.cu) with 4 softmax warps;
 // AXRL_ATTN_FWD=mma selects the mma.sync kernel below, =tc8 the tcgen05 kernel with 8 softmax
-// warps (two per row) and packed bf16x2 exponentials, =tc2 the double-buffered-P variant.
+// warps (two per row) and packed bf16x2 exponentials, =tc8t the same with P in tensor memory,
+// =tc2 the double-buffered-P variant.
 static int tc_forward_mode() {  // -1: mma.sync, else the attn_fwd_tc variant
   static int mode = [] {
     const char* e = std::getenv("AXRL_ATTN_FWD");
     const std::string v = e ? e : "";
-    return v == "mma" ? -1 : v == "tc2" ? 1 : v == "tc8" ? 2 : 0;
+    return v == "mma" ? -1 : v == "tc2" ? 1 : v == "tc8" ? 2 : v == "tc8t" ? 3 : 0;
   }();
   return mode;
 }

@@ -340,6 +340,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
 // bf16x2 word and exponentiated with one ex2.approx.ftz.bf16x2 (the bf16 P the PV product
 // consumes), which halves the special-function work per tile; the row sum adds the same bf16
 // values in fp32.
+//
+// TMEM_P: P goes to tensor memory instead of shared memory (two buffers, TMEM columns [384, 448)
+// and [448, 512), written with tcgen05.st) and the PV product takes its A operand from there.
+// The softmax of tile j + 1 then no longer waits for PV(j): P buffer j % 2 is reused by tile j + 2,
+// and S(j + 2) completes only after every earlier MMA, PV(j) included, has.  Only the rare O
+// rescale waits for PV(j).
 constexpr int THREADS8 = 320;  // warps 0-7 softmax, 8 TMA producer, 9 MMA issuer
 constexpr int B8_Q = 0, B8_KV_FULL = 1, B8_KV_EMPTY = 3, B8_S_FULL = 5, B8_S_FREE = 7, B8_P_FULL = 9, B8_O_DONE = 10, B8_DRAIN = 11,
               B8_XCH = 12, NBAR8 = 16;
@@ -355,6 +361,7 @@ __device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
   return y;
 }
 
+template <bool TMEM_P>
 __global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                                                             const __grid_constant__ CUtensorMap tv, Params p) {
   extern __shared__ char smem_raw[];
@@ -441,9 +448,13 @@ __global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_const
         const uint32_t vb = v_base + (t & 1) * TILE;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = sdesc(p_base + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
           const uint64_t b = sdesc(vb + kk * 2048, HALF, 1024);
-          tc_mma(tmem + 256, a, b, ID_PV, (t > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (TMEM_P) {
+            tc_mma_ts(tmem + 256, tmem + 384 + (t & 1) * 64 + kk * 8, b, ID_PV, (t > 0 || kk > 0) ? 1u : 0u);
+          } else {
+            const uint64_t a = sdesc(p_base + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
+            tc_mma(tmem + 256, a, b, ID_PV, (t > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         tc_commit(&bar[B8_O_DONE]);
         tc_commit(&bar[B8_KV_EMPTY + (t & 1)]);
@@ -510,13 +521,20 @@ __global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_const
       mbar_arrive(xbar);
       if (!__all_sync(0xffffffffu, mbar_wait(xbar, j & 1, abort, p.err, 10))) break;
       mt = fmaxf(mt, xmax[((j & 1) * 2 + (half ^ 1)) * BM + r]);
-      // P_j overwrites P_{j-1} (and O may be rescaled) only once PV_{j-1} has finished
-      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&bar[B8_O_DONE], (j - 1) & 1, abort, p.err, 7))) break;
-      tc_fence_after();
+      if constexpr (!TMEM_P) {
+        // P_j overwrites P_{j-1} (and O may be rescaled) only once PV_{j-1} has finished
+        if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&bar[B8_O_DONE], (j - 1) & 1, abort, p.err, 7))) break;
+        tc_fence_after();
+      }
       const float m_new = fmaxf(m_used, mt);
       const bool raise = m_new > m_used + RESCALE_THRESHOLD;
       const bool rescale = raise && j >= 1 && m_used != -INFINITY;
       if (__any_sync(0xffffffffu, rescale)) {  // both halves of these rows decide alike
+        if constexpr (TMEM_P) {  // O may only be rescaled once PV_{j-1} has finished (its phase is the
+                                 // latest O_DONE can have reached: PV_j needs this tile's P)
+          if (!__all_sync(0xffffffffu, mbar_wait(&bar[B8_O_DONE], (j - 1) & 1, abort, p.err, 7))) break;
+          tc_fence_after();
+        }
         const float alpha = rescale ? exp2f(m_used - m_new) : 1.f;
         l *= alpha;
 #pragma unroll 1
@@ -532,20 +550,33 @@ __global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_const
       if (raise) m_used = m_new;
       float rs = 0.f;
       const bool live = m_used != -INFINITY;
+      if constexpr (TMEM_P) {
+        uint32_t w[32];
 #pragma unroll
-      for (int c8 = 0; c8 < BN / 16; ++c8) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float x0 = s[c8 * 8 + 2 * i] - m_used, x1 = s[c8 * 8 + 2 * i + 1] - m_used;
+        for (int i = 0; i < 32; ++i) {
+          const float x0 = s[2 * i] - m_used, x1 = s[2 * i + 1] - m_used;
           const uint32_t e = live ? ex2_bf16x2(pack_bf16x2(x0, x1)) : 0u;
           rs += __uint_as_float(e << 16) + __uint_as_float(e & 0xffff0000u);
           w[i] = e;
         }
-        *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tmem_st32u(lane_addr + 384 + (j & 1) * 64 + half * 32, w);
+        tmem_st_wait();
+      } else {
+#pragma unroll
+        for (int c8 = 0; c8 < BN / 16; ++c8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float x0 = s[c8 * 8 + 2 * i] - m_used, x1 = s[c8 * 8 + 2 * i + 1] - m_used;
+            const uint32_t e = live ? ex2_bf16x2(pack_bf16x2(x0, x1)) : 0u;
+            rs += __uint_as_float(e << 16) + __uint_as_float(e & 0xffff0000u);
+            w[i] = e;
+          }
+          *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
       }
       l += rs;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B8_P_FULL]);
@@ -628,7 +659,8 @@ static at::Tensor& err_flag(int dev) {
 }  // namespace atc
 
 // q (T,Hq,128), k/v (Tk,Hkv,128) -> o (T,Hq,128) bf16, lse2 (Hq,T) fp32 (base-2, +inf for rows without keys)
-// variant: 0 = 4 softmax warps, 1 = 4 softmax warps with double-buffered P, 2 = 8 softmax warps
+// variant: 0 = 4 softmax warps, 1 = 4 softmax warps with double-buffered P, 2 = 8 softmax warps,
+// 3 = 8 softmax warps with P in tensor memory
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles, double scale,
                                     int64_t variant) {
   using namespace atc;
@@ -646,15 +678,17 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
   const CUtensorMap tv = map_rows(v.data_ptr(), Tk, (long)Hkv * D);
   Params p{(bf16*)o.data_ptr(), lse2.data_ptr<float>(), qseg.data_ptr<int>(), kr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
            (float)(scale * 1.4426950408889634), err_flag(q.get_device()).data_ptr<int>()};
-  if (variant == 2) {
+  if (variant == 2 || variant == 3) {
     const int smem8 = 6 * TILE + 3 * 2 * BM * 4 + NBAR8 * 8 + 16 + 1024;
-    static bool attr8[16] = {false};
+    static bool attr8[2][16] = {{false}};
     const int dev = q.get_device();
-    if (!attr8[dev]) {
-      AX_CUDA_OK(cudaFuncSetAttribute(attn_fwd_tc8_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem8));
-      attr8[dev] = true;
+    const int tp = variant == 3;
+    auto* kern = tp ? attn_fwd_tc8_k<true> : attn_fwd_tc8_k<false>;
+    if (!attr8[tp][dev]) {
+      AX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem8));
+      attr8[tp][dev] = true;
     }
-    attn_fwd_tc8_k<<<dim3(nt, Hq), THREADS8, smem8, stream()>>>(tq, tk, tv, p);
+    kern<<<dim3(nt, Hq), THREADS8, smem8, stream()>>>(tq, tk, tv, p);
     AX_LAUNCH_OK();
     return {o, lse2};
   }
