@@ -54,6 +54,7 @@ def _args():
     ap.add_argument("--ep", type=int, default=None,
                     help="expert parallelism for MoE models (default: every GPU, dense parts data-parallel over the same ranks)")
     ap.add_argument("--ep-backend", choices=["p2p", "torch"], default="p2p", help="EP dispatch / combine: NVLink kernels or NCCL all-to-all")
+    ap.add_argument("--deterministic", action="store_true", help="deterministic attention backward (separate dQ pass)")
     ap.add_argument("--verbose", action="store_true")
     return ap.parse_args()
 
@@ -145,7 +146,10 @@ def main() -> None:
     from axrl_b200.train.engine import ParallelCtx, TrainEngine
 
     mcfg = resolve_preset(a.model)
-    wc = MegatronWorkerConfig(recompute_granularity="full", max_tokens_per_micro_batch=a.mb_tokens, seed=1234)
+    # deterministic_mode=False: the attention backward accumulates dQ with fp32 atomics (the
+    # deterministic variant adds a separate dQ pass); stated in the printed config
+    wc = MegatronWorkerConfig(recompute_granularity="full", max_tokens_per_micro_batch=a.mb_tokens, seed=1234,
+                              deterministic_mode=a.deterministic)
     grpo = GrpoTrainerConfig(loss_type="grpo", mismatch_token_clip_max=2.0)
     ep = (a.ep or world) if mcfg.is_moe else 1
     if ep not in (1, world):
@@ -239,7 +243,7 @@ def main() -> None:
                        "seq_len": a.prompt_len + a.max_len, "prompt_len": a.prompt_len,
                        "response_len": f"lognormal(median {a.median:g}, sigma 1) clipped [16,{a.max_len}]",
                        "micro_batch_tokens": a.mb_tokens, "parallelism": f"dp{world}" + (f"ep{ep}" if ep > 1 else ""), "colocated": True,
-                       "ref_logprobs": not a.no_ref, "kv_pool_gb": round(kv_gb, 1), "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
+                       "ref_logprobs": not a.no_ref, "deterministic_attention_backward": a.deterministic, "kv_pool_gb": round(kv_gb, 1), "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
             "sync_s": round(sum(m["sync_s"] for m in step_metrics) / len(step_metrics), 4),
             "step_breakdown_s": {k: round(v, 3) for k, v in zip(phases, ph)},
             "step_breakdown_note": "wall seconds per step, mean over the timed steps, max over ranks",
