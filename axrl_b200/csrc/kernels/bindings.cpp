@@ -87,6 +87,7 @@ void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_
 int64_t tc_linear_error();
 at::Tensor tc_stream_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 int64_t tc_stream_error();
+int64_t decode_tma_error();
 }  // namespace ax
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -163,4 +164,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_linear_error", &ax::tc_linear_error);
   m.def("tc_stream_linear", &ax::tc_stream_linear, py::arg("x"), py::arg("w"), py::arg("residual") = py::none());
   m.def("tc_stream_error", &ax::tc_stream_error);
+  m.def("decode_tma_error", &ax::decode_tma_error);
 }

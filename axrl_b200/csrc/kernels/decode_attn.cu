@@ -10,6 +10,8 @@
 // 32-token slice.  The GQA group's q heads (<= 16) form the M=16 rows of mma.m16n8k16, so K/V
 // are read exactly once per kv head.  The grid's split count is fixed by the cache capacity
 // (graph-capture friendly); CTAs past a sequence's end exit.  A combine kernel merges splits.
+#include <string>
+
 #include "common.cuh"
 
 namespace ax {
@@ -367,6 +369,19 @@ void decode_plan(at::Tensor seq_lens, at::Tensor prefix) {
   AX_LAUNCH_OK();
 }
 
+void paged_decode_attn_tma_partials(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table, at::Tensor seq_lens,
+                                    at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, at::Tensor prefix, int max_len);
+
+// AXRL_DECODE_ATTN=tma: the TMA page-pipeline kernel (decode_attn_tma.cu) for planned launches
+// with 64-token pages.
+static bool decode_tma_enabled() {
+  static bool on = [] {
+    const char* e = std::getenv("AXRL_DECODE_ATTN");
+    return e && std::string(e) == "tma";
+  }();
+  return on;
+}
+
 void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table, at::Tensor seq_lens, at::Tensor out,
                        at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, c10::optional<at::Tensor> prefix) {
   using namespace dec;
@@ -390,7 +405,10 @@ void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bl
     AX_CUDA_OK(cudaFuncSetAttribute(decode_persist_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr[dev] = true;
   }
-  if (prefix.has_value()) {  // planned: persistent grid over the live work items
+  if (prefix.has_value() && decode_tma_enabled() && P == 64) {  // planned, TMA page pipeline
+    AX_CHECK(prefix->scalar_type() == at::kInt && prefix->numel() >= B + 1, "prefix: int32 (B + 1)");
+    paged_decode_attn_tma_partials(q, kc, vc, block_table, seq_lens, part_o, part_ml, splits, scale, *prefix, max_len);
+  } else if (prefix.has_value()) {  // planned: persistent grid over the live work items
     AX_CHECK(prefix->scalar_type() == at::kInt && prefix->numel() >= B + 1, "prefix: int32 (B + 1)");
     launch_pdl(decode_persist_k, dim3(num_sms() * 3), dim3(128), smem, stream(), p, (const int*)prefix->data_ptr<int>(), B);
   } else {

@@ -1,0 +1,336 @@
+// Paged decode attention with a TMA page pipeline (one new query token per sequence, split-KV).
+//
+// Same work list, partial buffers and combine kernel as decode_attn.cu (128-token splits of each
+// sequence, (sequence, split, kv head) items numbered by decode_plan), but every CTA of the
+// persistent grid streams the K / V pages of ALL its items through one ring, so loads never stop at
+// an item boundary:
+//
+//   warp 4      producer (one thread): for each 64-token page of each item, four 2-D TMA loads
+//               (K and V, two 64-column boxes each, 128-byte swizzle; the cache viewed as
+//               (pages * Hkv * 64) rows of 128 values) into a 4-stage ring of 32 KB slots.
+//   warps 0-3   one item at a time: the GQA group's q heads (<= 16) are the M = 16 rows of
+//               mma.sync m16n8k16; warp w takes tokens 32 (w % 2) .. +31 of the item's page w / 2;
+//               online softmax per warp, then a cross-warp merge through shared memory and the
+//               item's (max, sum, unnormalised output) partial.
+//
+// The page size must be 64.  Reference counterpart: the rollout engine's decode attention backends
+// (SGLang FA3 / FlashInfer), reached via axrl/worker/sglang_worker.py:80-107.  Every wait is bounded:
+// on expiry the CTA records an error code, lets its copies land and exits; the consumers decide to
+// stop only after a barrier, so all four reach the same barriers.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace ax {
+namespace dtm {
+
+constexpr int D = 128, PAGE = 64, SPLIT = 128, STAGES = 4, CW = 4, THREADS = 160;
+constexpr int BOX = PAGE * 64 * 2;  // 64 rows x 64 columns bf16 = 8 KB
+constexpr int SLOT = 4 * BOX;       // K lo, K hi, V lo, V hi
+constexpr int RS = D + 2;           // merge buffer row: D outputs, max, sum
+
+struct Params {
+  const bf16* q;          // (B, Hq, D)
+  const int* bt;          // (B, max_pages)
+  const int* seq_lens;    // (B,)
+  const int* prefix;      // (B + 1,) items per sequence (128-token splits), cumulative
+  float* part_o;          // (B, Hq, splits, D)
+  float* part_ml;         // (B, Hq, splits, 2)
+  int B, Hq, Hkv, max_pages, splits, max_len;
+  float scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t sa(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// byte offset of (row, col) in a page slot region of two 64-column 128-byte-swizzled boxes
+__device__ __forceinline__ uint32_t pg_off(int row, int col) {
+  return (uint32_t)((col >> 6) * BOX + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
+}
+__device__ __forceinline__ int q_swz(int row, int col) { return row * (D * 2) + (((col >> 3) ^ (row & 7)) << 4) + (col & 7) * 2; }
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3]) : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  bf162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+struct Item {
+  int b, hk, sp, t0, len, npages;
+};
+__device__ __forceinline__ Item item_of(const Params& p, int w) {
+  Item it;
+  it.hk = w % p.Hkv;
+  const int j = w / p.Hkv;
+  int lo = 0, hi = p.B - 1;  // last b with prefix[b] <= j
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.prefix[mid] <= j) lo = mid;
+    else hi = mid - 1;
+  }
+  it.b = lo;
+  it.sp = j - p.prefix[lo];
+  it.len = min(p.seq_lens[lo], p.max_len);
+  it.t0 = it.sp * SPLIT;
+  const int rem = it.len - it.t0;
+  it.npages = rem <= 0 ? 0 : min(SPLIT / PAGE, (rem + PAGE - 1) / PAGE);
+  return it;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                                                        Params p) {
+  extern __shared__ char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  char* ring = sm;                                           // STAGES x SLOT
+  char* sQ = ring + STAGES * SLOT;                           // 2 x (16 x 128 bf16)
+  float* sRed = reinterpret_cast<float*>(sQ + 2 * 16 * D * 2);  // CW x 16 x RS
+  uint64_t* full = reinterpret_cast<uint64_t*>(sRed + CW * 16 * RS);
+  uint64_t* empty = full + STAGES;
+  volatile int* abort = reinterpret_cast<volatile int*>(empty + STAGES);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.Hq / p.Hkv;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 2);  // the two warps reading a page release it
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == CW) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      pdl_wait();  // the work list and block table come from the preceding kernels
+      const int total = p.prefix[p.B] * p.Hkv;
+      int pc = 0;
+      for (int w = blockIdx.x; w < total && !*abort; w += gridDim.x) {
+        const Item it = item_of(p, w);
+        for (int pg = 0; pg < it.npages; ++pg, ++pc) {
+          const int s = pc % STAGES;
+          if (pc >= STAGES && !tc::mbar_wait(&empty[s], ((pc / STAGES) - 1) & 1, abort, p.err, 31)) break;
+          const int page = p.bt[(long)it.b * p.max_pages + it.t0 / PAGE + pg];
+          const int y = (page * p.Hkv + it.hk) * PAGE;
+          tc::mbar_expect_tx(&full[s], SLOT);
+          char* dst = ring + s * SLOT;
+          tc::tma_2d(dst, &tk, 0, y, &full[s]);
+          tc::tma_2d(dst + BOX, &tk, 64, y, &full[s]);
+          tc::tma_2d(dst + 2 * BOX, &tv, 0, y, &full[s]);
+          tc::tma_2d(dst + 3 * BOX, &tv, 64, y, &full[s]);
+        }
+      }
+      if (*abort) {  // let every copy this CTA started land before shared memory is released
+        int zero = 0;
+        for (int i = max(0, pc - STAGES); i < pc; ++i) tc::mbar_wait(&full[i % STAGES], (i / STAGES) & 1, (volatile int*)&zero, p.err, 31);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers (warps 0-3)
+  pdl_wait();
+  const int total = p.prefix[p.B] * p.Hkv;
+  int pc = 0, n = 0;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const Item it = item_of(p, w);
+    if (it.npages == 0) continue;  // same decision in every warp
+    char* q_s = sQ + (n & 1) * 16 * D * 2;
+    for (int i = tid; i < 16 * 16; i += 128) {  // Q rows of the group (rows >= G are zero)
+      const int r = i >> 4, c = (i & 15) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < G) v = *reinterpret_cast<const uint4*>(p.q + ((long)it.b * p.Hq + it.hk * G + r) * D + c);
+      *reinterpret_cast<uint4*>(q_s + q_swz(r, c)) = v;
+    }
+    consumers_sync();  // Q visible; the previous item's merge buffer is free
+    if (*abort) break;
+    const int pg = warp >> 1;
+    const bool has = pg < it.npages;
+    const int s = (pc + pg) % STAGES;
+    const int rb = (warp & 1) * 32;  // first row of this warp's 32 tokens within the page
+    const int ws = it.t0 + pg * PAGE + rb, we = min(ws + 32, it.len);
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    float acc[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    if (has) {
+      const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&full[s], ((pc + pg) / STAGES) & 1, abort, p.err, 32));
+      if (ok && ws < we) {
+        const uint32_t kb = sa(ring + s * SLOT), vb = kb + 2 * BOX;
+        float sc[4][4];
+#pragma unroll
+        for (int nn = 0; nn < 4; ++nn) sc[nn][0] = sc[nn][1] = sc[nn][2] = sc[nn][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(sa(q_s + q_swz(lane & 15, kk * 16 + (lane >> 4) * 8)), a0, a1, a2, a3);
+#pragma unroll
+          for (int n2 = 0; n2 < 2; ++n2) {
+            uint32_t b0, b1, b2, b3;
+            const int key = n2 * 16 + (lane & 7) + (lane >> 4) * 8, col = kk * 16 + ((lane >> 3) & 1) * 8;
+            ldsm_x4(kb + pg_off(rb + key, col), b0, b1, b2, b3);
+            mma16816(sc[2 * n2], a0, a1, a2, a3, b0, b1);
+            mma16816(sc[2 * n2 + 1], a0, a1, a2, a3, b2, b3);
+          }
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float mx = -INFINITY;
+#pragma unroll
+          for (int nn = 0; nn < 4; ++nn)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int tok = ws + nn * 8 + (lane & 3) * 2 + e;
+              const float x = tok < we ? sc[nn][2 * hh + e] * p.scale_log2 : -INFINITY;
+              sc[nn][2 * hh + e] = x;
+              mx = fmaxf(mx, x);
+            }
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          m[hh] = mx;
+          float rsum = 0.f;
+#pragma unroll
+          for (int nn = 0; nn < 4; ++nn)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float v = exp2f(sc[nn][2 * hh + e] - mx);
+              sc[nn][2 * hh + e] = v;
+              rsum += v;
+            }
+          rsum += __shfl_xor_sync(0xffffffffu, rsum, 1);
+          rsum += __shfl_xor_sync(0xffffffffu, rsum, 2);
+          l[hh] = rsum;
+        }
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint32_t a0 = pack_bf16(sc[2 * kk][0], sc[2 * kk][1]), a1 = pack_bf16(sc[2 * kk][2], sc[2 * kk][3]);
+          const uint32_t a2 = pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]), a3 = pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+          for (int d2 = 0; d2 < 8; ++d2) {
+            uint32_t b0, b1, b2, b3;
+            const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, col = d2 * 16 + (lane >> 4) * 8;
+            ldsm_x4_t(vb + pg_off(rb + key, col), b0, b1, b2, b3);
+            mma16816(acc[2 * d2], a0, a1, a2, a3, b0, b1);
+            mma16816(acc[2 * d2 + 1], a0, a1, a2, a3, b2, b3);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty[s]);  // this warp is done with the page
+    }
+    // cross-warp merge
+    float* mine = sRed + warp * 16 * RS;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int r = (lane >> 2) + hh * 8;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        const int c = d * 8 + (lane & 3) * 2;
+        mine[r * RS + c] = acc[d][2 * hh];
+        mine[r * RS + c + 1] = acc[d][2 * hh + 1];
+      }
+      if ((lane & 3) == 0) {
+        mine[r * RS + D] = m[hh];
+        mine[r * RS + D + 1] = l[hh];
+      }
+    }
+    consumers_sync();
+    {
+      const int r = tid >> 3, c0 = (tid & 7) * 16;
+      if (r < G) {
+        float M = -INFINITY;
+        for (int w2 = 0; w2 < CW; ++w2) M = fmaxf(M, sRed[(w2 * 16 + r) * RS + D]);
+        float L = 0.f, o[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j] = 0.f;
+        for (int w2 = 0; w2 < CW; ++w2) {
+          const float mw = sRed[(w2 * 16 + r) * RS + D];
+          const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+          L += f * sRed[(w2 * 16 + r) * RS + D + 1];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] += f * sRed[(w2 * 16 + r) * RS + c0 + j];
+        }
+        const long base = (((long)it.b * p.Hq + it.hk * G + r) * p.splits + it.sp);
+        float* po = p.part_o + base * D + c0;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(po + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+        if ((tid & 7) == 0) {
+          p.part_ml[base * 2] = M;
+          p.part_ml[base * 2 + 1] = L;
+        }
+      }
+    }
+    pc += it.npages;
+    ++n;
+  }
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+static EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    AX_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess && ptr, "cuTensorMapEncodeTiled");
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+// the cache (pages, Hkv, 64, 128) as (pages * Hkv * 64) rows of 128 bf16; box 64 x 64, 128-byte swizzle
+static CUtensorMap cache_map(const void* base, long rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)PAGE};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AX_CHECK(r == CUDA_SUCCESS, "tensor map encode failed (", (int)r, ")");
+  return m;
+}
+static at::Tensor& err_flag(int dev) {
+  static at::Tensor e[64];
+  if (!e[dev].defined()) e[dev] = at::zeros({1}, at::TensorOptions().device(at::kCUDA, dev).dtype(at::kInt));
+  return e[dev];
+}
+}  // namespace dtm
+
+// The split-KV partials of paged_decode_attn from the TMA-fed kernel (page size 64, planned work
+// list).  Launches only the partial kernel; the caller runs the combine.
+void paged_decode_attn_tma_partials(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table, at::Tensor seq_lens,
+                                    at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, at::Tensor prefix, int max_len) {
+  using namespace dtm;
+  const int B = q.size(0), Hq = q.size(1), Hkv = kc.size(1);
+  AX_CHECK(kc.size(2) == PAGE && kc.size(3) == D && kc.is_contiguous() && vc.is_contiguous(), "TMA decode: page size 64, head dim 128");
+  const long rows = kc.size(0) * (long)Hkv * PAGE;
+  const CUtensorMap tk = cache_map(kc.data_ptr(), rows), tv = cache_map(vc.data_ptr(), rows);
+  Params p{(const bf16*)q.data_ptr(), block_table.data_ptr<int>(), seq_lens.data_ptr<int>(), prefix.data_ptr<int>(), part_o.data_ptr<float>(),
+           part_ml.data_ptr<float>(), B, Hq, Hkv, (int)block_table.size(1), (int)splits, max_len, (float)(scale * 1.4426950408889634),
+           err_flag(q.get_device()).data_ptr<int>()};
+  const int smem = STAGES * SLOT + 2 * 16 * D * 2 + CW * 16 * RS * 4 + 2 * STAGES * 8 + 16 + 1024;
+  static bool attr[64] = {false};
+  const int dev = q.get_device();
+  if (!attr[dev]) {
+    AX_CUDA_OK(cudaFuncSetAttribute(decode_tma_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr[dev] = true;
+  }
+  launch_pdl(decode_tma_k, dim3(num_sms()), dim3(THREADS), smem, stream(), tk, tv, p);
+  AX_LAUNCH_OK();
+}
+
+int64_t decode_tma_error() { return dtm::err_flag(c10::cuda::current_device()).item<int>(); }
+
+}  // namespace ax
