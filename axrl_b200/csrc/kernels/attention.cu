@@ -755,14 +755,14 @@ void set_attn_deterministic(bool on) { deterministic_flag() = on ? 1 : 0; }
 void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor lse2, at::Tensor dsum, at::Tensor dq_acc,
                        at::Tensor dk, at::Tensor dv, at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale);
 
-// Backward implementation: the mma.sync kernel below (measured faster on B200 so far);
-// AXRL_ATTN_BWD=tc selects the tcgen05 kernel (attention_tc_bwd.cu, 128-key tiles from
-// ``tiles_tc``).  Deterministic mode always runs the mma.sync key-tile kernel without dQ atomics
-// plus the separate dQ pass.
+// Backward implementation: the tcgen05 kernel (attention_tc_bwd.cu, 128-key tiles from
+// ``tiles_tc``; 307 TFLOP/s against 157 for the mma.sync kernel on the 15 872-token Qwen3-8B
+// pack); AXRL_ATTN_BWD=mma selects the mma.sync kernel below.  Deterministic mode always runs the
+// mma.sync key-tile kernel without dQ atomics plus the separate dQ pass.
 static int& tc_backward_flag() {
   static int on = [] {
     const char* e = std::getenv("AXRL_ATTN_BWD");
-    return (e && std::string(e) == "tc") ? 1 : 0;
+    return (e && std::string(e) == "mma") ? 0 : 1;
   }();
   return on;
 }

@@ -336,10 +336,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
 // 64-127).  The two threads of a row exchange their partial maxima through shared memory once per
 // tile (a per-pair mbarrier with bounded waits; the exchange buffer alternates with the tile
 // parity), so both raise the running maximum identically, and they add their partial row sums
-// once at the end.  P is computed in packed pairs: the two scaled scores are rounded to a
-// bf16x2 word and exponentiated with one ex2.approx.ftz.bf16x2 (the bf16 P the PV product
-// consumes), which halves the special-function work per tile; the row sum adds the same bf16
-// values in fp32.
+// once at the end.  P is exponentiated in fp32 (ex2.approx.ftz.f32) and rounded to bf16 pairs for
+// the PV product, with the row sum taken in fp32; exponentiating bf16x2 pairs instead
+// (ex2.approx.ftz.bf16x2, half the special-function work) rounds the exponent's input to bf16 and
+// moved the log-sum-exp by up to 6e-3 (log2 units) against fp32, so it is not used.
 //
 // TMEM_P: P goes to tensor memory instead of shared memory (two buffers, TMEM columns [384, 448)
 // and [448, 512), written with tcgen05.st) and the PV product takes its A operand from there.
@@ -355,9 +355,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
-__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -554,10 +554,9 @@ __global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_const
         uint32_t w[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float x0 = s[2 * i] - m_used, x1 = s[2 * i + 1] - m_used;
-          const uint32_t e = live ? ex2_bf16x2(pack_bf16x2(x0, x1)) : 0u;
-          rs += __uint_as_float(e << 16) + __uint_as_float(e & 0xffff0000u);
-          w[i] = e;
+          const float e0 = live ? ex2f(s[2 * i] - m_used) : 0.f, e1 = live ? ex2f(s[2 * i + 1] - m_used) : 0.f;
+          rs += e0 + e1;
+          w[i] = pack_bf16x2(e0, e1);
         }
         tmem_st32u(lane_addr + 384 + (j & 1) * 64 + half * 32, w);
         tmem_st_wait();
@@ -567,10 +566,9 @@ __global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_const
           uint32_t w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float x0 = s[c8 * 8 + 2 * i] - m_used, x1 = s[c8 * 8 + 2 * i + 1] - m_used;
-            const uint32_t e = live ? ex2_bf16x2(pack_bf16x2(x0, x1)) : 0u;
-            rs += __uint_as_float(e << 16) + __uint_as_float(e & 0xffff0000u);
-            w[i] = e;
+            const float e0 = live ? ex2f(s[c8 * 8 + 2 * i] - m_used) : 0.f, e1 = live ? ex2f(s[c8 * 8 + 2 * i + 1] - m_used) : 0.f;
+            rs += e0 + e1;
+            w[i] = pack_bf16x2(e0, e1);
           }
           *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }

@@ -127,10 +127,12 @@ def available() -> bool:
 
 
 def check_kernel_waits() -> None:
-    """Raise if the tcgen05 attention (bounded internal waits) gave up on a wait since the process
-    started: its outputs are then incomplete.  Synchronises the stream."""
+    """Raise if a kernel with bounded internal waits (tcgen05 attention forward / backward, the
+    hand-written tcgen05 GEMM) gave up on a wait since the process started: its outputs are then
+    incomplete.  Synchronises the stream."""
     e = ext()
-    codes = {"tcgen05 attention": int(e.attn_tc_error())}
+    codes = {"tcgen05 attention": int(e.attn_tc_error()), "tcgen05 attention backward": int(e.attn_bwd_tc_error()),
+             "tcgen05 GEMM": int(e.tc_linear_error())}
     bad = {k: v for k, v in codes.items() if v}
     if bad:
         raise RuntimeError(f"kernel wait timed out: {bad}")

@@ -41,7 +41,7 @@ def _args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", default="qwen3-8b")
     ap.add_argument("--prompts-per-gpu", type=int, default=4, help="groups trained per step per GPU")
-    ap.add_argument("--inflight-per-gpu", type=int, default=8, help="groups kept in generation per GPU (partial rollout)")
+    ap.add_argument("--inflight-per-gpu", type=int, default=16, help="groups kept in generation per GPU (partial rollout)")
     ap.add_argument("--no-partial", action="store_true", help="every step generates its own groups to completion")
     ap.add_argument("--group", type=int, default=8)
     ap.add_argument("--prompt-len", type=int, default=512)

@@ -539,7 +539,6 @@ def test_attention_tcgen05_forward_matches_reference(case, variant):
     close(lse[fin], lse2[fin], 1e-3, 1e-4, msg="lse")
 
 
-@pytest.mark.skipif(os.environ.get("AXRL_TEST_ATTN_BWD_TC") != "1", reason="8-warp tcgen05 backward: opt-in until validated on a B200")
 @pytest.mark.parametrize("case", [0, 1, 2, 3])
 def test_attention_tcgen05_backward_matches_mma(case):
     """tcgen05 backward (attention_tc_bwd.cu) against the mma.sync backward on the same inputs:
@@ -562,12 +561,11 @@ def test_attention_tcgen05_backward_matches_mma(case):
     scale = 1 / math.sqrt(D)
     o, lse = e.attn_fwd_mma(q, k, v, spec.qseg, spec.kr, spec.fwd_tiles, scale)
     e.set_attn_bwd_tc(False)
-    ref = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
-    e.set_attn_bwd_tc(True)
     try:
-        got = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
+        ref = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
     finally:
-        e.set_attn_bwd_tc(False)
+        e.set_attn_bwd_tc(True)
+    got = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
     torch.cuda.synchronize()
     assert e.attn_bwd_tc_error() == 0
     for name, a, b in zip(("dq", "dk", "dv"), got, ref):
@@ -620,7 +618,6 @@ def test_gdn_step_kernel_matches_reference():
     close(pool[slots], S_ref, 1e-4, 1e-4, msg="state")
 
 
-@pytest.mark.skipif(os.environ.get("AXRL_TEST_TCGEMM") != "1", reason="hand-written tcgen05 GEMM: opt-in until validated on a B200")
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 256), (4096, 4096, 4096), (1000, 6144, 4096), (77, 1056, 128)])
 def test_tcgemm_matches_fp32(M, N, K):
     """Persistent tcgen05 GEMM (tcgemm.cu) against fp32: ragged M, N a multiple of 32 but not of
