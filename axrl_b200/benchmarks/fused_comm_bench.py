@@ -75,6 +75,10 @@ def bench_tp(T: int, warmup: int, iters: int, tflops: float) -> list[dict]:
     w_dn = (torch.randn(H, F // N, device="cuda", generator=g) * 0.02).bfloat16()
     out = []
     ctxs = {b: TPContext.from_group(dist.group.WORLD, backend=b) for b in ("torch", "p2p")}
+    # the GEMM -> reduce-scatter fused into one tcgen05 kernel storing tiles into the owners' slots
+    os.environ["AXRL_TP_FUSED"] = "1"
+    ctxs["p2p_fused"] = TPContext.from_group(dist.group.WORLD, backend="p2p")
+    os.environ["AXRL_TP_FUSED"] = "0"
     ref_ag = column_parallel_linear(x_sp, w_gu, ctxs["torch"])
     ref_rs = row_parallel_linear(y, w_dn, ctxs["torch"])
     for name, fn, flops, nbytes, ref in (
@@ -91,8 +95,10 @@ def bench_tp(T: int, warmup: int, iters: int, tflops: float) -> list[dict]:
         target_ms = max(flops / (tflops * 1e12), nbytes / (NVLINK_GBS * 1e9)) * 1e3
         row.update({"gflop": round(flops / 1e9, 1), "nvlink_mb_per_gpu": round(nbytes / 1e6, 1), "roofline_ms": round(target_ms, 4),
                     "p2p_frac_of_roofline": round(target_ms / row["p2p_ms"], 3),
+                    "p2p_fused_frac_of_roofline": round(target_ms / row["p2p_fused_ms"], 3),
                     "nccl_frac_of_roofline": round(target_ms / row["torch_ms"], 3)})
         ctxs["p2p"].comm.check()
+        ctxs["p2p_fused"].comm.check()
         out.append(row)
     return out
 
