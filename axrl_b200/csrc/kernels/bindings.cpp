@@ -88,6 +88,8 @@ int64_t tc_linear_error();
 at::Tensor tc_stream_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 int64_t tc_stream_error();
 int64_t decode_tma_error();
+at::Tensor tc_linear_dgrad(at::Tensor dy, at::Tensor w);
+void tc_linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc, bool accumulate);
 }  // namespace ax
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -165,4 +167,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_stream_linear", &ax::tc_stream_linear, py::arg("x"), py::arg("w"), py::arg("residual") = py::none());
   m.def("tc_stream_error", &ax::tc_stream_error);
   m.def("decode_tma_error", &ax::decode_tma_error);
+  m.def("tc_linear_dgrad", &ax::tc_linear_dgrad);
+  m.def("tc_linear_wgrad_acc", &ax::tc_linear_wgrad_acc);
 }

@@ -45,6 +45,20 @@ static bool use_tcgemm() {
   return on;
 }
 
+void tcgemm_nn(const void* dY, const void* W, void* dX, int M, int Ko, int Nr, int* err, cudaStream_t st);
+void tcgemm_wgrad(const void* dY, const void* X, float* G, int Nw, int Kw, int T, bool accumulate, int* err, cudaStream_t st);
+
+// Backward GEMMs (data and weight gradients) on the hand-written kernel: AXRL_TRAIN_GEMM_BWD=tc
+// (CUTLASS otherwise).
+static bool use_tcgemm_bwd() {
+  static bool on = [] {
+    const char* e = std::getenv("AXRL_TRAIN_GEMM_BWD");
+    return e && std::string(e) == "tc";
+  }();
+  return on;
+}
+static bool tc_ok(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
 static void tn(const void* A, const void* B, const void* C, void* D, int M, int N, int K) {
   int dev = 0;
   if (M >= 512 && use_tcgemm() && K % 64 == 0 && N % 32 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0 &&
@@ -199,6 +213,10 @@ void linear_dgrad_into(at::Tensor dy, at::Tensor w, at::Tensor out) {
   int M = dy.size(0), N = dy.size(1), K = w.size(1);
   AX_CHECK(w.size(0) == N && out.size(0) == M && out.size(1) == K, "shapes");
   if (M == 0 || K == 0) return;
+  if (M >= 512 && use_tcgemm_bwd() && K % 32 == 0 && N % 8 == 0 && tc_ok(dy.data_ptr()) && tc_ok(w.data_ptr()) && tc_ok(out.data_ptr())) {
+    tcgemm_nn(dy.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, tcgemm_err(dy.get_device()).data_ptr<int>(), stream());
+    return;
+  }
   if (M >= 512) gemm::nn_sm2(dy.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, stream());
   else gemm::nn_sm1_sk(dy.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, stream());
 }
@@ -212,6 +230,10 @@ at::Tensor linear_dgrad(at::Tensor dy, at::Tensor w) {
   auto dx = at::empty({M, K}, dy.options());
   if (M == 0 || K == 0) return dx;
   if (N == 0) return dx.zero_();
+  if (M >= 512 && use_tcgemm_bwd() && K % 32 == 0 && N % 8 == 0 && tc_ok(dy.data_ptr()) && tc_ok(w.data_ptr())) {
+    tcgemm_nn(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), M, K, N, tcgemm_err(dy.get_device()).data_ptr<int>(), stream());
+    return dx;
+  }
   if (M >= 512) gemm::nn_sm2(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), M, K, N, stream());
   else gemm::nn_sm1_sk(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), M, K, N, stream());
   return dx;
@@ -235,6 +257,10 @@ void linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc) {
   int M = dy.size(0), N = dy.size(1), K = x.size(1);
   AX_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.size(0) == N && acc.size(1) == K, "acc fp32 [N,K]");
   if (M == 0) return;
+  if (use_tcgemm_bwd() && M >= 64 && N % 8 == 0 && K % 32 == 0 && tc_ok(dy.data_ptr()) && tc_ok(x.data_ptr()) && tc_ok(acc.data_ptr())) {
+    tcgemm_wgrad(dy.data_ptr(), x.data_ptr(), acc.data_ptr<float>(), N, K, M, true, tcgemm_err(dy.get_device()).data_ptr<int>(), stream());
+    return;
+  }
   if (N >= 512 && K >= 512) gemm::wgrad_f32_sm2(dy.data_ptr(), x.data_ptr(), acc.data_ptr(), N, K, M, true, stream());
   else gemm::wgrad_f32_sm1(dy.data_ptr(), x.data_ptr(), acc.data_ptr(), N, K, M, true, stream());
 }
@@ -397,6 +423,24 @@ at::Tensor tc_stream_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor
 }
 
 int64_t tc_stream_error() { return stream_workspace(c10::cuda::current_device()).err.item<int>(); }
+
+// Test / benchmark entries of the hand-written backward GEMMs.
+at::Tensor tc_linear_dgrad(at::Tensor dy, at::Tensor w) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(w, "w");
+  const int M = dy.size(0), N = dy.size(1), K = w.size(1);
+  AX_CHECK(w.size(0) == N, "N mismatch");
+  auto dx = at::empty({M, K}, dy.options());
+  tcgemm_nn(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), M, K, N, tcgemm_err(dy.get_device()).data_ptr<int>(), stream());
+  return dx;
+}
+void tc_linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc, bool accumulate) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(x, "x");
+  const int M = dy.size(0), N = dy.size(1), K = x.size(1);
+  AX_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.size(0) == N && acc.size(1) == K, "acc fp32 [N,K]");
+  tcgemm_wgrad(dy.data_ptr(), x.data_ptr(), acc.data_ptr<float>(), N, K, M, accumulate, tcgemm_err(dy.get_device()).data_ptr<int>(), stream());
+}
 
 int64_t tc_linear_error() { return tcgemm_err(c10::cuda::current_device()).item<int>(); }
 

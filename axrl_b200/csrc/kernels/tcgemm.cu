@@ -4,7 +4,12 @@
 // reduce-scatter of Megatron / TransformerEngine (axrl/worker/megatron_worker.py:833-870), which
 // runs a cuBLAS GEMM and then an NCCL reduce-scatter.
 //
-//   D[M, N] = A[M, K] @ B[N, K]^T (+ C[M, N])      A, B K-major (x @ W^T), bf16 in, fp32 accumulate
+//   D[M, N] = A[M, K] @ B[N, K]^T (+ C[M, N])      bf16 in, fp32 accumulate
+//
+// Either operand may be K-major (reduction dimension contiguous: the forward x @ W^T) or MN-major
+// (loaded as 64 x 64 boxes, the descriptor's leading offset stepping from one 64-wide block to
+// the next): the data-gradient GEMM dY @ W reads W MN-major, the weight-gradient GEMM dY^T @ X
+// reads both operands MN-major and accumulates into an fp32 gradient (mode F32ACC).
 //
 // One CTA per SM walks output tiles of 128 x 256 (grouped raster: GROUP_M row tiles share the
 // column tiles they visit, so weight tiles stay in L2):
@@ -17,6 +22,7 @@
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes 32 (w % 4)),
 //               optional residual, bf16 conversion, and the store:
 //                 mode LOCAL   D row-major in this GPU's memory;
+//                 mode F32ACC  fp32 D row-major, added to (or replacing) what it holds;
 //                 mode SLOTS   row r of the output belongs to TP rank r / rows_per_rank; the tile
 //                              is stored into that rank's receive slot for this rank
 //                              (peer[owner] + (rank * rows_per_rank + r % rows_per_rank) * N),
@@ -43,12 +49,14 @@ constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr long WAIT_LIMIT = 1L << 26;
 enum { B_FULL = 0, B_EMPTY = STAGES, B_ACC_FULL = 2 * STAGES, B_ACC_EMPTY = 2 * STAGES + 2, B_DRAIN = 2 * STAGES + 4, NBAR = 2 * STAGES + 5 };
-enum Mode { LOCAL = 0, SLOTS = 1 };
+enum Mode { LOCAL = 0, SLOTS = 1, F32ACC = 2 };
 
 struct Params {
   int M, N, K;
   int tiles_m, tiles_n;
   bf16* d;               // LOCAL: D (M x N)
+  float* d32;            // F32ACC: D (M x N) fp32
+  int accumulate;        // F32ACC: D += A @ B (else D = A @ B)
   const bf16* c;         // optional residual (M x N), LOCAL mode
   const int64_t* peers;  // SLOTS: receive buffer of every TP rank (device pointers as int64)
   int rank, rows_per_rank;
@@ -144,8 +152,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ uint64_t desc_k128(uint32_t saddr) {
   return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
-// kind::f16 instruction descriptor: bf16 x bf16 -> fp32, M = 128, N = BN, both operands K-major
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// MN-major, 128-byte swizzle descriptor: 64-element blocks of 8 KB (64 K rows x 128 bytes) one after
+// the other (leading offset), 8-row groups 1024 bytes apart
+__device__ __forceinline__ uint64_t desc_mn128(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)(8192 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// kind::f16 instruction descriptor: bf16 x bf16 -> fp32, M = 128, N = BN; bits 15 / 16 mark an
+// MN-major A / B
+template <bool A_MN, bool B_MN>
+constexpr uint32_t idesc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+constexpr uint32_t IDESC = idesc<false, false>();
 
 // Tile t of the grouped raster -> (row tile, column tile).
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
@@ -157,7 +176,7 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   tn = in / rows;
 }
 
-template <int MODE>
+template <int MODE, bool A_MN = false, bool B_MN = false>
 __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
   extern __shared__ char smem_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -165,7 +184,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ntiles = p.tiles_m * p.tiles_n, kslices = p.K / BK;
+  const int ntiles = p.tiles_m * p.tiles_n, kslices = (p.K + BK - 1) / BK;  // a ragged last slice reads zeros
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -205,8 +224,18 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
           if (it >= STAGES && !wait(&bar[B_EMPTY + s], ((it / STAGES) - 1) & 1, abort, p.err, 1)) break;
           expect_tx(&bar[B_FULL + s], STAGE_BYTES);
           char* st = sm + s * STAGE_BYTES;
-          tma2d(st, &ta, kb * BK, tm * BM, &bar[B_FULL + s]);
-          tma2d(st + A_BYTES, &tb, kb * BK, tn * BN, &bar[B_FULL + s]);
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int i = 0; i < BM / 64; ++i) tma2d(st + i * 8192, &ta, tm * BM + i * 64, kb * BK, &bar[B_FULL + s]);
+          } else {
+            tma2d(st, &ta, kb * BK, tm * BM, &bar[B_FULL + s]);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i) tma2d(st + A_BYTES + i * 8192, &tb, tn * BN + i * 64, kb * BK, &bar[B_FULL + s]);
+          } else {
+            tma2d(st + A_BYTES, &tb, kb * BK, tn * BN, &bar[B_FULL + s]);
+          }
         }
       }
       if (*abort) {  // every copy this CTA started lands before shared memory is released
@@ -232,7 +261,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
           fence_after();
           const uint32_t sa = s32(sm + s * STAGE_BYTES), sb = sa + A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) mma(tmem + a * BN, desc_k128(sa + kk * 32), desc_k128(sb + kk * 32), IDESC, (kb | kk) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t da = A_MN ? desc_mn128(sa + kk * 2048) : desc_k128(sa + kk * 32);
+            const uint64_t db = B_MN ? desc_mn128(sb + kk * 2048) : desc_k128(sb + kk * 32);
+            mma(tmem + a * BN, da, db, idesc<A_MN, B_MN>(), (kb | kk) ? 1u : 0u);
+          }
           commit(&bar[B_EMPTY + s]);
         }
         if (!ok) break;
@@ -268,6 +301,32 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
       const int row = tm * BM + q * 32 + lane;
+      if constexpr (MODE == F32ACC) {
+        float* d = row < p.M ? p.d32 + (long)row * p.N : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(lane_base + a * BN + c * 32, r);
+          const int col = tn * BN + c * 32;
+          if (d != nullptr && col < p.N) {
+            float4* d4 = reinterpret_cast<float4*>(d + col);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              float4 o = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
+                                     __uint_as_float(r[4 * v + 3]));
+              if (p.accumulate) {
+                const float4 old = d4[v];
+                o.x += old.x, o.y += old.y, o.z += old.z, o.w += old.w;
+              }
+              d4[v] = o;
+            }
+          }
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) arrive(&bar[B_ACC_EMPTY + a]);
+        continue;
+      }
       bf16* dst = nullptr;
       const bf16* res = nullptr;
       if (row < p.M) {
@@ -585,25 +644,42 @@ static CUtensorMap kmajor_map(const void* base, long rows, long cols, int box_ro
 
 static int smem_bytes() { return STAGES * STAGE_BYTES + NBAR * 8 + 32 + 1024; }
 
-template <int MODE>
+// K x MN matrix stored row-major (MN contiguous), box 64 x 64, 128-byte swizzle; out-of-range rows
+// and columns read as zero
+static CUtensorMap mnmajor_map(const void* base, long k_rows, long mn_cols) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)mn_cols, (cuuint64_t)k_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)mn_cols * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AX_REQUIRE(r == CUDA_SUCCESS, "tensor map encode failed (", (int)r, ")");
+  return m;
+}
+
+// A: K-major (M x K) or MN-major (K x M); B: K-major (N x K) or MN-major (K x N)
+template <int MODE, bool A_MN = false, bool B_MN = false>
 static void launch(const void* A, const void* B, Params p, cudaStream_t st) {
-  AX_REQUIRE(p.K % BK == 0, "tcgemm: K must be a multiple of 64, got ", p.K);
+  AX_REQUIRE((A_MN || B_MN) ? true : p.K % 8 == 0, "tcgemm: K must be a multiple of 8, got ", p.K);
   AX_REQUIRE(p.N % 32 == 0, "tcgemm: N must be a multiple of 32, got ", p.N);
+  AX_REQUIRE(!A_MN || p.M % 8 == 0, "tcgemm: M must be a multiple of 8 for an MN-major A");
   AX_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(B) % 16 == 0, "tcgemm: 16-byte aligned operands");
-  if (p.M == 0 || p.N == 0) return;
-  const CUtensorMap ta = kmajor_map(A, p.M, p.K, BM);
-  const CUtensorMap tb = kmajor_map(B, p.N, p.K, BN);
+  if (p.M == 0 || p.N == 0 || p.K == 0) return;
+  const CUtensorMap ta = A_MN ? mnmajor_map(A, p.K, p.M) : kmajor_map(A, p.M, p.K, BM);
+  const CUtensorMap tb = B_MN ? mnmajor_map(B, p.K, p.N) : kmajor_map(B, p.N, p.K, BN);
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (p.N + BN - 1) / BN;
-  static bool attr[2][64] = {{false}};
+  static bool attr[64] = {false};  // one flag set per instantiation
   int dev = 0;
   AX_CUDA_OK(cudaGetDevice(&dev));
-  if (!attr[MODE][dev]) {
-    AX_CUDA_OK(cudaFuncSetAttribute(gemm_k<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes()));
-    attr[MODE][dev] = true;
+  if (!attr[dev]) {
+    AX_CUDA_OK(cudaFuncSetAttribute(gemm_k<MODE, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes()));
+    attr[dev] = true;
   }
   const int grid = std::min(p.tiles_m * p.tiles_n, num_sms());
-  launch_pdl(gemm_k<MODE>, dim3(grid), dim3(THREADS), (size_t)smem_bytes(), st, ta, tb, p);
+  launch_pdl(gemm_k<MODE, A_MN, B_MN>, dim3(grid), dim3(THREADS), (size_t)smem_bytes(), st, ta, tb, p);
 }
 
 template <int NTOK>
@@ -646,6 +722,20 @@ void tcgemm_tn(const void* A, const void* B, const void* C, void* D, int M, int 
   tg::Params p{};
   p.M = M, p.N = N, p.K = K, p.d = static_cast<bf16*>(D), p.c = static_cast<const bf16*>(C), p.rows_per_rank = 1, p.err = err;
   tg::launch<tg::LOCAL>(A, B, p, st);
+}
+
+// Data gradient: dX[M, Ko] = dY[M, Nr] @ W[Nr, Ko] (W read MN-major), bf16.
+void tcgemm_nn(const void* dY, const void* W, void* dX, int M, int Ko, int Nr, int* err, cudaStream_t st) {
+  tg::Params p{};
+  p.M = M, p.N = Ko, p.K = Nr, p.d = static_cast<bf16*>(dX), p.rows_per_rank = 1, p.err = err;
+  tg::launch<tg::LOCAL, false, true>(dY, W, p, st);
+}
+
+// Weight gradient: G[Nw, Kw] (fp32) (+)= dY[T, Nw]^T @ X[T, Kw] (both read MN-major).
+void tcgemm_wgrad(const void* dY, const void* X, float* G, int Nw, int Kw, int T, bool accumulate, int* err, cudaStream_t st) {
+  tg::Params p{};
+  p.M = Nw, p.N = Kw, p.K = T, p.d32 = G, p.accumulate = accumulate ? 1 : 0, p.rows_per_rank = 1, p.err = err;
+  tg::launch<tg::F32ACC, true, true>(dY, X, p, st);
 }
 
 // Row-parallel GEMM whose output rows are reduce-scattered: row r of A @ B^T goes to rank

@@ -654,3 +654,27 @@ def test_tcgemm_stream_matches_fp32(M, N, K):
         assert e.tc_stream_error() == 0
         close(y, ref, 2e-2, 1e-2, msg=f"tcstream call {it}")
         close(y2, ref + r.float(), 3e-2, 1e-2, msg=f"tcstream + residual call {it}")
+
+
+@pytest.mark.skipif(os.environ.get("AXRL_TEST_TCGEMM_BWD") != "1", reason="hand-written backward GEMMs: opt-in until validated on a B200")
+@pytest.mark.parametrize("M,N,K", [(512, 256, 128), (1000, 4096, 1024), (4096, 6144, 4096), (777, 512, 96)])
+def test_tcgemm_dgrad_wgrad_match_fp32(M, N, K):
+    """Data gradient (W read MN-major) and fp32 weight-gradient accumulation (both operands MN-major,
+    ragged token count) on the hand-written tcgen05 GEMM, against fp32."""
+    e = _ext()
+    torch.manual_seed(M + K)
+    dy = torch.randn(M, N, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    dx = e.tc_linear_dgrad(dy, w)
+    acc = torch.randn(N, K, device=DEV)
+    acc0 = acc.clone()
+    e.tc_linear_wgrad_acc(dy, x, acc, True)
+    g = torch.empty(N, K, device=DEV)
+    e.tc_linear_wgrad_acc(dy, x, g, False)
+    torch.cuda.synchronize()
+    assert e.tc_linear_error() == 0
+    close(dx, dy.float() @ w.float(), 2e-2, 1e-2, msg="dgrad")
+    ref = dy.float().t() @ x.float()
+    close(g, ref, 1e-2, 1e-3, msg="wgrad")
+    close(acc, acc0 + ref, 1e-2, 1e-3, msg="wgrad accumulate")
