@@ -19,11 +19,14 @@ def main() -> None:
     ap.add_argument("--variants", default="auto,tma,skinny,swapab,cutlass,tcgemm,tcstream")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--sweep-decomp", action="store_true", help="skinny shapes under every stream-K decomposition")
+    ap.add_argument("--bwd", action="store_true", help="data- and weight-gradient GEMMs: CUTLASS vs the hand-written kernel")
     ap.add_argument("--ms", default="1,8,32,64,128,256,4096", help="comma-separated M values")
     ap.add_argument("--shapes", default="qkv,o,gate_up,down,lm_head")
     a = ap.parse_args()
     if a.sweep_decomp:
         return sweep_decomp(a.iters)
+    if a.bwd:
+        return bench_bwd(a)
     from axrl_b200.ops import _ext
 
     e = _ext.ext()
@@ -63,6 +66,31 @@ def main() -> None:
                     res[v] = {"us": round(ms * 1000, 1), "TBps": round(bytes_ / ms / 1e9, 2), "TFLOPs": round(2 * M * N * K / ms / 1e9, 1)}
                 except Exception as ex:  # noqa: BLE001
                     res[v] = str(ex)[:80]
+            print(json.dumps(res), flush=True)
+
+
+def bench_bwd(a) -> None:  # noqa: ANN001
+    """dX = dY @ W and dW += dY^T @ X for the Qwen3-8B projections at M tokens."""
+    from axrl_b200.ops import _ext
+
+    e = _ext.ext()
+    flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
+    shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288)}
+    for M in [int(m) for m in a.ms.split(",")]:
+        for name, (N, K) in shapes.items():
+            if name not in a.shapes.split(","):
+                continue
+            dy = torch.randn(M, N, device="cuda").bfloat16()
+            w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+            x = torch.randn(M, K, device="cuda").bfloat16()
+            acc = torch.zeros(N, K, device="cuda")
+            fl = 2.0 * M * N * K
+            res = {"M": M, "shape": name, "N": N, "K": K}
+            for label, fn in (("dgrad_cutlass", lambda: e.linear_dgrad(dy, w)), ("dgrad_tc", lambda: e.tc_linear_dgrad(dy, w)),
+                              ("wgrad_cutlass", lambda: e.linear_wgrad_acc(dy, x, acc)),
+                              ("wgrad_tc", lambda: e.tc_linear_wgrad_acc(dy, x, acc, True))):
+                ms = _time(fn, flush, a.iters)
+                res[label] = {"us": round(ms * 1000, 1), "TFLOPs": round(fl / ms / 1e9, 1)}
             print(json.dumps(res), flush=True)
 
 
