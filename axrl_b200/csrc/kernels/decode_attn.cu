@@ -219,17 +219,24 @@ __global__ void __launch_bounds__(128) decode_k(Params p) {
 }
 
 // Work list of the live (sequence, split) pairs: prefix[b] = sum over earlier sequences of
-// ceil(len / SPLIT).  Computed once per decode step and shared by every layer.
-__global__ void decode_plan_k(const int* __restrict__ seq_lens, int B, int* __restrict__ prefix) {
+// ceil(len / SPLIT).  With `chunks` (the array holds 2 (B + 1) entries) the second half is the
+// same count in 512-token chunks (the items of the TMA-fed kernel).  Computed once per decode
+// step and shared by every layer.
+__global__ void decode_plan_k(const int* __restrict__ seq_lens, int B, int* __restrict__ prefix, int chunks) {
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int acc = 0;
+  int acc = 0, acc4 = 0;
   for (int b = 0; b < B; ++b) {
     prefix[b] = acc;
     acc += (seq_lens[b] + SPLIT - 1) / SPLIT;
+    if (chunks) {
+      prefix[B + 1 + b] = acc4;
+      acc4 += (seq_lens[b] + 4 * SPLIT - 1) / (4 * SPLIT);
+    }
   }
   prefix[B] = acc;
+  if (chunks) prefix[2 * B + 1] = acc4;
 }
 
 // Persistent grid sized to the SMs: each CTA walks work items (kv head fastest), so the launch
@@ -268,6 +275,7 @@ __global__ void combine_k(const float* __restrict__ part_o, const float* __restr
   float4 o = make_float4(0, 0, 0, 0);
   for (int s = 0; s < ns; ++s) {
     float f = ml[2 * s] == -INFINITY ? 0.f : exp2f(ml[2 * s] - M);
+    if (f == 0.f) continue;  // an empty split (its output rows were never written) contributes nothing
     L += f * ml[2 * s + 1];
     float4 v = *reinterpret_cast<const float4*>(part_o + ((long)w * splits + s) * D + lane * 4);
     o.x += f * v.x; o.y += f * v.y; o.z += f * v.z; o.w += f * v.w;
@@ -365,7 +373,8 @@ void decode_advance(int64_t B, at::Tensor out_tok, at::Tensor out_lp, at::Tensor
 void decode_plan(at::Tensor seq_lens, at::Tensor prefix) {
   int B = seq_lens.numel();
   AX_CHECK(prefix.scalar_type() == at::kInt && prefix.numel() >= B + 1, "prefix: int32 (B + 1)");
-  launch_pdl(dec::decode_plan_k, dim3(1), dim3(32), 0, stream(), seq_lens.data_ptr<int>(), B, prefix.data_ptr<int>());
+  const int chunks = prefix.numel() >= 2 * (B + 1) ? 1 : 0;
+  launch_pdl(dec::decode_plan_k, dim3(1), dim3(32), 0, stream(), seq_lens.data_ptr<int>(), B, prefix.data_ptr<int>(), chunks);
   AX_LAUNCH_OK();
 }
 
@@ -405,7 +414,7 @@ void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bl
     AX_CUDA_OK(cudaFuncSetAttribute(decode_persist_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr[dev] = true;
   }
-  if (prefix.has_value() && decode_tma_enabled() && P == 64) {  // planned, TMA page pipeline
+  if (prefix.has_value() && decode_tma_enabled() && P == 64 && prefix->numel() >= 2 * (B + 1)) {  // planned, TMA page pipeline
     AX_CHECK(prefix->scalar_type() == at::kInt && prefix->numel() >= B + 1, "prefix: int32 (B + 1)");
     paged_decode_attn_tma_partials(q, kc, vc, block_table, seq_lens, part_o, part_ml, splits, scale, *prefix, max_len);
   } else if (prefix.has_value()) {  // planned: persistent grid over the live work items

@@ -1,22 +1,26 @@
 // Paged decode attention with a TMA page pipeline (one new query token per sequence, split-KV).
 //
-// Same work list, partial buffers and combine kernel as decode_attn.cu (128-token splits of each
-// sequence, (sequence, split, kv head) items numbered by decode_plan), but every CTA of the
-// persistent grid streams the K / V pages of ALL its items through one ring, so loads never stop at
-// an item boundary:
+// Same partial buffers and combine kernel as decode_attn.cu, with larger work items: an item is a
+// 512-token chunk of one sequence for one kv head (the second, chunk-granular work list that
+// decode_plan writes after the 128-token one).  Every CTA of the persistent grid (one per SM)
+// streams the K / V pages of ALL its items through one ring, so loads never stop at an item
+// boundary:
 //
-//   warp 4      producer (one thread): for each 64-token page of each item, four 2-D TMA loads
-//               (K and V, two 64-column boxes each, 128-byte swizzle; the cache viewed as
-//               (pages * Hkv * 64) rows of 128 values) into a 4-stage ring of 32 KB slots.
-//   warps 0-3   one item at a time: the GQA group's q heads (<= 16) are the M = 16 rows of
-//               mma.sync m16n8k16; warp w takes tokens 32 (w % 2) .. +31 of the item's page w / 2;
-//               online softmax per warp, then a cross-warp merge through shared memory and the
-//               item's (max, sum, unnormalised output) partial.
+//   warp 4      producer (one thread): per item the GQA group's q rows (one 2-D TMA load of
+//               16 rows), then per 64-token page four 2-D TMA loads (K and V, two 64-column
+//               boxes each, 128-byte swizzle; the cache viewed as (pages * Hkv * 64) rows of 128
+//               values) into a 4-stage ring of 32 KB slots.
+//   warps 0-3   one item at a time: the group's q heads (<= 16) are the M = 16 rows of mma.sync
+//               m16n8k16; warp w takes token rows 32 (w % 2) .. +31 of pages w / 2, w / 2 + 2, ...
+//               of the chunk with an online softmax across them, then the warps merge through
+//               shared memory into the partial of the chunk's first 128-token split; the chunk's
+//               other splits are marked empty (max -inf), which the combine skips.
 //
+// Per-item costs (q rows, merge, partial store) are paid once per 512 tokens instead of per 128.
 // The page size must be 64.  Reference counterpart: the rollout engine's decode attention backends
-// (SGLang FA3 / FlashInfer), reached via axrl/worker/sglang_worker.py:80-107.  Every wait is bounded:
-// on expiry the CTA records an error code, lets its copies land and exits; the consumers decide to
-// stop only after a barrier, so all four reach the same barriers.
+// (SGLang FA3 / FlashInfer), reached via axrl/worker/sglang_worker.py:80-107.  Every wait is
+// bounded: on expiry the CTA records an error code, lets its copies land and exits; the consumers
+// decide to stop only after a barrier, so all four reach the same barriers.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -25,7 +29,8 @@
 namespace ax {
 namespace dtm {
 
-constexpr int D = 128, PAGE = 64, SPLIT = 128, STAGES = 4, CW = 4, THREADS = 160;
+constexpr int D = 128, PAGE = 64, SPLIT = 128, CHUNK = 512, STAGES = 4, CW = 4, THREADS = 160;
+constexpr int QBOX = 16 * 64 * 2;  // 16 q rows x 64 columns bf16 = 2 KB
 constexpr int BOX = PAGE * 64 * 2;  // 64 rows x 64 columns bf16 = 8 KB
 constexpr int SLOT = 4 * BOX;       // K lo, K hi, V lo, V hi
 constexpr int RS = D + 2;           // merge buffer row: D outputs, max, sum
@@ -34,7 +39,7 @@ struct Params {
   const bf16* q;          // (B, Hq, D)
   const int* bt;          // (B, max_pages)
   const int* seq_lens;    // (B,)
-  const int* prefix;      // (B + 1,) items per sequence (128-token splits), cumulative
+  const int* prefix4;     // (B + 1,) items per sequence (512-token chunks), cumulative
   float* part_o;          // (B, Hq, splits, D)
   float* part_ml;         // (B, Hq, splits, 2)
   int B, Hq, Hkv, max_pages, splits, max_len;
@@ -47,7 +52,10 @@ __device__ __forceinline__ uint32_t sa(const void* p) { return (uint32_t)__cvta_
 __device__ __forceinline__ uint32_t pg_off(int row, int col) {
   return (uint32_t)((col >> 6) * BOX + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
 }
-__device__ __forceinline__ int q_swz(int row, int col) { return row * (D * 2) + (((col >> 3) ^ (row & 7)) << 4) + (col & 7) * 2; }
+// byte offset of (row, col) in the q tile: two 64-column 128-byte-swizzled boxes of 16 rows
+__device__ __forceinline__ uint32_t q_off(int row, int col) {
+  return (uint32_t)((col >> 6) * QBOX + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
+}
 __device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
 }
@@ -65,37 +73,41 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 struct Item {
-  int b, hk, sp, t0, len, npages;
+  int b, hk, sp, t0, len, npages, nsplits;
 };
 __device__ __forceinline__ Item item_of(const Params& p, int w) {
   Item it;
   it.hk = w % p.Hkv;
   const int j = w / p.Hkv;
-  int lo = 0, hi = p.B - 1;  // last b with prefix[b] <= j
+  int lo = 0, hi = p.B - 1;  // last b with prefix4[b] <= j
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (p.prefix[mid] <= j) lo = mid;
+    if (p.prefix4[mid] <= j) lo = mid;
     else hi = mid - 1;
   }
   it.b = lo;
-  it.sp = j - p.prefix[lo];
+  const int c = j - p.prefix4[lo];
   it.len = min(p.seq_lens[lo], p.max_len);
-  it.t0 = it.sp * SPLIT;
+  it.t0 = c * CHUNK;
+  it.sp = c * (CHUNK / SPLIT);
   const int rem = it.len - it.t0;
-  it.npages = rem <= 0 ? 0 : min(SPLIT / PAGE, (rem + PAGE - 1) / PAGE);
+  it.npages = rem <= 0 ? 0 : min(CHUNK / PAGE, (rem + PAGE - 1) / PAGE);
+  it.nsplits = rem <= 0 ? 0 : min(CHUNK / SPLIT, (rem + SPLIT - 1) / SPLIT);
   return it;
 }
 
 __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
-                                                        Params p) {
+                                                        const __grid_constant__ CUtensorMap tq, Params p) {
   extern __shared__ char smem_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   char* ring = sm;                                           // STAGES x SLOT
-  char* sQ = ring + STAGES * SLOT;                           // 2 x (16 x 128 bf16)
-  float* sRed = reinterpret_cast<float*>(sQ + 2 * 16 * D * 2);  // CW x 16 x RS
+  char* sQ = ring + STAGES * SLOT;                           // 2 x (16 x 128 bf16), by item parity
+  float* sRed = reinterpret_cast<float*>(sQ + 2 * 2 * QBOX);  // CW x 16 x RS
   uint64_t* full = reinterpret_cast<uint64_t*>(sRed + CW * 16 * RS);
   uint64_t* empty = full + STAGES;
-  volatile int* abort = reinterpret_cast<volatile int*>(empty + STAGES);
+  uint64_t* qfull = empty + STAGES;
+  uint64_t* qempty = qfull + 2;
+  volatile int* abort = reinterpret_cast<volatile int*>(qempty + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = p.Hq / p.Hkv;
 
@@ -103,6 +115,10 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 2);  // the two warps reading a page release it
+    }
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(&qfull[s], 1);
+      tc::mbar_init(&qempty[s], CW);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -112,11 +128,19 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
   if (warp == CW) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      pdl_wait();  // the work list and block table come from the preceding kernels
-      const int total = p.prefix[p.B] * p.Hkv;
-      int pc = 0;
+      pdl_wait();  // the work list, block table and q come from the preceding kernels
+      const int total = p.prefix4[p.B] * p.Hkv;
+      const int G = p.Hq / p.Hkv;
+      int pc = 0, n = 0;
       for (int w = blockIdx.x; w < total && !*abort; w += gridDim.x) {
         const Item it = item_of(p, w);
+        if (it.npages == 0) continue;
+        const int qs = n & 1;
+        if (n >= 2 && !tc::mbar_wait(&qempty[qs], ((n >> 1) - 1) & 1, abort, p.err, 33)) break;
+        tc::mbar_expect_tx(&qfull[qs], 2 * QBOX);
+        tc::tma_2d(sQ + qs * 2 * QBOX, &tq, 0, it.b * p.Hq + it.hk * G, &qfull[qs]);
+        tc::tma_2d(sQ + qs * 2 * QBOX + QBOX, &tq, 64, it.b * p.Hq + it.hk * G, &qfull[qs]);
+        ++n;
         for (int pg = 0; pg < it.npages; ++pg, ++pc) {
           const int s = pc % STAGES;
           if (pc >= STAGES && !tc::mbar_wait(&empty[s], ((pc / STAGES) - 1) & 1, abort, p.err, 31)) break;
@@ -133,6 +157,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
       if (*abort) {  // let every copy this CTA started land before shared memory is released
         int zero = 0;
         for (int i = max(0, pc - STAGES); i < pc; ++i) tc::mbar_wait(&full[i % STAGES], (i / STAGES) & 1, (volatile int*)&zero, p.err, 31);
+        for (int i = max(0, n - 2); i < n; ++i) tc::mbar_wait(&qfull[i & 1], (i >> 1) & 1, (volatile int*)&zero, p.err, 33);
       }
     }
     return;
@@ -140,31 +165,23 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
 
   // ------------------------------------------------------------------ consumers (warps 0-3)
   pdl_wait();
-  const int total = p.prefix[p.B] * p.Hkv;
+  const int total = p.prefix4[p.B] * p.Hkv;
   int pc = 0, n = 0;
   for (int w = blockIdx.x; w < total; w += gridDim.x) {
     const Item it = item_of(p, w);
     if (it.npages == 0) continue;  // same decision in every warp
-    char* q_s = sQ + (n & 1) * 16 * D * 2;
-    for (int i = tid; i < 16 * 16; i += 128) {  // Q rows of the group (rows >= G are zero)
-      const int r = i >> 4, c = (i & 15) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (r < G) v = *reinterpret_cast<const uint4*>(p.q + ((long)it.b * p.Hq + it.hk * G + r) * D + c);
-      *reinterpret_cast<uint4*>(q_s + q_swz(r, c)) = v;
-    }
-    consumers_sync();  // Q visible; the previous item's merge buffer is free
-    if (*abort) break;
-    const int pg = warp >> 1;
-    const bool has = pg < it.npages;
-    const int s = (pc + pg) % STAGES;
-    const int rb = (warp & 1) * 32;  // first row of this warp's 32 tokens within the page
-    const int ws = it.t0 + pg * PAGE + rb, we = min(ws + 32, it.len);
+    const int qs = n & 1;
+    const uint32_t qb = sa(sQ + qs * 2 * QBOX);
+    const int rb = (warp & 1) * 32;  // first row of this warp's 32 tokens within each page
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
     float acc[16][4];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    if (has) {
-      const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&full[s], ((pc + pg) / STAGES) & 1, abort, p.err, 32));
+    bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&qfull[qs], (n >> 1) & 1, abort, p.err, 34));
+    for (int pg = warp >> 1; ok && pg < it.npages; pg += 2) {
+      const int s = (pc + pg) % STAGES;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&full[s], ((pc + pg) / STAGES) & 1, abort, p.err, 32));
+      const int ws = it.t0 + pg * PAGE + rb, we = min(ws + 32, it.len);
       if (ok && ws < we) {
         const uint32_t kb = sa(ring + s * SLOT), vb = kb + 2 * BOX;
         float sc[4][4];
@@ -173,7 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           uint32_t a0, a1, a2, a3;
-          ldsm_x4(sa(q_s + q_swz(lane & 15, kk * 16 + (lane >> 4) * 8)), a0, a1, a2, a3);
+          ldsm_x4(qb + q_off(lane & 15, kk * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
 #pragma unroll
           for (int n2 = 0; n2 < 2; ++n2) {
             uint32_t b0, b1, b2, b3;
@@ -183,6 +200,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
             mma16816(sc[2 * n2 + 1], a0, a1, a2, a3, b2, b3);
           }
         }
+        // online softmax across this warp's pages (rows hh = 0, 1 of the fragment)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           float mx = -INFINITY;
@@ -197,19 +215,26 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
             }
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          m[hh] = mx;
+          const float m_new = fmaxf(m[hh], mx);  // finite: this slice has at least one valid token
+          const float alpha = m[hh] == -INFINITY ? 0.f : exp2f(m[hh] - m_new);
           float rsum = 0.f;
 #pragma unroll
           for (int nn = 0; nn < 4; ++nn)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const float v = exp2f(sc[nn][2 * hh + e] - mx);
+              const float v = exp2f(sc[nn][2 * hh + e] - m_new);
               sc[nn][2 * hh + e] = v;
               rsum += v;
             }
           rsum += __shfl_xor_sync(0xffffffffu, rsum, 1);
           rsum += __shfl_xor_sync(0xffffffffu, rsum, 2);
-          l[hh] = rsum;
+          l[hh] = l[hh] * alpha + rsum;
+          m[hh] = m_new;
+#pragma unroll
+          for (int d = 0; d < 16; ++d) {
+            acc[d][2 * hh] *= alpha;
+            acc[d][2 * hh + 1] *= alpha;
+          }
         }
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
@@ -228,23 +253,29 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&empty[s]);  // this warp is done with the page
     }
-    // cross-warp merge
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&qempty[qs]);
+    // cross-warp merge (rows < G only)
+    const int G = p.Hq / p.Hkv;
     float* mine = sRed + warp * 16 * RS;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int r = (lane >> 2) + hh * 8;
+      if (r < G) {
 #pragma unroll
-      for (int d = 0; d < 16; ++d) {
-        const int c = d * 8 + (lane & 3) * 2;
-        mine[r * RS + c] = acc[d][2 * hh];
-        mine[r * RS + c + 1] = acc[d][2 * hh + 1];
-      }
-      if ((lane & 3) == 0) {
-        mine[r * RS + D] = m[hh];
-        mine[r * RS + D + 1] = l[hh];
+        for (int d = 0; d < 16; ++d) {
+          const int c = d * 8 + (lane & 3) * 2;
+          mine[r * RS + c] = acc[d][2 * hh];
+          mine[r * RS + c + 1] = acc[d][2 * hh + 1];
+        }
+        if ((lane & 3) == 0) {
+          mine[r * RS + D] = m[hh];
+          mine[r * RS + D + 1] = l[hh];
+        }
       }
     }
     consumers_sync();
+    if (*abort) break;
     {
       const int r = tid >> 3, c0 = (tid & 7) * 16;
       if (r < G) {
@@ -260,16 +291,21 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] += f * sRed[(w2 * 16 + r) * RS + c0 + j];
         }
-        const long base = (((long)it.b * p.Hq + it.hk * G + r) * p.splits + it.sp);
+        const long row = (long)it.b * p.Hq + it.hk * G + r;
+        const long base = row * p.splits + it.sp;
         float* po = p.part_o + base * D + c0;
 #pragma unroll
         for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(po + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
         if ((tid & 7) == 0) {
           p.part_ml[base * 2] = M;
           p.part_ml[base * 2 + 1] = L;
+        } else if ((tid & 7) < it.nsplits) {  // the chunk's other splits hold nothing
+          p.part_ml[(base + (tid & 7)) * 2] = -INFINITY;
+          p.part_ml[(base + (tid & 7)) * 2 + 1] = 0.f;
         }
       }
     }
+    consumers_sync();  // the merge buffer is read before the next item overwrites it
     pc += it.npages;
     ++n;
   }
@@ -289,6 +325,18 @@ static EncodeFn encoder() {
   return fn;
 }
 // the cache (pages, Hkv, 64, 128) as (pages * Hkv * 64) rows of 128 bf16; box 64 x 64, 128-byte swizzle
+static CUtensorMap rows_map(const void* base, long rows, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AX_CHECK(r == CUDA_SUCCESS, "tensor map encode failed (", (int)r, ")");
+  return m;
+}
 static CUtensorMap cache_map(const void* base, long rows) {
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
@@ -315,19 +363,21 @@ void paged_decode_attn_tma_partials(at::Tensor q, at::Tensor kc, at::Tensor vc, 
   using namespace dtm;
   const int B = q.size(0), Hq = q.size(1), Hkv = kc.size(1);
   AX_CHECK(kc.size(2) == PAGE && kc.size(3) == D && kc.is_contiguous() && vc.is_contiguous(), "TMA decode: page size 64, head dim 128");
+  AX_CHECK(q.is_contiguous() && prefix.numel() >= 2 * (B + 1), "contiguous q, chunk work list");
   const long rows = kc.size(0) * (long)Hkv * PAGE;
   const CUtensorMap tk = cache_map(kc.data_ptr(), rows), tv = cache_map(vc.data_ptr(), rows);
-  Params p{(const bf16*)q.data_ptr(), block_table.data_ptr<int>(), seq_lens.data_ptr<int>(), prefix.data_ptr<int>(), part_o.data_ptr<float>(),
+  const CUtensorMap tq = rows_map(q.data_ptr(), (long)B * Hq, 16);
+  Params p{(const bf16*)q.data_ptr(), block_table.data_ptr<int>(), seq_lens.data_ptr<int>(), prefix.data_ptr<int>() + B + 1, part_o.data_ptr<float>(),
            part_ml.data_ptr<float>(), B, Hq, Hkv, (int)block_table.size(1), (int)splits, max_len, (float)(scale * 1.4426950408889634),
            err_flag(q.get_device()).data_ptr<int>()};
-  const int smem = STAGES * SLOT + 2 * 16 * D * 2 + CW * 16 * RS * 4 + 2 * STAGES * 8 + 16 + 1024;
+  const int smem = STAGES * SLOT + 2 * 2 * QBOX + CW * 16 * RS * 4 + (2 * STAGES + 4) * 8 + 16 + 1024;
   static bool attr[64] = {false};
   const int dev = q.get_device();
   if (!attr[dev]) {
     AX_CUDA_OK(cudaFuncSetAttribute(decode_tma_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr[dev] = true;
   }
-  launch_pdl(decode_tma_k, dim3(num_sms()), dim3(THREADS), smem, stream(), tk, tv, p);
+  launch_pdl(decode_tma_k, dim3(num_sms()), dim3(THREADS), smem, stream(), tk, tv, tq, p);
   AX_LAUNCH_OK();
 }
 

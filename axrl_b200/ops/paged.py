@@ -62,7 +62,8 @@ class DecodeWorkspace:
         self.splits = max(1, math.ceil(max_context / SPLIT_TOKENS))
         self.part_o = torch.empty(max_batch * hq * self.splits * 128, dtype=torch.float32, device=device)
         self.part_ml = torch.empty(max_batch * hq * self.splits * 2, dtype=torch.float32, device=device)
-        self.prefix = torch.zeros(max_batch + 1, dtype=torch.int32, device=device)
+        # work lists of the planned decode kernels: 128-token splits, then 512-token chunks
+        self.prefix = torch.zeros(2 * (max_batch + 1), dtype=torch.int32, device=device)
 
     def plan(self, seq_lens: torch.Tensor) -> None:
         """Work list of live (sequence, split) pairs for ``seq_lens``; every layer of a step reuses it."""
