@@ -89,6 +89,8 @@ at::Tensor tc_stream_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor
 int64_t tc_stream_error();
 int64_t decode_tma_error();
 at::Tensor tc_linear_dgrad(at::Tensor dy, at::Tensor w);
+void adamw_p2p_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor ptrs, int64_t s0, int64_t decay_end, double lr,
+                    double b1, double b2, double eps, double wd, int64_t step, at::Tensor sqnorm, double clip, double extra_scale);
 void tc_linear_wgrad_acc(at::Tensor dy, at::Tensor x, at::Tensor acc, bool accumulate);
 }  // namespace ax
 
@@ -168,5 +170,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_stream_error", &ax::tc_stream_error);
   m.def("decode_tma_error", &ax::decode_tma_error);
   m.def("tc_linear_dgrad", &ax::tc_linear_dgrad);
+  m.def("adamw_p2p_step", &ax::adamw_p2p_step);
   m.def("tc_linear_wgrad_acc", &ax::tc_linear_wgrad_acc);
 }

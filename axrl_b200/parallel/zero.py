@@ -22,9 +22,11 @@ complete are reduced on a side stream right away:
   accumulates its squared norm;
 * ``backend="nccl"``: ``reduce_scatter_tensor`` of the bucket.
 
-``step`` then all-reduces the squared norm (one float), runs the fused clipped AdamW kernel on
-each shard and stores the new bf16 values into every rank's parameter buffer (P2P stores) or
-all-gathers them (NCCL).
+``step`` then all-reduces the squared norm (one float) and, per bucket, runs ONE kernel that
+applies the clipped AdamW update to this rank's shard and stores the new bf16 values into every
+rank's parameter buffer over NVLink (``adamw_p2p_k``: the partitioned update fused with the
+parameter all-gather); with the NCCL backend the update writes the local bf16 shard and the
+buckets are all-gathered.
 """
 
 from __future__ import annotations
@@ -250,6 +252,8 @@ class BucketedZeroAdamW:
             so, n = self.shard_off[bi], b["shard"]
             g = self.grad[b["s0"]:b["s0"] + n]
             dec = max(0, min(n, b["start"] + b["decay_n"] - b["s0"]))
+            if p2p and self.state.step_range_p2p(so, n, g, self.param_ptrs, b["s0"], dec, lr, o, self.step_count, sqnorm, grad_scale):
+                continue  # one kernel: AdamW on this shard and the bf16 store into every rank's parameters
             out = None if p2p else self.bf16[b["s0"]:b["s0"] + n]
             m = self.state.step_range(so, n, g, out, dec, lr, o, self.step_count, sqnorm, grad_scale, need_master=p2p)
             if p2p:  # the updated shard goes straight into every rank's parameters over NVLink

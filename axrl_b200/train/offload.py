@@ -91,6 +91,20 @@ class AdamState:
             self._staging = torch.empty(n, dtype=torch.float32, device=self.device)
         return self._staging[:n]
 
+    def step_range_p2p(self, lo: int, n: int, grad: torch.Tensor, peer_ptrs: torch.Tensor, s0: int, decay_n: int, lr: float, opt,  # noqa: ANN001
+                       step: int, sqnorm: torch.Tensor, grad_scale: float) -> bool:
+        """AdamW over [lo, lo + n) fused with the store of the new bf16 values into every rank's
+        parameter buffer at element ``s0`` (``peer_ptrs``: int64 device pointers).  False (nothing
+        done) when part of the range lives on the host or the sizes do not allow the fused kernel."""
+        if self.device.type != "cuda" or lo + n > self.split or n % 8 or s0 % 8:
+            return False
+        from axrl_b200.ops import _ext
+
+        _ext.ext().adamw_p2p_step(self.dev_master[lo:lo + n], grad[:n], self.dev_m[lo:lo + n], self.dev_v[lo:lo + n], peer_ptrs, s0,
+                                  max(0, min(decay_n, n)), lr, opt.adam_beta1, opt.adam_beta2, opt.adam_eps, opt.weight_decay, step,
+                                  sqnorm, float(opt.clip_grad), float(grad_scale))
+        return True
+
     def step_range(self, lo: int, n: int, grad: torch.Tensor, out_bf16: torch.Tensor | None, decay_n: int, lr: float, opt,  # noqa: ANN001
                    step: int, sqnorm: torch.Tensor, grad_scale: float, need_master: bool = False) -> torch.Tensor | None:
         """AdamW over elements [lo, lo + n) of the state with gradient ``grad`` (n device floats).

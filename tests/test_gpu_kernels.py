@@ -675,3 +675,29 @@ def test_tcgemm_dgrad_wgrad_match_fp32(M, N, K):
     ref = dy.float().t() @ x.float()
     close(g, ref, 1e-2, 1e-3, msg="wgrad")
     close(acc, acc0 + ref, 1e-2, 1e-3, msg="wgrad accumulate")
+
+
+def test_adamw_fused_with_parameter_store_matches_unfused():
+    """Partitioned AdamW fused with the bf16 parameter store (the distributed optimizer's update +
+    all-gather kernel), here with this GPU's own buffer as the only destination: same masters,
+    moments and bf16 parameters as the AdamW kernel with its bf16 write-back."""
+    e = _ext()
+    n, s0 = 40_000, 1024
+    g = torch.randn(n, device=DEV)
+    outs = []
+    for fused in (False, True):
+        torch.manual_seed(3)
+        p = torch.randn(n, device=DEV)
+        m, v = torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+        params = torch.zeros(s0 + n, dtype=torch.bfloat16, device=DEV)
+        sq = (g.pow(2).sum() * 4.0).reshape(1)
+        for step in (1, 2):
+            if fused:
+                ptrs = torch.tensor([params.data_ptr()], dtype=torch.int64, device=DEV)
+                e.adamw_p2p_step(p, g, m, v, ptrs, s0, 30_000, 1e-3, 0.9, 0.999, 1e-8, 0.01, step, sq, 1.0, 0.5)
+            else:
+                e.adamw_step(p, g, m, v, params[s0:], 30_000, 1e-3, 0.9, 0.999, 1e-8, 0.01, step, sq, 1.0, 0.5)
+        torch.cuda.synchronize()
+        outs.append((p, m, v, params))
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
