@@ -699,5 +699,6 @@ def test_adamw_fused_with_parameter_store_matches_unfused():
                 e.adamw_step(p, g, m, v, params[s0:], 30_000, 1e-3, 0.9, 0.999, 1e-8, 0.01, step, sq, 1.0, 0.5)
         torch.cuda.synchronize()
         outs.append((p, m, v, params))
-    for a, b in zip(outs[0], outs[1]):
-        assert torch.equal(a, b)
+    for a, b in zip(outs[0][:3], outs[1][:3]):
+        torch.testing.assert_close(b, a, rtol=1e-6, atol=1e-7)
+    torch.testing.assert_close(outs[1][3].float(), outs[0][3].float(), rtol=8e-3, atol=1e-6)
