@@ -653,7 +653,6 @@ def test_tcgemm_stream_matches_fp32(M, N, K):
         close(y2, ref + r.float(), 3e-2, 1e-2, msg=f"tcstream + residual call {it}")
 
 
-@pytest.mark.skipif(os.environ.get("AXRL_TEST_TCGEMM_BWD") != "1", reason="hand-written backward GEMMs: opt-in until validated on a B200")
 @pytest.mark.parametrize("M,N,K", [(512, 256, 128), (1000, 4096, 1024), (4096, 6144, 4096), (777, 512, 96)])
 def test_tcgemm_dgrad_wgrad_match_fp32(M, N, K):
     """Data gradient (W read MN-major) and fp32 weight-gradient accumulation (both operands MN-major,
