@@ -520,6 +520,49 @@ __global__ void f32_to_bf16_k(const float* __restrict__ a, bf16* __restrict__ b,
   }
 }
 
+// Merge of split-key partials (o_s, lse2_s), s < P, of the same queries: lse2 = log2(sum 2^lse2_s)
+// over the sources that saw keys (lse2_s = +inf marks a row with no keys in source s), o = sum
+// o_s * 2^(lse2_s - lse2).  One warp per (token, head) row, four bf16 per lane.
+constexpr int MERGE_MAX = 16;
+struct MergeParams {
+  const bf16* o[MERGE_MAX];
+  const float* lse[MERGE_MAX];
+  bf16* out;
+  float* lse_out;
+  int P, T, Hq;
+};
+
+__global__ void attn_merge_k(MergeParams p) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (w >= p.T * p.Hq) return;
+  const int t = w / p.Hq, h = w % p.Hq;
+  const long li = (long)h * p.T + t, oi = ((long)t * p.Hq + h) * D + lane * 4;
+  float m = -INFINITY;
+  for (int s = 0; s < p.P; ++s) {
+    const float l = p.lse[s][li];
+    if (l != INFINITY) m = fmaxf(m, l);
+  }
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.f;
+  if (m != -INFINITY) {
+    for (int s = 0; s < p.P; ++s) {
+      const float l = p.lse[s][li];
+      if (l == INFINITY) continue;
+      const float wgt = exp2f(l - m);
+      den += wgt;
+      const uint2 raw = *reinterpret_cast<const uint2*>(p.o[s] + oi);
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.y));
+      acc[0] += wgt * a.x, acc[1] += wgt * a.y, acc[2] += wgt * b.x, acc[3] += wgt * b.y;
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  uint2 o;
+  o.x = pack_bf16(acc[0] * inv, acc[1] * inv);
+  o.y = pack_bf16(acc[2] * inv, acc[3] * inv);
+  *reinterpret_cast<uint2*>(p.out + oi) = o;
+  if (lane == 0) p.lse_out[li] = den > 0.f ? m + log2f(den) : INFINITY;
+}
+
 }  // namespace attn
 
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
@@ -751,6 +794,7 @@ static int& deterministic_flag() {
   return on;
 }
 void set_attn_deterministic(bool on) { deterministic_flag() = on ? 1 : 0; }
+bool attn_deterministic() { return deterministic_flag() != 0; }
 
 void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor lse2, at::Tensor dsum, at::Tensor dq_acc,
                        at::Tensor dk, at::Tensor dv, at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale);
@@ -769,6 +813,88 @@ static int& tc_backward_flag() {
 static bool use_tc_backward() { return tc_backward_flag() != 0; }
 void set_attn_bwd_tc(bool on) { tc_backward_flag() = on ? 1 : 0; }
 
+// dK/dV of one key set and dQ added into `dq_acc` (fp32), given the softmax statistics of the whole
+// row: `lse2` and `dsum` = rowsum(dO * O) of the final output.  Exact for a split over key sources,
+// since every source's probabilities are 2^(S * scale * log2e - lse2) with the final lse2.
+static void attn_bwd_core(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                          const at::Tensor& lse2, const at::Tensor& dsum, at::Tensor& dq_acc, at::Tensor& dk, at::Tensor& dv,
+                          const at::Tensor& kseg, const at::Tensor& qr, const at::Tensor& tiles, double scale,
+                          const c10::optional<at::Tensor>& tiles_tc) {
+  using namespace attn;
+  const int T = q.size(0), Hq = q.size(1), Hkv = k.size(1);
+  if (use_tc_backward() && tiles_tc.has_value()) {
+    attn_bwd_tc_tiles(dout, q, k, v, lse2, dsum, dq_acc, dk, dv, kseg, qr, *tiles_tc, scale);
+    return;
+  }
+  const int nt = tiles.size(0);
+  if (nt == 0) return;
+  AX_CHECK(kseg.is_cuda() && qr.is_cuda() && tiles.is_cuda(), "attention tables must be on the device");
+  BwdParams p{(const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), (const bf16*)dout.data_ptr(),
+              lse2.data_ptr<float>(), dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), (bf16*)dk.data_ptr(),
+              (bf16*)dv.data_ptr(), kseg.data_ptr<int>(), qr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
+              (float)(scale * 1.4426950408889634), (float)scale, 0};
+  const int smem = (2 * BWD_BN + 2 * BWD_BM) * D * 2 + BWD_BN * (BWD_BM + 8) * 2 + 2 * BWD_BM * 4;
+  static bool attr = false;
+  if (!attr) {
+    AX_CUDA_OK(cudaFuncSetAttribute(attn_bwd_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  attn_bwd_k<<<dim3(nt, Hkv), 128, smem, stream()>>>(p);
+  AX_LAUNCH_OK();
+}
+
+// rowsum(dO * O) per (head, token): (Hq, T) fp32.
+at::Tensor attn_bwd_dsum(at::Tensor o, at::Tensor dout) {
+  using namespace attn;
+  AX_CHECK(o.is_contiguous() && dout.is_contiguous() && o.sizes() == dout.sizes() && o.size(2) == D, "attn_bwd_dsum: o/dout shape");
+  const int T = o.size(0), Hq = o.size(1);
+  auto dsum = at::empty({Hq, T}, o.options().dtype(at::kFloat));
+  const long w = (long)T * Hq;
+  if (w == 0) return dsum;
+  attn_bwd_pre_k<<<(w * 32 + 255) / 256, 256, 0, stream()>>>((const bf16*)o.data_ptr(), (const bf16*)dout.data_ptr(),
+                                                            dsum.data_ptr<float>(), T, Hq);
+  AX_LAUNCH_OK();
+  return dsum;
+}
+
+// One key source of a split attention: returns (dK, dV) of that source's keys and adds its share
+// of dQ into `dq_acc` ((T, Hq, 128) fp32).
+std::vector<at::Tensor> attn_bwd_partial(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor lse2, at::Tensor dsum,
+                                         at::Tensor dq_acc, at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale,
+                                         c10::optional<at::Tensor> tiles_tc) {
+  AX_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous() && dq_acc.sizes() == q.sizes(), "attn_bwd_partial: dq_acc");
+  AX_CHECK(lse2.size(0) == q.size(1) && lse2.size(1) == q.size(0) && dsum.sizes() == lse2.sizes(), "attn_bwd_partial: lse2/dsum");
+  auto dk = at::zeros_like(k), dv = at::zeros_like(v);
+  if (q.size(0) > 0 && k.size(0) > 0) attn_bwd_core(dout, q, k, v, lse2, dsum, dq_acc, dk, dv, kseg, qr, tiles, scale, tiles_tc);
+  return {dk, dv};
+}
+
+// Merge the per-source partial outputs of a split attention (see attn_merge_k).
+std::vector<at::Tensor> attn_merge(std::vector<at::Tensor> os, std::vector<at::Tensor> lses) {
+  using namespace attn;
+  const int P = (int)os.size();
+  AX_CHECK(P >= 1 && P <= MERGE_MAX && (int)lses.size() == P, "attn_merge: 1..16 partials");
+  const int T = os[0].size(0), Hq = os[0].size(1);
+  MergeParams mp{};
+  for (int s = 0; s < P; ++s) {
+    AX_CHECK(os[s].is_contiguous() && os[s].sizes() == os[0].sizes() && os[s].size(2) == D && os[s].scalar_type() == at::kBFloat16,
+             "attn_merge: partial outputs (T, Hq, 128) bf16");
+    AX_CHECK(lses[s].is_contiguous() && lses[s].size(0) == Hq && lses[s].size(1) == T, "attn_merge: lse2 (Hq, T)");
+    mp.o[s] = (const bf16*)os[s].data_ptr();
+    mp.lse[s] = lses[s].data_ptr<float>();
+  }
+  auto out = at::empty_like(os[0]);
+  auto lse = at::empty({Hq, T}, os[0].options().dtype(at::kFloat));
+  mp.out = (bf16*)out.data_ptr();
+  mp.lse_out = lse.data_ptr<float>();
+  mp.P = P, mp.T = T, mp.Hq = Hq;
+  const long w = (long)T * Hq;
+  if (w == 0) return {out, lse};
+  attn_merge_k<<<(w * 32 + 255) / 256, 256, 0, stream()>>>(mp);
+  AX_LAUNCH_OK();
+  return {out, lse};
+}
+
 std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse2,
                                  at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc,
                                  c10::optional<at::Tensor> qseg, c10::optional<at::Tensor> kr, c10::optional<at::Tensor> fwd_tiles) {
@@ -783,27 +909,21 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
   attn_bwd_pre_k<<<(w * 32 + 255) / 256, 256, 0, stream()>>>((const bf16*)o.data_ptr(), (const bf16*)dout.data_ptr(),
                                                             dsum.data_ptr<float>(), T, Hq);
   AX_LAUNCH_OK();
-  int nt = tiles.size(0);
   const bool det = deterministic_flag() != 0 && fwd_tiles.has_value() && qseg.has_value() && kr.has_value();
-  if (use_tc_backward() && tiles_tc.has_value() && !det) {
-    attn_bwd_tc_tiles(dout, q, k, v, lse2, dsum, dq_acc, dk, dv, kseg, qr, *tiles_tc, scale);
-    nt = 0;
-  }
-  if (nt > 0) {
+  if (!det) attn_bwd_core(dout, q, k, v, lse2, dsum, dq_acc, dk, dv, kseg, qr, tiles, scale, tiles_tc);
+  else if (tiles.size(0) > 0) {  // dK/dV by the mma.sync kernel without its dQ atomics
     AX_CHECK(kseg.is_cuda() && qr.is_cuda() && tiles.is_cuda(), "attention tables must be on the device");
-    auto& kseg_d = kseg;
-    auto& qr_d = qr;
     BwdParams p{(const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), (const bf16*)dout.data_ptr(),
                 lse2.data_ptr<float>(), dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), (bf16*)dk.data_ptr(),
-                (bf16*)dv.data_ptr(), kseg_d.data_ptr<int>(), qr_d.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
-                (float)(scale * 1.4426950408889634), (float)scale, det ? 1 : 0};
-    int smem = (2 * BWD_BN + 2 * BWD_BM) * D * 2 + BWD_BN * (BWD_BM + 8) * 2 + 2 * BWD_BM * 4;
+                (bf16*)dv.data_ptr(), kseg.data_ptr<int>(), qr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
+                (float)(scale * 1.4426950408889634), (float)scale, 1};
+    const int smem = (2 * BWD_BN + 2 * BWD_BM) * D * 2 + BWD_BN * (BWD_BM + 8) * 2 + 2 * BWD_BM * 4;
     static bool attr = false;
     if (!attr) {
       AX_CUDA_OK(cudaFuncSetAttribute(attn_bwd_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       attr = true;
     }
-    attn_bwd_k<<<dim3(nt, Hkv), 128, smem, stream()>>>(p);
+    attn_bwd_k<<<dim3(tiles.size(0), Hkv), 128, smem, stream()>>>(p);
     AX_LAUNCH_OK();
   }
   if (det) {  // dQ owned by one CTA per q tile: no atomics, fixed summation order

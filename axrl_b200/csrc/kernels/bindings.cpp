@@ -31,6 +31,12 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
                                  at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale, c10::optional<at::Tensor> tiles_tc,
                                  c10::optional<at::Tensor> qseg, c10::optional<at::Tensor> kr, c10::optional<at::Tensor> fwd_tiles);
 void set_attn_deterministic(bool on);
+bool attn_deterministic();
+at::Tensor attn_bwd_dsum(at::Tensor o, at::Tensor dout);
+std::vector<at::Tensor> attn_bwd_partial(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor lse2, at::Tensor dsum,
+                                         at::Tensor dq_acc, at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale,
+                                         c10::optional<at::Tensor> tiles_tc);
+std::vector<at::Tensor> attn_merge(std::vector<at::Tensor> os, std::vector<at::Tensor> lses);
 at::Tensor gdn_step(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, at::Tensor pool, at::Tensor slots);
 int64_t attn_bwd_tc_error();
 void set_attn_bwd_tc(bool on);
@@ -144,6 +150,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("kseg"), py::arg("qr"), py::arg("tiles"), py::arg("scale"), py::arg("tiles_tc") = py::none(), py::arg("qseg") = py::none(),
         py::arg("kr") = py::none(), py::arg("fwd_tiles") = py::none());
   m.def("set_attn_deterministic", &ax::set_attn_deterministic);
+  m.def("attn_deterministic", &ax::attn_deterministic);
+  m.def("attn_bwd_dsum", &ax::attn_bwd_dsum);
+  m.def("attn_bwd_partial", &ax::attn_bwd_partial, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("lse2"),
+        py::arg("dsum"), py::arg("dq_acc"), py::arg("kseg"), py::arg("qr"), py::arg("tiles"), py::arg("scale"),
+        py::arg("tiles_tc") = py::none());
+  m.def("attn_merge", &ax::attn_merge);
   m.def("gdn_step", &ax::gdn_step);
   m.def("attn_bwd_tc_error", &ax::attn_bwd_tc_error);
   m.def("set_attn_bwd_tc", &ax::set_attn_bwd_tc);

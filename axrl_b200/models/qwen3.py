@@ -224,11 +224,16 @@ class Attention(nn.Module):
     def forward(self, x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, spec: AttnSpec, tp: TPContext = _NO_TP) -> torch.Tensor:
         qkv = tpl.column_parallel_linear(x, self.qkv_proj, tp)
         q, k, v = ops.qk_norm_rope(qkv, self.q_norm, self.k_norm, pos, inv_freq, self.nq, self.nkv, self.eps)
+        stash = self.stash if (self.training and torch.is_grad_enabled()) else None
         if self.cp is not None and self.cp.enabled:  # keys/values of every context-parallel rank
-            from axrl_b200.parallel.context_parallel import gather_kv
+            from axrl_b200.parallel import context_parallel as cpx
 
-            k, v = gather_kv(k, self.cp), gather_kv(v, self.cp)
-        o = ops.attention(q, k, v, spec, stash=self.stash if (self.training and torch.is_grad_enabled()) else None)
+            if cpx.ring_attention_supported(spec, self.cp):
+                o = cpx.ring_attention(q, k, v, spec, self.cp, stash=stash)
+            else:
+                o = ops.attention(q, cpx.gather_kv(k, self.cp), cpx.gather_kv(v, self.cp), spec, stash=stash)
+        else:
+            o = ops.attention(q, k, v, spec, stash=stash)
         o = o.reshape(o.shape[0], -1)
         if self.attn_gate is not None:
             o = o * torch.sigmoid(tpl.column_parallel_linear(x, self.attn_gate, tp).float()).to(o.dtype)

@@ -47,6 +47,9 @@ class AttnSpec:
     # host-side token layout for sequence mixers that need whole sequences (Gated DeltaNet under
     # context parallelism: see ``parallel.context_parallel.CPSeqLayout``); None = flat packing
     seq_layout: Any = None
+    # context parallelism: one spec per key source rank, queries local and keys in that rank's
+    # own stream coordinates (ring attention attends to each source's chunk as it arrives)
+    cp_sources: list | None = None
 
     def to(self, device, non_blocking: bool = True) -> "AttnSpec":  # noqa: ANN001
         """Move every table to ``device`` in ONE host->device copy (pinned staging)."""
@@ -59,7 +62,9 @@ class AttnSpec:
             n = p.numel()
             out.append(flat[off:off + n].view(p.shape))
             off += n
-        return AttnSpec(*out[:4], self.total_q, self.total_k, self.max_q_len, self.max_k_len, out[4], out[5], out[6], self.seq_layout)
+        srcs = [c.to(device, non_blocking) for c in self.cp_sources] if self.cp_sources is not None else None
+        return AttnSpec(*out[:4], self.total_q, self.total_k, self.max_q_len, self.max_k_len, out[4], out[5], out[6], self.seq_layout,
+                        srcs)
 
     def triples(self) -> list[tuple[int, int, int, int, int]]:
         out = []

@@ -222,6 +222,85 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: AttnSpec,
     return _Attn.apply(q.contiguous(), k.contiguous(), v.contiguous(), spec, scale, stash)
 
 
+# ------------------------------------------------------- split-key attention (ring / context parallel)
+# The keys of one query set split over sources s (context-parallel ranks): each source gives a
+# partial (o_s, lse2_s) — lse2 in the log2 domain, (Hq, T), +inf for a row with no keys there —
+# and the merge weights o_s by 2^(lse2_s - lse2).  The backward of every source uses the final
+# (o, lse2): its probabilities 2^(S*scale*log2e - lse2) are the rows of the full softmax.
+
+_LOG2E = 1.4426950408889634
+
+
+def _part_probs(q, k, spec, scale, lse2):  # noqa: ANN001, ANN202
+    rep = q.shape[1] // k.shape[1]
+    kk = k.float().repeat_interleave(rep, 1)
+    s2 = torch.einsum("thd,shd->hts", q.float(), kk) * (scale * _LOG2E)
+    mask = dense_mask(spec).to(q.device)[None]
+    if lse2 is None:
+        m = s2.masked_fill(~mask, float("-inf")).amax(-1, keepdim=True)
+        l = torch.exp2(s2 - m.clamp_min(-1e30)).masked_fill(~mask, 0.0).sum(-1)
+        lse2 = torch.where(l > 0, m.squeeze(-1) + torch.log2(l.clamp_min(1e-30)), torch.full_like(l, float("inf")))
+    p = torch.exp2(s2 - lse2[..., None]).masked_fill(~mask, 0.0)
+    return p, lse2
+
+
+def attn_partial(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: AttnSpec, scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(o, lse2) of the queries against one key source (no autograd)."""
+    if q.is_cuda:
+        if not spec.qseg.is_cuda:
+            spec = spec.to(q.device)
+        o, lse2 = _ext.ext().attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), spec.qseg, spec.kr, spec.fwd_tiles, scale)
+        return o, lse2
+    p, lse2 = _part_probs(q, k, spec, scale, None)
+    rep = q.shape[1] // k.shape[1]
+    o = torch.einsum("hts,shd->thd", p, v.float().repeat_interleave(rep, 1))
+    return o.to(q.dtype), lse2.contiguous()
+
+
+def attn_merge(parts: list[tuple[torch.Tensor, torch.Tensor]]) -> tuple[torch.Tensor, torch.Tensor]:
+    """Merge per-source partials into (o, lse2)."""
+    if parts[0][0].is_cuda:
+        o, lse2 = _ext.ext().attn_merge([p[0] for p in parts], [p[1] for p in parts])
+        return o, lse2
+    lse = torch.stack([p[1] for p in parts])
+    fin = torch.where(torch.isinf(lse) & (lse > 0), torch.full_like(lse, float("-inf")), lse)
+    m = fin.amax(0)
+    w = torch.exp2(fin - m.clamp_min(-1e30)[None])
+    den = w.sum(0)
+    o = sum(p[0].float() * (w[i] / den.clamp_min(1e-30)).t()[..., None] for i, p in enumerate(parts))
+    lse2 = torch.where(den > 0, m + torch.log2(den.clamp_min(1e-30)), torch.full_like(den, float("inf")))
+    return o.to(parts[0][0].dtype), lse2
+
+
+def attn_bwd_dsum(o: torch.Tensor, do: torch.Tensor) -> torch.Tensor:
+    """rowsum(dO * O) as (Hq, T) fp32."""
+    if o.is_cuda:
+        return _ext.ext().attn_bwd_dsum(o.contiguous(), do.contiguous())
+    return (o.float() * do.float()).sum(-1).t().contiguous()
+
+
+def attn_bwd_partial(do: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lse2: torch.Tensor, dsum: torch.Tensor,
+                     dq_acc: torch.Tensor, spec: AttnSpec, scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(dK, dV) of one key source; its share of dQ is added into ``dq_acc`` (fp32)."""
+    if q.is_cuda:
+        if not spec.qseg.is_cuda:
+            spec = spec.to(q.device)
+        dk, dv = _ext.ext().attn_bwd_partial(do.contiguous(), q, k.contiguous(), v.contiguous(), lse2, dsum, dq_acc, spec.kseg, spec.qr,
+                                             spec.bwd_tiles, scale, spec.bwd_tiles_tc)
+        return dk, dv
+    Hkv = k.shape[1]
+    rep = q.shape[1] // Hkv
+    p, _ = _part_probs(q, k, spec, scale, lse2)
+    dof = do.float()
+    dp = torch.einsum("thd,shd->hts", dof, v.float().repeat_interleave(rep, 1))
+    ds = p * (dp - dsum[..., None])
+    dq_acc += torch.einsum("hts,shd->thd", ds, k.float().repeat_interleave(rep, 1)) * scale
+    dk = torch.einsum("hts,thd->shd", ds, q.float()) * scale
+    dv = torch.einsum("hts,thd->shd", p, dof)
+    S = k.shape[0]
+    return (dk.view(S, Hkv, rep, -1).sum(2).to(k.dtype), dv.view(S, Hkv, rep, -1).sum(2).to(v.dtype))
+
+
 # ----------------------------------------------------------------------------- linear
 
 

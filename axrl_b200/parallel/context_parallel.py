@@ -16,6 +16,15 @@ triples (flat causal, or a prefix tree's full-to-ancestors + causal-self ranges)
 boundaries; a causal self range becomes ``full`` for earlier chunks and ``causal`` on the
 diagonal chunk.  The gather's backward reduce-scatters the key/value gradients to their owners.
 
+Ring attention (the default when the spec carries per-source tables).  Instead of waiting for the
+whole gather, each rank passes its K/V chunk around the ring (send to rank+1, receive from rank-1,
+NCCL point-to-point over NVLink on NCCL's stream) and attends to the chunk it holds while the next
+one is in flight; the P partial (o, lse) pairs are merged with log-sum-exp weights.  The backward
+walks the ring the other way round: at step j a rank computes the dK/dV contribution for the chunk
+of rank ``rank-j-1`` (against the final o and lse, which is exact), adds the partial sum received
+from rank-1, and forwards it, so the key/value gradients arrive at their owners as a ring
+reduce-scatter overlapped with the attention backward; dQ accumulates in fp32 across sources.
+
 Loss.  A rank trains on its own tokens (its loss mask is restricted to them); gradients are then
 summed over the CP group, and per-token log-probs are assembled by summing the ranks' disjoint
 parts.  Token-level loss aggregation is exact under this split; sequence-level ratios (GSPO) would
@@ -24,6 +33,7 @@ need cross-rank sums and are rejected.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Any
 
@@ -71,6 +81,136 @@ class _GatherKV(torch.autograd.Function):
 def gather_kv(x: torch.Tensor, cp: CPContext) -> torch.Tensor:
     """(L, H, D) local keys or values -> (cp*L, H, D) in rank-major order."""
     return _GatherKV.apply(x.contiguous(), cp.comm) if cp.enabled else x
+
+
+class _Ring:
+    """Neighbour exchange on the CP ring: every rank sends to ``rank+1`` and receives from
+    ``rank-1`` in one batched point-to-point call (NCCL runs it on its own stream; ``wait`` makes
+    the current stream wait for it)."""
+
+    def __init__(self, cp: CPContext) -> None:
+        P, r = cp.size, cp.rank
+        self.group = cp.group
+        self.nxt = dist.get_global_rank(cp.group, (r + 1) % P)
+        self.prv = dist.get_global_rank(cp.group, (r - 1) % P)
+
+    def shift(self, tensors: tuple[torch.Tensor, ...]) -> "_Pending":
+        recv = tuple(torch.empty_like(t) for t in tensors)
+        ops = [dist.P2POp(dist.isend, t, self.nxt, self.group, tag=i) for i, t in enumerate(tensors)]
+        ops += [dist.P2POp(dist.irecv, t, self.prv, self.group, tag=i) for i, t in enumerate(recv)]
+        return _Pending(dist.batch_isend_irecv(ops), tensors, recv)
+
+
+class _Pending:
+    def __init__(self, works: list, sent: tuple, recv: tuple) -> None:
+        self.works, self.sent, self.recv = works, sent, recv
+
+    def wait(self) -> tuple[torch.Tensor, ...]:
+        for w in self.works:
+            w.wait()
+        self.sent = None  # the send buffers may be reused from here on
+        return self.recv
+
+
+def _stash_pop(stash, spec, q):  # noqa: ANN001, ANN202
+    from axrl_b200.ops.core import AttnStash
+
+    if stash is None or AttnStash.pushing:
+        return None
+    key = (id(spec), tuple(q.shape))
+    lst = stash.items.get(key)
+    if not lst:
+        return None
+    hit = lst.pop(0)
+    if not lst:
+        del stash.items[key]
+    return hit
+
+
+class _RingAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, spec, cp, scale, stash):  # noqa: ANN001, ANN205
+        from axrl_b200.ops import core as ops
+
+        P, r = cp.size, cp.rank
+        srcs = spec.cp_sources
+        hit = _stash_pop(stash, spec, q)
+        ring = _Ring(cp)
+        chunks: list = [None] * P
+        chunks[r] = (k, v)
+        cur, parts = (k, v), []
+        for step in range(P):
+            s = (r - step) % P
+            pend = ring.shift(cur) if step < P - 1 else None
+            if hit is None:
+                parts.append(ops.attn_partial(q, cur[0], cur[1], srcs[s], scale))
+            if pend is not None:
+                cur = pend.wait()
+                chunks[(r - step - 1) % P] = cur
+        if hit is None:
+            o, lse2 = ops.attn_merge(parts)
+            from axrl_b200.ops.core import AttnStash
+
+            if stash is not None and AttnStash.pushing:
+                stash.items.setdefault((id(spec), tuple(q.shape)), []).append((o, lse2))
+        else:
+            o, lse2 = hit
+        ctx.save_for_backward(q, o, lse2, *[c[0] for c in chunks], *[c[1] for c in chunks])
+        ctx.spec, ctx.cp, ctx.scale = spec, cp, scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):  # noqa: ANN001, ANN205
+        from axrl_b200.ops import core as ops
+
+        cp, scale, srcs = ctx.cp, ctx.scale, ctx.spec.cp_sources
+        P, r = cp.size, cp.rank
+        q, o, lse2, *kv = ctx.saved_tensors
+        ks, vs = kv[:P], kv[P:]
+        do = do.contiguous()
+        dsum = ops.attn_bwd_dsum(o, do)
+        dq_acc = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+        ring = _Ring(cp)
+        pend = None
+        for j in range(P):
+            c = (r - j - 1) % P  # j = P-1: this rank's own chunk, the last to be completed
+            dk, dv = ops.attn_bwd_partial(do, q, ks[c], vs[c], lse2, dsum, dq_acc, srcs[c], scale)
+            if pend is not None:
+                rk, rv = pend.wait()
+                dk, dv = dk + rk, dv + rv
+            pend = ring.shift((dk, dv)) if j < P - 1 else None
+        return dq_acc.to(q.dtype), dk, dv, None, None, None, None
+
+
+def ring_attention_supported(spec, cp: CPContext) -> bool:  # noqa: ANN001
+    """Ring attention needs the per-source tables and non-deterministic dQ (the deterministic
+    backward owns dQ per query tile in one kernel over all keys: the gathered path keeps it);
+    ``AXRL_CP_ATTN=gather`` selects the gathered path."""
+    if not cp.enabled or getattr(spec, "cp_sources", None) is None or len(spec.cp_sources) != cp.size or cp.size > 16:
+        return False
+    if os.environ.get("AXRL_CP_ATTN", "ring") == "gather":
+        return False
+    if spec.qseg.is_cuda or torch.cuda.is_available():
+        from axrl_b200.ops import _ext
+
+        try:
+            return not _ext.ext().attn_deterministic()
+        except Exception:  # noqa: BLE001 - no extension on this host: the CPU path has no such mode
+            return True
+    return True
+
+
+def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec, cp: CPContext, scale: float | None = None,  # noqa: ANN001
+                   stash=None) -> torch.Tensor:  # noqa: ANN001
+    """Attention of the local queries over the keys of every CP rank, overlapped with the K/V ring
+    exchange.  q: (L, Hq, D) local; k, v: (L, Hkv, D) local; ``spec.cp_sources[s]`` addresses the
+    keys of rank s in that rank's stream coordinates."""
+    import math
+
+    scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
+    if q.is_cuda and not spec.qseg.is_cuda:
+        spec = spec.to(q.device)
+    return _RingAttn.apply(q.contiguous(), k.contiguous(), v.contiguous(), spec, cp, scale, stash)
 
 
 @dataclass
@@ -230,6 +370,11 @@ def pack_rows_cp(batch, rows: list[int], cp: CPContext):  # noqa: ANN001, ANN201
                         continue
                     triples.append((lq + qa - kq * c, lq + qb - kq * c, glob_k(kk) + ka - kk * c, glob_k(kk) + kb - kk * c, typ))
     spec = spec_from_triples(triples, L, L * P)
+    by_src: list[list] = [[] for _ in range(P)]
+    for q0, q1, k0, k1, t in triples:  # a triple's keys never cross a chunk, so one source each
+        s = k0 // L
+        by_src[s].append((q0, q1, k0 - s * L, k1 - s * L, t))
+    spec.cp_sources = [spec_from_triples(t, L, L) for t in by_src]
     spec.seq_layout = CPSeqLayout(torch.cat(perm) if perm else torch.zeros(0, dtype=torch.int64), segs)
     return PackedMicroBatch(rows=list(rows), row_len=row_len, row_off=[0] * len(rows), ids=torch.cat(ids), pos=torch.cat(pos).int(),
                             labels=torch.cat(lab), loss_mask=torch.cat(lm), token_row=torch.cat(trow), spec=spec,

@@ -361,6 +361,54 @@ def case_rollout_tp() -> None:
         print(f"rank {rank}: rollout_tp graph={use_graph} ok (mean |dlp| {diff.mean().item():.4f})", flush=True)
 
 
+def case_cp() -> None:
+    """CP=world over NCCL: ring attention (K/V chunks passed around the ring while the per-source
+    attention kernels run; dK/dV reduce-scattered around the ring in the backward) and the
+    all-gathered path, each against CP=1 on this GPU with the same weights and batch."""
+    from axrl_b200.configs import GrpoTrainerConfig, MegatronWorkerConfig
+    from axrl_b200.data.sample import Sample, SampleBatch
+    from axrl_b200.models.qwen3 import Qwen3Config
+    from axrl_b200.train.engine import ParallelCtx, TrainEngine
+    from axrl_b200.trainer.grpo_trainer import GrpoTrainer
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = Qwen3Config(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=8,
+                      num_key_value_heads=4, head_dim=128)
+    g = torch.Generator().manual_seed(1)
+    samples = []
+    for i in range(4):
+        p = torch.randint(1, 1024, (300 + 100 * i,), generator=g).tolist()
+        r = torch.randint(1, 1024, (200 + 50 * i,), generator=g).tolist()
+        samples.append(Sample.from_tokens(p, r, advantage=float(i % 3) - 1.0, rollout_logprobs=(-torch.rand(len(r), generator=g)).tolist(),
+                                          trajectory_id=i))
+    batch = SampleBatch.from_samples(samples)
+
+    def wc():
+        c = MegatronWorkerConfig(max_tokens_per_micro_batch=4096, seed=3)
+        c.lr_scheduler.lr_warmup_steps = 0
+        c.lr_scheduler.max_lr = 1e-4
+        return c
+
+    trainer = GrpoTrainer(GrpoTrainerConfig(loss_type="grpo", loss_agg_type="token-mean"))
+    ref = TrainEngine(wc(), cfg, "cuda")
+    lp_ref = ref.compute_logprobs(batch)
+    batch["old_logprobs"] = lp_ref
+    batch["ref_logprobs"] = lp_ref
+    gn_ref = ref.train_step(batch, trainer)["grad_norm"]
+    mask = batch["loss_mask"].bool()
+    for mode in ("ring", "gather"):
+        os.environ["AXRL_CP_ATTN"] = mode
+        eng = TrainEngine(wc(), cfg, "cuda", par=ParallelCtx(cp_group=dist.group.WORLD, cp_size=world))
+        lp = eng.compute_logprobs(batch)
+        d = (lp - lp_ref)[mask].abs().max().item()
+        gn = eng.train_step(batch, trainer)["grad_norm"]
+        torch.cuda.synchronize()
+        rel = abs(gn - gn_ref) / max(gn_ref, 1e-6)
+        assert d < 5e-2 and rel < 2e-2, f"cp {mode}: lp diff {d}, grad norm {gn} vs {gn_ref}"
+        print(f"rank {rank}: cp {mode} ok (lp diff {d:.2e}, grad norm rel {rel:.2e})", flush=True)
+    os.environ.pop("AXRL_CP_ATTN", None)
+
+
 if __name__ == "__main__":
     from datetime import timedelta
 

@@ -52,6 +52,11 @@ def test_expert_parallel_two_gpus():
     assert out.count("ep torch ok") == 2 and out.count("ep p2p ok") == 2, out[-2000:]
 
 
+def test_context_parallel_ring_two_gpus():
+    out = _run("cp")
+    assert out.count("cp ring ok") == 2 and out.count("cp gather ok") == 2, out[-2000:]
+
+
 def test_bucketed_zero_two_gpus():
     out = _run("zero")
     assert out.count("zero nccl ok") == 2 and out.count("zero p2p ok") == 2, out[-2000:]
