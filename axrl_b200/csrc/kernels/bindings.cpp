@@ -43,6 +43,7 @@ void set_attn_bwd_tc(bool on);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
                        double, c10::optional<at::Tensor>);
 void decode_plan(at::Tensor seq_lens, at::Tensor prefix);
+void set_decode_attn_tma(bool on);
 void kv_store(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
 void sqnorm_accumulate(at::Tensor x, at::Tensor acc);
 void adamw_step(at::Tensor, at::Tensor, at::Tensor, at::Tensor, c10::optional<at::Tensor>, int64_t, double, double, double, double,
@@ -159,6 +160,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_step", &ax::gdn_step);
   m.def("attn_bwd_tc_error", &ax::attn_bwd_tc_error);
   m.def("set_attn_bwd_tc", &ax::set_attn_bwd_tc);
+  m.def("set_decode_attn_tma", &ax::set_decode_attn_tma);
   m.def("paged_decode_attn", &ax::paged_decode_attn);
   m.def("kv_store", &ax::kv_store);
   m.def("sqnorm_accumulate", &ax::sqnorm_accumulate);

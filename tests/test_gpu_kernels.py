@@ -208,8 +208,13 @@ def test_sampler():
     close(freq, torch.softmax(small[0], -1), 0.02, msg="sampling frequencies")
 
 
-def test_paged_decode_attention():
+@pytest.mark.parametrize("planned_kernel", ["tma", "persist"])
+def test_paged_decode_attention(planned_kernel):
+    """Fixed-grid split-KV kernel, then the planned work-list kernels (the TMA page pipeline, the
+    default, and the cp.async persistent kernel) after in-place length changes."""
     from axrl_b200.ops.paged import DecodeWorkspace, decode_attention_ref, paged_decode_attention
+
+    _ext().set_decode_attn_tma(planned_kernel == "tma")
 
     B, Hq, Hkv, D, P, pages = 5, 32, 8, 128, 64, 64
     kc = torch.randn(pages, Hkv, P, D, device=DEV).bfloat16()
@@ -237,6 +242,7 @@ def test_paged_decode_attention():
         o = paged_decode_attention(q, kc, vc, bt, lens, ws, planned=True)
         close(o, decode_attention_ref(q, kc, vc, bt, lens, 1 / math.sqrt(D)), 2e-2)
     assert ws.prefix[:B + 1].tolist() == [0, 2, 3, 23, 24, 29]
+    _ext().set_decode_attn_tma(True)
 
 
 def test_adamw_and_sqnorm():
