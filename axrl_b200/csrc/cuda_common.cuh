@@ -9,9 +9,12 @@
 #include <stdint.h>
 
 #include <cstdlib>
+#include <mutex>
+#include <set>
 #include <sstream>
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <utility>
 
 namespace ax {
@@ -75,6 +78,20 @@ inline int num_sms() {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   }
   return n;
+}
+
+// Raise a kernel's dynamic shared memory limit on the current device.  The attribute is per
+// device, so the (kernel, device, bytes) triples already set are remembered, not one flag per process.
+inline void smem_attr(const void* kern, int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int>> done;
+  int dev = 0;
+  AX_CUDA_OK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> g(mu);
+  const auto key = std::make_tuple(kern, dev, bytes);
+  if (done.count(key)) return;
+  AX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert(key);
 }
 
 // 16-byte vector of 8 bf16.

@@ -612,11 +612,7 @@ std::vector<at::Tensor> attn_fwd_mma(at::Tensor q, at::Tensor k, at::Tensor v, a
               lse2.data_ptr<float>(), qseg_d.data_ptr<int>(), kr_d.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
               (float)(scale * 1.4426950408889634)};
   int smem = (FWD_BM + 4 * FWD_BN) * D * 2;
-  static bool attr = false;
-  if (!attr) {
-    AX_CUDA_OK(cudaFuncSetAttribute(attn_fwd_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  smem_attr(reinterpret_cast<const void*>(attn_fwd_k), smem);
   attn_fwd_k<<<dim3(nt, Hq), 256, smem, stream()>>>(p);
   AX_LAUNCH_OK();
   return {o, lse2};
@@ -834,11 +830,7 @@ static void attn_bwd_core(const at::Tensor& dout, const at::Tensor& q, const at:
               (bf16*)dv.data_ptr(), kseg.data_ptr<int>(), qr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
               (float)(scale * 1.4426950408889634), (float)scale, 0};
   const int smem = (2 * BWD_BN + 2 * BWD_BM) * D * 2 + BWD_BN * (BWD_BM + 8) * 2 + 2 * BWD_BM * 4;
-  static bool attr = false;
-  if (!attr) {
-    AX_CUDA_OK(cudaFuncSetAttribute(attn_bwd_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  smem_attr(reinterpret_cast<const void*>(attn_bwd_k), smem);
   attn_bwd_k<<<dim3(nt, Hkv), 128, smem, stream()>>>(p);
   AX_LAUNCH_OK();
 }
@@ -918,11 +910,7 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
                 (bf16*)dv.data_ptr(), kseg.data_ptr<int>(), qr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
                 (float)(scale * 1.4426950408889634), (float)scale, 1};
     const int smem = (2 * BWD_BN + 2 * BWD_BM) * D * 2 + BWD_BN * (BWD_BM + 8) * 2 + 2 * BWD_BM * 4;
-    static bool attr = false;
-    if (!attr) {
-      AX_CUDA_OK(cudaFuncSetAttribute(attn_bwd_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr = true;
-    }
+    smem_attr(reinterpret_cast<const void*>(attn_bwd_k), smem);
     attn_bwd_k<<<dim3(tiles.size(0), Hkv), 128, smem, stream()>>>(p);
     AX_LAUNCH_OK();
   }
@@ -934,11 +922,7 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
     dq.zero_();
     if (ntq > 0) {
       const int smem = (2 * FWD_BM + 4 * FWD_BN) * D * 2;
-      static bool attr_dq = false;
-      if (!attr_dq) {
-        AX_CUDA_OK(cudaFuncSetAttribute(attn_bwd_dq_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr_dq = true;
-      }
+      smem_attr(reinterpret_cast<const void*>(attn_bwd_dq_k), smem);
       attn_bwd_dq_k<<<dim3(ntq, Hq), 256, smem, stream()>>>(dp);
       AX_LAUNCH_OK();
     }

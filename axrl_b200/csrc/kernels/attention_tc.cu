@@ -678,25 +678,15 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
            (float)(scale * 1.4426950408889634), err_flag(q.get_device()).data_ptr<int>()};
   if (variant == 2 || variant == 3) {
     const int smem8 = 6 * TILE + 3 * 2 * BM * 4 + NBAR8 * 8 + 16 + 1024;
-    static bool attr8[2][16] = {{false}};
-    const int dev = q.get_device();
-    const int tp = variant == 3;
-    auto* kern = tp ? attn_fwd_tc8_k<true> : attn_fwd_tc8_k<false>;
-    if (!attr8[tp][dev]) {
-      AX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem8));
-      attr8[tp][dev] = true;
-    }
+    auto* kern = variant == 3 ? attn_fwd_tc8_k<true> : attn_fwd_tc8_k<false>;
+    smem_attr(reinterpret_cast<const void*>(kern), smem8);
     kern<<<dim3(nt, Hq), THREADS8, smem8, stream()>>>(tq, tk, tv, p);
     AX_LAUNCH_OK();
     return {o, lse2};
   }
   const bool dbl = variant == 1;
   const int smem = (dbl ? 7 : 6) * TILE + NBAR * 8 + 16 + 1024;
-  static bool attr[2] = {false, false};
-  if (!attr[dbl]) {
-    AX_CUDA_OK(cudaFuncSetAttribute(dbl ? attn_fwd_tc_k<true> : attn_fwd_tc_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr[dbl] = true;
-  }
+  smem_attr(dbl ? reinterpret_cast<const void*>(attn_fwd_tc_k<true>) : reinterpret_cast<const void*>(attn_fwd_tc_k<false>), smem);
   if (dbl) attn_fwd_tc_k<true><<<dim3(nt, Hq), THREADS, smem, stream()>>>(tq, tk, tv, p);
   else attn_fwd_tc_k<false><<<dim3(nt, Hq), THREADS, smem, stream()>>>(tq, tk, tv, p);
   AX_LAUNCH_OK();

@@ -372,11 +372,7 @@ void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v
            kseg.data_ptr<int>(), qr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T, (float)(scale * 1.4426950408889634), (float)scale,
            err_flag(q.get_device()).data_ptr<int>()};
   const int smem = 6 * TILE + 4 * BQ * 4 + NBAR * 8 + 16 + 1024;
-  static bool attr = false;
-  if (!attr) {
-    AX_CUDA_OK(cudaFuncSetAttribute(attn_bwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_k), smem);
   attn_bwd_tc_k<<<dim3(nt, Hkv), THREADS, smem, stream()>>>(tq, tk, tv, tdo, p);
   AX_LAUNCH_OK();
 }

@@ -286,11 +286,7 @@ static void launch(const at::Tensor& x, const at::Tensor& w, const bf16* r, at::
   CUtensorMap tw = make_map(w.data_ptr(), N, K, NT);
   CUtensorMap tx = make_map(x.data_ptr(), M, K, MT);
   const int smem = STAGES * (NT * KT * 2 + MT * KT * 2) + 2 * STAGES * 8 + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
-    AX_CHECK(cudaFuncSetAttribute(skinny_tma_k<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess, "smem attribute");
-    attr_set = true;
-  }
+  smem_attr(reinterpret_cast<const void*>(skinny_tma_k<MT>), smem);
   launch_pdl(skinny_tma_k<MT>, dim3(used), dim3(THREADS), smem, stream(), tw, tx, p);
   AX_LAUNCH_OK();
 }

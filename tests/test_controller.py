@@ -2,6 +2,7 @@
 normalisation, packing, training, partial-rollout pause/resume; plus queue and router logic."""
 
 import asyncio
+from unittest import mock
 
 import torch
 
@@ -184,7 +185,10 @@ def test_ppo_with_value_worker_tiny_cpu():
         seen["adv"], seen["ret"], seen["mask"] = b["advantage"].clone(), b["returns"].clone(), b["loss_mask"].bool().clone()
 
     ctl.prepare_ppo_training_samples = spy
-    asyncio.run(ctl.start())
+    # a reward that every batch sees both values of (token presence on a random tiny model is
+    # usually 0 for a whole batch, which leaves the critic with nothing to fit)
+    with mock.patch("axrl_b200.recipe.synthetic_recipe.token_presence_reward", lambda ids, tok: float(bool(ids) and ids[0] % 2 == 0)):
+        asyncio.run(ctl.start())
     assert ctl.global_step == 2 and ctl.value_step == 3  # one value-only warmup update, then both train
     m = seen["mask"]
     assert torch.isfinite(seen["adv"]).all() and (seen["adv"][~m] == 0).all()
