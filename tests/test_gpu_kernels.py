@@ -266,7 +266,8 @@ def test_adamw_and_sqnorm():
     upd = (mr / 0.1) / ((vr / 0.001).sqrt() + 1e-8)
     upd[:5000] += 0.01 * p0[:5000]
     close(p, p0 - 1e-3 * upd, 1e-6, 1e-5)
-    close(pb, p, 1e-2)
+    # the bf16 copy is the fp32 master rounded to bf16 (within one bf16 ulp, 2^-7 relative)
+    torch.testing.assert_close(pb.float(), p.bfloat16().float(), atol=0.0, rtol=8e-3)
 
 
 def test_embedding():
