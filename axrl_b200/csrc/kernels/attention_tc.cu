@@ -619,6 +619,256 @@ __global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_const
   }
 }
 
+// ---------------------------------------------------------------------------------- paired heads
+// Two q heads of one GQA group per CTA (heads 2hp and 2hp + 1 read the same K/V rows, so every K/V
+// tile feeds twice the tensor-core work):
+//   warps 0-3   softmax of head A, one query row per thread over all 128 key columns (no exchange
+//               between warps);
+//   warps 4-7   softmax of head B;
+//   warp 8      TMA producer: both Q tiles, then K and V tiles through one 4-slot ring (K(j) in
+//               slot 2j % 4, V(j) in slot (2j + 1) % 4);
+//   warp 9      MMA issuer and TMEM owner.
+// TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512).  P_X (bf16 pairs) overwrites the
+// first 64 columns of S_X and is the A operand of PV_X straight from tensor memory.  Per key tile j
+// the issue order is PV_A(j-1), QK_A(j), PV_B(j-1), QK_B(j): while one head's softmax runs, the
+// tensor cores work for the other.  S_X(j) may overwrite P_X(j-1) because the tensor pipe executes
+// one thread's MMAs in issue order, and the commit that signals S_X(j) also covers PV_X(j-1), so
+// the softmax may rescale O_X without another wait.  A K slot is released once both QK products of
+// its tile are done, a V slot once both PV products are.
+constexpr int THREADS_P = 320;
+constexpr int NSLOT = 4;
+constexpr int BP_Q = 0, BP_FULL = 1, BP_EMPTY = BP_FULL + NSLOT, BP_S = BP_EMPTY + NSLOT, BP_P = BP_S + 2, BP_O = BP_P + 2,
+              BP_DRAIN = BP_O + 1, NBARP = BP_DRAIN + 1;
+
+__global__ void __launch_bounds__(THREADS_P, 1) attn_fwd_tcp_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                                                              const __grid_constant__ CUtensorMap tv, Params p) {
+  extern __shared__ char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  char* sQ = sm;              // head A, then head B
+  char* ring = sm + 2 * TILE;  // NSLOT tiles
+  uint64_t* bar = reinterpret_cast<uint64_t*>(ring + NSLOT * TILE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBARP);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seg = p.tiles[blockIdx.x * 2], qs = p.tiles[blockIdx.x * 2 + 1];
+  const int hA = blockIdx.y * 2, hk = hA / (p.Hq / p.Hkv);
+  const int q0 = p.qseg[seg * 4], q1 = p.qseg[seg * 4 + 1], r_first = p.qseg[seg * 4 + 2], r_last = p.qseg[seg * 4 + 3];
+  const int qe = min(qs + BM, q1);
+
+  if (tid == 0) {
+    mbar_init(&bar[BP_Q], 1);
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&bar[BP_FULL + s], 1);
+      mbar_init(&bar[BP_EMPTY + s], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bar[BP_S + x], 1);
+      mbar_init(&bar[BP_P + x], 4);
+    }
+    mbar_init(&bar[BP_O], 1);
+    mbar_init(&bar[BP_DRAIN], 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tq)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tv)) : "memory");
+  }
+  if (warp == 9) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  KeyTiles kt{p.kr, r_first, r_last, q0, qe, 0, 0, 0, 0};
+  kt.load_range();
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(&bar[BP_Q], 2 * TILE);
+      tma_2d(sQ, &tq, hA * D, qs, &bar[BP_Q]);
+      tma_2d(sQ + HALF, &tq, hA * D + 64, qs, &bar[BP_Q]);
+      tma_2d(sQ + TILE, &tq, (hA + 1) * D, qs, &bar[BP_Q]);
+      tma_2d(sQ + TILE + HALF, &tq, (hA + 1) * D + 64, qs, &bar[BP_Q]);
+      int u = 0;  // slot uses issued
+      for (bool go = true; go && kt.valid(); kt.next()) {
+        for (int kv = 0; kv < 2; ++kv, ++u) {
+          const int s = u % NSLOT;
+          if (u >= NSLOT && !mbar_wait(&bar[BP_EMPTY + s], ((u / NSLOT) - 1) & 1, abort, p.err, 41)) {
+            go = false;
+            break;
+          }
+          mbar_expect_tx(&bar[BP_FULL + s], TILE);
+          const CUtensorMap* m = kv ? &tv : &tk;
+          tma_2d(ring + s * TILE, m, hk * D, kt.ka, &bar[BP_FULL + s]);
+          tma_2d(ring + s * TILE + HALF, m, hk * D + 64, kt.ka, &bar[BP_FULL + s]);
+        }
+      }
+      if (*abort) {  // let every copy this CTA started land before its shared memory is released
+        int zero = 0;
+        mbar_wait(&bar[BP_Q], 0, (volatile int*)&zero, p.err, 41);
+        for (int i = max(0, u - NSLOT); i < u; ++i) mbar_wait(&bar[BP_FULL + i % NSLOT], (i / NSLOT) & 1, (volatile int*)&zero, p.err, 41);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_QK = idesc_bf16(BN, false), ID_PV = idesc_bf16(D, true);
+      const uint32_t qa = s32(sQ), qb = qa + TILE, rb = s32(ring);
+      auto slot = [&](int u) { return rb + (uint32_t)(u % NSLOT) * TILE; };
+      auto full = [&](int u) { return mbar_wait(&bar[BP_FULL + u % NSLOT], (u / NSLOT) & 1, abort, p.err, 42); };
+      auto qk = [&](uint32_t d, uint32_t qbase, uint32_t kbase) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          tc_mma(d, sdesc(qbase + off, 16, 1024), sdesc(kbase + off, 16, 1024), ID_QK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto pv = [&](uint32_t o, uint32_t pcol, uint32_t vbase, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          tc_mma_ts(o, pcol + kk * 8, sdesc(vbase + kk * 2048, HALF, 1024), ID_PV, (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&bar[BP_Q], 0, abort, p.err, 43);
+      tc_fence_after();
+      int j = 0;
+      for (; ok && kt.valid(); kt.next(), ++j) {
+        const int uk = 2 * j, uv = 2 * j - 1;  // K(j); V(j - 1)
+        if (!(ok = full(uk))) break;
+        if (j > 0 && !(ok = full(uv) && mbar_wait(&bar[BP_P], (j - 1) & 1, abort, p.err, 44))) break;
+        tc_fence_after();
+        if (j > 0) pv(tmem + 256, tmem, slot(uv), j > 1);
+        qk(tmem, qa, slot(uk));
+        tc_commit(&bar[BP_S]);
+        if (j > 0) {
+          if (!(ok = mbar_wait(&bar[BP_P + 1], (j - 1) & 1, abort, p.err, 45))) break;
+          tc_fence_after();
+          pv(tmem + 384, tmem + 128, slot(uv), j > 1);
+          tc_commit(&bar[BP_EMPTY + uv % NSLOT]);
+        }
+        qk(tmem + 128, qb, slot(uk));
+        tc_commit(&bar[BP_S + 1]);
+        tc_commit(&bar[BP_EMPTY + uk % NSLOT]);
+      }
+      if (ok && j >= 1) {
+        const int uv = 2 * j - 1;
+        ok = full(uv) && mbar_wait(&bar[BP_P], (j - 1) & 1, abort, p.err, 46);
+        if (ok) {
+          tc_fence_after();
+          pv(tmem + 256, tmem, slot(uv), j > 1);
+          ok = mbar_wait(&bar[BP_P + 1], (j - 1) & 1, abort, p.err, 47);
+        }
+        if (ok) {
+          tc_fence_after();
+          pv(tmem + 384, tmem + 128, slot(uv), j > 1);
+          tc_commit(&bar[BP_EMPTY + uv % NSLOT]);
+          tc_commit(&bar[BP_O]);
+        }
+      }
+      tc_commit(&bar[BP_DRAIN]);
+      int zero = 0;
+      mbar_wait(&bar[BP_DRAIN], 0, (volatile int*)&zero, p.err, 48);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (warps 0-7)
+    const int hx = warp >> 2, wq = warp & 3;
+    const int r = wq * 32 + lane;  // row within the tile == TMEM lane
+    const int row = qs + r;
+    const uint32_t lane_addr = tmem + ((uint32_t)(wq * 32) << 16);
+    const uint32_t s_col = hx * 128, o_col = 256 + hx * 128;
+    float m_used = -INFINITY, l = 0.f;
+    int j = 0;
+    for (; kt.valid(); kt.next(), ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar[BP_S + hx], j & 1, abort, p.err, 50 + hx))) break;
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32];
+        tmem_ld32(lane_addr + s_col + c * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
+      }
+      const int kend = min(kt.ka + BN, kt.rend);
+      const int climit = row < qe ? (kt.ty == 1 ? min(kend - kt.ka, row - q0 + kt.k0 - kt.ka + 1) : kend - kt.ka) : 0;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        s[c] = c < climit ? s[c] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, s[c]);
+      }
+      const float m_new = fmaxf(m_used, mt);
+      const bool raise = m_new > m_used + RESCALE_THRESHOLD;
+      const bool rescale = raise && j >= 1 && m_used != -INFINITY;
+      if (__any_sync(0xffffffffu, rescale)) {  // PV_X(j-1) is complete: S_X(j)'s commit covers it
+        const float alpha = rescale ? exp2f(m_used - m_new) : 1.f;
+        l *= alpha;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(lane_addr + o_col + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(lane_addr + o_col + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      if (raise) m_used = m_new;
+      const bool live = m_used != -INFINITY;
+      float rs = 0.f;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float e0 = live ? ex2f(s[h2 * 64 + 2 * i] - m_used) : 0.f, e1 = live ? ex2f(s[h2 * 64 + 2 * i + 1] - m_used) : 0.f;
+          rs += e0 + e1;
+          w[i] = pack_bf16x2(e0, e1);
+        }
+        tmem_st32u(lane_addr + s_col + h2 * 32, w);
+      }
+      tmem_st_wait();
+      l += rs;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[BP_P + hx]);
+    }
+    const int n = j;
+    bool ok = __all_sync(0xffffffffu, !*abort);
+    if (ok && n >= 1) ok = __all_sync(0xffffffffu, mbar_wait(&bar[BP_O], 0, abort, p.err, 52));
+    if (ok && n >= 1) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      bf16* orow = p.o + ((long)row * p.Hq + hA + hx) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        tmem_ld32(lane_addr + o_col + c * 32, o);
+        if (row < qe) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = o[i + e] * inv;
+            store8(orow + c * 32 + i, f);
+          }
+        }
+      }
+      if (row < qe) p.lse2[(long)(hA + hx) * p.T + row] = l > 0.f ? m_used + log2f(l) : INFINITY;
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
 // ---------------------------------------------------------------------------------- host side
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
@@ -658,7 +908,8 @@ static at::Tensor& err_flag(int dev) {
 
 // q (T,Hq,128), k/v (Tk,Hkv,128) -> o (T,Hq,128) bf16, lse2 (Hq,T) fp32 (base-2, +inf for rows without keys)
 // variant: 0 = 4 softmax warps, 1 = 4 softmax warps with double-buffered P, 2 = 8 softmax warps,
-// 3 = 8 softmax warps with P in tensor memory
+// 3 = 8 softmax warps with P in tensor memory, 4 = two heads of a GQA group per CTA (variant 3 when
+// the group size is odd)
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles, double scale,
                                     int64_t variant) {
   using namespace atc;
@@ -676,7 +927,15 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
   const CUtensorMap tv = map_rows(v.data_ptr(), Tk, (long)Hkv * D);
   Params p{(bf16*)o.data_ptr(), lse2.data_ptr<float>(), qseg.data_ptr<int>(), kr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T,
            (float)(scale * 1.4426950408889634), err_flag(q.get_device()).data_ptr<int>()};
-  if (variant == 2 || variant == 3) {
+  if (variant == 4 && (Hq / Hkv) % 2 == 0) {
+    const int smemp = (2 + NSLOT) * TILE + NBARP * 8 + 16 + 1024;
+    smem_attr(reinterpret_cast<const void*>(attn_fwd_tcp_k), smemp);
+    attn_fwd_tcp_k<<<dim3(nt, Hq / 2), THREADS_P, smemp, stream()>>>(tq, tk, tv, p);
+    AX_LAUNCH_OK();
+    return {o, lse2};
+  }
+  if (variant == 2 || variant == 3 || variant == 4) {
+    if (variant == 4) variant = 3;  // odd GQA group: one head per CTA
     const int smem8 = 6 * TILE + 3 * 2 * BM * 4 + NBAR8 * 8 + 16 + 1024;
     auto* kern = variant == 3 ? attn_fwd_tc8_k<true> : attn_fwd_tc8_k<false>;
     smem_attr(reinterpret_cast<const void*>(kern), smem8);

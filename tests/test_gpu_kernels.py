@@ -500,7 +500,7 @@ def test_decode_gemm_chain_with_programmatic_launch(variant):
     assert e.skinny_tma_error() == 0
 
 
-@pytest.mark.parametrize("variant", [0, 2, 3,
+@pytest.mark.parametrize("variant", [0, 2, 3, 4,
     pytest.param(1, marks=pytest.mark.skipif(
         os.environ.get("AXRL_TEST_ATTN_TC2") != "1", reason="double-buffered-P variant: gives NaN on some inputs, under investigation"))])
 @pytest.mark.parametrize("case", [0, 1, 2, 3, 4])
