@@ -19,6 +19,8 @@ each GPU must receive over NVLink at the measured 770 GB/s per direction.  Every
 device time, max over ranks, median of ``--iters`` after ``--warmup`` iterations.
 
 torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m axrl_b200.benchmarks.fused_comm_bench [--paths tp,ep] [--tokens 16384]
+
+``--paths kernels`` (one GPU, plain ``python -m``): the fused kernels alone, for profiler captures.
 """
 
 from __future__ import annotations
@@ -141,6 +143,48 @@ def bench_ep(T: int, warmup: int, iters: int, tflops: float) -> list[dict]:
     return out
 
 
+def bench_kernels_1gpu(T: int, warmup: int, iters: int, tflops: float, hbm_gbs: float) -> list[dict]:
+    """The fused kernels on ONE GPU (world size 1), for a profiler capture of the kernel itself:
+    the tcgen05 GEMM storing its tiles into the (here local) owner slots with the channel handshake,
+    against the plain tcgen05 GEMM; the partitioned AdamW storing bf16 parameters through the
+    pointer table, against the AdamW kernel with its local bf16 write-back."""
+    from axrl_b200.ops import _ext
+    from axrl_b200.parallel.tp_overlap import P2PTPComm
+
+    e = _ext.ext()
+    H, F = 4096, 12288
+    g = torch.Generator(device="cuda").manual_seed(3)
+    y = torch.randn(T, F // 2, device="cuda", generator=g).bfloat16()  # a TP=2 down-projection shard
+    w = (torch.randn(H, F // 2, device="cuda", generator=g) * 0.02).bfloat16()
+    os.environ["AXRL_TP_FUSED"] = "1"
+    comm = P2PTPComm(dist.group.WORLD, cap_tokens=T, hidden=H)
+    os.environ["AXRL_TP_FUSED"] = "0"
+    ref = e.linear_fwd(y, w)
+    got = comm.gemm_rs_fused(y, w, None)
+    err = ((got.float() - ref.float()).abs().max() / (ref.float().abs().max() + 1e-6)).item()
+    flops = 2.0 * T * (F // 2) * H
+    rows = []
+    t_plain = _time(lambda: e.linear_fwd(y, w), warmup, iters)
+    t_fused = _time(lambda: comm.gemm_rs_fused(y, w, None), warmup, iters)
+    comm.check()
+    rows.append({"path": "gemm_to_slots_1gpu", "M": T, "N": H, "K": F // 2, "plain_ms": round(t_plain, 4), "fused_ms": round(t_fused, 4),
+                 "plain_tflops": round(flops / t_plain / 1e9, 1), "fused_tflops": round(flops / t_fused / 1e9, 1), "rel_err": float(f"{err:.2e}")})
+    n = 64 << 20  # 64 M parameters of one partition
+    p = torch.randn(n, device="cuda", generator=g)
+    gr = torch.randn(n, device="cuda", generator=g) * 1e-3
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    pb = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    ptrs = torch.tensor([pb.data_ptr()], dtype=torch.int64, device="cuda")
+    sq = (gr.pow(2).sum()).reshape(1)
+    t_adam = _time(lambda: e.adamw_step(p, gr, m, v, pb, n, 1e-5, 0.9, 0.999, 1e-8, 0.01, 2, sq, 1.0, 1.0), warmup, iters)
+    t_p2p = _time(lambda: e.adamw_p2p_step(p, gr, m, v, ptrs, 0, n, 1e-5, 0.9, 0.999, 1e-8, 0.01, 2, sq, 1.0, 1.0), warmup, iters)
+    nbytes = n * (4 * 4 + 4 * 3 + 2)  # read p, g, m, v; write p, m, v and the bf16 parameter
+    rows.append({"path": "adamw_param_store_1gpu", "params": n, "adamw_ms": round(t_adam, 4), "adamw_p2p_ms": round(t_p2p, 4),
+                 "adamw_gbs": round(nbytes / t_adam / 1e6, 1), "adamw_p2p_gbs": round(nbytes / t_p2p / 1e6, 1),
+                 "adamw_p2p_frac_of_hbm": round(nbytes / t_p2p / 1e6 / hbm_gbs, 3)})
+    return rows
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--paths", default="tp,ep")
@@ -149,16 +193,20 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
+    for k, val in (("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29561"), ("RANK", "0"), ("WORLD_SIZE", "1")):
+        os.environ.setdefault(k, val)  # a plain ``python -m`` run is a one-rank job
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(minutes=5), device_id=torch.device("cuda", local))
-    tflops, _ = _peaks()
+    tflops, hbm = _peaks()
     rows = []
     paths = a.paths.split(",")
     if "tp" in paths:
         rows += bench_tp(a.tokens, a.warmup, a.iters, tflops)
     if "ep" in paths:
         rows += bench_ep(a.ep_tokens, a.warmup, a.iters, tflops)
+    if "kernels" in paths:
+        rows += bench_kernels_1gpu(a.tokens, a.warmup, a.iters, tflops, hbm)
     if dist.get_rank() == 0:
         for r in rows:
             print(json.dumps(r), flush=True)
