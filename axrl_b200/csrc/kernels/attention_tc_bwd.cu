@@ -29,6 +29,8 @@
 // code, drains its copies and tensor-core work, frees TMEM and exits.
 #include <cuda.h>
 
+#include <string>
+
 #include "common.cuh"
 #include "tcgen05.cuh"
 
@@ -48,6 +50,7 @@ constexpr int C_S = 0, C_DP = 128, C_DV = 256, C_DK = 384;
 
 constexpr int B_KV = 0, B_QD = 1, B_S = 2, B_P = 3, B_MM = 4, B_DQF = 5, B_DRAIN = 6, B_LD = 7, NBAR = 8;
 
+__device__ __forceinline__ void red_add_f32(float* p, float a) { asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory"); }
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
@@ -72,6 +75,7 @@ struct QTiles {
   const int* qr;
   int it0, it1, G, ks, k0s;
   int g, it, q0, q1, ty, qs;
+  int step = BQ;  // q rows per tile
   __device__ void seek() {
     while (g < G) {
       while (it < it1) {
@@ -88,7 +92,7 @@ struct QTiles {
   }
   __device__ bool valid() const { return g < G; }
   __device__ void next() {
-    qs += BQ;
+    qs += step;
     if (qs >= q1) {
       ++it;
       seek();
@@ -319,6 +323,281 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
   }
 }
 
+// ---------------------------------------------------------------------------------- 64-row q blocks
+// Second backward kernel, one CTA per (128-key tile, kv head) as above, reorganised so that loads,
+// element-wise work and the dQ read-out leave the tensor cores busy:
+//   * q rows come in blocks of 64 through a 3-stage ring (Q, dO: 16 KB each, plus the block's lse2
+//     and Dsum, loaded by the producer warp's lanes), so the next blocks load during this one;
+//   * S^T = K Q^T and dP^T = V dO^T are 128 x 64 (TMEM cols [0,64) and [64,128)); the element-wise
+//     warps write P^T and dS^T back into the first 32 columns of each as bf16 pairs, and dV += P^T dO,
+//     dK += dS^T Q take them as the A operand straight from tensor memory;
+//   * dQ^T = K^T dS^T (M = head dim, N = 64 q rows) goes to one of two 64-column TMEM buffers
+//     ([384,448), [448,512)) and is read out by four separate warps (TMEM lane = head dim, so each
+//     fp32 reduction instruction covers 128 consecutive bytes of the dQ accumulator) while the
+//     tensor cores already work on the next block; dS^T is also written to shared memory (two
+//     buffers) as the B operand of that product;
+//   * dV and dK accumulate in TMEM columns [128,256) and [256,384) over every block and head.
+// Warps 0-3 element-wise (TMEM lane = key), 4-7 dQ read-out and the final dK / dV store, 8 TMA,
+// 9 MMA issuer and TMEM owner.  Every mbarrier wait is bounded.
+namespace atb2 {
+using namespace tc;
+constexpr int BQ2 = 64, NST = 3, THREADS2 = 320;
+constexpr int QT = BQ2 * D * 2;  // 16 KB: 64 rows x 128 head dims (two 64-column boxes of 8 KB)
+constexpr int QHALF = QT / 2;
+constexpr int DST = 128 * BQ2 * 2;           // 16 KB: dS^T [128 keys][64 q], one 128-byte swizzled box
+constexpr uint32_t C2_S = 0, C2_DP = 64, C2_DV = 128, C2_DK = 256, C2_DQ = 384;
+constexpr int B2_KV = 0, B2_FULL = 1, B2_EMPTY = B2_FULL + NST, B2_S = B2_EMPTY + NST, B2_P = B2_S + 1, B2_DQF = B2_P + 1, B2_DQE = B2_DQF + 2,
+              B2_DONE = B2_DQE + 2, B2_DRAIN = B2_DONE + 1, NBAR2 = B2_DRAIN + 1;
+}  // namespace atb2
+
+__global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                                                                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                                                                     Params p) {
+  using namespace atb2;
+  extern __shared__ char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  char* sK = sm;
+  char* sV = sm + TILE;
+  char* sSt = sm + 2 * TILE;       // NST stages of (Q, dO), 32 KB each
+  char* sDS = sSt + NST * 2 * QT;  // two dS^T buffers
+  float* sLD = reinterpret_cast<float*>(sDS + 2 * DST);  // [stage][lse2 64 | Dsum 64]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sLD + NST * 2 * BQ2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seg = p.tiles[blockIdx.x * 2], ks = p.tiles[blockIdx.x * 2 + 1];
+  const int hk = blockIdx.y, G = p.Hq / p.Hkv;
+  const int k0s = p.kseg[seg * 4], k1s = p.kseg[seg * 4 + 1], it0 = p.kseg[seg * 4 + 2], it1 = p.kseg[seg * 4 + 3];
+  const int ke = min(ks + BK, k1s);
+
+  if (tid == 0) {
+    mbar_init(&bar[B2_KV], 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&bar[B2_FULL + s], 1);
+      mbar_init(&bar[B2_EMPTY + s], 1);
+    }
+    mbar_init(&bar[B2_S], 1);
+    mbar_init(&bar[B2_P], 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar[B2_DQF + b], 1);
+      mbar_init(&bar[B2_DQE + b], 4);
+    }
+    mbar_init(&bar[B2_DONE], 1);
+    mbar_init(&bar[B2_DRAIN], 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 9) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  QTiles qt{p.qr, it0, it1, G, ks, k0s, 0, it0, 0, 0, 0, 0, BQ2};
+  qt.seek();
+  auto q_at = [&](int s) { return sSt + s * 2 * QT; };       // Q of stage s (dO at + QT)
+  auto ld_at = [&](int s) { return sLD + s * 2 * BQ2; };     // lse2 of stage s (Dsum at + BQ2)
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer: K/V once, then (Q, dO, lse2, Dsum) per block
+    if (lane == 0) {
+      mbar_expect_tx(&bar[B2_KV], 2 * TILE);
+      tma_2d(sK, &tk, hk * D, ks, &bar[B2_KV]);
+      tma_2d(sK + HALF, &tk, hk * D + 64, ks, &bar[B2_KV]);
+      tma_2d(sV, &tv, hk * D, ks, &bar[B2_KV]);
+      tma_2d(sV + HALF, &tv, hk * D + 64, ks, &bar[B2_KV]);
+    }
+    int i = 0;
+    for (; qt.valid(); qt.next(), ++i) {
+      const int s = i % NST;
+      if (i >= NST && !__all_sync(0xffffffffu, mbar_wait(&bar[B2_EMPTY + s], ((i / NST) - 1) & 1, abort, p.err, 61))) break;
+      const int h = hk * G + qt.g, qe = min(qt.qs + BQ2, qt.q1);
+      float* L = ld_at(s);
+      for (int c = lane; c < BQ2; c += 32) {
+        const bool in = qt.qs + c < qe;
+        L[c] = in ? p.lse2[(long)h * p.T + qt.qs + c] : INFINITY;
+        L[BQ2 + c] = in ? p.dsum[(long)h * p.T + qt.qs + c] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        char* dst = q_at(s);
+        mbar_expect_tx(&bar[B2_FULL + s], 2 * QT);
+        tma_2d(dst, &tq, h * D, qt.qs, &bar[B2_FULL + s]);
+        tma_2d(dst + QHALF, &tq, h * D + 64, qt.qs, &bar[B2_FULL + s]);
+        tma_2d(dst + QT, &tdo, h * D, qt.qs, &bar[B2_FULL + s]);
+        tma_2d(dst + QT + QHALF, &tdo, h * D + 64, qt.qs, &bar[B2_FULL + s]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0 && *abort) {  // every copy this CTA started lands before its shared memory is released
+      int zero = 0;
+      mbar_wait(&bar[B2_KV], 0, (volatile int*)&zero, p.err, 61);
+      for (int j = max(0, i - NST); j < i; ++j) mbar_wait(&bar[B2_FULL + j % NST], (j / NST) & 1, (volatile int*)&zero, p.err, 61);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(BQ2, false);               // A = K / V, B = Q / dO, both K-major, N = 64
+      constexpr uint32_t ID_G = idesc_bf16(D, true);                  // A from TMEM, B = dO / Q MN-major, N = 128
+      constexpr uint32_t ID_Q = idesc_bf16(BQ2, true, true);          // A = K^T and B = dS^T, both MN-major, N = 64
+      const uint32_t k_b = s32(sK), v_b = s32(sV), ds_b = s32(sDS);
+      bool ok = mbar_wait(&bar[B2_KV], 0, abort, p.err, 62);
+      int i = 0;
+      for (; ok && qt.valid(); qt.next(), ++i) {
+        const int s = i % NST;
+        const uint32_t q_b = s32(q_at(s)), do_b = q_b + QT;
+        if (!(ok = mbar_wait(&bar[B2_FULL + s], (i / NST) & 1, abort, p.err, 63))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {  // S^T = K Q^T, dP^T = V dO^T (K = head dim)
+          const uint32_t ak = (kk >> 2) * HALF + (kk & 3) * 32, bk = (kk >> 2) * QHALF + (kk & 3) * 32;
+          tc_mma(tmem + C2_S, sdesc(k_b + ak, 16, 1024), sdesc(q_b + bk, 16, 1024), ID_S, kk > 0);
+          tc_mma(tmem + C2_DP, sdesc(v_b + ak, 16, 1024), sdesc(do_b + bk, 16, 1024), ID_S, kk > 0);
+        }
+        tc_commit(&bar[B2_S]);
+        if (!(ok = mbar_wait(&bar[B2_P], i & 1, abort, p.err, 64))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ2 / 16; ++kk) {  // dV += P^T dO, dK += dS^T Q (K = q rows; P^T, dS^T from TMEM)
+          tc_mma_ts(tmem + C2_DV, tmem + C2_S + kk * 8, sdesc(do_b + kk * 2048, QHALF, 1024), ID_G, (i > 0 || kk > 0));
+          tc_mma_ts(tmem + C2_DK, tmem + C2_DP + kk * 8, sdesc(q_b + kk * 2048, QHALF, 1024), ID_G, (i > 0 || kk > 0));
+        }
+        tc_commit(&bar[B2_EMPTY + s]);
+        const int b = i & 1;
+        if (i >= 2 && !(ok = mbar_wait(&bar[B2_DQE + b], ((i - 2) >> 1) & 1, abort, p.err, 65))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)  // dQ^T = K^T dS^T (K = keys)
+          tc_mma(tmem + C2_DQ + b * BQ2, sdesc(k_b + kk * 2048, HALF, 1024), sdesc(ds_b + b * DST + kk * 2048, DST, 1024), ID_Q, kk > 0);
+        tc_commit(&bar[B2_DQF + b]);
+      }
+      if (ok) tc_commit(&bar[B2_DONE]);
+      tc_commit(&bar[B2_DRAIN]);
+      int zero = 0;
+      mbar_wait(&bar[B2_DRAIN], 0, (volatile int*)&zero, p.err, 66);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ element-wise gradient (TMEM lane = key)
+    const int r = warp * 32 + lane;
+    const int key = ks + r;
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    int i = 0;
+    for (; qt.valid(); qt.next(), ++i) {
+      const int s = i % NST, b = i & 1;
+      const int qs = qt.qs, qe = min(qs + BQ2, qt.q1);
+      const int climit = key < ke ? qe - qs : 0;
+      const int cfirst = qt.ty == 1 ? max(0, (key - k0s) - (qs - qt.q0)) : 0;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar[B2_S], i & 1, abort, p.err, 67))) break;
+      // the stage's lse2 / Dsum were stored by the producer's lanes before its arrival on FULL
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar[B2_FULL + s], (i / NST) & 1, abort, p.err, 67))) break;
+      // dS^T buffer b is free once dQ of block i - 2 has been computed
+      if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&bar[B2_DQF + b], ((i - 2) >> 1) & 1, abort, p.err, 68))) break;
+      tc_fence_after();
+      const float* L = ld_at(s);
+      const float* Ds = L + BQ2;
+      char* dsrow = sDS + b * DST + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        const int c0 = hh * 32;
+        float sv[32], dp[32];
+        tmem_ld32(lane_addr + C2_S + c0, sv);
+        tmem_ld32(lane_addr + C2_DP + c0, dp);
+        uint32_t pw[16], dw[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dv2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int c = c0 + e + u;
+            const bool vis = c >= cfirst && c < climit;
+            const float pr = vis ? exp2f(sv[e + u] * p.scale_log2 - L[c]) : 0.f;
+            pv[u] = pr;
+            dv2[u] = vis ? pr * (dp[e + u] - Ds[c]) * p.scale : 0.f;
+          }
+          bf162 a = __floats2bfloat162_rn(pv[0], pv[1]), d2 = __floats2bfloat162_rn(dv2[0], dv2[1]);
+          pw[e / 2] = *reinterpret_cast<uint32_t*>(&a);
+          dw[e / 2] = *reinterpret_cast<uint32_t*>(&d2);
+        }
+        tmem_st16u(lane_addr + C2_S + hh * 16, pw);   // P^T (bf16 pairs) over the consumed S^T columns
+        tmem_st16u(lane_addr + C2_DP + hh * 16, dw);  // dS^T over dP^T
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {  // dS^T row r, q columns c0 + 8 q8 .. +7: 16-byte chunk (hh*4 + q8) of the 128-byte row
+          const int ch = hh * 4 + q8;
+          *reinterpret_cast<uint4*>(dsrow + ((ch ^ (r & 7)) << 4)) = make_uint4(dw[q8 * 4], dw[q8 * 4 + 1], dw[q8 * 4 + 2], dw[q8 * 4 + 3]);
+        }
+      }
+      tmem_st_wait();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // dS^T visible to the tensor cores
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B2_P]);
+    }
+  } else {
+    // ------------------------------------------------------------ dQ read-out (TMEM lane = head dim), then dK / dV
+    const int wq = warp - 4;
+    const int d = wq * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(wq * 32) << 16);
+    int i = 0;
+    bool ok = true;
+    for (; qt.valid(); qt.next(), ++i) {
+      const int b = i & 1;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&bar[B2_DQF + b], (i >> 1) & 1, abort, p.err, 69)))) break;
+      tc_fence_after();
+      const int h = hk * G + qt.g, qs = qt.qs, n = min(qs + BQ2, qt.q1) - qs;
+      float* dq = p.dq_acc + ((long)qs * p.Hq + h) * D + d;
+      const long rstride = (long)p.Hq * D;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        float v[32];
+        tmem_ld32(lane_addr + C2_DQ + b * BQ2 + hh * 32, v);
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (hh * 32 + c < n) red_add_f32(dq + (hh * 32 + c) * rstride, v[c]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B2_DQE + b]);
+    }
+    ok = ok && __all_sync(0xffffffffu, !*abort) && i > 0;
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar[B2_DONE], 0, abort, p.err, 70));
+    if (ok) {  // TMEM lane = key for dK / dV
+      tc_fence_after();
+      const int key = ks + d;
+      bf16* dkr = p.dk + ((long)key * p.Hkv + hk) * D;
+      bf16* dvr = p.dv + ((long)key * p.Hkv + hk) * D;
+#pragma unroll 1
+      for (int cc = 0; cc < D; cc += 32) {
+        float a[32], bb[32];
+        tmem_ld32(lane_addr + C2_DK + cc, a);
+        tmem_ld32(lane_addr + C2_DV + cc, bb);
+        if (key < ke) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            float fa[8], fb[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              fa[u] = a[e + u];
+              fb[u] = bb[e + u];
+            }
+            store8(dkr + cc + e, fa);
+            store8(dvr + cc + e, fb);
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
 // ---------------------------------------------------------------------------------- host side
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
@@ -335,11 +614,11 @@ static EncodeFn encoder() {
   return fn;
 }
 
-static CUtensorMap map_rows(const void* base, long rows, long width) {
+static CUtensorMap map_rows(const void* base, long rows, long width, int box_rows = 128) {
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)width * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -357,6 +636,18 @@ static at::Tensor& err_flag(int dev) {
 
 // The key-tile part of the backward: dq_acc (fp32, zeroed by the caller) += dQ, dk / dv (zeroed) = dK / dV.
 // tiles: (n, 2) int32 (kseg index, 128-key tile start); dsum = rowsum(dO o O) (Hq, T).
+// AXRL_ATTN_BWD_BLOCKS=64 selects attn_bwd_tc2_k (64-row q blocks through a 3-stage ring, dQ read out
+// by separate warps); set_attn_bwd_blocks64 switches it at run time.
+static int& bwd_blocks64_flag() {
+  static int on = [] {
+    const char* e = std::getenv("AXRL_ATTN_BWD_BLOCKS");
+    return (e && std::string(e) == "64") ? 1 : 0;
+  }();
+  return on;
+}
+static bool bwd_blocks64() { return bwd_blocks64_flag() != 0; }
+void set_attn_bwd_blocks64(bool on) { bwd_blocks64_flag() = on ? 1 : 0; }
+
 void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor lse2, at::Tensor dsum, at::Tensor dq_acc,
                        at::Tensor dk, at::Tensor dv, at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale) {
   using namespace atb;
@@ -371,6 +662,16 @@ void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v
   Params p{lse2.data_ptr<float>(), dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), (bf16*)dk.data_ptr(), (bf16*)dv.data_ptr(),
            kseg.data_ptr<int>(), qr.data_ptr<int>(), tiles.data_ptr<int>(), Hq, Hkv, T, (float)(scale * 1.4426950408889634), (float)scale,
            err_flag(q.get_device()).data_ptr<int>()};
+  if (bwd_blocks64()) {
+    using namespace atb2;
+    const CUtensorMap tq64 = map_rows(q.data_ptr(), T, (long)Hq * D, BQ2);
+    const CUtensorMap tdo64 = map_rows(dout.data_ptr(), T, (long)Hq * D, BQ2);
+    const int smem2 = 2 * TILE + NST * 2 * QT + 2 * DST + NST * 2 * BQ2 * 4 + NBAR2 * 8 + 16 + 1024;
+    smem_attr(reinterpret_cast<const void*>(attn_bwd_tc2_k), smem2);
+    attn_bwd_tc2_k<<<dim3(nt, Hkv), THREADS2, smem2, stream()>>>(tq64, tk, tv, tdo64, p);
+    AX_LAUNCH_OK();
+    return;
+  }
   const int smem = 6 * TILE + 4 * BQ * 4 + NBAR * 8 + 16 + 1024;
   smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_k), smem);
   attn_bwd_tc_k<<<dim3(nt, Hkv), THREADS, smem, stream()>>>(tq, tk, tv, tdo, p);

@@ -40,6 +40,7 @@ std::vector<at::Tensor> attn_merge(std::vector<at::Tensor> os, std::vector<at::T
 at::Tensor gdn_step(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, at::Tensor pool, at::Tensor slots);
 int64_t attn_bwd_tc_error();
 void set_attn_bwd_tc(bool on);
+void set_attn_bwd_blocks64(bool on);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
                        double, c10::optional<at::Tensor>);
 void decode_plan(at::Tensor seq_lens, at::Tensor prefix);
@@ -160,6 +161,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_step", &ax::gdn_step);
   m.def("attn_bwd_tc_error", &ax::attn_bwd_tc_error);
   m.def("set_attn_bwd_tc", &ax::set_attn_bwd_tc);
+  m.def("set_attn_bwd_blocks64", &ax::set_attn_bwd_blocks64);
   m.def("set_decode_attn_tma", &ax::set_decode_attn_tma);
   m.def("paged_decode_attn", &ax::paged_decode_attn);
   m.def("kv_store", &ax::kv_store);

@@ -79,6 +79,14 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[3
       "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
+// 16 consecutive 32-bit columns of this thread's TMEM lane (raw words).
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr), "r"(v[0]),
+      "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]),
+      "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 // 32 consecutive fp32 columns of this thread's TMEM lane.  The wait is part of the same asm
 // statement, so no use of the destination registers can be scheduled before the data arrived.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {

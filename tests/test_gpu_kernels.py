@@ -544,9 +544,11 @@ def test_attention_tcgen05_forward_matches_reference(case, variant):
     close(lse[fin], lse2[fin], 1e-3, 1e-4, msg="lse")
 
 
+@pytest.mark.parametrize("blocks64", [False, True])
 @pytest.mark.parametrize("case", [0, 1, 2, 3])
-def test_attention_tcgen05_backward_matches_mma(case):
-    """tcgen05 backward (attention_tc_bwd.cu) against the mma.sync backward on the same inputs:
+def test_attention_tcgen05_backward_matches_mma(case, blocks64):
+    """tcgen05 backward (attention_tc_bwd.cu; 128-row q tiles, or 64-row blocks through a 3-stage
+    ring with dQ^T read out by separate warps) against the mma.sync backward on the same inputs:
     causal packs, a prefix tree, full ranges with a longer key buffer."""
     from axrl_b200.ops.attention_spec import spec_from_triples
 
@@ -570,8 +572,12 @@ def test_attention_tcgen05_backward_matches_mma(case):
         ref = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
     finally:
         e.set_attn_bwd_tc(True)
-    got = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
-    torch.cuda.synchronize()
+    e.set_attn_bwd_blocks64(blocks64)
+    try:
+        got = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
+        torch.cuda.synchronize()
+    finally:
+        e.set_attn_bwd_blocks64(False)
     assert e.attn_bwd_tc_error() == 0
     for name, a, b in zip(("dq", "dk", "dv"), got, ref):
         close(a, b, 3e-2, 2e-2, msg=name)
