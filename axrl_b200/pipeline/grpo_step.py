@@ -61,6 +61,9 @@ class SyntheticGRPOConfig:
     eos_token_id: int = 0
     merge_group_prompts: bool = True  # prefix-tree pack each group's shared prompt
     compute_ref_logprobs: bool = True
+    # keep the reference-policy weights in device memory (a device-to-device copy before the ref
+    # log-prob pass) instead of pinned host memory (a host-to-device copy of the whole model)
+    ref_on_device: bool = False
     compute_old_logprobs: bool = True
     separate_rollout_copy: bool = False
     seed: int = 0
@@ -101,9 +104,14 @@ class SyntheticGRPO:
         self.train = train_engine or TrainEngine(worker_cfg, model_cfg, self.device)
         self.trainer = GrpoTrainer(grpo_cfg)
         self.rng = np.random.default_rng(sc.seed)
-        self.ref_weights = self.train.snapshot_weights() if sc.compute_ref_logprobs else None
-        if self.ref_weights is not None and self.device.type == "cuda":
-            self.ref_weights = self.ref_weights.pin_memory()
+        self.ref_weights = None
+        if sc.compute_ref_logprobs:
+            if sc.ref_on_device and self.device.type == "cuda" and self.train.optim is not None:
+                self.ref_weights = self.train.optim.bf16.detach().clone()
+            else:
+                self.ref_weights = self.train.snapshot_weights()
+                if self.device.type == "cuda":
+                    self.ref_weights = self.ref_weights.pin_memory()
         rollout_model = self.train.model
         if sc.separate_rollout_copy:
             rollout_model = copy.deepcopy(self.train.model)

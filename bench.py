@@ -160,12 +160,16 @@ def main() -> None:
     train.optim.release_grads()  # gradients live only inside the train phase
     torch.cuda.empty_cache()  # the caching allocator still holds the released blocks
     free = torch.cuda.mem_get_info(dev)[0]
-    kv_gb = a.kv_gb if a.kv_gb else max(2.0, (free - (a.headroom_gb << 30)) / (1 << 30))
+    # reference-policy weights on the device when that still leaves a 40 GB KV pool (a device copy
+    # per step instead of a host-to-device copy of the whole model)
+    ref_bytes = sum(p.numel() * p.element_size() for p in train.model.parameters())
+    ref_dev = not a.no_ref and free - ref_bytes - (a.headroom_gb << 30) >= (40 << 30)
+    kv_gb = a.kv_gb if a.kv_gb else max(2.0, (free - (ref_bytes if ref_dev else 0) - (a.headroom_gb << 30)) / (1 << 30))
     sc = SyntheticGRPOConfig(num_prompts=a.prompts_per_gpu, prompt_len=a.prompt_len, group_size=a.group, temperature=1.0,
                              forced_len_median=a.median, forced_len_sigma=1.0, forced_len_min=16, forced_len_max=a.max_len,
                              eos_token_id=151645 % mcfg.vocab_size, merge_group_prompts=False, compute_ref_logprobs=not a.no_ref,
                              seed=1000 + rank, use_cuda_graph=True, kv_gb=kv_gb, kv_memory_saver=True,
-                             partial_rollout=not a.no_partial, inflight_prompts=a.inflight_per_gpu)
+                             partial_rollout=not a.no_partial, inflight_prompts=a.inflight_per_gpu, ref_on_device=ref_dev)
     pipe = SyntheticGRPO(mcfg, wc, grpo, sc, dev, train_engine=train)
 
     def barrier() -> None:
@@ -243,7 +247,7 @@ def main() -> None:
                        "seq_len": a.prompt_len + a.max_len, "prompt_len": a.prompt_len,
                        "response_len": f"lognormal(median {a.median:g}, sigma 1) clipped [16,{a.max_len}]",
                        "micro_batch_tokens": a.mb_tokens, "parallelism": f"dp{world}" + (f"ep{ep}" if ep > 1 else ""), "colocated": True,
-                       "ref_logprobs": not a.no_ref, "deterministic_attention_backward": a.deterministic, "kv_pool_gb": round(kv_gb, 1), "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
+                       "ref_logprobs": not a.no_ref, "ref_weights": "device" if ref_dev else "pinned host", "deterministic_attention_backward": a.deterministic, "kv_pool_gb": round(kv_gb, 1), "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
             "sync_s": round(sum(m["sync_s"] for m in step_metrics) / len(step_metrics), 4),
             "step_breakdown_s": {k: round(v, 3) for k, v in zip(phases, ph)},
             "step_breakdown_note": "wall seconds per step, mean over the timed steps, max over ranks",
