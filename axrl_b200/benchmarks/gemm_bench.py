@@ -22,7 +22,12 @@ def main() -> None:
     ap.add_argument("--bwd", action="store_true", help="data- and weight-gradient GEMMs: CUTLASS vs the hand-written kernel")
     ap.add_argument("--ms", default="1,8,32,64,128,256,4096", help="comma-separated M values")
     ap.add_argument("--shapes", default="qkv,o,gate_up,down,lm_head")
+    ap.add_argument("--chain", type=int, default=0,
+                    help="time N back-to-back GEMMs on distinct weights (up to 6 GB), stream-ordered with programmatic "
+                         "dependent launch as in a decode step, instead of single isolated launches")
     a = ap.parse_args()
+    if a.chain:
+        return bench_chain(a)
     if a.sweep_decomp:
         return sweep_decomp(a.iters)
     if a.bwd:
@@ -67,6 +72,53 @@ def main() -> None:
                 except Exception as ex:  # noqa: BLE001
                     res[v] = str(ex)[:80]
             print(json.dumps(res), flush=True)
+
+
+def bench_chain(a) -> None:  # noqa: ANN001
+    """Per-GEMM time inside a stream-ordered chain: every GEMM reads the same activation rows and its
+    own weight matrix (never the same weights twice in a row, so every weight byte comes from HBM);
+    launches overlap through programmatic dependent launch as in the decode step."""
+    from axrl_b200.ops import _ext
+
+    e = _ext.ext()
+    shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288), "lm_head": (151936, 4096)}
+    shapes = {k: v for k, v in shapes.items() if k in a.shapes.split(",")}
+    e.set_pdl(True)
+    e.set_weights_static(True)
+    try:
+        for M in [int(m) for m in a.ms.split(",")]:
+            for name, (N, K) in shapes.items():
+                n = max(2, min(a.chain, (6 << 30) // (2 * N * K)))
+                ws = [(torch.randn(N, K, device="cuda") * 0.02).bfloat16() for _ in range(n)]
+                x = torch.randn(M, K, device="cuda").bfloat16()
+                res = {"M": M, "shape": name, "N": N, "K": K, "chain": n}
+                for v in a.variants.split(","):
+                    if (v in ("skinny", "swapab", "tcstream") and M > 64) or (v == "tma" and M > 32):
+                        continue
+                    try:
+                        if v == "auto":
+                            fn = lambda w: e.linear_fwd(x, w)  # noqa: E731
+                        else:
+                            fn = lambda w, v=v: e.linear_variant(x, w, v)  # noqa: E731
+                        for w in ws[:2]:
+                            fn(w)
+                        torch.cuda.synchronize()
+                        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        s0.record()
+                        for w in ws:
+                            fn(w)
+                        s1.record()
+                        s1.synchronize()
+                        ms = s0.elapsed_time(s1) / n
+                        bytes_ = 2 * (M * K + N * K + M * N)
+                        res[v] = {"us": round(ms * 1000, 1), "TBps": round(bytes_ / ms / 1e9, 2)}
+                    except Exception as ex:  # noqa: BLE001
+                        res[v] = str(ex)[:80]
+                print(json.dumps(res), flush=True)
+                del ws
+                torch.cuda.empty_cache()
+    finally:
+        e.set_weights_static(False)
 
 
 def bench_bwd(a) -> None:  # noqa: ANN001

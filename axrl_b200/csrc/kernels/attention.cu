@@ -568,16 +568,16 @@ __global__ void attn_merge_k(MergeParams p) {
 std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor qseg, at::Tensor kr, at::Tensor tiles,
                                     double scale, int64_t variant);
 
-// Forward implementation: the tcgen05 kernel (attention_tc.cu) with 8 softmax warps (two per
-// row) and P in tensor memory (477 TFLOP/s against 257 for the 4-warp variant on the 15 872-token
-// Qwen3-8B pack); AXRL_ATTN_FWD=tc4 selects the 4-warp variant, =tc8 8 warps with P in shared
-// memory, =tc2 the 4-warp double-buffered-P variant, =tcp two heads of a GQA group per CTA, =mma
-// the mma.sync kernel below.
+// Forward implementation: the tcgen05 kernel (attention_tc.cu) with two q heads of a GQA group per
+// CTA (588 TFLOP/s on the 15 872-token Qwen3-8B pack, against 479 for one head per CTA with 8
+// softmax warps and P in tensor memory, AXRL_ATTN_FWD=tc8p, and 257 for the 4-warp variant);
+// AXRL_ATTN_FWD=tc4 selects the 4-warp variant, =tc8 8 warps with P in shared memory, =tc2 the
+// 4-warp double-buffered-P variant, =mma the mma.sync kernel below.
 static int tc_forward_mode() {  // -1: mma.sync, else the attn_fwd_tc variant
   static int mode = [] {
     const char* e = std::getenv("AXRL_ATTN_FWD");
     const std::string v = e ? e : "";
-    return v == "mma" ? -1 : v == "tc2" ? 1 : v == "tc8" ? 2 : v == "tc4" ? 0 : v == "tcp" ? 4 : 3;
+    return v == "mma" ? -1 : v == "tc2" ? 1 : v == "tc8" ? 2 : v == "tc4" ? 0 : v == "tc8p" ? 3 : 4;
   }();
   return mode;
 }

@@ -107,9 +107,9 @@ def test_gemm_family(M, N, K):
 @pytest.mark.parametrize("M", [1, 7, 16, 33, 64, 100])
 @pytest.mark.parametrize("N,K", [(6144, 4096), (4096, 12288), (24576, 4096), (1024, 256), (65600, 128)])
 def test_linear_residual_and_skinny(M, N, K):
-    """Decode-shaped GEMMs: skinny weight-streaming kernel (M <= 64; equal unit ranges per CTA, tiles
-    split between CTAs through the self-cleaning workspace, whole tiles per CTA when M x N exceeds
-    it) and the residual-fused epilogue; called twice to check the workspace is left clean."""
+    """Decode-shaped GEMMs: skinny weight-streaming kernel (M <= 64, split-K with self-cleaning
+    workspace, no split when M x N exceeds it) and the residual-fused epilogue; called twice to
+    check the workspace is left clean."""
     e = _ext()
     x = torch.randn(M, K, device=DEV).bfloat16()
     w = (torch.randn(N, K, device=DEV) / math.sqrt(K)).bfloat16()
