@@ -127,11 +127,20 @@ class SyntheticGRPO:
         if sc.kv_gb is not None:
             per_tok = 2 * model_cfg.num_hidden_layers * model_cfg.num_key_value_heads * model_cfg.head_dim * 2
             kv_tokens = min(kv_tokens, int(sc.kv_gb * (1 << 30)) // per_tok)
+        # tensor parallelism: the rollout engine runs on the trainer's own shards (same TP layout) and
+        # needs the whole embedding table, gathered from the vocabulary shards after every update
+        tp = self.train.tp
+        self.embed_full = None
+        if tp.enabled:
+            emb = self.train.model.embed_tokens
+            self.embed_full = torch.empty(emb.shape[0] * tp.size, emb.shape[1], dtype=emb.dtype, device=emb.device)
+            self._gather_embedding()
         self.rollout = RolloutEngine(rollout_model, max_batch=sc.max_batch or n_seq, kv_tokens=kv_tokens, page_size=64,
                                      max_context=max_ctx, max_prefill_tokens=max(16384, sc.prompt_len), seed=sc.seed,
                                      use_cuda_graph=sc.use_cuda_graph, eos_token_id=sc.eos_token_id,
                                      kv_memory_saver=cuda and sc.kv_memory_saver,
-                                     dp_attention=_ep_active(rollout_model))
+                                     dp_attention=_ep_active(rollout_model),
+                                     tp_group=self.train.par.tp_group if tp.enabled else None, embed_full=self.embed_full)
         if cuda and self.train.optim is not None:
             self.train.release_grads_after_step = True  # the grad buffer is not needed during rollout
         self.weight_version = 0
@@ -288,10 +297,20 @@ class SyntheticGRPO:
                 "carried_groups": len(self.pool), "multi_segment_trajectories": sum(m.segments > 1 for g in take for m in g.members)}
         return out_reqs, out_res, info
 
+    @torch.no_grad()
+    def _gather_embedding(self) -> None:
+        """The whole embedding table from the TP ranks' vocabulary shards, into the same buffer (the
+        rollout engine's CUDA graphs hold its address)."""
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(self.embed_full, self.train.model.embed_tokens.detach().contiguous(), group=self.train.par.tp_group)
+
     def sync_weights(self) -> None:
         """Trainer -> rollout weight sync (in-process)."""
         if self.sc.separate_rollout_copy:
             self.rollout.update_weights_from_model(self.train.model)
+        if self.embed_full is not None:
+            self._gather_embedding()
         self.rollout.reset_prefix_cache()
         self.weight_version += 1
 

@@ -51,6 +51,7 @@ def _args():
     ap.add_argument("--no-ref", action="store_true", help="skip the reference-policy logprob pass")
     ap.add_argument("--kv-gb", type=float, default=None, help="KV pool size (default: free memory minus --headroom-gb)")
     ap.add_argument("--headroom-gb", type=int, default=24)
+    ap.add_argument("--tp", type=int, default=1, help="tensor parallelism (TP groups of consecutive ranks, data parallel across them)")
     ap.add_argument("--ep", type=int, default=None,
                     help="expert parallelism for MoE models (default: every GPU, dense parts data-parallel over the same ranks)")
     ap.add_argument("--ep-backend", choices=["p2p", "torch"], default="p2p", help="EP dispatch / combine: NVLink kernels or NCCL all-to-all")
@@ -154,8 +155,18 @@ def main() -> None:
     ep = (a.ep or world) if mcfg.is_moe else 1
     if ep not in (1, world):
         raise SystemExit("--ep must be 1 or the number of GPUs")
-    par = ParallelCtx(dp_group=dist.group.WORLD if world > 1 else None, dp_size=world, dp_rank=rank,
-                      ep_group=dist.group.WORLD if ep > 1 else None, ep_size=ep, ep_backend=a.ep_backend)
+    tp = a.tp
+    if world % tp or (tp > 1 and mcfg.is_moe):
+        raise SystemExit("--tp must divide the number of GPUs (dense models)")
+    dp, dp_rank = world // tp, rank // tp
+    if tp > 1:  # every rank creates every group, in the same order
+        tp_groups = [dist.new_group(list(range(i, i + tp))) for i in range(0, world, tp)]
+        dp_groups = [dist.new_group(list(range(j, world, tp))) for j in range(tp)]
+        par = ParallelCtx(dp_group=dp_groups[rank % tp] if dp > 1 else None, dp_size=dp, dp_rank=dp_rank, tp_group=tp_groups[rank // tp],
+                          tp_size=tp, tp_rank=rank % tp, tp_backend="p2p")
+    else:
+        par = ParallelCtx(dp_group=dist.group.WORLD if world > 1 else None, dp_size=world, dp_rank=rank,
+                          ep_group=dist.group.WORLD if ep > 1 else None, ep_size=ep, ep_backend=a.ep_backend)
     train = TrainEngine(wc, mcfg, dev, par=par)
     train.optim.release_grads()  # gradients live only inside the train phase
     torch.cuda.empty_cache()  # the caching allocator still holds the released blocks
@@ -165,11 +176,11 @@ def main() -> None:
     ref_bytes = sum(p.numel() * p.element_size() for p in train.model.parameters())
     ref_dev = not a.no_ref and free - ref_bytes - (a.headroom_gb << 30) >= (40 << 30)
     kv_gb = a.kv_gb if a.kv_gb else max(2.0, (free - (ref_bytes if ref_dev else 0) - (a.headroom_gb << 30)) / (1 << 30))
-    sc = SyntheticGRPOConfig(num_prompts=a.prompts_per_gpu, prompt_len=a.prompt_len, group_size=a.group, temperature=1.0,
+    sc = SyntheticGRPOConfig(num_prompts=a.prompts_per_gpu * tp, prompt_len=a.prompt_len, group_size=a.group, temperature=1.0,
                              forced_len_median=a.median, forced_len_sigma=1.0, forced_len_min=16, forced_len_max=a.max_len,
                              eos_token_id=151645 % mcfg.vocab_size, merge_group_prompts=False, compute_ref_logprobs=not a.no_ref,
-                             seed=1000 + rank, use_cuda_graph=True, kv_gb=kv_gb, kv_memory_saver=True,
-                             partial_rollout=not a.no_partial, inflight_prompts=a.inflight_per_gpu, ref_on_device=ref_dev)
+                             seed=1000 + dp_rank, use_cuda_graph=True, kv_gb=kv_gb, kv_memory_saver=True,
+                             partial_rollout=not a.no_partial, inflight_prompts=a.inflight_per_gpu * tp, ref_on_device=ref_dev)
     pipe = SyntheticGRPO(mcfg, wc, grpo, sc, dev, train_engine=train)
 
     def barrier() -> None:
@@ -215,7 +226,7 @@ def main() -> None:
         tot = t.clone()
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
         dev_ms, wall = float(mx[0]), float(mx[1])
-        tokens_all, launches_all = float(tot[2]), float(tot[3])
+        tokens_all, launches_all = float(tot[2]) / tp, float(tot[3])  # the ranks of a TP group train the same tokens
         ph = [float(x) for x in mx[4:]]
     else:
         tokens_all, launches_all = float(tokens), float(launches)
@@ -246,7 +257,7 @@ def main() -> None:
                        "inflight_groups": (a.inflight_per_gpu if not a.no_partial else a.prompts_per_gpu) * world,
                        "seq_len": a.prompt_len + a.max_len, "prompt_len": a.prompt_len,
                        "response_len": f"lognormal(median {a.median:g}, sigma 1) clipped [16,{a.max_len}]",
-                       "micro_batch_tokens": a.mb_tokens, "parallelism": f"dp{world}" + (f"ep{ep}" if ep > 1 else ""), "colocated": True,
+                       "micro_batch_tokens": a.mb_tokens, "parallelism": (f"tp{tp}" if tp > 1 else "") + f"dp{dp}" + (f"ep{ep}" if ep > 1 else ""), "colocated": True,
                        "ref_logprobs": not a.no_ref, "ref_weights": "device" if ref_dev else "pinned host", "deterministic_attention_backward": a.deterministic, "kv_pool_gb": round(kv_gb, 1), "l2": "inputs larger than L2 (weights 16 GB + KV cache per step)"},
             "sync_s": round(sum(m["sync_s"] for m in step_metrics) / len(step_metrics), 4),
             "step_breakdown_s": {k: round(v, 3) for k, v in zip(phases, ph)},
