@@ -66,6 +66,8 @@ bool get_pdl();
 void set_weights_static(bool on);
 at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 int64_t skinny_tma_error();
+at::Tensor moe_combine(at::Tensor y, at::Tensor w, at::Tensor pos);
+std::vector<at::Tensor> moe_combine_bwd(at::Tensor y, at::Tensor w, at::Tensor pos, at::Tensor dout);
 std::vector<at::Tensor> router_topk(at::Tensor, int64_t, bool, c10::optional<at::Tensor>, c10::optional<at::Tensor>);
 void tp_ar_rms(at::Tensor, int64_t, int64_t, int64_t, c10::optional<at::Tensor>, at::Tensor, double, c10::optional<at::Tensor>, at::Tensor,
                at::Tensor, at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor);
@@ -120,6 +122,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_pdl", &ax::set_pdl);
   m.def("get_pdl", &ax::get_pdl);
   m.def("set_weights_static", &ax::set_weights_static);
+  m.def("moe_combine", &ax::moe_combine);
+  m.def("moe_combine_bwd", &ax::moe_combine_bwd);
   m.def("router_topk", &ax::router_topk);
   m.def("decode_plan", &ax::decode_plan);
   m.def("skinny_tma_linear", &ax::skinny_tma_linear);

@@ -115,4 +115,97 @@ std::vector<at::Tensor> router_topk(at::Tensor logits, int64_t k, bool renorm, c
   return {w, ids, probs};
 }
 
+// Weighted top-k combine of expert outputs: out[t] = sum_j w[t, j] * y[pos[t k + j]], summed in
+// fp32 and stored as bf16 (one gather per token instead of scattering every (token, expert) row
+// into an fp32 buffer with atomics).  One warp per token, 8 bf16 per lane per step, k <= 8.
+__global__ void moe_combine_fwd_k(const bf16* __restrict__ y, const float* __restrict__ w, const int* __restrict__ pos,
+                                  bf16* __restrict__ out, int T, int k, int H) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  int p[8];
+  float wt[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    p[j] = j < k ? pos[(long)t * k + j] : 0;
+    wt[j] = j < k ? w[(long)t * k + j] : 0.f;
+  }
+  for (int c = lane * 8; c < H; c += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= k) break;
+      float v[8];
+      load8(y + (long)p[j] * H + c, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += wt[j] * v[e];
+    }
+    store8(out + (long)t * H + c, acc);
+  }
+}
+
+// Its backward: dy[pos[t k + j]] = w[t, j] * dout[t] (bf16), dw[t, j] = <y[pos[t k + j]], dout[t]> (fp32).
+__global__ void moe_combine_bwd_k(const bf16* __restrict__ y, const float* __restrict__ w, const int* __restrict__ pos,
+                                  const bf16* __restrict__ dout, bf16* __restrict__ dy, float* __restrict__ dw, int T, int k, int H) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  int p[8];
+  float wt[8], dot[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    p[j] = j < k ? pos[(long)t * k + j] : 0;
+    wt[j] = j < k ? w[(long)t * k + j] : 0.f;
+    dot[j] = 0.f;
+  }
+  for (int c = lane * 8; c < H; c += 256) {
+    float g[8];
+    load8(dout + (long)t * H + c, g);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= k) break;
+      float v[8], d[8];
+      load8(y + (long)p[j] * H + c, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        dot[j] += v[e] * g[e];
+        d[e] = wt[j] * g[e];
+      }
+      store8(dy + (long)p[j] * H + c, d);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (j >= k) break;
+    const float s = warp_sum(dot[j]);
+    if (lane == 0) dw[(long)t * k + j] = s;
+  }
+}
+
+// y (R, H) bf16 rows, w (T, k) fp32, pos (T k) int32 row of y for each (token, slot) -> (T, H) bf16
+at::Tensor moe_combine(at::Tensor y, at::Tensor w, at::Tensor pos) {
+  AX_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous() && y.dim() == 2 && y.size(1) % 8 == 0, "y: (R, H) bf16, H % 8 == 0");
+  AX_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.dim() == 2 && w.size(1) <= 8, "w: (T, k <= 8) fp32");
+  AX_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous() && pos.numel() == w.numel(), "pos: (T k) int32");
+  const int T = w.size(0), k = w.size(1), H = y.size(1);
+  auto out = at::empty({T, H}, y.options());
+  if (T == 0) return out;
+  moe_combine_fwd_k<<<(T * 32 + 255) / 256, 256, 0, stream()>>>((const bf16*)y.data_ptr(), w.data_ptr<float>(), pos.data_ptr<int>(),
+                                                                (bf16*)out.data_ptr(), T, k, H);
+  AX_LAUNCH_OK();
+  return out;
+}
+
+std::vector<at::Tensor> moe_combine_bwd(at::Tensor y, at::Tensor w, at::Tensor pos, at::Tensor dout) {
+  AX_CHECK(dout.scalar_type() == at::kBFloat16 && dout.is_contiguous() && dout.size(0) == w.size(0) && dout.size(1) == y.size(1),
+           "dout: (T, H) bf16");
+  const int T = w.size(0), k = w.size(1), H = y.size(1);
+  auto dy = at::zeros_like(y);  // rows no token points at (dropped or padding) get zero gradient
+  auto dw = at::empty_like(w);
+  if (T == 0) return {dy, dw};
+  moe_combine_bwd_k<<<(T * 32 + 255) / 256, 256, 0, stream()>>>((const bf16*)y.data_ptr(), w.data_ptr<float>(), pos.data_ptr<int>(),
+                                                                (const bf16*)dout.data_ptr(), (bf16*)dy.data_ptr(), dw.data_ptr<float>(),
+                                                                T, k, H);
+  AX_LAUNCH_OK();
+  return {dy, dw};
+}
+
 }  // namespace ax

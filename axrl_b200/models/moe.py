@@ -20,7 +20,7 @@ import torch
 from torch import nn
 
 from axrl_b200.ops import core as ops
-from axrl_b200.ops.grouped import expert_offsets, grouped_swiglu_ffn
+from axrl_b200.ops.grouped import expert_offsets, grouped_swiglu_ffn, moe_combine
 
 
 @dataclass
@@ -194,6 +194,4 @@ class MoEBlock(nn.Module):
         offsets = expert_offsets(flat, self.E)
         xs = x.index_select(0, tok)
         ys = grouped_swiglu_ffn(xs, offsets, self.experts_gate_up, self.experts_down)
-        ys = ys.float() * w.reshape(-1)[order][:, None]
-        out = torch.zeros(T, H, dtype=torch.float32, device=x.device).index_add_(0, tok, ys)
-        return out.to(x.dtype)
+        return moe_combine(ys, w, order).to(x.dtype)

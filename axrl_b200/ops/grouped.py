@@ -65,3 +65,31 @@ def expert_offsets(expert_ids: torch.Tensor, num_experts: int) -> torch.Tensor:
 
 def grouped_swiglu_ffn(x_sorted: torch.Tensor, offsets: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
     return grouped_linear(ops.swiglu(grouped_linear(x_sorted, w_gate_up, offsets)), w_down, offsets)
+
+
+class _MoECombine(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, w, pos):  # noqa: ANN001, ANN205
+        ctx.save_for_backward(y, w, pos)
+        return _ext.ext().moe_combine(y, w, pos)
+
+    @staticmethod
+    def backward(ctx, g):  # noqa: ANN001, ANN205
+        y, w, pos = ctx.saved_tensors
+        dy, dw = _ext.ext().moe_combine_bwd(y, w, pos, g.contiguous())
+        return dy, dw, None
+
+
+def moe_combine(y_sorted: torch.Tensor, w: torch.Tensor, order: torch.Tensor) -> torch.Tensor:
+    """(T, H) = sum over each token's k slots of ``w[t, j]`` times its expert output row.
+
+    ``y_sorted`` row i is the output for flat slot ``order[i]`` (= t k + j), i.e. rows in the
+    expert-sorted order; the sum is taken in fp32."""
+    T, k = w.shape
+    if not y_sorted.is_cuda:
+        tok = order // k
+        ys = y_sorted.float() * w.reshape(-1)[order][:, None]
+        return torch.zeros(T, y_sorted.shape[1], dtype=torch.float32, device=y_sorted.device).index_add_(0, tok, ys).to(y_sorted.dtype)
+    pos = torch.empty_like(order, dtype=torch.int32)
+    pos[order] = torch.arange(order.numel(), device=order.device, dtype=torch.int32)
+    return _MoECombine.apply(y_sorted.contiguous(), w.float().contiguous(), pos)

@@ -12,7 +12,7 @@ Per MoE layer, with no host synchronisation:
 
 Backward mirrors it (combine^T = dispatch of the output gradients, dispatch^T = combine of the
 input gradients).  Receive buffers have a fixed capacity (``cap_factor`` x the average rows per
-rank); rows beyond it are dropped and reported by :meth:`P2PEPComm.check`.
+rank); a layer whose received rows would exceed it raises before any row moves.
 
 Reference counterpart: Megatron's NCCL all-to-all token dispatcher
 (``axrl/worker/megatron_worker.py:833``); :class:`axrl_b200.parallel.expert.TorchEPComm` is that
@@ -112,6 +112,11 @@ class P2PEPComm:
         assert n_send <= self.max_rows, "more (token, expert) rows than the EP send buffers hold"
         p = _Plan(C, self.E // self.size, n_send)
         e.ep_plan(C, self.rank, p.offsets, p.dst_start, p.blk_pos, p.blk_src, p.totals)
+        # rows this rank receives: one host read per layer, so the expert FFN and the copies out of
+        # the receive buffer cover the received rows only, not the whole capacity
+        p.n_recv = int(p.totals[0].item())
+        if p.n_recv > self.cap_recv:  # the expert FFN would read past the receive buffer
+            raise RuntimeError(f"EP receive capacity exceeded: {p.n_recv} rows for {self.cap_recv} (raise AXRL_EP_CAP_FACTOR)")
         return p
 
     def _transfer(self, mode: int, rows: torch.Tensor, p: _Plan, dst_ptrs: torch.Tensor, cap: int, ch: int) -> None:
@@ -122,13 +127,13 @@ class P2PEPComm:
         e.tp_wait(self.flags, ch, self._all(), ep, self.timeout_ns, self.status)
 
     def to_owners(self, rows: torch.Tensor, p: _Plan, which: str) -> torch.Tensor:
-        """Source-sorted rows (n_send, H) -> this rank's owner layout (cap_recv, H), a fresh tensor."""
+        """Source-sorted rows (n_send, H) -> this rank's owner layout (n_recv, H), a fresh tensor."""
         buf, ptrs, ch = (self.recv_a, self.recv_a_ptrs, CH_A_RECV) if which == "a" else (self.recv_b, self.recv_b_ptrs, CH_B_RECV)
         self._transfer(0, rows.contiguous(), p, ptrs, self.cap_recv, ch)
-        return buf.view(self.cap_recv, self.hidden).clone()
+        return buf[:p.n_recv * self.hidden].view(p.n_recv, self.hidden).clone()
 
     def to_sources(self, rows: torch.Tensor, p: _Plan, which: str) -> torch.Tensor:
-        """Owner-layout rows (cap_recv, H) -> this rank's source-sorted rows (n_send, H)."""
+        """Owner-layout rows (n_recv, H) -> this rank's source-sorted rows (n_send, H)."""
         buf, ptrs, ch = (self.back_a, self.back_a_ptrs, CH_A_BACK) if which == "a" else (self.back_b, self.back_b_ptrs, CH_B_BACK)
         self._transfer(1, rows.contiguous(), p, ptrs, self.max_rows, ch)
         return buf[:p.n_send * self.hidden].view(p.n_send, self.hidden).clone()
@@ -168,5 +173,6 @@ def p2p_moe_forward(block, x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, 
     xr = _Dispatch.apply(x.index_select(0, tok), comm, plan)
     y = grouped_swiglu_ffn(xr, plan.offsets, block.experts_gate_up, block.experts_down)
     yb = _Combine.apply(y, comm, plan)
-    ys = yb.float() * w.reshape(-1)[order][:, None]
-    return torch.zeros(T, H, dtype=torch.float32, device=x.device).index_add_(0, tok, ys).to(x.dtype)
+    from axrl_b200.ops.grouped import moe_combine
+
+    return moe_combine(yb, w, order).to(x.dtype)

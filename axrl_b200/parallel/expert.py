@@ -193,8 +193,9 @@ def ep_moe_forward(block, x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, e
     if ep.etp_size > 1:  # partial sums over the FFN columns -> this rank's rows
         y = _ETPReduceScatter.apply(y, counts, ep.etp_rank, ep.etp_group)
     yb = ep.comm.combine(y, handle) if handle is not None else y
-    ys = yb.float() * w.reshape(-1)[order][:, None]
-    return torch.zeros(T, H, dtype=torch.float32, device=x.device).index_add_(0, tok, ys).to(x.dtype)
+    from axrl_b200.ops.grouped import moe_combine
+
+    return moe_combine(yb, w, order).to(x.dtype)
 
 
 # ----------------------------------------------------------------------------- params

@@ -759,3 +759,27 @@ def test_split_key_attention_kernels_match_fp32():
     close(dq, qf.grad, 3e-2, 2e-2, msg="dq")
     close(torch.cat([g[0] for g in grads]), kf.grad, 3e-2, 2e-2, msg="dk")
     close(torch.cat([g[1] for g in grads]), vf.grad, 3e-2, 2e-2, msg="dv")
+
+
+@pytest.mark.parametrize("k", [1, 8])
+def test_moe_combine_matches_index_add(k):
+    """Weighted top-k combine of expert rows (one gather per token, fp32 sums) and its backward,
+    against the fp32 scatter with index_add and autograd."""
+    from axrl_b200.ops.grouped import moe_combine
+
+    torch.manual_seed(k)
+    T, H, E = 777, 2048, 64
+    ids = torch.stack([torch.randperm(E, device=DEV)[:k] for _ in range(T)])
+    flat = ids.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    y = torch.randn(T * k, H, device=DEV).bfloat16().requires_grad_(True)
+    w = torch.rand(T, k, device=DEV).requires_grad_(True)
+    out = moe_combine(y, w, order)
+    g = torch.randn(T, H, device=DEV).bfloat16()
+    out.backward(g)
+    yr, wr = y.detach().float().requires_grad_(True), w.detach().clone().requires_grad_(True)
+    ref = torch.zeros(T, H, device=DEV).index_add_(0, order // k, yr * wr.reshape(-1)[order][:, None])
+    ref.backward(g.float())
+    close(out, ref, 2e-2, 1e-2, msg="combine")
+    close(y.grad, yr.grad, 1e-2, 1e-2, msg="dy")
+    close(w.grad, wr.grad, 5e-2, 1e-3, msg="dw")
