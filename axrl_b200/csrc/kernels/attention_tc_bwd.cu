@@ -325,29 +325,32 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
 
 // ---------------------------------------------------------------------------------- 64-row q blocks
 // Second backward kernel, one CTA per (128-key tile, kv head) as above, reorganised so that loads,
-// element-wise work and the dQ read-out leave the tensor cores busy:
+// the element-wise work and the dQ read-out overlap the tensor-core products:
 //   * q rows come in blocks of 64 through a 3-stage ring (Q, dO: 16 KB each, plus the block's lse2
-//     and Dsum, loaded by the producer warp's lanes), so the next blocks load during this one;
-//   * S^T = K Q^T and dP^T = V dO^T are 128 x 64 (TMEM cols [0,64) and [64,128)); the element-wise
-//     warps write P^T and dS^T back into the first 32 columns of each as bf16 pairs, and dV += P^T dO,
-//     dK += dS^T Q take them as the A operand straight from tensor memory;
-//   * dQ^T = K^T dS^T (M = head dim, N = 64 q rows) goes to one of two 64-column TMEM buffers
-//     ([384,448), [448,512)) and is read out by four separate warps (TMEM lane = head dim, so each
-//     fp32 reduction instruction covers 128 consecutive bytes of the dQ accumulator) while the
-//     tensor cores already work on the next block; dS^T is also written to shared memory (two
-//     buffers) as the B operand of that product;
-//   * dV and dK accumulate in TMEM columns [128,256) and [256,384) over every block and head.
-// Warps 0-3 element-wise (TMEM lane = key), 4-7 dQ read-out and the final dK / dV store, 8 TMA,
-// 9 MMA issuer and TMEM owner.  Every mbarrier wait is bounded.
+//     and Dsum, loaded by the producer warp's lanes);
+//   * S^T = K Q^T and dP^T = V dO^T (128 x 64 each) go to one of two TMEM buffers ([0,128) or
+//     [128,256): S^T in the first 64 columns, dP^T in the next 64), so the products of block i + 1
+//     run while the element-wise warps work on block i;
+//   * the element-wise warps write P^T and dS^T back over the first 32 columns of S^T and dP^T as
+//     bf16 pairs, where dV += P^T dO and dK += dS^T Q (TMEM cols [256,384) and [384,512)) take them
+//     as the A operand; dS^T also goes to shared memory (two buffers) as the B operand of
+//     dQ^T = K^T dS^T (M = head dim, N = 64 q rows), which lands on the S^T columns of its buffer;
+//   * four separate warps read dQ^T out (TMEM lane = head dim, so each fp32 reduction instruction
+//     covers 128 consecutive bytes of the dQ accumulator) and store dK / dV at the end.
+// The tensor pipe executes one thread's products in issue order, which makes the reuse of TMEM
+// columns by a later product safe once the earlier one has been issued.
+// Warps 0-7 element-wise (warps w and w + 4 share TMEM lanes 32 (w % 4) = key rows and split the 64
+// q columns), 8-11 dQ read-out and the final dK / dV store, 12 TMA, 13 MMA issuer and TMEM owner.
+// Every mbarrier wait is bounded.
 namespace atb2 {
 using namespace tc;
-constexpr int BQ2 = 64, NST = 3, THREADS2 = 320;
+constexpr int BQ2 = 64, NST = 3, THREADS2 = 448;
 constexpr int QT = BQ2 * D * 2;  // 16 KB: 64 rows x 128 head dims (two 64-column boxes of 8 KB)
 constexpr int QHALF = QT / 2;
-constexpr int DST = 128 * BQ2 * 2;           // 16 KB: dS^T [128 keys][64 q], one 128-byte swizzled box
-constexpr uint32_t C2_S = 0, C2_DP = 64, C2_DV = 128, C2_DK = 256, C2_DQ = 384;
-constexpr int B2_KV = 0, B2_FULL = 1, B2_EMPTY = B2_FULL + NST, B2_S = B2_EMPTY + NST, B2_P = B2_S + 1, B2_DQF = B2_P + 1, B2_DQE = B2_DQF + 2,
-              B2_DONE = B2_DQE + 2, B2_DRAIN = B2_DONE + 1, NBAR2 = B2_DRAIN + 1;
+constexpr int DST = 128 * BQ2 * 2;  // 16 KB: dS^T [128 keys][64 q], one 128-byte swizzled box
+constexpr uint32_t C2_BUF = 128, C2_DP = 64, C2_DV = 256, C2_DK = 384;  // buffer b: S^T / dQ^T at 128 b, dP^T at 128 b + 64
+constexpr int B2_KV = 0, B2_FULL = 1, B2_EMPTY = B2_FULL + NST, B2_S = B2_EMPTY + NST, B2_P = B2_S + 2, B2_DQF = B2_P + 2,
+              B2_DQE = B2_DQF + 2, B2_DONE = B2_DQE + 2, B2_DRAIN = B2_DONE + 1, NBAR2 = B2_DRAIN + 1;
 }  // namespace atb2
 
 __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -377,9 +380,9 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
       mbar_init(&bar[B2_FULL + s], 1);
       mbar_init(&bar[B2_EMPTY + s], 1);
     }
-    mbar_init(&bar[B2_S], 1);
-    mbar_init(&bar[B2_P], 4);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar[B2_S + b], 1);
+      mbar_init(&bar[B2_P + b], 8);
       mbar_init(&bar[B2_DQF + b], 1);
       mbar_init(&bar[B2_DQE + b], 4);
     }
@@ -388,7 +391,7 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 9) {
+  if (warp == 13) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)), "r"(TMEM_COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -399,10 +402,10 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
 
   QTiles qt{p.qr, it0, it1, G, ks, k0s, 0, it0, 0, 0, 0, 0, BQ2};
   qt.seek();
-  auto q_at = [&](int s) { return sSt + s * 2 * QT; };       // Q of stage s (dO at + QT)
-  auto ld_at = [&](int s) { return sLD + s * 2 * BQ2; };     // lse2 of stage s (Dsum at + BQ2)
+  auto q_at = [&](int s) { return sSt + s * 2 * QT; };    // Q of stage s (dO at + QT)
+  auto ld_at = [&](int s) { return sLD + s * 2 * BQ2; };  // lse2 of stage s (Dsum at + BQ2)
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ------------------------------------------------------------ producer: K/V once, then (Q, dO, lse2, Dsum) per block
     if (lane == 0) {
       mbar_expect_tx(&bar[B2_KV], 2 * TILE);
@@ -438,41 +441,49 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
       mbar_wait(&bar[B2_KV], 0, (volatile int*)&zero, p.err, 61);
       for (int j = max(0, i - NST); j < i; ++j) mbar_wait(&bar[B2_FULL + j % NST], (j / NST) & 1, (volatile int*)&zero, p.err, 61);
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t ID_S = idesc_bf16(BQ2, false);               // A = K / V, B = Q / dO, both K-major, N = 64
-      constexpr uint32_t ID_G = idesc_bf16(D, true);                  // A from TMEM, B = dO / Q MN-major, N = 128
-      constexpr uint32_t ID_Q = idesc_bf16(BQ2, true, true);          // A = K^T and B = dS^T, both MN-major, N = 64
+      constexpr uint32_t ID_S = idesc_bf16(BQ2, false);       // A = K / V, B = Q / dO, both K-major, N = 64
+      constexpr uint32_t ID_G = idesc_bf16(D, true);          // A from TMEM, B = dO / Q MN-major, N = 128
+      constexpr uint32_t ID_Q = idesc_bf16(BQ2, true, true);  // A = K^T and B = dS^T, both MN-major, N = 64
       const uint32_t k_b = s32(sK), v_b = s32(sV), ds_b = s32(sDS);
-      bool ok = mbar_wait(&bar[B2_KV], 0, abort, p.err, 62);
-      int i = 0;
-      for (; ok && qt.valid(); qt.next(), ++i) {
-        const int s = i % NST;
-        const uint32_t q_b = s32(q_at(s)), do_b = q_b + QT;
-        if (!(ok = mbar_wait(&bar[B2_FULL + s], (i / NST) & 1, abort, p.err, 63))) break;
+      // S^T / dP^T of block j into buffer j & 1, once its Q / dO landed and dQ^T of block j - 2
+      // (same columns) has been read out
+      auto sp = [&](int j) -> bool {
+        const int s = j % NST, b = j & 1;
+        if (!mbar_wait(&bar[B2_FULL + s], (j / NST) & 1, abort, p.err, 63)) return false;
+        if (j >= 2 && !mbar_wait(&bar[B2_DQE + b], ((j - 2) >> 1) & 1, abort, p.err, 65)) return false;
         tc_fence_after();
+        const uint32_t q_b = s32(q_at(s)), do_b = q_b + QT, cs = tmem + b * C2_BUF;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {  // S^T = K Q^T, dP^T = V dO^T (K = head dim)
+        for (int kk = 0; kk < D / 16; ++kk) {  // K = head dim
           const uint32_t ak = (kk >> 2) * HALF + (kk & 3) * 32, bk = (kk >> 2) * QHALF + (kk & 3) * 32;
-          tc_mma(tmem + C2_S, sdesc(k_b + ak, 16, 1024), sdesc(q_b + bk, 16, 1024), ID_S, kk > 0);
-          tc_mma(tmem + C2_DP, sdesc(v_b + ak, 16, 1024), sdesc(do_b + bk, 16, 1024), ID_S, kk > 0);
+          tc_mma(cs, sdesc(k_b + ak, 16, 1024), sdesc(q_b + bk, 16, 1024), ID_S, kk > 0);
+          tc_mma(cs + C2_DP, sdesc(v_b + ak, 16, 1024), sdesc(do_b + bk, 16, 1024), ID_S, kk > 0);
         }
-        tc_commit(&bar[B2_S]);
-        if (!(ok = mbar_wait(&bar[B2_P], i & 1, abort, p.err, 64))) break;
+        tc_commit(&bar[B2_S + b]);
+        return true;
+      };
+      bool ok = mbar_wait(&bar[B2_KV], 0, abort, p.err, 62);
+      int n = 0;  // blocks of this CTA
+      for (QTiles c = qt; c.valid(); c.next()) ++n;
+      if (ok && n > 0) ok = sp(0);
+      for (int i = 0; ok && i < n; ++i) {
+        const int s = i % NST, b = i & 1;
+        if (i + 1 < n && !(ok = sp(i + 1))) break;
+        if (!(ok = mbar_wait(&bar[B2_P + b], (i >> 1) & 1, abort, p.err, 64))) break;
         tc_fence_after();
+        const uint32_t q_b = s32(q_at(s)), do_b = q_b + QT, cs = tmem + b * C2_BUF;
 #pragma unroll
         for (int kk = 0; kk < BQ2 / 16; ++kk) {  // dV += P^T dO, dK += dS^T Q (K = q rows; P^T, dS^T from TMEM)
-          tc_mma_ts(tmem + C2_DV, tmem + C2_S + kk * 8, sdesc(do_b + kk * 2048, QHALF, 1024), ID_G, (i > 0 || kk > 0));
-          tc_mma_ts(tmem + C2_DK, tmem + C2_DP + kk * 8, sdesc(q_b + kk * 2048, QHALF, 1024), ID_G, (i > 0 || kk > 0));
+          tc_mma_ts(tmem + C2_DV, cs + kk * 8, sdesc(do_b + kk * 2048, QHALF, 1024), ID_G, (i > 0 || kk > 0));
+          tc_mma_ts(tmem + C2_DK, cs + C2_DP + kk * 8, sdesc(q_b + kk * 2048, QHALF, 1024), ID_G, (i > 0 || kk > 0));
         }
         tc_commit(&bar[B2_EMPTY + s]);
-        const int b = i & 1;
-        if (i >= 2 && !(ok = mbar_wait(&bar[B2_DQE + b], ((i - 2) >> 1) & 1, abort, p.err, 65))) break;
-        tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)  // dQ^T = K^T dS^T (K = keys)
-          tc_mma(tmem + C2_DQ + b * BQ2, sdesc(k_b + kk * 2048, HALF, 1024), sdesc(ds_b + b * DST + kk * 2048, DST, 1024), ID_Q, kk > 0);
+        for (int kk = 0; kk < BK / 16; ++kk)  // dQ^T = K^T dS^T (K = keys), over S^T of this buffer
+          tc_mma(cs, sdesc(k_b + kk * 2048, HALF, 1024), sdesc(ds_b + b * DST + kk * 2048, DST, 1024), ID_Q, kk > 0);
         tc_commit(&bar[B2_DQF + b]);
       }
       if (ok) tc_commit(&bar[B2_DONE]);
@@ -480,18 +491,20 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
       int zero = 0;
       mbar_wait(&bar[B2_DRAIN], 0, (volatile int*)&zero, p.err, 66);
     }
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ element-wise gradient (TMEM lane = key)
-    const int r = warp * 32 + lane;
+    const int wq = warp & 3, half = warp >> 2;
+    const int r = wq * 32 + lane;
     const int key = ks + r;
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_addr = tmem + ((uint32_t)(wq * 32) << 16);
+    const int c0 = half * 32;  // this warp's q columns
     int i = 0;
     for (; qt.valid(); qt.next(), ++i) {
       const int s = i % NST, b = i & 1;
       const int qs = qt.qs, qe = min(qs + BQ2, qt.q1);
       const int climit = key < ke ? qe - qs : 0;
       const int cfirst = qt.ty == 1 ? max(0, (key - k0s) - (qs - qt.q0)) : 0;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar[B2_S], i & 1, abort, p.err, 67))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar[B2_S + b], (i >> 1) & 1, abort, p.err, 67))) break;
       // the stage's lse2 / Dsum were stored by the producer's lanes before its arrival on FULL
       if (!__all_sync(0xffffffffu, mbar_wait(&bar[B2_FULL + s], (i / NST) & 1, abort, p.err, 67))) break;
       // dS^T buffer b is free once dQ of block i - 2 has been computed
@@ -499,46 +512,43 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
       tc_fence_after();
       const float* L = ld_at(s);
       const float* Ds = L + BQ2;
+      const uint32_t cs = lane_addr + b * C2_BUF;
       char* dsrow = sDS + b * DST + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        const int c0 = hh * 32;
-        float sv[32], dp[32];
-        tmem_ld32(lane_addr + C2_S + c0, sv);
-        tmem_ld32(lane_addr + C2_DP + c0, dp);
-        uint32_t pw[16], dw[16];
+      float sv[32], dp[32];
+      tmem_ld32(cs + c0, sv);
+      tmem_ld32(cs + C2_DP + c0, dp);
+      uint32_t pw[16], dw[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pv[2], dv2[2];
+      for (int e = 0; e < 32; e += 2) {
+        float pv[2], dv2[2];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int c = c0 + e + u;
-            const bool vis = c >= cfirst && c < climit;
-            const float pr = vis ? exp2f(sv[e + u] * p.scale_log2 - L[c]) : 0.f;
-            pv[u] = pr;
-            dv2[u] = vis ? pr * (dp[e + u] - Ds[c]) * p.scale : 0.f;
-          }
-          bf162 a = __floats2bfloat162_rn(pv[0], pv[1]), d2 = __floats2bfloat162_rn(dv2[0], dv2[1]);
-          pw[e / 2] = *reinterpret_cast<uint32_t*>(&a);
-          dw[e / 2] = *reinterpret_cast<uint32_t*>(&d2);
+        for (int u = 0; u < 2; ++u) {
+          const int c = c0 + e + u;
+          const bool vis = c >= cfirst && c < climit;
+          const float pr = vis ? exp2f(sv[e + u] * p.scale_log2 - L[c]) : 0.f;
+          pv[u] = pr;
+          dv2[u] = vis ? pr * (dp[e + u] - Ds[c]) * p.scale : 0.f;
         }
-        tmem_st16u(lane_addr + C2_S + hh * 16, pw);   // P^T (bf16 pairs) over the consumed S^T columns
-        tmem_st16u(lane_addr + C2_DP + hh * 16, dw);  // dS^T over dP^T
+        bf162 a2 = __floats2bfloat162_rn(pv[0], pv[1]), d2 = __floats2bfloat162_rn(dv2[0], dv2[1]);
+        pw[e / 2] = *reinterpret_cast<uint32_t*>(&a2);
+        dw[e / 2] = *reinterpret_cast<uint32_t*>(&d2);
+      }
+      tmem_st16u(cs + half * 16, pw);          // P^T (bf16 pairs) over the consumed S^T columns
+      tmem_st16u(cs + C2_DP + half * 16, dw);  // dS^T over dP^T
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {  // dS^T row r, q columns c0 + 8 q8 .. +7: 16-byte chunk (hh*4 + q8) of the 128-byte row
-          const int ch = hh * 4 + q8;
-          *reinterpret_cast<uint4*>(dsrow + ((ch ^ (r & 7)) << 4)) = make_uint4(dw[q8 * 4], dw[q8 * 4 + 1], dw[q8 * 4 + 2], dw[q8 * 4 + 3]);
-        }
+      for (int q8 = 0; q8 < 4; ++q8) {  // dS^T row r, q columns c0 + 8 q8 .. +7: 16-byte chunk (half*4 + q8) of the 128-byte row
+        const int ch = half * 4 + q8;
+        *reinterpret_cast<uint4*>(dsrow + ((ch ^ (r & 7)) << 4)) = make_uint4(dw[q8 * 4], dw[q8 * 4 + 1], dw[q8 * 4 + 2], dw[q8 * 4 + 3]);
       }
       tmem_st_wait();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // dS^T visible to the tensor cores
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B2_P]);
+      if (lane == 0) mbar_arrive(&bar[B2_P + b]);
     }
   } else {
     // ------------------------------------------------------------ dQ read-out (TMEM lane = head dim), then dK / dV
-    const int wq = warp - 4;
+    const int wq = warp - 8;
     const int d = wq * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(wq * 32) << 16);
     int i = 0;
@@ -553,7 +563,7 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
         float v[32];
-        tmem_ld32(lane_addr + C2_DQ + b * BQ2 + hh * 32, v);
+        tmem_ld32(lane_addr + b * C2_BUF + hh * 32, v);
 #pragma unroll
         for (int c = 0; c < 32; ++c)
           if (hh * 32 + c < n) red_add_f32(dq + (hh * 32 + c) * rstride, v[c]);
@@ -592,7 +602,7 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
     tc_fence_before();
   }
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
