@@ -85,7 +85,7 @@ at::Tensor grpo_pg_bwd(at::Tensor, at::Tensor);
 std::vector<at::Tensor> quant_fp8_rows(at::Tensor x);
 at::Tensor fp8_block_linear(at::Tensor xq, at::Tensor xs, at::Tensor wq, at::Tensor ws);
 void ep_transfer(int64_t, at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
-                 at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, int64_t);
+                 at::Tensor, at::Tensor, int64_t, int64_t, at::Tensor, int64_t, at::Tensor, int64_t, c10::optional<at::Tensor>);
 void tp_reduce_slots(at::Tensor, int64_t, int64_t, c10::optional<at::Tensor>, at::Tensor);
 at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant);
 at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
@@ -141,7 +141,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grpo_pg_bwd", &ax::grpo_pg_bwd);
   m.def("quant_fp8_rows", &ax::quant_fp8_rows);
   m.def("fp8_block_linear", &ax::fp8_block_linear);
-  m.def("ep_transfer", &ax::ep_transfer);
+  m.def("ep_transfer", &ax::ep_transfer, py::arg("mode"), py::arg("rows"), py::arg("C"), py::arg("self"), py::arg("dst_start"),
+        py::arg("offsets"), py::arg("blk_pos"), py::arg("blk_src"), py::arg("totals"), py::arg("dst_ptrs"), py::arg("dst_cap_rows"),
+        py::arg("flag_ptrs"), py::arg("my_flags"), py::arg("ch"), py::arg("epoch"), py::arg("ticket"), py::arg("timeout_ns"),
+        py::arg("status"), py::arg("ctas"), py::arg("src_idx") = py::none());
   m.def("tp_reduce_slots", &ax::tp_reduce_slots);
   m.def("linear_dgrad", &ax::linear_dgrad);
   m.def("linear_wgrad", &ax::linear_wgrad);

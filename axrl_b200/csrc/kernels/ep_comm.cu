@@ -89,9 +89,11 @@ __global__ void ep_plan_k(const int* __restrict__ C, int P, int E, int self, int
   totals[1] = sent;
 }
 
-// mode 0: rows of this rank's sorted order (n = totals[1]) -> owners' buffers.
+// mode 0: rows of this rank's sorted order (n = totals[1]) -> owners' buffers; with `src_idx`, sorted
+//         row r is row src_idx[r] of `rows` (the token rows, gathered on the fly).
 // mode 1: rows of this rank's receive buffer (n = totals[0]) -> sources' buffers.
-__global__ void ep_transfer_k(int mode, const uint4* __restrict__ rows, int row16, const int* __restrict__ C, int P, int E, int self,
+__global__ void ep_transfer_k(int mode, const uint4* __restrict__ rows, const int64_t* __restrict__ src_idx, int row16,
+                              const int* __restrict__ C, int P, int E, int self,
                               const int* __restrict__ dst_start, const int* __restrict__ offsets, const int* __restrict__ blk_pos,
                               const int* __restrict__ blk_src, const int* __restrict__ totals, Peers dst, long dst_cap_rows, Peers flags,
                               const int* __restrict__ my_flags, int ch, int epoch, unsigned* ticket, uint64_t timeout_ns,
@@ -145,7 +147,7 @@ __global__ void ep_transfer_k(int mode, const uint4* __restrict__ rows, int row1
         if (lane == 0) atomicCAS(status, 0, 3);
         continue;
       }
-      const uint4* src = rows + r * row16;
+      const uint4* src = rows + (src_idx != nullptr ? src_idx[r] : r) * row16;
       uint4* out = reinterpret_cast<uint4*>(dst.p[peer]) + at * row16;
       for (int i = lane; i < row16; i += 32) out[i] = src[i];
     }
@@ -185,13 +187,19 @@ void ep_plan(at::Tensor C, int64_t self, at::Tensor offsets, at::Tensor dst_star
 
 void ep_transfer(int64_t mode, at::Tensor rows, at::Tensor C, int64_t self, at::Tensor dst_start, at::Tensor offsets, at::Tensor blk_pos,
                  at::Tensor blk_src, at::Tensor totals, at::Tensor dst_ptrs, int64_t dst_cap_rows, at::Tensor flag_ptrs,
-                 at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ticket, int64_t timeout_ns, at::Tensor status, int64_t ctas) {
+                 at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ticket, int64_t timeout_ns, at::Tensor status, int64_t ctas,
+                 c10::optional<at::Tensor> src_idx) {
   AX_CHECK(rows.is_cuda() && rows.is_contiguous() && rows.dim() == 2, "rows");
+  const int64_t* idx = nullptr;
+  if (src_idx.has_value()) {
+    AX_CHECK(mode == 0 && src_idx->is_cuda() && src_idx->scalar_type() == at::kLong && src_idx->is_contiguous(), "src_idx: int64 (mode 0)");
+    idx = src_idx->data_ptr<int64_t>();
+  }
   long row_bytes = rows.size(1) * rows.element_size();
   AX_CHECK(row_bytes % 16 == 0, "row bytes must be a multiple of 16");
   int P = C.size(0), E = C.size(1);
   epc::ep_transfer_k<<<(int)ctas, 256, 0, stream()>>>(
-      (int)mode, reinterpret_cast<const uint4*>(rows.data_ptr()), (int)(row_bytes / 16), C.data_ptr<int>(), P, E, (int)self,
+      (int)mode, reinterpret_cast<const uint4*>(rows.data_ptr()), idx, (int)(row_bytes / 16), C.data_ptr<int>(), P, E, (int)self,
       dst_start.data_ptr<int>(), offsets.data_ptr<int>(), blk_pos.data_ptr<int>(), blk_src.data_ptr<int>(), totals.data_ptr<int>(),
       epc::to_peers(dst_ptrs), (long)dst_cap_rows, epc::to_peers(flag_ptrs), my_flags.data_ptr<int>(), (int)ch, (int)epoch,
       reinterpret_cast<unsigned*>(ticket.data_ptr<int>()) + ch, (uint64_t)timeout_ns, status.data_ptr<int>());

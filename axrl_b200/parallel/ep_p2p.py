@@ -119,17 +119,20 @@ class P2PEPComm:
             raise RuntimeError(f"EP receive capacity exceeded: {p.n_recv} rows for {self.cap_recv} (raise AXRL_EP_CAP_FACTOR)")
         return p
 
-    def _transfer(self, mode: int, rows: torch.Tensor, p: _Plan, dst_ptrs: torch.Tensor, cap: int, ch: int) -> None:
+    def _transfer(self, mode: int, rows: torch.Tensor, p: _Plan, dst_ptrs: torch.Tensor, cap: int, ch: int,
+                  src_idx: torch.Tensor | None = None) -> None:
         e = _ext.ext()
         ep = self._next()
         e.ep_transfer(mode, rows, p.C, self.rank, p.dst_start, p.offsets, p.blk_pos, p.blk_src, p.totals, dst_ptrs, cap,
-                      self.flag_ptrs, self.flags, ch, ep, self.ticket, self.timeout_ns, self.status, self.ctas)
+                      self.flag_ptrs, self.flags, ch, ep, self.ticket, self.timeout_ns, self.status, self.ctas, src_idx)
         e.tp_wait(self.flags, ch, self._all(), ep, self.timeout_ns, self.status)
 
-    def to_owners(self, rows: torch.Tensor, p: _Plan, which: str) -> torch.Tensor:
-        """Source-sorted rows (n_send, H) -> this rank's owner layout (n_recv, H), a fresh tensor."""
+    def to_owners(self, rows: torch.Tensor, p: _Plan, which: str, src_idx: torch.Tensor | None = None) -> torch.Tensor:
+        """Source-sorted rows (n_send, H) -> this rank's owner layout (n_recv, H), a fresh tensor.  With
+        ``src_idx``, ``rows`` are token rows and sorted row r is ``rows[src_idx[r]]`` (gathered in the
+        transfer kernel)."""
         buf, ptrs, ch = (self.recv_a, self.recv_a_ptrs, CH_A_RECV) if which == "a" else (self.recv_b, self.recv_b_ptrs, CH_B_RECV)
-        self._transfer(0, rows.contiguous(), p, ptrs, self.cap_recv, ch)
+        self._transfer(0, rows.contiguous(), p, ptrs, self.cap_recv, ch, src_idx)
         return buf[:p.n_recv * self.hidden].view(p.n_recv, self.hidden).clone()
 
     def to_sources(self, rows: torch.Tensor, p: _Plan, which: str) -> torch.Tensor:
@@ -150,6 +153,28 @@ class _Dispatch(torch.autograd.Function):
         return ctx.comm.to_sources(g, ctx.plan, "b"), None, None
 
 
+class _DispatchTokens(torch.autograd.Function):
+    """Dispatch of token rows ``x`` (T, H) in the expert-sorted order ``order`` (flat slot t k + j),
+    gathered inside the transfer kernel; the backward brings the row gradients back to the sources
+    and sums each token's k slots."""
+
+    @staticmethod
+    def forward(ctx, x, order, k, comm, plan):  # noqa: ANN001, ANN205
+        ctx.comm, ctx.plan, ctx.k = comm, plan, k
+        ctx.save_for_backward(order)
+        ctx.T = x.shape[0]
+        return comm.to_owners(x, plan, "a", src_idx=(order // k).contiguous())
+
+    @staticmethod
+    def backward(ctx, g):  # noqa: ANN001, ANN205
+        from axrl_b200.ops.grouped import moe_combine
+
+        (order,) = ctx.saved_tensors
+        g_sorted = ctx.comm.to_sources(g, ctx.plan, "b")
+        ones = torch.ones(ctx.T, ctx.k, dtype=torch.float32, device=g.device)
+        return moe_combine(g_sorted, ones, order), None, None, None, None
+
+
 class _Combine(torch.autograd.Function):
     @staticmethod
     def forward(ctx, y_owner, comm, plan):  # noqa: ANN001, ANN205
@@ -168,9 +193,8 @@ def p2p_moe_forward(block, x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, 
     k = ids.shape[1]
     flat = ids.reshape(-1)
     order = torch.argsort(flat, stable=True)
-    tok = order // k
     plan = comm.plan(flat[order])
-    xr = _Dispatch.apply(x.index_select(0, tok), comm, plan)
+    xr = _DispatchTokens.apply(x, order, k, comm, plan)
     y = grouped_swiglu_ffn(xr, plan.offsets, block.experts_gate_up, block.experts_down)
     yb = _Combine.apply(y, comm, plan)
     from axrl_b200.ops.grouped import moe_combine
