@@ -104,8 +104,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_tc_k(const __grid_constan
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int seg = p.tiles[blockIdx.x * 2], qs = p.tiles[blockIdx.x * 2 + 1];
-  const int h = blockIdx.y, hk = h / (p.Hq / p.Hkv);
+  const int seg = p.tiles[blockIdx.y * 2], qs = p.tiles[blockIdx.y * 2 + 1];
+  const int h = blockIdx.x, hk = h / (p.Hq / p.Hkv);
   const int q0 = p.qseg[seg * 4], q1 = p.qseg[seg * 4 + 1], r_first = p.qseg[seg * 4 + 2], r_last = p.qseg[seg * 4 + 3];
   const int qe = min(qs + BM, q1);
 
@@ -377,8 +377,8 @@ __global__ void __launch_bounds__(THREADS8, 1) attn_fwd_tc8_k(const __grid_const
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int seg = p.tiles[blockIdx.x * 2], qs = p.tiles[blockIdx.x * 2 + 1];
-  const int h = blockIdx.y, hk = h / (p.Hq / p.Hkv);
+  const int seg = p.tiles[blockIdx.y * 2], qs = p.tiles[blockIdx.y * 2 + 1];
+  const int h = blockIdx.x, hk = h / (p.Hq / p.Hkv);
   const int q0 = p.qseg[seg * 4], q1 = p.qseg[seg * 4 + 1], r_first = p.qseg[seg * 4 + 2], r_last = p.qseg[seg * 4 + 3];
   const int qe = min(qs + BM, q1);
 
@@ -651,8 +651,8 @@ __global__ void __launch_bounds__(THREADS_P, 1) attn_fwd_tcp_k(const __grid_cons
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int seg = p.tiles[blockIdx.x * 2], qs = p.tiles[blockIdx.x * 2 + 1];
-  const int hA = blockIdx.y * 2, hk = hA / (p.Hq / p.Hkv);
+  const int seg = p.tiles[blockIdx.y * 2], qs = p.tiles[blockIdx.y * 2 + 1];
+  const int hA = blockIdx.x * 2, hk = hA / (p.Hq / p.Hkv);
   const int q0 = p.qseg[seg * 4], q1 = p.qseg[seg * 4 + 1], r_first = p.qseg[seg * 4 + 2], r_last = p.qseg[seg * 4 + 3];
   const int qe = min(qs + BM, q1);
 
@@ -920,6 +920,9 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
   auto o = at::zeros_like(q);
   auto lse2 = at::full({Hq, T}, INFINITY, q.options().dtype(at::kFloat));
   const int nt = tiles.size(0);
+  // grid (heads, tiles): blocks start in index order, so the heaviest tiles (first in the table) of
+  // every head start first
+  AX_CHECK(nt <= 65535, "attention: at most 65535 tiles per launch");
   if (nt == 0 || T == 0 || Tk == 0) return {o, lse2};
   AX_CHECK(qseg.is_cuda() && kr.is_cuda() && tiles.is_cuda(), "attention tables on the device");
   const CUtensorMap tq = map_rows(q.data_ptr(), T, (long)Hq * D);
@@ -930,7 +933,7 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
   if (variant == 4 && (Hq / Hkv) % 2 == 0) {
     const int smemp = (2 + NSLOT) * TILE + NBARP * 8 + 16 + 1024;
     smem_attr(reinterpret_cast<const void*>(attn_fwd_tcp_k), smemp);
-    attn_fwd_tcp_k<<<dim3(nt, Hq / 2), THREADS_P, smemp, stream()>>>(tq, tk, tv, p);
+    attn_fwd_tcp_k<<<dim3(Hq / 2, nt), THREADS_P, smemp, stream()>>>(tq, tk, tv, p);
     AX_LAUNCH_OK();
     return {o, lse2};
   }
@@ -939,15 +942,15 @@ std::vector<at::Tensor> attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at
     const int smem8 = 6 * TILE + 3 * 2 * BM * 4 + NBAR8 * 8 + 16 + 1024;
     auto* kern = variant == 3 ? attn_fwd_tc8_k<true> : attn_fwd_tc8_k<false>;
     smem_attr(reinterpret_cast<const void*>(kern), smem8);
-    kern<<<dim3(nt, Hq), THREADS8, smem8, stream()>>>(tq, tk, tv, p);
+    kern<<<dim3(Hq, nt), THREADS8, smem8, stream()>>>(tq, tk, tv, p);
     AX_LAUNCH_OK();
     return {o, lse2};
   }
   const bool dbl = variant == 1;
   const int smem = (dbl ? 7 : 6) * TILE + NBAR * 8 + 16 + 1024;
   smem_attr(dbl ? reinterpret_cast<const void*>(attn_fwd_tc_k<true>) : reinterpret_cast<const void*>(attn_fwd_tc_k<false>), smem);
-  if (dbl) attn_fwd_tc_k<true><<<dim3(nt, Hq), THREADS, smem, stream()>>>(tq, tk, tv, p);
-  else attn_fwd_tc_k<false><<<dim3(nt, Hq), THREADS, smem, stream()>>>(tq, tk, tv, p);
+  if (dbl) attn_fwd_tc_k<true><<<dim3(Hq, nt), THREADS, smem, stream()>>>(tq, tk, tv, p);
+  else attn_fwd_tc_k<false><<<dim3(Hq, nt), THREADS, smem, stream()>>>(tq, tk, tv, p);
   AX_LAUNCH_OK();
   return {o, lse2};
 }

@@ -118,8 +118,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int seg = p.tiles[blockIdx.x * 2], ks = p.tiles[blockIdx.x * 2 + 1];
-  const int hk = blockIdx.y, G = p.Hq / p.Hkv;
+  const int seg = p.tiles[blockIdx.y * 2], ks = p.tiles[blockIdx.y * 2 + 1];
+  const int hk = blockIdx.x, G = p.Hq / p.Hkv;
   const int k0s = p.kseg[seg * 4], k1s = p.kseg[seg * 4 + 1], it0 = p.kseg[seg * 4 + 2], it1 = p.kseg[seg * 4 + 3];
   const int ke = min(ks + BK, k1s);
 
@@ -369,8 +369,8 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int seg = p.tiles[blockIdx.x * 2], ks = p.tiles[blockIdx.x * 2 + 1];
-  const int hk = blockIdx.y, G = p.Hq / p.Hkv;
+  const int seg = p.tiles[blockIdx.y * 2], ks = p.tiles[blockIdx.y * 2 + 1];
+  const int hk = blockIdx.x, G = p.Hq / p.Hkv;
   const int k0s = p.kseg[seg * 4], k1s = p.kseg[seg * 4 + 1], it0 = p.kseg[seg * 4 + 2], it1 = p.kseg[seg * 4 + 3];
   const int ke = min(ks + BK, k1s);
 
@@ -663,6 +663,9 @@ void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v
   using namespace atb;
   const int T = q.size(0), Hq = q.size(1), Tk = k.size(0), Hkv = k.size(1);
   const int nt = tiles.size(0);
+  // grid (heads, tiles): blocks start in index order, so the heaviest tiles (first in the table) of
+  // every head start first
+  AX_CHECK(nt <= 65535, "attention: at most 65535 tiles per launch");
   if (nt == 0 || T == 0 || Tk == 0) return;
   AX_CHECK(q.size(2) == D && k.size(2) == D && dout.sizes() == q.sizes() && k.sizes() == v.sizes(), "attention backward shapes");
   const CUtensorMap tq = map_rows(q.data_ptr(), T, (long)Hq * D);
@@ -678,13 +681,13 @@ void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v
     const CUtensorMap tdo64 = map_rows(dout.data_ptr(), T, (long)Hq * D, BQ2);
     const int smem2 = 2 * TILE + NST * 2 * QT + 2 * DST + NST * 2 * BQ2 * 4 + NBAR2 * 8 + 16 + 1024;
     smem_attr(reinterpret_cast<const void*>(attn_bwd_tc2_k), smem2);
-    attn_bwd_tc2_k<<<dim3(nt, Hkv), THREADS2, smem2, stream()>>>(tq64, tk, tv, tdo64, p);
+    attn_bwd_tc2_k<<<dim3(Hkv, nt), THREADS2, smem2, stream()>>>(tq64, tk, tv, tdo64, p);
     AX_LAUNCH_OK();
     return;
   }
   const int smem = 6 * TILE + 4 * BQ * 4 + NBAR * 8 + 16 + 1024;
   smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_k), smem);
-  attn_bwd_tc_k<<<dim3(nt, Hkv), THREADS, smem, stream()>>>(tq, tk, tv, tdo, p);
+  attn_bwd_tc_k<<<dim3(Hkv, nt), THREADS, smem, stream()>>>(tq, tk, tv, tdo, p);
   AX_LAUNCH_OK();
 }
 
