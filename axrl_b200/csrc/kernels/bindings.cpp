@@ -42,7 +42,8 @@ int64_t attn_bwd_tc_error();
 void set_attn_bwd_tc(bool on);
 void set_attn_bwd_blocks64(bool on);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
-                       double, c10::optional<at::Tensor>);
+                       double, c10::optional<at::Tensor>,
+                       c10::optional<at::Tensor>);
 void decode_plan(at::Tensor seq_lens, at::Tensor prefix);
 void set_decode_attn_tma(bool on);
 void kv_store(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor);
@@ -170,7 +171,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_attn_bwd_tc", &ax::set_attn_bwd_tc);
   m.def("set_attn_bwd_blocks64", &ax::set_attn_bwd_blocks64);
   m.def("set_decode_attn_tma", &ax::set_decode_attn_tma);
-  m.def("paged_decode_attn", &ax::paged_decode_attn);
+  m.def("paged_decode_attn", &ax::paged_decode_attn, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("block_table"),
+        py::arg("seq_lens"), py::arg("out"), py::arg("part_o"), py::arg("part_ml"), py::arg("splits"), py::arg("scale"),
+        py::arg("prefix") = py::none(), py::arg("chunk_cnt") = py::none());
   m.def("kv_store", &ax::kv_store);
   m.def("sqnorm_accumulate", &ax::sqnorm_accumulate);
   m.def("adamw_step", &ax::adamw_step);

@@ -379,7 +379,8 @@ void decode_plan(at::Tensor seq_lens, at::Tensor prefix) {
 }
 
 void paged_decode_attn_tma_partials(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table, at::Tensor seq_lens,
-                                    at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, at::Tensor prefix, int max_len);
+                                    at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, at::Tensor prefix, int max_len,
+                                    bf16* out, int* cnt);
 
 // Planned launches with 64-token pages run the TMA page-pipeline kernel (decode_attn_tma.cu):
 // Qwen3-8B decode at 2048-token contexts on B200, 8.75 ms per step at batch 64 and 4.72 ms at
@@ -395,8 +396,11 @@ static int& decode_tma_flag() {
 static bool decode_tma_enabled() { return decode_tma_flag() != 0; }
 void set_decode_attn_tma(bool on) { decode_tma_flag() = on ? 1 : 0; }
 
+// chunk_cnt: optional zeroed int32 buffer of >= B * Hkv (sequence, kv head) counters; with it the
+// TMA kernel merges its chunks itself (no combine launch) and leaves the counters zeroed again.
 void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table, at::Tensor seq_lens, at::Tensor out,
-                       at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, c10::optional<at::Tensor> prefix) {
+                       at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, c10::optional<at::Tensor> prefix,
+                       c10::optional<at::Tensor> chunk_cnt) {
   using namespace dec;
   int B = q.size(0), Hq = q.size(1), Hkv = kc.size(1), P = kc.size(2);
   AX_CHECK(q.size(2) == D && kc.size(3) == D, "head_dim 128");
@@ -420,7 +424,14 @@ void paged_decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bl
   }
   if (prefix.has_value() && decode_tma_enabled() && P == 64 && prefix->numel() >= 2 * (B + 1)) {  // planned, TMA page pipeline
     AX_CHECK(prefix->scalar_type() == at::kInt && prefix->numel() >= B + 1, "prefix: int32 (B + 1)");
-    paged_decode_attn_tma_partials(q, kc, vc, block_table, seq_lens, part_o, part_ml, splits, scale, *prefix, max_len);
+    if (chunk_cnt.has_value() && out.is_contiguous()) {  // combine fused into the TMA kernel
+      AX_CHECK(chunk_cnt->is_cuda() && chunk_cnt->scalar_type() == at::kInt && chunk_cnt->numel() >= (long)B * Hkv,
+               "chunk_cnt: int32 >= B * Hkv");
+      paged_decode_attn_tma_partials(q, kc, vc, block_table, seq_lens, part_o, part_ml, splits, scale, *prefix, max_len,
+                                     (bf16*)out.data_ptr(), chunk_cnt->data_ptr<int>());
+      return;
+    }
+    paged_decode_attn_tma_partials(q, kc, vc, block_table, seq_lens, part_o, part_ml, splits, scale, *prefix, max_len, nullptr, nullptr);
   } else if (prefix.has_value()) {  // planned: persistent grid over the live work items
     AX_CHECK(prefix->scalar_type() == at::kInt && prefix->numel() >= B + 1, "prefix: int32 (B + 1)");
     launch_pdl(decode_persist_k, dim3(num_sms() * 3), dim3(128), smem, stream(), p, (const int*)prefix->data_ptr<int>(), B);

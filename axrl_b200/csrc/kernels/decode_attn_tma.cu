@@ -45,6 +45,8 @@ struct Params {
   int B, Hq, Hkv, max_pages, splits, max_len;
   float scale_log2;
   int* err;
+  bf16* out;  // (B, Hq, D); non-null: the combine is fused (the last chunk of a (sequence, kv head) merges)
+  int* cnt;   // (B * Hkv) chunk arrival counters, zero between launches (self-cleaning)
 };
 
 __device__ __forceinline__ uint32_t sa(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -94,6 +96,43 @@ __device__ __forceinline__ Item item_of(const Params& p, int w) {
   it.npages = rem <= 0 ? 0 : min(CHUNK / PAGE, (rem + PAGE - 1) / PAGE);
   it.nsplits = rem <= 0 ? 0 : min(CHUNK / SPLIT, (rem + SPLIT - 1) / SPLIT);
   return it;
+}
+
+// Merge of every chunk partial of (it.b, it.hk) into the output rows of the GQA group (consumer
+// thread tid: row tid / 8, 16 columns from (tid % 8) * 16); resets the arrival counter.
+__device__ void combine_group(const Params& p, const Item& it, int tid) {
+  const int G = p.Hq / p.Hkv, r = tid >> 3, c0 = (tid & 7) * 16;
+  const int nch = p.prefix4[it.b + 1] - p.prefix4[it.b];
+  if (r < G) {
+    const long row = (long)it.b * p.Hq + it.hk * G + r;
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, __ldcg(p.part_ml + (row * p.splits + c * (CHUNK / SPLIT)) * 2));
+    float L = 0.f, o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = 0.f;
+    for (int c = 0; c < nch; ++c) {
+      const long base = row * p.splits + c * (CHUNK / SPLIT);
+      const float mc = __ldcg(p.part_ml + base * 2);
+      const float f = mc == -INFINITY ? 0.f : exp2f(mc - M);
+      if (f == 0.f) continue;  // an empty chunk
+      L += f * __ldcg(p.part_ml + base * 2 + 1);
+      const float* po = p.part_o + base * D + c0;
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(po + j));
+        o[j] += f * v.x, o[j + 1] += f * v.y, o[j + 2] += f * v.z, o[j + 3] += f * v.w;
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    float f8[8];
+#pragma unroll
+    for (int h8 = 0; h8 < 16; h8 += 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f8[j] = o[h8 + j] * inv;
+      store8(p.out + row * D + c0 + h8, f8);
+    }
+  }
+  if (tid == 0) p.cnt[it.b * p.Hkv + it.hk] = 0;
 }
 
 __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
@@ -167,9 +206,26 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
   pdl_wait();
   const int total = p.prefix4[p.B] * p.Hkv;
   int pc = 0, n = 0;
+  __shared__ int s_last;
   for (int w = blockIdx.x; w < total; w += gridDim.x) {
     const Item it = item_of(p, w);
-    if (it.npages == 0) continue;  // same decision in every warp
+    if (it.npages == 0) {  // same decision in every warp (and in the producer)
+      if (p.out != nullptr) {  // an empty chunk still arrives (as an empty partial), so its (sequence, kv head) completes
+        const int r = tid >> 3;
+        if (r < G && (tid & 7) == 0) {
+          const long base = ((long)it.b * p.Hq + it.hk * G + r) * p.splits + it.sp;
+          p.part_ml[base * 2] = -INFINITY;
+          p.part_ml[base * 2 + 1] = 0.f;
+        }
+        __threadfence();
+        consumers_sync();
+        if (tid == 0) s_last = atomicAdd(p.cnt + it.b * p.Hkv + it.hk, 1) + 1 == p.prefix4[it.b + 1] - p.prefix4[it.b];
+        consumers_sync();
+        if (s_last) combine_group(p, it, tid);
+        consumers_sync();
+      }
+      continue;
+    }
     const int qs = n & 1;
     const uint32_t qb = sa(sQ + qs * 2 * QBOX);
     const int rb = (warp & 1) * 32;  // first row of this warp's 32 tokens within each page
@@ -292,17 +348,40 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
           for (int j = 0; j < 16; ++j) o[j] += f * sRed[(w2 * 16 + r) * RS + c0 + j];
         }
         const long row = (long)it.b * p.Hq + it.hk * G + r;
-        const long base = row * p.splits + it.sp;
-        float* po = p.part_o + base * D + c0;
+        const int nch = p.prefix4[it.b + 1] - p.prefix4[it.b];
+        if (p.out != nullptr && nch == 1) {  // the only chunk: this is the output
+          const float inv = L > 0.f ? 1.f / L : 0.f;
+          float f[8];
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(po + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-        if ((tid & 7) == 0) {
-          p.part_ml[base * 2] = M;
-          p.part_ml[base * 2 + 1] = L;
-        } else if ((tid & 7) < it.nsplits) {  // the chunk's other splits hold nothing
-          p.part_ml[(base + (tid & 7)) * 2] = -INFINITY;
-          p.part_ml[(base + (tid & 7)) * 2 + 1] = 0.f;
+          for (int h8 = 0; h8 < 16; h8 += 8) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = o[h8 + j] * inv;
+            store8(p.out + row * D + c0 + h8, f);
+          }
+        } else {
+          const long base = row * p.splits + it.sp;
+          float* po = p.part_o + base * D + c0;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(po + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+          if ((tid & 7) == 0) {
+            p.part_ml[base * 2] = M;
+            p.part_ml[base * 2 + 1] = L;
+          } else if (p.out == nullptr && (tid & 7) < it.nsplits) {  // the chunk's other splits hold nothing
+            p.part_ml[(base + (tid & 7)) * 2] = -INFINITY;
+            p.part_ml[(base + (tid & 7)) * 2 + 1] = 0.f;
+          }
         }
+      }
+    }
+    if (p.out != nullptr && p.prefix4[it.b + 1] - p.prefix4[it.b] > 1) {
+      // the last chunk of this (sequence, kv head) to finish merges all of them into the output
+      __threadfence();
+      consumers_sync();
+      if (tid == 0) s_last = atomicAdd(p.cnt + it.b * p.Hkv + it.hk, 1) + 1 == p.prefix4[it.b + 1] - p.prefix4[it.b];
+      consumers_sync();
+      if (s_last) {
+        __threadfence();
+        combine_group(p, it, tid);
       }
     }
     consumers_sync();  // the merge buffer is read before the next item overwrites it
@@ -356,10 +435,12 @@ static at::Tensor& err_flag(int dev) {
 }
 }  // namespace dtm
 
-// The split-KV partials of paged_decode_attn from the TMA-fed kernel (page size 64, planned work
-// list).  Launches only the partial kernel; the caller runs the combine.
+// paged_decode_attn on the TMA-fed kernel (page size 64, planned work list).  With `out` and `cnt`
+// the combine is fused (the caller launches nothing else); without them only the partials are
+// written and the caller runs the combine.
 void paged_decode_attn_tma_partials(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table, at::Tensor seq_lens,
-                                    at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, at::Tensor prefix, int max_len) {
+                                    at::Tensor part_o, at::Tensor part_ml, int64_t splits, double scale, at::Tensor prefix, int max_len,
+                                    bf16* out, int* cnt) {
   using namespace dtm;
   const int B = q.size(0), Hq = q.size(1), Hkv = kc.size(1);
   AX_CHECK(kc.size(2) == PAGE && kc.size(3) == D && kc.is_contiguous() && vc.is_contiguous(), "TMA decode: page size 64, head dim 128");
@@ -369,7 +450,7 @@ void paged_decode_attn_tma_partials(at::Tensor q, at::Tensor kc, at::Tensor vc, 
   const CUtensorMap tq = rows_map(q.data_ptr(), (long)B * Hq, 16);
   Params p{(const bf16*)q.data_ptr(), block_table.data_ptr<int>(), seq_lens.data_ptr<int>(), prefix.data_ptr<int>() + B + 1, part_o.data_ptr<float>(),
            part_ml.data_ptr<float>(), B, Hq, Hkv, (int)block_table.size(1), (int)splits, max_len, (float)(scale * 1.4426950408889634),
-           err_flag(q.get_device()).data_ptr<int>()};
+           err_flag(q.get_device()).data_ptr<int>(), out, cnt};
   const int smem = STAGES * SLOT + 2 * 2 * QBOX + CW * 16 * RS * 4 + (2 * STAGES + 4) * 8 + 16 + 1024;
   static bool attr[64] = {false};
   const int dev = q.get_device();

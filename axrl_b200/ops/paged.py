@@ -64,6 +64,8 @@ class DecodeWorkspace:
         self.part_ml = torch.empty(max_batch * hq * self.splits * 2, dtype=torch.float32, device=device)
         # work lists of the planned decode kernels: 128-token splits, then 512-token chunks
         self.prefix = torch.zeros(2 * (max_batch + 1), dtype=torch.int32, device=device)
+        # (sequence, kv head) chunk counters of the TMA decode kernel's fused combine (self-cleaning)
+        self.chunk_cnt = torch.zeros(max_batch * hq, dtype=torch.int32, device=device)
 
     def plan(self, seq_lens: torch.Tensor) -> None:
         """Work list of live (sequence, split) pairs for ``seq_lens``; every layer of a step reuses it."""
@@ -80,7 +82,8 @@ def paged_decode_attention(q, k_cache, v_cache, block_table, seq_lens, ws: Decod
     out = torch.empty_like(q)
     if not planned:
         ws.plan(seq_lens)
-    _ext.ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, out, ws.part_o, ws.part_ml, ws.splits, scale, ws.prefix)
+    _ext.ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, out, ws.part_o, ws.part_ml, ws.splits, scale, ws.prefix,
+                                 ws.chunk_cnt)
     return out
 
 
