@@ -472,12 +472,19 @@ __device__ __forceinline__ void flush_stripe(const Params& p, int tile, int slab
   if (!last) return;
   __threadfence();
   if (n < p.N)
-    for (int t = 0; t < p.M; ++t) {
-      float* w = p.ws + (long)t * p.N + n;
-      float f = __ldcg(w);
-      *w = 0.f;
-      if (p.r) f += __bfloat162float(p.r[(long)t * p.N + n]);
-      p.y[(long)t * p.N + n] = __float2bfloat16_rn(f);
+    for (int t0 = 0; t0 < p.M; t0 += 8) {  // eight independent loads in flight per thread, then the stores
+      float f[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) f[u] = t0 + u < p.M ? __ldcg(p.ws + (long)(t0 + u) * p.N + n) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (t0 + u >= p.M) break;
+        const long at = (long)(t0 + u) * p.N + n;
+        p.ws[at] = 0.f;
+        float v = f[u];
+        if (p.r) v += __bfloat162float(p.r[at]);
+        p.y[at] = __float2bfloat16_rn(v);
+      }
     }
 }
 
