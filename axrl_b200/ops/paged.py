@@ -9,6 +9,7 @@ tensors use the PyTorch definitions here (oracle + CPU plumbing runs).
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -55,6 +56,9 @@ def decode_attention_ref(q, k_cache, v_cache, block_table, seq_lens, scale):  # 
     return out
 
 
+_FUSED_COMBINE = os.environ.get("AXRL_DECODE_FUSED_COMBINE", "0") == "1"
+
+
 class DecodeWorkspace:
     """Split-KV partial buffers sized for (max_batch, Hq, max_context)."""
 
@@ -82,8 +86,11 @@ def paged_decode_attention(q, k_cache, v_cache, block_table, seq_lens, ws: Decod
     out = torch.empty_like(q)
     if not planned:
         ws.plan(seq_lens)
+    # the TMA kernel can merge its own chunks (AXRL_DECODE_FUSED_COMBINE=1), but the arrival handshake
+    # per chunk cost more than the separate combine launch it saves (batch 64: 12.6 vs 8.8 ms per
+    # Qwen3-8B decode step), so the combine kernel is the default
     _ext.ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, out, ws.part_o, ws.part_ml, ws.splits, scale, ws.prefix,
-                                 ws.chunk_cnt)
+                                 ws.chunk_cnt if _FUSED_COMBINE else None)
     return out
 
 
