@@ -93,6 +93,9 @@ at::Tensor skinny_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> r
 void decode_advance(int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor,
                     at::Tensor, at::Tensor, int64_t, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t, at::Tensor);
 at::Tensor tc_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
+void tc_linear_ag(at::Tensor gather, at::Tensor w, at::Tensor out, at::Tensor src_ptrs, int64_t rank, int64_t rows_per_rank,
+                  at::Tensor flag_ptrs, at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ag_cnt, int64_t call, int64_t timeout_ns,
+                  at::Tensor status);
 void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_t rank, int64_t rows_per_rank, at::Tensor flag_ptrs,
                         at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ticket, int64_t timeout_ns, at::Tensor status);
 int64_t tc_linear_error();
@@ -191,6 +194,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_advance", &ax::decode_advance);
   m.def("tc_linear", &ax::tc_linear, py::arg("x"), py::arg("w"), py::arg("residual") = py::none());
   m.def("tc_linear_to_slots", &ax::tc_linear_to_slots);
+  m.def("tc_linear_ag", &ax::tc_linear_ag);
   m.def("tc_linear_error", &ax::tc_linear_error);
   m.def("tc_stream_linear", &ax::tc_stream_linear, py::arg("x"), py::arg("w"), py::arg("residual") = py::none());
   m.def("tc_stream_error", &ax::tc_stream_error);

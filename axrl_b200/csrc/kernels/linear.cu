@@ -371,6 +371,9 @@ at::Tensor fp8_block_linear(at::Tensor xq, at::Tensor xs, at::Tensor wq, at::Ten
 }
 
 // ---------------------------------------------------------------- hand-written tcgen05 GEMM (tcgemm.cu)
+void tcgemm_ag(const int64_t* src_peers, const void* B, void* D, int rank, int world, int rows_per_rank, int N, int K,
+               const int64_t* flag_peers, const int* my_flags, int ch, int epoch, int* ag_cnt, int call, uint64_t timeout_ns, int* status,
+               int* err, const void* A_local_buffer, cudaStream_t st);
 void tcgemm_tn_to_slots(const void* A, const void* B, const int64_t* peers, int rank, int world, int rows_per_rank, int M, int N, int K,
                         const int64_t* flag_peers, const int* my_flags, int ch, int epoch, unsigned* ticket, uint64_t timeout_ns,
                         int* status, int* err, cudaStream_t st);
@@ -410,6 +413,26 @@ void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_
                      flag_ptrs.data_ptr<int64_t>(), my_flags.data_ptr<int>(), (int)ch, (int)epoch,
                      reinterpret_cast<unsigned*>(ticket.data_ptr<int>()) + ch, (uint64_t)timeout_ns, status.data_ptr<int>(),
                      tcgemm_err(x.get_device()).data_ptr<int>(), stream());
+}
+
+// All-gather -> GEMM in one kernel: out (world * rows_per_rank, N) = gather(x) @ w^T, where `gather`
+// is this rank's symmetric gather buffer with its own rows already at rank * rows_per_rank and
+// src_ptrs (int64 device pointers) every rank's gather buffer; the kernel pulls the other ranks'
+// rows over NVLink.  ag_cnt: world ints, zero before the first call and kept (call = 1, 2, ...).
+void tc_linear_ag(at::Tensor gather, at::Tensor w, at::Tensor out, at::Tensor src_ptrs, int64_t rank, int64_t rows_per_rank,
+                  at::Tensor flag_ptrs, at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ag_cnt, int64_t call, int64_t timeout_ns,
+                  at::Tensor status) {
+  check_bf16_2d(w, "w");
+  AX_CHECK(gather.is_cuda() && gather.scalar_type() == at::kBFloat16 && gather.is_contiguous(), "gather: bf16 buffer");
+  AX_CHECK(src_ptrs.is_cuda() && src_ptrs.scalar_type() == at::kLong && flag_ptrs.is_cuda() && flag_ptrs.numel() == src_ptrs.numel(),
+           "src_ptrs / flag_ptrs: int64 device tensors");
+  AX_CHECK(ag_cnt.is_cuda() && ag_cnt.scalar_type() == at::kInt && ag_cnt.numel() >= src_ptrs.numel(), "ag_cnt: int32 per rank");
+  const int world = src_ptrs.numel(), N = w.size(0), K = w.size(1);
+  AX_CHECK(out.is_contiguous() && out.size(0) == world * rows_per_rank && out.size(1) == N, "out: (world * rows_per_rank, N)");
+  AX_CHECK(gather.numel() >= (long)world * rows_per_rank * K, "gather buffer too small");
+  tcgemm_ag(src_ptrs.data_ptr<int64_t>(), w.data_ptr(), out.data_ptr(), (int)rank, world, (int)rows_per_rank, N, K, flag_ptrs.data_ptr<int64_t>(),
+            my_flags.data_ptr<int>(), (int)ch, (int)epoch, ag_cnt.data_ptr<int>(), (int)call, (uint64_t)timeout_ns, status.data_ptr<int>(),
+            tcgemm_err(w.get_device()).data_ptr<int>(), gather.data_ptr(), stream());
 }
 
 // Decode-size GEMM on the tcgen05 weight-streaming kernel (1..64 rows), for tests and benchmarks.

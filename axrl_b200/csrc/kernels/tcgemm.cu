@@ -34,6 +34,18 @@
 //                              the last CTA to finish fences and raises the epoch's data flag on
 //                              every peer.
 //
+//   mode AGATHER (all-gather -> GEMM of tensor parallelism): A is the gathered activation (world x
+//                rows_per_rank rows) in this rank's gather buffer, where the caller has placed this
+//                rank's own rows.  Four extra warps per CTA pull the other ranks' rows from their
+//                gather buffers over NVLink (16-byte loads, each row crossing the link once) into
+//                this rank's buffer, every CTA a share of every chunk; a chunk is complete when its
+//                copy counter reaches the call's target, and the TMA producer waits (bounded) for
+//                that before loading A tiles of the chunk.  Row tiles are visited this rank's chunk
+//                first, so the local MMAs cover the transfers.  Handshakes on the TP channel: CTA 0
+//                raises this rank's data flag on every peer (its rows are in place), copy warps
+//                wait for each peer's data flag before reading it, and the CTA that completes a
+//                peer's chunk tells that peer its buffer is free again.
+//
 // Every mbarrier wait is bounded: on expiry the CTA records an error code, drains what it issued,
 // frees its TMEM and exits.  TMA reads only this GPU's memory.
 #include <cuda.h>
@@ -49,7 +61,8 @@ constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr long WAIT_LIMIT = 1L << 26;
 enum { B_FULL = 0, B_EMPTY = STAGES, B_ACC_FULL = 2 * STAGES, B_ACC_EMPTY = 2 * STAGES + 2, B_DRAIN = 2 * STAGES + 4, NBAR = 2 * STAGES + 5 };
-enum Mode { LOCAL = 0, SLOTS = 1, F32ACC = 2 };
+enum Mode { LOCAL = 0, SLOTS = 1, F32ACC = 2, AGATHER = 3 };
+constexpr int threads_of(int mode) { return mode == AGATHER ? 320 : THREADS; }  // AGATHER: warps 6-9 copy
 
 struct Params {
   int M, N, K;
@@ -68,6 +81,11 @@ struct Params {
   unsigned* ticket;
   unsigned long long timeout_ns;
   int* status;
+  // AGATHER: every rank's gather buffer (world x rows_per_rank rows of K), this rank's copy counters
+  // (one per source chunk, monotonic) and the counter value of a complete chunk for this call
+  const int64_t* src_peers;
+  int* ag_cnt;
+  int ag_target;
 };
 
 constexpr int kMaxTP = 8, kFreeBase = 16;
@@ -166,18 +184,25 @@ constexpr uint32_t idesc() {
 }
 constexpr uint32_t IDESC = idesc<false, false>();
 
-// Tile t of the grouped raster -> (row tile, column tile).
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+// Tile t of the grouped raster -> (row tile, column tile); `rot` rotates the row tiles (AGATHER:
+// this rank's chunk first).
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn, int rot = 0) {
   const int per_group = GROUP_M * tiles_n;
   const int g = t / per_group, first = g * GROUP_M;
   const int rows = min(GROUP_M, tiles_m - first);
   const int in = t - g * per_group;
-  tm = first + in % rows;
+  tm = (first + in % rows + rot) % tiles_m;
   tn = in / rows;
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* f) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
 }
 
 template <int MODE, bool A_MN = false, bool B_MN = false>
-__global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
+__global__ void __launch_bounds__(threads_of(MODE), 1) gemm_k(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                                                              Params p) {
   extern __shared__ char smem_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + STAGES * STAGE_BYTES);
@@ -185,6 +210,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = p.tiles_m * p.tiles_n, kslices = (p.K + BK - 1) / BK;  // a ragged last slice reads zeros
+  const int rot = MODE == AGATHER ? p.rank * (p.rows_per_rank / BM) : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -216,9 +242,28 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
     if (lane == 0) {
       asm volatile("griddepcontrol.wait;" ::: "memory");
       int it = 0;  // global K-slice counter (ring position)
+      unsigned ready = MODE == AGATHER ? (1u << p.rank) : 0u;  // AGATHER: source chunks complete in this buffer
       for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
         int tm, tn;
-        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn, rot);
+        if constexpr (MODE == AGATHER) {
+          const int c = tm * BM / p.rows_per_rank;
+          if (!(ready & (1u << c))) {
+            const uint64_t t0 = gtimer();
+            while (ld_acquire_gpu(p.ag_cnt + c) < p.ag_target) {
+              if (*abort) break;
+              if (gtimer() - t0 > p.timeout_ns) {
+                atomicCAS(p.status, 0, 2);
+                *abort = 1;
+                break;
+              }
+              __nanosleep(64);
+            }
+            if (*abort) break;
+            asm volatile("fence.proxy.async.global;" ::: "memory");  // the copies are visible to the TMA reads
+            ready |= 1u << c;
+          }
+        }
         for (int kb = 0; kb < kslices; ++kb, ++it) {
           const int s = it % STAGES;
           if (it >= STAGES && !wait(&bar[B_EMPTY + s], ((it / STAGES) - 1) & 1, abort, p.err, 1)) break;
@@ -275,6 +320,63 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
       int zero = 0;
       wait(&bar[B_DRAIN], 0, (volatile int*)&zero, p.err, 4);
     }
+  } else if (MODE == AGATHER && warp >= 6) {
+    // ---------------------------------------------------------------- copy warps (AGATHER): pull peer chunks
+    const int cw = warp - 6;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the preceding kernels (this rank's rows) are complete
+    if (blockIdx.x == 0 && cw == 0 && lane == 0)  // this rank's rows are in place in its gather buffer
+      for (int s = 0; s < p.world; ++s)
+        if (s != p.rank) st_release(reinterpret_cast<int*>(p.flag_peers[s]) + p.ch * kMaxTP + p.rank, p.epoch);
+    const long row16 = (long)p.K * 2 / 16;
+    const int per_cta = (p.rows_per_rank + gridDim.x - 1) / gridDim.x;
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(p.src_peers[p.rank]));
+    volatile uint32_t* s_ok = tmem_slot + 3;  // the copy warps' shared decision for the current chunk
+    for (int k = 1; k < p.world; ++k) {
+      const int s = (p.rank + k) % p.world;
+      if (cw == 0 && lane == 0) {  // the peer's rows are in place (one poller, bounded)
+        uint32_t ok = 1;
+        const uint64_t t0 = gtimer();
+        const int* f = p.my_flags + p.ch * kMaxTP + s;
+        while (ld_acquire(f) < p.epoch) {
+          if (*abort || gtimer() - t0 > p.timeout_ns) {
+            ok = 0;
+            break;
+          }
+          __nanosleep(128);
+        }
+        if (!ok && !*abort) {
+          atomicCAS(p.status, 0, 2);
+          *abort = 1;
+        }
+        *s_ok = ok;
+      }
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      const bool go = *s_ok != 0;
+      asm volatile("bar.sync 2, 128;" ::: "memory");  // every copy warp read the decision before the next chunk's
+      if (!go) break;
+      const long r0 = (long)s * p.rows_per_rank + (long)blockIdx.x * per_cta;
+      const long r1 = min((long)(s + 1) * p.rows_per_rank, r0 + per_cta);
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.src_peers[s]));
+      if (r0 < r1) {
+        const long v1 = r1 * row16;
+        for (long v = r0 * row16 + (cw * 32 + lane); v < v1; v += 4 * 4 * 32) {  // four 16-byte loads in flight per lane
+          uint4 a[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (v + u * 128 < v1) a[u] = src[v + u * 128];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (v + u * 128 < v1) dst[v + u * 128] = a[u];
+        }
+      }
+      asm volatile("bar.sync 2, 128;" ::: "memory");  // the four copy warps finished this CTA's share
+      if (cw == 0 && lane == 0) {
+        __threadfence();
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        if (atomicAdd(p.ag_cnt + s, 1) + 1 == p.ag_target)  // the chunk is complete here: the peer may reuse its rows
+          st_release(reinterpret_cast<int*>(p.flag_peers[s]) + (p.ch + kFreeBase) * kMaxTP + p.rank, p.epoch);
+      }
+    }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2-5)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -299,7 +401,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
       if (!__all_sync(0xffffffffu, wait(&bar[B_ACC_FULL + a], (ti >> 1) & 1, abort, p.err, 5))) break;
       fence_after();
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn, rot);
       const int row = tm * BM + q * 32 + lane;
       if constexpr (MODE == F32ACC) {
         float* d = row < p.M ? p.d32 + (long)row * p.N : nullptr;
@@ -330,7 +432,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_k(const __grid_constant__ CUt
       bf16* dst = nullptr;
       const bf16* res = nullptr;
       if (row < p.M) {
-        if (MODE == LOCAL) {
+        if (MODE == LOCAL || MODE == AGATHER) {
           dst = p.d + (long)row * p.N;
           if (p.c) res = p.c + (long)row * p.N;
         } else {
@@ -685,8 +787,9 @@ static void launch(const void* A, const void* B, Params p, cudaStream_t st) {
     AX_CUDA_OK(cudaFuncSetAttribute(gemm_k<MODE, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes()));
     attr[dev] = true;
   }
-  const int grid = std::min(p.tiles_m * p.tiles_n, num_sms());
-  launch_pdl(gemm_k<MODE, A_MN, B_MN>, dim3(grid), dim3(THREADS), (size_t)smem_bytes(), st, ta, tb, p);
+  const int grid = MODE == AGATHER ? num_sms() : std::min(p.tiles_m * p.tiles_n, num_sms());
+  if (MODE == AGATHER) p.ag_target *= grid;  // every CTA copies a share of every chunk
+  launch_pdl(gemm_k<MODE, A_MN, B_MN>, dim3(grid), dim3(threads_of(MODE)), (size_t)smem_bytes(), st, ta, tb, p);
 }
 
 template <int NTOK>
@@ -757,6 +860,24 @@ void tcgemm_tn_to_slots(const void* A, const void* B, const int64_t* peers, int 
   p.flag_peers = flag_peers, p.my_flags = my_flags, p.ch = ch, p.epoch = epoch, p.world = world, p.ticket = ticket;
   p.timeout_ns = timeout_ns, p.status = status;
   tg::launch<tg::SLOTS>(A, B, p, st);
+}
+
+// All-gather -> GEMM: D[world * rows_per_rank, N] = gather(A) @ B^T, where this rank's rows are already
+// at rows [rank * rows_per_rank, ...) of its gather buffer src_peers[rank] (the A operand) and the
+// other ranks' rows are pulled from src_peers[s] by the kernel.  ag_cnt: world zeroed ints, kept
+// across calls (call index `call` >= 1, consecutive); channel `ch` of the TP flags carries the
+// data / free handshakes of epoch `epoch`.
+void tcgemm_ag(const int64_t* src_peers, const void* B, void* D, int rank, int world, int rows_per_rank, int N, int K,
+               const int64_t* flag_peers, const int* my_flags, int ch, int epoch, int* ag_cnt, int call, uint64_t timeout_ns, int* status,
+               int* err, const void* A_local_buffer, cudaStream_t st) {
+  AX_REQUIRE(world >= 1 && world <= tg::kMaxTP && rank < world && ch >= 0 && ch < tg::kFreeBase, "tcgemm ag: TP layout");
+  AX_REQUIRE(rows_per_rank % tg::BM == 0 && K % 8 == 0, "tcgemm ag: rows per rank a multiple of 128, K a multiple of 8");
+  AX_REQUIRE(((long)K * 2) % 16 == 0 && world <= 32, "tcgemm ag: 16-byte rows");
+  tg::Params p{};
+  p.M = world * rows_per_rank, p.N = N, p.K = K, p.d = static_cast<bf16*>(D), p.rank = rank, p.rows_per_rank = rows_per_rank;
+  p.err = err, p.flag_peers = flag_peers, p.my_flags = my_flags, p.ch = ch, p.epoch = epoch, p.world = world;
+  p.timeout_ns = timeout_ns, p.status = status, p.src_peers = src_peers, p.ag_cnt = ag_cnt, p.ag_target = call;
+  tg::launch<tg::AGATHER>(A_local_buffer, B, p, st);
 }
 
 }  // namespace ax

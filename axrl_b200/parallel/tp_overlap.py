@@ -19,6 +19,10 @@ all-gather / reduce-scatter around cuBLAS GEMMs (``axrl/worker/megatron_worker.p
   receive slot over NVLink, so the transfer of each tile overlaps the MMAs of the next; the kernel
   itself performs the free / data handshakes of the channel, and the owner then sums its slots
   (plus the residual).
+* fused all-gather -> GEMM (``AXRL_TP_FUSED=1``): ONE kernel (mode AGATHER) whose copy warps pull
+  the other ranks' rows from their gather buffers over NVLink into this rank's (each row crosses the
+  link once) while its MMAs start on the local rows; the TMA producer waits per source chunk for the
+  copies to complete.
 
 All waits are bounded; :meth:`P2PTPComm.check` raises if a peer timed out.
 """
@@ -34,7 +38,7 @@ import torch.distributed as dist
 from axrl_b200.ops import _ext
 from axrl_b200.parallel.tensor_parallel import TorchTPComm, TPComm
 
-CH_AG, CH_RS = 0, 1
+CH_AG, CH_RS, CH_AGF = 0, 1, 2
 _K_CHANNELS, _K_MAXTP = 32, 8
 
 
@@ -68,6 +72,13 @@ class P2PTPComm(TPComm):
         self.rs_ptrs_dev = self.rs_ptrs.to(dev)
         self.flag_ptrs_dev = self.flag_ptrs.to(dev)
         self.fused = os.environ.get("AXRL_TP_FUSED", "0") == "1"
+        if self.fused:  # all-gather -> GEMM in one kernel: a gather buffer the kernels pull from
+            self.agf = symm_mem.empty(cap, dtype=torch.bfloat16, device=dev)
+            self.h_agf = symm_mem.rendezvous(self.agf, gname)
+            self.agf_ptrs_dev = torch.tensor(self.h_agf.buffer_ptrs, dtype=torch.int64).to(dev)
+            self.ag_cnt = torch.zeros(_K_MAXTP, dtype=torch.int32, device=dev)
+            self.ag_calls = 0
+            self.ag_last_epoch = 0
         self.stage = torch.empty(2, cap // self.size, dtype=torch.bfloat16, device=dev)
         self.ticket = torch.zeros(_K_CHANNELS, dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -193,6 +204,30 @@ class P2PTPComm(TPComm):
         _ext.ext().tp_reduce_slots(self.rs, self.size, n * N, residual, out)
         return out
 
+    def fused_ag_ok(self, x_local: torch.Tensor, w: torch.Tensor) -> bool:
+        """Shapes the one-kernel all-gather -> GEMM accepts."""
+        n, K = x_local.shape
+        return (self.fused and n % 128 == 0 and K % 8 == 0 and w.shape[0] % 32 == 0 and n * self.size * K <= self.agf.numel()
+                and x_local.dtype == torch.bfloat16)
+
+    def ag_gemm_fused(self, x_local: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """y (T, N) = AG(x_local) @ w^T in one kernel: this rank's rows go into its gather buffer, the
+        kernel pulls the other ranks' rows over NVLink while it multiplies the local ones."""
+        n, K = x_local.shape
+        T = n * self.size
+        peers = ((1 << self.size) - 1) & ~(1 << self.rank)
+        if self.ag_last_epoch:  # every peer has pulled this rank's rows of the previous call
+            _ext.ext().tp_wait(self.flags, CH_AGF + 16, peers, self.ag_last_epoch, self.timeout_ns, self.status)
+        buf = self.agf[:T * K].view(T, K)
+        buf[self.rank * n:(self.rank + 1) * n].copy_(x_local)
+        e = self._next_epoch()
+        self.ag_calls += 1
+        y = torch.empty(T, w.shape[0], dtype=x_local.dtype, device=x_local.device)
+        _ext.ext().tc_linear_ag(self.agf, w, y, self.agf_ptrs_dev, self.rank, n, self.flag_ptrs_dev, self.flags, CH_AGF, e, self.ag_cnt,
+                                self.ag_calls, self.timeout_ns, self.status)
+        self.ag_last_epoch = e
+        return y
+
     def ag_linear(self, x_local: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         T = x_local.shape[0] * self.size
         if not self._fits(x_local.reshape(x_local.shape[0], -1), T) or not w.is_cuda:
@@ -221,10 +256,13 @@ class _AGLinear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_local, w, comm):  # noqa: ANN001, ANN205
         n = x_local.shape[0]
-        y = torch.empty(n * comm.size, w.shape[0], dtype=x_local.dtype, device=x_local.device)
-        e = _ext.ext()
-        comm._gather_chunks(x_local, lambda src, rows: e.linear_fwd_into(rows, w, y[src * n:(src + 1) * n]))
-        torch.cuda.current_stream().wait_stream(comm.comm_stream)
+        if comm.fused_ag_ok(x_local, w):  # one kernel: peer rows pulled over NVLink under the local MMAs
+            y = comm.ag_gemm_fused(x_local, w)
+        else:
+            y = torch.empty(n * comm.size, w.shape[0], dtype=x_local.dtype, device=x_local.device)
+            e = _ext.ext()
+            comm._gather_chunks(x_local, lambda src, rows: e.linear_fwd_into(rows, w, y[src * n:(src + 1) * n]))
+            torch.cuda.current_stream().wait_stream(comm.comm_stream)
         ctx.save_for_backward(x_local, w)
         ctx.comm = comm
         return y
