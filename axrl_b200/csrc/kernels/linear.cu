@@ -117,14 +117,14 @@ static int decode_gemm_mode() {
   return mode;
 }
 
-// Default by rows, from in-stream chains of Qwen3-8B projections on B200 (distinct weights, PDL):
-// <= 16 rows the cp.async skinny kernel; 17-40 rows the tcgen05 streaming kernel (32 rows: qkv 19.0,
-// o 16.0, down 26.4 us against 21.7 / 21.4 / 32.8 for CUTLASS swap-AB); above, CUTLASS swap-AB.
+// Default by rows: <= 16 rows the cp.async skinny kernel, above CUTLASS swap-AB.  The tcgen05
+// streaming kernel (AXRL_DECODE_GEMM=tcstream) wins in-stream chains of single projections at 32 rows
+// (qkv 19.0, o 16.0, down 26.4 us against 21.7 / 21.4 / 32.8) but not the whole Qwen3-8B decode step
+// (batch 32: 7.10 vs 6.88 ms), so it stays opt-in.
 static DecodeGemm decode_gemm(int M, int N, int K) {
   const int forced = decode_gemm_mode();
   const bool stream_ok = M <= 64 && K % 64 == 0 && N % 8 == 0 && N <= 262144 && (long)M * N <= 64L * 262144;
   if (forced == kTcStream && stream_ok) return kTcStream;
-  if (forced < 0 && M > 16 && M <= 40 && stream_ok && (long)N * K <= (128L << 20)) return kTcStream;  // not the LM head
   if (M > 16 || K % 64 || N % 8 || (long)N * K > (64L << 20)) return kTcgen05;
   return forced >= 0 && forced != kTcStream ? (DecodeGemm)forced : kSkinny;
 }
