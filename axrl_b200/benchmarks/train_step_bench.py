@@ -52,6 +52,7 @@ def main() -> None:
     ap.add_argument("--mb-tokens", type=int, default=16384)
     ap.add_argument("--iters", type=int, default=2)
     ap.add_argument("--one-micro-batch", action="store_true")
+    ap.add_argument("--deterministic", action="store_true", help="deterministic attention backward (separate dQ pass), as bench.py --deterministic")
     ap.add_argument("--device", default="cuda")
     a = ap.parse_args()
 
@@ -63,7 +64,8 @@ def main() -> None:
     cfg = resolve_preset(a.model)
     dev = torch.device(a.device)
     cuda = dev.type == "cuda"
-    eng = TrainEngine(MegatronWorkerConfig(recompute_granularity="full", max_tokens_per_micro_batch=a.mb_tokens, seed=1234), cfg, dev)
+    eng = TrainEngine(MegatronWorkerConfig(recompute_granularity="full", max_tokens_per_micro_batch=a.mb_tokens, seed=1234,
+                                           deterministic_mode=a.deterministic), cfg, dev)
     trainer = GrpoTrainer(GrpoTrainerConfig(loss_type="grpo", mismatch_token_clip_max=2.0))
     batch = make_batch(a.prompts, a.group, a.prompt_len, a.median, a.max_len, cfg.vocab_size)
     tokens = int(batch["seq_len"].sum())

@@ -47,6 +47,7 @@ static bool use_tcgemm() {
 
 void tcgemm_nn(const void* dY, const void* W, void* dX, int M, int Ko, int Nr, int* err, cudaStream_t st);
 void tcgemm_wgrad(const void* dY, const void* X, float* G, int Nw, int Kw, int T, bool accumulate, int* err, cudaStream_t st);
+void tcgemm_wgrad_bf16(const void* dY, const void* X, void* G, int Nw, int Kw, int T, int* err, cudaStream_t st);
 
 // Backward GEMMs (data and weight gradients) run on the hand-written kernel unless
 // AXRL_TRAIN_GEMM_BWD=cutlass (Qwen3-8B shapes at 16k tokens on B200: 10.2 ms against 10.9 ms
@@ -252,6 +253,10 @@ at::Tensor linear_wgrad(at::Tensor dy, at::Tensor x) {
   int M = dy.size(0), N = dy.size(1), K = x.size(1);
   auto dw = at::empty({N, K}, dy.options());
   if (M == 0) return dw.zero_();
+  if (use_tcgemm_bwd() && M >= 64 && N % 8 == 0 && K % 32 == 0 && tc_ok(dy.data_ptr()) && tc_ok(x.data_ptr())) {
+    tcgemm_wgrad_bf16(dy.data_ptr(), x.data_ptr(), dw.data_ptr(), N, K, M, tcgemm_err(dy.get_device()).data_ptr<int>(), stream());
+    return dw;
+  }
   gemm::wgrad_bf16_sm1(dy.data_ptr(), x.data_ptr(), dw.data_ptr(), N, K, M, stream());
   return dw;
 }

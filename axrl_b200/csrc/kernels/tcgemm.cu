@@ -841,6 +841,13 @@ void tcgemm_nn(const void* dY, const void* W, void* dX, int M, int Ko, int Nr, i
   tg::launch<tg::LOCAL, false, true>(dY, W, p, st);
 }
 
+// Weight gradient in bf16: G[Nw, Kw] = dY[T, Nw]^T @ X[T, Kw] (both read MN-major).
+void tcgemm_wgrad_bf16(const void* dY, const void* X, void* G, int Nw, int Kw, int T, int* err, cudaStream_t st) {
+  tg::Params p{};
+  p.M = Nw, p.N = Kw, p.K = T, p.d = static_cast<bf16*>(G), p.rows_per_rank = 1, p.err = err;
+  tg::launch<tg::LOCAL, true, true>(dY, X, p, st);
+}
+
 // Weight gradient: G[Nw, Kw] (fp32) (+)= dY[T, Nw]^T @ X[T, Kw] (both read MN-major).
 void tcgemm_wgrad(const void* dY, const void* X, float* G, int Nw, int Kw, int T, bool accumulate, int* err, cudaStream_t st) {
   tg::Params p{};
