@@ -213,7 +213,27 @@ class SyntheticGRPO:
         t["pack_s"] = time.perf_counter() - t1
 
         t2 = time.perf_counter()
-        if sc.compute_ref_logprobs:
+        streamed = (sc.compute_ref_logprobs and sc.compute_old_logprobs and self.device.type == "cuda" and self.train.optim is not None
+                    and not self.ref_weights.is_cuda)
+        if streamed:
+            # reference weights in host memory: copy them in on a side stream while the old-policy
+            # pass runs (the KV pool is released in this phase), then swap them in on the device
+            cs = getattr(self, "_ref_stream", None) or torch.cuda.Stream(device=self.device)
+            self._ref_stream = cs
+            ref_dev = torch.empty_like(self.train.optim.bf16)
+            cs.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(cs):
+                ref_dev.copy_(self.ref_weights, non_blocking=True)
+            batch["old_logprobs"] = self.train.compute_logprobs(batch, sc.temperature)
+            cur = self.train.optim.bf16.clone()
+            torch.cuda.current_stream().wait_stream(cs)
+            ref_dev.record_stream(torch.cuda.current_stream())
+            self.train.load_weights(ref_dev)
+            del ref_dev
+            batch["ref_logprobs"] = self.train.compute_logprobs(batch, sc.temperature)
+            self.train.load_weights(cur)
+            del cur
+        elif sc.compute_ref_logprobs:
             cur = self.train.snapshot_weights() if self.device.type == "cpu" else None
             if cur is None:
                 cur = self.train.optim.bf16.clone() if self.train.optim else None
@@ -221,7 +241,7 @@ class SyntheticGRPO:
             batch["ref_logprobs"] = self.train.compute_logprobs(batch, sc.temperature)
             self.train.load_weights(cur)
             del cur
-        if sc.compute_old_logprobs:
+        if sc.compute_old_logprobs and not streamed:
             batch["old_logprobs"] = self.train.compute_logprobs(batch, sc.temperature)
         else:
             batch["old_logprobs"] = batch["rollout_logprobs"].clone()
