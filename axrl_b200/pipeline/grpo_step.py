@@ -64,6 +64,9 @@ class SyntheticGRPOConfig:
     # keep the reference-policy weights in device memory (a device-to-device copy before the ref
     # log-prob pass) instead of pinned host memory (a host-to-device copy of the whole model)
     ref_on_device: bool = False
+    # partial rollout under data parallelism: stop when the ranks' completed groups add up to the
+    # global batch (the groups land where they finish), not when every rank has its own share
+    global_stop: bool = True
     compute_old_logprobs: bool = True
     separate_rollout_copy: bool = False
     seed: int = 0
@@ -298,15 +301,38 @@ class SyntheticGRPO:
 
         self.rollout.acquire_kv()
         self.rollout.add_requests(reqs)
-        while sum(g.done for g in self.pool) < sc.num_prompts and (self.rollout.waiting or self.rollout.running):
-            for res in self.rollout.step():
-                absorb(res)
+        par = self.train.par
+        if sc.global_stop and par.dp_group is not None and par.dp_size > 1:
+            # data-parallel ranks stop together, once the ranks' completed groups add up to the
+            # global batch (num_prompts per rank): one all-reduce per decode burst, so no rank idles
+            # in the next collective while another finishes its longest group
+            import torch.distributed as dist
+
+            mine = torch.zeros(2, dtype=torch.int64, device=self.device)
+            every = torch.zeros(2 * par.dp_size, dtype=torch.int64, device=self.device)
+            while True:
+                if self.rollout.waiting or self.rollout.running:
+                    for res in self.rollout.step():
+                        absorb(res)
+                mine[0] = sum(g.done for g in self.pool)
+                mine[1] = int(bool(self.rollout.waiting or self.rollout.running))
+                dist.all_gather_into_tensor(every, mine, group=par.dp_group)
+                done, busy = every.view(-1, 2)[:, 0].tolist(), every.view(-1, 2)[:, 1].tolist()
+                # every rank needs at least one group of its own to train on
+                if (sum(done) >= sc.num_prompts * par.dp_size and min(done) >= 1) or sum(busy) == 0:
+                    break
+            take_n = len(self.pool)  # every group this rank completed
+        else:
+            while sum(g.done for g in self.pool) < sc.num_prompts and (self.rollout.waiting or self.rollout.running):
+                for res in self.rollout.step():
+                    absorb(res)
+            take_n = sc.num_prompts
         aborted = 0
         for res in self.rollout.abort_all():
             aborted += 1
             absorb(res)
         self.rollout.release_kv()
-        take = [g for g in self.pool if g.done][:sc.num_prompts]
+        take = [g for g in self.pool if g.done][:take_n]
         self.pool = [g for g in self.pool if not any(g is t for t in take)]
         out_reqs, out_res = [], []
         for g in take:

@@ -226,3 +226,66 @@ def test_agentic_group_packing_shares_prefix():
     real = s.merge_info.real_total
     paths = sum(len(t.turn_samples[i].input_ids) for t in (x.trace for x in pipe.pool[0]) for i in range(2))
     assert real < paths and real <= 20 + 4 * (3 + 2 + 3 + 2)  # prefix once; each trajectory's turns + fork tokens
+
+
+def _dp_partial_worker(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from axrl_b200.configs import GrpoTrainerConfig, MegatronWorkerConfig
+        from axrl_b200.models.qwen3 import resolve_preset
+        from axrl_b200.pipeline.grpo_step import SyntheticGRPO, SyntheticGRPOConfig
+        from axrl_b200.train.engine import ParallelCtx, TrainEngine
+
+        torch.manual_seed(0)
+        wc = MegatronWorkerConfig()
+        wc.lr_scheduler.lr_warmup_steps = 0
+        par = ParallelCtx(dp_group=dist.group.WORLD, dp_size=world, dp_rank=rank, zero_backend="off")
+        train = TrainEngine(wc, resolve_preset("tiny"), "cpu", par=par)
+        # rank 1's responses are much longer: its groups finish later
+        sc = SyntheticGRPOConfig(num_prompts=2, prompt_len=16, group_size=4, forced_len_median=8 + 40 * rank, forced_len_sigma=0.3,
+                                 forced_len_min=2, forced_len_max=80, partial_rollout=True, inflight_prompts=4, seed=3 + rank,
+                                 separate_rollout_copy=True, use_cuda_graph=False)
+        pipe = SyntheticGRPO(resolve_preset("tiny"), wc, GrpoTrainerConfig(loss_type="grpo"), sc, "cpu", train_engine=train)
+        got = []
+        for _ in range(3):
+            m = pipe.run_step()
+            got.append(m["groups_done"])
+            assert np.isfinite(m["loss"]) and m["groups_done"] >= 1
+        tot = torch.tensor(got)
+        dist.all_reduce(tot)
+        assert all(int(x) >= sc.num_prompts * world for x in tot), tot  # the global batch every step
+        q.put((rank, "ok", got))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_partial_rollout_data_parallel_global_stop():
+    """Data-parallel partial rollout stops on the global batch: the ranks' completed groups add up
+    to num_prompts per rank every step, the rank with the shorter responses contributing more."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_dp_partial_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in procs])
+    for p in procs:
+        p.join(timeout=60)
+    for r, msg, _ in res:
+        assert msg == "ok", f"rank {r}:\n{msg}"
+    assert sum(res[0][2]) >= sum(res[1][2])  # the faster rank trained at least as many groups
