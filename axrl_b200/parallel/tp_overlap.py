@@ -19,7 +19,7 @@ all-gather / reduce-scatter around cuBLAS GEMMs (``axrl/worker/megatron_worker.p
   receive slot over NVLink, so the transfer of each tile overlaps the MMAs of the next; the kernel
   itself performs the free / data handshakes of the channel, and the owner then sums its slots
   (plus the residual).
-* fused all-gather -> GEMM (``AXRL_TP_FUSED=1``): ONE kernel (mode AGATHER) whose copy warps pull
+* fused all-gather -> GEMM (default; ``AXRL_TP_FUSED_AG=0`` disables): ONE kernel (mode AGATHER) whose copy warps pull
   the other ranks' rows from their gather buffers over NVLink into this rank's (each row crosses the
   link once) while its MMAs start on the local rows; the TMA producer waits per source chunk for the
   copies to complete.
@@ -71,8 +71,11 @@ class P2PTPComm(TPComm):
         self.flag_ptrs = torch.tensor(self.h_flags.buffer_ptrs, dtype=torch.int64)
         self.rs_ptrs_dev = self.rs_ptrs.to(dev)
         self.flag_ptrs_dev = self.flag_ptrs.to(dev)
+        # one-kernel GEMM -> reduce-scatter: opt-in (slower than the chunked path at 2 GPUs);
+        # one-kernel all-gather -> GEMM: default (the fastest of the three at 2 GPUs)
         self.fused = os.environ.get("AXRL_TP_FUSED", "0") == "1"
-        if self.fused:  # all-gather -> GEMM in one kernel: a gather buffer the kernels pull from
+        self.fused_ag = self.fused or os.environ.get("AXRL_TP_FUSED_AG", "1") == "1"
+        if self.fused_ag:  # all-gather -> GEMM in one kernel: a gather buffer the kernels pull from
             self.agf = symm_mem.empty(cap, dtype=torch.bfloat16, device=dev)
             self.h_agf = symm_mem.rendezvous(self.agf, gname)
             self.agf_ptrs_dev = torch.tensor(self.h_agf.buffer_ptrs, dtype=torch.int64).to(dev)
@@ -207,7 +210,7 @@ class P2PTPComm(TPComm):
     def fused_ag_ok(self, x_local: torch.Tensor, w: torch.Tensor) -> bool:
         """Shapes the one-kernel all-gather -> GEMM accepts."""
         n, K = x_local.shape
-        return (self.fused and n % 128 == 0 and K % 8 == 0 and w.shape[0] % 32 == 0 and n * self.size * K <= self.agf.numel()
+        return (self.fused_ag and n % 128 == 0 and K % 8 == 0 and w.shape[0] % 32 == 0 and n * self.size * K <= self.agf.numel()
                 and x_local.dtype == torch.bfloat16)
 
     def ag_gemm_fused(self, x_local: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
