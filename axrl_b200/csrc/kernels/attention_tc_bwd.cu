@@ -50,6 +50,12 @@ constexpr int C_S = 0, C_DP = 128, C_DV = 256, C_DK = 384;
 
 constexpr int B_KV = 0, B_QD = 1, B_S = 2, B_P = 3, B_MM = 4, B_DQF = 5, B_DRAIN = 6, B_LD = 7, NBAR = 8;
 
+// 2^x with the hardware approximation (flushes denormal results to zero; P is rounded to bf16 anyway)
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void red_add_f32(float* p, float a) { asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory"); }
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
@@ -250,7 +256,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
           for (int u = 0; u < 2; ++u) {
             const int c = c0 + e + u;
             const bool vis = c >= cfirst && c < climit;
-            const float pr = vis ? exp2f(s[e + u] * p.scale_log2 - L[c]) : 0.f;
+            const float pr = vis ? ex2_fast(fmaf(s[e + u], p.scale_log2, -L[c])) : 0.f;
             pv[u] = pr;
             dv2[u] = vis ? pr * (dp[e + u] - Ds[c]) * p.scale : 0.f;
           }
@@ -525,7 +531,7 @@ __global__ void __launch_bounds__(atb2::THREADS2, 1) attn_bwd_tc2_k(const __grid
         for (int u = 0; u < 2; ++u) {
           const int c = c0 + e + u;
           const bool vis = c >= cfirst && c < climit;
-          const float pr = vis ? exp2f(sv[e + u] * p.scale_log2 - L[c]) : 0.f;
+          const float pr = vis ? ex2_fast(fmaf(sv[e + u], p.scale_log2, -L[c])) : 0.f;
           pv[u] = pr;
           dv2[u] = vis ? pr * (dp[e + u] - Ds[c]) * p.scale : 0.f;
         }
