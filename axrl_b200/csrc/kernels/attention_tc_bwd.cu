@@ -48,7 +48,7 @@ constexpr int HALF = TILE / 2;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int C_S = 0, C_DP = 128, C_DV = 256, C_DK = 384;
 
-constexpr int B_KV = 0, B_QD = 1, B_S = 2, B_P = 3, B_MM = 4, B_DQF = 5, B_DRAIN = 6, B_LD = 7, NBAR = 8;
+constexpr int B_KV = 0, B_QD = 1, B_S = 2, B_P = 3, B_MM = 4, B_DQF = 5, B_DRAIN = 6, B_LD = 7, B_QD1 = 8, B_EM = 9, NBAR = 11;
 
 // 2^x with the hardware approximation (flushes denormal results to zero; P is rounded to bf16 anyway)
 __device__ __forceinline__ float ex2_fast(float x) {
@@ -106,18 +106,31 @@ struct QTiles {
   }
 };
 
+// DBL: Q and dO double-buffered (the next q tile loads while this one is in the products); P^T goes
+// back into tensor memory over the consumed S^T columns (each half-row warp inside its own half:
+// q columns [0, 64) -> TMEM columns [0, 32), [64, 128) -> [64, 96)) and is the A operand of dV from
+// there, which frees the shared-memory P^T tile for the second buffers.  Shared memory is then
+// 7 tiles + the lse / Dsum stages, so the dynamic shared memory base must be 1024-byte aligned
+// (checked; a misaligned base records an error and the CTA exits).
+template <bool DBL>
 __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                                                           const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
                                                           Params p) {
-  extern __shared__ char smem_raw[];
-  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) char smem_raw[];
+  if constexpr (DBL) {
+    if (reinterpret_cast<uintptr_t>(smem_raw) & 1023) {
+      if (threadIdx.x == 0) atomicCAS(p.err, 0, 19);
+      return;
+    }
+  }
+  char* sm = DBL ? smem_raw : reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   char* sK = sm;
   char* sV = sm + TILE;
-  char* sQ = sm + 2 * TILE;
-  char* sdO = sm + 3 * TILE;
-  char* sP = sm + 4 * TILE;   // P^T  [key][q]
-  char* sdS = sm + 5 * TILE;  // dS^T [key][q]
-  float* sL = reinterpret_cast<float*>(sm + 6 * TILE);  // [tile parity][q column]: lse2
+  char* sQ = sm + 2 * TILE;                  // DBL: two buffers (2, 3)
+  char* sdO = sm + (DBL ? 4 : 3) * TILE;     // DBL: two buffers (4, 5)
+  char* sP = sm + 4 * TILE;                  // P^T  [key][q] (not DBL)
+  char* sdS = sm + (DBL ? 6 : 5) * TILE;     // dS^T [key][q]
+  float* sL = reinterpret_cast<float*>(sm + (DBL ? 7 : 6) * TILE);  // [tile parity][q column]: lse2
   float* sDs = sL + 2 * BQ;                              // [tile parity][q column]: Dsum
   uint64_t* bar = reinterpret_cast<uint64_t*>(sDs + 2 * BQ);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
@@ -138,6 +151,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
     mbar_init(&bar[B_DQF], 8);
     mbar_init(&bar[B_DRAIN], 1);
     mbar_init(&bar[B_LD], 256);
+    mbar_init(&bar[B_QD1], 1);
+    mbar_init(&bar[B_EM], 1);
+    mbar_init(&bar[B_EM + 1], 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -163,29 +179,42 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
       tma_2d(sV + HALF, &tv, hk * D + 64, ks, &bar[B_KV]);
       int i = 0;
       for (; qt.valid(); qt.next(), ++i) {
-        if (i >= 1 && !mbar_wait(&bar[B_MM], (i - 1) & 1, abort, p.err, 11)) break;  // Q / dO of the previous tile consumed
+        const int b = DBL ? (i & 1) : 0;
+        if constexpr (DBL) {  // this buffer's previous tile (i - 2) consumed
+          if (i >= 2 && !mbar_wait(&bar[B_EM + b], ((i - 2) >> 1) & 1, abort, p.err, 11)) break;
+        } else {
+          if (i >= 1 && !mbar_wait(&bar[B_MM], (i - 1) & 1, abort, p.err, 11)) break;  // Q / dO of the previous tile consumed
+        }
         const int h = hk * G + qt.g;
-        mbar_expect_tx(&bar[B_QD], 2 * TILE);
-        tma_2d(sQ, &tq, h * D, qt.qs, &bar[B_QD]);
-        tma_2d(sQ + HALF, &tq, h * D + 64, qt.qs, &bar[B_QD]);
-        tma_2d(sdO, &tdo, h * D, qt.qs, &bar[B_QD]);
-        tma_2d(sdO + HALF, &tdo, h * D + 64, qt.qs, &bar[B_QD]);
+        uint64_t* qd = &bar[b ? B_QD1 : B_QD];
+        char* q_dst = sQ + b * TILE;
+        char* do_dst = sdO + b * TILE;
+        mbar_expect_tx(qd, 2 * TILE);
+        tma_2d(q_dst, &tq, h * D, qt.qs, qd);
+        tma_2d(q_dst + HALF, &tq, h * D + 64, qt.qs, qd);
+        tma_2d(do_dst, &tdo, h * D, qt.qs, qd);
+        tma_2d(do_dst + HALF, &tdo, h * D + 64, qt.qs, qd);
       }
       if (*abort) {  // every copy this CTA started lands before its shared memory is released
         int zero = 0;
         mbar_wait(&bar[B_KV], 0, (volatile int*)&zero, p.err, 11);
-        if (i >= 1) mbar_wait(&bar[B_QD], (i - 1) & 1, (volatile int*)&zero, p.err, 11);
+        for (int j = max(0, i - (DBL ? 2 : 1)); j < i; ++j) {
+          const int b = DBL ? (j & 1) : 0;
+          mbar_wait(&bar[b ? B_QD1 : B_QD], (DBL ? (j >> 1) : j) & 1, (volatile int*)&zero, p.err, 11);
+        }
       }
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t ID_KMAJ = idesc_bf16(128, false), ID_BMN = idesc_bf16(128, true), ID_ABMN = idesc_bf16(128, true, true);
-      const uint32_t k_b = s32(sK), v_b = s32(sV), q_b = s32(sQ), do_b = s32(sdO), p_b = s32(sP), ds_b = s32(sdS);
+      const uint32_t k_b = s32(sK), v_b = s32(sV), p_b = s32(sP), ds_b = s32(sdS);
       bool ok = mbar_wait(&bar[B_KV], 0, abort, p.err, 12);
       int i = 0;
       for (; ok && qt.valid(); qt.next(), ++i) {
-        if (!mbar_wait(&bar[B_QD], i & 1, abort, p.err, 12)) break;
+        const int b = DBL ? (i & 1) : 0;
+        const uint32_t q_b = s32(sQ + b * TILE), do_b = s32(sdO + b * TILE);
+        if (!mbar_wait(&bar[b ? B_QD1 : B_QD], (DBL ? (i >> 1) : i) & 1, abort, p.err, 12)) break;
         if (i >= 1 && !mbar_wait(&bar[B_DQF], (i - 1) & 1, abort, p.err, 12)) break;  // dQ of the previous tile read out
         tc_fence_after();
 #pragma unroll
@@ -200,9 +229,13 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {  // dV += P^T dO, dK += dS^T Q (K = q rows)
           const uint32_t a_off = (kk >> 2) * HALF + (kk & 3) * 32;
-          tc_mma(tmem + C_DV, sdesc(p_b + a_off, 16, 1024), sdesc(do_b + kk * 2048, HALF, 1024), ID_BMN, (i > 0 || kk > 0));
+          if constexpr (DBL)  // P^T from TMEM: q 16 kk .. +15 at column (kk < 4 ? 0 : 64) + (kk % 4) * 8
+            tc_mma_ts(tmem + C_DV, tmem + C_S + (kk >> 2) * 64 + (kk & 3) * 8, sdesc(do_b + kk * 2048, HALF, 1024), ID_BMN, (i > 0 || kk > 0));
+          else
+            tc_mma(tmem + C_DV, sdesc(p_b + a_off, 16, 1024), sdesc(do_b + kk * 2048, HALF, 1024), ID_BMN, (i > 0 || kk > 0));
           tc_mma(tmem + C_DK, sdesc(ds_b + a_off, 16, 1024), sdesc(q_b + kk * 2048, HALF, 1024), ID_BMN, (i > 0 || kk > 0));
         }
+        if constexpr (DBL) tc_commit(&bar[B_EM + b]);  // Q / dO of this buffer consumed
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)  // dQ = dS K (K = keys; dS read MN-major from dS^T)
           tc_mma(tmem + C_S, sdesc(ds_b + kk * 2048, HALF, 1024), sdesc(k_b + kk * 2048, HALF, 1024), ID_ABMN, kk > 0);
@@ -264,14 +297,17 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
           pw[e / 2] = *reinterpret_cast<uint32_t*>(&a);
           dw[e / 2] = *reinterpret_cast<uint32_t*>(&b);
         }
+        if constexpr (DBL) tmem_st16u(lane_addr + C_S + half * 64 + (cc >> 1), pw);  // over S^T columns this warp has read
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {  // 4 chunks of 8 q columns, 128-byte swizzled rows of this half's box
           const int ch = (cc >> 3) + q8;  // 16-byte chunk index within the 64-column box
           const int off = ((ch ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[q8 * 4], pw[q8 * 4 + 1], pw[q8 * 4 + 2], pw[q8 * 4 + 3]);
+          if constexpr (!DBL)
+            *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[q8 * 4], pw[q8 * 4 + 1], pw[q8 * 4 + 2], pw[q8 * 4 + 3]);
           *reinterpret_cast<uint4*>(dsrow + off) = make_uint4(dw[q8 * 4], dw[q8 * 4 + 1], dw[q8 * 4 + 2], dw[q8 * 4 + 3]);
         }
       }
+      if constexpr (DBL) tmem_st_wait();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P^T / dS^T visible to the tensor cores
       tc_fence_before();
       __syncwarp();
@@ -663,6 +699,16 @@ static int& bwd_blocks64_flag() {
 }
 static bool bwd_blocks64() { return bwd_blocks64_flag() != 0; }
 void set_attn_bwd_blocks64(bool on) { bwd_blocks64_flag() = on ? 1 : 0; }
+// AXRL_ATTN_BWD_DBL=1: the 128-row kernel with Q / dO double-buffered and P^T in tensor memory.
+static int& bwd_dbl_flag() {
+  static int on = [] {
+    const char* e = std::getenv("AXRL_ATTN_BWD_DBL");
+    return (e && std::string(e) == "1") ? 1 : 0;
+  }();
+  return on;
+}
+static bool bwd_dbl() { return bwd_dbl_flag() != 0; }
+void set_attn_bwd_dbl(bool on) { bwd_dbl_flag() = on ? 1 : 0; }
 
 void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor lse2, at::Tensor dsum, at::Tensor dq_acc,
                        at::Tensor dk, at::Tensor dv, at::Tensor kseg, at::Tensor qr, at::Tensor tiles, double scale) {
@@ -691,9 +737,16 @@ void attn_bwd_tc_tiles(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v
     AX_LAUNCH_OK();
     return;
   }
+  if (bwd_dbl()) {
+    const int smem_d = 7 * TILE + 4 * BQ * 4 + NBAR * 8 + 16;  // the base is 1024-byte aligned (checked in the kernel)
+    smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_k<true>), smem_d);
+    attn_bwd_tc_k<true><<<dim3(Hkv, nt), THREADS, smem_d, stream()>>>(tq, tk, tv, tdo, p);
+    AX_LAUNCH_OK();
+    return;
+  }
   const int smem = 6 * TILE + 4 * BQ * 4 + NBAR * 8 + 16 + 1024;
-  smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_k), smem);
-  attn_bwd_tc_k<<<dim3(Hkv, nt), THREADS, smem, stream()>>>(tq, tk, tv, tdo, p);
+  smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_k<false>), smem);
+  attn_bwd_tc_k<false><<<dim3(Hkv, nt), THREADS, smem, stream()>>>(tq, tk, tv, tdo, p);
   AX_LAUNCH_OK();
 }
 

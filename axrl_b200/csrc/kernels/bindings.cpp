@@ -41,6 +41,7 @@ at::Tensor gdn_step(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::
 int64_t attn_bwd_tc_error();
 void set_attn_bwd_tc(bool on);
 void set_attn_bwd_blocks64(bool on);
+void set_attn_bwd_dbl(bool on);
 void paged_decode_attn(at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, int64_t,
                        double, c10::optional<at::Tensor>,
                        c10::optional<at::Tensor>);
@@ -173,6 +174,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd_tc_error", &ax::attn_bwd_tc_error);
   m.def("set_attn_bwd_tc", &ax::set_attn_bwd_tc);
   m.def("set_attn_bwd_blocks64", &ax::set_attn_bwd_blocks64);
+  m.def("set_attn_bwd_dbl", &ax::set_attn_bwd_dbl);
   m.def("set_decode_attn_tma", &ax::set_decode_attn_tma);
   m.def("paged_decode_attn", &ax::paged_decode_attn, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("block_table"),
         py::arg("seq_lens"), py::arg("out"), py::arg("part_o"), py::arg("part_ml"), py::arg("splits"), py::arg("scale"),

@@ -544,11 +544,12 @@ def test_attention_tcgen05_forward_matches_reference(case, variant):
     close(lse[fin], lse2[fin], 1e-3, 1e-4, msg="lse")
 
 
-@pytest.mark.parametrize("blocks64", [False, True])
+@pytest.mark.parametrize("variant", ["tile128", "blocks64", "dbl"])
 @pytest.mark.parametrize("case", [0, 1, 2, 3])
-def test_attention_tcgen05_backward_matches_mma(case, blocks64):
-    """tcgen05 backward (attention_tc_bwd.cu; 128-row q tiles, or 64-row blocks through a 3-stage
-    ring with dQ^T read out by separate warps) against the mma.sync backward on the same inputs:
+def test_attention_tcgen05_backward_matches_mma(case, variant):
+    """tcgen05 backward (attention_tc_bwd.cu; 128-row q tiles, the same with Q / dO double-buffered
+    and P^T in tensor memory, or 64-row blocks through a 3-stage ring with dQ^T read out by separate
+    warps) against the mma.sync backward on the same inputs:
     causal packs, a prefix tree, full ranges with a longer key buffer."""
     from axrl_b200.ops.attention_spec import spec_from_triples
 
@@ -572,12 +573,14 @@ def test_attention_tcgen05_backward_matches_mma(case, blocks64):
         ref = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
     finally:
         e.set_attn_bwd_tc(True)
-    e.set_attn_bwd_blocks64(blocks64)
+    e.set_attn_bwd_blocks64(variant == "blocks64")
+    e.set_attn_bwd_dbl(variant == "dbl")
     try:
         got = e.attn_bwd(do, q, k, v, o, lse, spec.kseg, spec.qr, spec.bwd_tiles, scale, spec.bwd_tiles_tc)
         torch.cuda.synchronize()
     finally:
         e.set_attn_bwd_blocks64(False)
+        e.set_attn_bwd_dbl(False)
     assert e.attn_bwd_tc_error() == 0
     for name, a, b in zip(("dq", "dk", "dv"), got, ref):
         close(a, b, 3e-2, 2e-2, msg=name)
