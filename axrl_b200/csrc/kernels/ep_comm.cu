@@ -30,6 +30,7 @@ namespace epc {
 
 constexpr int kMaxEP = 8;
 constexpr int kMaxTP = 8;
+constexpr int kMaxE = 1024;  // experts per layer
 constexpr int kFreeBase = 16;
 
 struct Peers {
@@ -120,36 +121,60 @@ __global__ void ep_transfer_k(int mode, const uint4* __restrict__ rows, const in
     ok = good;
     if (!good) atomicCAS(status, 0, 1);
   }
+  // row -> (expert / local expert) lookups by binary search over prefix sums staged in shared memory
+  __shared__ int pre[kMaxE + 1];
+  if (threadIdx.x == 0) {
+    if (mode == 0) {  // this rank's sorted rows: exclusive prefix of its per-expert counts
+      int a = 0;
+      for (int e = 0; e < E; ++e) {
+        pre[e] = a;
+        a += C[self * E + e];
+      }
+      pre[E] = a;
+    } else {
+      for (int el = 0; el <= El; ++el) pre[el] = offsets[el];
+    }
+  }
   __syncthreads();
   if (ok) {
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x / 32;
     const long n = mode == 0 ? totals[1] : totals[0];
+    const int nb = mode == 0 ? E : El;
     for (long r = (long)blockIdx.x * warps + threadIdx.x / 32; r < n; r += (long)gridDim.x * warps) {
+      int lo = 0, hi = nb;  // first index with pre[index] > r, minus one: pre[x] <= r < pre[x + 1]
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (pre[mid] <= r) lo = mid + 1;
+        else hi = mid;
+      }
+      const int x = lo - 1;
       int peer;
       long at;
       if (mode == 0) {
-        // global expert of sorted row r: walk this rank's prefix of C (E <= 1024)
-        int e = 0;
-        long acc = 0;
-        while (e < E && acc + C[self * E + e] <= r) acc += C[self * E + e++];
-        peer = e / El;
-        at = dst_start[e] + (r - acc);
+        peer = x / El;
+        at = dst_start[x] + (r - pre[x]);
       } else {
-        int el = 0;
-        while (el + 1 < El && offsets[el + 1] <= r) ++el;
         int s = 0;
-        while (s + 1 < P && blk_pos[el * P + s + 1] <= r) ++s;
+        while (s + 1 < P && blk_pos[x * P + s + 1] <= r) ++s;
         peer = s;
-        at = blk_src[el * P + s] + (r - blk_pos[el * P + s]);
+        at = blk_src[x * P + s] + (r - blk_pos[x * P + s]);
       }
       if (at >= dst_cap_rows) {
         if (lane == 0) atomicCAS(status, 0, 3);
         continue;
       }
-      const uint4* src = rows + (src_idx != nullptr ? src_idx[r] : r) * row16;
-      uint4* out = reinterpret_cast<uint4*>(dst.p[peer]) + at * row16;
-      for (int i = lane; i < row16; i += 32) out[i] = src[i];
+      const uint4* __restrict__ src = rows + (src_idx != nullptr ? src_idx[r] : r) * row16;
+      uint4* __restrict__ out = reinterpret_cast<uint4*>(dst.p[peer]) + at * row16;
+      for (int i0 = 0; i0 < row16; i0 += 8 * 32) {  // eight 16-byte loads in flight per lane, then the stores
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i0 + j * 32 + lane < row16) v[j] = src[i0 + j * 32 + lane];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i0 + j * 32 + lane < row16) out[i0 + j * 32 + lane] = v[j];
+      }
     }
   }
   __threadfence_system();
@@ -179,7 +204,7 @@ void ep_plan(at::Tensor C, int64_t self, at::Tensor offsets, at::Tensor dst_star
              at::Tensor totals) {
   AX_CHECK(C.scalar_type() == at::kInt && C.dim() == 2 && C.is_contiguous(), "C: (P, E) int32");
   int P = C.size(0), E = C.size(1);
-  AX_CHECK(P <= epc::kMaxEP && E % P == 0, "EP shape");
+  AX_CHECK(P <= epc::kMaxEP && E % P == 0 && E <= epc::kMaxE, "EP shape");
   epc::ep_plan_k<<<1, 32, 0, stream()>>>(C.data_ptr<int>(), P, E, (int)self, offsets.data_ptr<int>(), dst_start.data_ptr<int>(),
                                         blk_pos.data_ptr<int>(), blk_src.data_ptr<int>(), totals.data_ptr<int>());
   AX_LAUNCH_OK();
@@ -190,6 +215,7 @@ void ep_transfer(int64_t mode, at::Tensor rows, at::Tensor C, int64_t self, at::
                  at::Tensor my_flags, int64_t ch, int64_t epoch, at::Tensor ticket, int64_t timeout_ns, at::Tensor status, int64_t ctas,
                  c10::optional<at::Tensor> src_idx) {
   AX_CHECK(rows.is_cuda() && rows.is_contiguous() && rows.dim() == 2, "rows");
+  AX_CHECK(C.dim() == 2 && C.size(1) <= epc::kMaxE && C.size(0) <= epc::kMaxEP, "C: (P <= 8, E <= 1024)");
   const int64_t* idx = nullptr;
   if (src_idx.has_value()) {
     AX_CHECK(mode == 0 && src_idx->is_cuda() && src_idx->scalar_type() == at::kLong && src_idx->is_contiguous(), "src_idx: int64 (mode 0)");
