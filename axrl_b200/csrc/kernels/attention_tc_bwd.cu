@@ -169,7 +169,47 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
   QTiles qt{p.qr, it0, it1, G, ks, k0s, 0, it0, 0, 0, 0, 0};
   qt.seek();
 
-  if (warp == 8) {
+  if (warp == 8 && DBL) {
+    // ------------------------------------------------------------ producer (DBL): K/V once, then per q tile
+    // its lse2 / Dsum (the warp's lanes) and Q / dO (TMA) into buffer i & 1
+    if (lane == 0) {
+      mbar_expect_tx(&bar[B_KV], 2 * TILE);
+      tma_2d(sK, &tk, hk * D, ks, &bar[B_KV]);
+      tma_2d(sK + HALF, &tk, hk * D + 64, ks, &bar[B_KV]);
+      tma_2d(sV, &tv, hk * D, ks, &bar[B_KV]);
+      tma_2d(sV + HALF, &tv, hk * D + 64, ks, &bar[B_KV]);
+    }
+    int i = 0;
+    for (; qt.valid(); qt.next(), ++i) {
+      const int b = i & 1;
+      int ok = 1;
+      if (lane == 0 && i >= 2) ok = mbar_wait(&bar[B_EM + b], ((i - 2) >> 1) & 1, abort, p.err, 11);  // buffer b consumed
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int h = hk * G + qt.g, qe = min(qt.qs + BQ, qt.q1);
+      float* L = sL + b * BQ;
+      float* Ds = sDs + b * BQ;
+      for (int c = lane; c < BQ; c += 32) {
+        const bool in = qt.qs + c < qe;
+        L[c] = in ? p.lse2[(long)h * p.T + qt.qs + c] : 0.f;
+        Ds[c] = in ? p.dsum[(long)h * p.T + qt.qs + c] : 0.f;
+      }
+      __syncwarp();  // the stores are ordered before lane 0's arrival on this buffer's barrier
+      if (lane == 0) {
+        uint64_t* qd = &bar[b ? B_QD1 : B_QD];
+        mbar_expect_tx(qd, 2 * TILE);
+        tma_2d(sQ + b * TILE, &tq, h * D, qt.qs, qd);
+        tma_2d(sQ + b * TILE + HALF, &tq, h * D + 64, qt.qs, qd);
+        tma_2d(sdO + b * TILE, &tdo, h * D, qt.qs, qd);
+        tma_2d(sdO + b * TILE + HALF, &tdo, h * D + 64, qt.qs, qd);
+      }
+      __syncwarp();
+    }
+    if (lane == 0 && *abort) {  // every copy this CTA started lands before its shared memory is released
+      int zero = 0;
+      mbar_wait(&bar[B_KV], 0, (volatile int*)&zero, p.err, 11);
+      for (int j = max(0, i - 2); j < i; ++j) mbar_wait(&bar[(j & 1) ? B_QD1 : B_QD], (j >> 1) & 1, (volatile int*)&zero, p.err, 11);
+    }
+  } else if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       mbar_expect_tx(&bar[B_KV], 2 * TILE);
@@ -262,16 +302,17 @@ __global__ void __launch_bounds__(THREADS, 1) attn_bwd_tc_k(const __grid_constan
       // rows with (q - q0) >= (key - k0s)
       const int climit = key < ke ? qe - qs : 0;
       const int cfirst = qt.ty == 1 ? max(0, (key - k0s) - (qs - qt.q0)) : 0;
-      // stage the tile's lse2 / Dsum once (thread (half, r) loads column r of its half's copy)
-      {
+      if constexpr (!DBL) {  // stage the tile's lse2 / Dsum once (thread (half, r) loads column r of its half's copy)
         float* L = sL + (i & 1) * BQ;
         float* Ds = sDs + (i & 1) * BQ;
         if (half == 0) L[r] = qs + r < qe ? p.lse2[(long)h * p.T + qs + r] : 0.f;
         else Ds[r] = qs + r < qe ? p.dsum[(long)h * p.T + qs + r] : 0.f;
         mbar_arrive(&bar[B_LD]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[B_LD], i & 1, abort, p.err, 17))) break;
       }
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar[B_LD], i & 1, abort, p.err, 17))) break;
       if (!__all_sync(0xffffffffu, mbar_wait(&bar[B_S], i & 1, abort, p.err, 15))) break;
+      if constexpr (DBL)  // the producer staged this tile's lse2 / Dsum with buffer i & 1
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[(i & 1) ? B_QD1 : B_QD], (i >> 1) & 1, abort, p.err, 17))) break;
       tc_fence_after();
       const float* L = sL + (i & 1) * BQ;
       const float* Ds = sDs + (i & 1) * BQ;
@@ -699,11 +740,12 @@ static int& bwd_blocks64_flag() {
 }
 static bool bwd_blocks64() { return bwd_blocks64_flag() != 0; }
 void set_attn_bwd_blocks64(bool on) { bwd_blocks64_flag() = on ? 1 : 0; }
-// AXRL_ATTN_BWD_DBL=1: the 128-row kernel with Q / dO double-buffered and P^T in tensor memory.
+// The 128-row kernel runs with Q / dO double-buffered and P^T in tensor memory (468 against 434
+// TFLOP/s single-buffered on the 15 872-token Qwen3-8B pack); AXRL_ATTN_BWD_DBL=0 selects the latter.
 static int& bwd_dbl_flag() {
   static int on = [] {
     const char* e = std::getenv("AXRL_ATTN_BWD_DBL");
-    return (e && std::string(e) == "1") ? 1 : 0;
+    return (e && std::string(e) == "0") ? 0 : 1;
   }();
   return on;
 }

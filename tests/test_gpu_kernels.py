@@ -580,7 +580,7 @@ def test_attention_tcgen05_backward_matches_mma(case, variant):
         torch.cuda.synchronize()
     finally:
         e.set_attn_bwd_blocks64(False)
-        e.set_attn_bwd_dbl(False)
+        e.set_attn_bwd_dbl(True)  # the default
     assert e.attn_bwd_tc_error() == 0
     for name, a, b in zip(("dq", "dk", "dv"), got, ref):
         close(a, b, 3e-2, 2e-2, msg=name)
