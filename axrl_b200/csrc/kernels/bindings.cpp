@@ -66,6 +66,7 @@ void set_streamk_decomposition(int64_t mode, int64_t splits);
 void set_pdl(bool on);
 bool get_pdl();
 void set_weights_static(bool on);
+void set_decode_gemm(std::string mode);
 at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 int64_t skinny_tma_error();
 at::Tensor moe_combine(at::Tensor y, at::Tensor w, at::Tensor pos);
@@ -127,6 +128,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_pdl", &ax::set_pdl);
   m.def("get_pdl", &ax::get_pdl);
   m.def("set_weights_static", &ax::set_weights_static);
+  m.def("set_decode_gemm", &ax::set_decode_gemm, "force the decode GEMM for <= 64 rows: skinny, tma, tcgen05, tcstream, tccluster; \"\" = by shape");
   m.def("moe_combine", &ax::moe_combine);
   m.def("moe_combine_bwd", &ax::moe_combine_bwd);
   m.def("router_topk", &ax::router_topk);

@@ -78,12 +78,14 @@ static void tn(const void* A, const void* B, const void* C, void* D, int M, int 
 // calls): up to 16 activation rows and 64M weight elements the streaming kernels (skinny_gemm.cu,
 // cp.async ring; skinny_tma.cu, TMA ring) beat the tcgen05 swap-AB GEMM by 10-40%; from 32 rows on
 // and for the large gate/up and vocabulary matrices the tcgen05 GEMM streams at least as fast.
-// AXRL_DECODE_GEMM = skinny | tma | tcgen05 | tcstream overrides the choice (tcstream: the
+// AXRL_DECODE_GEMM = skinny | tma | tcgen05 | tcstream | tccluster overrides the choice (tcstream: the
 // hand-written tcgen05 weight-streaming kernel of tcgemm.cu, 1..64 rows).
-enum DecodeGemm { kTcgen05 = 0, kSkinny = 1, kTma = 2, kTcStream = 3 };
+enum DecodeGemm { kTcgen05 = 0, kSkinny = 1, kTma = 2, kTcStream = 3, kTcCluster = 4 };
 
 void tcgemm_stream(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, float* ws, int* cnt, int* err, bool prefetch_w,
                    cudaStream_t st);
+void tcgemm_stream_cluster(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, int* err, bool prefetch_w,
+                           cudaStream_t st);
 
 // Zero-initialised, self-cleaning workspace of the streaming kernel, one per device.
 struct StreamWorkspace {
@@ -108,15 +110,32 @@ static void tc_stream_into(const at::Tensor& x, const at::Tensor& w, const bf16*
                 ws.err.data_ptr<int>(), weights_static(), stream());
 }
 
-static int decode_gemm_mode() {
+static void tc_cluster_into(const at::Tensor& x, const at::Tensor& w, const bf16* r, at::Tensor& y) {
+  const int M = x.size(0), N = w.size(0), K = x.size(1);
+  auto& ws = stream_workspace(x.get_device());
+  tcgemm_stream_cluster(x.data_ptr(), w.data_ptr(), r, y.data_ptr(), M, N, K, ws.err.data_ptr<int>(), weights_static(), stream());
+}
+
+static int parse_decode_gemm(const std::string& v) {
+    return v == "skinny"     ? (int)kSkinny
+           : v == "tma"       ? (int)kTma
+           : v == "tcgen05"   ? (int)kTcgen05
+           : v == "tcstream"  ? (int)kTcStream
+           : v == "tccluster" ? (int)kTcCluster
+                              : -1;
+}
+
+static int& decode_gemm_forced() {
   static int mode = [] {
     const char* e = std::getenv("AXRL_DECODE_GEMM");
-    if (!e) return -1;
-    std::string v(e);
-    return v == "skinny" ? (int)kSkinny : v == "tma" ? (int)kTma : v == "tcgen05" ? (int)kTcgen05 : v == "tcstream" ? (int)kTcStream : -1;
+    return e ? parse_decode_gemm(e) : -1;
   }();
   return mode;
 }
+static int decode_gemm_mode() { return decode_gemm_forced(); }
+
+// Force one decode GEMM for M <= 64 ("" or "auto": choose by shape); tests and benchmarks.
+void set_decode_gemm(std::string mode) { decode_gemm_forced() = parse_decode_gemm(mode); }
 
 // Default by rows: <= 16 rows the cp.async skinny kernel, above CUTLASS swap-AB.  The tcgen05
 // streaming kernel (AXRL_DECODE_GEMM=tcstream) wins in-stream chains of single projections at 32 rows
@@ -126,8 +145,9 @@ static DecodeGemm decode_gemm(int M, int N, int K) {
   const int forced = decode_gemm_mode();
   const bool stream_ok = M <= 64 && K % 64 == 0 && N % 8 == 0 && N <= 262144 && (long)M * N <= 64L * 262144;
   if (forced == kTcStream && stream_ok) return kTcStream;
+  if (forced == kTcCluster && M <= 64 && K % 64 == 0 && N % 8 == 0) return kTcCluster;
   if (M > 16 || K % 64 || N % 8 || (long)N * K > (64L << 20)) return kTcgen05;
-  return forced >= 0 && forced != kTcStream ? (DecodeGemm)forced : kSkinny;
+  return forced >= 0 && forced != kTcStream && forced != kTcCluster ? (DecodeGemm)forced : kSkinny;
 }
 
 static bool streaming_into(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& r, at::Tensor& y) {
@@ -135,6 +155,7 @@ static bool streaming_into(const at::Tensor& x, const at::Tensor& w, const c10::
   const DecodeGemm g = decode_gemm(M, N, K);
   if (g == kTcgen05) return false;
   if (g == kTcStream) tc_stream_into(x, w, r ? (const bf16*)r->data_ptr() : nullptr, y);
+  else if (g == kTcCluster) tc_cluster_into(x, w, r ? (const bf16*)r->data_ptr() : nullptr, y);
   else if (g == kSkinny) skinny_linear_out(x, w, r, y);
   else skinny_tma_linear_out(x, w, r, y);
   return true;
@@ -164,6 +185,10 @@ at::Tensor linear_fwd(at::Tensor x, at::Tensor w) {
       tc_stream_into(x, w, nullptr, y);
       return y;
     }
+    if (decode_gemm(M, N, K) == kTcCluster) {
+      tc_cluster_into(x, w, nullptr, y);
+      return y;
+    }
     if (decode_gemm(M, N, K) == kSkinny) return skinny_linear(x, w, c10::nullopt);
     if (decode_gemm(M, N, K) == kTma) return skinny_tma_linear(x, w, c10::nullopt);
     gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, y.data_ptr(), M, N, K, stream());
@@ -185,6 +210,10 @@ at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual) {
   if (M <= 64) {
     if (decode_gemm(M, N, K) == kTcStream) {
       tc_stream_into(x, w, (const bf16*)residual.data_ptr(), y);
+      return y;
+    }
+    if (decode_gemm(M, N, K) == kTcCluster) {
+      tc_cluster_into(x, w, (const bf16*)residual.data_ptr(), y);
       return y;
     }
     if (decode_gemm(M, N, K) == kSkinny) return skinny_linear(x, w, residual);
@@ -288,6 +317,11 @@ at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant) {
   if (variant == "tcstream") {
     AX_CHECK(M <= 64, "tcstream needs M <= 64");
     tc_stream_into(x, w, nullptr, y);
+    return y;
+  }
+  if (variant == "tccluster") {
+    AX_CHECK(M <= 64, "tccluster needs M <= 64");
+    tc_cluster_into(x, w, nullptr, y);
     return y;
   }
   if (variant == "swapab") {

@@ -720,6 +720,199 @@ __global__ void __launch_bounds__(THREADS, 1) stream_k(const __grid_constant__ C
 }
 }  // namespace sk
 
+// ---------------------------------------------------------------------------------- weight streaming, cluster split-K
+// Same product as stream_k (Y^T tile of 128 weight rows x NTOK tokens = W tile @ X^T on the tensor
+// cores, M <= 64 token rows), on a fixed grid instead of persistent units: CTA (t, s) streams the
+// K slabs [s * per, (s + 1) * per) of weight tile t, and the `splits` CTAs of a tile form one
+// thread-block cluster.  The split-K partials are reduced over distributed shared memory, in a
+// fixed order, so the result is deterministic and there is no workspace, counter or global atomic
+// (a scattered fp32 reduction of M x N x splits values is what limits the persistent kernel at 32-64
+// rows).  Two CTAs fit on an SM, and `splits` is the largest count (<= 8) whose grid is resident in
+// one wave.
+//
+//   warp 0      TMA producer: W slab (128 x 64) + X slab (NTOK x 64) per stage; with `prefetch_w`
+//               the first W slabs are requested before the preceding kernel has finished.
+//   warp 1      TMEM owner and MMA issuer: four tcgen05.mma (M 128, N NTOK, K 16) per slab.
+//   warps 2-5   epilogue: TMEM -> this CTA's fp32 partial in shared memory (token-major rows of
+//               128 floats, over the drained stage ring); after a cluster barrier, cluster rank r
+//               sums its 1/splits share of the tile's M x 128 outputs over every rank's partial
+//               (ld.shared::cluster, ranks in order), adds R and stores bf16.
+//   all         a second cluster barrier keeps every partial alive until its readers are done.
+// Every mbarrier wait is bounded; every thread reaches both cluster barriers whatever happened.
+namespace cs {
+constexpr int BW = 128, BK = 64, THREADS = 192, MAX_SPLITS = 8;
+template <int NTOK>
+constexpr int stages() {
+  return NTOK == 64 ? 4 : 5;
+}
+template <int NTOK>
+constexpr int stage_bytes() {
+  return BW * BK * 2 + NTOK * BK * 2;
+}
+template <int NTOK>
+constexpr int smem_bytes() {
+  return stages<NTOK>() * stage_bytes<NTOK>() + (2 * stages<NTOK>() + 1) * 8 + 16 + 1024;
+}
+
+struct Params {
+  int M, N, K, kslabs, per;
+  const bf16* r;
+  bf16* y;
+  int* err;
+  int prefetch_w;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_cluster4(uint32_t local_addr, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(local_addr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(ra) : "memory");
+  return v;
+}
+
+template <int NTOK>
+__global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
+                                                               Params p) {
+  constexpr int S = stages<NTOK>(), W_BYTES = BW * BK * 2, STAGE = stage_bytes<NTOK>();
+  constexpr uint32_t TCOLS = NTOK < 32 ? 32 : NTOK;
+  constexpr uint32_t IDS = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NTOK >> 3) << 17) | ((uint32_t)(BW >> 4) << 24);
+  static_assert(NTOK * BW * 4 <= S * STAGE, "the partial must fit over the stage ring");
+  extern __shared__ char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + S * STAGE);
+  uint64_t* empty = full + S;
+  uint64_t* acc_bar = full + 2 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 2 * S + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* part = reinterpret_cast<float*>(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int k0 = blockIdx.y * p.per, n_slabs = max(0, min(p.kslabs, k0 + p.per) - k0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      tg::mbar_init(&full[s], 1);
+      tg::mbar_init(&empty[s], 1);
+    }
+    tg::mbar_init(acc_bar, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tg::s32(tmem_slot)), "r"(TCOLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tg::fence_before();
+  __syncthreads();
+  tg::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();  // the successor may be scheduled once every CTA of this grid is resident
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int pre = 0;
+      if (p.prefetch_w) {  // weight slabs do not depend on the preceding kernel
+        pre = min(n_slabs, S);
+        for (int i = 0; i < pre; ++i) {
+          tg::expect_tx(&full[i], STAGE);
+          tg::tma2d(sm + i * STAGE, &tw, (k0 + i) * BK, tile * BW, &full[i]);
+        }
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) tg::tma2d(sm + i * STAGE + W_BYTES, &tx, (k0 + i) * BK, 0, &full[i]);
+      int i = pre;
+      for (; i < n_slabs; ++i) {
+        const int s = i % S;
+        if (i >= S && !tg::wait(&empty[s], ((i / S) - 1) & 1, abort, p.err, 31)) break;
+        tg::expect_tx(&full[s], STAGE);
+        tg::tma2d(sm + s * STAGE, &tw, (k0 + i) * BK, tile * BW, &full[s]);
+        tg::tma2d(sm + s * STAGE + W_BYTES, &tx, (k0 + i) * BK, 0, &full[s]);
+      }
+      if (*abort) {  // let the copies in flight land before the ring is reused or released
+        int zero = 0;
+        for (int k = max(0, i - S); k < i; ++k) tg::wait(&full[k % S], (k / S) & 1, (volatile int*)&zero, p.err, 31);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int i = 0; i < n_slabs; ++i) {
+        const int s = i % S;
+        if (!tg::wait(&full[s], (i / S) & 1, abort, p.err, 32)) break;
+        tg::fence_after();
+        const uint32_t sw = tg::s32(sm + s * STAGE), sx = sw + W_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) tg::mma(tmem, tg::desc_k128(sw + kk * 32), tg::desc_k128(sx + kk * 32), IDS, (i | kk) ? 1u : 0u);
+        tg::commit(&empty[s]);
+      }
+      tg::commit(acc_bar);  // arrives once every MMA issued above has completed
+    }
+  } else {
+    const int q = warp & 3, n = q * 32 + lane;
+    const bool ok = __all_sync(0xffffffffu, tg::wait(acc_bar, 0, abort, p.err, 33)) && n_slabs > 0;
+    tg::fence_after();
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+    for (int c0 = 0; c0 < NTOK; c0 += 32) {
+      uint32_t v[32];
+      tg::tmem_ld32(lane_base + c0, v);
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (c0 + e < NTOK) part[(c0 + e) * BW + n] = ok ? __uint_as_float(v[e]) : 0.f;
+    }
+    tg::fence_before();
+  }
+  __syncwarp();
+  cluster_sync();  // every rank's partial is complete and visible
+
+  pdl_wait();  // R may be written and Y read by earlier kernels
+  {
+    const uint32_t rank = cluster_rank(), ranks = cluster_size();
+    const int groups = p.M * (BW / 4), share = (groups + (int)ranks - 1) / (int)ranks;
+    const int g0 = (int)rank * share, g1 = min(groups, g0 + share);
+    const uint32_t pbase = tg::s32(part);
+    for (int g = g0 + threadIdx.x; g < g1; g += THREADS) {
+      const int t = g / (BW / 4), c = (g % (BW / 4)) * 4, n = tile * BW + c;
+      if (n >= p.N) continue;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (uint32_t r = 0; r < ranks; ++r) {
+        const float4 b = ld_cluster4(pbase + (uint32_t)((t * BW + c) * 4), r);
+        a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+      }
+      const long at = (long)t * p.N + n;
+      if (p.r) {
+        const uint2 rr = *reinterpret_cast<const uint2*>(p.r + at);
+        const float2 r0 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&rr.x));
+        const float2 r1 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&rr.y));
+        a.x += r0.x, a.y += r0.y, a.z += r1.x, a.w += r1.y;
+      }
+      bf162 o0 = __floats2bfloat162_rn(a.x, a.y), o1 = __floats2bfloat162_rn(a.z, a.w);
+      uint2 ov;
+      ov.x = *reinterpret_cast<uint32_t*>(&o0);
+      ov.y = *reinterpret_cast<uint32_t*>(&o1);
+      *reinterpret_cast<uint2*>(p.y + at) = ov;
+    }
+  }
+  cluster_sync();  // no partial is released while another rank may still read it
+  if (warp == 1) {
+    tg::fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
+  }
+}
+}  // namespace cs
+
 // ---------------------------------------------------------------------------------- host side
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
@@ -815,6 +1008,65 @@ static void launch_stream(const void* X, const void* W, const void* R, void* Y, 
   launch_pdl(sk::stream_k<NTOK>, dim3((p.units + p.per - 1) / p.per), dim3(sk::THREADS), (size_t)smem, st, tw, tx, p);
 }
 
+
+// Largest split count (<= 8, <= K slabs) whose (tiles x splits) grid of clusters is resident in one
+// wave; 1 when even single-CTA tiles need several waves (large matrices).
+template <int NTOK>
+static int cluster_splits(int n_tiles, int kslabs) {
+  static std::mutex mu;
+  static int fit[64][cs::MAX_SPLITS + 1] = {};  // clusters resident at once, per device and split count
+  int dev = 0;
+  AX_CUDA_OK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> g(mu);
+  for (int s = std::min(cs::MAX_SPLITS, kslabs); s >= 1; --s) {
+    if (!fit[dev][s]) {
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = s, attr[0].val.clusterDim.z = 1;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, s, 1);
+      cfg.blockDim = dim3(cs::THREADS);
+      cfg.dynamicSmemBytes = cs::smem_bytes<NTOK>();
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      AX_CUDA_OK(cudaOccupancyMaxActiveClusters(&n, cs::stream_cluster_k<NTOK>, &cfg));
+      fit[dev][s] = std::max(n, 1);
+    }
+    if (n_tiles <= fit[dev][s]) return s;
+  }
+  return 1;
+}
+
+template <int NTOK>
+static void launch_stream_cluster(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, int* err, bool prefetch_w,
+                                  cudaStream_t st) {
+  const int smem = cs::smem_bytes<NTOK>();
+  smem_attr(reinterpret_cast<const void*>(cs::stream_cluster_k<NTOK>), smem);
+  const CUtensorMap tw = kmajor_map(W, N, K, cs::BW);
+  const CUtensorMap tx = kmajor_map(X, M, K, NTOK);
+  cs::Params p{};
+  p.M = M, p.N = N, p.K = K, p.kslabs = K / cs::BK;
+  const int n_tiles = (N + cs::BW - 1) / cs::BW;
+  int splits = cluster_splits<NTOK>(n_tiles, p.kslabs);
+  p.per = (p.kslabs + splits - 1) / splits;
+  splits = (p.kslabs + p.per - 1) / p.per;  // every split covers at least one slab
+  p.r = static_cast<const bf16*>(R), p.y = static_cast<bf16*>(Y), p.err = err, p.prefetch_w = prefetch_w ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = splits, attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_tiles, splits, 1);
+  cfg.blockDim = dim3(cs::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  AX_CUDA_OK(cudaLaunchKernelEx(&cfg, cs::stream_cluster_k<NTOK>, tw, tx, p));
+}
+
 }  // namespace tg
 
 // Decode-size GEMM (M <= 64 rows) streaming the weights on the tensor cores.  ws: M x N fp32 and
@@ -825,6 +1077,20 @@ void tcgemm_stream(const void* X, const void* W, const void* R, void* Y, int M, 
   AX_REQUIRE(K % 64 == 0 && N % 8 == 0, "tcgemm_stream: K multiple of 64, N multiple of 8");
   if (M <= 32) tg::launch_stream<32>(X, W, R, Y, M, N, K, ws, cnt, err, prefetch_w, st);
   else tg::launch_stream<64>(X, W, R, Y, M, N, K, ws, cnt, err, prefetch_w, st);
+}
+
+// Decode-size GEMM (M <= 64 rows) streaming the weights on the tensor cores, split-K partials
+// reduced inside a thread-block cluster (deterministic; no workspace).  Y and R: 8-byte aligned.
+void tcgemm_stream_cluster(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, int* err, bool prefetch_w,
+                           cudaStream_t st) {
+  AX_REQUIRE(M >= 1 && M <= 64, "tcgemm_stream_cluster: 1..64 rows, got ", M);
+  AX_REQUIRE(K % 64 == 0 && N % 8 == 0, "tcgemm_stream_cluster: K multiple of 64, N multiple of 8");
+  AX_REQUIRE(reinterpret_cast<uintptr_t>(X) % 16 == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0 && reinterpret_cast<uintptr_t>(Y) % 8 == 0 &&
+                 reinterpret_cast<uintptr_t>(R) % 8 == 0,
+             "tcgemm_stream_cluster: operand alignment");
+  if (M <= 16) tg::launch_stream_cluster<16>(X, W, R, Y, M, N, K, err, prefetch_w, st);
+  else if (M <= 32) tg::launch_stream_cluster<32>(X, W, R, Y, M, N, K, err, prefetch_w, st);
+  else tg::launch_stream_cluster<64>(X, W, R, Y, M, N, K, err, prefetch_w, st);
 }
 
 // D[M,N] (+)= A[M,K] @ B[N,K]^T (+ C), bf16; err: device int that records a wait timeout.

@@ -670,6 +670,32 @@ def test_tcgemm_stream_matches_fp32(M, N, K):
         close(y2, ref + r.float(), 3e-2, 1e-2, msg=f"tcstream + residual call {it}")
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (8, 6144, 4096), (16, 1000, 512), (17, 6144, 4096), (32, 4096, 12288),
+                                   (48, 24576, 4096), (64, 4096, 64), (64, 50000, 1024)])
+def test_tcgemm_stream_cluster_matches_fp32(M, N, K):
+    """Decode-size GEMM streaming the weights on tcgen05 with the split-K partials reduced inside a
+    thread-block cluster: against fp32, with and without the residual, bit-identical across calls."""
+    e = _ext()
+    torch.manual_seed(M * 5 + N)
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    e.set_decode_gemm("tccluster")
+    try:
+        for it in range(2):
+            x = torch.randn(M, K, device=DEV).bfloat16()
+            r = torch.randn(M, N, device=DEV).bfloat16()
+            ref = x.float() @ w.float().t()
+            y = e.linear_fwd(x, w)
+            y_again = e.linear_fwd(x, w)
+            y2 = e.linear_residual(x, w, r)
+            torch.cuda.synchronize()
+            assert e.tc_stream_error() == 0
+            close(y, ref, 2e-2, 1e-2, msg=f"tccluster call {it}")
+            close(y2, ref + r.float(), 3e-2, 1e-2, msg=f"tccluster + residual call {it}")
+            assert torch.equal(y, y_again), "cluster reduction must be deterministic"
+    finally:
+        e.set_decode_gemm("")
+
+
 @pytest.mark.parametrize("M,N,K", [(512, 256, 128), (1000, 4096, 1024), (4096, 6144, 4096), (777, 512, 96)])
 def test_tcgemm_dgrad_wgrad_match_fp32(M, N, K):
     """Data gradient (W read MN-major) and fp32 weight-gradient accumulation (both operands MN-major,
