@@ -74,12 +74,11 @@ static void tn(const void* A, const void* B, const void* C, void* D, int M, int 
   else gemm::tn_narrow_sk(A, B, C, D, M, N, K, stream());
 }
 
-// Decode-size GEMMs are reads of the weight matrix.  Measured on B200 (bf16, L2 flushed between
-// calls): up to 16 activation rows and 64M weight elements the streaming kernels (skinny_gemm.cu,
-// cp.async ring; skinny_tma.cu, TMA ring) beat the tcgen05 swap-AB GEMM by 10-40%; from 32 rows on
-// and for the large gate/up and vocabulary matrices the tcgen05 GEMM streams at least as fast.
-// AXRL_DECODE_GEMM = skinny | tma | tcgen05 | tcstream | tccluster overrides the choice (tcstream: the
-// hand-written tcgen05 weight-streaming kernel of tcgemm.cu, 1..64 rows).
+// Decode-size GEMMs are reads of the weight matrix.  Kernels for <= 64 activation rows: the
+// cluster split-K tcgen05 streaming kernel (tcgemm.cu, stream_cluster_k), the persistent tcgen05
+// streaming kernel (tcgemm.cu, stream_k), the cp.async / TMA mma.sync streaming kernels for <= 16
+// rows (skinny_gemm.cu, skinny_tma.cu) and CUTLASS swap-AB (gemm_tn_swapab.cu).
+// AXRL_DECODE_GEMM = skinny | tma | tcgen05 | tcstream | tccluster (or set_decode_gemm) forces one.
 enum DecodeGemm { kTcgen05 = 0, kSkinny = 1, kTma = 2, kTcStream = 3, kTcCluster = 4 };
 
 void tcgemm_stream(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, float* ws, int* cnt, int* err, bool prefetch_w,
@@ -137,17 +136,23 @@ static int decode_gemm_mode() { return decode_gemm_forced(); }
 // Force one decode GEMM for M <= 64 ("" or "auto": choose by shape); tests and benchmarks.
 void set_decode_gemm(std::string mode) { decode_gemm_forced() = parse_decode_gemm(mode); }
 
-// Default by rows: <= 16 rows the cp.async skinny kernel, above CUTLASS swap-AB.  The tcgen05
-// streaming kernel (AXRL_DECODE_GEMM=tcstream) wins in-stream chains of single projections at 32 rows
-// (qkv 19.0, o 16.0, down 26.4 us against 21.7 / 21.4 / 32.8) but not the whole Qwen3-8B decode step
-// (batch 32: 7.10 vs 6.88 ms), so it stays opt-in.
+// Default (in-stream chains of 48 distinct weight matrices, Qwen3-8B projections): the cluster
+// split-K tcgen05 kernel for every matrix up to 128M elements at 1..64 rows (at 48 rows qkv 17.7,
+// o 12.0, gate/up 42.3, down 24.6 us against 23.0 / 23.0 / 44.2 / 34.2 for CUTLASS swap-AB; at 8
+// rows 15.1 / 10.6 / 37.9 / 21.8 against the skinny kernel's 16.4 / 9.5 / 40.1 / 24.7), the skinny
+// kernel for matrices up to 16M elements at <= 16 rows, CUTLASS swap-AB for the vocabulary
+// projection (151936 x 4096: 195-203 us against 199-223).
 static DecodeGemm decode_gemm(int M, int N, int K) {
   const int forced = decode_gemm_mode();
-  const bool stream_ok = M <= 64 && K % 64 == 0 && N % 8 == 0 && N <= 262144 && (long)M * N <= 64L * 262144;
+  const bool shape_ok = M <= 64 && K % 64 == 0 && N % 8 == 0;
+  const bool stream_ok = shape_ok && N <= 262144 && (long)M * N <= 64L * 262144;
   if (forced == kTcStream && stream_ok) return kTcStream;
-  if (forced == kTcCluster && M <= 64 && K % 64 == 0 && N % 8 == 0) return kTcCluster;
-  if (M > 16 || K % 64 || N % 8 || (long)N * K > (64L << 20)) return kTcgen05;
-  return forced >= 0 && forced != kTcStream && forced != kTcCluster ? (DecodeGemm)forced : kSkinny;
+  if (forced == kTcCluster && shape_ok) return kTcCluster;
+  if (forced == kTcgen05) return kTcgen05;
+  if ((forced == kSkinny || forced == kTma) && M <= 16 && shape_ok && (long)N * K <= (64L << 20)) return (DecodeGemm)forced;
+  if (M <= 16 && shape_ok && (long)N * K <= (16L << 20)) return kSkinny;
+  if (shape_ok && (long)N * K <= (128L << 20)) return kTcCluster;
+  return kTcgen05;
 }
 
 static bool streaming_into(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& r, at::Tensor& y) {

@@ -464,7 +464,7 @@ def test_skinny_tma_gemm_matches_fp32(M):
     assert e.skinny_tma_error() == 0
 
 
-@pytest.mark.parametrize("variant", ["skinny", "tma"])
+@pytest.mark.parametrize("variant", ["skinny", "tma", "tccluster"])
 def test_decode_gemm_chain_with_programmatic_launch(variant):
     """Decode-size GEMMs launched with programmatic dependent launch and early weight loads: each
     GEMM must read the activation its predecessor (RMSNorm) just wrote, add the residual that an
@@ -478,8 +478,10 @@ def test_decode_gemm_chain_with_programmatic_launch(variant):
     g = torch.ones(H, device=DEV).bfloat16()
     e.set_pdl(True)
     e.set_weights_static(True)
+    if variant == "tccluster":
+        e.set_decode_gemm("tccluster")
     try:
-        for M in (1, 8, 13):
+        for M in (1, 8, 13) + ((40, 64) if variant == "tccluster" else ()):
             h = torch.randn(M, H, device=DEV).bfloat16()
             for _ in range(4):
                 x = e.rmsnorm_fwd(h, g, 1e-6)[0]
@@ -496,8 +498,9 @@ def test_decode_gemm_chain_with_programmatic_launch(variant):
                 h = h2
     finally:
         e.set_weights_static(False)
+        e.set_decode_gemm("")
     torch.cuda.synchronize()
-    assert e.skinny_tma_error() == 0
+    assert e.skinny_tma_error() == 0 and e.tc_stream_error() == 0
 
 
 @pytest.mark.parametrize("variant", [0, 2, 3, 4,
