@@ -16,7 +16,7 @@ import torch
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--variants", default="auto,tma,skinny,swapab,cutlass,tcgemm,tcstream")
+    ap.add_argument("--variants", default="auto,tma,skinny,swapab,cutlass,tcgemm,tcstream,tccluster")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--sweep-decomp", action="store_true", help="skinny shapes under every stream-K decomposition")
     ap.add_argument("--bwd", action="store_true", help="data- and weight-gradient GEMMs: CUTLASS vs the hand-written kernel")
@@ -46,7 +46,7 @@ def main() -> None:
             for v in a.variants.split(","):
                 if v == "skinny" and M > 64:
                     continue
-                if (v in ("swapab", "tcstream", "tccluster") and M > 64) or (v == "tma" and M > 32):
+                if (v in ("swapab", "tcstream") and M > 64) or (v == "tccluster" and M > 128) or (v == "tma" and M > 32):
                     continue
                 try:
                     if v == "auto":
@@ -93,7 +93,7 @@ def bench_chain(a) -> None:  # noqa: ANN001
                 x = torch.randn(M, K, device="cuda").bfloat16()
                 res = {"M": M, "shape": name, "N": N, "K": K, "chain": n}
                 for v in a.variants.split(","):
-                    if (v in ("skinny", "swapab", "tcstream", "tccluster") and M > 64) or (v == "tma" and M > 32):
+                    if (v in ("skinny", "swapab", "tcstream") and M > 64) or (v == "tccluster" and M > 128) or (v == "tma" and M > 32):
                         continue
                     try:
                         if v == "auto":

@@ -147,7 +147,9 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
 // predecessor grid has completed and its writes are visible.  Only reads of data that no recent
 // kernel writes (weights during a rollout, see weights_static()) may be issued before it.  Every
 // kernel launched this way waits unconditionally, so a grid completes only after its predecessor,
-// and ordering stays transitive along the stream.
+// and ordering stays transitive along the stream.  Kernels on the decode path trigger before they
+// wait: a successor then becomes resident as soon as SM room frees up and streams its weights during
+// the tail of this grid and its predecessor (its own pdl_wait() still orders every dependent access).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -67,6 +67,8 @@ void set_pdl(bool on);
 bool get_pdl();
 void set_weights_static(bool on);
 void set_decode_gemm(std::string mode);
+at::Tensor linear_rms_stream(at::Tensor h, at::Tensor g, double eps, at::Tensor w, c10::optional<at::Tensor> residual);
+at::Tensor linear_swiglu_stream(at::Tensor gu, at::Tensor w, c10::optional<at::Tensor> residual);
 at::Tensor skinny_tma_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 int64_t skinny_tma_error();
 at::Tensor moe_combine(at::Tensor y, at::Tensor w, at::Tensor pos);
@@ -128,6 +130,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_pdl", &ax::set_pdl);
   m.def("get_pdl", &ax::get_pdl);
   m.def("set_weights_static", &ax::set_weights_static);
+  m.def("linear_rms_stream", &ax::linear_rms_stream, "RMSNorm(h) @ w^T (+ residual), <= 64 rows, norm folded into the streaming GEMM",
+        py::arg("h"), py::arg("g"), py::arg("eps"), py::arg("w"), py::arg("residual") = py::none());
+  m.def("linear_swiglu_stream", &ax::linear_swiglu_stream, "SwiGLU(gu) @ w^T (+ residual), <= 64 rows, activation folded into the streaming GEMM",
+        py::arg("gu"), py::arg("w"), py::arg("residual") = py::none());
   m.def("set_decode_gemm", &ax::set_decode_gemm, "force the decode GEMM for <= 64 rows: skinny, tma, tcgen05, tcstream, tccluster; \"\" = by shape");
   m.def("moe_combine", &ax::moe_combine);
   m.def("moe_combine_bwd", &ax::moe_combine_bwd);

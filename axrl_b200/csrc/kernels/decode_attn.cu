@@ -223,8 +223,8 @@ __global__ void __launch_bounds__(128) decode_k(Params p) {
 // same count in 512-token chunks (the items of the TMA-fed kernel).  Computed once per decode
 // step and shared by every layer.
 __global__ void decode_plan_k(const int* __restrict__ seq_lens, int B, int* __restrict__ prefix, int chunks) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int acc = 0, acc4 = 0;
   for (int b = 0; b < B; ++b) {
@@ -242,8 +242,8 @@ __global__ void decode_plan_k(const int* __restrict__ seq_lens, int B, int* __re
 // Persistent grid sized to the SMs: each CTA walks work items (kv head fastest), so the launch
 // costs the live work only, not B x Hkv x (capacity / SPLIT) mostly-empty CTAs.
 __global__ void __launch_bounds__(128) decode_persist_k(Params p, const int* __restrict__ prefix, int B) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   extern __shared__ __align__(128) char smem[];
   const int total = prefix[B] * p.Hkv;
   for (int w = blockIdx.x; w < total; w += gridDim.x) {
@@ -262,8 +262,8 @@ __global__ void __launch_bounds__(128) decode_persist_k(Params p, const int* __r
 // out[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s ; one warp per (b, h)
 __global__ void combine_k(const float* __restrict__ part_o, const float* __restrict__ part_ml, const int* __restrict__ seq_lens,
                           bf16* __restrict__ out, int B, int Hq, int splits, int max_len) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (w >= B * Hq) return;
   int b = w / Hq;
@@ -314,8 +314,8 @@ __global__ void decode_advance_k(int B, const int64_t* __restrict__ out_tok, con
                                  const int* __restrict__ stop_on_eos, int64_t eos, int64_t* __restrict__ forced,
                                  int64_t* __restrict__ ring_tok, float* __restrict__ ring_lp, int* __restrict__ ring_step,
                                  int ring_cap, int ring_ld, int64_t scratch_slot, int64_t* __restrict__ seed) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   __shared__ int step;
   if (threadIdx.x == 0) step = ring_step[0];
   __syncthreads();

@@ -163,6 +163,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_tma_k(const __grid_constant
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  pdl_trigger();  // successors (the output projection) may become resident and stream weights now
 
   if (warp == CW) {
     // ---------------------------------------------------------------- producer

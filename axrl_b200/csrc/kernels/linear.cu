@@ -84,7 +84,7 @@ enum DecodeGemm { kTcgen05 = 0, kSkinny = 1, kTma = 2, kTcStream = 3, kTcCluster
 void tcgemm_stream(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, float* ws, int* cnt, int* err, bool prefetch_w,
                    cudaStream_t st);
 void tcgemm_stream_cluster(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, int* err, bool prefetch_w,
-                           cudaStream_t st);
+                           cudaStream_t st, int xmode, const void* g, float eps);
 
 // Zero-initialised, self-cleaning workspace of the streaming kernel, one per device.
 struct StreamWorkspace {
@@ -112,7 +112,49 @@ static void tc_stream_into(const at::Tensor& x, const at::Tensor& w, const bf16*
 static void tc_cluster_into(const at::Tensor& x, const at::Tensor& w, const bf16* r, at::Tensor& y) {
   const int M = x.size(0), N = w.size(0), K = x.size(1);
   auto& ws = stream_workspace(x.get_device());
-  tcgemm_stream_cluster(x.data_ptr(), w.data_ptr(), r, y.data_ptr(), M, N, K, ws.err.data_ptr<int>(), weights_static(), stream());
+  tcgemm_stream_cluster(x.data_ptr(), w.data_ptr(), r, y.data_ptr(), M, N, K, ws.err.data_ptr<int>(), weights_static(), stream(), 0, nullptr,
+                        0.f);
+}
+
+// Decode projections with the preceding element-wise step folded into the weight-streaming GEMM
+// (<= 128 rows): y = RMSNorm(h; g, eps) @ w^T (+ residual), and y = SwiGLU(gu) @ w^T (+ residual)
+// with gu = [gate | up] of width 2K.  The normalised / activated rows are never written to memory.
+at::Tensor linear_rms_stream(at::Tensor h, at::Tensor g, double eps, at::Tensor w, c10::optional<at::Tensor> residual) {
+  check_bf16_2d(h, "h");
+  check_bf16_2d(w, "w");
+  const int M = h.size(0), K = h.size(1), N = w.size(0);
+  AX_CHECK(w.size(1) == K && g.numel() == K && g.scalar_type() == at::kBFloat16 && g.is_contiguous(), "linear_rms_stream: shapes");
+  AX_CHECK(M >= 1 && M <= 128 && K % 64 == 0 && N % 8 == 0, "linear_rms_stream: 1..128 rows, K % 64 == 0, N % 8 == 0");
+  const bf16* r = nullptr;
+  if (residual.has_value()) {
+    check_bf16_2d(*residual, "residual");
+    AX_CHECK(residual->size(0) == M && residual->size(1) == N, "residual shape");
+    r = (const bf16*)residual->data_ptr();
+  }
+  auto y = at::empty({M, N}, h.options());
+  auto& ws = stream_workspace(h.get_device());
+  tcgemm_stream_cluster(h.data_ptr(), w.data_ptr(), r, y.data_ptr(), M, N, K, ws.err.data_ptr<int>(), weights_static(), stream(), 1,
+                        g.data_ptr(), (float)eps);
+  return y;
+}
+
+at::Tensor linear_swiglu_stream(at::Tensor gu, at::Tensor w, c10::optional<at::Tensor> residual) {
+  check_bf16_2d(gu, "gu");
+  check_bf16_2d(w, "w");
+  const int M = gu.size(0), K = gu.size(1) / 2, N = w.size(0);
+  AX_CHECK(gu.size(1) == 2 * K && w.size(1) == K, "linear_swiglu_stream: gu is [M, 2K], w is [N, K]");
+  AX_CHECK(M >= 1 && M <= 128 && K % 64 == 0 && N % 8 == 0, "linear_swiglu_stream: 1..128 rows, K % 64 == 0, N % 8 == 0");
+  const bf16* r = nullptr;
+  if (residual.has_value()) {
+    check_bf16_2d(*residual, "residual");
+    AX_CHECK(residual->size(0) == M && residual->size(1) == N, "residual shape");
+    r = (const bf16*)residual->data_ptr();
+  }
+  auto y = at::empty({M, N}, gu.options());
+  auto& ws = stream_workspace(gu.get_device());
+  tcgemm_stream_cluster(gu.data_ptr(), w.data_ptr(), r, y.data_ptr(), M, N, K, ws.err.data_ptr<int>(), weights_static(), stream(), 2,
+                        nullptr, 0.f);
+  return y;
 }
 
 static int parse_decode_gemm(const std::string& v) {
@@ -137,21 +179,21 @@ static int decode_gemm_mode() { return decode_gemm_forced(); }
 void set_decode_gemm(std::string mode) { decode_gemm_forced() = parse_decode_gemm(mode); }
 
 // Default (in-stream chains of 48 distinct weight matrices, Qwen3-8B projections): the cluster
-// split-K tcgen05 kernel for every matrix up to 128M elements at 1..64 rows (at 48 rows qkv 17.7,
+// split-K tcgen05 kernel for every matrix up to 128M elements at 1..128 rows (at 48 rows qkv 17.7,
 // o 12.0, gate/up 42.3, down 24.6 us against 23.0 / 23.0 / 44.2 / 34.2 for CUTLASS swap-AB; at 8
 // rows 15.1 / 10.6 / 37.9 / 21.8 against the skinny kernel's 16.4 / 9.5 / 40.1 / 24.7), the skinny
 // kernel for matrices up to 16M elements at <= 16 rows, CUTLASS swap-AB for the vocabulary
 // projection (151936 x 4096: 195-203 us against 199-223).
 static DecodeGemm decode_gemm(int M, int N, int K) {
   const int forced = decode_gemm_mode();
-  const bool shape_ok = M <= 64 && K % 64 == 0 && N % 8 == 0;
-  const bool stream_ok = shape_ok && N <= 262144 && (long)M * N <= 64L * 262144;
+  const bool aligned = K % 64 == 0 && N % 8 == 0;
+  const bool stream_ok = M <= 64 && aligned && N <= 262144 && (long)M * N <= 64L * 262144;
   if (forced == kTcStream && stream_ok) return kTcStream;
-  if (forced == kTcCluster && shape_ok) return kTcCluster;
+  if (forced == kTcCluster && M <= 128 && aligned) return kTcCluster;
   if (forced == kTcgen05) return kTcgen05;
-  if ((forced == kSkinny || forced == kTma) && M <= 16 && shape_ok && (long)N * K <= (64L << 20)) return (DecodeGemm)forced;
-  if (M <= 16 && shape_ok && (long)N * K <= (16L << 20)) return kSkinny;
-  if (shape_ok && (long)N * K <= (128L << 20)) return kTcCluster;
+  if ((forced == kSkinny || forced == kTma) && M <= 16 && aligned && (long)N * K <= (64L << 20)) return (DecodeGemm)forced;
+  if (M <= 16 && aligned && (long)N * K <= (16L << 20)) return kSkinny;
+  if (M <= 128 && aligned && (long)N * K <= (128L << 20)) return kTcCluster;
   return kTcgen05;
 }
 
@@ -185,6 +227,10 @@ at::Tensor linear_fwd(at::Tensor x, at::Tensor w) {
   auto y = at::empty({M, N}, x.options());
   if (M == 0 || N == 0) return y;
   if (K == 0) return y.zero_();
+  if (M <= 128 && M > 64 && decode_gemm(M, N, K) == kTcCluster) {  // decode at 65..128 rows
+    tc_cluster_into(x, w, nullptr, y);
+    return y;
+  }
   if (M <= 64) {  // decode: weight streaming
     if (decode_gemm(M, N, K) == kTcStream) {
       tc_stream_into(x, w, nullptr, y);
@@ -212,6 +258,10 @@ at::Tensor linear_residual(at::Tensor x, at::Tensor w, at::Tensor residual) {
   AX_CHECK(residual.size(0) == M && residual.size(1) == N, "residual shape");
   auto y = at::empty({M, N}, x.options());
   if (M == 0 || N == 0) return y;
+  if (M <= 128 && M > 64 && decode_gemm(M, N, K) == kTcCluster) {
+    tc_cluster_into(x, w, (const bf16*)residual.data_ptr(), y);
+    return y;
+  }
   if (M <= 64) {
     if (decode_gemm(M, N, K) == kTcStream) {
       tc_stream_into(x, w, (const bf16*)residual.data_ptr(), y);
@@ -238,6 +288,10 @@ void linear_fwd_into(at::Tensor x, at::Tensor w, at::Tensor out) {
   int M = x.size(0), N = w.size(0), K = x.size(1);
   AX_CHECK(out.size(0) == M && out.size(1) == N && w.size(1) == K, "shapes");
   if (M == 0 || N == 0) return;
+  if (M <= 128 && M > 64 && decode_gemm(M, N, K) == kTcCluster) {
+    tc_cluster_into(x, w, nullptr, out);
+    return;
+  }
   if (M <= 64) {
     if (streaming_into(x, w, c10::nullopt, out)) return;
     gemm::tn_swapab(x.data_ptr(), w.data_ptr(), nullptr, out.data_ptr(), M, N, K, stream());
@@ -325,7 +379,7 @@ at::Tensor linear_variant(at::Tensor x, at::Tensor w, std::string variant) {
     return y;
   }
   if (variant == "tccluster") {
-    AX_CHECK(M <= 64, "tccluster needs M <= 64");
+    AX_CHECK(M <= 128, "tccluster needs M <= 128");
     tc_cluster_into(x, w, nullptr, y);
     return y;
   }

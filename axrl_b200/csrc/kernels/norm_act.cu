@@ -9,8 +9,8 @@ namespace ax {
 // One CTA per row; row re-read from L1/L2 on the second pass.
 __global__ void rmsnorm_fwd_k(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ y,
                               float* __restrict__ rstd, int H, float eps) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   __shared__ float sh[32];
   const bf16* xr = x + (size_t)blockIdx.x * H;
   bf16* yr = y + (size_t)blockIdx.x * H;
@@ -117,8 +117,8 @@ __global__ void qknorm_rope_fwd_k(const bf16* __restrict__ qkv, const bf16* __re
                                   bf16* __restrict__ q, bf16* __restrict__ k, bf16* __restrict__ v,
                                   float* __restrict__ rstd, int T, int nq, int nkv, float eps,
                                   bf16* __restrict__ kc, bf16* __restrict__ vc, const int64_t* __restrict__ slots, int P) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   constexpr int D = 128;
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
@@ -309,8 +309,8 @@ std::vector<at::Tensor> qknorm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor
 __device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
 
 __global__ void swiglu_fwd_k(const bf16* __restrict__ gu, bf16* __restrict__ y, long T, int F) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   long n8 = T * (F / 8);
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
     long t = i / (F / 8);

@@ -80,8 +80,8 @@ __global__ void __launch_bounds__(THREADS) skinny_k(Params p) {
     for (int s = 0; s < STAGES - 1; ++s)
       if (s < nk) load_w(s, s);
   }
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
     if (s < nk) {

@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_k(const __grid_constant__ C
 
 // ---------------------------------------------------------------------------------- weight streaming, cluster split-K
 // Same product as stream_k (Y^T tile of 128 weight rows x NTOK tokens = W tile @ X^T on the tensor
-// cores, M <= 64 token rows), on a fixed grid instead of persistent units: CTA (t, s) streams the
+// cores, M <= 128 token rows), on a fixed grid instead of persistent units: CTA (t, s) streams the
 // K slabs [s * per, (s + 1) * per) of weight tile t, and the `splits` CTAs of a tile form one
 // thread-block cluster.  The split-K partials are reduced over distributed shared memory, in a
 // fixed order, so the result is deterministic and there is no workspace, counter or global atomic
@@ -741,17 +741,26 @@ __global__ void __launch_bounds__(THREADS, 1) stream_k(const __grid_constant__ C
 // Every mbarrier wait is bounded; every thread reaches both cluster barriers whatever happened.
 namespace cs {
 constexpr int BW = 128, BK = 64, THREADS = 192, MAX_SPLITS = 8;
-template <int NTOK>
-constexpr int stages() {
-  return NTOK == 64 ? 4 : 5;
-}
-template <int NTOK>
+// Input transform applied to each X slab in shared memory before its MMAs (warps 2-5):
+//   X_PLAIN   none;
+//   X_RMS     X = RMSNorm(H) with weight g: the slab becomes bf16(H * g) and the per-token sums of
+//             squares are accumulated; the token's 1/rms scales its outputs after the cluster
+//             reduction (the MMA is linear in each token row), so the normalised activation is never
+//             written to memory;
+//   X_SWIGLU  X = silu(G) * U from the fused gate/up activation [M, 2K] (gate columns [0, K), up
+//             columns [K, 2K)); both slabs are loaded and the product replaces the gate slab.
+enum XMode { X_PLAIN = 0, X_RMS = 1, X_SWIGLU = 2 };
+template <int NTOK, int XM>
 constexpr int stage_bytes() {
-  return BW * BK * 2 + NTOK * BK * 2;
+  return BW * BK * 2 + NTOK * BK * 2 * (XM == X_SWIGLU ? 2 : 1);
 }
-template <int NTOK>
+template <int NTOK, int XM>
+constexpr int stages() {
+  return (100 * 1024) / stage_bytes<NTOK, XM>() < 5 ? (100 * 1024) / stage_bytes<NTOK, XM>() : 5;
+}
+template <int NTOK, int XM>
 constexpr int smem_bytes() {
-  return stages<NTOK>() * stage_bytes<NTOK>() + (2 * stages<NTOK>() + 1) * 8 + 16 + 1024;
+  return stages<NTOK, XM>() * stage_bytes<NTOK, XM>() + (3 * stages<NTOK, XM>() + 1) * 8 + 16 + 5 * NTOK * 4 + 1024;
 }
 
 struct Params {
@@ -760,6 +769,8 @@ struct Params {
   bf16* y;
   int* err;
   int prefetch_w;
+  const bf16* g;  // X_RMS: norm weight [K]
+  float eps;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -775,28 +786,43 @@ __device__ __forceinline__ uint32_t cluster_size() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
 }
-__device__ __forceinline__ float4 ld_cluster4(uint32_t local_addr, uint32_t rank) {
+__device__ __forceinline__ uint32_t map_rank(uint32_t local_addr, uint32_t rank) {
   uint32_t ra;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(local_addr), "r"(rank));
+  return ra;
+}
+__device__ __forceinline__ float4 ld_cluster4(uint32_t local_addr, uint32_t rank) {
+  const uint32_t ra = map_rank(local_addr, rank);
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(ra) : "memory");
   return v;
 }
+__device__ __forceinline__ float ld_cluster1(uint32_t local_addr, uint32_t rank) {
+  const uint32_t ra = map_rank(local_addr, rank);
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
 
-template <int NTOK>
+template <int NTOK, int XM>
 __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
                                                                Params p) {
-  constexpr int S = stages<NTOK>(), W_BYTES = BW * BK * 2, STAGE = stage_bytes<NTOK>();
+  constexpr int S = stages<NTOK, XM>(), W_BYTES = BW * BK * 2, X_BYTES = NTOK * BK * 2, STAGE = stage_bytes<NTOK, XM>();
   constexpr uint32_t TCOLS = NTOK < 32 ? 32 : NTOK;
   constexpr uint32_t IDS = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NTOK >> 3) << 17) | ((uint32_t)(BW >> 4) << 24);
   static_assert(NTOK * BW * 4 <= S * STAGE, "the partial must fit over the stage ring");
+  static_assert(S >= 2, "at least two stages");
   extern __shared__ char smem_raw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + S * STAGE);
   uint64_t* empty = full + S;
-  uint64_t* acc_bar = full + 2 * S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 2 * S + 1);
+  uint64_t* xready = full + 2 * S;
+  uint64_t* acc_bar = full + 3 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 3 * S + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* ssq = reinterpret_cast<float*>(tmem_slot + 4);  // X_RMS: this CTA's per-token partial sums of squares
+  float* ssq_w = ssq + NTOK;                             // X_RMS: the same per transform warp
   float* part = reinterpret_cast<float*>(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x;
@@ -806,6 +832,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_cons
     for (int s = 0; s < S; ++s) {
       tg::mbar_init(&full[s], 1);
       tg::mbar_init(&empty[s], 1);
+      tg::mbar_init(&xready[s], 1);
     }
     tg::mbar_init(acc_bar, 1);
     *abort = 0;
@@ -821,6 +848,12 @@ __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_cons
   const uint32_t tmem = *tmem_slot;
   pdl_trigger();  // the successor may be scheduled once every CTA of this grid is resident
 
+  auto load_x = [&](int i, int s) {
+    char* dst = sm + s * STAGE + W_BYTES;
+    tg::tma2d(dst, &tx, (k0 + i) * BK, 0, &full[s]);
+    if constexpr (XM == X_SWIGLU) tg::tma2d(dst + X_BYTES, &tx, p.K + (k0 + i) * BK, 0, &full[s]);
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       int pre = 0;
@@ -832,14 +865,14 @@ __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_cons
         }
       }
       pdl_wait();
-      for (int i = 0; i < pre; ++i) tg::tma2d(sm + i * STAGE + W_BYTES, &tx, (k0 + i) * BK, 0, &full[i]);
+      for (int i = 0; i < pre; ++i) load_x(i, i);
       int i = pre;
       for (; i < n_slabs; ++i) {
         const int s = i % S;
         if (i >= S && !tg::wait(&empty[s], ((i / S) - 1) & 1, abort, p.err, 31)) break;
         tg::expect_tx(&full[s], STAGE);
         tg::tma2d(sm + s * STAGE, &tw, (k0 + i) * BK, tile * BW, &full[s]);
-        tg::tma2d(sm + s * STAGE + W_BYTES, &tx, (k0 + i) * BK, 0, &full[s]);
+        load_x(i, s);
       }
       if (*abort) {  // let the copies in flight land before the ring is reused or released
         int zero = 0;
@@ -850,7 +883,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_cons
     if (lane == 0) {
       for (int i = 0; i < n_slabs; ++i) {
         const int s = i % S;
-        if (!tg::wait(&full[s], (i / S) & 1, abort, p.err, 32)) break;
+        if (!tg::wait(XM == X_PLAIN ? &full[s] : &xready[s], (i / S) & 1, abort, p.err, 32)) break;
         tg::fence_after();
         const uint32_t sw = tg::s32(sm + s * STAGE), sx = sw + W_BYTES;
 #pragma unroll
@@ -860,7 +893,60 @@ __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_cons
       tg::commit(acc_bar);  // arrives once every MMA issued above has completed
     }
   } else {
-    const int q = warp & 3, n = q * 32 + lane;
+    const int tt = threadIdx.x - 64;  // 0..127
+    const int q = warp & 3, wq = warp - 2;  // TMEM lane quarter; transform warp index 0..3
+    constexpr int CPL = NTOK / 4;            // 16-byte chunks per lane of one slab
+    if constexpr (XM != X_PLAIN) {
+      // Warp wq transforms slabs wq, wq + 4, ... in place (four slabs in flight hide each one's load /
+      // compute / store latency).  Lane l covers 16-byte chunk j = l % 8 of rows l / 8 + 4m of the
+      // 128-byte-swizzled slab; that chunk holds logical columns 8 * (j ^ (row % 8)) .. +7, and
+      // row % 8 is l / 8 + 4 (m % 2).  X_RMS: each warp adds its slabs' per-token sums of squares
+      // into its own row of ssq_w, in slab order.
+      const int j = lane & 7, rb = lane >> 3;
+      const int c0a = (j ^ rb) * 8, c0b = (j ^ (rb + 4)) * 8;
+      if constexpr (XM == X_RMS) {
+        for (int t = lane; t < NTOK; t += 32) ssq_w[wq * NTOK + t] = 0.f;
+        __syncwarp();
+      }
+      for (int i = wq; i < n_slabs; i += 4) {
+        const int s = i % S;
+        float ga[8], gb[8];
+        if constexpr (XM == X_RMS) {  // the norm weights of this slab, requested before the wait
+          load8(p.g + (long)(k0 + i) * BK + c0a, ga);
+          load8(p.g + (long)(k0 + i) * BK + c0b, gb);
+        }
+        if (!tg::wait(&full[s], (i / S) & 1, abort, p.err, 34)) break;
+        char* xs = sm + s * STAGE + W_BYTES;
+#pragma unroll 2
+        for (int m = 0; m < CPL; ++m) {
+          const int off = (rb + 4 * m) * 128 + j * 16;
+          float f[8], o[8];
+          load8(reinterpret_cast<const bf16*>(xs + off), f);
+          if constexpr (XM == X_RMS) {
+            float v = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              v += f[e] * f[e];
+              o[e] = f[e] * ((m & 1) ? gb[e] : ga[e]);
+            }
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            if (j == 0) ssq_w[wq * NTOK + rb + 4 * m] += v;
+          } else {
+            float u[8];
+            load8(reinterpret_cast<const bf16*>(xs + X_BYTES + off), u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = silu_f(f[e]) * u[e];
+          }
+          store8(reinterpret_cast<bf16*>(xs + off), o);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) tg::arrive(&xready[s]);
+      }
+    }
+    const int n = q * 32 + lane;
     const bool ok = __all_sync(0xffffffffu, tg::wait(acc_bar, 0, abort, p.err, 33)) && n_slabs > 0;
     tg::fence_after();
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
@@ -873,6 +959,10 @@ __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_cons
         if (c0 + e < NTOK) part[(c0 + e) * BW + n] = ok ? __uint_as_float(v[e]) : 0.f;
     }
     tg::fence_before();
+    if constexpr (XM == X_RMS) {  // per-token sums of the 4 warps, in order
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (tt < NTOK) ssq[tt] = ((ssq_w[tt] + ssq_w[NTOK + tt]) + ssq_w[2 * NTOK + tt]) + ssq_w[3 * NTOK + tt];
+    }
   }
   __syncwarp();
   cluster_sync();  // every rank's partial is complete and visible
@@ -882,14 +972,20 @@ __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_cons
     const uint32_t rank = cluster_rank(), ranks = cluster_size();
     const int groups = p.M * (BW / 4), share = (groups + (int)ranks - 1) / (int)ranks;
     const int g0 = (int)rank * share, g1 = min(groups, g0 + share);
-    const uint32_t pbase = tg::s32(part);
+    const uint32_t pbase = tg::s32(part), sbase = tg::s32(ssq);
     for (int g = g0 + threadIdx.x; g < g1; g += THREADS) {
       const int t = g / (BW / 4), c = (g % (BW / 4)) * 4, n = tile * BW + c;
       if (n >= p.N) continue;
       float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      float ss = 0.f;
       for (uint32_t r = 0; r < ranks; ++r) {
         const float4 b = ld_cluster4(pbase + (uint32_t)((t * BW + c) * 4), r);
         a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+        if constexpr (XM == X_RMS) ss += ld_cluster1(sbase + (uint32_t)(t * 4), r);
+      }
+      if constexpr (XM == X_RMS) {
+        const float rs = rsqrtf(ss / (float)p.K + p.eps);
+        a.x *= rs, a.y *= rs, a.z *= rs, a.w *= rs;
       }
       const long at = (long)t * p.N + n;
       if (p.r) {
@@ -1011,7 +1107,7 @@ static void launch_stream(const void* X, const void* W, const void* R, void* Y, 
 
 // Largest split count (<= 8, <= K slabs) whose (tiles x splits) grid of clusters is resident in one
 // wave; 1 when even single-CTA tiles need several waves (large matrices).
-template <int NTOK>
+template <int NTOK, int XM>
 static int cluster_splits(int n_tiles, int kslabs) {
   static std::mutex mu;
   static int fit[64][cs::MAX_SPLITS + 1] = {};  // clusters resident at once, per device and split count
@@ -1026,11 +1122,11 @@ static int cluster_splits(int n_tiles, int kslabs) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(1, s, 1);
       cfg.blockDim = dim3(cs::THREADS);
-      cfg.dynamicSmemBytes = cs::smem_bytes<NTOK>();
+      cfg.dynamicSmemBytes = cs::smem_bytes<NTOK, XM>();
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      AX_CUDA_OK(cudaOccupancyMaxActiveClusters(&n, cs::stream_cluster_k<NTOK>, &cfg));
+      AX_CUDA_OK(cudaOccupancyMaxActiveClusters(&n, cs::stream_cluster_k<NTOK, XM>, &cfg));
       fit[dev][s] = std::max(n, 1);
     }
     if (n_tiles <= fit[dev][s]) return s;
@@ -1038,20 +1134,21 @@ static int cluster_splits(int n_tiles, int kslabs) {
   return 1;
 }
 
-template <int NTOK>
+template <int NTOK, int XM>
 static void launch_stream_cluster(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, int* err, bool prefetch_w,
-                                  cudaStream_t st) {
-  const int smem = cs::smem_bytes<NTOK>();
-  smem_attr(reinterpret_cast<const void*>(cs::stream_cluster_k<NTOK>), smem);
+                                  const void* g, float eps, cudaStream_t st) {
+  const int smem = cs::smem_bytes<NTOK, XM>();
+  smem_attr(reinterpret_cast<const void*>(cs::stream_cluster_k<NTOK, XM>), smem);
   const CUtensorMap tw = kmajor_map(W, N, K, cs::BW);
-  const CUtensorMap tx = kmajor_map(X, M, K, NTOK);
+  const CUtensorMap tx = kmajor_map(X, M, XM == cs::X_SWIGLU ? 2L * K : (long)K, NTOK);
   cs::Params p{};
   p.M = M, p.N = N, p.K = K, p.kslabs = K / cs::BK;
   const int n_tiles = (N + cs::BW - 1) / cs::BW;
-  int splits = cluster_splits<NTOK>(n_tiles, p.kslabs);
+  int splits = cluster_splits<NTOK, XM>(n_tiles, p.kslabs);
   p.per = (p.kslabs + splits - 1) / splits;
   splits = (p.kslabs + p.per - 1) / p.per;  // every split covers at least one slab
   p.r = static_cast<const bf16*>(R), p.y = static_cast<bf16*>(Y), p.err = err, p.prefetch_w = prefetch_w ? 1 : 0;
+  p.g = static_cast<const bf16*>(g), p.eps = eps;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = splits, attr[0].val.clusterDim.z = 1;
@@ -1064,7 +1161,16 @@ static void launch_stream_cluster(const void* X, const void* W, const void* R, v
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  AX_CUDA_OK(cudaLaunchKernelEx(&cfg, cs::stream_cluster_k<NTOK>, tw, tx, p));
+  AX_CUDA_OK(cudaLaunchKernelEx(&cfg, cs::stream_cluster_k<NTOK, XM>, tw, tx, p));
+}
+
+template <int XM>
+static void stream_cluster_rows(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, int* err, bool prefetch_w,
+                                const void* g, float eps, cudaStream_t st) {
+  if (M <= 16) launch_stream_cluster<16, XM>(X, W, R, Y, M, N, K, err, prefetch_w, g, eps, st);
+  else if (M <= 32) launch_stream_cluster<32, XM>(X, W, R, Y, M, N, K, err, prefetch_w, g, eps, st);
+  else if (M <= 64) launch_stream_cluster<64, XM>(X, W, R, Y, M, N, K, err, prefetch_w, g, eps, st);
+  else launch_stream_cluster<128, XM>(X, W, R, Y, M, N, K, err, prefetch_w, g, eps, st);
 }
 
 }  // namespace tg
@@ -1079,18 +1185,21 @@ void tcgemm_stream(const void* X, const void* W, const void* R, void* Y, int M, 
   else tg::launch_stream<64>(X, W, R, Y, M, N, K, ws, cnt, err, prefetch_w, st);
 }
 
-// Decode-size GEMM (M <= 64 rows) streaming the weights on the tensor cores, split-K partials
-// reduced inside a thread-block cluster (deterministic; no workspace).  Y and R: 8-byte aligned.
+// Decode-size GEMM (M <= 128 rows) streaming the weights on the tensor cores, split-K partials
+// reduced inside a thread-block cluster (deterministic; no workspace).  xmode 0: Y = X @ W^T (+ R);
+// 1: Y = RMSNorm(X; g, eps) @ W^T (+ R); 2: Y = (silu(X[:, :K]) * X[:, K:]) @ W^T (+ R) with X of
+// width 2K.  Y and R: 8-byte aligned.
 void tcgemm_stream_cluster(const void* X, const void* W, const void* R, void* Y, int M, int N, int K, int* err, bool prefetch_w,
-                           cudaStream_t st) {
-  AX_REQUIRE(M >= 1 && M <= 64, "tcgemm_stream_cluster: 1..64 rows, got ", M);
+                           cudaStream_t st, int xmode, const void* g, float eps) {
+  AX_REQUIRE(M >= 1 && M <= 128, "tcgemm_stream_cluster: 1..128 rows, got ", M);
   AX_REQUIRE(K % 64 == 0 && N % 8 == 0, "tcgemm_stream_cluster: K multiple of 64, N multiple of 8");
   AX_REQUIRE(reinterpret_cast<uintptr_t>(X) % 16 == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0 && reinterpret_cast<uintptr_t>(Y) % 8 == 0 &&
-                 reinterpret_cast<uintptr_t>(R) % 8 == 0,
+                 reinterpret_cast<uintptr_t>(R) % 8 == 0 && reinterpret_cast<uintptr_t>(g) % 16 == 0,
              "tcgemm_stream_cluster: operand alignment");
-  if (M <= 16) tg::launch_stream_cluster<16>(X, W, R, Y, M, N, K, err, prefetch_w, st);
-  else if (M <= 32) tg::launch_stream_cluster<32>(X, W, R, Y, M, N, K, err, prefetch_w, st);
-  else tg::launch_stream_cluster<64>(X, W, R, Y, M, N, K, err, prefetch_w, st);
+  AX_REQUIRE(xmode >= 0 && xmode <= 2 && (xmode != 1 || g != nullptr), "tcgemm_stream_cluster: input transform");
+  if (xmode == 1) tg::stream_cluster_rows<tg::cs::X_RMS>(X, W, R, Y, M, N, K, err, prefetch_w, g, eps, st);
+  else if (xmode == 2) tg::stream_cluster_rows<tg::cs::X_SWIGLU>(X, W, R, Y, M, N, K, err, prefetch_w, g, eps, st);
+  else tg::stream_cluster_rows<tg::cs::X_PLAIN>(X, W, R, Y, M, N, K, err, prefetch_w, g, eps, st);
 }
 
 // D[M,N] (+)= A[M,K] @ B[N,K]^T (+ C), bf16; err: device int that records a wait timeout.

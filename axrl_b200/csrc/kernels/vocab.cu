@@ -155,8 +155,8 @@ __device__ __forceinline__ void argmax_merge(ArgMax& a, float v, int i) {
 template <typename T>
 __global__ void sample_part_k(const T* __restrict__ logits, int V, const float* __restrict__ temp, const int64_t* __restrict__ seed,
                               const int* __restrict__ row_ids, float4* __restrict__ part) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   __shared__ ArgMax shm[32];
   int row = blockIdx.x, S = gridDim.y, sp = blockIdx.y;
   int chunk = (V + S - 1) / S, j0 = sp * chunk, j1 = min(V, j0 + chunk);
@@ -194,8 +194,8 @@ __global__ void sample_part_k(const T* __restrict__ logits, int V, const float* 
 template <typename T>
 __global__ void sample_merge_k(const T* __restrict__ logits, int V, int S, const float* __restrict__ temp, const float4* __restrict__ part,
                                const int64_t* __restrict__ forced, int64_t* __restrict__ out_tok, float* __restrict__ out_lp, int B) {
+  pdl_trigger();  // successors may launch now; they wait for this grid's completion
   pdl_wait();
-  pdl_trigger();
   int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (row >= B) return;
   LseAcc a{-INFINITY, 0.f, 0.f};

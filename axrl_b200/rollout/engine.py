@@ -319,24 +319,43 @@ class RolloutEngine:
             return
         _ext.ext().linear_fwd_into(x.contiguous(), w, out)
 
+    def _fold_elementwise(self, rows: int) -> bool:
+        """Decode-size forwards (<= 128 rows) fold the RMSNorms before the qkv and gate/up projections
+        and the SwiGLU before the down projection into the weight-streaming GEMMs (``linear_rms_stream``,
+        ``linear_swiglu_stream``): three fewer kernels per layer.  Opt-in: ``AXRL_DECODE_FOLD=1``."""
+        return (self.is_cuda and not self.fp8 and 1 <= rows <= 128 and self.cfg.hidden_size % 64 == 0
+                and os.environ.get("AXRL_DECODE_FOLD", "0") == "1")
+
     def _layers(self, h, pos, slots, attend, capture=None, mix=None):  # noqa: ANN001, ANN202
         """``mix(li, module, x)``: the token mixer of linear-attention layers (hybrid models)."""
         if self.tp is not None:
             return self._layers_tp(h, pos, slots, attend)
         inv = self.model.inv_freq
+        fold = self._fold_elementwise(h.shape[0])
+        e = _ext.ext() if fold else None
+        eps = self.cfg.rms_norm_eps
         for li, layer in enumerate(self.model.layers):
             a = layer.self_attn
-            x = self._rms(h, layer.input_layernorm.weight)
             if li in self.gdn_index:
+                x = self._rms(h, layer.input_layernorm.weight)
                 h = h + mix(li, a, x)
                 x = self._rms(h, layer.post_attention_layernorm.weight)
                 h = self._mlp(layer, x, h, capture, li)
                 continue
-            qkv = self._lin(x, a.qkv_proj)
+            if fold and a.attn_gate is None:
+                x = None
+                qkv = e.linear_rms_stream(h, layer.input_layernorm.weight, eps, a.qkv_proj)
+            else:
+                x = self._rms(h, layer.input_layernorm.weight)
+                qkv = self._lin(x, a.qkv_proj)
             q, k, v = paged.qk_norm_rope_cache(qkv, a.q_norm, a.k_norm, pos, inv, a.nq, a.nkv, a.eps,
                                                self.kv[li, 0], self.kv[li, 1], slots)
             o = a.gate_output(attend(li, q, k, v).reshape(q.shape[0], -1), x, self._lin)
             h = self._lin(o, a.o_proj, residual=h)
+            if fold and not hasattr(layer.mlp, "router"):
+                gu = e.linear_rms_stream(h, layer.post_attention_layernorm.weight, eps, layer.mlp.gate_up_proj)
+                h = e.linear_swiglu_stream(gu, layer.mlp.down_proj, h)
+                continue
             x = self._rms(h, layer.post_attention_layernorm.weight)
             h = self._mlp(layer, x, h, capture, li)
         return self._rms(h, self.model.norm.weight)

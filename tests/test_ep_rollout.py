@@ -159,6 +159,10 @@ def _worker_lockstep(rank: int, world: int, port: int, q) -> None:  # noqa: ANN0
         w.resume_generation()
         outs = asyncio.run(batch(1))
         assert len(outs[0].output_ids) == 6 + 5 * rank
+        # A stop from any rank ends every rank's engine loop, so shut down once every rank is done:
+        # pause first (no expert collectives in flight), then meet, then stop.
+        w.pause_generation()
+        dist.barrier()
         w.shutdown()
         q.put((rank, "ok"))
     except Exception:  # noqa: BLE001

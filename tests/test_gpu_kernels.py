@@ -674,7 +674,8 @@ def test_tcgemm_stream_matches_fp32(M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (8, 6144, 4096), (16, 1000, 512), (17, 6144, 4096), (32, 4096, 12288),
-                                   (48, 24576, 4096), (64, 4096, 64), (64, 50000, 1024)])
+                                   (48, 24576, 4096), (64, 4096, 64), (64, 50000, 1024), (65, 6144, 4096), (128, 4096, 12288),
+                                   (100, 1000, 512)])
 def test_tcgemm_stream_cluster_matches_fp32(M, N, K):
     """Decode-size GEMM streaming the weights on tcgen05 with the split-K partials reduced inside a
     thread-block cluster: against fp32, with and without the residual, bit-identical across calls."""
@@ -697,6 +698,38 @@ def test_tcgemm_stream_cluster_matches_fp32(M, N, K):
             assert torch.equal(y, y_again), "cluster reduction must be deterministic"
     finally:
         e.set_decode_gemm("")
+
+
+@pytest.mark.parametrize("M", [1, 8, 17, 40, 64, 96, 128])
+def test_streaming_gemm_with_folded_rmsnorm_and_swiglu(M):
+    """RMSNorm folded into the weight-streaming GEMM (per-token 1/rms applied after the cluster
+    reduction) and SwiGLU folded into it (gate and up slabs combined in shared memory), against fp32
+    compositions of the separate ops, with and without the residual."""
+    e = _ext()
+    torch.manual_seed(100 + M)
+    K, N, F = 4096, 6144, 1536
+    h = (torch.randn(M, K, device=DEV) * 3).bfloat16()
+    g = (1 + 0.1 * torch.randn(K, device=DEV)).bfloat16()
+    w = (torch.randn(N, K, device=DEV) * 0.02).bfloat16()
+    r = torch.randn(M, N, device=DEV).bfloat16()
+    hf = h.float()
+    xn = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6) * g.float()
+    ref = xn @ w.float().t()
+    y = e.linear_rms_stream(h, g, 1e-6, w)
+    y2 = e.linear_rms_stream(h, g, 1e-6, w, r)
+    gu = torch.randn(M, 2 * F, device=DEV).bfloat16()
+    wd = (torch.randn(K, F, device=DEV) * 0.03).bfloat16()
+    rd = torch.randn(M, K, device=DEV).bfloat16()
+    gf, uf = gu.float()[:, :F], gu.float()[:, F:]
+    ref_d = (gf * torch.sigmoid(gf) * uf) @ wd.float().t()
+    yd = e.linear_swiglu_stream(gu, wd)
+    yd2 = e.linear_swiglu_stream(gu, wd, rd)
+    torch.cuda.synchronize()
+    assert e.tc_stream_error() == 0
+    close(y, ref, 3e-2, 2e-2, msg="rms-folded GEMM")
+    close(y2, ref + r.float(), 4e-2, 2e-2, msg="rms-folded GEMM + residual")
+    close(yd, ref_d, 3e-2, 2e-2, msg="swiglu-folded GEMM")
+    close(yd2, ref_d + rd.float(), 4e-2, 2e-2, msg="swiglu-folded GEMM + residual")
 
 
 @pytest.mark.parametrize("M,N,K", [(512, 256, 128), (1000, 4096, 1024), (4096, 6144, 4096), (777, 512, 96)])
