@@ -897,19 +897,22 @@ __global__ void __launch_bounds__(THREADS, 1) stream_cluster_k(const __grid_cons
     const int q = warp & 3, wq = warp - 2;  // TMEM lane quarter; transform warp index 0..3
     constexpr int CPL = NTOK / 4;            // 16-byte chunks per lane of one slab
     if constexpr (XM != X_PLAIN) {
-      // Warp wq transforms slabs wq, wq + 4, ... in place (four slabs in flight hide each one's load /
-      // compute / store latency).  Lane l covers 16-byte chunk j = l % 8 of rows l / 8 + 4m of the
-      // 128-byte-swizzled slab; that chunk holds logical columns 8 * (j ^ (row % 8)) .. +7, and
-      // row % 8 is l / 8 + 4 (m % 2).  X_RMS: each warp adds its slabs' per-token sums of squares
-      // into its own row of ssq_w, in slab order.
+      // Warp wq transforms, in place, the slabs of the ring stages s with s % 4 == wq (up to four
+      // slabs in flight hide each one's load / compute / store latency).  A stage always belongs to
+      // the same warp, which waits on its barrier phase by phase: a parity wait issued before the
+      // previous phase completed would return at once.  Lane l covers 16-byte chunk j = l % 8 of rows
+      // l / 8 + 4m of the 128-byte-swizzled slab; that chunk holds logical columns
+      // 8 * (j ^ (row % 8)) .. +7, and row % 8 is l / 8 + 4 (m % 2).  X_RMS: each warp adds its slabs'
+      // per-token sums of squares into its own row of ssq_w, in slab order.
       const int j = lane & 7, rb = lane >> 3;
       const int c0a = (j ^ rb) * 8, c0b = (j ^ (rb + 4)) * 8;
       if constexpr (XM == X_RMS) {
         for (int t = lane; t < NTOK; t += 32) ssq_w[wq * NTOK + t] = 0.f;
         __syncwarp();
       }
-      for (int i = wq; i < n_slabs; i += 4) {
+      for (int i = 0; i < n_slabs; ++i) {
         const int s = i % S;
+        if ((s & 3) != wq) continue;
         float ga[8], gb[8];
         if constexpr (XM == X_RMS) {  // the norm weights of this slab, requested before the wait
           load8(p.g + (long)(k0 + i) * BK + c0a, ga);
