@@ -105,6 +105,7 @@ void tc_linear_to_slots(at::Tensor x, at::Tensor w, at::Tensor peer_ptrs, int64_
 int64_t tc_linear_error();
 at::Tensor tc_stream_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> residual);
 int64_t tc_stream_error();
+std::vector<int64_t> stream_cluster_fit(int64_t ntok);
 int64_t decode_tma_error();
 at::Tensor tc_linear_dgrad(at::Tensor dy, at::Tensor w);
 void adamw_p2p_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor ptrs, int64_t s0, int64_t decay_end, double lr,
@@ -208,6 +209,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_linear_error", &ax::tc_linear_error);
   m.def("tc_stream_linear", &ax::tc_stream_linear, py::arg("x"), py::arg("w"), py::arg("residual") = py::none());
   m.def("tc_stream_error", &ax::tc_stream_error);
+  m.def("stream_cluster_fit", &ax::stream_cluster_fit, "resident clusters of 1..16 CTAs of the cluster streaming GEMM for ntok rows");
   m.def("decode_tma_error", &ax::decode_tma_error);
   m.def("tc_linear_dgrad", &ax::tc_linear_dgrad);
   m.def("adamw_p2p_step", &ax::adamw_p2p_step);

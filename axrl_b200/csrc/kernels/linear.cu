@@ -549,6 +549,8 @@ at::Tensor tc_stream_linear(at::Tensor x, at::Tensor w, c10::optional<at::Tensor
   return y;
 }
 
+std::vector<int64_t> tcgemm_stream_cluster_fit(int ntok);
+std::vector<int64_t> stream_cluster_fit(int64_t ntok) { return tcgemm_stream_cluster_fit((int)ntok); }
 int64_t tc_stream_error() { return stream_workspace(c10::cuda::current_device()).err.item<int>(); }
 
 // Test / benchmark entries of the hand-written backward GEMMs.

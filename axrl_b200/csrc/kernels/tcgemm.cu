@@ -50,6 +50,8 @@
 // frees its TMEM and exits.  TMA reads only this GPU's memory.
 #include <cuda.h>
 
+#include <vector>
+
 #include "../cuda_common.cuh"
 
 namespace ax {
@@ -740,7 +742,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_k(const __grid_constant__ C
 //   all         a second cluster barrier keeps every partial alive until its readers are done.
 // Every mbarrier wait is bounded; every thread reaches both cluster barriers whatever happened.
 namespace cs {
-constexpr int BW = 128, BK = 64, THREADS = 192, MAX_SPLITS = 8;
+constexpr int BW = 128, BK = 64, THREADS = 192, MAX_SPLITS = 16;  // > 8: non-portable cluster sizes
 // Input transform applied to each X slab in shared memory before its MMAs (warps 2-5):
 //   X_PLAIN   none;
 //   X_RMS     X = RMSNorm(H) with weight g: the slab becomes bf16(H * g) and the per-token sums of
@@ -1108,32 +1110,54 @@ static void launch_stream(const void* X, const void* W, const void* R, void* Y, 
 }
 
 
+// Clusters of s CTAs (1 <= s <= 16) of this kernel that can be resident at once on the current device.
+template <int NTOK, int XM>
+static int cluster_fit(int s) {
+  static std::mutex mu;
+  static int fit[64][cs::MAX_SPLITS + 1] = {};
+  int dev = 0;
+  AX_CUDA_OK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> g(mu);
+  if (!fit[dev][s]) {
+    const void* kern = reinterpret_cast<const void*>(cs::stream_cluster_k<NTOK, XM>);
+    smem_attr(kern, cs::smem_bytes<NTOK, XM>());
+    if (s > 8) AX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = s, attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, s, 1);
+    cfg.blockDim = dim3(cs::THREADS);
+    cfg.dynamicSmemBytes = cs::smem_bytes<NTOK, XM>();
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    AX_CUDA_OK(cudaOccupancyMaxActiveClusters(&n, cs::stream_cluster_k<NTOK, XM>, &cfg));
+    fit[dev][s] = std::max(n, 1);
+  }
+  return fit[dev][s];
+}
+
+// Split count forced by AXRL_CLUSTER_SPLITS (1..16), 0 when unset.
+static int forced_cluster_splits() {
+  static int v = [] {
+    const char* e = std::getenv("AXRL_CLUSTER_SPLITS");
+    const int n = e ? std::atoi(e) : 0;
+    return (n >= 1 && n <= cs::MAX_SPLITS) ? n : 0;
+  }();
+  return v;
+}
+
 // Largest split count (<= 8, <= K slabs) whose (tiles x splits) grid of clusters is resident in one
 // wave; 1 when even single-CTA tiles need several waves (large matrices).
 template <int NTOK, int XM>
 static int cluster_splits(int n_tiles, int kslabs) {
-  static std::mutex mu;
-  static int fit[64][cs::MAX_SPLITS + 1] = {};  // clusters resident at once, per device and split count
-  int dev = 0;
-  AX_CUDA_OK(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> g(mu);
-  for (int s = std::min(cs::MAX_SPLITS, kslabs); s >= 1; --s) {
-    if (!fit[dev][s]) {
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = s, attr[0].val.clusterDim.z = 1;
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(1, s, 1);
-      cfg.blockDim = dim3(cs::THREADS);
-      cfg.dynamicSmemBytes = cs::smem_bytes<NTOK, XM>();
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      AX_CUDA_OK(cudaOccupancyMaxActiveClusters(&n, cs::stream_cluster_k<NTOK, XM>, &cfg));
-      fit[dev][s] = std::max(n, 1);
-    }
-    if (n_tiles <= fit[dev][s]) return s;
+  if (const int f = forced_cluster_splits()) {
+    if (f > 8) cluster_fit<NTOK, XM>(f);  // sets the non-portable cluster size attribute
+    return std::min(f, kslabs);
   }
+  for (int s = std::min(8, kslabs); s >= 1; --s)
+    if (n_tiles <= cluster_fit<NTOK, XM>(s)) return s;
   return 1;
 }
 
@@ -1186,6 +1210,17 @@ void tcgemm_stream(const void* X, const void* W, const void* R, void* Y, int M, 
   AX_REQUIRE(K % 64 == 0 && N % 8 == 0, "tcgemm_stream: K multiple of 64, N multiple of 8");
   if (M <= 32) tg::launch_stream<32>(X, W, R, Y, M, N, K, ws, cnt, err, prefetch_w, st);
   else tg::launch_stream<64>(X, W, R, Y, M, N, K, ws, cnt, err, prefetch_w, st);
+}
+
+// Resident clusters of 1..16 CTAs of the streaming kernel for `ntok` token rows (plain input).
+std::vector<int64_t> tcgemm_stream_cluster_fit(int ntok) {
+  std::vector<int64_t> out;
+  for (int s = 1; s <= tg::cs::MAX_SPLITS; ++s)
+    out.push_back(ntok <= 16   ? tg::cluster_fit<16, 0>(s)
+                  : ntok <= 32 ? tg::cluster_fit<32, 0>(s)
+                  : ntok <= 64 ? tg::cluster_fit<64, 0>(s)
+                               : tg::cluster_fit<128, 0>(s));
+  return out;
 }
 
 // Decode-size GEMM (M <= 128 rows) streaming the weights on the tensor cores, split-K partials
