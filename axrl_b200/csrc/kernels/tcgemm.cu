@@ -1148,8 +1148,13 @@ static int forced_cluster_splits() {
   return v;
 }
 
-// Largest split count (<= 8, <= K slabs) whose (tiles x splits) grid of clusters is resident in one
-// wave; 1 when even single-CTA tiles need several waves (large matrices).
+// Largest split count (<= 8, <= K slabs) for which the occupancy query (cluster_fit) reports every
+// cluster of the (tiles x splits) grid resident at once; 1 when even single-CTA tiles need several
+// waves (large matrices).  The query counts one CTA per SM for this cluster launch although two fit
+// by shared memory, so the grids are small (2 splits for the 48-tile qkv matrix, 4 for the 32-tile o
+// / down matrices).  Larger grids (4 / 8 splits) are faster in isolated chains of one projection
+// (qkv 13.3 vs 15.2 us, down 20.0 vs 22.2 at 8 rows) but made the whole Qwen3-8B decode step slower
+// (batch 8: 4.68 vs 4.30 ms), so the choice stays; AXRL_CLUSTER_SPLITS forces a count for tuning.
 template <int NTOK, int XM>
 static int cluster_splits(int n_tiles, int kslabs) {
   if (const int f = forced_cluster_splits()) {
