@@ -124,11 +124,13 @@ at::Tensor linear_rms_stream(at::Tensor h, at::Tensor g, double eps, at::Tensor 
   check_bf16_2d(w, "w");
   const int M = h.size(0), K = h.size(1), N = w.size(0);
   AX_CHECK(w.size(1) == K && g.numel() == K && g.scalar_type() == at::kBFloat16 && g.is_contiguous(), "linear_rms_stream: shapes");
+  AX_CHECK(g.is_cuda() && g.get_device() == h.get_device() && w.get_device() == h.get_device(),
+           "linear_rms_stream: h, g and w must be on the same CUDA device");
   AX_CHECK(M >= 1 && M <= 128 && K % 64 == 0 && N % 8 == 0, "linear_rms_stream: 1..128 rows, K % 64 == 0, N % 8 == 0");
   const bf16* r = nullptr;
   if (residual.has_value()) {
     check_bf16_2d(*residual, "residual");
-    AX_CHECK(residual->size(0) == M && residual->size(1) == N, "residual shape");
+    AX_CHECK(residual->size(0) == M && residual->size(1) == N && residual->get_device() == h.get_device(), "residual shape / device");
     r = (const bf16*)residual->data_ptr();
   }
   auto y = at::empty({M, N}, h.options());
@@ -143,11 +145,12 @@ at::Tensor linear_swiglu_stream(at::Tensor gu, at::Tensor w, c10::optional<at::T
   check_bf16_2d(w, "w");
   const int M = gu.size(0), K = gu.size(1) / 2, N = w.size(0);
   AX_CHECK(gu.size(1) == 2 * K && w.size(1) == K, "linear_swiglu_stream: gu is [M, 2K], w is [N, K]");
+  AX_CHECK(w.get_device() == gu.get_device(), "linear_swiglu_stream: gu and w must be on the same CUDA device");
   AX_CHECK(M >= 1 && M <= 128 && K % 64 == 0 && N % 8 == 0, "linear_swiglu_stream: 1..128 rows, K % 64 == 0, N % 8 == 0");
   const bf16* r = nullptr;
   if (residual.has_value()) {
     check_bf16_2d(*residual, "residual");
-    AX_CHECK(residual->size(0) == M && residual->size(1) == N, "residual shape");
+    AX_CHECK(residual->size(0) == M && residual->size(1) == N && residual->get_device() == gu.get_device(), "residual shape / device");
     r = (const bf16*)residual->data_ptr();
   }
   auto y = at::empty({M, N}, gu.options());
